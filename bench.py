@@ -1,0 +1,462 @@
+"""Benchmark of the speculative verify step on B200.
+
+One step = one verify pass over a batch of 64 sequences per GPU, the
+workload BASELINE.json's metric is quoted on (config 1):
+  kv_reserve (k+1 slots) -> kv_write (new K/V rows) -> verify attention
+  (Llama-3-8B layer: Hq 32, Hkv 8, D 128, bf16 paged KV, block 16,
+  context ~ U[512, 4096]) -> acceptance sampling (k = 5, V = 128256, fp32,
+  T = 1.0) -> kv_commit.
+Contexts grow by the committed tokens from step to step, as in decoding.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 runs under torchrun, one rank per GPU; sequences are sharded by
+rank (weak scaling, no collective on the data path).  `value` is verified
+positions per second over all ranks, device-timed with CUDA events, max
+over ranks.  `e2e` is the same metric through the C ABI with host buffers:
+each step copies its inputs from pinned host memory and reads its results
+back.  `--impl reference` times the CPU restatement of the reference path
+(oracle/, the reference itself is Rust and cannot be built here) on the
+host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "spec-verify tokens/s (attn+accept)"
+UNIT = "verified positions/s"
+
+
+def workload_desc(cfg, n):
+    return {
+        "workload": "config1: chain verify (paged attention + accept + KV commit), Llama-3-8B "
+                    "layer Hq32/Hkv8/D128 bf16 KV block16, ctx U[512,4096], k=5 (+1), "
+                    "V=128256 fp32, T=1.0",
+        "batch_per_gpu": cfg.batch, "global_batch": cfg.batch * n, "k": cfg.k,
+        "vocab": cfg.vocab, "kv_blocks_per_gpu": cfg.num_blocks,
+        "parallelism": f"batch-sharded x{n} (no collective)",
+        "l2": "inputs larger than L2 each step (~0.6 GB KV + 0.36 GB logits)",
+    }
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def load_traffic():
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f)
+    except Exception:
+        return {}
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.gpu)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.reader = threading.Thread(target=self._read, daemon=True)
+            self.reader.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, r in rows for i, v in enumerate(r)
+                          if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": rows[0][1],
+                "reasons": reasons, "samples": len(rows)}
+
+
+# --------------------------------------------------------------------- ours
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    from kyro_b200 import _lib
+    from kyro_b200.verify import (Context, kv_commit, kv_reserve, kv_write, sample_tokens,
+                                  spec_accept, verify_attention)
+    from kyro_b200.workloads import CONFIG1, accept_inputs, chain_bytes_per_step, paged_state
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    cfg = CONFIG1
+    ctx = Context(local)
+    seq_offset = rank * cfg.batch
+    st = paged_state(cfg, dev, seed=1000 + rank)
+    tgt, drf = accept_inputs(cfg.batch, cfg.k, cfg.vocab, dev, seed=2000 + rank)
+    drafts, _ = sample_tokens(ctx, drf, cfg.temperature, seed=0, seq_offset=seq_offset)
+    g = torch.Generator(device=dev).manual_seed(3000 + rank)
+    nq = cfg.num_query
+    k_new = torch.randn(cfg.batch, nq, cfg.num_kv_heads, cfg.head_dim, generator=g, device=dev,
+                        dtype=torch.bfloat16)
+    v_new = torch.randn(cfg.batch, nq, cfg.num_kv_heads, cfg.head_dim, generator=g, device=dev,
+                        dtype=torch.bfloat16)
+    attn_out = torch.empty_like(st.q)
+    acc = torch.empty(cfg.batch, dtype=torch.int32, device=dev)
+    toks = torch.empty(cfg.batch, nq, dtype=torch.int32, device=dev)
+    num = torch.empty(cfg.batch, dtype=torch.int32, device=dev)
+    ok = torch.empty(cfg.batch, dtype=torch.int32, device=dev)
+    L = _lib.load()
+    from kyro_b200.verify import attn_params
+    import ctypes as C
+    from kyro_b200._lib import AcceptParams
+    ws_attn = torch.empty(max(256, L.kyro_verify_attention_workspace_size(
+        C.byref(attn_params(st.q, st.k_cache, st.block_table)))), dtype=torch.uint8, device=dev)
+    ws_acc = torch.empty(max(256, L.kyro_spec_accept_workspace_size(C.byref(AcceptParams(
+        cfg.batch, cfg.k, cfg.vocab, 0, cfg.temperature, 0, 0, 0)))), dtype=torch.uint8, device=dev)
+    lens_hist = torch.empty(args.warmup + args.steps + 2, cfg.batch, dtype=torch.int64, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    ev = {n: [] for n in ("attention", "accept")}
+
+    def step(i, timed):
+        lens_hist[i].copy_(st.context_lens)
+        kv_reserve(ctx, nq, st.block_table, st.context_lens, st.free_stack, st.free_top,
+                   st.ref_counts, cfg.block_size, out_ok=ok)
+        kv_write(ctx, k_new, v_new, st.block_table, st.context_lens, st.k_cache, st.v_cache,
+                 cfg.block_size)
+        if timed:
+            e0 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+        verify_attention(ctx, st.q, st.k_cache, st.v_cache, st.block_table, st.context_lens,
+                         out=attn_out, workspace=ws_attn)
+        if timed:
+            e1 = torch.cuda.Event(enable_timing=True)
+            e1.record(stream)
+        spec_accept(ctx, tgt, drf, drafts, temperature=cfg.temperature, seed=0, step=i,
+                    seq_offset=seq_offset, out=(acc, toks, num, None), workspace=ws_acc)
+        if timed:
+            e2 = torch.cuda.Event(enable_timing=True)
+            e2.record(stream)
+            ev["attention"].append((e0, e1))
+            ev["accept"].append((e1, e2))
+        kv_commit(ctx, nq, acc, st.block_table, st.context_lens, st.free_stack, st.free_top,
+                  st.ref_counts, cfg.block_size)
+
+    for i in range(args.warmup):
+        step(i, False)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    phys = local
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    if vis:
+        ids = [v.strip() for v in vis.split(",")]
+        if local < len(ids) and ids[local].isdigit():
+            phys = int(ids[local])
+    clocks = ClockSampler(phys) if rank == 0 else None
+    if clocks:
+        clocks.start()
+        time.sleep(0.3)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(args.warmup, args.warmup + args.steps):
+        step(i, True)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop() if clocks else None
+    ms = t0.elapsed_time(t1)
+    if world > 1:
+        tms = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(tms, op=dist.ReduceOp.MAX)
+        ms = float(tms.item())
+    status = ctx.device_status()
+    if status:
+        raise SystemExit(f"device status word 0x{status:x} after the timed region")
+
+    # algorithmic bytes per step, from the context lengths each step saw
+    hist = lens_hist[args.warmup:args.warmup + args.steps].cpu().numpy()
+    per = [chain_bytes_per_step(h, cfg) for h in hist]
+    att_ms = np.mean([a.elapsed_time(b) for a, b in ev["attention"]])
+    acc_ms = np.mean([a.elapsed_time(b) for a, b in ev["accept"]])
+    att_bytes = float(np.mean([p["attention"] for p in per]))
+    acc_bytes = float(np.mean([p["accept"] for p in per]))
+    peak, peak_kind = load_peaks()
+    traffic = load_traffic()
+    if att_ms >= acc_ms:
+        dom, dbytes, dms = "verify_attention_kernel", att_bytes, att_ms
+    else:
+        dom, dbytes, dms = "accept (3 kernels)", acc_bytes, acc_ms
+    achieved = dbytes / (dms * 1e-3) / 1e9
+    units = cfg.batch * nq * world * args.steps
+    value = units / (ms * 1e-3)
+    step_bytes = att_bytes + acc_bytes
+    launches_per_step = 1 + 1 + 1 + (1 if _attn_splits(st, cfg) else 0) + 3 + 1
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded; BASELINE config 1 shapes and distributions)",
+        "config": workload_desc(cfg, world),
+        "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak,
+                     "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": traffic.get(dom.split(" ")[0])},
+        "kernels": {
+            "verify_attention": {"ms": att_ms, "algorithmic_bytes": att_bytes,
+                                 "GBps": att_bytes / (att_ms * 1e-3) / 1e9,
+                                 "frac": att_bytes / (att_ms * 1e-3) / 1e9 / peak},
+            "accept": {"ms": acc_ms, "algorithmic_bytes": acc_bytes,
+                       "GBps": acc_bytes / (acc_ms * 1e-3) / 1e9,
+                       "frac": acc_bytes / (acc_ms * 1e-3) / 1e9 / peak},
+            "step_frac_of_hbm": step_bytes / (ms / args.steps * 1e-3) / 1e9 / peak,
+        },
+        "acceptance_rate": float(acc.float().mean().item() / cfg.k),
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clk,
+    }
+    line["e2e"] = run_e2e(args, ctx, cfg, st, tgt, drf, drafts, k_new, v_new, seq_offset, world,
+                          dist if world > 1 else None, dev)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(cfg, st, tgt, drf, drafts, k_new, v_new, args)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _attn_splits(st, cfg):
+    import ctypes as C
+    from kyro_b200 import _lib
+    from kyro_b200.verify import attn_params
+    p = attn_params(st.q, st.k_cache, st.block_table)
+    return _lib.load().kyro_verify_attention_workspace_size(C.byref(p)) > 0
+
+
+def run_e2e(args, ctx, cfg, st, tgt, drf, drafts, k_new, v_new, seq_offset, world, dist, dev):
+    """The same step through the C ABI with host buffers: inputs copied from
+    pinned host memory each step, results read back each step."""
+    import torch
+    from kyro_b200.verify import kv_commit, kv_reserve, kv_write, spec_accept, verify_attention
+    nq = cfg.num_query
+    h = {n: t.cpu().pin_memory() for n, t in
+         dict(q=st.q, k_new=k_new, v_new=v_new, tgt=tgt, drf=drf, drafts=drafts).items()}
+    d = {n: torch.empty_like(t, device=dev) for n, t in h.items()}
+    out_h = {n: torch.empty(s, dtype=torch.int32).pin_memory()
+             for n, s in dict(acc=(cfg.batch,), toks=(cfg.batch, nq), num=(cfg.batch,)).items()}
+    out_d = {n: torch.empty(t.shape, dtype=torch.int32, device=dev) for n, t in out_h.items()}
+    attn_out = torch.empty_like(st.q)
+    stream = torch.cuda.current_stream(dev)
+    h2d = sum(t.numel() * t.element_size() for t in h.values())
+    d2h = sum(t.numel() * t.element_size() for t in out_h.values())
+    steps = max(3, min(args.steps, 10))
+
+    def step(i):
+        for n in h:
+            d[n].copy_(h[n], non_blocking=True)
+        kv_reserve(ctx, nq, st.block_table, st.context_lens, st.free_stack, st.free_top,
+                   st.ref_counts, cfg.block_size)
+        kv_write(ctx, d["k_new"], d["v_new"], st.block_table, st.context_lens, st.k_cache,
+                 st.v_cache, cfg.block_size)
+        verify_attention(ctx, d["q"], st.k_cache, st.v_cache, st.block_table, st.context_lens,
+                         out=attn_out)
+        spec_accept(ctx, d["tgt"], d["drf"], d["drafts"], temperature=cfg.temperature, seed=0,
+                    step=1000 + i, seq_offset=seq_offset,
+                    out=(out_d["acc"], out_d["toks"], out_d["num"], None))
+        kv_commit(ctx, nq, out_d["acc"], st.block_table, st.context_lens, st.free_stack,
+                  st.free_top, st.ref_counts, cfg.block_size)
+        for n in out_h:
+            out_h[n].copy_(out_d[n], non_blocking=True)
+        stream.synchronize()  # the caller reads the emitted tokens
+
+    step(0)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(steps):
+        step(1 + i)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1)
+    if dist:
+        tms = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(tms, op=dist.ReduceOp.MAX)
+        ms = float(tms.item())
+    value = cfg.batch * nq * world * steps / (ms * 1e-3)
+    return {"value": value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "steps": steps, "ms_per_step": ms / steps}
+
+
+# ------------------------------------------------------------------ CPU side
+def _cpu_step(O, cfg, inp, seqs, step, nthreads):
+    """The reference path's verify step on host cores for the sequences in
+    `seqs`: KV write, attention, acceptance, commit (oracle restatement)."""
+    sel = np.asarray(seqs)
+    nq = cfg.num_query
+    bt, cl = inp["bt"][sel].copy(), inp["cl"][sel].copy()
+    fs, top, rc = inp["fs"].copy(), inp["top"].copy(), inp["rc"].copy()
+    O.kv_reserve(nq, bt, cl, fs, top, rc, cfg.block_size)
+    O.kv_write(inp["k_new"][sel], inp["v_new"][sel], bt, cl, inp["kc"], inp["vc"],
+               cfg.block_size)
+    O.paged_attention(inp["q"][sel], inp["kc"], inp["vc"], bt, cl, cfg.block_size,
+                      nthreads=nthreads)
+    acc, _, _, _ = O.spec_accept(inp["tgt"][sel], inp["drf"][sel], inp["drafts"][sel],
+                                 temperature=cfg.temperature, seed=0, step=step,
+                                 nthreads=nthreads)
+    O.kv_commit(nq, acc, bt, cl, fs, top, rc, cfg.block_size)
+
+
+def _host_inputs(st, tgt, drf, drafts, k_new, v_new):
+    from kyro_b200.workloads import bf16_bits
+    return {"q": bf16_bits(st.q), "kc": bf16_bits(st.k_cache), "vc": bf16_bits(st.v_cache),
+            "bt": st.block_table.cpu().numpy(), "cl": st.context_lens.cpu().numpy(),
+            "fs": st.free_stack.cpu().numpy(), "top": st.free_top.cpu().numpy(),
+            "rc": st.ref_counts.cpu().numpy(), "tgt": tgt.cpu().numpy(),
+            "drf": drf.cpu().numpy(), "drafts": drafts.cpu().numpy(),
+            "k_new": bf16_bits(k_new), "v_new": bf16_bits(v_new)}
+
+
+def cpu_baseline(cfg, st, tgt, drf, drafts, k_new, v_new, args):
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    O.build()
+    inp = _host_inputs(st, tgt, drf, drafts, k_new, v_new)
+    nthreads = os.cpu_count() or 1
+    seqs = list(range(min(cfg.batch, args.cpu_sample)))
+    t = time.perf_counter()
+    _cpu_step(O, cfg, inp, seqs, 0, nthreads)
+    dt = time.perf_counter() - t
+    return {"value": len(seqs) * cfg.num_query / dt, "unit": UNIT, "cores": nthreads,
+            "kind": "port",
+            "sample": f"{len(seqs)} of {cfg.batch} config-1 sequences, one verify step "
+                      f"(kv write + attention + accept + commit), {dt:.2f} s"}
+
+
+def run_reference(args):
+    """CPU restatement of the reference path on the host cores, same config."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import torch
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    O.build()
+    from kyro_b200.workloads import CONFIG1, accept_inputs, paged_state
+    cfg = CONFIG1
+    st = paged_state(cfg, "cpu", seed=1000)
+    tgt, drf = accept_inputs(cfg.batch, cfg.k, cfg.vocab, "cpu", seed=2000)
+    drafts, _ = O.sample_tokens(drf.numpy(), cfg.temperature, seed=0, nthreads=os.cpu_count())
+    g = torch.Generator().manual_seed(3000)
+    shape = (cfg.batch, cfg.num_query, cfg.num_kv_heads, cfg.head_dim)
+    k_new = torch.randn(shape, generator=g).to(torch.bfloat16)
+    v_new = torch.randn(shape, generator=g).to(torch.bfloat16)
+    inp = _host_inputs(st, tgt, drf, torch.from_numpy(drafts), k_new, v_new)
+    nthreads = os.cpu_count() or 1
+    sample = min(cfg.batch, args.cpu_sample)
+    for i in range(args.warmup):
+        _cpu_step(O, cfg, inp, list(range(sample)), i, nthreads)
+    times = []
+    for i in range(args.steps):
+        seqs = [(i * sample + j) % cfg.batch for j in range(sample)]
+        t = time.perf_counter()
+        _cpu_step(O, cfg, inp, seqs, args.warmup + i, nthreads)
+        times.append(time.perf_counter() - t)
+    total = sum(times)
+    value = sample * cfg.num_query * args.steps / total
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": total / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic (seeded; BASELINE config 1 shapes and distributions)",
+        "config": workload_desc(cfg, 1), "impl": "reference",
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": nthreads, "kind": "port",
+                         "sample": f"{sample} of {cfg.batch} config-1 sequences per step"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-sample", type=int, default=8,
+                    help="sequences per CPU step (cpu_baseline and --impl reference)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,268 @@
+/*
+ * kyro_spec.h -- C ABI of the B200 (sm_100a) speculative-decoding verify step.
+ *
+ * Three kernels families sit behind this header:
+ *   K1  paged multi-query verify attention (chain of k+1 positions, or the
+ *       nodes of a draft tree under an ancestor mask);
+ *   K2  vocab-wide rejection sampling (accept test, residual resample, bonus
+ *       token), plus the draft-token sampler that feeds it;
+ *   K3  KV-slot reserve / commit / rollback on the BlockManager block table.
+ *
+ * Conventions
+ *   - Every function returns an int status (KYRO_OK == 0).  Arguments are
+ *     validated on the host before anything is launched; kyro_last_error()
+ *     returns a message for the calling thread.
+ *   - The caller owns every device buffer (inputs, outputs, KV cache, block
+ *     tables, workspace).  Nothing on these entry points allocates device
+ *     memory; *_workspace_size() says how much scratch to pass.
+ *   - Calls enqueue on the context's stream and return without a host sync.
+ *   - One kyro_ctx per GPU; a context is not re-entrant, distinct contexts
+ *     are independent.
+ *   - Device-side range checks (block ids, token ids) set bits in a status
+ *     word instead of trapping; kyro_ctx_device_status() reads it.
+ *
+ * The reference (an all-Rust server) has no native code for this path; each
+ * declaration cites the Rust item whose role it takes.
+ */
+#ifndef KYRO_SPEC_H
+#define KYRO_SPEC_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KYRO_VERSION 1
+
+/* Status codes.  The Rust wrapper maps each to candle_core::Error::Msg
+ * (src/speculative.rs:224 builds errors the same way). */
+#define KYRO_OK 0
+#define KYRO_ERR_INVALID_ARG 1
+#define KYRO_ERR_CUDA 2
+#define KYRO_ERR_NCCL 3
+#define KYRO_ERR_TIMEOUT 4
+#define KYRO_ERR_OOB 5
+#define KYRO_ERR_OOM 6
+#define KYRO_ERR_UNSUPPORTED 7
+#define KYRO_ERR_WORKSPACE 8
+
+/* Bits of the device status word. */
+#define KYRO_DEV_BAD_TOKEN 0x1u      /* a draft token outside [0, vocab)        */
+#define KYRO_DEV_BAD_BLOCK 0x2u      /* a block id outside [0, num_blocks)      */
+#define KYRO_DEV_BAD_LENGTH 0x4u     /* context length beyond the block table   */
+#define KYRO_DEV_WAIT_TIMEOUT 0x8u   /* a bounded device-side wait gave up      */
+#define KYRO_DEV_STACK_OVERFLOW 0x10u /* free-stack push beyond num_blocks      */
+
+typedef struct kyro_ctx kyro_ctx;
+
+/* ---------------------------------------------------------------- context */
+
+/* Create a context bound to `device` and enqueueing on `stream`
+ * (a cudaStream_t; NULL = legacy default stream).  Allocates only the
+ * 16-byte device status word. */
+int kyro_ctx_create(int device, void* stream, kyro_ctx** out);
+int kyro_ctx_destroy(kyro_ctx* ctx);
+int kyro_ctx_set_stream(kyro_ctx* ctx, void* stream);
+/* Synchronise the context's stream, return the device status word in
+ * *out_flags (KYRO_DEV_* bits) and clear it when `clear` != 0. */
+int kyro_ctx_device_status(kyro_ctx* ctx, uint32_t* out_flags, int clear);
+/* Copy the calling thread's last error message into buf (NUL-terminated);
+ * returns the full message length. */
+size_t kyro_last_error(char* buf, size_t len);
+const char* kyro_status_string(int status);
+int kyro_version(void);
+/* Names of the kernels this library launches, ';'-separated. */
+const char* kyro_kernel_names(void);
+
+/* ------------------------------------------------ K2: acceptance sampling */
+
+/* Accept modes.
+ *  STOCHASTIC  rejection sampling (Leviathan et al. 2023 / Chen et al. 2023):
+ *              accept draft x_j iff u_j < p_j(x_j)/q_j(x_j); at the first
+ *              rejection resample from norm(max(p_j - q_j, 0)); if all k are
+ *              accepted, sample a bonus token from p_k.  temperature <= 0
+ *              falls back to GREEDY, as sample_token does
+ *              (src/worker.rs:290-296).
+ *  GREEDY      accept x_j iff x_j == argmax p_j; emit argmax at the first
+ *              mismatch, or the bonus argmax p_k when all match.
+ *  GREEDY_REF  exactly the reference rule of verify_drafts
+ *              (src/speculative.rs:314-323): like GREEDY but no bonus token
+ *              when every draft matches, and k == 0 emits argmax of row 0
+ *              (src/speculative.rs:296-305).
+ * argmax ties resolve to the lowest index. */
+#define KYRO_ACCEPT_STOCHASTIC 0
+#define KYRO_ACCEPT_GREEDY 1
+#define KYRO_ACCEPT_GREEDY_REF 2
+
+typedef struct kyro_accept_params {
+  int32_t batch;       /* B sequences in this call                          */
+  int32_t num_draft;   /* k draft tokens per sequence (0..64)               */
+  int32_t vocab;       /* V entries per logits row held by this process     */
+  int32_t mode;        /* KYRO_ACCEPT_*                                     */
+  float temperature;   /* softmax temperature for p and q (stochastic mode) */
+  uint32_t step;       /* Philox counter word 3 (the caller's step number)  */
+  uint64_t seed;       /* Philox key                                        */
+  int64_t seq_offset;  /* global index of sequence 0 (Philox counter word 0)*/
+} kyro_accept_params;
+
+size_t kyro_spec_accept_workspace_size(const kyro_accept_params* p);
+
+/* Replaces SpeculativeDecoder::verify_drafts (src/speculative.rs:286-339),
+ * batched over B sequences, with the sampling conventions of sample_token
+ * (src/worker.rs:298 temperature, :314-323 max-subtracted softmax,
+ * :352-360 inverse CDF).
+ *   target_logits  fp32 [B, k+1, V]   row j scores position j; row k is the
+ *                                     bonus row (unused by GREEDY_REF)
+ *   draft_logits   fp32 [B, k, V]     draft model logits (STOCHASTIC only;
+ *                                     may be NULL otherwise)
+ *   draft_tokens   int32 [B, k]
+ *   out_accept_len int32 [B]          accepted drafts a in [0, k]
+ *   out_tokens     int32 [B, k+1]     x_0..x_{a-1}, then the resampled /
+ *                                     bonus / argmax token; -1 padded
+ *   out_num_tokens int32 [B]          tokens emitted (a+1, or k for
+ *                                     GREEDY_REF when all match)
+ *   out_probs      fp32 [B, k, 2]     optional (NULL): (p_j(x_j), q_j(x_j)) */
+int kyro_spec_accept(kyro_ctx* ctx, const kyro_accept_params* p, const float* target_logits,
+                     const float* draft_logits, const int32_t* draft_tokens,
+                     int32_t* out_accept_len, int32_t* out_tokens, int32_t* out_num_tokens,
+                     float* out_probs, void* workspace, size_t workspace_bytes);
+
+/* Draft sampler: one token per row from softmax(logits / T) with Philox
+ * stream 0 (counter (seq_offset + b, pos, 0, step)); temperature <= 0 is
+ * argmax.  Replaces the draft loop's argmax (src/speculative.rs:229-241)
+ * with on-device sampling.
+ *   logits fp32 [B, num_pos, V] -> out_tokens int32 [B, num_pos]
+ *   out_probs fp32 [B, num_pos] optional: q(token). */
+typedef struct kyro_sample_params {
+  int32_t batch;
+  int32_t num_pos;
+  int32_t vocab;
+  float temperature;
+  uint32_t step;
+  uint32_t _pad;
+  uint64_t seed;
+  int64_t seq_offset;
+} kyro_sample_params;
+
+size_t kyro_sample_workspace_size(const kyro_sample_params* p);
+int kyro_sample_tokens(kyro_ctx* ctx, const kyro_sample_params* p, const float* logits,
+                       int32_t* out_tokens, float* out_probs, void* workspace,
+                       size_t workspace_bytes);
+
+/* ------------------------------------------- K1: paged verify attention */
+
+typedef struct kyro_attn_params {
+  int32_t batch;              /* B                                              */
+  int32_t num_query;          /* query positions per sequence: k+1 (chain) or
+                                 tree nodes (<= 64)                             */
+  int32_t num_heads;          /* Hq                                             */
+  int32_t num_kv_heads;       /* Hkv; Hq % Hkv == 0                             */
+  int32_t head_dim;           /* D (128 supported)                              */
+  int32_t block_size;         /* tokens per KV block (16 supported)             */
+  int32_t max_blocks_per_seq; /* width of block_table                           */
+  int32_t num_blocks;         /* KV cache capacity in blocks                    */
+  float scale;                /* softmax scale; 0 selects 1/sqrt(D)             */
+  int32_t kv_split_blocks;    /* KV blocks per work item; 0 = automatic         */
+} kyro_attn_params;
+
+size_t kyro_verify_attention_workspace_size(const kyro_attn_params* p);
+
+/* Replaces PagedAttention::forward (src/model/attention_kernel.rs:22-31) for
+ * num_query query positions per sequence, with the reference layouts
+ * (:52-57):
+ *   q            bf16 [B, num_query, Hq, D]
+ *   k_cache      bf16 [num_blocks, Hkv, block_size, D]
+ *   v_cache      bf16 [num_blocks, Hkv, block_size, D]
+ *   block_table  int64 [B, max_blocks_per_seq]
+ *   context_lens int64 [B]   tokens cached before the new ones
+ *   tree_mask    uint64 [B, num_query] or NULL.  Query j sits at position
+ *                context_len + j; its K/V must already be in the cache.
+ *                Query j attends every cached position and new position i
+ *                iff bit i of tree_mask[b][j] is set.  NULL means the chain
+ *                mask (i <= j).
+ *   out          bf16 [B, num_query, Hq, D]
+ * Query head h reads KV head h / (Hq/Hkv) (attention_kernel.rs:39-46);
+ * fp32 accumulation; scale 1/sqrt(D) (attention_kernel.rs:69). */
+int kyro_verify_attention(kyro_ctx* ctx, const kyro_attn_params* p, const void* q,
+                          const void* k_cache, const void* v_cache, const int64_t* block_table,
+                          const int64_t* context_lens, const uint64_t* tree_mask, void* out,
+                          void* workspace, size_t workspace_bytes);
+
+/* ------------------------------------------------ K3: KV commit / rollback */
+
+typedef struct kyro_kv_params {
+  int32_t batch;              /* B sequences                         */
+  int32_t block_size;         /* tokens per block                    */
+  int32_t max_blocks_per_seq; /* width of block_table                */
+  int32_t num_blocks;         /* pool size                           */
+} kyro_kv_params;
+
+/* Device mirror of BlockManager (src/scheduler/block_manager.rs:15-30):
+ *   block_table  int64 [B, max_blocks_per_seq]  seq b holds
+ *                ceil(context_lens[b]/block_size) blocks in entries 0..;
+ *                unused entries are -1
+ *   context_lens int64 [B]
+ *   free_stack   int32 [num_blocks]   free_gpu_blocks; entries
+ *                [0, *free_top) are free, the top is popped first
+ *                (Vec::pop, block_manager.rs:92-98)
+ *   free_top     int32 [1]
+ *   ref_counts   int32 [num_blocks]   (block_manager.rs:29)
+ *
+ * kyro_kv_reserve: make room for num_new more token slots in every
+ * sequence, popping new blocks in sequence order with ref_count = 1
+ * (allocate, block_manager.rs:109-125).  A sequence whose blocks do not fit
+ * in what is left of the free list gets nothing and out_ok[b] = 0 (out_ok
+ * may be NULL), like allocate() returning None (:111-113); later sequences
+ * are still served in order.  context_lens is not changed. */
+int kyro_kv_reserve(kyro_ctx* ctx, const kyro_kv_params* p, int32_t num_new,
+                    int64_t* block_table, const int64_t* context_lens, int32_t* free_stack,
+                    int32_t* free_top, int32_t* ref_counts, int32_t* out_ok);
+
+/* kyro_kv_commit: after verification keep accept_len[b] + 1 of the num_new
+ * reserved slots (the last accepted token plus the accepted drafts),
+ * advance context_lens, and release the blocks that now lie wholly beyond
+ * the new length: ref_count -= 1 and, at zero, push onto the free stack in
+ * sequence order and ascending table position (free, block_manager.rs:
+ * 129-153).  accept_len[b] < 0 leaves sequence b untouched. */
+int kyro_kv_commit(kyro_ctx* ctx, const kyro_kv_params* p, int32_t num_new,
+                   const int32_t* accept_len, int64_t* block_table, int64_t* context_lens,
+                   int32_t* free_stack, int32_t* free_top, int32_t* ref_counts);
+
+/* kyro_kv_commit_tree: tree verification wrote node n's K/V at position
+ * context_len + n.  For the accepted root-to-leaf path path[b][0..len-1]
+ * (path[b][0] == 0), move node path[b][i]'s K/V rows to position
+ * context_len + i in every one of the num_layers caches, then commit
+ * path_len[b] slots as kyro_kv_commit does.  k_caches / v_caches are host
+ * arrays of num_layers device pointers, each bf16
+ * [num_blocks, num_kv_heads, block_size, head_dim]. */
+int kyro_kv_commit_tree(kyro_ctx* ctx, const kyro_kv_params* p, int32_t num_nodes,
+                        const int32_t* path, const int32_t* path_len, int32_t num_layers,
+                        void* const* k_caches, void* const* v_caches, int32_t num_kv_heads,
+                        int32_t head_dim, int64_t* block_table, int64_t* context_lens,
+                        int32_t* free_stack, int32_t* free_top, int32_t* ref_counts);
+
+/* kyro_kv_write: store the K/V rows of the num_new new tokens of every
+ * sequence at positions context_lens[b] .. context_lens[b]+num_new-1 of its
+ * block table (slots made by kyro_kv_reserve).  Replaces
+ * KVCacheManager::append_kv (src/model/kv_cache.rs:49-75), which
+ * concatenates dense per-request tensors, with a paged scatter.
+ *   k_new, v_new bf16 [B, num_new, num_kv_heads, head_dim]
+ *                (the [batch, seq, Hkv, D] layout append_kv takes, :47-48)
+ *   k_cache, v_cache bf16 [num_blocks, num_kv_heads, block_size, head_dim] */
+int kyro_kv_write(kyro_ctx* ctx, const kyro_kv_params* p, int32_t num_new, int32_t num_kv_heads,
+                  int32_t head_dim, const void* k_new, const void* v_new,
+                  const int64_t* block_table, const int64_t* context_lens, void* k_cache,
+                  void* v_cache);
+
+/* Philox4x32-10 uniforms exactly as the kernels draw them (test aid):
+ * out[i] = u for counter (seq, pos0 + i, stream, step), i < n. */
+int kyro_philox_uniforms(kyro_ctx* ctx, uint64_t seed, uint32_t seq, uint32_t pos0,
+                         uint32_t stream, uint32_t step, int32_t n, float* out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KYRO_SPEC_H */

@@ -1,0 +1,582 @@
+// attention.cu -- K1: paged multi-query verify attention for sm_100a.
+//
+// Replaces PagedAttention::forward / paged_attention_kernel
+// (src/model/attention_kernel.rs:22-136), which walks the block table one
+// scalar at a time with a host sync per block and makes two passes over
+// K/V.  Here one pass streams each 16-token K and V block of a KV head once
+// for all query rows that share it (GQA group x verify positions).
+//
+// Work item: (sequence b, KV head, row group, KV split).  A CTA has one
+// producer warp and four consumer warps.  The producer issues TMA tile
+// loads (128-byte swizzle, no multicast) of the paged K/V blocks named by
+// the block table into an NS-stage shared-memory ring guarded by
+// mbarriers.  Each consumer warp takes one 16-token block per stage and
+// computes, with bf16 mma.sync (m16n8k16):
+//     S^T = K Q^T      (M = 16 tokens, N = query rows, K = head_dim)
+//     O^T += V^T P^T   (M = head_dim, N = query rows, K = 16 tokens)
+// so the query rows (24 for GQA 4 x 6 positions) sit in the N dimension in
+// 8-wide tiles without padding to 16.  Online softmax runs per query
+// column in the log2 domain.  The four warps' partial states are merged in
+// shared memory; when a sequence needs more than one split the partials go
+// to the workspace and verify_attention_merge_kernel combines them.
+#include <cuda_bf16.h>
+#include <cudaTypedefs.h>
+
+
+#include "kyro_internal.cuh"
+#include "ptx.cuh"
+
+namespace {
+
+constexpr int kBS = 16;               // tokens per KV block
+constexpr int kConsumers = 4;         // consumer warps
+constexpr int kThreads = (kConsumers + 1) * 32;
+constexpr int kStages = 3;
+constexpr int kMaxCols = 32;          // query rows per work item
+
+// Shared-memory geometry for head_dim D (64 or 128).
+template <int D>
+struct Geo {
+  static constexpr int kTileBytes = kBS * D * 2;       // one K or V block of one head
+  static constexpr int kSlotBytes = 2 * kTileBytes;    // K + V
+  static constexpr int kStageBytes = kConsumers * kSlotBytes;
+  static constexpr int kQStride = D + 8;               // padded bf16 row stride of the Q tile
+  static constexpr int kQBytes = kMaxCols * kQStride * 2;
+  static constexpr int kRingBytes = kStages * kStageBytes;
+  static constexpr int kMergeBytes = kConsumers * (D * kMaxCols + 2 * kMaxCols) * 4;
+  static_assert(kMergeBytes <= kRingBytes, "merge area reuses the ring");
+  static constexpr int kSmemBytes = 1024 + kRingBytes + kQBytes + kMaxCols * 8 + 64;
+};
+
+struct AttnArgs {
+  int B, nq, hq, hkv, group, rows, ngroups, max_blocks, num_blocks, split_blocks, max_splits;
+  float scale_log2;
+  int d;
+};
+
+// byte offset of (token row, 16-byte chunk along D) inside a swizzled tile
+__device__ __forceinline__ uint32_t kv_off(int row, int cidx) {
+  return (uint32_t)((cidx >> 3) * 2048 + row * 128 + (((cidx & 7) ^ (row & 7)) << 4));
+}
+
+template <int NT, int D>
+__global__ void __launch_bounds__(kThreads, 2)
+verify_attention_kernel(const __grid_constant__ CUtensorMap tmK,
+                        const __grid_constant__ CUtensorMap tmV, const __nv_bfloat16* __restrict__ q,
+                        const int64_t* __restrict__ block_table,
+                        const int64_t* __restrict__ context_lens,
+                        const uint64_t* __restrict__ tree_mask, __nv_bfloat16* __restrict__ out,
+                        float* __restrict__ part_o, float* __restrict__ part_ml, AttnArgs a,
+                        uint32_t* status) {
+  extern __shared__ uint8_t smem_raw[];
+  using G = Geo<D>;
+  constexpr int kD = D;
+  constexpr int kTileBytes = G::kTileBytes, kSlotBytes = G::kSlotBytes;
+  constexpr int kStageBytes = G::kStageBytes, kQStride = G::kQStride, kQBytes = G::kQBytes;
+  constexpr int kRingBytes = G::kRingBytes;
+  constexpr int kMT = D / 16;   // m-tiles of O^T along head_dim
+  constexpr int kKK = D / 16;   // k-steps of S^T along head_dim
+  const int split = blockIdx.x;
+  const int kvh = blockIdx.y / a.ngroups;
+  const int grp = blockIdx.y % a.ngroups;
+  const int b = blockIdx.z;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+  const int64_t ctx = context_lens[b];
+  const int64_t total = ctx + a.nq;
+  if (ctx < 0 || (total + kBS - 1) / kBS > a.max_blocks) {
+    if (tid == 0 && split == 0) kyro::dev::flag(status, KYRO_DEV_BAD_LENGTH);
+    return;
+  }
+  const int nblk = (int)((total + kBS - 1) / kBS);
+  const int nsplit = (nblk + a.split_blocks - 1) / a.split_blocks;
+  if (split >= nsplit) return;
+  const int blk0 = split * a.split_blocks;
+  const int blk1 = min(nblk, blk0 + a.split_blocks);
+  const int niter = (blk1 - blk0 + kConsumers - 1) / kConsumers;
+  const int col0 = grp * kMaxCols;
+  const int ncols = min(kMaxCols, a.rows - col0);
+
+  // ---- shared memory carve-up (ring 1024-aligned for the 128B swizzle)
+  const uint32_t raw = kyro::ptx::smem_addr(smem_raw);
+  const uint32_t ring_s = (raw + 1023u) & ~1023u;
+  uint8_t* ring = smem_raw + (ring_s - raw);
+  uint8_t* qtile = ring + kRingBytes;
+  uint64_t* col_mask = reinterpret_cast<uint64_t*>(qtile + kQBytes);
+  uint64_t* bars = col_mask + kMaxCols;  // full[kStages], empty[kStages]
+  const uint32_t q_s = ring_s + kRingBytes;
+  const uint32_t bar_s = kyro::ptx::smem_addr(bars);
+
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      kyro::ptx::mbar_init(bar_s + 8 * s, 1);
+      kyro::ptx::mbar_init(bar_s + 8 * (kStages + s), kConsumers);
+    }
+    kyro::ptx::fence_barrier_init();
+  }
+  // ---- Q rows of this work item -> padded smem tile; column masks
+  for (int i = tid; i < kMaxCols * (kD / 8); i += kThreads) {
+    const int col = i / (kD / 8), ch = i % (kD / 8);
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (col < ncols) {
+      const int r = col0 + col, j = r / a.group, gi = r % a.group;
+      const int h = kvh * a.group + gi;
+      v = *reinterpret_cast<const uint4*>(q + (((int64_t)b * a.nq + j) * a.hq + h) * kD + ch * 8);
+    }
+    *reinterpret_cast<uint4*>(qtile + col * kQStride * 2 + ch * 16) = v;
+  }
+  for (int col = tid; col < kMaxCols; col += kThreads) {
+    uint64_t m = 0;
+    if (col < ncols) {
+      const int j = (col0 + col) / a.group;
+      m = tree_mask ? tree_mask[(int64_t)b * a.nq + j]
+                    : (j >= 63 ? ~0ull : ((1ull << (j + 1)) - 1ull));
+    }
+    col_mask[col] = m;
+  }
+  __syncthreads();
+
+  bool timed_out = false;
+  if (warp == kConsumers) {
+    // ================= producer
+    if (lane == 0) {
+      kyro::ptx::prefetch_tensormap(&tmK);
+      kyro::ptx::prefetch_tensormap(&tmV);
+      const int64_t* bt = block_table + (int64_t)b * a.max_blocks;
+      for (int it = 0; it < niter; ++it) {
+        const int s = it % kStages;
+        if (it >= kStages && !timed_out) {
+          if (!kyro::ptx::mbar_wait_bounded(bar_s + 8 * (kStages + s), ((it / kStages) - 1) & 1,
+                                            kyro::dev::kWaitBudgetCycles)) {
+            timed_out = true;
+            kyro::dev::flag(status, KYRO_DEV_WAIT_TIMEOUT);
+          }
+        }
+        const int nvalid = min(kConsumers, blk1 - blk0 - it * kConsumers);
+        const uint32_t full = bar_s + 8 * s;
+        kyro::ptx::mbar_arrive_expect_tx(full, (uint32_t)(nvalid * kSlotBytes));
+        for (int w = 0; w < nvalid; ++w) {
+          int64_t phys = bt[blk0 + it * kConsumers + w];
+          if (phys < 0 || phys >= a.num_blocks) {
+            kyro::dev::flag(status, KYRO_DEV_BAD_BLOCK);
+            phys = 0;
+          }
+          const int32_t y = (int32_t)((phys * a.hkv + kvh) * kBS);
+          const uint32_t dst = ring_s + s * kStageBytes + w * kSlotBytes;
+#pragma unroll
+          for (int half = 0; half < kD / 64; ++half) {
+            kyro::ptx::tma_load_2d(dst + half * 2048, &tmK, half * 64, y, full);
+            kyro::ptx::tma_load_2d(dst + kTileBytes + half * 2048, &tmV, half * 64, y, full);
+          }
+        }
+      }
+    }
+    __syncwarp();
+  }
+
+  // ================= consumers
+  float o[kMT][NT][4];
+  float m_run[NT][2], l_run[NT][2];
+  if (warp < kConsumers) {
+#pragma unroll
+    for (int mt = 0; mt < kMT; ++mt)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o[mt][nt][e] = 0.0f;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      m_run[nt][0] = m_run[nt][1] = -INFINITY;
+      l_run[nt][0] = l_run[nt][1] = 0.0f;
+    }
+    const int g8 = lane >> 3, r8 = lane & 7;
+    for (int it = 0; it < niter; ++it) {
+      const int s = it % kStages;
+      if (!timed_out) {
+        if (!kyro::ptx::mbar_wait_bounded(bar_s + 8 * s, (it / kStages) & 1,
+                                          kyro::dev::kWaitBudgetCycles)) {
+          timed_out = true;
+          kyro::dev::flag(status, KYRO_DEV_WAIT_TIMEOUT);
+        }
+      }
+      const int blk = blk0 + it * kConsumers + warp;
+      if (blk < blk1) {
+        const uint32_t ks = ring_s + s * kStageBytes + warp * kSlotBytes;
+        const uint32_t vs = ks + kTileBytes;
+        // ---- S^T = K Q^T
+        float sc[NT][4];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) sc[nt][e] = 0.0f;
+#pragma unroll
+        for (int kk = 0; kk < kKK; kk += 2) {
+          uint32_t qb[NT][4];
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+            kyro::ptx::ldsm_x4(q_s + (uint32_t)((nt * 8 + r8) * kQStride * 2 + (2 * kk + g8) * 16),
+                               qb[nt][0], qb[nt][1], qb[nt][2], qb[nt][3]);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            uint32_t a0, a1, a2, a3;
+            // matrices: (tokens 0-7 | 8-15) x (dims lo | hi) of k-step kk+h
+            kyro::ptx::ldsm_x4(ks + kv_off((g8 & 1) * 8 + r8, 2 * (kk + h) + (g8 >> 1)), a0, a1,
+                               a2, a3);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+              kyro::ptx::mma_bf16_16816(sc[nt], a0, a1, a2, a3, qb[nt][2 * h], qb[nt][2 * h + 1]);
+          }
+        }
+        // ---- scale, mask, online softmax (per query column)
+        const int64_t tok0 = (int64_t)blk * kBS;
+        const bool need_mask = tok0 + kBS > ctx;
+        const int trow = lane >> 2;
+        uint32_t pb[NT][2];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float v = sc[nt][e] * a.scale_log2;
+            if (need_mask) {
+              const int64_t t = tok0 + trow + (e >> 1) * 8;
+              const int col = nt * 8 + 2 * (lane & 3) + (e & 1);
+              const int64_t rel = t - ctx;
+              const bool ok = t < ctx || (rel < a.nq && ((col_mask[col] >> rel) & 1ull));
+              if (!ok) v = -INFINITY;
+            }
+            sc[nt][e] = v;
+          }
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            float cm = fmaxf(sc[nt][c], sc[nt][c + 2]);
+            cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 4));
+            cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 8));
+            cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 16));
+            const float m_new = fmaxf(m_run[nt][c], cm);
+            const float m_use = m_new == -INFINITY ? 0.0f : m_new;
+            const float alpha = kyro::ptx::fast_exp2(m_run[nt][c] - m_use);
+            const float p0 = kyro::ptx::fast_exp2(sc[nt][c] - m_use);
+            const float p1 = kyro::ptx::fast_exp2(sc[nt][c + 2] - m_use);
+            sc[nt][c] = p0;
+            sc[nt][c + 2] = p1;
+            l_run[nt][c] = l_run[nt][c] * alpha + p0 + p1;
+            m_run[nt][c] = m_new;
+#pragma unroll
+            for (int mt = 0; mt < kMT; ++mt) {
+              o[mt][nt][c] *= alpha;
+              o[mt][nt][c + 2] *= alpha;
+            }
+          }
+          // P^T fragment (tokens x cols) -> B operand (k = tokens, n = cols)
+          pb[nt][0] = kyro::ptx::movmatrix_trans(kyro::ptx::pack_bf16x2(sc[nt][0], sc[nt][1]));
+          pb[nt][1] = kyro::ptx::movmatrix_trans(kyro::ptx::pack_bf16x2(sc[nt][2], sc[nt][3]));
+        }
+        // ---- O^T += V^T P^T
+#pragma unroll
+        for (int mt = 0; mt < kMT; ++mt) {
+          uint32_t a0, a1, a2, a3;
+          // matrices: (tokens 0-7 | 8-15) x (dims 16mt.. | 16mt+8..), transposed
+          kyro::ptx::ldsm_x4_trans(vs + kv_off((g8 >> 1) * 8 + r8, 2 * mt + (g8 & 1)), a0, a1, a2,
+                                   a3);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+            kyro::ptx::mma_bf16_16816(o[mt][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) kyro::ptx::mbar_arrive(bar_s + 8 * (kStages + s));
+    }
+    // reduce the per-thread partial sums over the 8 lanes sharing a column
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        float l = l_run[nt][c];
+        l += __shfl_xor_sync(0xffffffffu, l, 4);
+        l += __shfl_xor_sync(0xffffffffu, l, 8);
+        l += __shfl_xor_sync(0xffffffffu, l, 16);
+        l_run[nt][c] = l;
+      }
+  }
+  __syncthreads();  // every TMA has landed and every consumer is done with the ring
+
+  // ---- merge the four consumer warps in shared memory
+  float* mo = reinterpret_cast<float*>(ring);           // [warp][d][col]
+  float* mm = mo + kConsumers * kD * kMaxCols;          // [warp][col]
+  float* ml = mm + kConsumers * kMaxCols;               // [warp][col]
+  if (warp < kConsumers) {
+    float* wo = mo + warp * kD * kMaxCols;
+#pragma unroll
+    for (int mt = 0; mt < kMT; ++mt)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int d = mt * 16 + (lane >> 2) + (e >> 1) * 8;
+          const int col = nt * 8 + 2 * (lane & 3) + (e & 1);
+          wo[d * kMaxCols + col] = o[mt][nt][e];
+        }
+    if (lane < 4) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const int col = nt * 8 + 2 * lane + c;
+          mm[warp * kMaxCols + col] = m_run[nt][c];
+          ml[warp * kMaxCols + col] = l_run[nt][c];
+        }
+    }
+  }
+  __syncthreads();
+  const bool single = nsplit == 1;
+  const int64_t item = ((int64_t)b * a.hkv + kvh) * a.ngroups + grp;
+  float* po = part_o + (item * a.max_splits + split) * (kMaxCols * kD);
+  float* pml = part_ml + (item * a.max_splits + split) * (kMaxCols * 2);
+  for (int i = tid; i < ncols * kD; i += kThreads) {
+    const int col = i / kD, d = i % kD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kConsumers; ++w) M = fmaxf(M, mm[w * kMaxCols + col]);
+    const float Mu = M == -INFINITY ? 0.0f : M;
+    float L = 0.0f, O = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kConsumers; ++w) {
+      const float f = kyro::ptx::fast_exp2(mm[w * kMaxCols + col] - Mu);
+      L += f * ml[w * kMaxCols + col];
+      O += f * mo[(w * kD + d) * kMaxCols + col];
+    }
+    if (single) {
+      const int r = col0 + col, j = r / a.group, gi = r % a.group;
+      const int h = kvh * a.group + gi;
+      out[(((int64_t)b * a.nq + j) * a.hq + h) * kD + d] = __float2bfloat16(L > 0.0f ? O / L : 0.0f);
+    } else {
+      po[col * kD + d] = O;
+      if (d == 0) {
+        pml[col * 2 + 0] = M;
+        pml[col * 2 + 1] = L;
+      }
+    }
+  }
+}
+
+// Combine the splits of every (sequence, KV head, row group) with more than one.
+template <int kD>
+__global__ void __launch_bounds__(256)
+verify_attention_merge_kernel(const int64_t* __restrict__ context_lens,
+                              const float* __restrict__ part_o, const float* __restrict__ part_ml,
+                              __nv_bfloat16* __restrict__ out, AttnArgs a) {
+  const int64_t item = blockIdx.x;
+  const int grp = (int)(item % a.ngroups);
+  const int kvh = (int)((item / a.ngroups) % a.hkv);
+  const int b = (int)(item / ((int64_t)a.ngroups * a.hkv));
+  const int64_t ctx = context_lens[b];
+  const int64_t total = ctx + a.nq;
+  if (ctx < 0 || (total + kBS - 1) / kBS > a.max_blocks) return;
+  const int nblk = (int)((total + kBS - 1) / kBS);
+  const int nsplit = (nblk + a.split_blocks - 1) / a.split_blocks;
+  if (nsplit <= 1) return;
+  const int col0 = grp * kMaxCols;
+  const int ncols = min(kMaxCols, a.rows - col0);
+  const float* po = part_o + item * a.max_splits * (kMaxCols * kD);
+  const float* pml = part_ml + item * a.max_splits * (kMaxCols * 2);
+  for (int i = threadIdx.x; i < ncols * kD; i += blockDim.x) {
+    const int col = i / kD, d = i % kD;
+    float M = -INFINITY;
+    for (int s = 0; s < nsplit; ++s) M = fmaxf(M, pml[(s * kMaxCols + col) * 2]);
+    const float Mu = M == -INFINITY ? 0.0f : M;
+    float L = 0.0f, O = 0.0f;
+    for (int s = 0; s < nsplit; ++s) {
+      const float f = kyro::ptx::fast_exp2(pml[(s * kMaxCols + col) * 2] - Mu);
+      L += f * pml[(s * kMaxCols + col) * 2 + 1];
+      O += f * po[(s * kMaxCols + col) * kD + d];
+    }
+    const int r = col0 + col, j = r / a.group, gi = r % a.group;
+    const int h = kvh * a.group + gi;
+    out[(((int64_t)b * a.nq + j) * a.hq + h) * kD + d] = __float2bfloat16(L > 0.0f ? O / L : 0.0f);
+  }
+}
+
+// ------------------------------------------------------------------ host
+
+}  // namespace
+
+#include <mutex>
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+int make_kv_map(CUtensorMap* map, const void* base, int64_t rows, int kD) {
+  auto encode = get_encode_fn();
+  if (!encode) return kyro::set_error(KYRO_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)kD, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)kD * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)kBS};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
+                      strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return kyro::set_error(KYRO_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return KYRO_OK;
+}
+
+struct Plan {
+  AttnArgs a;
+  int nt;
+  size_t part_o_bytes, part_ml_bytes;
+};
+
+int plan(const kyro_attn_params* p, int num_sms, Plan* out) {
+  KY_REQUIRE(p, "kyro_verify_attention: params is NULL");
+  KY_REQUIRE(p->batch >= 0, "kyro_verify_attention: batch = %d", p->batch);
+  KY_REQUIRE(p->num_query >= 1 && p->num_query <= 64,
+             "kyro_verify_attention: num_query = %d (1..64)", p->num_query);
+  KY_REQUIRE(p->head_dim == 64 || p->head_dim == 128,
+             "kyro_verify_attention: head_dim = %d (64 or 128 supported)", p->head_dim);
+  KY_REQUIRE(p->block_size == kBS, "kyro_verify_attention: block_size = %d (only %d supported)",
+             p->block_size, kBS);
+  KY_REQUIRE(p->num_heads > 0 && p->num_kv_heads > 0 && p->num_heads % p->num_kv_heads == 0,
+             "kyro_verify_attention: num_heads %d not a multiple of num_kv_heads %d",
+             p->num_heads, p->num_kv_heads);
+  KY_REQUIRE(p->max_blocks_per_seq > 0, "kyro_verify_attention: max_blocks_per_seq = %d",
+             p->max_blocks_per_seq);
+  KY_REQUIRE(p->num_blocks > 0, "kyro_verify_attention: num_blocks = %d", p->num_blocks);
+  KY_REQUIRE((int64_t)p->num_blocks * p->num_kv_heads * kBS < (1ll << 31),
+             "kyro_verify_attention: cache too large for 32-bit TMA rows");
+  KY_REQUIRE(p->kv_split_blocks >= 0, "kyro_verify_attention: kv_split_blocks = %d",
+             p->kv_split_blocks);
+  Plan pl;
+  AttnArgs& a = pl.a;
+  a.B = p->batch;
+  a.nq = p->num_query;
+  a.hq = p->num_heads;
+  a.hkv = p->num_kv_heads;
+  a.group = p->num_heads / p->num_kv_heads;
+  a.rows = a.group * a.nq;
+  a.ngroups = (a.rows + kMaxCols - 1) / kMaxCols;
+  a.max_blocks = p->max_blocks_per_seq;
+  a.num_blocks = p->num_blocks;
+  const float scale = p->scale > 0.0f ? p->scale : 1.0f / sqrtf((float)p->head_dim);
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.d = p->head_dim;
+  int split = p->kv_split_blocks;
+  if (split == 0) {
+    // aim for about four waves of work items at two CTAs per SM, assuming
+    // half the table width is used on average
+    const int64_t items = (int64_t)a.B * a.hkv * a.ngroups;
+    const int64_t avg_blocks = (a.max_blocks + 1) / 2;
+    const int64_t target = (int64_t)num_sms * 2 * 4;
+    int64_t s = (items * avg_blocks + target - 1) / (target > 0 ? target : 1);
+    s = (s + kConsumers - 1) / kConsumers * kConsumers;
+    if (s < 16) s = 16;
+    split = (int)s;
+  }
+  a.split_blocks = split;
+  a.max_splits = (a.max_blocks + split - 1) / split;
+  pl.nt = a.rows >= kMaxCols ? 4 : (a.rows + 7) / 8;
+  const int64_t items = (int64_t)a.B * a.hkv * a.ngroups * (a.max_splits > 1 ? a.max_splits : 0);
+  pl.part_o_bytes = (size_t)items * kMaxCols * p->head_dim * 4;
+  pl.part_ml_bytes = (size_t)items * kMaxCols * 2 * 4;
+  *out = pl;
+  return KYRO_OK;
+}
+
+size_t ws_bytes(const Plan& pl) {
+  return ((pl.part_o_bytes + 255) & ~size_t(255)) + ((pl.part_ml_bytes + 255) & ~size_t(255));
+}
+
+template <int NT, int D>
+void launch(const Plan& pl, dim3 grid, cudaStream_t st, const CUtensorMap& mk, const CUtensorMap& mv,
+            const void* q, const int64_t* bt, const int64_t* cl, const uint64_t* tm, void* out,
+            float* po, float* pml, uint32_t* status) {
+  cudaFuncSetAttribute(verify_attention_kernel<NT, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       Geo<D>::kSmemBytes);
+  verify_attention_kernel<NT, D><<<grid, kThreads, Geo<D>::kSmemBytes, st>>>(
+      mk, mv, (const __nv_bfloat16*)q, bt, cl, tm, (__nv_bfloat16*)out, po, pml, pl.a, status);
+}
+
+template <int D>
+void launch_d(const Plan& pl, dim3 grid, cudaStream_t st, const CUtensorMap& mk,
+              const CUtensorMap& mv, const void* q, const int64_t* bt, const int64_t* cl,
+              const uint64_t* tm, void* out, float* po, float* pml, uint32_t* status) {
+  switch (pl.nt) {
+    case 1: launch<1, D>(pl, grid, st, mk, mv, q, bt, cl, tm, out, po, pml, status); break;
+    case 2: launch<2, D>(pl, grid, st, mk, mv, q, bt, cl, tm, out, po, pml, status); break;
+    case 3: launch<3, D>(pl, grid, st, mk, mv, q, bt, cl, tm, out, po, pml, status); break;
+    default: launch<4, D>(pl, grid, st, mk, mv, q, bt, cl, tm, out, po, pml, status); break;
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t kyro_verify_attention_workspace_size(const kyro_attn_params* p) {
+  Plan pl;
+  if (plan(p, 148, &pl) != KYRO_OK) return 0;
+  return ws_bytes(pl);
+}
+
+int kyro_verify_attention(kyro_ctx* ctx, const kyro_attn_params* p, const void* q,
+                          const void* k_cache, const void* v_cache, const int64_t* block_table,
+                          const int64_t* context_lens, const uint64_t* tree_mask, void* out,
+                          void* workspace, size_t workspace_bytes) {
+  KY_TRY(kyro::enter(ctx));
+  Plan pl;
+  // plan with the SM count the workspace size was computed for, so that
+  // kyro_verify_attention_workspace_size() and this call agree
+  KY_TRY(plan(p, 148, &pl));
+  if (p->batch == 0) return KYRO_OK;
+  KY_REQUIRE(q && k_cache && v_cache && block_table && context_lens && out,
+             "kyro_verify_attention: a required pointer is NULL");
+  KY_REQUIRE((uintptr_t)k_cache % 16 == 0 && (uintptr_t)v_cache % 16 == 0 &&
+                 (uintptr_t)q % 16 == 0,
+             "kyro_verify_attention: q and the caches must be 16-byte aligned");
+  const size_t need = ws_bytes(pl);
+  if (need > 0 && (workspace_bytes < need || !workspace))
+    return kyro::set_error(KYRO_ERR_WORKSPACE, "kyro_verify_attention: workspace %zu < %zu bytes",
+                           workspace_bytes, need);
+  float* po = (float*)workspace;
+  float* pml = (float*)((char*)workspace + ((pl.part_o_bytes + 255) & ~size_t(255)));
+  CUtensorMap mk, mv;
+  const int64_t rows = (int64_t)p->num_blocks * p->num_kv_heads * kBS;
+  KY_TRY(make_kv_map(&mk, k_cache, rows, p->head_dim));
+  KY_TRY(make_kv_map(&mv, v_cache, rows, p->head_dim));
+  dim3 grid((unsigned)pl.a.max_splits, (unsigned)(pl.a.hkv * pl.a.ngroups), (unsigned)pl.a.B);
+  KY_REQUIRE(pl.a.B <= 65535, "kyro_verify_attention: batch %d > 65535", pl.a.B);
+  cudaStream_t st = ctx->stream;
+  if (p->head_dim == 128)
+    launch_d<128>(pl, grid, st, mk, mv, q, block_table, context_lens, tree_mask, out, po, pml,
+                  ctx->d_status);
+  else
+    launch_d<64>(pl, grid, st, mk, mv, q, block_table, context_lens, tree_mask, out, po, pml,
+                 ctx->d_status);
+  KY_TRY(kyro::check_launch("verify_attention_kernel"));
+  if (pl.a.max_splits > 1) {
+    const int64_t items = (int64_t)pl.a.B * pl.a.hkv * pl.a.ngroups;
+    if (p->head_dim == 128)
+      verify_attention_merge_kernel<128><<<(unsigned)items, 256, 0, st>>>(context_lens, po, pml,
+                                                                         (__nv_bfloat16*)out, pl.a);
+    else
+      verify_attention_merge_kernel<64><<<(unsigned)items, 256, 0, st>>>(context_lens, po, pml,
+                                                                        (__nv_bfloat16*)out, pl.a);
+    KY_TRY(kyro::check_launch("verify_attention_merge_kernel"));
+  }
+  return KYRO_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,84 @@
+// kyro_internal.cuh -- shared plumbing of the sm_100a verify-step library:
+// the context object, host-side error reporting, device status word and
+// small device helpers (warp reductions, bounded mbarrier waits).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "../../include/kyro_spec.h"
+
+struct kyro_ctx {
+  int device;
+  cudaStream_t stream;
+  uint32_t* d_status;  // KYRO_DEV_* bits, atomically OR-ed by kernels
+  int num_sms;
+};
+
+namespace kyro {
+
+// Record `msg` as the calling thread's last error and return `status`.
+int set_error(int status, const char* fmt, ...);
+// Map a CUDA error to KYRO_ERR_CUDA with a message naming `what`.
+int cuda_error(cudaError_t err, const char* what);
+// Check for a launch error right after enqueueing kernels.
+int check_launch(const char* what);
+// Validate a context and make its device current.
+int enter(kyro_ctx* ctx);
+
+}  // namespace kyro
+
+#define KY_REQUIRE(cond, ...)                                       \
+  do {                                                              \
+    if (!(cond)) return kyro::set_error(KYRO_ERR_INVALID_ARG, __VA_ARGS__); \
+  } while (0)
+
+#define KY_TRY(expr)              \
+  do {                            \
+    int _st = (expr);             \
+    if (_st != KYRO_OK) return _st; \
+  } while (0)
+
+// ---------------------------------------------------------------- device
+namespace kyro {
+namespace dev {
+
+__device__ __forceinline__ void flag(uint32_t* status, uint32_t bits) {
+  if (status) atomicOr(status, bits);
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ unsigned long long warp_sum_u64(unsigned long long v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// max value, lowest index among equal maxima
+__device__ __forceinline__ void warp_argmax(float& v, int& idx) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float ov = __shfl_xor_sync(0xffffffffu, v, o);
+    int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+    if (ov > v || (ov == v && oi < idx)) {
+      v = ov;
+      idx = oi;
+    }
+  }
+}
+
+// Upper bound on the clock cycles any single device-side wait may take
+// before the kernel records KYRO_DEV_WAIT_TIMEOUT and moves on (~1 s).
+constexpr long long kWaitBudgetCycles = 2000000000ll;
+
+}  // namespace dev
+}  // namespace kyro

@@ -1,0 +1,259 @@
+/*
+ * kyro_math.h -- arithmetic shared bit-for-bit by the sm_100a kernels and the
+ * CPU oracle of the speculative verify step.
+ *
+ * The reference verifier (src/speculative.rs:286-339) and sampler
+ * (src/worker.rs:267-362) draw from an unseeded thread RNG and use candle's
+ * softmax, so nothing in the reference fixes the random numbers or the
+ * summation order.  This header fixes both, so that a CPU restatement and the
+ * GPU kernels make identical accept/reject decisions and emit identical
+ * tokens on identical inputs:
+ *
+ *   1. Philox4x32-10 counter-based uniforms (Salmon, Moraes, Dror, Shaw,
+ *      "Parallel Random Numbers: As Easy as 1, 2, 3", SC'11), written from
+ *      the paper: S-box multipliers 0xD2511F53 / 0xCD9E8D57, Weyl key bumps
+ *      0x9E3779B9 / 0xBB67AE85, ten rounds.
+ *      counter = (sequence, position, stream, step), key = seed.
+ *      Streams: 0 draft sampling, 1 accept test, 2 resample / bonus token.
+ *   2. ky_exp(): an fp32 exponential for x <= 0 built from basic IEEE
+ *      operations only (round-to-nearest fma/mul/add), so host and device
+ *      produce the same bits.  Cody-Waite reduction x = n*ln2 + r,
+ *      |r| <= ln2/2, then a degree-6 polynomial whose coefficients were
+ *      fitted for this project by iterated weighted least squares on
+ *      [-ln2/2, ln2/2] (max relative error 1.9e-9 before rounding).
+ *      Inputs below -87 (and NaN) return 0; ky_exp(0) == 1 exactly.
+ *   3. Exact fixed-point accumulation.  Softmax mass is summed as integers:
+ *      fix40(e) = floor(e * 2^40) for e in [0,1] and fix62(w) = floor(w * 2^62)
+ *      for w in [0,2).  Integer sums do not depend on the order in which a
+ *      kernel adds them, so the inverse-CDF cut point is reproducible.
+ *   4. The inverse-CDF threshold: with a uniform u = odd * 2^-24 and integer
+ *      total mass W, the sampled index is the smallest i whose inclusive
+ *      prefix C_i satisfies u*W <= C_i, i.e. C_i >= ceil(odd*W / 2^24).
+ *      This is the exact form of worker.rs:352-360 ("r -= p; if r <= 0").
+ *
+ * This header compiles as C11 (oracle, gcc) and as CUDA C++ (nvcc).
+ */
+#ifndef KYRO_MATH_H
+#define KYRO_MATH_H
+
+#include <stdint.h>
+
+#if defined(__CUDACC__)
+#define KY_HD __host__ __device__ __forceinline__
+#else
+#include <math.h>
+#include <string.h>
+#define KY_HD static inline
+#endif
+
+/* Round-to-nearest IEEE operations that the compiler may not contract or
+ * reassociate.  Host code including this header is compiled with
+ * -ffp-contract=off; device code uses the _rn intrinsics, which nvcc never
+ * fuses. */
+#if defined(__CUDA_ARCH__)
+#define KY_FMAF(a, b, c) __fmaf_rn((a), (b), (c))
+#define KY_FMUL(a, b) __fmul_rn((a), (b))
+#define KY_FADD(a, b) __fadd_rn((a), (b))
+#define KY_FSUB(a, b) __fsub_rn((a), (b))
+#define KY_FDIV(a, b) __fdiv_rn((a), (b))
+#define KY_DMUL(a, b) __dmul_rn((a), (b))
+#define KY_DADD(a, b) __dadd_rn((a), (b))
+#define KY_DDIV(a, b) __ddiv_rn((a), (b))
+#else
+#define KY_FMAF(a, b, c) fmaf((a), (b), (c))
+#define KY_FMUL(a, b) ((float)(a) * (float)(b))
+#define KY_FADD(a, b) ((float)(a) + (float)(b))
+#define KY_FSUB(a, b) ((float)(a) - (float)(b))
+#define KY_FDIV(a, b) ((float)(a) / (float)(b))
+#define KY_DMUL(a, b) ((double)(a) * (double)(b))
+#define KY_DADD(a, b) ((double)(a) + (double)(b))
+#define KY_DDIV(a, b) ((double)(a) / (double)(b))
+#endif
+
+KY_HD uint32_t ky_f2u(float f) {
+#if defined(__CUDA_ARCH__)
+  return __float_as_uint(f);
+#else
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  return u;
+#endif
+}
+
+KY_HD float ky_u2f(uint32_t u) {
+#if defined(__CUDA_ARCH__)
+  return __uint_as_float(u);
+#else
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
+#endif
+}
+
+/* ------------------------------------------------------------------ */
+/* Philox4x32-10                                                        */
+/* ------------------------------------------------------------------ */
+#define KY_PHILOX_M0 0xD2511F53u
+#define KY_PHILOX_M1 0xCD9E8D57u
+#define KY_PHILOX_W0 0x9E3779B9u
+#define KY_PHILOX_W1 0xBB67AE85u
+
+enum {
+  KY_STREAM_DRAFT = 0,   /* sampling a draft token from q          */
+  KY_STREAM_ACCEPT = 1,  /* the accept test u < p(x)/q(x)           */
+  KY_STREAM_RESAMPLE = 2 /* residual resample or bonus token        */
+};
+
+KY_HD void ky_mulhilo32(uint32_t a, uint32_t b, uint32_t* hi, uint32_t* lo) {
+#if defined(__CUDA_ARCH__)
+  *hi = __umulhi(a, b);
+  *lo = a * b;
+#else
+  uint64_t p = (uint64_t)a * (uint64_t)b;
+  *hi = (uint32_t)(p >> 32);
+  *lo = (uint32_t)p;
+#endif
+}
+
+/* Ten rounds of Philox4x32 on counter c[0..3] with key (k0, k1). */
+KY_HD void ky_philox4x32_10(const uint32_t c_in[4], uint32_t k0, uint32_t k1, uint32_t out[4]) {
+  uint32_t c0 = c_in[0], c1 = c_in[1], c2 = c_in[2], c3 = c_in[3];
+  for (int round = 0; round < 10; ++round) {
+    uint32_t hi0, lo0, hi1, lo1;
+    ky_mulhilo32(KY_PHILOX_M0, c0, &hi0, &lo0);
+    ky_mulhilo32(KY_PHILOX_M1, c2, &hi1, &lo1);
+    uint32_t n0 = hi1 ^ c1 ^ k0;
+    uint32_t n2 = hi0 ^ c3 ^ k1;
+    c0 = n0;
+    c1 = lo1;
+    c2 = n2;
+    c3 = lo0;
+    k0 += KY_PHILOX_W0;
+    k1 += KY_PHILOX_W1;
+  }
+  out[0] = c0;
+  out[1] = c1;
+  out[2] = c2;
+  out[3] = c3;
+}
+
+/* The odd 24-bit numerator of a uniform in (0,1): u = odd * 2^-24, with
+ * odd = 2*(x>>9)+1 taken from the first Philox output word. u is exactly
+ * representable in fp32 and never 0 or 1. */
+KY_HD uint32_t ky_uniform_odd(uint64_t seed, uint32_t seq, uint32_t pos, uint32_t stream,
+                              uint32_t step) {
+  uint32_t c[4] = {seq, pos, stream, step};
+  uint32_t o[4];
+  ky_philox4x32_10(c, (uint32_t)seed, (uint32_t)(seed >> 32), o);
+  return ((o[0] >> 9) << 1) | 1u;
+}
+
+KY_HD float ky_odd_to_float(uint32_t odd) { return KY_FMUL((float)odd, 0x1p-24f); }
+
+/* ------------------------------------------------------------------ */
+/* exp for x <= 0                                                       */
+/* ------------------------------------------------------------------ */
+#define KY_LOG2E 0x1.715476p+0f
+#define KY_LN2_HI 0x1.62e430p-1f /* ln2 rounded to fp32                 */
+#define KY_LN2_LO -0x1.05c610p-29f /* ln2 - KY_LN2_HI rounded to fp32   */
+#define KY_RND_MAGIC 12582912.0f   /* 1.5 * 2^23                         */
+#define KY_EXP_C0 0x1.000000p+0f
+#define KY_EXP_C1 0x1.000000p+0f
+#define KY_EXP_C2 0x1.fffffap-2f
+#define KY_EXP_C3 0x1.55540ap-3f
+#define KY_EXP_C4 0x1.55589cp-5f
+#define KY_EXP_C5 0x1.126d66p-7f
+#define KY_EXP_C6 0x1.6ab91ep-10f
+
+KY_HD float ky_exp(float x) {
+  if (!(x >= -87.0f)) return 0.0f; /* also maps NaN and -inf to 0 */
+  /* t = rint(x*log2e) + 1.5*2^23: the integer lands in the low mantissa bits */
+  float t = KY_FMAF(x, KY_LOG2E, KY_RND_MAGIC);
+  int32_t n = (int32_t)ky_f2u(t) - (int32_t)0x4B400000;
+  float nf = KY_FSUB(t, KY_RND_MAGIC);
+  float r = KY_FMAF(-nf, KY_LN2_HI, x);
+  r = KY_FMAF(-nf, KY_LN2_LO, r);
+  float p = KY_EXP_C6;
+  p = KY_FMAF(p, r, KY_EXP_C5);
+  p = KY_FMAF(p, r, KY_EXP_C4);
+  p = KY_FMAF(p, r, KY_EXP_C3);
+  p = KY_FMAF(p, r, KY_EXP_C2);
+  p = KY_FMAF(p, r, KY_EXP_C1);
+  p = KY_FMAF(p, r, KY_EXP_C0);
+  /* n in [-126, 0] for x in [-87, 0], so 2^n is a normal number */
+  float scale = ky_u2f((uint32_t)(n + 127) << 23);
+  return KY_FMUL(p, scale);
+}
+
+/* ------------------------------------------------------------------ */
+/* fixed point                                                          */
+/* ------------------------------------------------------------------ */
+/* floor(e * 2^40) for e in [0, 1]; at most 2^40. */
+KY_HD uint64_t ky_fix40(float e) {
+#if defined(__CUDA_ARCH__)
+  return __float2ull_rz(KY_FMUL(e, 0x1p40f));
+#else
+  return (uint64_t)KY_FMUL(e, 0x1p40f);
+#endif
+}
+
+/* floor(w * 2^62) for w in [0, 2). */
+KY_HD uint64_t ky_fix62(float w) {
+#if defined(__CUDA_ARCH__)
+  return __float2ull_rz(KY_FMUL(w, 0x1p62f));
+#else
+  return (uint64_t)KY_FMUL(w, 0x1p62f);
+#endif
+}
+
+/* ceil(odd * W / 2^24): the smallest inclusive prefix C_i >= this value
+ * marks the sampled index.  1 <= result <= W whenever W >= 1. */
+KY_HD uint64_t ky_cdf_threshold(uint32_t odd, uint64_t W) {
+  unsigned __int128 p = (unsigned __int128)odd * (unsigned __int128)W;
+  p += (unsigned __int128)((1u << 24) - 1u);
+  return (uint64_t)(p >> 24);
+}
+
+/* ------------------------------------------------------------------ */
+/* softmax normaliser contract                                          */
+/* ------------------------------------------------------------------ */
+/* A vocabulary row is split into shards (tensor-parallel ranks; one shard
+ * without TP), and each shard into chunks of KY_CHUNK consecutive entries
+ * starting at the shard start (the last chunk may be short).  With
+ * s_i = z_i * inv_t:
+ *   m_c = max_{i in c} s_i,  e_i = ky_exp(s_i - m_c),  E_c = sum fix40(e_i)
+ *   M   = max_c m_c
+ *   S   = sum over shards r (in rank order) of
+ *           sum over chunks c of r (in chunk order) of E_c*2^-40 * ky_exp(m_c - M)
+ *         (double precision, each partial sum starting from 0.0)
+ *   g_c = (float)(ky_exp(m_c - M) / S)        (double division)
+ *   p_i = e_i * g_c                           (fp32)
+ * The same row statistics drive the accept test, the residual and the
+ * bonus sample. */
+#define KY_CHUNK 2048
+
+/* inv_t for temperature t > 0: (float)(1/(double)t); candle's `tensor / t`
+ * (worker.rs:298) is an affine op multiplying by the reciprocal. */
+KY_HD float ky_inv_temperature(float t) { return (float)KY_DDIV(1.0, (double)t); }
+
+KY_HD double ky_chunk_mass(uint64_t E, float m_c, float M) {
+  return KY_DMUL((double)E * 0x1p-40, (double)ky_exp(KY_FSUB(m_c, M)));
+}
+
+KY_HD float ky_chunk_scale(float m_c, float M, double S) {
+  return (float)KY_DDIV((double)ky_exp(KY_FSUB(m_c, M)), S);
+}
+
+/* accept iff u < p/q (Leviathan et al. 2023, Alg. 1; u < min(1,p/q) since u < 1) */
+KY_HD int ky_accept(uint32_t odd, float p, float q) {
+  float ratio = KY_FDIV(p, q);
+  return ky_odd_to_float(odd) < ratio;
+}
+
+/* residual weight max(p - q, 0) in fix62 */
+KY_HD uint64_t ky_residual_w(float p, float q) {
+  float d = KY_FSUB(p, q);
+  return d > 0.0f ? ky_fix62(d) : 0ull;
+}
+
+#endif /* KYRO_MATH_H */

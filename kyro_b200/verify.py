@@ -1,0 +1,288 @@
+"""Host-side operators of the speculative verify step, over the C ABI.
+
+Each function validates its tensors, then calls one entry point of
+include/kyro_spec.h through ctypes on the current torch CUDA stream.  torch
+supplies device memory and streams only; all computation happens in the
+sm_100a kernels of libkyro_spec.so.  There is no CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from typing import Optional, Sequence
+
+import torch
+
+from . import _lib
+from ._lib import (ACCEPT_GREEDY, ACCEPT_GREEDY_REF, ACCEPT_STOCHASTIC, AcceptParams, AttnParams,
+                   KVParams, SampleParams, check)
+
+__all__ = [
+    "Context", "spec_accept", "sample_tokens", "verify_attention", "kv_reserve", "kv_commit",
+    "kv_commit_tree", "kv_write", "philox_uniforms", "ACCEPT_STOCHASTIC", "ACCEPT_GREEDY", "ACCEPT_GREEDY_REF",
+]
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def _need(t: torch.Tensor, name: str, dtype, device, ndim=None):
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    if t.device != device:
+        raise ValueError(f"{name} must be on {device}, got {t.device}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    if ndim is not None and t.dim() != ndim:
+        raise ValueError(f"{name} must have {ndim} dims, got shape {tuple(t.shape)}")
+
+
+class Context:
+    """One kyro_ctx per GPU: the device, the stream kernels go to, and a
+    cached workspace buffer.  Calls enqueue on torch's current stream."""
+
+    def __init__(self, device: Optional[int] = None):
+        L = _lib.load()
+        if device is None:
+            device = torch.cuda.current_device()
+        self.device = torch.device("cuda", device)
+        self.index = device
+        h = C.c_void_p()
+        with torch.cuda.device(device):
+            stream = torch.cuda.current_stream(device).cuda_stream
+            check(L.kyro_ctx_create(device, C.c_void_p(stream), C.byref(h)))
+        self._h = h
+        self._ws: Optional[torch.Tensor] = None
+
+    @property
+    def handle(self):
+        return self._h
+
+    def bind_stream(self):
+        stream = torch.cuda.current_stream(self.index).cuda_stream
+        check(_lib.load().kyro_ctx_set_stream(self._h, C.c_void_p(stream)))
+
+    def workspace(self, nbytes: int) -> torch.Tensor:
+        """A caller-owned scratch buffer of at least nbytes (grown on demand)."""
+        if nbytes <= 0:
+            nbytes = 256
+        if self._ws is None or self._ws.numel() < nbytes:
+            self._ws = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+        return self._ws
+
+    def device_status(self, clear: bool = True) -> int:
+        flags = C.c_uint32(0)
+        check(_lib.load().kyro_ctx_device_status(self._h, C.byref(flags), int(clear)))
+        return flags.value
+
+    def close(self):
+        if self._h is not None and self._h.value:
+            _lib.load().kyro_ctx_destroy(self._h)
+        self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def spec_accept(ctx: Context, target_logits: torch.Tensor, draft_logits: Optional[torch.Tensor],
+                draft_tokens: torch.Tensor, mode: int = ACCEPT_STOCHASTIC,
+                temperature: float = 1.0, seed: int = 0, step: int = 0, seq_offset: int = 0,
+                want_probs: bool = False, out=None, workspace: Optional[torch.Tensor] = None):
+    """kyro_spec_accept.  target_logits fp32 [B,k+1,V], draft_logits fp32 [B,k,V]
+    (stochastic mode), draft_tokens int32 [B,k].
+
+    Returns (accept_len [B], tokens [B,k+1], num_tokens [B], probs [B,k,2] or None).
+    """
+    dev = ctx.device
+    _need(target_logits, "target_logits", torch.float32, dev, 3)
+    B, k1, V = target_logits.shape
+    k = k1 - 1
+    _need(draft_tokens, "draft_tokens", torch.int32, dev)
+    if draft_tokens.numel() != B * k:
+        raise ValueError(f"draft_tokens must hold B*k = {B * k} entries")
+    if draft_logits is not None:
+        _need(draft_logits, "draft_logits", torch.float32, dev, 3)
+        if tuple(draft_logits.shape) != (B, k, V):
+            raise ValueError(f"draft_logits must be {(B, k, V)}, got {tuple(draft_logits.shape)}")
+    if out is None:
+        acc = torch.empty(B, dtype=torch.int32, device=dev)
+        toks = torch.empty(B, k + 1, dtype=torch.int32, device=dev)
+        num = torch.empty(B, dtype=torch.int32, device=dev)
+        probs = torch.empty(B, k, 2, dtype=torch.float32, device=dev) if want_probs else None
+    else:
+        acc, toks, num, probs = out
+    p = AcceptParams(B, k, V, mode, float(temperature), step & 0xFFFFFFFF,
+                     seed & 0xFFFFFFFFFFFFFFFF, seq_offset)
+    L = _lib.load()
+    need = L.kyro_spec_accept_workspace_size(C.byref(p))
+    ws = workspace if workspace is not None else ctx.workspace(need)
+    ctx.bind_stream()
+    check(L.kyro_spec_accept(ctx.handle, C.byref(p), _ptr(target_logits), _ptr(draft_logits),
+                             _ptr(draft_tokens), _ptr(acc), _ptr(toks), _ptr(num), _ptr(probs),
+                             _ptr(ws), ws.numel()))
+    return acc, toks, num, probs
+
+
+def sample_tokens(ctx: Context, logits: torch.Tensor, temperature: float, seed: int = 0,
+                  step: int = 0, seq_offset: int = 0, workspace: Optional[torch.Tensor] = None):
+    """kyro_sample_tokens.  logits fp32 [B,P,V] -> (tokens int32 [B,P], probs fp32 [B,P])."""
+    dev = ctx.device
+    _need(logits, "logits", torch.float32, dev, 3)
+    B, P, V = logits.shape
+    toks = torch.empty(B, P, dtype=torch.int32, device=dev)
+    probs = torch.empty(B, P, dtype=torch.float32, device=dev)
+    p = SampleParams(B, P, V, float(temperature), step & 0xFFFFFFFF, 0, seed & 0xFFFFFFFFFFFFFFFF,
+                     seq_offset)
+    L = _lib.load()
+    need = L.kyro_sample_workspace_size(C.byref(p))
+    ws = workspace if workspace is not None else ctx.workspace(need)
+    ctx.bind_stream()
+    check(L.kyro_sample_tokens(ctx.handle, C.byref(p), _ptr(logits), _ptr(toks), _ptr(probs),
+                               _ptr(ws), ws.numel()))
+    return toks, probs
+
+
+def attn_params(q: torch.Tensor, k_cache: torch.Tensor, block_table: torch.Tensor,
+                scale: Optional[float] = None, kv_split_blocks: int = 0) -> AttnParams:
+    B, nq, hq, d = q.shape
+    nb, hkv, bs, d2 = k_cache.shape
+    return AttnParams(B, nq, hq, hkv, d, bs, block_table.shape[1], nb,
+                      float(scale) if scale else 0.0, kv_split_blocks)
+
+
+def verify_attention(ctx: Context, q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                     block_table: torch.Tensor, context_lens: torch.Tensor,
+                     tree_mask: Optional[torch.Tensor] = None, scale: Optional[float] = None,
+                     kv_split_blocks: int = 0, out: Optional[torch.Tensor] = None,
+                     workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """kyro_verify_attention.  q bf16 [B,nq,Hq,D]; caches bf16 [NB,Hkv,bs,D];
+    block_table int64 [B,max_blocks]; context_lens int64 [B]; tree_mask
+    int64/uint64 [B,nq] or None (chain).  Returns bf16 [B,nq,Hq,D]."""
+    dev = ctx.device
+    _need(q, "q", torch.bfloat16, dev, 4)
+    _need(k_cache, "k_cache", torch.bfloat16, dev, 4)
+    _need(v_cache, "v_cache", torch.bfloat16, dev, 4)
+    if k_cache.shape != v_cache.shape:
+        raise ValueError("k_cache and v_cache shapes differ")
+    _need(block_table, "block_table", torch.int64, dev, 2)
+    _need(context_lens, "context_lens", torch.int64, dev, 1)
+    B = q.shape[0]
+    if block_table.shape[0] != B or context_lens.shape[0] != B:
+        raise ValueError("block_table / context_lens batch mismatch")
+    if tree_mask is not None:
+        if tree_mask.dtype not in (torch.int64, torch.uint64):
+            raise TypeError("tree_mask must be int64 or uint64")
+        _need(tree_mask, "tree_mask", tree_mask.dtype, dev, 2)
+    p = attn_params(q, k_cache, block_table, scale, kv_split_blocks)
+    if out is None:
+        out = torch.empty_like(q)
+    L = _lib.load()
+    need = L.kyro_verify_attention_workspace_size(C.byref(p))
+    ws = workspace if workspace is not None else ctx.workspace(need)
+    ctx.bind_stream()
+    check(L.kyro_verify_attention(ctx.handle, C.byref(p), _ptr(q), _ptr(k_cache), _ptr(v_cache),
+                                  _ptr(block_table), _ptr(context_lens), _ptr(tree_mask),
+                                  _ptr(out), _ptr(ws), ws.numel()))
+    return out
+
+
+def _kv_params(block_table: torch.Tensor, block_size: int, num_blocks: int) -> KVParams:
+    return KVParams(block_table.shape[0], block_size, block_table.shape[1], num_blocks)
+
+
+def _check_kv_state(ctx, block_table, context_lens, free_stack, free_top, ref_counts):
+    dev = ctx.device
+    _need(block_table, "block_table", torch.int64, dev, 2)
+    _need(context_lens, "context_lens", torch.int64, dev, 1)
+    _need(free_stack, "free_stack", torch.int32, dev, 1)
+    _need(free_top, "free_top", torch.int32, dev)
+    _need(ref_counts, "ref_counts", torch.int32, dev, 1)
+    if free_stack.numel() != ref_counts.numel():
+        raise ValueError("free_stack and ref_counts must both hold num_blocks entries")
+
+
+def kv_reserve(ctx: Context, num_new: int, block_table, context_lens, free_stack, free_top,
+               ref_counts, block_size: int, out_ok: Optional[torch.Tensor] = None):
+    """kyro_kv_reserve (in place).  Returns out_ok int32 [B]."""
+    _check_kv_state(ctx, block_table, context_lens, free_stack, free_top, ref_counts)
+    if out_ok is None:
+        out_ok = torch.empty(block_table.shape[0], dtype=torch.int32, device=ctx.device)
+    p = _kv_params(block_table, block_size, ref_counts.numel())
+    ctx.bind_stream()
+    check(_lib.load().kyro_kv_reserve(ctx.handle, C.byref(p), num_new, _ptr(block_table),
+                                      _ptr(context_lens), _ptr(free_stack), _ptr(free_top),
+                                      _ptr(ref_counts), _ptr(out_ok)))
+    return out_ok
+
+
+def kv_commit(ctx: Context, num_new: int, accept_len: torch.Tensor, block_table, context_lens,
+              free_stack, free_top, ref_counts, block_size: int):
+    """kyro_kv_commit (in place)."""
+    _check_kv_state(ctx, block_table, context_lens, free_stack, free_top, ref_counts)
+    _need(accept_len, "accept_len", torch.int32, ctx.device, 1)
+    p = _kv_params(block_table, block_size, ref_counts.numel())
+    ctx.bind_stream()
+    check(_lib.load().kyro_kv_commit(ctx.handle, C.byref(p), num_new, _ptr(accept_len),
+                                     _ptr(block_table), _ptr(context_lens), _ptr(free_stack),
+                                     _ptr(free_top), _ptr(ref_counts)))
+
+
+def kv_commit_tree(ctx: Context, num_nodes: int, path: torch.Tensor, path_len: torch.Tensor,
+                   k_caches: Sequence[torch.Tensor], v_caches: Sequence[torch.Tensor],
+                   block_table, context_lens, free_stack, free_top, ref_counts, block_size: int):
+    """kyro_kv_commit_tree (in place): move the accepted path's K/V rows in
+    every layer's cache, then commit path_len slots."""
+    _check_kv_state(ctx, block_table, context_lens, free_stack, free_top, ref_counts)
+    _need(path, "path", torch.int32, ctx.device, 2)
+    _need(path_len, "path_len", torch.int32, ctx.device, 1)
+    if len(k_caches) != len(v_caches):
+        raise ValueError("k_caches and v_caches differ in length")
+    for c in list(k_caches) + list(v_caches):
+        _need(c, "cache", torch.bfloat16, ctx.device, 4)
+    nl = len(k_caches)
+    kp = (C.c_void_p * max(nl, 1))(*[c.data_ptr() for c in k_caches])
+    vp = (C.c_void_p * max(nl, 1))(*[c.data_ptr() for c in v_caches])
+    hkv = k_caches[0].shape[1] if nl else 1
+    d = k_caches[0].shape[3] if nl else 8
+    p = _kv_params(block_table, block_size, ref_counts.numel())
+    ctx.bind_stream()
+    check(_lib.load().kyro_kv_commit_tree(ctx.handle, C.byref(p), num_nodes, _ptr(path),
+                                          _ptr(path_len), nl, C.cast(kp, C.c_void_p),
+                                          C.cast(vp, C.c_void_p), hkv, d, _ptr(block_table),
+                                          _ptr(context_lens), _ptr(free_stack), _ptr(free_top),
+                                          _ptr(ref_counts)))
+
+
+def kv_write(ctx: Context, k_new: torch.Tensor, v_new: torch.Tensor, block_table, context_lens,
+             k_cache: torch.Tensor, v_cache: torch.Tensor, block_size: int):
+    """kyro_kv_write: k_new / v_new bf16 [B, num_new, Hkv, D] into the paged
+    slots at context_lens[b] + j."""
+    dev = ctx.device
+    _need(k_new, "k_new", torch.bfloat16, dev, 4)
+    _need(v_new, "v_new", torch.bfloat16, dev, 4)
+    _need(k_cache, "k_cache", torch.bfloat16, dev, 4)
+    _need(v_cache, "v_cache", torch.bfloat16, dev, 4)
+    _need(block_table, "block_table", torch.int64, dev, 2)
+    _need(context_lens, "context_lens", torch.int64, dev, 1)
+    B, n, hkv, d = k_new.shape
+    if tuple(v_new.shape) != (B, n, hkv, d) or k_cache.shape[1] != hkv or k_cache.shape[3] != d:
+        raise ValueError("k_new / v_new / cache shapes disagree")
+    p = _kv_params(block_table, block_size, k_cache.shape[0])
+    ctx.bind_stream()
+    check(_lib.load().kyro_kv_write(ctx.handle, C.byref(p), n, hkv, d, _ptr(k_new), _ptr(v_new),
+                                    _ptr(block_table), _ptr(context_lens), _ptr(k_cache),
+                                    _ptr(v_cache)))
+
+
+def philox_uniforms(ctx: Context, seed: int, seq: int, pos0: int, stream: int, step: int,
+                    n: int) -> torch.Tensor:
+    out = torch.empty(n, dtype=torch.float32, device=ctx.device)
+    ctx.bind_stream()
+    check(_lib.load().kyro_philox_uniforms(ctx.handle, seed, seq, pos0, stream, step, n,
+                                           _ptr(out)))
+    return out

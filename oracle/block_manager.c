@@ -1,0 +1,154 @@
+/*
+ * block_manager.c -- CPU restatement of the KV slot bookkeeping
+ * (TEST INFRASTRUCTURE: the checker for the sm_100a commit kernels).
+ *
+ * Mirrors BlockManager, src/scheduler/block_manager.rs:
+ *   free list is a Vec popped from the back        (:36, :92-98, :115-121)
+ *   a newly allocated block gets ref_count = 1      (:97, :120)
+ *   allocation fails as a whole when too few blocks are free (:111-113)
+ *   release decrements ref_count and returns the block to the free list
+ *   when it reaches zero, in table order            (:133-150)
+ * The reference never grows a sequence after its prompt and never rolls
+ * back; reserve/commit apply the same rules to the k+1 verify slots.
+ */
+#include <stdlib.h>
+#include <string.h>
+
+#include "kyro_oracle.h"
+
+static int64_t blocks_for(int64_t tokens, int32_t bs) { return (tokens + bs - 1) / bs; }
+
+void ko_kv_reserve(int32_t batch, int32_t bs, int32_t max_blocks, int32_t num_blocks,
+                   int32_t num_new, int64_t* block_table, const int64_t* context_lens,
+                   int32_t* free_stack, int32_t* free_top, int32_t* ref_counts,
+                   int32_t* out_ok) {
+  int32_t top = *free_top;
+  for (int32_t b = 0; b < batch; ++b) {
+    int64_t have = blocks_for(context_lens[b], bs);
+    int64_t want = blocks_for(context_lens[b] + num_new, bs);
+    int64_t need = want - have;
+    if (want > max_blocks || need > top) {
+      if (out_ok) out_ok[b] = 0;
+      continue;
+    }
+    for (int64_t i = 0; i < need; ++i) {
+      int32_t blk = free_stack[--top];
+      if (blk < 0 || blk >= num_blocks) continue; /* the kernel flags KYRO_DEV_BAD_BLOCK */
+      ref_counts[blk] = 1;
+      block_table[(size_t)b * max_blocks + have + i] = blk;
+    }
+    if (out_ok) out_ok[b] = 1;
+  }
+  *free_top = top;
+}
+
+static void release_tail(int32_t b, int32_t bs, int32_t max_blocks, int32_t num_blocks,
+                         int64_t old_len,
+                         int64_t reserved_len, int64_t new_len, int64_t* block_table,
+                         int32_t* free_stack, int32_t* top, int32_t* ref_counts) {
+  (void)old_len;
+  int64_t keep = blocks_for(new_len, bs);
+  int64_t had = blocks_for(reserved_len, bs);
+  if (had > max_blocks) had = max_blocks;
+  for (int64_t i = keep; i < had; ++i) {
+    int64_t* slot = &block_table[(size_t)b * max_blocks + i];
+    int64_t blk = *slot;
+    *slot = -1;
+    if (blk < 0 || blk >= num_blocks) continue;
+    if (ref_counts[blk] > 0) ref_counts[blk] -= 1;
+    if (ref_counts[blk] == 0 && *top < num_blocks) free_stack[(*top)++] = (int32_t)blk;
+  }
+}
+
+void ko_kv_commit(int32_t batch, int32_t bs, int32_t max_blocks, int32_t num_blocks,
+                  int32_t num_new, const int32_t* accept_len, int64_t* block_table,
+                  int64_t* context_lens, int32_t* free_stack, int32_t* free_top,
+                  int32_t* ref_counts) {
+  int32_t top = *free_top;
+  for (int32_t b = 0; b < batch; ++b) {
+    int32_t a = accept_len[b];
+    if (a < 0) continue;
+    int64_t kept = (int64_t)a + 1 < num_new ? (int64_t)a + 1 : num_new;
+    int64_t old_len = context_lens[b];
+    int64_t new_len = old_len + kept;
+    release_tail(b, bs, max_blocks, num_blocks, old_len, old_len + num_new, new_len, block_table,
+                 free_stack, &top, ref_counts);
+    context_lens[b] = new_len;
+  }
+  *free_top = top;
+}
+
+void ko_kv_commit_tree(int32_t batch, int32_t bs, int32_t max_blocks, int32_t num_blocks,
+                       int32_t num_nodes, const int32_t* path, const int32_t* path_len,
+                       int32_t num_layers, uint16_t* const* k_caches, uint16_t* const* v_caches,
+                       int32_t hkv, int32_t d, int64_t* block_table, int64_t* context_lens,
+                       int32_t* free_stack, int32_t* free_top, int32_t* ref_counts) {
+  /* 1. move the accepted path's K/V rows to consecutive positions (read all
+   *    sources before writing any destination) */
+  size_t row = (size_t)d;
+  uint16_t* tmp = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)num_nodes * hkv * row);
+  for (int32_t b = 0; b < batch; ++b) {
+    int32_t L = path_len[b] < num_nodes ? path_len[b] : num_nodes;
+    if (L <= 1) continue;
+    int64_t ctx = context_lens[b];
+    for (int32_t layer = 0; layer < num_layers; ++layer) {
+      for (int32_t which = 0; which < 2; ++which) {
+        uint16_t* cache = which ? v_caches[layer] : k_caches[layer];
+        for (int32_t i = 0; i < L; ++i) {
+          int32_t node = path[(size_t)b * num_nodes + i];
+          if (node < 0 || node >= num_nodes) node = i;
+          int64_t pos = ctx + node;
+          int64_t blk = block_table[(size_t)b * max_blocks + pos / bs];
+          if (blk < 0 || blk >= num_blocks) {
+            memset(tmp + (size_t)i * hkv * row, 0, sizeof(uint16_t) * hkv * row);
+            continue;
+          }
+          for (int32_t h = 0; h < hkv; ++h)
+            memcpy(tmp + ((size_t)i * hkv + h) * row,
+                   cache + (((size_t)blk * hkv + h) * bs + (size_t)(pos % bs)) * row,
+                   sizeof(uint16_t) * row);
+        }
+        for (int32_t i = 1; i < L; ++i) {
+          if (path[(size_t)b * num_nodes + i] == i) continue; /* already in place */
+          int64_t pos = ctx + i;
+          int64_t blk = block_table[(size_t)b * max_blocks + pos / bs];
+          if (blk < 0 || blk >= num_blocks) continue;
+          for (int32_t h = 0; h < hkv; ++h)
+            memcpy(cache + (((size_t)blk * hkv + h) * bs + (size_t)(pos % bs)) * row,
+                   tmp + ((size_t)i * hkv + h) * row, sizeof(uint16_t) * row);
+        }
+      }
+    }
+  }
+  free(tmp);
+  /* 2. commit path_len slots */
+  int32_t* acc = (int32_t*)malloc(sizeof(int32_t) * (size_t)(batch > 0 ? batch : 1));
+  for (int32_t b = 0; b < batch; ++b) acc[b] = path_len[b] > 0 ? path_len[b] - 1 : -1;
+  ko_kv_commit(batch, bs, max_blocks, num_blocks, num_nodes, acc, block_table, context_lens,
+               free_stack, free_top, ref_counts);
+  free(acc);
+}
+
+void ko_kv_write(int32_t batch, int32_t bs, int32_t max_blocks, int32_t num_blocks,
+                 int32_t num_new, int32_t hkv, int32_t d, const uint16_t* k_new,
+                 const uint16_t* v_new, const int64_t* block_table, const int64_t* context_lens,
+                 uint16_t* k_cache, uint16_t* v_cache) {
+  /* KVCacheManager::append_kv (src/model/kv_cache.rs:49-75) appends the
+   * [batch, seq, Hkv, D] rows after the cached ones; here each row goes to
+   * its paged slot context_len + j. */
+  for (int32_t b = 0; b < batch; ++b) {
+    int64_t ctx = context_lens[b];
+    for (int32_t j = 0; j < num_new; ++j) {
+      int64_t pos = ctx + j;
+      if (ctx < 0 || pos / bs >= max_blocks) continue;
+      int64_t blk = block_table[(size_t)b * max_blocks + pos / bs];
+      if (blk < 0 || blk >= num_blocks) continue;
+      for (int32_t h = 0; h < hkv; ++h) {
+        size_t src = (((size_t)b * num_new + j) * hkv + h) * (size_t)d;
+        size_t dst = (((size_t)blk * hkv + h) * bs + (size_t)(pos % bs)) * (size_t)d;
+        memcpy(k_cache + dst, k_new + src, sizeof(uint16_t) * (size_t)d);
+        memcpy(v_cache + dst, v_new + src, sizeof(uint16_t) * (size_t)d);
+      }
+    }
+  }
+}

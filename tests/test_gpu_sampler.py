@@ -1,0 +1,167 @@
+"""GPU parity of the acceptance sampler and the draft sampler against the
+CPU oracle, through the C ABI.
+
+Bar: accept lengths and emitted tokens bit-exact given identical uniforms;
+p(x)/q(x) identical to the oracle and within 1e-5 relative of a torch fp32
+softmax."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+NTHREADS = os.cpu_count() or 1
+
+
+def _np(t):
+    return t.detach().cpu().numpy()
+
+
+def test_device_philox_matches_oracle(ctx, oracle):
+    from kyro_b200.verify import philox_uniforms
+    for seed, seq, stream, step in [(0, 0, 1, 0), (12345678901234, 7, 2, 99), (2**64 - 1, 2**32 - 1, 0, 5)]:
+        u = _np(philox_uniforms(ctx, seed, seq, 3, stream, step, 64))
+        ref = np.array([oracle.uniform(seed, seq, 3 + i, stream, step) for i in range(64)],
+                       dtype=np.float32)
+        assert np.array_equal(u, ref)
+
+
+def _sample_drafts(ctx, oracle, drf, T, seed, step=0):
+    from kyro_b200.verify import sample_tokens
+    toks, probs = sample_tokens(ctx, drf, T, seed=seed, step=step)
+    otoks, oprobs = oracle.sample_tokens(_np(drf), T, seed=seed, step=step, nthreads=NTHREADS)
+    assert np.array_equal(_np(toks), otoks)
+    assert np.array_equal(_np(probs), oprobs)
+    return toks
+
+
+CASES = [
+    # B, k, V, T, seed
+    (8, 4, 32000, 1.0, 0),     # config 0
+    (8, 4, 32000, 1.0, 1),
+    (3, 1, 1000, 0.7, 2),      # one ragged chunk
+    (5, 8, 4099, 0.8, 3),      # V % 4 != 0: scalar loads
+    (2, 0, 2048, 1.0, 4),      # k = 0: bonus only
+    (16, 5, 128256, 0.7, 5),   # config-1 vocabulary
+]
+
+
+@pytest.mark.parametrize("B,k,V,T,seed", CASES)
+def test_stochastic_accept_matches_oracle(ctx, oracle, B, k, V, T, seed):
+    from kyro_b200.verify import spec_accept
+    from kyro_b200.workloads import accept_inputs
+    tgt, drf = accept_inputs(B, k, V, ctx.device, seed=seed)
+    drafts = (_sample_drafts(ctx, oracle, drf, T, seed) if k > 0
+              else torch.zeros(B, 0, dtype=torch.int32, device=ctx.device))
+    for step in (0, 1):
+        acc, toks, num, probs = spec_accept(ctx, tgt, drf, drafts, temperature=T, seed=seed,
+                                            step=step, want_probs=True)
+        oacc, otoks, onum, oprobs = oracle.spec_accept(_np(tgt), _np(drf), _np(drafts),
+                                                       temperature=T, seed=seed, step=step,
+                                                       nthreads=NTHREADS)
+        assert np.array_equal(_np(acc), oacc)
+        assert np.array_equal(_np(num), onum)
+        assert np.array_equal(_np(toks), otoks)
+        assert np.array_equal(_np(probs), oprobs)
+    assert ctx.device_status() == 0
+
+
+def test_probabilities_match_torch_softmax(ctx, oracle):
+    """probabilities within 1e-5 relative (fp32) of softmax(z / T)."""
+    from kyro_b200.verify import spec_accept
+    from kyro_b200.workloads import accept_inputs
+    B, k, V, T = 8, 4, 32000, 0.8
+    tgt, drf = accept_inputs(B, k, V, ctx.device, seed=11)
+    drafts = _sample_drafts(ctx, oracle, drf, T, 11)
+    _, _, _, probs = spec_accept(ctx, tgt, drf, drafts, temperature=T, seed=11, want_probs=True)
+    inv_t = np.float32(1.0 / T)
+    p_ref = torch.softmax(tgt[:, :k].double() * float(inv_t), -1)
+    q_ref = torch.softmax(drf.double() * float(inv_t), -1)
+    idx = drafts.long().unsqueeze(-1)
+    p_x = p_ref.gather(-1, idx).squeeze(-1)
+    q_x = q_ref.gather(-1, idx).squeeze(-1)
+    torch.testing.assert_close(probs[..., 0].double(), p_x, rtol=1e-5, atol=0)
+    torch.testing.assert_close(probs[..., 1].double(), q_x, rtol=1e-5, atol=0)
+
+
+@pytest.mark.parametrize("mode", [1, 2])
+def test_greedy_modes_match_oracle(ctx, oracle, mode):
+    from kyro_b200.verify import spec_accept
+    from kyro_b200.workloads import accept_inputs
+    B, k, V = 32, 5, 32000
+    tgt, _ = accept_inputs(B, k, V, ctx.device, seed=21)
+    top = tgt.argmax(-1).to(torch.int32)
+    rng = np.random.default_rng(0)
+    drafts = top[:, :k].clone()
+    # sequence b mismatches at position b % (k+1) (k+1: all match)
+    for b in range(B):
+        j = b % (k + 1)
+        if j < k:
+            drafts[b, j] = int((top[b, j].item() + 1 + rng.integers(0, V - 1)) % V)
+    acc, toks, num, _ = spec_accept(ctx, tgt, None, drafts.contiguous(), mode=mode)
+    oacc, otoks, onum, _ = oracle.spec_accept(_np(tgt), None, _np(drafts), mode=mode)
+    assert np.array_equal(_np(acc), oacc)
+    assert np.array_equal(_np(toks), otoks)
+    assert np.array_equal(_np(num), onum)
+    assert list(oacc) == [b % (k + 1) for b in range(B)]
+
+
+def test_reference_argmax_cases_on_device(ctx, oracle):
+    """src/worker.rs:395-422: argmax at T = 0 through the device sampler."""
+    import json
+    from kyro_b200.verify import sample_tokens
+    cases = json.load(open(os.path.join(os.path.dirname(__file__), "golden",
+                                        "reference_known_answers.json")))["sample_token"]
+    for c in cases:
+        if not c["logits"] or "expect_token" not in c:
+            continue
+        lg = torch.tensor(c["logits"], dtype=torch.float32, device=ctx.device)[None, None]
+        toks, _ = sample_tokens(ctx, lg.contiguous(), c["temperature"], seed=0)
+        assert int(toks[0, 0]) == c["expect_token"], c["name"]
+
+
+def test_out_of_range_draft_token_is_flagged_and_rejected(ctx, oracle):
+    from kyro_b200.verify import spec_accept
+    from kyro_b200.workloads import accept_inputs
+    B, k, V = 4, 3, 4096
+    tgt, drf = accept_inputs(B, k, V, ctx.device, seed=31)
+    drafts = _sample_drafts(ctx, oracle, drf, 1.0, 31)
+    drafts[1, 0] = V + 5
+    drafts[2, 1] = -1
+    ctx.device_status(clear=True)
+    acc, toks, num, _ = spec_accept(ctx, tgt, drf, drafts, seed=31)
+    from kyro_b200._lib import DEV_BAD_TOKEN
+    assert ctx.device_status() & DEV_BAD_TOKEN
+    oacc, otoks, onum, _ = oracle.spec_accept(_np(tgt), _np(drf), _np(drafts), seed=31)
+    assert np.array_equal(_np(acc), oacc) and np.array_equal(_np(toks), otoks)
+    assert oacc[1] == 0 and oacc[2] <= 1
+
+
+def test_determinism(ctx, oracle):
+    from kyro_b200.verify import spec_accept
+    from kyro_b200.workloads import accept_inputs
+    tgt, drf = accept_inputs(16, 5, 32000, ctx.device, seed=41)
+    drafts = _sample_drafts(ctx, oracle, drf, 1.0, 41)
+    a = spec_accept(ctx, tgt, drf, drafts, seed=41, want_probs=True)
+    b = spec_accept(ctx, tgt, drf, drafts, seed=41, want_probs=True)
+    for x, y in zip(a, b):
+        assert torch.equal(x, y)
+
+
+def test_full_config1_accept_matches_oracle(ctx, oracle):
+    """config 1 acceptance at full size: B=64, k=5, V=128256."""
+    from kyro_b200.verify import spec_accept
+    from kyro_b200.workloads import accept_inputs
+    B, k, V = 64, 5, 128256
+    tgt, drf = accept_inputs(B, k, V, ctx.device, seed=0)
+    drafts = _sample_drafts(ctx, oracle, drf, 1.0, 0)
+    acc, toks, num, probs = spec_accept(ctx, tgt, drf, drafts, seed=0, want_probs=True)
+    oacc, otoks, onum, oprobs = oracle.spec_accept(_np(tgt), _np(drf), _np(drafts), seed=0,
+                                                   nthreads=NTHREADS)
+    assert np.array_equal(_np(acc), oacc)
+    assert np.array_equal(_np(toks), otoks)
+    assert np.array_equal(_np(probs), oprobs)
+    rate = oacc.mean() / k
+    assert 0.3 < rate < 1.0

@@ -1,0 +1,312 @@
+"""CPU tests of the oracle: pinned against published known answers and the
+reference's own unit-test cases (tests/golden/), plus the distributional
+property of the published rejection-sampling rule."""
+import json
+import math
+import os
+
+import numpy as np
+import pytest
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "reference_known_answers.json")
+
+
+def golden():
+    with open(GOLDEN) as f:
+        return json.load(f)
+
+
+# Random123 known-answer vectors for philox4x32-10 (counter, key, output).
+PHILOX_KAT = [
+    ([0, 0, 0, 0], 0, [0x6627e8d5, 0xe169c58d, 0xbc57ac4c, 0x9b00dbd8]),
+    ([0xffffffff] * 4, 0xffffffffffffffff, [0x408f276d, 0x41c83b0e, 0xa20bc7c6, 0x6d5451fd]),
+    ([0x243f6a88, 0x85a308d3, 0x13198a2e, 0x03707344], (0x299f31d0 << 32) | 0xa4093822,
+     [0xd16cfe09, 0x94fdcceb, 0x5001e420, 0x24126ea1]),
+]
+
+
+@pytest.mark.parametrize("ctr,key,expect", PHILOX_KAT)
+def test_philox_known_answers(oracle, ctr, key, expect):
+    assert list(oracle.philox4x32_10(ctr, key)) == expect
+
+
+def test_uniform_range_and_form(oracle):
+    us = np.array([oracle.uniform(0, s, p, 1, 0) for s in range(64) for p in range(8)])
+    assert (us > 0).all() and (us < 1).all()
+    odd = us * 2 ** 24
+    assert np.all(odd == np.round(odd)) and np.all(np.round(odd) % 2 == 1)
+
+
+def test_exp_accuracy(oracle):
+    rng = np.random.default_rng(0)
+    xs = np.concatenate([-rng.uniform(0, 87, 20000), -rng.uniform(0, 1, 5000),
+                         [0.0, -1e-30, -0.3465, -0.3466, -86.999]]).astype(np.float32)
+    got = np.array([oracle.exp(float(x)) for x in xs], dtype=np.float64)
+    ref = np.exp(xs.astype(np.float64))
+    ulp = np.abs(got - ref) / np.spacing(ref.astype(np.float32)).astype(np.float64)
+    assert ulp.max() <= 2.0
+    assert oracle.exp(0.0) == 1.0
+    assert oracle.exp(-87.5) == 0.0 and oracle.exp(float("-inf")) == 0.0
+
+
+@pytest.mark.parametrize("V,shards", [(7, 1), (2048, 1), (32000, 1), (128256, 1), (128256, 2),
+                                      (128256, 8)])
+def test_softmax_contract_matches_float64(oracle, V, shards):
+    rng = np.random.default_rng(V + shards)
+    z = (rng.standard_normal(V) * 3).astype(np.float32)
+    for T in (1.0, 0.7):
+        p = oracle.softmax_row(z, temperature=T, num_shards=shards)
+        s = z.astype(np.float64) * np.float64(np.float32(1.0 / T))
+        ref = np.exp(s - s.max())
+        ref /= ref.sum()
+        rel = np.abs(p - ref) / ref
+        assert rel.max() < 1e-5, rel.max()
+
+
+def test_reference_sample_token_cases(oracle):
+    """src/worker.rs:395-457 known answers through the oracle's draft sampler
+    (T <= 0 -> argmax; peaked rows at T > 0 -> the peak)."""
+    for case in golden()["sample_token"]:
+        if not case["logits"]:
+            continue  # empty rows are rejected by argument validation here
+        lg = np.array(case["logits"], dtype=np.float32)[None, None, :]
+        tok, _ = oracle.sample_tokens(lg, case["temperature"], seed=0)
+        t = int(tok[0, 0])
+        if "expect_token" in case:
+            assert t == case["expect_token"], case["name"]
+        elif "expect_one_of" in case:
+            assert t in case["expect_one_of"], case["name"]
+
+
+def test_reference_greedy_verify_rule(oracle):
+    """verify_drafts (src/speculative.rs:286-339): accept while the draft
+    equals the target argmax; on the first mismatch emit the argmax and
+    stop; no bonus when all match; k == 0 emits one argmax."""
+    rows = [c["logits"] for c in golden()["sample_token"][:3]]
+    V = 8
+    tgt = np.full((1, 4, V), -1.0, dtype=np.float32)
+    for j, r in enumerate(rows):
+        tgt[0, j, :len(r)] = r
+    tgt[0, 3, 7] = 9.0
+    tops = tgt[0].argmax(-1)  # [5, 2, 2, 7]
+    # all match
+    acc, toks, num, _ = oracle.spec_accept(tgt, None, tops[None, :3], mode=oracle.MODE_GREEDY_REF)
+    assert acc[0] == 3 and num[0] == 3 and list(toks[0, :3]) == list(tops[:3])
+    # GREEDY adds the bonus argmax
+    acc, toks, num, _ = oracle.spec_accept(tgt, None, tops[None, :3], mode=oracle.MODE_GREEDY)
+    assert acc[0] == 3 and num[0] == 4 and toks[0, 3] == 7
+    # mismatch at position 1
+    drafts = np.array([[5, 3, 2]], dtype=np.int32)
+    acc, toks, num, _ = oracle.spec_accept(tgt, None, drafts, mode=oracle.MODE_GREEDY_REF)
+    assert acc[0] == 1 and num[0] == 2 and list(toks[0, :2]) == [5, 2]
+    # k == 0
+    acc, toks, num, _ = oracle.spec_accept(tgt[:, :1], None, np.zeros((1, 0), np.int32),
+                                           mode=oracle.MODE_GREEDY_REF)
+    assert acc[0] == 0 and num[0] == 1 and toks[0, 0] == 5
+
+
+def test_stochastic_rule_emits_target_distribution(oracle):
+    """Leviathan et al. 2023, Thm. 1: the first emitted token is distributed
+    as p whatever q is; the acceptance rate is sum(min(p, q))."""
+    V, N = 8, 200_000
+    rng = np.random.default_rng(1)
+    zt = (rng.standard_normal(V) * 1.5).astype(np.float32)
+    zd = (zt + rng.standard_normal(V)).astype(np.float32)
+    tgt = np.broadcast_to(np.stack([zt, zt])[None], (N, 2, V)).copy()
+    drf = np.broadcast_to(zd[None, None], (N, 1, V)).copy()
+    drafts, _ = oracle.sample_tokens(drf, 1.0, seed=7, nthreads=8)
+    acc, toks, num, _ = oracle.spec_accept(tgt, drf, drafts, temperature=1.0, seed=7, nthreads=8)
+    p = oracle.softmax_row(zt)
+    q = oracle.softmax_row(zd)
+    counts = np.bincount(toks[:, 0], minlength=V)
+    expected = p * N
+    chi2 = ((counts - expected) ** 2 / expected).sum()
+    assert chi2 < 35.0, (chi2, counts, expected)  # dof 7: p ~ 1e-5
+    rate = (acc == 1).mean()
+    assert abs(rate - np.minimum(p, q).sum()) < 4 * math.sqrt(0.25 / N)
+
+
+def test_stochastic_identical_models_accept_everything(oracle):
+    V, B, k = 64, 32, 4
+    rng = np.random.default_rng(2)
+    z = (rng.standard_normal((B, k + 1, V)) * 3).astype(np.float32)
+    drafts, _ = oracle.sample_tokens(z[:, :k].copy(), 1.0, seed=3)
+    acc, toks, num, probs = oracle.spec_accept(z, z[:, :k].copy(), drafts, seed=3)
+    assert (acc == k).all() and (num == k + 1).all()
+    assert np.array_equal(probs[..., 0], probs[..., 1])
+
+
+def test_sharded_normaliser_is_consistent(oracle):
+    """Splitting the vocabulary into TP shards changes only the grouping of
+    the double-precision normaliser; decisions agree on these inputs."""
+    B, k, V = 8, 4, 32000
+    rng = np.random.default_rng(4)
+    z = (rng.standard_normal((B, k + 1, V)) * 3).astype(np.float32)
+    d = (z[:, :k] + rng.standard_normal((B, k, V))).astype(np.float32)
+    drafts, _ = oracle.sample_tokens(d, 1.0, seed=0)
+    r1 = oracle.spec_accept(z, d, drafts, seed=0, num_shards=1)
+    r4 = oracle.spec_accept(z, d, drafts, seed=0, num_shards=4)
+    assert np.array_equal(r1[0], r4[0])
+    np.testing.assert_allclose(r1[3], r4[3], rtol=1e-6)
+
+
+def _numpy_attention(q, kc, vc, bt, cl, bs, mask=None):
+    B, nq, hq, d = q.shape
+    hkv = kc.shape[1]
+    g = hq // hkv
+    out = np.zeros((B, nq, hq, d))
+    for b in range(B):
+        total = cl[b] + nq
+        pos = np.arange(total)
+        blocks = bt[b, pos // bs]
+        K = kc[blocks, :, pos % bs, :]  # [total, hkv, d]
+        Vv = vc[blocks, :, pos % bs, :]
+        for j in range(nq):
+            m = mask[b, j] if mask is not None else (1 << (j + 1)) - 1
+            allowed = (pos < cl[b]) | (((m >> np.maximum(pos - cl[b], 0)) & 1).astype(bool) &
+                                       (pos >= cl[b]))
+            for h in range(hq):
+                s = K[:, h // g, :] @ q[b, j, h] / math.sqrt(d)
+                s = np.where(allowed, s, -np.inf)
+                w = np.exp(s - s.max())
+                w /= w.sum()
+                out[b, j, h] = w @ Vv[:, h // g, :]
+    return out
+
+
+def _bf16_bits(x):
+    return (np.asarray(x, np.float32).view(np.uint32) >> 16).astype(np.uint16)
+
+
+def _from_bits(b):
+    return (b.astype(np.uint32) << 16).view(np.float32)
+
+
+@pytest.mark.parametrize("hq,hkv,nq,tree", [(8, 2, 3, False), (4, 4, 1, False), (8, 1, 5, True)])
+def test_attention_oracle_vs_numpy(oracle, hq, hkv, nq, tree):
+    rng = np.random.default_rng(hq * 10 + nq)
+    B, d, bs, NB = 3, 32, 16, 40
+    cl = np.array([0, 17, 40], dtype=np.int64)
+    maxb = 8
+    bt = np.stack([rng.permutation(NB)[:maxb] for _ in range(B)]).astype(np.int64)
+    qb = _bf16_bits(rng.standard_normal((B, nq, hq, d)))
+    kb = _bf16_bits(rng.standard_normal((NB, hkv, bs, d)))
+    vb = _bf16_bits(rng.standard_normal((NB, hkv, bs, d)))
+    mask = None
+    if tree:
+        parent = [-1] + [int(rng.integers(0, i)) for i in range(1, nq)]
+        anc = []
+        for j in range(nq):
+            m, n = 0, j
+            while n >= 0:
+                m |= 1 << n
+                n = parent[n]
+            anc.append(m)
+        mask = np.array([anc] * B, dtype=np.uint64)
+    got = oracle.paged_attention(qb, kb, vb, bt, cl, bs, tree_mask=mask)
+    ref = _numpy_attention(_from_bits(qb).astype(np.float64), _from_bits(kb).astype(np.float64),
+                           _from_bits(vb).astype(np.float64), bt, cl, bs,
+                           None if mask is None else mask.astype(object))
+    np.testing.assert_allclose(got, ref, atol=1e-5)
+
+
+def test_reference_attention_cases(oracle):
+    """src/model/attention_kernel.rs:163-227: shapes [1, 8, 64]; with
+    all-ones K/V the output is all ones; zero context gives zeros."""
+    for c in golden()["paged_attention"]:
+        hq, hkv, d, bs, nb = c["num_heads"], c["num_kv_heads"], c["head_dim"], c["block_size"], \
+            c["num_blocks"]
+        q = _bf16_bits(np.full((1, 1, hq, d), c["fill"], np.float32))
+        kc = _bf16_bits(np.full((nb, hkv, bs, d), c["fill"], np.float32))
+        bt = np.zeros((1, 4), np.int64)
+        ctx = c["context_len"]
+        if ctx == 0:
+            out = np.zeros((1, hq, d), np.float32)  # the reference's zero-context branch
+        else:
+            out = oracle.paged_attention(q, kc, kc, bt, np.array([ctx - 1]), bs)[:, 0]
+        assert list(out.shape) == c["expect_shape"]
+        np.testing.assert_allclose(out, c["expect_value"], atol=1e-6)
+
+
+def _fresh_pool(n, B, maxb):
+    return (np.full((B, maxb), -1, np.int64), np.zeros(B, np.int64),
+            np.arange(n, dtype=np.int32), np.array([n], np.int32), np.zeros(n, np.int32))
+
+
+def _prefill(bt, cl, fs, top, rc, bs, lens):
+    """Give each sequence blocks for lens[b] cached tokens, popping the free
+    list from the back in batch order (prompt admission)."""
+    for b, n in enumerate(lens):
+        for i in range(-(-n // bs)):
+            top[0] -= 1
+            blk = fs[top[0]]
+            rc[blk] = 1
+            bt[b, i] = blk
+        cl[b] = n
+
+
+def test_reference_block_manager_cases(oracle):
+    g = golden()["block_manager"]
+    c = g[0]
+    bt, cl, fs, top, rc = _fresh_pool(c["num_gpu_blocks"], 1, 8)
+    ok = oracle.kv_reserve(c["tokens"], bt, cl, fs, top, rc, c["block_size"])
+    assert ok[0] == 1 and (bt[0] >= 0).sum() == c["expect_blocks"]
+    assert top[0] == c["expect_free_after"]
+    # LIFO: the first block handed out is the last one in the free list (Vec::pop)
+    assert bt[0, 0] == c["num_gpu_blocks"] - 1 and rc[bt[0, 0]] == 1
+    c = g[1]
+    bt, cl, fs, top, rc = _fresh_pool(c["num_gpu_blocks"], 1, 8)
+    ok = oracle.kv_reserve(c["tokens"], bt, cl, fs, top, rc, c["block_size"])
+    assert ok[0] == 0 and top[0] == 1 and (bt < 0).all()
+    c = g[2]
+    bt, cl, fs, top, rc = _fresh_pool(c["num_gpu_blocks"], 2, 8)
+    ok = oracle.kv_reserve(4, bt, cl, fs, top, rc, c["block_size"])
+    assert ok.all() and set(bt[0][bt[0] >= 0]).isdisjoint(bt[1][bt[1] >= 0])
+
+
+def test_block_manager_reserve_commit_conserves_blocks(oracle):
+    rng = np.random.default_rng(5)
+    n, B, maxb, bs = 200, 16, 40, 4
+    bt, cl, fs, top, rc = _fresh_pool(n, B, maxb)
+    fs[:] = rng.permutation(n).astype(np.int32)
+    for step in range(30):
+        k = int(rng.integers(1, 7))
+        ok = oracle.kv_reserve(k + 1, bt, cl, fs, top, rc, bs)
+        acc = np.where(ok == 1, rng.integers(0, k + 1, B), -1).astype(np.int32)
+        oracle.kv_commit(k + 1, acc, bt, cl, fs, top, rc, bs)
+        held = bt[bt >= 0]
+        assert len(set(held.tolist())) == held.size  # no block held twice
+        assert held.size + top[0] == n  # nothing lost
+        assert (rc[held] == 1).all()
+        for b in range(B):
+            assert (bt[b] >= 0).sum() == -(-cl[b] // bs)
+
+
+def test_tree_commit_moves_path_rows(oracle):
+    rng = np.random.default_rng(6)
+    n, B, maxb, bs, hkv, d, nodes = 64, 2, 16, 4, 2, 8, 7
+    bt, cl, fs, top, rc = _fresh_pool(n, B, maxb)
+    _prefill(bt, cl, fs, top, rc, bs, [5, 9])
+    oracle.kv_reserve(nodes, bt, cl, fs, top, rc, bs)
+    kc = [rng.integers(0, 65535, (n, hkv, bs, d), dtype=np.uint16) for _ in range(2)]
+    vc = [rng.integers(0, 65535, (n, hkv, bs, d), dtype=np.uint16) for _ in range(2)]
+    saved = [(k.copy(), v.copy()) for k, v in zip(kc, vc)]
+    bt0, ctx0 = bt.copy(), cl.copy()
+    path = np.array([[0, 2, 5, 6, 0, 0, 0], [0, 1, 0, 0, 0, 0, 0]], np.int32)
+    plen = np.array([4, 2], np.int32)
+    top0 = int(top[0])
+    oracle.kv_commit_tree(nodes, path, plen, kc, vc, bt, cl, fs, top, rc, bs)
+    assert list(cl) == [ctx0[0] + 4, ctx0[1] + 2]
+
+    def row(cache, table, b, pos):
+        return cache[table[b, pos // bs], :, pos % bs]
+
+    for (k0, v0), k1, v1 in zip(saved, kc, vc):
+        for b in range(B):
+            for i in range(plen[b]):
+                src, dst = ctx0[b] + path[b, i], ctx0[b] + i
+                assert np.array_equal(row(k1, bt, b, dst), row(k0, bt0, b, src))
+                assert np.array_equal(row(v1, bt, b, dst), row(v0, bt0, b, src))
+    # blocks wholly beyond the kept length went back to the free list
+    released = sum((bt0[b] >= 0).sum() - (bt[b] >= 0).sum() for b in range(B))
+    assert top[0] == top0 + released
