@@ -41,7 +41,7 @@ def test_reserve_commit_matches_oracle(ctx, oracle, B, NB, bs):
     from kyro_b200.verify import kv_commit, kv_reserve
     rng = np.random.default_rng(B)
     maxb = 300
-    lens = rng.integers(0, 16 * 200, B) if bs == 16 else rng.integers(0, 40, B)
+    lens = rng.integers(0, NB * bs // B, B)  # about half the pool in use
     dev = _device_state(rng, NB, B, maxb, bs, lens, ctx.device)
     host = _host(dev)
     for step in range(6):
