@@ -163,5 +163,6 @@ def test_full_config1_accept_matches_oracle(ctx, oracle):
     assert np.array_equal(_np(acc), oacc)
     assert np.array_equal(_np(toks), otoks)
     assert np.array_equal(_np(probs), oprobs)
-    rate = oacc.mean() / k
-    assert 0.3 < rate < 1.0
+    # per-token acceptance probability E[min(1, p/q)]: BASELINE quotes ~0.6-0.8
+    rate = np.minimum(1.0, oprobs[..., 0] / oprobs[..., 1]).mean()
+    assert 0.5 < rate < 0.9, rate
