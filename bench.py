@@ -70,6 +70,52 @@ def load_traffic():
         return {}
 
 
+class NvmlClockSampler:
+    """SM clock and clock-event reasons sampled through NVML every ~2 ms
+    while the timed region runs (reads only; changes no GPU setting)."""
+
+    def __init__(self, gpu_index):
+        import pynvml
+        self.nv = pynvml
+        pynvml.nvmlInit()
+        self.h = pynvml.nvmlDeviceGetHandleByIndex(gpu_index)
+        self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        self.samples = []
+        self.stop_flag = threading.Event()
+
+    def _run(self):
+        nv = self.nv
+        while not self.stop_flag.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)
+                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                self.samples.append((mhz, reasons))
+            except Exception:
+                pass
+            time.sleep(0.002)
+
+    def start(self):
+        self.t = threading.Thread(target=self._run, daemon=True)
+        self.t.start()
+        while not self.samples and self.t.is_alive():
+            time.sleep(0.001)
+
+    def stop(self):
+        self.stop_flag.set()
+        self.t.join(timeout=2)
+        nv = self.nv
+        if not self.samples:
+            return None
+        names = {nv.nvmlClocksEventReasonHwSlowdown: "hw_slowdown",
+                 nv.nvmlClocksEventReasonHwThermalSlowdown: "hw_thermal_slowdown",
+                 nv.nvmlClocksEventReasonSwThermalSlowdown: "sw_thermal_slowdown",
+                 nv.nvmlClocksEventReasonSwPowerCap: "sw_power_cap"}
+        reasons = sorted({n for _, r in self.samples for bit, n in names.items() if r & bit})
+        return {"sm_mhz": statistics.median(m for m, _ in self.samples),
+                "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(self.samples), "source": "nvml"}
+
+
 class ClockSampler:
     """nvidia-smi clock/throttle samples while the timed region runs."""
 
@@ -169,12 +215,19 @@ def run_ours(args):
         C.byref(attn_params(st.q, st.k_cache, st.block_table)))), dtype=torch.uint8, device=dev)
     ws_acc = torch.empty(max(256, L.kyro_spec_accept_workspace_size(C.byref(AcceptParams(
         cfg.batch, cfg.k, cfg.vocab, 0, cfg.temperature, 0, 0, 0)))), dtype=torch.uint8, device=dev)
-    lens_hist = torch.empty(args.warmup + args.steps + 2, cfg.batch, dtype=torch.int64, device=dev)
     stream = torch.cuda.current_stream(dev)
     ev = {n: [] for n in ("attention", "accept")}
+    # every step starts from the same KV state, so each step sees the same
+    # context lengths; the restore is four device-to-device copies (~0.5 MB)
+    snap = {n: getattr(st, n).clone() for n in
+            ("block_table", "context_lens", "free_stack", "free_top", "ref_counts")}
+
+    def restore():
+        for n, t in snap.items():
+            getattr(st, n).copy_(t, non_blocking=True)
 
     def step(i, timed):
-        lens_hist[i].copy_(st.context_lens)
+        restore()
         kv_reserve(ctx, nq, st.block_table, st.context_lens, st.free_stack, st.free_top,
                    st.ref_counts, cfg.block_size, out_ok=ok)
         kv_write(ctx, k_new, v_new, st.block_table, st.context_lens, st.k_cache, st.v_cache,
@@ -208,10 +261,14 @@ def run_ours(args):
         ids = [v.strip() for v in vis.split(",")]
         if local < len(ids) and ids[local].isdigit():
             phys = int(ids[local])
-    clocks = ClockSampler(phys) if rank == 0 else None
+    clocks = None
+    if rank == 0:
+        try:
+            clocks = NvmlClockSampler(phys)
+        except Exception:
+            clocks = ClockSampler(phys)
     if clocks:
         clocks.start()
-        time.sleep(0.3)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -234,9 +291,8 @@ def run_ours(args):
     if status:
         raise SystemExit(f"device status word 0x{status:x} after the timed region")
 
-    # algorithmic bytes per step, from the context lengths each step saw
-    hist = lens_hist[args.warmup:args.warmup + args.steps].cpu().numpy()
-    per = [chain_bytes_per_step(h, cfg) for h in hist]
+    # algorithmic bytes per step, from the context lengths every step starts from
+    per = [chain_bytes_per_step(snap["context_lens"].cpu().numpy(), cfg)]
     att_ms = np.mean([a.elapsed_time(b) for a, b in ev["attention"]])
     acc_ms = np.mean([a.elapsed_time(b) for a, b in ev["accept"]])
     att_bytes = float(np.mean([p["attention"] for p in per]))
@@ -251,6 +307,7 @@ def run_ours(args):
     units = cfg.batch * nq * world * args.steps
     value = units / (ms * 1e-3)
     step_bytes = att_bytes + acc_bytes
+    # kv_reserve, kv_write, attention (+ split merge), 3 accept kernels, kv_commit
     launches_per_step = 1 + 1 + 1 + (1 if _attn_splits(st, cfg) else 0) + 3 + 1
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -274,8 +331,9 @@ def run_ours(args):
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clk,
     }
-    line["e2e"] = run_e2e(args, ctx, cfg, st, tgt, drf, drafts, k_new, v_new, seq_offset, world,
-                          dist if world > 1 else None, dev)
+    if not args.no_e2e:
+        line["e2e"] = run_e2e(args, ctx, cfg, st, tgt, drf, drafts, k_new, v_new, seq_offset,
+                              world, dist if world > 1 else None, dev, restore)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cfg, st, tgt, drf, drafts, k_new, v_new, args)
     if rank == 0:
@@ -293,7 +351,8 @@ def _attn_splits(st, cfg):
     return _lib.load().kyro_verify_attention_workspace_size(C.byref(p)) > 0
 
 
-def run_e2e(args, ctx, cfg, st, tgt, drf, drafts, k_new, v_new, seq_offset, world, dist, dev):
+def run_e2e(args, ctx, cfg, st, tgt, drf, drafts, k_new, v_new, seq_offset, world, dist, dev,
+            restore):
     """The same step through the C ABI with host buffers: inputs copied from
     pinned host memory each step, results read back each step."""
     import torch
@@ -312,6 +371,7 @@ def run_e2e(args, ctx, cfg, st, tgt, drf, drafts, k_new, v_new, seq_offset, worl
     steps = max(3, min(args.steps, 10))
 
     def step(i):
+        restore()
         for n in h:
             d[n].copy_(h[n], non_blocking=True)
         kv_reserve(ctx, nq, st.block_table, st.context_lens, st.free_stack, st.free_top,
@@ -380,19 +440,25 @@ def _host_inputs(st, tgt, drf, drafts, k_new, v_new):
 
 
 def cpu_baseline(cfg, st, tgt, drf, drafts, k_new, v_new, args):
+    """The oracle's verify step over the whole config-1 batch on the host
+    cores, repeated for about ten seconds."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
     O.build()
     inp = _host_inputs(st, tgt, drf, drafts, k_new, v_new)
     nthreads = os.cpu_count() or 1
-    seqs = list(range(min(cfg.batch, args.cpu_sample)))
-    t = time.perf_counter()
-    _cpu_step(O, cfg, inp, seqs, 0, nthreads)
-    dt = time.perf_counter() - t
-    return {"value": len(seqs) * cfg.num_query / dt, "unit": UNIT, "cores": nthreads,
+    seqs = list(range(cfg.batch))
+    done, t0 = 0, time.perf_counter()
+    while True:
+        _cpu_step(O, cfg, inp, seqs, done, nthreads)
+        done += 1
+        dt = time.perf_counter() - t0
+        if dt > args.cpu_seconds or done >= 50:
+            break
+    return {"value": done * len(seqs) * cfg.num_query / dt, "unit": UNIT, "cores": nthreads,
             "kind": "port",
-            "sample": f"{len(seqs)} of {cfg.batch} config-1 sequences, one verify step "
-                      f"(kv write + attention + accept + commit), {dt:.2f} s"}
+            "sample": f"{done} verify steps over the full config-1 batch ({cfg.batch} sequences: "
+                      f"kv write + attention + accept + commit), {dt:.1f} s"}
 
 
 def run_reference(args):
@@ -443,12 +509,16 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-sample", type=int, default=8,
                     help="sequences per CPU step (cpu_baseline and --impl reference)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0,
+                    help="wall time the cpu_baseline leg repeats whole-batch steps for")
+    ap.add_argument("--no-e2e", action="store_true",
+                    help="skip the host-buffer leg (profiling runs)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         raise SystemExit("--warmup must be >= 3")
