@@ -17,8 +17,9 @@
 // so the query rows (24 for GQA 4 x 6 positions) sit in the N dimension in
 // 8-wide tiles without padding to 16.  Online softmax runs per query
 // column in the log2 domain.  The four warps' partial states are merged in
-// shared memory; when a sequence needs more than one split the partials go
-// to the workspace and verify_attention_merge_kernel combines them.
+// shared memory; when a sequence needs more than one split, each split
+// writes its partial state to the workspace and the split that finishes
+// last (atomic ticket) merges them all.
 #include <cuda_bf16.h>
 #include <cudaTypedefs.h>
 
@@ -33,6 +34,8 @@ constexpr int kConsumers = 4;         // consumer warps
 constexpr int kThreads = (kConsumers + 1) * 32;
 constexpr int kStages = 3;
 constexpr int kMaxCols = 32;          // query rows per work item
+constexpr int kMaxSplitBlocks = 512;  // KV blocks per work item
+constexpr int kMaxSplits = 64;        // work items per (sequence, KV head, row group)
 
 // Shared-memory geometry for head_dim D (64 or 128).
 template <int D>
@@ -43,9 +46,11 @@ struct Geo {
   static constexpr int kQStride = D + 8;               // padded bf16 row stride of the Q tile
   static constexpr int kQBytes = kMaxCols * kQStride * 2;
   static constexpr int kRingBytes = kStages * kStageBytes;
-  static constexpr int kMergeBytes = kConsumers * (D * kMaxCols + 2 * kMaxCols) * 4;
+  static constexpr int kMergeBytes =
+      (kConsumers * (D * kMaxCols + 2 * kMaxCols) + kMaxSplits * kMaxCols + kMaxCols) * 4;
   static_assert(kMergeBytes <= kRingBytes, "merge area reuses the ring");
-  static constexpr int kSmemBytes = 1024 + kRingBytes + kQBytes + kMaxCols * 8 + 64;
+  static constexpr int kSmemBytes =
+      1024 + kRingBytes + kQBytes + kMaxCols * 8 + kMaxSplitBlocks * 4 + 2 * kStages * 8 + 16;
 };
 
 struct AttnArgs {
@@ -66,8 +71,8 @@ verify_attention_kernel(const __grid_constant__ CUtensorMap tmK,
                         const int64_t* __restrict__ block_table,
                         const int64_t* __restrict__ context_lens,
                         const uint64_t* __restrict__ tree_mask, __nv_bfloat16* __restrict__ out,
-                        float* __restrict__ part_o, float* __restrict__ part_ml, AttnArgs a,
-                        uint32_t* status) {
+                        float* __restrict__ part_o, float* __restrict__ part_ml,
+                        uint32_t* __restrict__ tickets, AttnArgs a, uint32_t* status) {
   extern __shared__ uint8_t smem_raw[];
   using G = Geo<D>;
   constexpr int kD = D;
@@ -93,7 +98,8 @@ verify_attention_kernel(const __grid_constant__ CUtensorMap tmK,
   if (split >= nsplit) return;
   const int blk0 = split * a.split_blocks;
   const int blk1 = min(nblk, blk0 + a.split_blocks);
-  const int niter = (blk1 - blk0 + kConsumers - 1) / kConsumers;
+  const int nb = blk1 - blk0;
+  const int niter = (nb + kConsumers - 1) / kConsumers;
   const int col0 = grp * kMaxCols;
   const int ncols = min(kMaxCols, a.rows - col0);
 
@@ -103,7 +109,9 @@ verify_attention_kernel(const __grid_constant__ CUtensorMap tmK,
   uint8_t* ring = smem_raw + (ring_s - raw);
   uint8_t* qtile = ring + kRingBytes;
   uint64_t* col_mask = reinterpret_cast<uint64_t*>(qtile + kQBytes);
-  uint64_t* bars = col_mask + kMaxCols;  // full[kStages], empty[kStages]
+  int32_t* ids = reinterpret_cast<int32_t*>(col_mask + kMaxCols);      // [kMaxSplitBlocks]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ids + kMaxSplitBlocks);  // full[], empty[]
+  int* sh_last = reinterpret_cast<int*>(bars + 2 * kStages);
   const uint32_t q_s = ring_s + kRingBytes;
   const uint32_t bar_s = kyro::ptx::smem_addr(bars);
 
@@ -114,35 +122,26 @@ verify_attention_kernel(const __grid_constant__ CUtensorMap tmK,
     }
     kyro::ptx::fence_barrier_init();
   }
-  // ---- Q rows of this work item -> padded smem tile; column masks
-  for (int i = tid; i < kMaxCols * (kD / 8); i += kThreads) {
-    const int col = i / (kD / 8), ch = i % (kD / 8);
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (col < ncols) {
-      const int r = col0 + col, j = r / a.group, gi = r % a.group;
-      const int h = kvh * a.group + gi;
-      v = *reinterpret_cast<const uint4*>(q + (((int64_t)b * a.nq + j) * a.hq + h) * kD + ch * 8);
-    }
-    *reinterpret_cast<uint4*>(qtile + col * kQStride * 2 + ch * 16) = v;
-  }
-  for (int col = tid; col < kMaxCols; col += kThreads) {
-    uint64_t m = 0;
-    if (col < ncols) {
-      const int j = (col0 + col) / a.group;
-      m = tree_mask ? tree_mask[(int64_t)b * a.nq + j]
-                    : (j >= 63 ? ~0ull : ((1ull << (j + 1)) - 1ull));
-    }
-    col_mask[col] = m;
-  }
   __syncthreads();
 
   bool timed_out = false;
+  float o[kMT][NT][4];
+  float m_run[NT][2], l_run[NT][2];
   if (warp == kConsumers) {
-    // ================= producer
+    // ================= producer warp: block ids of this split -> smem, then TMA
+    const int64_t* bt = block_table + (int64_t)b * a.max_blocks + blk0;
+    for (int i = lane; i < nb; i += 32) {
+      int64_t phys = bt[i];
+      if (phys < 0 || phys >= a.num_blocks) {
+        kyro::dev::flag(status, KYRO_DEV_BAD_BLOCK);
+        phys = 0;
+      }
+      ids[i] = (int32_t)phys;
+    }
+    __syncwarp();
     if (lane == 0) {
       kyro::ptx::prefetch_tensormap(&tmK);
       kyro::ptx::prefetch_tensormap(&tmV);
-      const int64_t* bt = block_table + (int64_t)b * a.max_blocks;
       for (int it = 0; it < niter; ++it) {
         const int s = it % kStages;
         if (it >= kStages && !timed_out) {
@@ -152,16 +151,11 @@ verify_attention_kernel(const __grid_constant__ CUtensorMap tmK,
             kyro::dev::flag(status, KYRO_DEV_WAIT_TIMEOUT);
           }
         }
-        const int nvalid = min(kConsumers, blk1 - blk0 - it * kConsumers);
+        const int nvalid = min(kConsumers, nb - it * kConsumers);
         const uint32_t full = bar_s + 8 * s;
         kyro::ptx::mbar_arrive_expect_tx(full, (uint32_t)(nvalid * kSlotBytes));
         for (int w = 0; w < nvalid; ++w) {
-          int64_t phys = bt[blk0 + it * kConsumers + w];
-          if (phys < 0 || phys >= a.num_blocks) {
-            kyro::dev::flag(status, KYRO_DEV_BAD_BLOCK);
-            phys = 0;
-          }
-          const int32_t y = (int32_t)((phys * a.hkv + kvh) * kBS);
+          const int32_t y = (ids[it * kConsumers + w] * a.hkv + kvh) * kBS;
           const uint32_t dst = ring_s + s * kStageBytes + w * kSlotBytes;
 #pragma unroll
           for (int half = 0; half < kD / 64; ++half) {
@@ -172,12 +166,30 @@ verify_attention_kernel(const __grid_constant__ CUtensorMap tmK,
       }
     }
     __syncwarp();
-  }
+  } else {
+    // ================= consumer warps: Q tile and masks while the first loads fly
+    for (int i = tid; i < kMaxCols * (kD / 8); i += kConsumers * 32) {
+      const int col = i / (kD / 8), ch = i % (kD / 8);
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (col < ncols) {
+        const int r = col0 + col, j = r / a.group, gi = r % a.group;
+        const int h = kvh * a.group + gi;
+        v = *reinterpret_cast<const uint4*>(q + (((int64_t)b * a.nq + j) * a.hq + h) * kD +
+                                            ch * 8);
+      }
+      *reinterpret_cast<uint4*>(qtile + col * kQStride * 2 + ch * 16) = v;
+    }
+    for (int col = tid; col < kMaxCols; col += kConsumers * 32) {
+      uint64_t m = 0;
+      if (col < ncols) {
+        const int j = (col0 + col) / a.group;
+        m = tree_mask ? tree_mask[(int64_t)b * a.nq + j]
+                      : (j >= 63 ? ~0ull : ((1ull << (j + 1)) - 1ull));
+      }
+      col_mask[col] = m;
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory");
 
-  // ================= consumers
-  float o[kMT][NT][4];
-  float m_run[NT][2], l_run[NT][2];
-  if (warp < kConsumers) {
 #pragma unroll
     for (int mt = 0; mt < kMT; ++mt)
 #pragma unroll
@@ -231,7 +243,8 @@ verify_attention_kernel(const __grid_constant__ CUtensorMap tmK,
         const int64_t tok0 = (int64_t)blk * kBS;
         const bool need_mask = tok0 + kBS > ctx;
         const int trow = lane >> 2;
-        uint32_t pb[NT][2];
+        float alpha[NT][2];
+        bool moved = false;
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
@@ -254,20 +267,32 @@ verify_attention_kernel(const __grid_constant__ CUtensorMap tmK,
             cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 16));
             const float m_new = fmaxf(m_run[nt][c], cm);
             const float m_use = m_new == -INFINITY ? 0.0f : m_new;
-            const float alpha = kyro::ptx::fast_exp2(m_run[nt][c] - m_use);
+            alpha[nt][c] = kyro::ptx::fast_exp2(m_run[nt][c] - m_use);
+            moved |= m_new != m_run[nt][c];
             const float p0 = kyro::ptx::fast_exp2(sc[nt][c] - m_use);
             const float p1 = kyro::ptx::fast_exp2(sc[nt][c + 2] - m_use);
             sc[nt][c] = p0;
             sc[nt][c + 2] = p1;
-            l_run[nt][c] = l_run[nt][c] * alpha + p0 + p1;
+            l_run[nt][c] = l_run[nt][c] * alpha[nt][c] + p0 + p1;
             m_run[nt][c] = m_new;
-#pragma unroll
-            for (int mt = 0; mt < kMT; ++mt) {
-              o[mt][nt][c] *= alpha;
-              o[mt][nt][c + 2] *= alpha;
-            }
           }
-          // P^T fragment (tokens x cols) -> B operand (k = tokens, n = cols)
+        }
+        // rescale O only when some running max moved (alpha == 1 otherwise)
+        if (__any_sync(0xffffffffu, moved)) {
+#pragma unroll
+          for (int mt = 0; mt < kMT; ++mt)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              o[mt][nt][0] *= alpha[nt][0];
+              o[mt][nt][1] *= alpha[nt][1];
+              o[mt][nt][2] *= alpha[nt][0];
+              o[mt][nt][3] *= alpha[nt][1];
+            }
+        }
+        // P^T fragment (tokens x cols) -> B operand (k = tokens, n = cols)
+        uint32_t pb[NT][2];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
           pb[nt][0] = kyro::ptx::movmatrix_trans(kyro::ptx::pack_bf16x2(sc[nt][0], sc[nt][1]));
           pb[nt][1] = kyro::ptx::movmatrix_trans(kyro::ptx::pack_bf16x2(sc[nt][2], sc[nt][3]));
         }
@@ -304,6 +329,8 @@ verify_attention_kernel(const __grid_constant__ CUtensorMap tmK,
   float* mo = reinterpret_cast<float*>(ring);           // [warp][d][col]
   float* mm = mo + kConsumers * kD * kMaxCols;          // [warp][col]
   float* ml = mm + kConsumers * kMaxCols;               // [warp][col]
+  float* fscale = ml + kConsumers * kMaxCols;           // [split][col] (last-CTA merge)
+  float* finv = fscale + kMaxSplits * kMaxCols;         // [col]
   if (warp < kConsumers) {
     float* wo = mo + warp * kD * kMaxCols;
 #pragma unroll
@@ -330,8 +357,8 @@ verify_attention_kernel(const __grid_constant__ CUtensorMap tmK,
   __syncthreads();
   const bool single = nsplit == 1;
   const int64_t item = ((int64_t)b * a.hkv + kvh) * a.ngroups + grp;
-  float* po = part_o + (item * a.max_splits + split) * (kMaxCols * kD);
-  float* pml = part_ml + (item * a.max_splits + split) * (kMaxCols * 2);
+  float* po = part_o + item * a.max_splits * (kMaxCols * kD);
+  float* pml = part_ml + item * a.max_splits * (kMaxCols * 2);
   for (int i = tid; i < ncols * kD; i += kThreads) {
     const int col = i / kD, d = i % kD;
     float M = -INFINITY;
@@ -348,55 +375,52 @@ verify_attention_kernel(const __grid_constant__ CUtensorMap tmK,
     if (single) {
       const int r = col0 + col, j = r / a.group, gi = r % a.group;
       const int h = kvh * a.group + gi;
-      out[(((int64_t)b * a.nq + j) * a.hq + h) * kD + d] = __float2bfloat16(L > 0.0f ? O / L : 0.0f);
+      out[(((int64_t)b * a.nq + j) * a.hq + h) * kD + d] =
+          __float2bfloat16(L > 0.0f ? O / L : 0.0f);
     } else {
-      po[col * kD + d] = O;
+      po[(split * kMaxCols + col) * kD + d] = O;
       if (d == 0) {
-        pml[col * 2 + 0] = M;
-        pml[col * 2 + 1] = L;
+        pml[(split * kMaxCols + col) * 2 + 0] = M;
+        pml[(split * kMaxCols + col) * 2 + 1] = L;
       }
     }
   }
-}
+  if (single) return;
 
-// Combine the splits of every (sequence, KV head, row group) with more than one.
-template <int kD>
-__global__ void __launch_bounds__(256)
-verify_attention_merge_kernel(const int64_t* __restrict__ context_lens,
-                              const float* __restrict__ part_o, const float* __restrict__ part_ml,
-                              __nv_bfloat16* __restrict__ out, AttnArgs a) {
-  const int64_t item = blockIdx.x;
-  const int grp = (int)(item % a.ngroups);
-  const int kvh = (int)((item / a.ngroups) % a.hkv);
-  const int b = (int)(item / ((int64_t)a.ngroups * a.hkv));
-  const int64_t ctx = context_lens[b];
-  const int64_t total = ctx + a.nq;
-  if (ctx < 0 || (total + kBS - 1) / kBS > a.max_blocks) return;
-  const int nblk = (int)((total + kBS - 1) / kBS);
-  const int nsplit = (nblk + a.split_blocks - 1) / a.split_blocks;
-  if (nsplit <= 1) return;
-  const int col0 = grp * kMaxCols;
-  const int ncols = min(kMaxCols, a.rows - col0);
-  const float* po = part_o + item * a.max_splits * (kMaxCols * kD);
-  const float* pml = part_ml + item * a.max_splits * (kMaxCols * 2);
-  for (int i = threadIdx.x; i < ncols * kD; i += blockDim.x) {
-    const int col = i / kD, d = i % kD;
+  // ---- the last split of this (sequence, KV head, row group) merges all splits
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    const uint32_t t = atomicAdd(&tickets[item], 1u);
+    *sh_last = (t == (uint32_t)nsplit - 1);
+  }
+  __syncthreads();
+  if (!*sh_last) return;
+  __threadfence();
+  for (int col = tid; col < ncols; col += kThreads) {
     float M = -INFINITY;
-    for (int s = 0; s < nsplit; ++s) M = fmaxf(M, pml[(s * kMaxCols + col) * 2]);
+    for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, __ldcg(&pml[(sp * kMaxCols + col) * 2]));
     const float Mu = M == -INFINITY ? 0.0f : M;
-    float L = 0.0f, O = 0.0f;
-    for (int s = 0; s < nsplit; ++s) {
-      const float f = kyro::ptx::fast_exp2(pml[(s * kMaxCols + col) * 2] - Mu);
-      L += f * pml[(s * kMaxCols + col) * 2 + 1];
-      O += f * po[(s * kMaxCols + col) * kD + d];
+    float L = 0.0f;
+    for (int sp = 0; sp < nsplit; ++sp) {
+      const float f = kyro::ptx::fast_exp2(__ldcg(&pml[(sp * kMaxCols + col) * 2]) - Mu);
+      fscale[sp * kMaxCols + col] = f;
+      L += f * __ldcg(&pml[(sp * kMaxCols + col) * 2 + 1]);
     }
+    finv[col] = L > 0.0f ? 1.0f / L : 0.0f;
+  }
+  __syncthreads();
+  for (int i = tid; i < ncols * kD; i += kThreads) {
+    const int col = i / kD, d = i % kD;
+    float O = 0.0f;
+    for (int sp = 0; sp < nsplit; ++sp)
+      O += fscale[sp * kMaxCols + col] * __ldcg(&po[(sp * kMaxCols + col) * kD + d]);
     const int r = col0 + col, j = r / a.group, gi = r % a.group;
     const int h = kvh * a.group + gi;
-    out[(((int64_t)b * a.nq + j) * a.hq + h) * kD + d] = __float2bfloat16(L > 0.0f ? O / L : 0.0f);
+    out[(((int64_t)b * a.nq + j) * a.hq + h) * kD + d] = __float2bfloat16(O * finv[col]);
   }
+  if (tid == 0) tickets[item] = 0;
 }
-
-// ------------------------------------------------------------------ host
 
 }  // namespace
 
@@ -437,7 +461,7 @@ int make_kv_map(CUtensorMap* map, const void* base, int64_t rows, int kD) {
 struct Plan {
   AttnArgs a;
   int nt;
-  size_t part_o_bytes, part_ml_bytes;
+  size_t part_o_bytes, part_ml_bytes, ticket_bytes;
 };
 
 int plan(const kyro_attn_params* p, int num_sms, Plan* out) {
@@ -473,51 +497,63 @@ int plan(const kyro_attn_params* p, int num_sms, Plan* out) {
   const float scale = p->scale > 0.0f ? p->scale : 1.0f / sqrtf((float)p->head_dim);
   a.scale_log2 = scale * 1.4426950408889634f;
   a.d = p->head_dim;
-  int split = p->kv_split_blocks;
+  int64_t split = p->kv_split_blocks;
   if (split == 0) {
     // aim for about four waves of work items at two CTAs per SM, assuming
     // half the table width is used on average
     const int64_t items = (int64_t)a.B * a.hkv * a.ngroups;
     const int64_t avg_blocks = (a.max_blocks + 1) / 2;
     const int64_t target = (int64_t)num_sms * 2 * 4;
-    int64_t s = (items * avg_blocks + target - 1) / (target > 0 ? target : 1);
-    s = (s + kConsumers - 1) / kConsumers * kConsumers;
-    if (s < 16) s = 16;
-    split = (int)s;
+    split = (items * avg_blocks + target - 1) / (target > 0 ? target : 1);
+    split = (split + kConsumers - 1) / kConsumers * kConsumers;
+    if (split < 16) split = 16;
   }
-  a.split_blocks = split;
-  a.max_splits = (a.max_blocks + split - 1) / split;
+  // a work item holds at most kMaxSplitBlocks block ids, and a sequence at
+  // most kMaxSplits work items
+  if (split > kMaxSplitBlocks) split = kMaxSplitBlocks;
+  const int64_t min_split = (a.max_blocks + kMaxSplits - 1) / kMaxSplits;
+  if (split < min_split) split = min_split;
+  KY_REQUIRE(split <= kMaxSplitBlocks,
+             "kyro_verify_attention: max_blocks_per_seq %d needs more than %d work items",
+             a.max_blocks, kMaxSplits);
+  a.split_blocks = (int)split;
+  a.max_splits = (int)((a.max_blocks + split - 1) / split);
   pl.nt = a.rows >= kMaxCols ? 4 : (a.rows + 7) / 8;
-  const int64_t items = (int64_t)a.B * a.hkv * a.ngroups * (a.max_splits > 1 ? a.max_splits : 0);
+  const int64_t groups = (int64_t)a.B * a.hkv * a.ngroups;
+  const int64_t items = groups * (a.max_splits > 1 ? a.max_splits : 0);
   pl.part_o_bytes = (size_t)items * kMaxCols * p->head_dim * 4;
   pl.part_ml_bytes = (size_t)items * kMaxCols * 2 * 4;
+  pl.ticket_bytes = a.max_splits > 1 ? (size_t)groups * 4 : 0;
   *out = pl;
   return KYRO_OK;
 }
 
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
 size_t ws_bytes(const Plan& pl) {
-  return ((pl.part_o_bytes + 255) & ~size_t(255)) + ((pl.part_ml_bytes + 255) & ~size_t(255));
+  return align256(pl.part_o_bytes) + align256(pl.part_ml_bytes) + align256(pl.ticket_bytes);
 }
 
 template <int NT, int D>
 void launch(const Plan& pl, dim3 grid, cudaStream_t st, const CUtensorMap& mk, const CUtensorMap& mv,
             const void* q, const int64_t* bt, const int64_t* cl, const uint64_t* tm, void* out,
-            float* po, float* pml, uint32_t* status) {
+            float* po, float* pml, uint32_t* tk, uint32_t* status) {
   cudaFuncSetAttribute(verify_attention_kernel<NT, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        Geo<D>::kSmemBytes);
   verify_attention_kernel<NT, D><<<grid, kThreads, Geo<D>::kSmemBytes, st>>>(
-      mk, mv, (const __nv_bfloat16*)q, bt, cl, tm, (__nv_bfloat16*)out, po, pml, pl.a, status);
+      mk, mv, (const __nv_bfloat16*)q, bt, cl, tm, (__nv_bfloat16*)out, po, pml, tk, pl.a, status);
 }
 
 template <int D>
 void launch_d(const Plan& pl, dim3 grid, cudaStream_t st, const CUtensorMap& mk,
               const CUtensorMap& mv, const void* q, const int64_t* bt, const int64_t* cl,
-              const uint64_t* tm, void* out, float* po, float* pml, uint32_t* status) {
+              const uint64_t* tm, void* out, float* po, float* pml, uint32_t* tk,
+              uint32_t* status) {
   switch (pl.nt) {
-    case 1: launch<1, D>(pl, grid, st, mk, mv, q, bt, cl, tm, out, po, pml, status); break;
-    case 2: launch<2, D>(pl, grid, st, mk, mv, q, bt, cl, tm, out, po, pml, status); break;
-    case 3: launch<3, D>(pl, grid, st, mk, mv, q, bt, cl, tm, out, po, pml, status); break;
-    default: launch<4, D>(pl, grid, st, mk, mv, q, bt, cl, tm, out, po, pml, status); break;
+    case 1: launch<1, D>(pl, grid, st, mk, mv, q, bt, cl, tm, out, po, pml, tk, status); break;
+    case 2: launch<2, D>(pl, grid, st, mk, mv, q, bt, cl, tm, out, po, pml, tk, status); break;
+    case 3: launch<3, D>(pl, grid, st, mk, mv, q, bt, cl, tm, out, po, pml, tk, status); break;
+    default: launch<4, D>(pl, grid, st, mk, mv, q, bt, cl, tm, out, po, pml, tk, status); break;
   }
 }
 
@@ -550,8 +586,12 @@ int kyro_verify_attention(kyro_ctx* ctx, const kyro_attn_params* p, const void* 
   if (need > 0 && (workspace_bytes < need || !workspace))
     return kyro::set_error(KYRO_ERR_WORKSPACE, "kyro_verify_attention: workspace %zu < %zu bytes",
                            workspace_bytes, need);
+  KY_REQUIRE(need == 0 || (uintptr_t)workspace % 256 == 0,
+             "kyro_verify_attention: workspace must be 256-byte aligned");
   float* po = (float*)workspace;
-  float* pml = (float*)((char*)workspace + ((pl.part_o_bytes + 255) & ~size_t(255)));
+  float* pml = (float*)((char*)workspace + align256(pl.part_o_bytes));
+  uint32_t* tk = (uint32_t*)((char*)workspace + align256(pl.part_o_bytes) +
+                             align256(pl.part_ml_bytes));
   CUtensorMap mk, mv;
   const int64_t rows = (int64_t)p->num_blocks * p->num_kv_heads * kBS;
   KY_TRY(make_kv_map(&mk, k_cache, rows, p->head_dim));
@@ -559,24 +599,18 @@ int kyro_verify_attention(kyro_ctx* ctx, const kyro_attn_params* p, const void* 
   dim3 grid((unsigned)pl.a.max_splits, (unsigned)(pl.a.hkv * pl.a.ngroups), (unsigned)pl.a.B);
   KY_REQUIRE(pl.a.B <= 65535, "kyro_verify_attention: batch %d > 65535", pl.a.B);
   cudaStream_t st = ctx->stream;
+  if (pl.ticket_bytes) {
+    // split tickets start at zero; the merging split also resets its ticket
+    cudaError_t err = cudaMemsetAsync(tk, 0, pl.ticket_bytes, st);
+    if (err != cudaSuccess) return kyro::cuda_error(err, "cudaMemsetAsync(attention tickets)");
+  }
   if (p->head_dim == 128)
-    launch_d<128>(pl, grid, st, mk, mv, q, block_table, context_lens, tree_mask, out, po, pml,
+    launch_d<128>(pl, grid, st, mk, mv, q, block_table, context_lens, tree_mask, out, po, pml, tk,
                   ctx->d_status);
   else
-    launch_d<64>(pl, grid, st, mk, mv, q, block_table, context_lens, tree_mask, out, po, pml,
+    launch_d<64>(pl, grid, st, mk, mv, q, block_table, context_lens, tree_mask, out, po, pml, tk,
                  ctx->d_status);
-  KY_TRY(kyro::check_launch("verify_attention_kernel"));
-  if (pl.a.max_splits > 1) {
-    const int64_t items = (int64_t)pl.a.B * pl.a.hkv * pl.a.ngroups;
-    if (p->head_dim == 128)
-      verify_attention_merge_kernel<128><<<(unsigned)items, 256, 0, st>>>(context_lens, po, pml,
-                                                                         (__nv_bfloat16*)out, pl.a);
-    else
-      verify_attention_merge_kernel<64><<<(unsigned)items, 256, 0, st>>>(context_lens, po, pml,
-                                                                        (__nv_bfloat16*)out, pl.a);
-    KY_TRY(kyro::check_launch("verify_attention_merge_kernel"));
-  }
-  return KYRO_OK;
+  return kyro::check_launch("verify_attention_kernel");
 }
 
 }  // extern "C"

@@ -223,9 +223,14 @@ KY_HD uint64_t ky_cdf_threshold(uint32_t odd, uint64_t W) {
  * s_i = z_i * inv_t:
  *   m_c = max_{i in c} s_i,  e_i = ky_exp(s_i - m_c),  E_c = sum fix40(e_i)
  *   M   = max_c m_c
- *   S   = sum over shards r (in rank order) of
- *           sum over chunks c of r (in chunk order) of E_c*2^-40 * ky_exp(m_c - M)
- *         (double precision, each partial sum starting from 0.0)
+ *   mass_c = E_c*2^-40 * ky_exp(m_c - M)                    (double)
+ *   S_r = butterfly sum of the chunk masses of shard r:
+ *           t[l] = sum of mass_c over c = l, l+32, l+64, ... (in that order,
+ *                  starting from 0.0), l = 0..31;
+ *           for off = 16, 8, 4, 2, 1: t[l] = t[l] + t[l ^ off];  S_r = t[0]
+ *         (the xor-shuffle reduction of a 32-lane warp, every lane ends
+ *          with the same value)
+ *   S   = sum of S_r over shards in rank order, starting from 0.0
  *   g_c = (float)(ky_exp(m_c - M) / S)        (double division)
  *   p_i = e_i * g_c                           (fp32)
  * The same row statistics drive the accept test, the residual and the
@@ -242,6 +247,17 @@ KY_HD double ky_chunk_mass(uint64_t E, float m_c, float M) {
 
 KY_HD float ky_chunk_scale(float m_c, float M, double S) {
   return (float)KY_DDIV((double)ky_exp(KY_FSUB(m_c, M)), S);
+}
+
+/* The butterfly combination of 32 partial sums (host side; the device uses
+ * __shfl_xor_sync with the same offsets). */
+KY_HD double ky_butterfly32(double t[32]) {
+  for (int off = 16; off > 0; off >>= 1) {
+    double n[32];
+    for (int l = 0; l < 32; ++l) n[l] = KY_DADD(t[l], t[l ^ off]);
+    for (int l = 0; l < 32; ++l) t[l] = n[l];
+  }
+  return t[0];
 }
 
 /* accept iff u < p/q (Leviathan et al. 2023, Alg. 1; u < min(1,p/q) since u < 1) */

@@ -7,22 +7,28 @@
 // to the host.  Everything here stays on the device and is batched.
 //
 // The normaliser contract of kyro_math.h makes every decision reproducible:
-// per-chunk maxima, ky_exp, exact integer (fix40) chunk masses, a fixed-order
-// double combination, and integer (fix62) inverse-CDF weights.  Integer
-// sums do not depend on how threads are arranged, so the parallel kernels
-// below reproduce the sequential oracle bit for bit.
+// per-chunk maxima, ky_exp, exact integer (fix40) chunk masses, a fixed
+// butterfly combination in double, and integer (fix62) inverse-CDF weights.
+// Integer sums do not depend on how threads are arranged, so the parallel
+// kernel reproduces the sequential oracle bit for bit.
 //
-// Three launches per call:
-//   accept_row_stats_kernel  one CTA per (row, 2048-entry chunk): chunk max
-//                            (and argmax), e at the draft token, and the
-//                            fix40 chunk mass.  Reads every logit once.
-//   accept_decide_kernel     one CTA per sequence: row normalisers, the k
-//                            accept tests, the accepted length, and the
-//                            descriptor of the row to resample from.
-//   accept_final_row_kernel  CTAs over the chunks of each sequence's final
-//                            row: fix62 weights (residual or p) and chunk
-//                            sums; the last CTA to finish finds the chunk
-//                            holding the cut point and scans it.
+// One persistent launch does the whole step.  Warps take units from an
+// atomic work queue in a fixed order:
+//   stats unit   one 2048-logit chunk of one row (target or draft) by one
+//                warp, 64 logits per lane held in registers: chunk max (or
+//                argmax), e at the draft token, fix40 chunk mass.  The next
+//                unit's loads are issued before the current one is reduced.
+//   decide       run inline by the warp that finishes a sequence's last
+//                stats unit: row normalisers, the k accept tests, the
+//                accepted length, and the row to draw the emitted token from.
+//   final unit   512 logits of that row: fix62 weights (residual or p) and
+//                their sum.  The warp that finishes a row's last final unit
+//                locates the sub-range holding the cut point and scans it.
+// A sequence's final units are queued kDelta sequences after its stats
+// units, so the final row is read again while it is still in L2, and a
+// final unit waits (bounded) for its sequence's decision.  Units a waiting
+// warp holds always come later in the queue than the unit it waits on, so
+// the wait always ends.
 //
 // This file is compiled with --fmad=false; the shared arithmetic also uses
 // explicit round-to-nearest intrinsics.
@@ -31,589 +37,734 @@
 
 namespace {
 
-constexpr int kThreads = 256;
-constexpr int kWarps = kThreads / 32;
-constexpr int kChunk = KY_CHUNK;
-static_assert(kChunk == kThreads * 8, "a chunk is two float4 per thread");
-constexpr int kMaxChunks = 256;  // V <= 524288
+constexpr int kChunk = KY_CHUNK;           // logits per stats unit
+constexpr int kPerLane = kChunk / 32;      // 64
+constexpr int kVecPerLane = kPerLane / 4;  // 16 float4
+constexpr int kSub = 512;                  // logits per final unit
+constexpr int kSubVec = kSub / 128;        // 4 float4 per lane
+constexpr int kSubsPerChunk = kChunk / kSub;
+constexpr int kWarps = 4;                  // warps per CTA
+constexpr int kThreads = kWarps * 32;
+constexpr int kMaxChunks = 256;            // V <= 524288
 constexpr int kMaxDraft = 64;
 constexpr int kMaxRows = 2 * kMaxDraft + 1;
+constexpr int kDelta = 6;                  // sequences between stats and final units
+constexpr int kBatch = 2;                  // units taken per queue access
 
 struct ChunkStat {
-  float m;                 // chunk max of s = z * inv_t (or of z, greedy)
-  int32_t arg;             // lowest index attaining m
-  unsigned long long E;    // sum of fix40(ky_exp(s - m)) over the chunk
+  float m;               // chunk max of s = z * inv_t (or of z, greedy)
+  int32_t arg;           // lowest index attaining m (greedy)
+  unsigned long long E;  // sum of fix40(ky_exp(s - m)) over the chunk
 };
 
 // The row a sequence (or a sampled row) draws its emitted token from.
 struct FinalRow {
-  int64_t p_row;    // row index into the target (or sampled) logits
-  int64_t q_row;    // row index into the draft logits, -1 = sample from p
-  int64_t p_stat;   // row index into the stats array
-  int64_t q_stat;
+  int64_t p_row;      // row index into plog
+  int64_t q_row;      // row index into qlog, -1 = sample from p
+  int64_t p_stat;     // stats row of p
+  int64_t q_stat;     // stats row of q
   float Mp, Mq;
   double Sp, Sq;
-  uint32_t odd;     // uniform numerator for the inverse CDF
+  uint32_t odd;       // uniform numerator for the inverse CDF
   int32_t out_index;  // where the token (and its probability) goes
-  int32_t skip;     // 1: token already written by the decide kernel
+  int32_t skip;       // 1: the decide step already wrote the token
   int32_t _pad;
 };
 
-__host__ __device__ inline size_t align_up(size_t x) {
-  return (x + 255) & ~size_t(255);
-}
-
-struct Workspace {
+struct Args {
+  const float* plog;            // target logits (accept) or the rows to sample
+  const float* qlog;            // draft logits (stochastic accept) or null
+  const int32_t* draft_tokens;  // [B, k] (accept)
+  int B;                        // sequences (accept) or rows (sampler)
+  int k;                        // drafts per sequence; 0 for the sampler
+  int R;                        // stats rows per sequence
+  int64_t V;
+  int nchunks, nsub;
+  float inv_t;
+  int stoch;                    // softmax statistics (else argmax only)
+  int greedy_ref;
+  int sample;                   // draft-sampler call
+  int pos_div;                  // sampler: Philox seq = r / pos_div, pos = r % pos_div
+  uint64_t seed;
+  uint32_t step;
+  int64_t seq_offset;
+  int32_t* out_accept_len;
+  int32_t* out_tokens;
+  int32_t* out_num_tokens;
+  float* out_probs;             // accept: [B,k,2] (p,q); sampler: [rows]
   ChunkStat* stats;
   float* ex;
   FinalRow* final_rows;
   unsigned long long* W;
-  uint32_t* ticket;
+  uint32_t* cnt_a;
+  uint32_t* cnt_c;
+  uint32_t* ready;
+  unsigned long long* queue;
+  int ua, uc;                   // stats units and final units per sequence
+  long long total;
+  uint32_t* status;
+};
+
+__host__ __device__ inline size_t align_up(size_t x) { return (x + 255) & ~size_t(255); }
+
+// Workspace: counters first (zeroed before every launch), then the rest.
+struct Workspace {
+  unsigned long long* queue;
+  uint32_t* cnt_a;
+  uint32_t* cnt_c;
+  uint32_t* ready;
+  size_t counter_bytes;
+  ChunkStat* stats;
+  float* ex;
+  FinalRow* final_rows;
+  unsigned long long* W;
   size_t bytes;
 };
 
-Workspace carve(void* base, int64_t stat_rows, int64_t nchunks, int64_t final_rows) {
+Workspace carve(void* base, int64_t B, int64_t R, int64_t nchunks, int64_t nsub) {
   Workspace w;
-  size_t off = 0;
   char* p = (char*)base;
+  size_t off = 0;
+  w.queue = (unsigned long long*)(p + off);
+  off += 256;
+  w.cnt_a = (uint32_t*)(p + off);
+  off += align_up(4 * (size_t)B);
+  w.cnt_c = (uint32_t*)(p + off);
+  off += align_up(4 * (size_t)B);
+  w.ready = (uint32_t*)(p + off);
+  off += align_up(4 * (size_t)B);
+  w.counter_bytes = off;
   w.stats = (ChunkStat*)(p + off);
-  off += align_up(sizeof(ChunkStat) * (size_t)(stat_rows * nchunks));
+  off += align_up(sizeof(ChunkStat) * (size_t)(B * R * nchunks));
   w.ex = (float*)(p + off);
-  off += align_up(sizeof(float) * (size_t)stat_rows);
+  off += align_up(sizeof(float) * (size_t)(B * R));
   w.final_rows = (FinalRow*)(p + off);
-  off += align_up(sizeof(FinalRow) * (size_t)final_rows);
+  off += align_up(sizeof(FinalRow) * (size_t)B);
   w.W = (unsigned long long*)(p + off);
-  off += align_up(sizeof(unsigned long long) * (size_t)(final_rows * nchunks));
-  w.ticket = (uint32_t*)(p + off);
-  off += align_up(sizeof(uint32_t) * (size_t)final_rows);
+  off += align_up(sizeof(unsigned long long) * (size_t)(B * nsub));
   w.bytes = off;
   return w;
 }
 
-// ------------------------------------------------------------ device helpers
+// ------------------------------------------------------------ warp helpers
 
-// Exclusive block-wide prefix of a u64 per thread; returns the block total
-// through *total.  `sh` holds kWarps entries.
-__device__ unsigned long long block_exclusive_scan_u64(unsigned long long v,
-                                                       unsigned long long* sh,
-                                                       unsigned long long* total) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  unsigned long long inc = v;
+__device__ __forceinline__ unsigned long long warp_sum(unsigned long long v) {
+  return kyro::dev::warp_sum_u64(v);
+}
+
+__device__ __forceinline__ double warp_butterfly(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = KY_DADD(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// inclusive warp scan of a u64
+__device__ __forceinline__ unsigned long long warp_inclusive(unsigned long long v) {
+  const int lane = threadIdx.x & 31;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
-    unsigned long long t = __shfl_up_sync(0xffffffffu, inc, o);
-    if (lane >= o) inc += t;
+    unsigned long long t = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += t;
   }
-  __syncthreads();
-  if (lane == 31) sh[warp] = inc;
-  __syncthreads();
-  unsigned long long warp_base = 0, all = 0;
-#pragma unroll
-  for (int w = 0; w < kWarps; ++w) {
-    unsigned long long s = sh[w];
-    if (w < warp) warp_base += s;
-    all += s;
-  }
-  *total = all;
-  return warp_base + inc - v;
+  return v;
 }
 
-__device__ unsigned long long block_sum_u64(unsigned long long v, unsigned long long* sh) {
-  unsigned long long t;
-  block_exclusive_scan_u64(v, sh, &t);
-  return t;
-}
-
-// Load the 8 logits of chunk `c` this thread owns: elements
-// c*2048 + g*1024 + 4*tid + i for g in {0,1}, i in {0..3}.
+// The 64 logits of chunk c this lane owns: float4 i (0..15) covers elements
+// c*2048 + (i*32 + lane)*4 + 0..3.  Entries beyond V read as -inf.
 template <bool VEC>
-__device__ __forceinline__ void load_chunk(const float* row, int64_t V, int c, float (&v)[8],
-                                           int (&idx)[8]) {
+__device__ __forceinline__ void load_chunk(const float* __restrict__ row, int64_t V, int c,
+                                           float (&v)[kPerLane]) {
+  const int lane = threadIdx.x & 31;
   const int64_t base = (int64_t)c * kChunk;
 #pragma unroll
-  for (int g = 0; g < 2; ++g) {
-    const int64_t e0 = base + g * 1024 + 4 * threadIdx.x;
-    if (VEC && e0 + 3 < V) {
-      float4 f = __ldcs(reinterpret_cast<const float4*>(row + e0));
-      v[4 * g + 0] = f.x;
-      v[4 * g + 1] = f.y;
-      v[4 * g + 2] = f.z;
-      v[4 * g + 3] = f.w;
+  for (int i = 0; i < kVecPerLane; ++i) {
+    const int64_t e0 = base + (i * 32 + lane) * 4;
+    if (VEC) {
+      float4 f = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+      if (e0 < V) f = __ldcs(reinterpret_cast<const float4*>(row + e0));
+      v[4 * i + 0] = f.x;
+      v[4 * i + 1] = f.y;
+      v[4 * i + 2] = f.z;
+      v[4 * i + 3] = f.w;
     } else {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) v[4 * g + i] = (e0 + i < V) ? row[e0 + i] : 0.0f;
+      for (int j = 0; j < 4; ++j) v[4 * i + j] = (e0 + j < V) ? __ldcs(row + e0 + j) : -INFINITY;
     }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) idx[4 * g + i] = (e0 + i < V) ? (int)(e0 + i) : -1;
   }
 }
 
-// -------------------------------------------------------------- kernel A
-
-// grid (rows, nchunks).  Rows [0, B*(k+1)) are target rows (b, j); with
-// draft logits present, rows [B*(k+1), B*(2k+1)) are draft rows (b, j).
-// For the sampler (k_draft_tokens == nullptr) every row is a plain row.
-template <bool STOCH, bool VEC>
-__global__ void __launch_bounds__(kThreads)
-accept_row_stats_kernel(const float* __restrict__ target, const float* __restrict__ draft,
-                        const int32_t* __restrict__ draft_tokens, int B, int k, int64_t V,
-                        int nchunks, float inv_t, ChunkStat* __restrict__ stats,
-                        float* __restrict__ ex, uint32_t* status) {
-  __shared__ float sh_m[kWarps];
-  __shared__ int sh_arg[kWarps];
-  __shared__ unsigned long long sh_E[kWarps];
-  const int64_t row = blockIdx.x;
-  const int c = blockIdx.y;
-  const int64_t tgt_rows = (int64_t)B * (k + 1);
-  const float* rowp;
-  int x = -1;
-  if (row < tgt_rows) {
-    rowp = target + row * V;
-    if (draft_tokens) {
-      const int64_t b = row / (k + 1);
-      const int j = (int)(row % (k + 1));
-      if (j < k) x = draft_tokens[b * k + j];
-    }
-  } else {
-    const int64_t r2 = row - tgt_rows;
-    rowp = draft + r2 * V;
-    x = draft_tokens[(r2 / k) * k + (r2 % k)];
-  }
-
-  float v[8];
-  int idx[8];
-  load_chunk<VEC>(rowp, V, c, v, idx);
-  float best = -INFINITY;
-  int best_i = 0x7fffffff;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    if (STOCH) v[i] = KY_FMUL(v[i], inv_t);
-    if (idx[i] >= 0 && v[i] > best) {
-      best = v[i];
-      best_i = idx[i];
-    }
-  }
-  kyro::dev::warp_argmax(best, best_i);
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (lane == 0) {
-    sh_m[warp] = best;
-    sh_arg[warp] = best_i;
-  }
-  __syncthreads();
-  float m = sh_m[0];
-  int arg = sh_arg[0];
-#pragma unroll
-  for (int w = 1; w < kWarps; ++w) {
-    float ov = sh_m[w];
-    int oi = sh_arg[w];
-    if (ov > m || (ov == m && oi < arg)) {
-      m = ov;
-      arg = oi;
-    }
-  }
-  unsigned long long E = 0;
-  if (STOCH) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      if (idx[i] >= 0) {
-        float e = ky_exp(KY_FSUB(v[i], m));
-        E += ky_fix40(e);
-        if (idx[i] == x) ex[row] = e;
-      }
-    }
-    E = kyro::dev::warp_sum_u64(E);
-    if (lane == 0) sh_E[warp] = E;
-    __syncthreads();
-    E = 0;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) E += sh_E[w];
-  }
-  if (threadIdx.x == 0) {
-    ChunkStat s;
-    s.m = m;
-    s.arg = arg;
-    s.E = E;
-    stats[row * nchunks + c] = s;
-  }
-  (void)status;
-}
-
-// -------------------------------------------------------------- kernel B
-
-// Row normaliser (M, S) of one stats row, computed by one warp: chunk
-// masses in parallel, then lane 0 adds them in chunk order.
-__device__ void warp_row_normaliser(const ChunkStat* st, int nchunks, double* scratch, float* M_out,
-                                    double* S_out) {
+// 16 logits of final unit `sub`: float4 i (0..3) covers elements
+// sub*512 + (i*32 + lane)*4 + 0..3.
+template <bool VEC>
+__device__ __forceinline__ void load_sub(const float* __restrict__ row, int64_t V, int sub,
+                                         float (&v)[kSubVec * 4]) {
   const int lane = threadIdx.x & 31;
-  float M = -INFINITY;
-  for (int c = lane; c < nchunks; c += 32) M = fmaxf(M, st[c].m);
-  M = kyro::dev::warp_max(M);
-  for (int c = lane; c < nchunks; c += 32) scratch[c] = ky_chunk_mass(st[c].E, st[c].m, M);
-  __syncwarp();
-  if (lane == 0) {
-    double S = 0.0;
-    for (int c = 0; c < nchunks; ++c) S = KY_DADD(S, scratch[c]);
-    *M_out = M;
-    *S_out = S;
+  const int64_t base = (int64_t)sub * kSub;
+#pragma unroll
+  for (int i = 0; i < kSubVec; ++i) {
+    const int64_t e0 = base + (i * 32 + lane) * 4;
+    if (VEC) {
+      float4 f = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+      if (e0 < V) f = __ldcg(reinterpret_cast<const float4*>(row + e0));
+      v[4 * i + 0] = f.x;
+      v[4 * i + 1] = f.y;
+      v[4 * i + 2] = f.z;
+      v[4 * i + 3] = f.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[4 * i + j] = (e0 + j < V) ? __ldcg(row + e0 + j) : -INFINITY;
+    }
   }
-  __syncwarp();
 }
 
-// one CTA per sequence
-template <bool STOCH>
-__global__ void __launch_bounds__(kThreads)
-accept_decide_kernel(const int32_t* __restrict__ draft_tokens, int B, int k, int64_t V,
-                     int nchunks, int greedy_ref, uint64_t seed, uint32_t step,
-                     int64_t seq_offset, const ChunkStat* __restrict__ stats,
-                     const float* __restrict__ ex, FinalRow* __restrict__ final_rows,
-                     uint32_t* __restrict__ ticket, int32_t* __restrict__ out_accept_len,
-                     int32_t* __restrict__ out_tokens, int32_t* __restrict__ out_num_tokens,
-                     float* __restrict__ out_probs, uint32_t* status) {
-  __shared__ float sh_M[kMaxRows];
-  __shared__ double sh_S[kMaxRows];
-  __shared__ int sh_arg[kMaxRows];
-  __shared__ int sh_acc[kMaxDraft];
-  __shared__ double scratch_all[kWarps][kMaxChunks];
-  const int b = blockIdx.x;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int nrows = STOCH ? 2 * k + 1 : k + 1;  // target rows, then draft rows
-  double* scratch = scratch_all[warp];
-  const int64_t tgt_rows = (int64_t)B * (k + 1);
-  auto stat_row = [&](int r) -> int64_t {
-    return r <= k ? (int64_t)b * (k + 1) + r : tgt_rows + (int64_t)b * k + (r - (k + 1));
-  };
+// Map queue position u to (kind, sequence, index within the sequence).
+// Slot s holds the stats units of sequence s (s < B), then the final units
+// of sequence s - kDelta (s >= kDelta).  off(s) = ua*min(s,B) + uc*max(0,s-kDelta).
+__device__ __forceinline__ long long slot_off(const Args& a, int s) {
+  return (long long)a.ua * min(s, a.B) + (long long)a.uc * max(0, s - kDelta);
+}
 
-  for (int r = warp; r < nrows; r += kWarps) {
-    const ChunkStat* st = stats + stat_row(r) * nchunks;
-    if (STOCH) {
-      warp_row_normaliser(st, nchunks, scratch, &sh_M[r], &sh_S[r]);
+__device__ __forceinline__ void unit_of(const Args& a, long long u, bool& is_stats, int& seq,
+                                        int& local) {
+  int lo = 0, hi = a.B + kDelta - 1;  // first slot s with off(s+1) > u
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (slot_off(a, mid + 1) > u)
+      hi = mid;
+    else
+      lo = mid + 1;
+  }
+  const long long rem = u - slot_off(a, lo);
+  if (lo < a.B && rem < a.ua) {
+    is_stats = true;
+    seq = lo;
+    local = (int)rem;
+  } else {
+    is_stats = false;
+    seq = lo - kDelta;
+    local = (int)(rem - (lo < a.B ? a.ua : 0));
+  }
+}
+
+__device__ __forceinline__ const float* stats_row_ptr(const Args& a, int b, int r) {
+  if (r <= a.k) return a.plog + ((int64_t)b * (a.k + 1) + r) * a.V;
+  return a.qlog + ((int64_t)b * a.k + (r - a.k - 1)) * a.V;
+}
+
+__device__ __forceinline__ int draft_token_of_row(const Args& a, int b, int r) {
+  if (a.sample) return -1;
+  if (r < a.k) return a.draft_tokens[(int64_t)b * a.k + r];
+  if (r > a.k) return a.draft_tokens[(int64_t)b * a.k + (r - a.k - 1)];
+  return -1;
+}
+
+// ------------------------------------------------------------ decide step
+
+// Runs in one warp once every stats unit of sequence b is done.
+__device__ void decide(const Args& a, int b, float* sM, double* sS, int* sArg) {
+  const int lane = threadIdx.x & 31;
+  const int R = a.R;
+  for (int r = 0; r < R; ++r) {
+    const ChunkStat* st = a.stats + ((int64_t)b * R + r) * a.nchunks;
+    if (a.stoch) {
+      float M = -INFINITY;
+      for (int c = lane; c < a.nchunks; c += 32) M = fmaxf(M, __ldcg(&st[c].m));
+      M = kyro::dev::warp_max(M);
+      double t = 0.0;
+      for (int c = lane; c < a.nchunks; c += 32)
+        t = KY_DADD(t, ky_chunk_mass(__ldcg(&st[c].E), __ldcg(&st[c].m), M));
+      const double S = warp_butterfly(t);
+      if (lane == 0) {
+        sM[r] = M;
+        sS[r] = S;
+      }
     } else {
       float best = -INFINITY;
       int bi = 0x7fffffff;
-      for (int c = lane; c < nchunks; c += 32) {
-        ChunkStat s = st[c];
-        if (s.m > best || (s.m == best && s.arg < bi)) {
-          best = s.m;
-          bi = s.arg;
+      for (int c = lane; c < a.nchunks; c += 32) {
+        const float m = __ldcg(&st[c].m);
+        const int ai = __ldcg(&st[c].arg);
+        if (m > best || (m == best && ai < bi)) {
+          best = m;
+          bi = ai;
         }
       }
       kyro::dev::warp_argmax(best, bi);
-      if (lane == 0) sh_arg[r] = bi == 0x7fffffff ? 0 : bi;
+      if (lane == 0) sArg[r] = bi == 0x7fffffff ? 0 : bi;
     }
   }
-  __syncthreads();
+  __syncwarp();
 
-  const uint32_t seq = (uint32_t)(seq_offset + b);
-  const int32_t* x = draft_tokens + (int64_t)b * k;
-  for (int j = threadIdx.x; j < k; j += kThreads) {
-    const int xj = x[j];
-    const bool ok = xj >= 0 && xj < V;
-    if (!ok) kyro::dev::flag(status, KYRO_DEV_BAD_TOKEN);
-    if (STOCH) {
-      float p = 0.0f, q = 0.0f;
-      if (ok) {
-        const int cx = xj / kChunk;
-        const int64_t pr = stat_row(j), qr = stat_row(k + 1 + j);
-        p = KY_FMUL(ex[pr], ky_chunk_scale(stats[pr * nchunks + cx].m, sh_M[j], sh_S[j]));
-        q = KY_FMUL(ex[qr], ky_chunk_scale(stats[qr * nchunks + cx].m, sh_M[k + 1 + j],
-                                           sh_S[k + 1 + j]));
-      }
-      if (out_probs) {
-        out_probs[((int64_t)b * k + j) * 2 + 0] = p;
-        out_probs[((int64_t)b * k + j) * 2 + 1] = q;
-      }
-      const uint32_t odd = ky_uniform_odd(seed, seq, (uint32_t)j, KY_STREAM_ACCEPT, step);
-      sh_acc[j] = ok && ky_accept(odd, p, q);
-    } else {
-      sh_acc[j] = ok && (sh_arg[j] == xj);
-    }
-  }
-  __syncthreads();
-
-  if (threadIdx.x == 0) {
-    int a = k;
-    for (int j = 0; j < k; ++j)
-      if (!sh_acc[j]) {
-        a = j;
-        break;
-      }
-    int32_t* toks = out_tokens + (int64_t)b * (k + 1);
-    for (int j = 0; j <= k; ++j) toks[j] = j < a ? x[j] : -1;
-    out_accept_len[b] = a;
-    FinalRow fr;
-    fr.p_row = (int64_t)b * (k + 1) + a;
-    fr.p_stat = stat_row(a);
-    fr.out_index = b * (k + 1) + a;
-    fr.odd = ky_uniform_odd(seed, seq, (uint32_t)a, KY_STREAM_RESAMPLE, step);
-    fr._pad = 0;
-    if (STOCH) {
-      fr.skip = 0;
-      fr.Mp = sh_M[a];
-      fr.Sp = sh_S[a];
-      if (a < k) {
-        fr.q_row = (int64_t)b * k + a;
-        fr.q_stat = stat_row(k + 1 + a);
-        fr.Mq = sh_M[k + 1 + a];
-        fr.Sq = sh_S[k + 1 + a];
-      } else {
-        fr.q_row = -1;
-        fr.q_stat = -1;
-        fr.Mq = 0.0f;
-        fr.Sq = 1.0;
-      }
-      out_num_tokens[b] = a + 1;
-    } else {
-      fr.skip = 1;
-      if (a == k && greedy_ref && k > 0) {
-        out_num_tokens[b] = k;
-      } else {
-        toks[a] = sh_arg[a];
-        out_num_tokens[b] = a + 1;
-      }
-    }
-    final_rows[b] = fr;
-    ticket[b] = 0;
-  }
-}
-
-// Per-row descriptor for the draft sampler: one warp per row.
-__global__ void __launch_bounds__(kThreads)
-sample_decide_kernel(int64_t nrows, int num_pos, int nchunks, int greedy, uint64_t seed,
-                     uint32_t step, int64_t seq_offset, const ChunkStat* __restrict__ stats,
-                     FinalRow* __restrict__ final_rows, uint32_t* __restrict__ ticket,
-                     int32_t* __restrict__ out_tokens, float* __restrict__ out_probs) {
-  __shared__ double scratch_all[kWarps][kMaxChunks];
-  __shared__ float shM[kWarps];
-  __shared__ double shS[kWarps];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t r = (int64_t)blockIdx.x * kWarps + warp;
-  if (r >= nrows) return;
-  const ChunkStat* st = stats + r * nchunks;
+  const int k = a.k;
   FinalRow fr;
-  fr.p_row = r;
-  fr.p_stat = r;
-  fr.q_row = -1;
-  fr.q_stat = -1;
-  fr.Mq = 0.0f;
-  fr.Sq = 1.0;
-  fr.out_index = (int32_t)r;
   fr._pad = 0;
-  const int64_t b = r / num_pos;
-  const int j = (int)(r % num_pos);
-  fr.odd = ky_uniform_odd(seed, (uint32_t)(seq_offset + b), (uint32_t)j, KY_STREAM_DRAFT, step);
-  if (greedy) {
-    float best = -INFINITY;
-    int bi = 0x7fffffff;
-    for (int c = lane; c < nchunks; c += 32) {
-      ChunkStat s = st[c];
-      if (s.m > best || (s.m == best && s.arg < bi)) {
-        best = s.m;
-        bi = s.arg;
-      }
-    }
-    kyro::dev::warp_argmax(best, bi);
+  if (a.sample) {
+    // one row per "sequence": the draft sampler
+    const int64_t seq = a.seq_offset + b / a.pos_div;
+    const int pos = b % a.pos_div;
     if (lane == 0) {
-      out_tokens[r] = bi == 0x7fffffff ? 0 : bi;
-      if (out_probs) out_probs[r] = 1.0f;
-      fr.skip = 1;
-      fr.Mp = 0.0f;
-      fr.Sp = 1.0;
-      final_rows[r] = fr;
-      ticket[r] = 0;
+      fr.p_row = b;
+      fr.p_stat = b;
+      fr.q_row = -1;
+      fr.q_stat = -1;
+      fr.Mq = 0.0f;
+      fr.Sq = 1.0;
+      fr.out_index = b;
+      fr.odd = ky_uniform_odd(a.seed, (uint32_t)seq, (uint32_t)pos, KY_STREAM_DRAFT, a.step);
+      if (a.stoch) {
+        fr.skip = 0;
+        fr.Mp = sM[0];
+        fr.Sp = sS[0];
+      } else {
+        fr.skip = 1;
+        fr.Mp = 0.0f;
+        fr.Sp = 1.0;
+        a.out_tokens[b] = sArg[0];
+        if (a.out_probs) a.out_probs[b] = 1.0f;
+      }
+      a.final_rows[b] = fr;
     }
-    return;
-  }
-  warp_row_normaliser(st, nchunks, scratch_all[warp], &shM[warp], &shS[warp]);
-  if (lane == 0) {
-    fr.skip = 0;
-    fr.Mp = shM[warp];
-    fr.Sp = shS[warp];
-    final_rows[r] = fr;
-    ticket[r] = 0;
-  }
-}
-
-// -------------------------------------------------------------- kernel C
-
-template <bool VEC>
-__device__ __forceinline__ void final_weights(const float* prow, const float* qrow, int64_t V,
-                                              int c, float inv_t, float mp, float gp, float mq,
-                                              float gq, bool residual, unsigned long long (&w)[8],
-                                              int (&idx)[8]) {
-  float zp[8], zq[8];
-  load_chunk<VEC>(prow, V, c, zp, idx);
-  if (residual) {
-    int idx2[8];
-    load_chunk<VEC>(qrow, V, c, zq, idx2);
-  }
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    float p = KY_FMUL(ky_exp(KY_FSUB(KY_FMUL(zp[i], inv_t), mp)), gp);
-    unsigned long long wi;
-    if (residual) {
-      float q = KY_FMUL(ky_exp(KY_FSUB(KY_FMUL(zq[i], inv_t), mq)), gq);
-      wi = ky_residual_w(p, q);
-    } else {
-      wi = ky_fix62(p);
-    }
-    w[i] = idx[i] >= 0 ? wi : 0ull;
-  }
-}
-
-// grid (nsplit, nfinal): CTA x covers chunks [x*per, (x+1)*per) of final row y.
-template <bool VEC>
-__global__ void __launch_bounds__(kThreads)
-accept_final_row_kernel(const float* __restrict__ plogits, const float* __restrict__ qlogits,
-                        int64_t V, int nchunks, int chunks_per_cta, float inv_t,
-                        const ChunkStat* __restrict__ stats, const FinalRow* __restrict__ final_rows,
-                        unsigned long long* __restrict__ Wbuf, uint32_t* __restrict__ ticket,
-                        int32_t* __restrict__ out_tokens, float* __restrict__ out_probs) {
-  __shared__ unsigned long long sh_red[kWarps];
-  __shared__ unsigned long long sh_W[kMaxChunks];
-  __shared__ int sh_last, sh_chunk, sh_token;
-  __shared__ unsigned long long sh_T;
-  __shared__ int sh_residual;
-  const int64_t fi = blockIdx.y;
-  const FinalRow fr = final_rows[fi];
-  if (fr.skip) return;
-  const float* prow = plogits + fr.p_row * V;
-  const float* qrow = fr.q_row >= 0 ? qlogits + fr.q_row * V : nullptr;
-  const ChunkStat* sp = stats + fr.p_stat * nchunks;
-  const ChunkStat* sq = fr.q_stat >= 0 ? stats + fr.q_stat * nchunks : nullptr;
-  unsigned long long* W = Wbuf + fi * nchunks;
-
-  const int c0 = blockIdx.x * chunks_per_cta;
-  const int c1 = min(nchunks, c0 + chunks_per_cta);
-  const bool residual = qrow != nullptr;
-  for (int c = c0; c < c1; ++c) {
-    const float mp = sp[c].m, gp = ky_chunk_scale(mp, fr.Mp, fr.Sp);
-    float mq = 0.0f, gq = 0.0f;
-    if (residual) {
-      mq = sq[c].m;
-      gq = ky_chunk_scale(mq, fr.Mq, fr.Sq);
-    }
-    unsigned long long w[8];
-    int idx[8];
-    final_weights<VEC>(prow, qrow, V, c, inv_t, mp, gp, mq, gq, residual, w, idx);
-    unsigned long long s = 0;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) s += w[i];
-    s = block_sum_u64(s, sh_red);
-    if (threadIdx.x == 0) W[c] = s;
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    const uint32_t t = atomicAdd(&ticket[fi], 1u);
-    sh_last = (t == gridDim.x - 1);
-  }
-  __syncthreads();
-  if (!sh_last) return;
-  __threadfence();
-
-  // ---- last CTA of this row: locate the chunk, then the index
-  for (int c = threadIdx.x; c < nchunks; c += kThreads) sh_W[c] = __ldcg(&W[c]);
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    unsigned long long tot = 0;
-    for (int c = 0; c < nchunks; ++c) tot += sh_W[c];
-    sh_residual = residual && tot != 0;
-  }
-  __syncthreads();
-  if (residual && !sh_residual) {
-    // residual without mass: fall back to sampling from p
-    for (int c = 0; c < nchunks; ++c) {
-      const float mp = sp[c].m, gp = ky_chunk_scale(mp, fr.Mp, fr.Sp);
-      unsigned long long w[8];
-      int idx[8];
-      final_weights<VEC>(prow, nullptr, V, c, inv_t, mp, gp, 0.0f, 0.0f, false, w, idx);
-      unsigned long long s = 0;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) s += w[i];
-      s = block_sum_u64(s, sh_red);
-      if (threadIdx.x == 0) sh_W[c] = s;
-    }
-    __syncthreads();
-  }
-  if (threadIdx.x == 0) {
-    unsigned long long tot = 0;
-    for (int c = 0; c < nchunks; ++c) tot += sh_W[c];
-    int chunk = -1;
-    unsigned long long T = 0;
-    if (tot != 0) {
-      T = ky_cdf_threshold(fr.odd, tot);
-      unsigned long long cum = 0;
-      for (int c = 0; c < nchunks; ++c) {
-        if (cum + sh_W[c] >= T) {
-          chunk = c;
-          T -= cum;
-          break;
+  } else {
+    const uint32_t seq = (uint32_t)(a.seq_offset + b);
+    const int32_t* x = a.draft_tokens + (int64_t)b * k;
+    int first_reject = k;
+    for (int j0 = 0; j0 < k; j0 += 32) {
+      const int j = j0 + lane;
+      bool acc = true;
+      if (j < k) {
+        const int xj = x[j];
+        const bool ok = xj >= 0 && xj < a.V;
+        if (!ok) kyro::dev::flag(a.status, KYRO_DEV_BAD_TOKEN);
+        if (a.stoch) {
+          float p = 0.0f, q = 0.0f;
+          if (ok) {
+            const int cx = xj / kChunk;
+            const int64_t pr = (int64_t)b * a.R + j, qr = (int64_t)b * a.R + k + 1 + j;
+            p = KY_FMUL(__ldcg(&a.ex[pr]),
+                        ky_chunk_scale(__ldcg(&a.stats[pr * a.nchunks + cx].m), sM[j], sS[j]));
+            q = KY_FMUL(__ldcg(&a.ex[qr]),
+                        ky_chunk_scale(__ldcg(&a.stats[qr * a.nchunks + cx].m), sM[k + 1 + j],
+                                       sS[k + 1 + j]));
+          }
+          if (a.out_probs) {
+            a.out_probs[((int64_t)b * k + j) * 2 + 0] = p;
+            a.out_probs[((int64_t)b * k + j) * 2 + 1] = q;
+          }
+          const uint32_t odd = ky_uniform_odd(a.seed, seq, (uint32_t)j, KY_STREAM_ACCEPT, a.step);
+          acc = ok && ky_accept(odd, p, q);
+        } else {
+          acc = ok && sArg[j] == xj;
         }
-        cum += sh_W[c];
+      }
+      const unsigned rej = __ballot_sync(0xffffffffu, !acc);
+      if (first_reject == k && rej) first_reject = j0 + __ffs(rej) - 1;
+    }
+    const int aa = first_reject;
+    if (lane == 0) {
+      int32_t* toks = a.out_tokens + (int64_t)b * (k + 1);
+      for (int j = 0; j <= k; ++j) toks[j] = j < aa ? x[j] : -1;
+      a.out_accept_len[b] = aa;
+      fr.p_row = (int64_t)b * (k + 1) + aa;
+      fr.p_stat = (int64_t)b * a.R + aa;
+      fr.out_index = b * (k + 1) + aa;
+      fr.odd = ky_uniform_odd(a.seed, seq, (uint32_t)aa, KY_STREAM_RESAMPLE, a.step);
+      if (a.stoch) {
+        fr.skip = 0;
+        fr.Mp = sM[aa];
+        fr.Sp = sS[aa];
+        if (aa < k) {
+          fr.q_row = (int64_t)b * k + aa;
+          fr.q_stat = (int64_t)b * a.R + k + 1 + aa;
+          fr.Mq = sM[k + 1 + aa];
+          fr.Sq = sS[k + 1 + aa];
+        } else {
+          fr.q_row = -1;
+          fr.q_stat = -1;
+          fr.Mq = 0.0f;
+          fr.Sq = 1.0;
+        }
+        a.out_num_tokens[b] = aa + 1;
+      } else {
+        fr.skip = 1;
+        fr.q_row = fr.q_stat = -1;
+        fr.Mp = fr.Mq = 0.0f;
+        fr.Sp = fr.Sq = 1.0;
+        if (aa == k && a.greedy_ref && k > 0) {
+          a.out_num_tokens[b] = k;
+        } else {
+          toks[aa] = sArg[aa];
+          a.out_num_tokens[b] = aa + 1;
+        }
+      }
+      a.final_rows[b] = fr;
+    }
+  }
+  if (lane == 0) {
+    __threadfence();
+    atomicExch(&a.ready[b], 1u);
+  }
+  __syncwarp();
+}
+
+// ------------------------------------------------------------ units
+
+template <bool VEC, bool STOCH>
+__device__ void stats_unit(const Args& a, int b, int local, float (&v)[kPerLane], float* sM,
+                           double* sS, int* sArg) {
+  const int lane = threadIdx.x & 31;
+  const int r = local / a.nchunks, c = local % a.nchunks;
+  const int64_t srow = (int64_t)b * a.R + r;
+  float m = -INFINITY;
+  int arg = 0x7fffffff;
+  if (STOCH) {
+#pragma unroll
+    for (int i = 0; i < kPerLane; ++i) {
+      v[i] = KY_FMUL(v[i], a.inv_t);
+      m = fmaxf(m, v[i]);
+    }
+    m = kyro::dev::warp_max(m);
+    unsigned long long E = 0;
+#pragma unroll
+    for (int i = 0; i < kPerLane; ++i) E += ky_fix40(ky_exp(KY_FSUB(v[i], m)));
+    E = warp_sum(E);
+    if (lane == 0) {
+      ChunkStat s;
+      s.m = m;
+      s.arg = 0;
+      s.E = E;
+      a.stats[srow * a.nchunks + c] = s;
+      const int x = draft_token_of_row(a, b, r);
+      if (x >= (int64_t)c * kChunk && x < (int64_t)(c + 1) * kChunk && x < a.V) {
+        const float* rowp = stats_row_ptr(a, b, r);
+        a.ex[srow] = ky_exp(KY_FSUB(KY_FMUL(__ldg(rowp + x), a.inv_t), m));
       }
     }
-    sh_chunk = chunk;
-    sh_T = T;
-    sh_token = (int)V - 1;
-  }
-  __syncthreads();
-  const int chunk = sh_chunk;
-  if (chunk >= 0) {
-    const bool res = sh_residual;
-    const float mp = sp[chunk].m, gp = ky_chunk_scale(mp, fr.Mp, fr.Sp);
-    float mq = 0.0f, gq = 0.0f;
-    if (res) {
-      mq = sq[chunk].m;
-      gq = ky_chunk_scale(mq, fr.Mq, fr.Sq);
+  } else {
+    const int64_t base = (int64_t)c * kChunk;
+#pragma unroll
+    for (int i = 0; i < kVecPerLane; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (v[4 * i + j] > m) {
+          m = v[4 * i + j];
+          arg = (int)(base + (i * 32 + lane) * 4 + j);
+        }
+    kyro::dev::warp_argmax(m, arg);
+    if (lane == 0) {
+      ChunkStat s;
+      s.m = m;
+      s.arg = arg;
+      s.E = 0;
+      a.stats[srow * a.nchunks + c] = s;
     }
-    unsigned long long w[8];
-    int idx[8];
-    final_weights<VEC>(prow, qrow, V, chunk, inv_t, mp, gp, mq, gq, res, w, idx);
-    const unsigned long long T = sh_T;
-    // element order within the chunk: group 0 of all threads, then group 1
+  }
+  // the warp that completes the sequence's last stats unit decides it
+  uint32_t last = 0;
+  if (lane == 0) {
+    __threadfence();
+    last = atomicAdd(&a.cnt_a[b], 1u) == (uint32_t)(a.ua - 1);
+  }
+  last = __shfl_sync(0xffffffffu, last, 0);
+  if (last) {
+    __threadfence();
+    decide(a, b, sM, sS, sArg);
+  }
+}
+
+// fix62 weights of 16 logits of one final unit
+template <bool VEC>
+__device__ __forceinline__ void final_weights(const Args& a, const FinalRow& fr, bool residual,
+                                              int sub, unsigned long long (&w)[kSubVec * 4]) {
+  const float* prow = a.plog + fr.p_row * a.V;
+  const int c = sub / kSubsPerChunk;
+  const ChunkStat* sp = a.stats + fr.p_stat * a.nchunks;
+  const float mp = __ldcg(&sp[c].m);
+  const float gp = ky_chunk_scale(mp, fr.Mp, fr.Sp);
+  float zp[kSubVec * 4];
+  load_sub<VEC>(prow, a.V, sub, zp);
+  if (residual) {
+    const float* qrow = a.qlog + fr.q_row * a.V;
+    const ChunkStat* sq = a.stats + fr.q_stat * a.nchunks;
+    const float mq = __ldcg(&sq[c].m);
+    const float gq = ky_chunk_scale(mq, fr.Mq, fr.Sq);
+    float zq[kSubVec * 4];
+    load_sub<VEC>(qrow, a.V, sub, zq);
+#pragma unroll
+    for (int i = 0; i < kSubVec * 4; ++i) {
+      const float p = KY_FMUL(ky_exp(KY_FSUB(KY_FMUL(zp[i], a.inv_t), mp)), gp);
+      const float q = KY_FMUL(ky_exp(KY_FSUB(KY_FMUL(zq[i], a.inv_t), mq)), gq);
+      w[i] = ky_residual_w(p, q);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < kSubVec * 4; ++i)
+      w[i] = ky_fix62(KY_FMUL(ky_exp(KY_FSUB(KY_FMUL(zp[i], a.inv_t), mp)), gp));
+  }
+}
+
+// Locate the cut point of a final row once all its unit sums are in W.
+template <bool VEC>
+__device__ void final_search(const Args& a, int b, const FinalRow& fr) {
+  const int lane = threadIdx.x & 31;
+  unsigned long long* W = a.W + (int64_t)b * a.nsub;
+  bool residual = fr.q_row >= 0;
+  unsigned long long tot = 0;
+  for (int s = lane; s < a.nsub; s += 32) tot += __ldcg(&W[s]);
+  tot = warp_sum(tot);
+  if (residual && tot == 0) {
+    // the residual has no mass: sample from p instead
+    residual = false;
+    for (int s = 0; s < a.nsub; ++s) {
+      unsigned long long w[kSubVec * 4];
+      final_weights<VEC>(a, fr, false, s, w);
+      unsigned long long t = 0;
+#pragma unroll
+      for (int i = 0; i < kSubVec * 4; ++i) t += w[i];
+      t = warp_sum(t);
+      if (lane == 0) W[s] = t;
+    }
+    __syncwarp();
+    __threadfence_block();
+    tot = 0;
+    for (int s = lane; s < a.nsub; s += 32) tot += __ldcg(&W[s]);
+    tot = warp_sum(tot);
+  }
+  int token = (int)a.V - 1;
+  if (tot != 0) {
+    unsigned long long T = ky_cdf_threshold(fr.odd, tot);
+    // find the unit whose inclusive prefix first reaches T
+    int sub = -1;
     unsigned long long base = 0;
+    for (int s0 = 0; s0 < a.nsub && sub < 0; s0 += 32) {
+      const unsigned long long ws = (s0 + lane < a.nsub) ? __ldcg(&W[s0 + lane]) : 0ull;
+      const unsigned long long inc = base + warp_inclusive(ws);
+      const unsigned hit = __ballot_sync(0xffffffffu, inc >= T && s0 + lane < a.nsub);
+      if (hit) {
+        const int l = __ffs(hit) - 1;
+        sub = s0 + l;
+        const unsigned long long before = __shfl_sync(0xffffffffu, inc - ws, l);
+        T -= before;
+      } else {
+        base = __shfl_sync(0xffffffffu, inc, 31);
+      }
+    }
+    if (sub >= 0) {
+      unsigned long long w[kSubVec * 4];
+      final_weights<VEC>(a, fr, residual, sub, w);
+      unsigned long long cbase = 0;
+      int found = -1;
 #pragma unroll
-    for (int g = 0; g < 2; ++g) {
-      unsigned long long s = w[4 * g] + w[4 * g + 1] + w[4 * g + 2] + w[4 * g + 3];
-      unsigned long long gtot;
-      unsigned long long ex = block_exclusive_scan_u64(s, sh_red, &gtot);
-      unsigned long long C = base + ex;
-      if (C < T && C + s >= T) {
+      for (int i = 0; i < kSubVec; ++i) {
+        const unsigned long long s4 = w[4 * i] + w[4 * i + 1] + w[4 * i + 2] + w[4 * i + 3];
+        const unsigned long long inc = warp_inclusive(s4);
+        unsigned long long C = cbase + inc - s4;
+        int mine = -1;
+        if (C < T && C + s4 >= T) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          C += w[4 * g + i];
-          if (C >= T) {
-            sh_token = idx[4 * g + i];
-            break;
+          for (int j = 0; j < 4; ++j) {
+            C += w[4 * i + j];
+            if (mine < 0 && C >= T) mine = j;
           }
         }
+        const unsigned hit = __ballot_sync(0xffffffffu, mine >= 0);
+        if (found < 0 && hit) {
+          const int l = __ffs(hit) - 1;
+          const int jj = __shfl_sync(0xffffffffu, mine, l);
+          found = sub * kSub + (i * 32 + l) * 4 + jj;
+        }
+        cbase += __shfl_sync(0xffffffffu, inc, 31);
       }
-      base += gtot;
+      if (found >= 0) token = found;
     }
   }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const int tok = sh_token;
-    out_tokens[fr.out_index] = tok;
-    if (out_probs) {
-      // p(token) under the row's normaliser (draft sampler output)
-      const int c = tok / kChunk;
-      const float mp = sp[c].m;
-      out_probs[fr.out_index] =
-          KY_FMUL(ky_exp(KY_FSUB(KY_FMUL(prow[tok], inv_t), mp)), ky_chunk_scale(mp, fr.Mp, fr.Sp));
+  if (lane == 0) {
+    a.out_tokens[fr.out_index] = token;
+    if (a.sample && a.out_probs) {
+      const int c = token / kChunk;
+      const float mp = __ldcg(&a.stats[fr.p_stat * a.nchunks + c].m);
+      a.out_probs[fr.out_index] =
+          KY_FMUL(ky_exp(KY_FSUB(KY_FMUL(__ldg(a.plog + fr.p_row * a.V + token), a.inv_t), mp)),
+                  ky_chunk_scale(mp, fr.Mp, fr.Sp));
     }
-    ticket[fi] = 0;
   }
 }
 
-size_t accept_ws_bytes(int64_t B, int64_t k, int64_t V, bool stoch) {
-  const int64_t nchunks = (V + kChunk - 1) / kChunk;
-  const int64_t stat_rows = stoch ? B * (2 * k + 1) : B * (k + 1);
-  return carve(nullptr, stat_rows, nchunks, B).bytes;
+template <bool VEC>
+__device__ void final_unit(const Args& a, int b, int sub) {
+  const int lane = threadIdx.x & 31;
+  // wait (bounded) until the decide step of sequence b has published
+  uint32_t ok = 1;
+  if (lane == 0) {
+    volatile uint32_t* flag = a.ready + b;
+    if (*flag == 0) {
+      const long long t0 = clock64();
+      while (*flag == 0) {
+        __nanosleep(200);
+        if (clock64() - t0 > kyro::dev::kWaitBudgetCycles) {
+          ok = 0;
+          break;
+        }
+      }
+    }
+    __threadfence();
+  }
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  if (!ok) {
+    if (lane == 0) kyro::dev::flag(a.status, KYRO_DEV_WAIT_TIMEOUT);
+    return;
+  }
+  FinalRow fr;
+  {
+    const FinalRow* src = a.final_rows + b;
+    fr.p_row = __ldcg(&src->p_row);
+    fr.q_row = __ldcg(&src->q_row);
+    fr.p_stat = __ldcg(&src->p_stat);
+    fr.q_stat = __ldcg(&src->q_stat);
+    fr.Mp = __ldcg(&src->Mp);
+    fr.Mq = __ldcg(&src->Mq);
+    fr.Sp = __ldcg(&src->Sp);
+    fr.Sq = __ldcg(&src->Sq);
+    fr.odd = __ldcg(&src->odd);
+    fr.out_index = __ldcg(&src->out_index);
+    fr.skip = __ldcg(&src->skip);
+  }
+  if (fr.skip) return;
+  unsigned long long w[kSubVec * 4];
+  final_weights<VEC>(a, fr, fr.q_row >= 0, sub, w);
+  unsigned long long t = 0;
+#pragma unroll
+  for (int i = 0; i < kSubVec * 4; ++i) t += w[i];
+  t = warp_sum(t);
+  uint32_t last = 0;
+  if (lane == 0) {
+    a.W[(int64_t)b * a.nsub + sub] = t;
+    __threadfence();
+    last = atomicAdd(&a.cnt_c[b], 1u) == (uint32_t)(a.uc - 1);
+  }
+  last = __shfl_sync(0xffffffffu, last, 0);
+  if (last) {
+    __threadfence();
+    final_search<VEC>(a, b, fr);
+  }
 }
+
+// ------------------------------------------------------------ the kernel
+
+struct UnitCursor {
+  long long next, end;
+};
+
+__device__ __forceinline__ long long take_unit(const Args& a, UnitCursor& cur) {
+  const int lane = threadIdx.x & 31;
+  if (cur.next >= cur.end) {
+    long long g = 0;
+    if (lane == 0) g = (long long)atomicAdd(a.queue, (unsigned long long)kBatch);
+    g = __shfl_sync(0xffffffffu, g, 0);
+    cur.next = g;
+    cur.end = g + kBatch;
+  }
+  return cur.next++;
+}
+
+template <bool VEC>
+__device__ __forceinline__ void prefetch(const Args& a, long long u, float (&buf)[kPerLane]) {
+  if (u >= a.total) return;
+  bool is_stats;
+  int seq, local;
+  unit_of(a, u, is_stats, seq, local);
+  if (!is_stats) return;
+  const int r = local / a.nchunks, c = local % a.nchunks;
+  load_chunk<VEC>(stats_row_ptr(a, seq, r), a.V, c, buf);
+}
+
+template <bool VEC, bool STOCH>
+__device__ __forceinline__ void run_unit(const Args& a, long long u, float (&buf)[kPerLane],
+                                         float* sM, double* sS, int* sArg) {
+  bool is_stats;
+  int seq, local;
+  unit_of(a, u, is_stats, seq, local);
+  if (is_stats)
+    stats_unit<VEC, STOCH>(a, seq, local, buf, sM, sS, sArg);
+  else
+    final_unit<VEC>(a, seq, local);
+}
+
+template <bool VEC, bool STOCH>
+__global__ void __launch_bounds__(kThreads, 2) accept_fused_kernel(Args a) {
+  __shared__ float sM_all[kWarps][kMaxRows];
+  __shared__ double sS_all[kWarps][kMaxRows];
+  __shared__ int sArg_all[kWarps][kMaxRows];
+  const int warp = threadIdx.x >> 5;
+  float* sM = sM_all[warp];
+  double* sS = sS_all[warp];
+  int* sArg = sArg_all[warp];
+  UnitCursor cur{0, 0};
+  float buf0[kPerLane], buf1[kPerLane];
+  long long u0 = take_unit(a, cur);
+  prefetch<VEC>(a, u0, buf0);
+  while (u0 < a.total) {
+    const long long u1 = take_unit(a, cur);
+    prefetch<VEC>(a, u1, buf1);
+    run_unit<VEC, STOCH>(a, u0, buf0, sM, sS, sArg);
+    if (u1 >= a.total) break;
+    u0 = take_unit(a, cur);
+    prefetch<VEC>(a, u0, buf0);
+    run_unit<VEC, STOCH>(a, u1, buf1, sM, sS, sArg);
+  }
+}
+
+// ------------------------------------------------------------ host side
 
 bool use_vec(const void* a, const void* b, int64_t V) {
   return (V % 4 == 0) && ((uintptr_t)a % 16 == 0) && (b == nullptr || (uintptr_t)b % 16 == 0);
+}
+
+template <bool VEC, bool STOCH>
+int resident_ctas(int num_sms) {
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, accept_fused_kernel<VEC, STOCH>,
+                                                    kThreads, 0) != cudaSuccess ||
+      per_sm < 1)
+    per_sm = 1;
+  return num_sms * per_sm;
+}
+
+int launch(kyro_ctx* ctx, Args& a, const Workspace& ws, bool vec) {
+  cudaStream_t st = ctx->stream;
+  // the queue, the per-sequence counters and the ready flags start at zero
+  cudaError_t err = cudaMemsetAsync(ws.queue, 0, ws.counter_bytes, st);
+  if (err != cudaSuccess) return kyro::cuda_error(err, "cudaMemsetAsync(sampler counters)");
+  int resident;
+  if (vec && a.stoch)
+    resident = resident_ctas<true, true>(ctx->num_sms);
+  else if (vec)
+    resident = resident_ctas<true, false>(ctx->num_sms);
+  else if (a.stoch)
+    resident = resident_ctas<false, true>(ctx->num_sms);
+  else
+    resident = resident_ctas<false, false>(ctx->num_sms);
+  const long long useful = (a.total + kWarps * kBatch - 1) / (kWarps * kBatch);
+  const int grid = (int)(useful < resident ? useful : resident);
+  if (vec && a.stoch)
+    accept_fused_kernel<true, true><<<grid, kThreads, 0, st>>>(a);
+  else if (vec)
+    accept_fused_kernel<true, false><<<grid, kThreads, 0, st>>>(a);
+  else if (a.stoch)
+    accept_fused_kernel<false, true><<<grid, kThreads, 0, st>>>(a);
+  else
+    accept_fused_kernel<false, false><<<grid, kThreads, 0, st>>>(a);
+  return kyro::check_launch("accept_fused_kernel");
+}
+
+void fill_workspace_args(Args& a, const Workspace& ws) {
+  a.stats = ws.stats;
+  a.ex = ws.ex;
+  a.final_rows = ws.final_rows;
+  a.W = ws.W;
+  a.cnt_a = ws.cnt_a;
+  a.cnt_c = ws.cnt_c;
+  a.ready = ws.ready;
+  a.queue = ws.queue;
 }
 
 }  // namespace
@@ -623,7 +774,10 @@ extern "C" {
 size_t kyro_spec_accept_workspace_size(const kyro_accept_params* p) {
   if (!p || p->batch < 0 || p->num_draft < 0 || p->vocab <= 0) return 0;
   const bool stoch = p->mode == KYRO_ACCEPT_STOCHASTIC && p->temperature > 0.0f;
-  return accept_ws_bytes(p->batch, p->num_draft, p->vocab, stoch);
+  const int64_t R = stoch ? 2 * (int64_t)p->num_draft + 1 : (int64_t)p->num_draft + 1;
+  const int64_t nchunks = (p->vocab + kChunk - 1) / kChunk;
+  const int64_t nsub = (p->vocab + kSub - 1) / kSub;
+  return carve(nullptr, p->batch, R, nchunks, nsub).bytes;
 }
 
 int kyro_spec_accept(kyro_ctx* ctx, const kyro_accept_params* p, const float* target_logits,
@@ -633,8 +787,8 @@ int kyro_spec_accept(kyro_ctx* ctx, const kyro_accept_params* p, const float* ta
   KY_TRY(kyro::enter(ctx));
   KY_REQUIRE(p, "kyro_spec_accept: params is NULL");
   KY_REQUIRE(p->batch >= 0, "kyro_spec_accept: batch = %d", p->batch);
-  KY_REQUIRE(p->num_draft >= 0 && p->num_draft <= kMaxDraft, "kyro_spec_accept: num_draft = %d (0..64)",
-             p->num_draft);
+  KY_REQUIRE(p->num_draft >= 0 && p->num_draft <= kMaxDraft,
+             "kyro_spec_accept: num_draft = %d (0..%d)", p->num_draft, kMaxDraft);
   KY_REQUIRE(p->vocab > 0 && (int64_t)p->vocab <= (int64_t)kMaxChunks * kChunk,
              "kyro_spec_accept: vocab = %d (1..%d)", p->vocab, kMaxChunks * kChunk);
   KY_REQUIRE(p->mode >= 0 && p->mode <= 2, "kyro_spec_accept: mode = %d", p->mode);
@@ -648,75 +802,53 @@ int kyro_spec_accept(kyro_ctx* ctx, const kyro_accept_params* p, const float* ta
              "kyro_spec_accept: stochastic mode needs draft_logits");
   KY_REQUIRE(out_accept_len && out_tokens && out_num_tokens,
              "kyro_spec_accept: an output pointer is NULL");
-  const size_t need = accept_ws_bytes(B, k, V, stoch);
+  const int R = stoch ? 2 * k + 1 : k + 1;
+  const int nchunks = (int)((V + kChunk - 1) / kChunk);
+  const int nsub = (int)((V + kSub - 1) / kSub);
+  KY_REQUIRE((int64_t)B * R * nchunks < (1ll << 40), "kyro_spec_accept: batch too large");
+  const size_t need = carve(nullptr, B, R, nchunks, nsub).bytes;
   if (workspace_bytes < need || !workspace)
     return kyro::set_error(KYRO_ERR_WORKSPACE, "kyro_spec_accept: workspace %zu < %zu bytes",
                            workspace_bytes, need);
-  KY_REQUIRE((uintptr_t)workspace % 256 == 0, "kyro_spec_accept: workspace must be 256-byte aligned");
-
-  const int nchunks = (int)((V + kChunk - 1) / kChunk);
-  const int64_t stat_rows = stoch ? (int64_t)B * (2 * k + 1) : (int64_t)B * (k + 1);
-  KY_REQUIRE(stat_rows < (1ll << 31), "kyro_spec_accept: too many rows");
-  Workspace ws = carve(workspace, stat_rows, nchunks, B);
-  const float inv_t = stoch ? ky_inv_temperature(p->temperature) : 1.0f;
-  const bool vec = use_vec(target_logits, stoch ? draft_logits : nullptr, V);
-  cudaStream_t st = ctx->stream;
-
-  dim3 gridA((unsigned)stat_rows, (unsigned)nchunks);
-  const int32_t* xt = k > 0 ? draft_tokens : nullptr;
-  if (stoch) {
-    if (vec)
-      accept_row_stats_kernel<true, true><<<gridA, kThreads, 0, st>>>(
-          target_logits, draft_logits, xt, B, k, V, nchunks, inv_t, ws.stats, ws.ex,
-          ctx->d_status);
-    else
-      accept_row_stats_kernel<true, false><<<gridA, kThreads, 0, st>>>(
-          target_logits, draft_logits, xt, B, k, V, nchunks, inv_t, ws.stats, ws.ex,
-          ctx->d_status);
-  } else {
-    if (vec)
-      accept_row_stats_kernel<false, true><<<gridA, kThreads, 0, st>>>(
-          target_logits, nullptr, xt, B, k, V, nchunks, 1.0f, ws.stats, ws.ex, ctx->d_status);
-    else
-      accept_row_stats_kernel<false, false><<<gridA, kThreads, 0, st>>>(
-          target_logits, nullptr, xt, B, k, V, nchunks, 1.0f, ws.stats, ws.ex, ctx->d_status);
-  }
-  KY_TRY(kyro::check_launch("accept_row_stats_kernel"));
-
-  if (stoch)
-    accept_decide_kernel<true><<<B, kThreads, 0, st>>>(
-        draft_tokens, B, k, V, nchunks, 0, p->seed, p->step, p->seq_offset, ws.stats, ws.ex,
-        ws.final_rows, ws.ticket, out_accept_len, out_tokens, out_num_tokens, out_probs,
-        ctx->d_status);
-  else
-    accept_decide_kernel<false><<<B, kThreads, 0, st>>>(
-        draft_tokens, B, k, V, nchunks, p->mode == KYRO_ACCEPT_GREEDY_REF, p->seed, p->step,
-        p->seq_offset, ws.stats, ws.ex, ws.final_rows, ws.ticket, out_accept_len, out_tokens,
-        out_num_tokens, nullptr, ctx->d_status);
-  KY_TRY(kyro::check_launch("accept_decide_kernel"));
-
-  if (stoch) {
-    const int per = 4;
-    KY_REQUIRE(B <= 65535, "kyro_spec_accept: batch %d > 65535", B);
-    dim3 gridC((unsigned)((nchunks + per - 1) / per), (unsigned)B);
-    if (vec)
-      accept_final_row_kernel<true><<<gridC, kThreads, 0, st>>>(
-          target_logits, draft_logits, V, nchunks, per, inv_t, ws.stats, ws.final_rows, ws.W,
-          ws.ticket, out_tokens, nullptr);
-    else
-      accept_final_row_kernel<false><<<gridC, kThreads, 0, st>>>(
-          target_logits, draft_logits, V, nchunks, per, inv_t, ws.stats, ws.final_rows, ws.W,
-          ws.ticket, out_tokens, nullptr);
-    KY_TRY(kyro::check_launch("accept_final_row_kernel"));
-  }
-  return KYRO_OK;
+  KY_REQUIRE((uintptr_t)workspace % 256 == 0,
+             "kyro_spec_accept: workspace must be 256-byte aligned");
+  Workspace ws = carve(workspace, B, R, nchunks, nsub);
+  Args a = {};
+  a.plog = target_logits;
+  a.qlog = stoch ? draft_logits : nullptr;
+  a.draft_tokens = draft_tokens;
+  a.B = B;
+  a.k = k;
+  a.R = R;
+  a.V = V;
+  a.nchunks = nchunks;
+  a.nsub = nsub;
+  a.inv_t = stoch ? ky_inv_temperature(p->temperature) : 1.0f;
+  a.stoch = stoch;
+  a.greedy_ref = p->mode == KYRO_ACCEPT_GREEDY_REF;
+  a.sample = 0;
+  a.pos_div = 1;
+  a.seed = p->seed;
+  a.step = p->step;
+  a.seq_offset = p->seq_offset;
+  a.out_accept_len = out_accept_len;
+  a.out_tokens = out_tokens;
+  a.out_num_tokens = out_num_tokens;
+  a.out_probs = stoch ? out_probs : nullptr;
+  fill_workspace_args(a, ws);
+  a.ua = R * nchunks;
+  a.uc = stoch ? nsub : 0;
+  a.total = (long long)B * (a.ua + a.uc);
+  a.status = ctx->d_status;
+  return launch(ctx, a, ws, use_vec(target_logits, a.qlog, V));
 }
 
 size_t kyro_sample_workspace_size(const kyro_sample_params* p) {
   if (!p || p->batch < 0 || p->num_pos < 0 || p->vocab <= 0) return 0;
   const int64_t rows = (int64_t)p->batch * p->num_pos;
   const int64_t nchunks = (p->vocab + kChunk - 1) / kChunk;
-  return carve(nullptr, rows, nchunks, rows).bytes;
+  const int64_t nsub = (p->vocab + kSub - 1) / kSub;
+  return carve(nullptr, rows, 1, nchunks, nsub).bytes;
 }
 
 int kyro_sample_tokens(kyro_ctx* ctx, const kyro_sample_params* p, const float* logits,
@@ -730,57 +862,45 @@ int kyro_sample_tokens(kyro_ctx* ctx, const kyro_sample_params* p, const float* 
              "kyro_sample_tokens: vocab = %d", p->vocab);
   const int64_t rows = (int64_t)p->batch * p->num_pos;
   if (rows == 0) return KYRO_OK;
-  KY_REQUIRE(rows < (1ll << 31), "kyro_sample_tokens: too many rows");
+  KY_REQUIRE(rows < (1ll << 30), "kyro_sample_tokens: too many rows");
   KY_REQUIRE(logits && out_tokens, "kyro_sample_tokens: NULL logits or out_tokens");
   const int64_t V = p->vocab;
   const int nchunks = (int)((V + kChunk - 1) / kChunk);
-  const size_t need = carve(nullptr, rows, nchunks, rows).bytes;
+  const int nsub = (int)((V + kSub - 1) / kSub);
+  const size_t need = carve(nullptr, rows, 1, nchunks, nsub).bytes;
   if (workspace_bytes < need || !workspace)
     return kyro::set_error(KYRO_ERR_WORKSPACE, "kyro_sample_tokens: workspace %zu < %zu bytes",
                            workspace_bytes, need);
-  KY_REQUIRE((uintptr_t)workspace % 256 == 0, "kyro_sample_tokens: workspace must be 256-byte aligned");
-  Workspace ws = carve(workspace, rows, nchunks, rows);
-  const bool greedy = !(p->temperature > 0.0f);
-  const float inv_t = greedy ? 1.0f : ky_inv_temperature(p->temperature);
-  const bool vec = use_vec(logits, nullptr, V);
-  cudaStream_t st = ctx->stream;
-  // rows are plain rows: B*(k+1) with k+1 == 1 per "sequence" slot
-  dim3 gridA((unsigned)rows, (unsigned)nchunks);
-  if (greedy) {
-    if (vec)
-      accept_row_stats_kernel<false, true><<<gridA, kThreads, 0, st>>>(
-          logits, nullptr, nullptr, (int)rows, 0, V, nchunks, 1.0f, ws.stats, ws.ex, ctx->d_status);
-    else
-      accept_row_stats_kernel<false, false><<<gridA, kThreads, 0, st>>>(
-          logits, nullptr, nullptr, (int)rows, 0, V, nchunks, 1.0f, ws.stats, ws.ex, ctx->d_status);
-  } else {
-    if (vec)
-      accept_row_stats_kernel<true, true><<<gridA, kThreads, 0, st>>>(
-          logits, nullptr, nullptr, (int)rows, 0, V, nchunks, inv_t, ws.stats, ws.ex, ctx->d_status);
-    else
-      accept_row_stats_kernel<true, false><<<gridA, kThreads, 0, st>>>(
-          logits, nullptr, nullptr, (int)rows, 0, V, nchunks, inv_t, ws.stats, ws.ex, ctx->d_status);
-  }
-  KY_TRY(kyro::check_launch("accept_row_stats_kernel(sample)"));
-  sample_decide_kernel<<<(unsigned)((rows + kWarps - 1) / kWarps), kThreads, 0, st>>>(
-      rows, p->num_pos, nchunks, greedy, p->seed, p->step, p->seq_offset, ws.stats,
-      ws.final_rows, ws.ticket, out_tokens, out_probs);
-  KY_TRY(kyro::check_launch("sample_decide_kernel"));
-  if (!greedy) {
-    const int per = 4;
-    KY_REQUIRE(rows <= 65535, "kyro_sample_tokens: batch*num_pos %lld > 65535", (long long)rows);
-    dim3 gridC((unsigned)((nchunks + per - 1) / per), (unsigned)rows);
-    if (vec)
-      accept_final_row_kernel<true><<<gridC, kThreads, 0, st>>>(
-          logits, nullptr, V, nchunks, per, inv_t, ws.stats, ws.final_rows, ws.W, ws.ticket,
-          out_tokens, out_probs);
-    else
-      accept_final_row_kernel<false><<<gridC, kThreads, 0, st>>>(
-          logits, nullptr, V, nchunks, per, inv_t, ws.stats, ws.final_rows, ws.W, ws.ticket,
-          out_tokens, out_probs);
-    KY_TRY(kyro::check_launch("accept_final_row_kernel(sample)"));
-  }
-  return KYRO_OK;
+  KY_REQUIRE((uintptr_t)workspace % 256 == 0,
+             "kyro_sample_tokens: workspace must be 256-byte aligned");
+  Workspace ws = carve(workspace, rows, 1, nchunks, nsub);
+  const bool stoch = p->temperature > 0.0f;
+  Args a = {};
+  a.plog = logits;
+  a.qlog = nullptr;
+  a.draft_tokens = nullptr;
+  a.B = (int)rows;
+  a.k = 0;
+  a.R = 1;
+  a.V = V;
+  a.nchunks = nchunks;
+  a.nsub = nsub;
+  a.inv_t = stoch ? ky_inv_temperature(p->temperature) : 1.0f;
+  a.stoch = stoch;
+  a.greedy_ref = 0;
+  a.sample = 1;
+  a.pos_div = p->num_pos;
+  a.seed = p->seed;
+  a.step = p->step;
+  a.seq_offset = p->seq_offset;
+  a.out_tokens = out_tokens;
+  a.out_probs = out_probs;
+  fill_workspace_args(a, ws);
+  a.ua = nchunks;
+  a.uc = stoch ? nsub : 0;
+  a.total = rows * (long long)(a.ua + a.uc);
+  a.status = ctx->d_status;
+  return launch(ctx, a, ws, use_vec(logits, nullptr, V));
 }
 
 }  // extern "C"

@@ -82,12 +82,15 @@ static void rowstat_init(ko_rowstat* st, const float* row, int32_t vocab, int32_
     if (st->m[c] > M) M = st->m[c];
   double S = 0.0;
   for (int32_t r = 0; r < num_shards; ++r) {
-    double Sr = 0.0;
-    for (int32_t c = 0; c < st->chunks_per_shard; ++c) {
-      int32_t gc = r * st->chunks_per_shard + c;
-      Sr = KY_DADD(Sr, ky_chunk_mass(E[gc], st->m[gc], M));
+    double t[32];
+    for (int32_t l = 0; l < 32; ++l) {
+      t[l] = 0.0;
+      for (int32_t c = l; c < st->chunks_per_shard; c += 32) {
+        int32_t gc = r * st->chunks_per_shard + c;
+        t[l] = KY_DADD(t[l], ky_chunk_mass(E[gc], st->m[gc], M));
+      }
     }
-    S = KY_DADD(S, Sr);
+    S = KY_DADD(S, ky_butterfly32(t));
   }
   for (int32_t c = 0; c < nc; ++c) st->g[c] = ky_chunk_scale(st->m[c], M, S);
   st->M = M;

@@ -46,7 +46,7 @@ def test_version_and_strings(lib):
     assert lib.kyro_status_string(0) == b"ok"
     assert b"workspace" in lib.kyro_status_string(8)
     names = lib.kyro_kernel_names().decode().split(";")
-    assert "verify_attention_kernel" in names and "accept_row_stats_kernel" in names
+    assert "verify_attention_kernel" in names and "accept_fused_kernel" in names
 
 
 def test_null_context_is_rejected(lib):
