@@ -129,6 +129,29 @@ int kyro_spec_accept(kyro_ctx* ctx, const kyro_accept_params* p, const float* ta
                      int32_t* out_accept_len, int32_t* out_tokens, int32_t* out_num_tokens,
                      float* out_probs, void* workspace, size_t workspace_bytes);
 
+/* kyro_spec_accept_static: kyro_spec_accept for callers that cannot
+ * allocate device memory.  No counterpart in the reference.  Some hosts
+ * hand this library only their own tensors and own every other byte of
+ * device memory themselves (a serving runtime with a fixed arena, or a
+ * real-time loop that must not call the allocator), so they have no
+ * workspace to pass.  This entry point takes the same inputs and outputs
+ * and uses instead a scratch buffer that the library keeps in a file-scope
+ * __device__ array of KYRO_ACCEPT_STATIC_SCRATCH_BYTES (8 MiB) on every GPU
+ * that loads it, held until the process exits.  It allocates nothing.
+ *   - Calls whose kyro_spec_accept_workspace_size() exceeds that size are
+ *     rejected with KYRO_ERR_WORKSPACE before anything is launched.
+ *   - The first call on a device looks up the buffer's device address (a
+ *     host-side runtime query, no allocation); make that first call before
+ *     capturing a stream into a CUDA graph.
+ *   - Every call on a device shares the one buffer and its counters are
+ *     cleared at the start of each call: calls that overlap on the GPU
+ *     (different streams, or different contexts on one device) race. */
+#define KYRO_ACCEPT_STATIC_SCRATCH_BYTES (8u << 20)
+int kyro_spec_accept_static(kyro_ctx* ctx, const kyro_accept_params* p,
+                            const float* target_logits, const float* draft_logits,
+                            const int32_t* draft_tokens, int32_t* out_accept_len,
+                            int32_t* out_tokens, int32_t* out_num_tokens, float* out_probs);
+
 /* Draft sampler: one token per row from softmax(logits / T) with Philox
  * stream 0 (counter (seq_offset + b, pos, 0, step)); temperature <= 0 is
  * argmax.  Replaces the draft loop's argmax (src/speculative.rs:229-241)

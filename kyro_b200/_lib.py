@@ -22,6 +22,9 @@ KYRO_ERR_OOM = 6
 KYRO_ERR_UNSUPPORTED = 7
 KYRO_ERR_WORKSPACE = 8
 
+# size of the library's static scratch used by kyro_spec_accept_static
+ACCEPT_STATIC_SCRATCH_BYTES = 8 << 20
+
 DEV_BAD_TOKEN = 0x1
 DEV_BAD_BLOCK = 0x2
 DEV_BAD_LENGTH = 0x4
@@ -36,7 +39,8 @@ ACCEPT_GREEDY_REF = 2
 EXPORTS = (
     "kyro_ctx_create", "kyro_ctx_destroy", "kyro_ctx_set_stream", "kyro_ctx_device_status",
     "kyro_last_error", "kyro_status_string", "kyro_version", "kyro_kernel_names",
-    "kyro_spec_accept_workspace_size", "kyro_spec_accept", "kyro_sample_workspace_size",
+    "kyro_spec_accept_workspace_size", "kyro_spec_accept", "kyro_spec_accept_static",
+    "kyro_sample_workspace_size",
     "kyro_sample_tokens", "kyro_verify_attention_workspace_size", "kyro_verify_attention",
     "kyro_kv_reserve", "kyro_kv_commit", "kyro_kv_commit_tree", "kyro_kv_write",
     "kyro_philox_uniforms",
@@ -99,6 +103,7 @@ def load():
         "kyro_kernel_names": (C.c_char_p, []),
         "kyro_spec_accept_workspace_size": (sz, [P(AcceptParams)]),
         "kyro_spec_accept": (C.c_int, [vp, P(AcceptParams), vp, vp, vp, vp, vp, vp, vp, vp, sz]),
+        "kyro_spec_accept_static": (C.c_int, [vp, P(AcceptParams), vp, vp, vp, vp, vp, vp, vp]),
         "kyro_sample_workspace_size": (sz, [P(SampleParams)]),
         "kyro_sample_tokens": (C.c_int, [vp, P(SampleParams), vp, vp, vp, vp, sz]),
         "kyro_verify_attention_workspace_size": (sz, [P(AttnParams)]),

@@ -32,6 +32,8 @@
 //
 // This file is compiled with --fmad=false; the shared arithmetic also uses
 // explicit round-to-nearest intrinsics.
+#include <mutex>
+
 #include "kyro_internal.cuh"
 #include "kyro_math.h"
 
@@ -904,3 +906,57 @@ int kyro_sample_tokens(kyro_ctx* ctx, const kyro_sample_params* p, const float* 
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------ no-allocation entry point
+//
+// kyro_spec_accept_static serves callers that cannot allocate device memory
+// and so cannot pass a workspace.  Its scratch is this file-scope array,
+// present on every device that loads the library until the process exits.
+// In host code the array's name is only a stand-in, so the device address
+// is looked up once per device with cudaGetSymbolAddress while that device
+// is current, and that address is what the kernel receives.
+
+namespace {
+
+static __device__ __align__(256) unsigned char g_accept_static_scratch[KYRO_ACCEPT_STATIC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_static_mu;
+void* g_static_ptr[kMaxDevices] = {};
+
+int static_scratch(int device, void** out) {
+  if (device < 0 || device >= kMaxDevices)
+    return kyro::set_error(KYRO_ERR_UNSUPPORTED, "kyro_spec_accept_static: device %d", device);
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  if (!g_static_ptr[device]) {
+    void* p = nullptr;
+    cudaError_t err = cudaGetSymbolAddress(&p, g_accept_static_scratch);
+    if (err != cudaSuccess)
+      return kyro::cuda_error(err, "cudaGetSymbolAddress(static accept scratch)");
+    g_static_ptr[device] = p;
+  }
+  *out = g_static_ptr[device];
+  return KYRO_OK;
+}
+
+}  // namespace
+
+extern "C" int kyro_spec_accept_static(kyro_ctx* ctx, const kyro_accept_params* p,
+                                       const float* target_logits, const float* draft_logits,
+                                       const int32_t* draft_tokens, int32_t* out_accept_len,
+                                       int32_t* out_tokens, int32_t* out_num_tokens,
+                                       float* out_probs) {
+  KY_TRY(kyro::enter(ctx));
+  KY_REQUIRE(p, "kyro_spec_accept_static: params is NULL");
+  const size_t need = kyro_spec_accept_workspace_size(p);
+  if (need > KYRO_ACCEPT_STATIC_SCRATCH_BYTES)
+    return kyro::set_error(KYRO_ERR_WORKSPACE,
+                           "kyro_spec_accept_static: this batch needs %zu bytes of scratch; the "
+                           "static scratch holds %u bytes (use kyro_spec_accept with a workspace)",
+                           need, (unsigned)KYRO_ACCEPT_STATIC_SCRATCH_BYTES);
+  void* scratch = nullptr;
+  KY_TRY(static_scratch(ctx->device, &scratch));
+  return kyro_spec_accept(ctx, p, target_logits, draft_logits, draft_tokens, out_accept_len,
+                          out_tokens, out_num_tokens, out_probs, scratch,
+                          KYRO_ACCEPT_STATIC_SCRATCH_BYTES);
+}
