@@ -6,23 +6,25 @@
 // K/V.  Here one pass streams each 16-token K and V block of a KV head once
 // for all query rows that share it (GQA group x verify positions).
 //
-// Work item: (sequence b, KV head, row group, KV split).  A CTA has one
-// producer warp and four consumer warps.  The producer issues TMA tile
-// loads (128-byte swizzle, no multicast) of the paged K/V blocks named by
-// the block table into an NS-stage shared-memory ring guarded by
-// mbarriers.  Each consumer warp takes one 16-token block per stage and
-// computes, with bf16 mma.sync (m16n8k16):
+// Work item: (sequence b, KV head, row group of <= 32 query rows, KV
+// split).  A CTA has four warps and each warp streams its own share of the
+// item's KV blocks (blocks w, w+4, w+8, ...) through a private shared-memory
+// ring with 16-byte cp.async copies.  Paged blocks are scattered 4 KB tiles,
+// and HBM bandwidth on this pattern follows the number of independent
+// warps issuing loads, so every warp is its own producer; three CTAs per SM
+// keep twelve streams in flight.  Tiles land XOR-swizzled (16-byte chunk
+// index ^ row) so ldmatrix reads them without bank conflicts.
+//
+// Per block a warp computes, with bf16 mma.sync (m16n8k16):
 //     S^T = K Q^T      (M = 16 tokens, N = query rows, K = head_dim)
 //     O^T += V^T P^T   (M = head_dim, N = query rows, K = 16 tokens)
 // so the query rows (24 for GQA 4 x 6 positions) sit in the N dimension in
-// 8-wide tiles without padding to 16.  Online softmax runs per query
-// column in the log2 domain.  The four warps' partial states are merged in
-// shared memory; when a sequence needs more than one split, each split
-// writes its partial state to the workspace and the split that finishes
-// last (atomic ticket) merges them all.
+// 8-wide tiles without padding to 16; movmatrix turns P^T into the B
+// operand.  Online softmax runs per query column in the log2 domain.  The
+// four warps' states merge in shared memory (a two-round tree); when a
+// sequence needs more than one split, each split writes its partial state
+// to the workspace and the split that finishes last (atomic ticket) merges.
 #include <cuda_bf16.h>
-#include <cudaTypedefs.h>
-
 
 #include "kyro_internal.cuh"
 #include "ptx.cuh"
@@ -30,27 +32,27 @@
 namespace {
 
 constexpr int kBS = 16;               // tokens per KV block
-constexpr int kConsumers = 4;         // consumer warps
-constexpr int kThreads = (kConsumers + 1) * 32;
-constexpr int kStages = 3;
+constexpr int kWarps = 4;
+constexpr int kThreads = kWarps * 32;
 constexpr int kMaxCols = 32;          // query rows per work item
-constexpr int kMaxSplitBlocks = 512;  // KV blocks per work item
+constexpr int kMaxSplitBlocks = 256;  // KV blocks per work item
 constexpr int kMaxSplits = 64;        // work items per (sequence, KV head, row group)
 
-// Shared-memory geometry for head_dim D (64 or 128).
-template <int D>
+// Shared-memory geometry for head_dim D (64 or 128) and NS ring stages.
+template <int D, int NS>
 struct Geo {
-  static constexpr int kTileBytes = kBS * D * 2;       // one K or V block of one head
-  static constexpr int kSlotBytes = 2 * kTileBytes;    // K + V
-  static constexpr int kStageBytes = kConsumers * kSlotBytes;
-  static constexpr int kQStride = D + 8;               // padded bf16 row stride of the Q tile
+  static constexpr int kTileBytes = kBS * D * 2;      // one K or V block of one head
+  static constexpr int kSlotBytes = 2 * kTileBytes;   // K + V
+  static constexpr int kWarpRing = NS * kSlotBytes;
+  static constexpr int kRingBytes = kWarps * kWarpRing;
+  static constexpr int kQStride = D + 8;              // padded bf16 row stride of the Q tile
   static constexpr int kQBytes = kMaxCols * kQStride * 2;
-  static constexpr int kRingBytes = kStages * kStageBytes;
-  static constexpr int kMergeBytes =
-      (kConsumers * (D * kMaxCols + 2 * kMaxCols) + kMaxSplits * kMaxCols + kMaxCols) * 4;
-  static_assert(kMergeBytes <= kRingBytes, "merge area reuses the ring");
+  // tree merge: two warps' (O, m, l) at a time
+  static constexpr int kMergeBytes = 2 * (D * kMaxCols + 2 * kMaxCols) * 4;
+  static constexpr int kFinalBytes = (kMaxSplits * kMaxCols + kMaxCols) * 4;
+  static_assert(kMergeBytes + kFinalBytes <= kRingBytes, "merge areas reuse the ring");
   static constexpr int kSmemBytes =
-      1024 + kRingBytes + kQBytes + kMaxCols * 8 + kMaxSplitBlocks * 4 + 2 * kStages * 8 + 16;
+      kRingBytes + kQBytes + kMaxCols * 8 + kMaxSplitBlocks * 4 + 16;
 };
 
 struct AttnArgs {
@@ -59,26 +61,46 @@ struct AttnArgs {
   int d;
 };
 
-// byte offset of (token row, 16-byte chunk along D) inside a swizzled tile
+// byte offset of (token row, 16-byte chunk along D) inside a swizzled tile:
+// 64-column halves of 2 KB, rows of 128 B, chunk index XOR (row & 7)
 __device__ __forceinline__ uint32_t kv_off(int row, int cidx) {
   return (uint32_t)((cidx >> 3) * 2048 + row * 128 + (((cidx & 7) ^ (row & 7)) << 4));
 }
 
-template <int NT, int D>
-__global__ void __launch_bounds__(kThreads, 2)
-verify_attention_kernel(const __grid_constant__ CUtensorMap tmK,
-                        const __grid_constant__ CUtensorMap tmV, const __nv_bfloat16* __restrict__ q,
+// Issue the cp.async copies of one block's K and V tiles (one KV head) into
+// a slot; every lane copies its share of 16-byte chunks.
+template <int D>
+__device__ __forceinline__ void load_block(uint32_t slot, const uint8_t* __restrict__ k_base,
+                                           const uint8_t* __restrict__ v_base, int64_t tile_off,
+                                           int lane) {
+  constexpr int kTile = kBS * D * 2;
+  constexpr int kChunks = kTile / 16;   // 256 (D=128) or 128 (D=64)
+  constexpr int kPerRow = D / 8;        // 16-byte chunks per token row
+  const uint8_t* ks = k_base + tile_off;
+  const uint8_t* vs = v_base + tile_off;
+#pragma unroll
+  for (int i = 0; i < kChunks / 32; ++i) {
+    const int c = lane + 32 * i;
+    const uint32_t off = kv_off(c / kPerRow, c % kPerRow);
+    kyro::ptx::cp_async_16(slot + off, ks + c * 16);
+    kyro::ptx::cp_async_16(slot + kTile + off, vs + c * 16);
+  }
+}
+
+template <int NT, int D, int NS>
+__global__ void __launch_bounds__(kThreads, 3)
+verify_attention_kernel(const __nv_bfloat16* __restrict__ q,
+                        const uint8_t* __restrict__ k_base, const uint8_t* __restrict__ v_base,
                         const int64_t* __restrict__ block_table,
                         const int64_t* __restrict__ context_lens,
                         const uint64_t* __restrict__ tree_mask, __nv_bfloat16* __restrict__ out,
                         float* __restrict__ part_o, float* __restrict__ part_ml,
                         uint32_t* __restrict__ tickets, AttnArgs a, uint32_t* status) {
-  extern __shared__ uint8_t smem_raw[];
-  using G = Geo<D>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  using G = Geo<D, NS>;
   constexpr int kD = D;
   constexpr int kTileBytes = G::kTileBytes, kSlotBytes = G::kSlotBytes;
-  constexpr int kStageBytes = G::kStageBytes, kQStride = G::kQStride, kQBytes = G::kQBytes;
-  constexpr int kRingBytes = G::kRingBytes;
+  constexpr int kQStride = G::kQStride, kQBytes = G::kQBytes;
   constexpr int kMT = D / 16;   // m-tiles of O^T along head_dim
   constexpr int kKK = D / 16;   // k-steps of S^T along head_dim
   const int split = blockIdx.x;
@@ -97,242 +119,198 @@ verify_attention_kernel(const __grid_constant__ CUtensorMap tmK,
   const int nsplit = (nblk + a.split_blocks - 1) / a.split_blocks;
   if (split >= nsplit) return;
   const int blk0 = split * a.split_blocks;
-  const int blk1 = min(nblk, blk0 + a.split_blocks);
-  const int nb = blk1 - blk0;
-  const int niter = (nb + kConsumers - 1) / kConsumers;
+  const int nb = min(nblk, blk0 + a.split_blocks) - blk0;
   const int col0 = grp * kMaxCols;
   const int ncols = min(kMaxCols, a.rows - col0);
 
-  // ---- shared memory carve-up (ring 1024-aligned for the 128B swizzle)
-  const uint32_t raw = kyro::ptx::smem_addr(smem_raw);
-  const uint32_t ring_s = (raw + 1023u) & ~1023u;
-  uint8_t* ring = smem_raw + (ring_s - raw);
-  uint8_t* qtile = ring + kRingBytes;
+  uint8_t* ring = smem;
+  uint8_t* qtile = ring + G::kRingBytes;
   uint64_t* col_mask = reinterpret_cast<uint64_t*>(qtile + kQBytes);
-  int32_t* ids = reinterpret_cast<int32_t*>(col_mask + kMaxCols);      // [kMaxSplitBlocks]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(ids + kMaxSplitBlocks);  // full[], empty[]
-  int* sh_last = reinterpret_cast<int*>(bars + 2 * kStages);
-  const uint32_t q_s = ring_s + kRingBytes;
-  const uint32_t bar_s = kyro::ptx::smem_addr(bars);
+  int32_t* ids = reinterpret_cast<int32_t*>(col_mask + kMaxCols);
+  int* sh_last = reinterpret_cast<int*>(ids + kMaxSplitBlocks);
+  const uint32_t ring_s = kyro::ptx::smem_addr(ring);
+  const uint32_t q_s = ring_s + G::kRingBytes;
 
-  if (tid == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      kyro::ptx::mbar_init(bar_s + 8 * s, 1);
-      kyro::ptx::mbar_init(bar_s + 8 * (kStages + s), kConsumers);
+  // ---- block ids of this split, Q rows, column masks
+  const int64_t* bt = block_table + (int64_t)b * a.max_blocks + blk0;
+  for (int i = tid; i < nb; i += kThreads) {
+    int64_t phys = bt[i];
+    if (phys < 0 || phys >= a.num_blocks) {
+      kyro::dev::flag(status, KYRO_DEV_BAD_BLOCK);
+      phys = 0;
     }
-    kyro::ptx::fence_barrier_init();
+    ids[i] = (int32_t)phys;
+  }
+  for (int i = tid; i < kMaxCols * (kD / 8); i += kThreads) {
+    const int col = i / (kD / 8), ch = i % (kD / 8);
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (col < ncols) {
+      const int r = col0 + col, j = r / a.group, gi = r % a.group;
+      const int h = kvh * a.group + gi;
+      v = *reinterpret_cast<const uint4*>(q + (((int64_t)b * a.nq + j) * a.hq + h) * kD + ch * 8);
+    }
+    *reinterpret_cast<uint4*>(qtile + col * kQStride * 2 + ch * 16) = v;
+  }
+  for (int col = tid; col < kMaxCols; col += kThreads) {
+    uint64_t m = 0;
+    if (col < ncols) {
+      const int j = (col0 + col) / a.group;
+      m = tree_mask ? tree_mask[(int64_t)b * a.nq + j]
+                    : (j >= 63 ? ~0ull : ((1ull << (j + 1)) - 1ull));
+    }
+    col_mask[col] = m;
   }
   __syncthreads();
 
-  bool timed_out = false;
+  // ---- this warp's blocks: w, w + 4, w + 8, ... of the split
+  const int nmy = nb > warp ? (nb - warp + kWarps - 1) / kWarps : 0;
+  const uint32_t wring = ring_s + warp * G::kWarpRing;
+  auto tile_off = [&](int i) -> int64_t {
+    return ((int64_t)ids[i * kWarps + warp] * a.hkv + kvh) * kTileBytes;
+  };
+#pragma unroll
+  for (int p = 0; p < NS - 1; ++p) {
+    if (p < nmy) load_block<D>(wring + p * kSlotBytes, k_base, v_base, tile_off(p), lane);
+    kyro::ptx::cp_async_commit();
+  }
+
   float o[kMT][NT][4];
   float m_run[NT][2], l_run[NT][2];
-  if (warp == kConsumers) {
-    // ================= producer warp: block ids of this split -> smem, then TMA
-    const int64_t* bt = block_table + (int64_t)b * a.max_blocks + blk0;
-    for (int i = lane; i < nb; i += 32) {
-      int64_t phys = bt[i];
-      if (phys < 0 || phys >= a.num_blocks) {
-        kyro::dev::flag(status, KYRO_DEV_BAD_BLOCK);
-        phys = 0;
-      }
-      ids[i] = (int32_t)phys;
-    }
-    __syncwarp();
-    if (lane == 0) {
-      kyro::ptx::prefetch_tensormap(&tmK);
-      kyro::ptx::prefetch_tensormap(&tmV);
-      for (int it = 0; it < niter; ++it) {
-        const int s = it % kStages;
-        if (it >= kStages && !timed_out) {
-          if (!kyro::ptx::mbar_wait_bounded(bar_s + 8 * (kStages + s), ((it / kStages) - 1) & 1,
-                                            kyro::dev::kWaitBudgetCycles)) {
-            timed_out = true;
-            kyro::dev::flag(status, KYRO_DEV_WAIT_TIMEOUT);
-          }
-        }
-        const int nvalid = min(kConsumers, nb - it * kConsumers);
-        const uint32_t full = bar_s + 8 * s;
-        kyro::ptx::mbar_arrive_expect_tx(full, (uint32_t)(nvalid * kSlotBytes));
-        for (int w = 0; w < nvalid; ++w) {
-          const int32_t y = (ids[it * kConsumers + w] * a.hkv + kvh) * kBS;
-          const uint32_t dst = ring_s + s * kStageBytes + w * kSlotBytes;
 #pragma unroll
-          for (int half = 0; half < kD / 64; ++half) {
-            kyro::ptx::tma_load_2d(dst + half * 2048, &tmK, half * 64, y, full);
-            kyro::ptx::tma_load_2d(dst + kTileBytes + half * 2048, &tmV, half * 64, y, full);
-          }
-        }
-      }
-    }
-    __syncwarp();
-  } else {
-    // ================= consumer warps: Q tile and masks while the first loads fly
-    for (int i = tid; i < kMaxCols * (kD / 8); i += kConsumers * 32) {
-      const int col = i / (kD / 8), ch = i % (kD / 8);
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (col < ncols) {
-        const int r = col0 + col, j = r / a.group, gi = r % a.group;
-        const int h = kvh * a.group + gi;
-        v = *reinterpret_cast<const uint4*>(q + (((int64_t)b * a.nq + j) * a.hq + h) * kD +
-                                            ch * 8);
-      }
-      *reinterpret_cast<uint4*>(qtile + col * kQStride * 2 + ch * 16) = v;
-    }
-    for (int col = tid; col < kMaxCols; col += kConsumers * 32) {
-      uint64_t m = 0;
-      if (col < ncols) {
-        const int j = (col0 + col) / a.group;
-        m = tree_mask ? tree_mask[(int64_t)b * a.nq + j]
-                      : (j >= 63 ? ~0ull : ((1ull << (j + 1)) - 1ull));
-      }
-      col_mask[col] = m;
-    }
-    asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory");
-
-#pragma unroll
-    for (int mt = 0; mt < kMT; ++mt)
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) o[mt][nt][e] = 0.0f;
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      m_run[nt][0] = m_run[nt][1] = -INFINITY;
-      l_run[nt][0] = l_run[nt][1] = 0.0f;
-    }
-    const int g8 = lane >> 3, r8 = lane & 7;
-    for (int it = 0; it < niter; ++it) {
-      const int s = it % kStages;
-      if (!timed_out) {
-        if (!kyro::ptx::mbar_wait_bounded(bar_s + 8 * s, (it / kStages) & 1,
-                                          kyro::dev::kWaitBudgetCycles)) {
-          timed_out = true;
-          kyro::dev::flag(status, KYRO_DEV_WAIT_TIMEOUT);
-        }
-      }
-      const int blk = blk0 + it * kConsumers + warp;
-      if (blk < blk1) {
-        const uint32_t ks = ring_s + s * kStageBytes + warp * kSlotBytes;
-        const uint32_t vs = ks + kTileBytes;
-        // ---- S^T = K Q^T
-        float sc[NT][4];
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) sc[nt][e] = 0.0f;
-#pragma unroll
-        for (int kk = 0; kk < kKK; kk += 2) {
-          uint32_t qb[NT][4];
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt)
-            kyro::ptx::ldsm_x4(q_s + (uint32_t)((nt * 8 + r8) * kQStride * 2 + (2 * kk + g8) * 16),
-                               qb[nt][0], qb[nt][1], qb[nt][2], qb[nt][3]);
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            uint32_t a0, a1, a2, a3;
-            // matrices: (tokens 0-7 | 8-15) x (dims lo | hi) of k-step kk+h
-            kyro::ptx::ldsm_x4(ks + kv_off((g8 & 1) * 8 + r8, 2 * (kk + h) + (g8 >> 1)), a0, a1,
-                               a2, a3);
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt)
-              kyro::ptx::mma_bf16_16816(sc[nt], a0, a1, a2, a3, qb[nt][2 * h], qb[nt][2 * h + 1]);
-          }
-        }
-        // ---- scale, mask, online softmax (per query column)
-        const int64_t tok0 = (int64_t)blk * kBS;
-        const bool need_mask = tok0 + kBS > ctx;
-        const int trow = lane >> 2;
-        float alpha[NT][2];
-        bool moved = false;
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            float v = sc[nt][e] * a.scale_log2;
-            if (need_mask) {
-              const int64_t t = tok0 + trow + (e >> 1) * 8;
-              const int col = nt * 8 + 2 * (lane & 3) + (e & 1);
-              const int64_t rel = t - ctx;
-              const bool ok = t < ctx || (rel < a.nq && ((col_mask[col] >> rel) & 1ull));
-              if (!ok) v = -INFINITY;
-            }
-            sc[nt][e] = v;
-          }
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            float cm = fmaxf(sc[nt][c], sc[nt][c + 2]);
-            cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 4));
-            cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 8));
-            cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 16));
-            const float m_new = fmaxf(m_run[nt][c], cm);
-            const float m_use = m_new == -INFINITY ? 0.0f : m_new;
-            alpha[nt][c] = kyro::ptx::fast_exp2(m_run[nt][c] - m_use);
-            moved |= m_new != m_run[nt][c];
-            const float p0 = kyro::ptx::fast_exp2(sc[nt][c] - m_use);
-            const float p1 = kyro::ptx::fast_exp2(sc[nt][c + 2] - m_use);
-            sc[nt][c] = p0;
-            sc[nt][c + 2] = p1;
-            l_run[nt][c] = l_run[nt][c] * alpha[nt][c] + p0 + p1;
-            m_run[nt][c] = m_new;
-          }
-        }
-        // rescale O only when some running max moved (alpha == 1 otherwise)
-        if (__any_sync(0xffffffffu, moved)) {
-#pragma unroll
-          for (int mt = 0; mt < kMT; ++mt)
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-              o[mt][nt][0] *= alpha[nt][0];
-              o[mt][nt][1] *= alpha[nt][1];
-              o[mt][nt][2] *= alpha[nt][0];
-              o[mt][nt][3] *= alpha[nt][1];
-            }
-        }
-        // P^T fragment (tokens x cols) -> B operand (k = tokens, n = cols)
-        uint32_t pb[NT][2];
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          pb[nt][0] = kyro::ptx::movmatrix_trans(kyro::ptx::pack_bf16x2(sc[nt][0], sc[nt][1]));
-          pb[nt][1] = kyro::ptx::movmatrix_trans(kyro::ptx::pack_bf16x2(sc[nt][2], sc[nt][3]));
-        }
-        // ---- O^T += V^T P^T
-#pragma unroll
-        for (int mt = 0; mt < kMT; ++mt) {
-          uint32_t a0, a1, a2, a3;
-          // matrices: (tokens 0-7 | 8-15) x (dims 16mt.. | 16mt+8..), transposed
-          kyro::ptx::ldsm_x4_trans(vs + kv_off((g8 >> 1) * 8 + r8, 2 * mt + (g8 & 1)), a0, a1, a2,
-                                   a3);
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt)
-            kyro::ptx::mma_bf16_16816(o[mt][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
-        }
-      }
-      __syncwarp();
-      if (lane == 0) kyro::ptx::mbar_arrive(bar_s + 8 * (kStages + s));
-    }
-    // reduce the per-thread partial sums over the 8 lanes sharing a column
+  for (int mt = 0; mt < kMT; ++mt)
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        float l = l_run[nt][c];
-        l += __shfl_xor_sync(0xffffffffu, l, 4);
-        l += __shfl_xor_sync(0xffffffffu, l, 8);
-        l += __shfl_xor_sync(0xffffffffu, l, 16);
-        l_run[nt][c] = l;
-      }
+      for (int e = 0; e < 4; ++e) o[mt][nt][e] = 0.0f;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    m_run[nt][0] = m_run[nt][1] = -INFINITY;
+    l_run[nt][0] = l_run[nt][1] = 0.0f;
   }
-  __syncthreads();  // every TMA has landed and every consumer is done with the ring
+  const int g8 = lane >> 3, r8 = lane & 7;
+  for (int i = 0; i < nmy; ++i) {
+    // keep NS-1 blocks in flight: issue block i+NS-1 into the slot freed last iteration
+    const int pf = i + NS - 1;
+    if (pf < nmy) load_block<D>(wring + (pf % NS) * kSlotBytes, k_base, v_base, tile_off(pf), lane);
+    kyro::ptx::cp_async_commit();
+    kyro::ptx::cp_async_wait<NS - 1>();  // block i has landed (this lane's copies)
+    __syncwarp();                        // ... and every lane's
+    const int blk = blk0 + i * kWarps + warp;
+    const uint32_t ks = wring + (i % NS) * kSlotBytes;
+    const uint32_t vs = ks + kTileBytes;
+    // ---- S^T = K Q^T
+    float sc[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sc[nt][e] = 0.0f;
+#pragma unroll
+    for (int kk = 0; kk < kKK; kk += 2) {
+      uint32_t qb[NT][4];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+        kyro::ptx::ldsm_x4(q_s + (uint32_t)((nt * 8 + r8) * kQStride * 2 + (2 * kk + g8) * 16),
+                           qb[nt][0], qb[nt][1], qb[nt][2], qb[nt][3]);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t a0, a1, a2, a3;
+        // matrices: (tokens 0-7 | 8-15) x (dims lo | hi) of k-step kk+h
+        kyro::ptx::ldsm_x4(ks + kv_off((g8 & 1) * 8 + r8, 2 * (kk + h) + (g8 >> 1)), a0, a1, a2,
+                           a3);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+          kyro::ptx::mma_bf16_16816(sc[nt], a0, a1, a2, a3, qb[nt][2 * h], qb[nt][2 * h + 1]);
+      }
+    }
+    // ---- scale, mask, online softmax (per query column)
+    const int64_t tok0 = (int64_t)blk * kBS;
+    const bool need_mask = tok0 + kBS > ctx;
+    const int trow = lane >> 2;
+    float alpha[NT][2];
+    bool moved = false;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float v = sc[nt][e] * a.scale_log2;
+        if (need_mask) {
+          const int64_t t = tok0 + trow + (e >> 1) * 8;
+          const int col = nt * 8 + 2 * (lane & 3) + (e & 1);
+          const int64_t rel = t - ctx;
+          const bool ok = t < ctx || (rel < a.nq && ((col_mask[col] >> rel) & 1ull));
+          if (!ok) v = -INFINITY;
+        }
+        sc[nt][e] = v;
+      }
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        float cm = fmaxf(sc[nt][c], sc[nt][c + 2]);
+        cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 4));
+        cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 8));
+        cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 16));
+        const float m_new = fmaxf(m_run[nt][c], cm);
+        const float m_use = m_new == -INFINITY ? 0.0f : m_new;
+        alpha[nt][c] = kyro::ptx::fast_exp2(m_run[nt][c] - m_use);
+        moved |= m_new != m_run[nt][c];
+        const float p0 = kyro::ptx::fast_exp2(sc[nt][c] - m_use);
+        const float p1 = kyro::ptx::fast_exp2(sc[nt][c + 2] - m_use);
+        sc[nt][c] = p0;
+        sc[nt][c + 2] = p1;
+        l_run[nt][c] = l_run[nt][c] * alpha[nt][c] + p0 + p1;
+        m_run[nt][c] = m_new;
+      }
+    }
+    // rescale O only when some running max moved (alpha == 1 otherwise)
+    if (__any_sync(0xffffffffu, moved)) {
+#pragma unroll
+      for (int mt = 0; mt < kMT; ++mt)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          o[mt][nt][0] *= alpha[nt][0];
+          o[mt][nt][1] *= alpha[nt][1];
+          o[mt][nt][2] *= alpha[nt][0];
+          o[mt][nt][3] *= alpha[nt][1];
+        }
+    }
+    // P^T fragment (tokens x cols) -> B operand (k = tokens, n = cols)
+    uint32_t pb[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      pb[nt][0] = kyro::ptx::movmatrix_trans(kyro::ptx::pack_bf16x2(sc[nt][0], sc[nt][1]));
+      pb[nt][1] = kyro::ptx::movmatrix_trans(kyro::ptx::pack_bf16x2(sc[nt][2], sc[nt][3]));
+    }
+    // ---- O^T += V^T P^T
+#pragma unroll
+    for (int mt = 0; mt < kMT; ++mt) {
+      uint32_t a0, a1, a2, a3;
+      // matrices: (tokens 0-7 | 8-15) x (dims 16mt.. | 16mt+8..), transposed
+      kyro::ptx::ldsm_x4_trans(vs + kv_off((g8 >> 1) * 8 + r8, 2 * mt + (g8 & 1)), a0, a1, a2, a3);
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+        kyro::ptx::mma_bf16_16816(o[mt][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
+    }
+    __syncwarp();  // every lane is done with this slot before it is refilled
+  }
+  kyro::ptx::cp_async_wait<0>();
+  // reduce the per-thread partial sums over the 8 lanes sharing a column
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      float l = l_run[nt][c];
+      l += __shfl_xor_sync(0xffffffffu, l, 4);
+      l += __shfl_xor_sync(0xffffffffu, l, 8);
+      l += __shfl_xor_sync(0xffffffffu, l, 16);
+      l_run[nt][c] = l;
+    }
+  __syncthreads();  // the ring is free
 
-  // ---- merge the four consumer warps in shared memory
-  float* mo = reinterpret_cast<float*>(ring);           // [warp][d][col]
-  float* mm = mo + kConsumers * kD * kMaxCols;          // [warp][col]
-  float* ml = mm + kConsumers * kMaxCols;               // [warp][col]
-  float* fscale = ml + kConsumers * kMaxCols;           // [split][col] (last-CTA merge)
-  float* finv = fscale + kMaxSplits * kMaxCols;         // [col]
-  if (warp < kConsumers) {
-    float* wo = mo + warp * kD * kMaxCols;
+  // ---- merge the four warps: (2,3) into (0,1), then 1 into 0
+  float* mo = reinterpret_cast<float*>(ring);           // [2][d][col]
+  float* mm = mo + 2 * kD * kMaxCols;                   // [2][col]
+  float* ml = mm + 2 * kMaxCols;                        // [2][col]
+  auto publish = [&](int slot) {
+    float* wo = mo + slot * kD * kMaxCols;
 #pragma unroll
     for (int mt = 0; mt < kMT; ++mt)
 #pragma unroll
@@ -349,29 +327,52 @@ verify_attention_kernel(const __grid_constant__ CUtensorMap tmK,
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           const int col = nt * 8 + 2 * lane + c;
-          mm[warp * kMaxCols + col] = m_run[nt][c];
-          ml[warp * kMaxCols + col] = l_run[nt][c];
+          mm[slot * kMaxCols + col] = m_run[nt][c];
+          ml[slot * kMaxCols + col] = l_run[nt][c];
         }
     }
-  }
+  };
+  auto absorb = [&](int slot) {
+    const float* wo = mo + slot * kD * kMaxCols;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int col = nt * 8 + 2 * (lane & 3) + c;
+        const float mo_ = mm[slot * kMaxCols + col], lo_ = ml[slot * kMaxCols + col];
+        const float M = fmaxf(m_run[nt][c], mo_);
+        const float Mu = M == -INFINITY ? 0.0f : M;
+        const float fa = kyro::ptx::fast_exp2(m_run[nt][c] - Mu);
+        const float fb = kyro::ptx::fast_exp2(mo_ - Mu);
+        l_run[nt][c] = l_run[nt][c] * fa + lo_ * fb;
+        m_run[nt][c] = M;
+#pragma unroll
+        for (int mt = 0; mt < kMT; ++mt) {
+          const int d = mt * 16 + (lane >> 2);
+          o[mt][nt][c] = o[mt][nt][c] * fa + wo[d * kMaxCols + col] * fb;
+          o[mt][nt][c + 2] = o[mt][nt][c + 2] * fa + wo[(d + 8) * kMaxCols + col] * fb;
+        }
+      }
+  };
+  if (warp >= 2) publish(warp - 2);
   __syncthreads();
+  if (warp < 2) absorb(warp);
+  __syncthreads();
+  if (warp == 1) publish(0);
+  __syncthreads();
+  if (warp == 0) absorb(0);
+  __syncthreads();
+  if (warp == 0) publish(0);  // the CTA's merged state, for the writers below
+  __syncthreads();
+
   const bool single = nsplit == 1;
   const int64_t item = ((int64_t)b * a.hkv + kvh) * a.ngroups + grp;
   float* po = part_o + item * a.max_splits * (kMaxCols * kD);
   float* pml = part_ml + item * a.max_splits * (kMaxCols * 2);
   for (int i = tid; i < ncols * kD; i += kThreads) {
     const int col = i / kD, d = i % kD;
-    float M = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < kConsumers; ++w) M = fmaxf(M, mm[w * kMaxCols + col]);
-    const float Mu = M == -INFINITY ? 0.0f : M;
-    float L = 0.0f, O = 0.0f;
-#pragma unroll
-    for (int w = 0; w < kConsumers; ++w) {
-      const float f = kyro::ptx::fast_exp2(mm[w * kMaxCols + col] - Mu);
-      L += f * ml[w * kMaxCols + col];
-      O += f * mo[(w * kD + d) * kMaxCols + col];
-    }
+    const float O = mo[d * kMaxCols + col];
+    const float L = ml[col];
     if (single) {
       const int r = col0 + col, j = r / a.group, gi = r % a.group;
       const int h = kvh * a.group + gi;
@@ -380,7 +381,7 @@ verify_attention_kernel(const __grid_constant__ CUtensorMap tmK,
     } else {
       po[(split * kMaxCols + col) * kD + d] = O;
       if (d == 0) {
-        pml[(split * kMaxCols + col) * 2 + 0] = M;
+        pml[(split * kMaxCols + col) * 2 + 0] = mm[col];
         pml[(split * kMaxCols + col) * 2 + 1] = L;
       }
     }
@@ -397,6 +398,8 @@ verify_attention_kernel(const __grid_constant__ CUtensorMap tmK,
   __syncthreads();
   if (!*sh_last) return;
   __threadfence();
+  float* fscale = reinterpret_cast<float*>(ring + G::kMergeBytes);  // [split][col]
+  float* finv = fscale + kMaxSplits * kMaxCols;                    // [col]
   for (int col = tid; col < ncols; col += kThreads) {
     float M = -INFINITY;
     for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, __ldcg(&pml[(sp * kMaxCols + col) * 2]));
@@ -422,41 +425,9 @@ verify_attention_kernel(const __grid_constant__ CUtensorMap tmK,
   if (tid == 0) tickets[item] = 0;
 }
 
-}  // namespace
+// ------------------------------------------------------------------ host
 
-#include <mutex>
-
-namespace {
-
-PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  return fn;
-}
-
-int make_kv_map(CUtensorMap* map, const void* base, int64_t rows, int kD) {
-  auto encode = get_encode_fn();
-  if (!encode) return kyro::set_error(KYRO_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
-  cuuint64_t dims[2] = {(cuuint64_t)kD, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)kD * 2};
-  cuuint32_t box[2] = {64, (cuuint32_t)kBS};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
-                      strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS)
-    return kyro::set_error(KYRO_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
-  return KYRO_OK;
-}
+constexpr int kStages = 2;
 
 struct Plan {
   AttnArgs a;
@@ -479,8 +450,8 @@ int plan(const kyro_attn_params* p, int num_sms, Plan* out) {
   KY_REQUIRE(p->max_blocks_per_seq > 0, "kyro_verify_attention: max_blocks_per_seq = %d",
              p->max_blocks_per_seq);
   KY_REQUIRE(p->num_blocks > 0, "kyro_verify_attention: num_blocks = %d", p->num_blocks);
-  KY_REQUIRE((int64_t)p->num_blocks * p->num_kv_heads * kBS < (1ll << 31),
-             "kyro_verify_attention: cache too large for 32-bit TMA rows");
+  KY_REQUIRE((int64_t)p->num_blocks * p->num_kv_heads < (1ll << 31),
+             "kyro_verify_attention: num_blocks * num_kv_heads must fit in 31 bits");
   KY_REQUIRE(p->kv_split_blocks >= 0, "kyro_verify_attention: kv_split_blocks = %d",
              p->kv_split_blocks);
   Plan pl;
@@ -499,13 +470,13 @@ int plan(const kyro_attn_params* p, int num_sms, Plan* out) {
   a.d = p->head_dim;
   int64_t split = p->kv_split_blocks;
   if (split == 0) {
-    // aim for about four waves of work items at two CTAs per SM, assuming
+    // aim for about two waves of work items at three CTAs per SM, assuming
     // half the table width is used on average
     const int64_t items = (int64_t)a.B * a.hkv * a.ngroups;
     const int64_t avg_blocks = (a.max_blocks + 1) / 2;
-    const int64_t target = (int64_t)num_sms * 2 * 4;
+    const int64_t target = (int64_t)num_sms * 3 * 2;
     split = (items * avg_blocks + target - 1) / (target > 0 ? target : 1);
-    split = (split + kConsumers - 1) / kConsumers * kConsumers;
+    split = (split + kWarps - 1) / kWarps * kWarps;
     if (split < 16) split = 16;
   }
   // a work item holds at most kMaxSplitBlocks block ids, and a sequence at
@@ -535,25 +506,26 @@ size_t ws_bytes(const Plan& pl) {
 }
 
 template <int NT, int D>
-void launch(const Plan& pl, dim3 grid, cudaStream_t st, const CUtensorMap& mk, const CUtensorMap& mv,
-            const void* q, const int64_t* bt, const int64_t* cl, const uint64_t* tm, void* out,
+void launch(const Plan& pl, dim3 grid, cudaStream_t st, const void* q, const void* kc,
+            const void* vc, const int64_t* bt, const int64_t* cl, const uint64_t* tm, void* out,
             float* po, float* pml, uint32_t* tk, uint32_t* status) {
-  cudaFuncSetAttribute(verify_attention_kernel<NT, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       Geo<D>::kSmemBytes);
-  verify_attention_kernel<NT, D><<<grid, kThreads, Geo<D>::kSmemBytes, st>>>(
-      mk, mv, (const __nv_bfloat16*)q, bt, cl, tm, (__nv_bfloat16*)out, po, pml, tk, pl.a, status);
+  constexpr int smem = Geo<D, kStages>::kSmemBytes;
+  cudaFuncSetAttribute(verify_attention_kernel<NT, D, kStages>,
+                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  verify_attention_kernel<NT, D, kStages><<<grid, kThreads, smem, st>>>(
+      (const __nv_bfloat16*)q, (const uint8_t*)kc, (const uint8_t*)vc, bt, cl, tm,
+      (__nv_bfloat16*)out, po, pml, tk, pl.a, status);
 }
 
 template <int D>
-void launch_d(const Plan& pl, dim3 grid, cudaStream_t st, const CUtensorMap& mk,
-              const CUtensorMap& mv, const void* q, const int64_t* bt, const int64_t* cl,
-              const uint64_t* tm, void* out, float* po, float* pml, uint32_t* tk,
-              uint32_t* status) {
+void launch_d(const Plan& pl, dim3 grid, cudaStream_t st, const void* q, const void* kc,
+              const void* vc, const int64_t* bt, const int64_t* cl, const uint64_t* tm,
+              void* out, float* po, float* pml, uint32_t* tk, uint32_t* status) {
   switch (pl.nt) {
-    case 1: launch<1, D>(pl, grid, st, mk, mv, q, bt, cl, tm, out, po, pml, tk, status); break;
-    case 2: launch<2, D>(pl, grid, st, mk, mv, q, bt, cl, tm, out, po, pml, tk, status); break;
-    case 3: launch<3, D>(pl, grid, st, mk, mv, q, bt, cl, tm, out, po, pml, tk, status); break;
-    default: launch<4, D>(pl, grid, st, mk, mv, q, bt, cl, tm, out, po, pml, tk, status); break;
+    case 1: launch<1, D>(pl, grid, st, q, kc, vc, bt, cl, tm, out, po, pml, tk, status); break;
+    case 2: launch<2, D>(pl, grid, st, q, kc, vc, bt, cl, tm, out, po, pml, tk, status); break;
+    case 3: launch<3, D>(pl, grid, st, q, kc, vc, bt, cl, tm, out, po, pml, tk, status); break;
+    default: launch<4, D>(pl, grid, st, q, kc, vc, bt, cl, tm, out, po, pml, tk, status); break;
   }
 }
 
@@ -582,6 +554,7 @@ int kyro_verify_attention(kyro_ctx* ctx, const kyro_attn_params* p, const void* 
   KY_REQUIRE((uintptr_t)k_cache % 16 == 0 && (uintptr_t)v_cache % 16 == 0 &&
                  (uintptr_t)q % 16 == 0,
              "kyro_verify_attention: q and the caches must be 16-byte aligned");
+  KY_REQUIRE(pl.a.B <= 65535, "kyro_verify_attention: batch %d > 65535", pl.a.B);
   const size_t need = ws_bytes(pl);
   if (need > 0 && (workspace_bytes < need || !workspace))
     return kyro::set_error(KYRO_ERR_WORKSPACE, "kyro_verify_attention: workspace %zu < %zu bytes",
@@ -592,12 +565,7 @@ int kyro_verify_attention(kyro_ctx* ctx, const kyro_attn_params* p, const void* 
   float* pml = (float*)((char*)workspace + align256(pl.part_o_bytes));
   uint32_t* tk = (uint32_t*)((char*)workspace + align256(pl.part_o_bytes) +
                              align256(pl.part_ml_bytes));
-  CUtensorMap mk, mv;
-  const int64_t rows = (int64_t)p->num_blocks * p->num_kv_heads * kBS;
-  KY_TRY(make_kv_map(&mk, k_cache, rows, p->head_dim));
-  KY_TRY(make_kv_map(&mv, v_cache, rows, p->head_dim));
   dim3 grid((unsigned)pl.a.max_splits, (unsigned)(pl.a.hkv * pl.a.ngroups), (unsigned)pl.a.B);
-  KY_REQUIRE(pl.a.B <= 65535, "kyro_verify_attention: batch %d > 65535", pl.a.B);
   cudaStream_t st = ctx->stream;
   if (pl.ticket_bytes) {
     // split tickets start at zero; the merging split also resets its ticket
@@ -605,11 +573,11 @@ int kyro_verify_attention(kyro_ctx* ctx, const kyro_attn_params* p, const void* 
     if (err != cudaSuccess) return kyro::cuda_error(err, "cudaMemsetAsync(attention tickets)");
   }
   if (p->head_dim == 128)
-    launch_d<128>(pl, grid, st, mk, mv, q, block_table, context_lens, tree_mask, out, po, pml, tk,
-                  ctx->d_status);
+    launch_d<128>(pl, grid, st, q, k_cache, v_cache, block_table, context_lens, tree_mask, out, po,
+                  pml, tk, ctx->d_status);
   else
-    launch_d<64>(pl, grid, st, mk, mv, q, block_table, context_lens, tree_mask, out, po, pml, tk,
-                 ctx->d_status);
+    launch_d<64>(pl, grid, st, q, k_cache, v_cache, block_table, context_lens, tree_mask, out, po,
+                 pml, tk, ctx->d_status);
   return kyro::check_launch("verify_attention_kernel");
 }
 

@@ -16,12 +16,12 @@
  *      counter = (sequence, position, stream, step), key = seed.
  *      Streams: 0 draft sampling, 1 accept test, 2 resample / bonus token.
  *   2. ky_exp(): an fp32 exponential for x <= 0 built from basic IEEE
- *      operations only (round-to-nearest fma/mul/add), so host and device
- *      produce the same bits.  Cody-Waite reduction x = n*ln2 + r,
- *      |r| <= ln2/2, then a degree-6 polynomial whose coefficients were
+ *      operations only (round-to-nearest fma/mul/add and integer ops), so
+ *      host and device produce the same bits.  Reduction x = n*ln2 + r,
+ *      |r| <= ln2/2, then a degree-5 polynomial whose coefficients were
  *      fitted for this project by iterated weighted least squares on
- *      [-ln2/2, ln2/2] (max relative error 1.9e-9 before rounding).
- *      Inputs below -87 (and NaN) return 0; ky_exp(0) == 1 exactly.
+ *      [-ln2/2, ln2/2] (max relative error 9.4e-8 before rounding).
+ *      Inputs below -87 (and NaN) behave as -87; ky_exp(0) == 1 exactly.
  *   3. Exact fixed-point accumulation.  Softmax mass is summed as integers:
  *      fix40(e) = floor(e * 2^40) for e in [0,1] and fix62(w) = floor(w * 2^62)
  *      for w in [0,2).  Integer sums do not depend on the order in which a
@@ -154,57 +154,79 @@ KY_HD float ky_odd_to_float(uint32_t odd) { return KY_FMUL((float)odd, 0x1p-24f)
 /* exp for x <= 0                                                       */
 /* ------------------------------------------------------------------ */
 #define KY_LOG2E 0x1.715476p+0f
-#define KY_LN2_HI 0x1.62e430p-1f /* ln2 rounded to fp32                 */
-#define KY_LN2_LO -0x1.05c610p-29f /* ln2 - KY_LN2_HI rounded to fp32   */
-#define KY_RND_MAGIC 12582912.0f   /* 1.5 * 2^23                         */
+#define KY_LN2 0x1.62e430p-1f     /* ln2 rounded to fp32                    */
+#define KY_RND_MAGIC 12582912.0f  /* 1.5 * 2^23                             */
 #define KY_EXP_C0 0x1.000000p+0f
-#define KY_EXP_C1 0x1.000000p+0f
-#define KY_EXP_C2 0x1.fffffap-2f
-#define KY_EXP_C3 0x1.55540ap-3f
-#define KY_EXP_C4 0x1.55589cp-5f
-#define KY_EXP_C5 0x1.126d66p-7f
-#define KY_EXP_C6 0x1.6ab91ep-10f
+#define KY_EXP_C1 0x1.fffff6p-1f
+#define KY_EXP_C2 0x1.fffdc0p-2f
+#define KY_EXP_C3 0x1.555a74p-3f
+#define KY_EXP_C4 0x1.573c44p-5f
+#define KY_EXP_C5 0x1.0fa6c8p-7f
 
-KY_HD float ky_exp(float x) {
-  if (!(x >= -87.0f)) return 0.0f; /* also maps NaN and -inf to 0 */
-  /* t = rint(x*log2e) + 1.5*2^23: the integer lands in the low mantissa bits */
-  float t = KY_FMAF(x, KY_LOG2E, KY_RND_MAGIC);
-  int32_t n = (int32_t)ky_f2u(t) - (int32_t)0x4B400000;
-  float nf = KY_FSUB(t, KY_RND_MAGIC);
-  float r = KY_FMAF(-nf, KY_LN2_HI, x);
-  r = KY_FMAF(-nf, KY_LN2_LO, r);
-  float p = KY_EXP_C6;
-  p = KY_FMAF(p, r, KY_EXP_C5);
+/* fmaxf returns the non-NaN operand on both host (C99) and device */
+#define KY_FMAX(a, b) fmaxf((a), (b))
+
+/* Shared core of ky_exp: x is clamped to [-87, +inf) (NaN -> -87), then
+ * x = n*ln2 + r with n = rint(x*log2e) found by the 1.5*2^23 rounding trick
+ * (t = 1.5*2^23 + n, so n sits in the low mantissa bits of t), r from one
+ * fma with fp32 ln2, and e^r from a degree-5 polynomial fitted for this
+ * project (relative error 9.4e-8 on |r| <= ln2/2, leading coefficient 1).
+ * Returns the polynomial value; *tbits gets the bits of t. */
+KY_HD float ky_exp_core(float x, uint32_t* tbits) {
+  const float xc = KY_FMAX(x, -87.0f);
+  const float t = KY_FMAF(xc, KY_LOG2E, KY_RND_MAGIC);
+  const float nf = KY_FSUB(t, KY_RND_MAGIC);
+  const float r = KY_FMAF(-nf, KY_LN2, xc);
+  float p = KY_EXP_C5;
   p = KY_FMAF(p, r, KY_EXP_C4);
   p = KY_FMAF(p, r, KY_EXP_C3);
   p = KY_FMAF(p, r, KY_EXP_C2);
   p = KY_FMAF(p, r, KY_EXP_C1);
   p = KY_FMAF(p, r, KY_EXP_C0);
-  /* n in [-126, 0] for x in [-87, 0], so 2^n is a normal number */
-  float scale = ky_u2f((uint32_t)(n + 127) << 23);
-  return KY_FMUL(p, scale);
+  *tbits = ky_f2u(t);
+  return p;
+}
+
+/* 2^(n+s) from the bits of t = 1.5*2^23 + n.  The high bits of t's
+ * encoding vanish when shifted left by 23, so (bits(t) + 127 + s) << 23
+ * is the encoding of 2^(n+s) for -126 <= n+s <= 127. */
+KY_HD float ky_pow2_from_t(uint32_t tbits, uint32_t s) {
+  return ky_u2f((tbits + 127u + s) << 23);
+}
+
+/* e^x for x <= 0 (x below -87 behaves as -87, about 1.6e-38).  Relative
+ * error within a few ulp; ky_exp(0) == 1 exactly. */
+KY_HD float ky_exp(float x) {
+  uint32_t tb;
+  const float p = ky_exp_core(x, &tb);
+  return KY_FMUL(p, ky_pow2_from_t(tb, 0u));
 }
 
 /* ------------------------------------------------------------------ */
 /* fixed point                                                          */
 /* ------------------------------------------------------------------ */
-/* floor(e * 2^40) for e in [0, 1]; at most 2^40. */
-KY_HD uint64_t ky_fix40(float e) {
+KY_HD uint64_t ky_f2u64_rz(float v) {
 #if defined(__CUDA_ARCH__)
-  return __float2ull_rz(KY_FMUL(e, 0x1p40f));
+  return __float2ull_rz(v);
 #else
-  return (uint64_t)KY_FMUL(e, 0x1p40f);
+  return (uint64_t)v;
 #endif
 }
 
-/* floor(w * 2^62) for w in [0, 2). */
-KY_HD uint64_t ky_fix62(float w) {
-#if defined(__CUDA_ARCH__)
-  return __float2ull_rz(KY_FMUL(w, 0x1p62f));
-#else
-  return (uint64_t)KY_FMUL(w, 0x1p62f);
-#endif
+/* floor(e * 2^40) for e in [0, 1]; at most 2^40. */
+KY_HD uint64_t ky_fix40(float e) { return ky_f2u64_rz(KY_FMUL(e, 0x1p40f)); }
+
+/* floor(ky_exp(x) * 2^40), computed as floor(p * 2^(n+40)).  Equal to
+ * ky_fix40(ky_exp(x)): the two differ only when ky_exp(x) is subnormal,
+ * and then both are 0. */
+KY_HD uint64_t ky_fix40_exp(float x) {
+  uint32_t tb;
+  const float p = ky_exp_core(x, &tb);
+  return ky_f2u64_rz(KY_FMUL(p, ky_pow2_from_t(tb, 40u)));
 }
+
+/* floor(w * 2^62) for w in [0, 2). */
+KY_HD uint64_t ky_fix62(float w) { return ky_f2u64_rz(KY_FMUL(w, 0x1p62f)); }
 
 /* ceil(odd * W / 2^24): the smallest inclusive prefix C_i >= this value
  * marks the sampled index.  1 <= result <= W whenever W >= 1. */
@@ -266,10 +288,19 @@ KY_HD int ky_accept(uint32_t odd, float p, float q) {
   return ky_odd_to_float(odd) < ratio;
 }
 
-/* residual weight max(p - q, 0) in fix62 */
-KY_HD uint64_t ky_residual_w(float p, float q) {
-  float d = KY_FSUB(p, q);
-  return d > 0.0f ? ky_fix62(d) : 0ull;
+/* Inverse-CDF weights.  With g62_c = g_c * 2^62 (exact) per chunk:
+ *   sampling from p:   w_i = floor(e_i * g62_c)               = fix62(p_i)
+ *   residual:          w_i = floor(max(e_i*g62_c - e'_i*g62'_c, 0))
+ *                          = fix62(max(p_i - q_i, 0))
+ * (scaling by 2^62 commutes with fp32 rounding except where a product is
+ * subnormal, and those weights are 0 either way). */
+KY_HD float ky_scale62(float g) { return KY_FMUL(g, 0x1p62f); }
+
+KY_HD uint64_t ky_weight_p(float e, float g62) { return ky_f2u64_rz(KY_FMUL(e, g62)); }
+
+KY_HD uint64_t ky_weight_residual(float ep, float g62p, float eq, float g62q) {
+  const float d = KY_FSUB(KY_FMUL(ep, g62p), KY_FMUL(eq, g62q));
+  return d > 0.0f ? ky_f2u64_rz(d) : 0ull;
 }
 
 #endif /* KYRO_MATH_H */

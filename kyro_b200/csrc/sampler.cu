@@ -16,8 +16,7 @@
 // atomic work queue in a fixed order:
 //   stats unit   one 2048-logit chunk of one row (target or draft) by one
 //                warp, 64 logits per lane held in registers: chunk max (or
-//                argmax), e at the draft token, fix40 chunk mass.  The next
-//                unit's loads are issued before the current one is reduced.
+//                argmax), e at the draft token, fix40 chunk mass.
 //   decide       run inline by the warp that finishes a sequence's last
 //                stats unit: row normalisers, the k accept tests, the
 //                accepted length, and the row to draw the emitted token from.
@@ -50,7 +49,7 @@ constexpr int kThreads = kWarps * 32;
 constexpr int kMaxChunks = 256;            // V <= 524288
 constexpr int kMaxDraft = 64;
 constexpr int kMaxRows = 2 * kMaxDraft + 1;
-constexpr int kDelta = 6;                  // sequences between stats and final units
+constexpr int kDelta = 12;                 // sequences between stats and final units
 constexpr int kBatch = 2;                  // units taken per queue access
 
 struct ChunkStat {
@@ -178,6 +177,19 @@ __device__ __forceinline__ void load_chunk(const float* __restrict__ row, int64_
                                            float (&v)[kPerLane]) {
   const int lane = threadIdx.x & 31;
   const int64_t base = (int64_t)c * kChunk;
+  if (VEC && base + kChunk <= V) {
+    // a whole chunk: no bound checks
+    const float4* p4 = reinterpret_cast<const float4*>(row + base) + lane;
+#pragma unroll
+    for (int i = 0; i < kVecPerLane; ++i) {
+      const float4 f = __ldcs(p4 + i * 32);
+      v[4 * i + 0] = f.x;
+      v[4 * i + 1] = f.y;
+      v[4 * i + 2] = f.z;
+      v[4 * i + 3] = f.w;
+    }
+    return;
+  }
 #pragma unroll
   for (int i = 0; i < kVecPerLane; ++i) {
     const int64_t e0 = base + (i * 32 + lane) * 4;
@@ -419,15 +431,24 @@ __device__ void stats_unit(const Args& a, int b, int local, float (&v)[kPerLane]
   float m = -INFINITY;
   int arg = 0x7fffffff;
   if (STOCH) {
+    if (a.inv_t != 1.0f) {
 #pragma unroll
-    for (int i = 0; i < kPerLane; ++i) {
-      v[i] = KY_FMUL(v[i], a.inv_t);
-      m = fmaxf(m, v[i]);
+      for (int i = 0; i < kPerLane; ++i) v[i] = KY_FMUL(v[i], a.inv_t);
     }
-    m = kyro::dev::warp_max(m);
-    unsigned long long E = 0;
+    // independent partial maxima and sums: max and integer addition give the
+    // same result in any order, and short chains keep the pipes busy
+    float m8[8];
 #pragma unroll
-    for (int i = 0; i < kPerLane; ++i) E += ky_fix40(ky_exp(KY_FSUB(v[i], m)));
+    for (int j = 0; j < 8; ++j) m8[j] = v[j];
+#pragma unroll
+    for (int i = 8; i < kPerLane; ++i) m8[i & 7] = fmaxf(m8[i & 7], v[i]);
+    m = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+              fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+    m = kyro::dev::warp_max(m);
+    unsigned long long e4[4] = {0ull, 0ull, 0ull, 0ull};
+#pragma unroll
+    for (int i = 0; i < kPerLane; ++i) e4[i & 3] += ky_fix40_exp(KY_FSUB(v[i], m));
+    unsigned long long E = (e4[0] + e4[1]) + (e4[2] + e4[3]);
     E = warp_sum(E);
     if (lane == 0) {
       ChunkStat s;
@@ -481,26 +502,31 @@ __device__ __forceinline__ void final_weights(const Args& a, const FinalRow& fr,
   const int c = sub / kSubsPerChunk;
   const ChunkStat* sp = a.stats + fr.p_stat * a.nchunks;
   const float mp = __ldcg(&sp[c].m);
-  const float gp = ky_chunk_scale(mp, fr.Mp, fr.Sp);
+  const float gp62 = ky_scale62(ky_chunk_scale(mp, fr.Mp, fr.Sp));
   float zp[kSubVec * 4];
   load_sub<VEC>(prow, a.V, sub, zp);
+  if (a.inv_t != 1.0f) {
+#pragma unroll
+    for (int i = 0; i < kSubVec * 4; ++i) zp[i] = KY_FMUL(zp[i], a.inv_t);
+  }
   if (residual) {
     const float* qrow = a.qlog + fr.q_row * a.V;
     const ChunkStat* sq = a.stats + fr.q_stat * a.nchunks;
     const float mq = __ldcg(&sq[c].m);
-    const float gq = ky_chunk_scale(mq, fr.Mq, fr.Sq);
+    const float gq62 = ky_scale62(ky_chunk_scale(mq, fr.Mq, fr.Sq));
     float zq[kSubVec * 4];
     load_sub<VEC>(qrow, a.V, sub, zq);
+    if (a.inv_t != 1.0f) {
 #pragma unroll
-    for (int i = 0; i < kSubVec * 4; ++i) {
-      const float p = KY_FMUL(ky_exp(KY_FSUB(KY_FMUL(zp[i], a.inv_t), mp)), gp);
-      const float q = KY_FMUL(ky_exp(KY_FSUB(KY_FMUL(zq[i], a.inv_t), mq)), gq);
-      w[i] = ky_residual_w(p, q);
+      for (int i = 0; i < kSubVec * 4; ++i) zq[i] = KY_FMUL(zq[i], a.inv_t);
     }
-  } else {
 #pragma unroll
     for (int i = 0; i < kSubVec * 4; ++i)
-      w[i] = ky_fix62(KY_FMUL(ky_exp(KY_FSUB(KY_FMUL(zp[i], a.inv_t), mp)), gp));
+      w[i] = ky_weight_residual(ky_exp(KY_FSUB(zp[i], mp)), gp62, ky_exp(KY_FSUB(zq[i], mq)),
+                                gq62);
+  } else {
+#pragma unroll
+    for (int i = 0; i < kSubVec * 4; ++i) w[i] = ky_weight_p(ky_exp(KY_FSUB(zp[i], mp)), gp62);
   }
 }
 
@@ -692,7 +718,7 @@ __device__ __forceinline__ void run_unit(const Args& a, long long u, float (&buf
 }
 
 template <bool VEC, bool STOCH>
-__global__ void __launch_bounds__(kThreads, 2) accept_fused_kernel(Args a) {
+__global__ void __launch_bounds__(kThreads, 3) accept_fused_kernel(Args a) {
   __shared__ float sM_all[kWarps][kMaxRows];
   __shared__ double sS_all[kWarps][kMaxRows];
   __shared__ int sArg_all[kWarps][kMaxRows];
@@ -701,17 +727,10 @@ __global__ void __launch_bounds__(kThreads, 2) accept_fused_kernel(Args a) {
   double* sS = sS_all[warp];
   int* sArg = sArg_all[warp];
   UnitCursor cur{0, 0};
-  float buf0[kPerLane], buf1[kPerLane];
-  long long u0 = take_unit(a, cur);
-  prefetch<VEC>(a, u0, buf0);
-  while (u0 < a.total) {
-    const long long u1 = take_unit(a, cur);
-    prefetch<VEC>(a, u1, buf1);
-    run_unit<VEC, STOCH>(a, u0, buf0, sM, sS, sArg);
-    if (u1 >= a.total) break;
-    u0 = take_unit(a, cur);
-    prefetch<VEC>(a, u0, buf0);
-    run_unit<VEC, STOCH>(a, u1, buf1, sM, sS, sArg);
+  float buf[kPerLane];
+  for (long long u = take_unit(a, cur); u < a.total; u = take_unit(a, cur)) {
+    prefetch<VEC>(a, u, buf);
+    run_unit<VEC, STOCH>(a, u, buf, sM, sS, sArg);
   }
 }
 

@@ -40,8 +40,9 @@ typedef struct {
   const float* row;
   int32_t vocab, num_shards, shard_len, chunks_per_shard;
   float inv_t;
-  float* m;  /* per chunk max of s                        */
-  float* g;  /* per chunk probability scale g_c            */
+  float* m;    /* per chunk max of s                        */
+  float* g;    /* per chunk probability scale g_c            */
+  float* g62;  /* g_c * 2^62                                 */
   float M;
   double S;
 } ko_rowstat;
@@ -63,6 +64,7 @@ static void rowstat_init(ko_rowstat* st, const float* row, int32_t vocab, int32_
   int32_t nc = st->chunks_per_shard * num_shards;
   st->m = (float*)malloc(sizeof(float) * (size_t)nc);
   st->g = (float*)malloc(sizeof(float) * (size_t)nc);
+  st->g62 = (float*)malloc(sizeof(float) * (size_t)nc);
   uint64_t* E = (uint64_t*)calloc((size_t)nc, sizeof(uint64_t));
   /* chunk maxima */
   for (int32_t c = 0; c < nc; ++c) st->m[c] = -INFINITY;
@@ -75,7 +77,7 @@ static void rowstat_init(ko_rowstat* st, const float* row, int32_t vocab, int32_
   for (int32_t i = 0; i < vocab; ++i) {
     float s = KY_FMUL(row[i], inv_t);
     int32_t c = chunk_of(st, i);
-    E[c] += ky_fix40(ky_exp(KY_FSUB(s, st->m[c])));
+    E[c] += ky_fix40_exp(KY_FSUB(s, st->m[c]));
   }
   float M = -INFINITY;
   for (int32_t c = 0; c < nc; ++c)
@@ -92,7 +94,10 @@ static void rowstat_init(ko_rowstat* st, const float* row, int32_t vocab, int32_
     }
     S = KY_DADD(S, ky_butterfly32(t));
   }
-  for (int32_t c = 0; c < nc; ++c) st->g[c] = ky_chunk_scale(st->m[c], M, S);
+  for (int32_t c = 0; c < nc; ++c) {
+    st->g[c] = ky_chunk_scale(st->m[c], M, S);
+    st->g62[c] = ky_scale62(st->g[c]);
+  }
   st->M = M;
   st->S = S;
   free(E);
@@ -101,6 +106,17 @@ static void rowstat_init(ko_rowstat* st, const float* row, int32_t vocab, int32_
 static void rowstat_free(ko_rowstat* st) {
   free(st->m);
   free(st->g);
+  free(st->g62);
+}
+
+static float rowstat_e(const ko_rowstat* st, int32_t i) {
+  int32_t c = chunk_of(st, i);
+  return ky_exp(KY_FSUB(KY_FMUL(st->row[i], st->inv_t), st->m[c]));
+}
+
+/* inverse-CDF weight of entry i for sampling from p */
+static uint64_t rowstat_wp(const ko_rowstat* st, int32_t i) {
+  return ky_weight_p(rowstat_e(st, i), st->g62[chunk_of(st, i)]);
 }
 
 static float rowstat_p(const ko_rowstat* st, int32_t i) {
@@ -170,7 +186,7 @@ static void sample_range(const sample_job* J) {
       } else {
         ko_rowstat st;
         rowstat_init(&st, row, J->vocab, 1, ky_inv_temperature(J->temperature));
-        for (int32_t i = 0; i < J->vocab; ++i) w[i] = ky_fix62(rowstat_p(&st, i));
+        for (int32_t i = 0; i < J->vocab; ++i) w[i] = rowstat_wp(&st, i);
         uint32_t odd = ky_uniform_odd(J->seed, (uint32_t)(J->seq_offset + b), (uint32_t)j,
                                       KY_STREAM_DRAFT, J->step);
         tok = inverse_cdf(w, J->vocab, odd);
@@ -317,13 +333,14 @@ static void accept_one_stochastic(const accept_job* J, int32_t b, uint64_t* w) {
     ko_rowstat Q;
     rowstat_init(&Q, drf + (size_t)a * V, V, J->num_shards, inv_t);
     for (int32_t i = 0; i < V; ++i) {
-      w[i] = ky_residual_w(rowstat_p(&P, i), rowstat_p(&Q, i));
+      w[i] = ky_weight_residual(rowstat_e(&P, i), P.g62[chunk_of(&P, i)], rowstat_e(&Q, i),
+                                Q.g62[chunk_of(&Q, i)]);
       W += w[i];
     }
     rowstat_free(&Q);
   }
   if (W == 0) /* bonus row, or a residual with no mass: sample from p */
-    for (int32_t i = 0; i < V; ++i) w[i] = ky_fix62(rowstat_p(&P, i));
+    for (int32_t i = 0; i < V; ++i) w[i] = rowstat_wp(&P, i);
   rowstat_free(&P);
   uint32_t odd = ky_uniform_odd(J->seed, seq, (uint32_t)a, KY_STREAM_RESAMPLE, J->step);
   toks[a] = inverse_cdf(w, V, odd);
