@@ -56,7 +56,7 @@ extern "C" {
 int kyro_version(void) { return KYRO_VERSION; }
 
 const char* kyro_kernel_names(void) {
-  return "accept_fused_kernel;verify_attention_kernel;kv_reserve_kernel;kv_commit_kernel;"
+  return "accept_stats_kernel;accept_decide_kernel;accept_final_kernel;verify_attention_kernel;kv_reserve_kernel;kv_commit_kernel;"
          "kv_tree_move_kernel;kv_write_kernel;philox_uniforms_kernel";
 }
 

@@ -257,7 +257,9 @@ KY_HD uint64_t ky_cdf_threshold(uint32_t odd, uint64_t W) {
  *   p_i = e_i * g_c                           (fp32)
  * The same row statistics drive the accept test, the residual and the
  * bonus sample. */
-#define KY_CHUNK 2048
+/* 512 entries: one warp holds a chunk in registers (16 per lane), so a
+ * chunk's statistics need no exchange between warps. */
+#define KY_CHUNK 512
 
 /* inv_t for temperature t > 0: (float)(1/(double)t); candle's `tensor / t`
  * (worker.rs:298) is an affine op multiplying by the reciprocal. */

@@ -106,6 +106,13 @@ __device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src) {
                : "memory");
 }
 
+// 4-byte asynchronous copy global -> shared (.ca), for unaligned rows.
+__device__ __forceinline__ void cp_async_4(uint32_t dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst),
+               "l"(reinterpret_cast<uint64_t>(src))
+               : "memory");
+}
+
 __device__ __forceinline__ void cp_async_commit() {
   asm volatile("cp.async.commit_group;" ::: "memory");
 }

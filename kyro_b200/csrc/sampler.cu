@@ -10,24 +10,23 @@
 // per-chunk maxima, ky_exp, exact integer (fix40) chunk masses, a fixed
 // butterfly combination in double, and integer (fix62) inverse-CDF weights.
 // Integer sums do not depend on how threads are arranged, so the parallel
-// kernel reproduces the sequential oracle bit for bit.
+// kernels reproduce the sequential oracle bit for bit.
 //
-// One persistent launch does the whole step.  Warps take units from an
-// atomic work queue in a fixed order:
-//   stats unit   one 2048-logit chunk of one row (target or draft) by one
-//                warp, 64 logits per lane held in registers: chunk max (or
-//                argmax), e at the draft token, fix40 chunk mass.
-//   decide       run inline by the warp that finishes a sequence's last
-//                stats unit: row normalisers, the k accept tests, the
-//                accepted length, and the row to draw the emitted token from.
-//   final unit   512 logits of that row: fix62 weights (residual or p) and
-//                their sum.  The warp that finishes a row's last final unit
-//                locates the sub-range holding the cut point and scans it.
-// A sequence's final units are queued kDelta sequences after its stats
-// units, so the final row is read again while it is still in L2, and a
-// final unit waits (bounded) for its sequence's decision.  Units a waiting
-// warp holds always come later in the queue than the unit it waits on, so
-// the wait always ends.
+// Three launches, none of which waits on another CTA:
+//   accept_stats_kernel   persistent, one warp per 512-entry chunk of every
+//                         row (target and draft), grid-stride.  A lane holds
+//                         16 logits in registers: chunk max (or argmax),
+//                         fix40 chunk mass, and e at the draft token.  Each
+//                         warp loads its next chunk while it reduces the
+//                         current one.  This kernel reads every logit once
+//                         and carries nearly all of the step's HBM traffic.
+//   accept_decide_kernel  one CTA per sequence: row normalisers (or argmaxes)
+//                         from the chunk statistics, then the k accept tests,
+//                         the accepted length and the row to draw from.
+//   accept_final_kernel   one warp per 512 entries of each chosen row: fix62
+//                         weights (residual or p) and their sum; the warp
+//                         that finishes a row's last sum finds the 512-entry
+//                         range holding the cut point and scans it.
 //
 // This file is compiled with --fmad=false; the shared arithmetic also uses
 // explicit round-to-nearest intrinsics.
@@ -38,24 +37,29 @@
 
 namespace {
 
-constexpr int kChunk = KY_CHUNK;           // logits per stats unit
-constexpr int kPerLane = kChunk / 32;      // 64
-constexpr int kVecPerLane = kPerLane / 4;  // 16 float4
-constexpr int kSub = 512;                  // logits per final unit
-constexpr int kSubVec = kSub / 128;        // 4 float4 per lane
-constexpr int kSubsPerChunk = kChunk / kSub;
-constexpr int kWarps = 4;                  // warps per CTA
+constexpr int kChunk = KY_CHUNK;     // 512 logits per chunk, one warp
+constexpr int kVec = kChunk / 128;   // 4 float4 per lane
+constexpr int kPerLane = kChunk / 32;
+constexpr int kWarps = 4;            // warps per CTA (stats and final kernels)
 constexpr int kThreads = kWarps * 32;
-constexpr int kMaxChunks = 256;            // V <= 524288
+constexpr int kStatsMinCtas = 8;     // resident CTAs per SM the registers allow
+constexpr int kMaxChunks = 1024;     // V <= 524288
 constexpr int kMaxDraft = 64;
 constexpr int kMaxRows = 2 * kMaxDraft + 1;
-constexpr int kDelta = 12;                 // sequences between stats and final units
-constexpr int kBatch = 2;                  // units taken per queue access
+constexpr int kDecideWarps = 8;
+
+static_assert(kChunk == 512, "the kernels assume 16 logits per lane");
 
 struct ChunkStat {
   float m;               // chunk max of s = z * inv_t (or of z, greedy)
   int32_t arg;           // lowest index attaining m (greedy)
   unsigned long long E;  // sum of fix40(ky_exp(s - m)) over the chunk
+};
+
+struct RowStat {
+  float M;      // row max
+  int32_t arg;  // row argmax (greedy)
+  double S;     // row normaliser
 };
 
 // The row a sequence (or a sampled row) draws its emitted token from.
@@ -72,6 +76,23 @@ struct FinalRow {
   int32_t _pad;
 };
 
+// n / d for 0 <= n < 2^31 as (umulhi(n, m) + n) >> s (Granlund and
+// Montgomery, "Division by invariant integers using multiplication", 1994).
+struct FastDiv {
+  uint32_t d, m, s;
+};
+
+FastDiv make_fastdiv(uint32_t d) {
+  uint32_t s = 0;
+  while ((1ull << s) < d) ++s;
+  const uint64_t m = ((1ull << 32) * ((1ull << s) - d)) / d + 1;
+  return FastDiv{d, (uint32_t)m, s};
+}
+
+__device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv& f) {
+  return (__umulhi(n, f.m) + n) >> f.s;
+}
+
 struct Args {
   const float* plog;            // target logits (accept) or the rows to sample
   const float* qlog;            // draft logits (stochastic accept) or null
@@ -80,7 +101,8 @@ struct Args {
   int k;                        // drafts per sequence; 0 for the sampler
   int R;                        // stats rows per sequence
   int64_t V;
-  int nchunks, nsub;
+  int nchunks;
+  FastDiv div_chunks, div_rows;  // by nchunks, by R
   float inv_t;
   int stoch;                    // softmax statistics (else argmax only)
   int greedy_ref;
@@ -93,27 +115,20 @@ struct Args {
   int32_t* out_tokens;
   int32_t* out_num_tokens;
   float* out_probs;             // accept: [B,k,2] (p,q); sampler: [rows]
-  ChunkStat* stats;
-  float* ex;
-  FinalRow* final_rows;
-  unsigned long long* W;
-  uint32_t* cnt_a;
-  uint32_t* cnt_c;
-  uint32_t* ready;
-  unsigned long long* queue;
-  int ua, uc;                   // stats units and final units per sequence
-  long long total;
+  ChunkStat* stats;             // [B*R][nchunks]
+  float* ex;                    // [B*R] e at the draft token
+  FinalRow* final_rows;         // [B]
+  unsigned long long* W;        // [B][nchunks] weight sums of the chosen rows
+  uint32_t* cnt_c;              // [B] finished weight sums per sequence
+  uint32_t units;               // stats units: B * R * nchunks
   uint32_t* status;
 };
 
 __host__ __device__ inline size_t align_up(size_t x) { return (x + 255) & ~size_t(255); }
 
-// Workspace: counters first (zeroed before every launch), then the rest.
+// Workspace: the counters first (zeroed before every launch), then the rest.
 struct Workspace {
-  unsigned long long* queue;
-  uint32_t* cnt_a;
   uint32_t* cnt_c;
-  uint32_t* ready;
   size_t counter_bytes;
   ChunkStat* stats;
   float* ex;
@@ -122,17 +137,11 @@ struct Workspace {
   size_t bytes;
 };
 
-Workspace carve(void* base, int64_t B, int64_t R, int64_t nchunks, int64_t nsub) {
+Workspace carve(void* base, int64_t B, int64_t R, int64_t nchunks) {
   Workspace w;
   char* p = (char*)base;
   size_t off = 0;
-  w.queue = (unsigned long long*)(p + off);
-  off += 256;
-  w.cnt_a = (uint32_t*)(p + off);
-  off += align_up(4 * (size_t)B);
   w.cnt_c = (uint32_t*)(p + off);
-  off += align_up(4 * (size_t)B);
-  w.ready = (uint32_t*)(p + off);
   off += align_up(4 * (size_t)B);
   w.counter_bytes = off;
   w.stats = (ChunkStat*)(p + off);
@@ -142,12 +151,21 @@ Workspace carve(void* base, int64_t B, int64_t R, int64_t nchunks, int64_t nsub)
   w.final_rows = (FinalRow*)(p + off);
   off += align_up(sizeof(FinalRow) * (size_t)B);
   w.W = (unsigned long long*)(p + off);
-  off += align_up(sizeof(unsigned long long) * (size_t)(B * nsub));
+  off += align_up(sizeof(unsigned long long) * (size_t)(B * nchunks));
   w.bytes = off;
   return w;
 }
 
-// ------------------------------------------------------------ warp helpers
+// ------------------------------------------------------------ primitives
+
+__device__ __forceinline__ uint32_t atomic_add_acq_rel(uint32_t* p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;"
+               : "=r"(old)
+               : "l"(p), "r"(v)
+               : "memory");
+  return old;
+}
 
 __device__ __forceinline__ unsigned long long warp_sum(unsigned long long v) {
   return kyro::dev::warp_sum_u64(v);
@@ -170,94 +188,39 @@ __device__ __forceinline__ unsigned long long warp_inclusive(unsigned long long 
   return v;
 }
 
-// The 64 logits of chunk c this lane owns: float4 i (0..15) covers elements
-// c*2048 + (i*32 + lane)*4 + 0..3.  Entries beyond V read as -inf.
-template <bool VEC>
-__device__ __forceinline__ void load_chunk(const float* __restrict__ row, int64_t V, int c,
-                                           float (&v)[kPerLane]) {
+// Lane 0 counts this warp's contribution (release: lane 0's earlier writes
+// become visible first; acquire: the other contributors' writes are visible
+// afterwards).  True in every lane of the warp that made the count reach
+// `total_minus_one + 1`.
+__device__ __forceinline__ bool warp_last_of(uint32_t* counter, uint32_t total_minus_one) {
   const int lane = threadIdx.x & 31;
-  const int64_t base = (int64_t)c * kChunk;
-  if (VEC && base + kChunk <= V) {
-    // a whole chunk: no bound checks
-    const float4* p4 = reinterpret_cast<const float4*>(row + base) + lane;
-#pragma unroll
-    for (int i = 0; i < kVecPerLane; ++i) {
-      const float4 f = __ldcs(p4 + i * 32);
-      v[4 * i + 0] = f.x;
-      v[4 * i + 1] = f.y;
-      v[4 * i + 2] = f.z;
-      v[4 * i + 3] = f.w;
-    }
-    return;
-  }
-#pragma unroll
-  for (int i = 0; i < kVecPerLane; ++i) {
-    const int64_t e0 = base + (i * 32 + lane) * 4;
-    if (VEC) {
-      float4 f = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-      if (e0 < V) f = __ldcs(reinterpret_cast<const float4*>(row + e0));
-      v[4 * i + 0] = f.x;
-      v[4 * i + 1] = f.y;
-      v[4 * i + 2] = f.z;
-      v[4 * i + 3] = f.w;
-    } else {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) v[4 * i + j] = (e0 + j < V) ? __ldcs(row + e0 + j) : -INFINITY;
-    }
-  }
+  uint32_t last = 0;
+  if (lane == 0) last = atomic_add_acq_rel(counter, 1u) == total_minus_one;
+  last = __shfl_sync(0xffffffffu, last, 0);
+  __syncwarp();
+  return last != 0;
 }
 
-// 16 logits of final unit `sub`: float4 i (0..3) covers elements
-// sub*512 + (i*32 + lane)*4 + 0..3.
-template <bool VEC>
-__device__ __forceinline__ void load_sub(const float* __restrict__ row, int64_t V, int sub,
-                                         float (&v)[kSubVec * 4]) {
-  const int lane = threadIdx.x & 31;
-  const int64_t base = (int64_t)sub * kSub;
-#pragma unroll
-  for (int i = 0; i < kSubVec; ++i) {
-    const int64_t e0 = base + (i * 32 + lane) * 4;
-    if (VEC) {
-      float4 f = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-      if (e0 < V) f = __ldcg(reinterpret_cast<const float4*>(row + e0));
-      v[4 * i + 0] = f.x;
-      v[4 * i + 1] = f.y;
-      v[4 * i + 2] = f.z;
-      v[4 * i + 3] = f.w;
-    } else {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) v[4 * i + j] = (e0 + j < V) ? __ldcg(row + e0 + j) : -INFINITY;
-    }
-  }
-}
-
-// Map queue position u to (kind, sequence, index within the sequence).
-// Slot s holds the stats units of sequence s (s < B), then the final units
-// of sequence s - kDelta (s >= kDelta).  off(s) = ua*min(s,B) + uc*max(0,s-kDelta).
-__device__ __forceinline__ long long slot_off(const Args& a, int s) {
-  return (long long)a.ua * min(s, a.B) + (long long)a.uc * max(0, s - kDelta);
-}
-
-__device__ __forceinline__ void unit_of(const Args& a, long long u, bool& is_stats, int& seq,
-                                        int& local) {
-  int lo = 0, hi = a.B + kDelta - 1;  // first slot s with off(s+1) > u
-  while (lo < hi) {
-    const int mid = (lo + hi) >> 1;
-    if (slot_off(a, mid + 1) > u)
-      hi = mid;
-    else
-      lo = mid + 1;
-  }
-  const long long rem = u - slot_off(a, lo);
-  if (lo < a.B && rem < a.ua) {
-    is_stats = true;
-    seq = lo;
-    local = (int)rem;
-  } else {
-    is_stats = false;
-    seq = lo - kDelta;
-    local = (int)(rem - (lo < a.B ? a.ua : 0));
-  }
+// ky_fix40_exp(x), bit for bit, in fewer instructions.  Scaling every
+// polynomial coefficient by 2^40 scales each round-to-nearest fma result by
+// exactly 2^40 (the values stay far from the subnormal and overflow ranges),
+// so p40 == 2^40 * p; and with t = 1.5*2^23 + n, bits(t) << 23 == n << 23
+// (mod 2^32), so adding it to bits(p40) multiplies by 2^n exactly (x >= -87
+// keeps n >= -126 and the product normal).  The contract's form is
+// floor(p * 2^(n+40)) with the same p and n.
+__device__ __forceinline__ unsigned long long fix40_exp_fast(float x) {
+  const float xc = fmaxf(x, -87.0f);
+  const float t = __fmaf_rn(xc, KY_LOG2E, KY_RND_MAGIC);
+  const float nf = __fsub_rn(t, KY_RND_MAGIC);
+  const float r = __fmaf_rn(-nf, KY_LN2, xc);
+  float p = KY_EXP_C5 * 0x1p40f;
+  p = __fmaf_rn(p, r, KY_EXP_C4 * 0x1p40f);
+  p = __fmaf_rn(p, r, KY_EXP_C3 * 0x1p40f);
+  p = __fmaf_rn(p, r, KY_EXP_C2 * 0x1p40f);
+  p = __fmaf_rn(p, r, KY_EXP_C1 * 0x1p40f);
+  p = __fmaf_rn(p, r, KY_EXP_C0 * 0x1p40f);
+  const uint32_t bits = __float_as_uint(p) + (__float_as_uint(t) << 23);
+  return __float2ull_rz(__uint_as_float(bits));
 }
 
 __device__ __forceinline__ const float* stats_row_ptr(const Args& a, int b, int r) {
@@ -272,51 +235,176 @@ __device__ __forceinline__ int draft_token_of_row(const Args& a, int b, int r) {
   return -1;
 }
 
-// ------------------------------------------------------------ decide step
+// ------------------------------------------------------------ stats kernel
 
-// Runs in one warp once every stats unit of sequence b is done.
-__device__ void decide(const Args& a, int b, float* sM, double* sS, int* sArg) {
+// One chunk in flight: its 16 logits per lane and where it belongs.
+struct Slice {
+  float v[kPerLane];  // float4 i (0..3) holds chunk entries (i*32 + lane)*4 + 0..3
+  uint32_t srow;      // stats row: b * R + r
+  int c;              // chunk index in the row
+  int x;              // draft token scored in this row, -1 if none
+};
+
+// Issue the loads of unit u (entries past V read as -inf).
+template <bool VEC>
+__device__ __forceinline__ void load_slice(const Args& a, uint32_t u, Slice& s) {
   const int lane = threadIdx.x & 31;
-  const int R = a.R;
-  for (int r = 0; r < R; ++r) {
-    const ChunkStat* st = a.stats + ((int64_t)b * R + r) * a.nchunks;
-    if (a.stoch) {
-      float M = -INFINITY;
-      for (int c = lane; c < a.nchunks; c += 32) M = fmaxf(M, __ldcg(&st[c].m));
-      M = kyro::dev::warp_max(M);
-      double t = 0.0;
-      for (int c = lane; c < a.nchunks; c += 32)
-        t = KY_DADD(t, ky_chunk_mass(__ldcg(&st[c].E), __ldcg(&st[c].m), M));
-      const double S = warp_butterfly(t);
-      if (lane == 0) {
-        sM[r] = M;
-        sS[r] = S;
-      }
+  const uint32_t srow = fdiv(u, a.div_chunks);
+  const int c = (int)(u - srow * (uint32_t)a.nchunks);
+  const int b = (int)fdiv(srow, a.div_rows);
+  const int r = (int)(srow - (uint32_t)b * (uint32_t)a.R);
+  s.srow = srow;
+  s.c = c;
+  s.x = draft_token_of_row(a, b, r);
+  const float* row = stats_row_ptr(a, b, r);
+  const int64_t base = (int64_t)c * kChunk;
+#pragma unroll
+  for (int i = 0; i < kVec; ++i) {
+    const int64_t e0 = base + (i * 32 + lane) * 4;
+    if (VEC) {
+      float4 f = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+      if (e0 < a.V) f = __ldcg(reinterpret_cast<const float4*>(row + e0));
+      s.v[4 * i + 0] = f.x;
+      s.v[4 * i + 1] = f.y;
+      s.v[4 * i + 2] = f.z;
+      s.v[4 * i + 3] = f.w;
     } else {
-      float best = -INFINITY;
-      int bi = 0x7fffffff;
-      for (int c = lane; c < a.nchunks; c += 32) {
-        const float m = __ldcg(&st[c].m);
-        const int ai = __ldcg(&st[c].arg);
-        if (m > best || (m == best && ai < bi)) {
-          best = m;
-          bi = ai;
-        }
-      }
-      kyro::dev::warp_argmax(best, bi);
-      if (lane == 0) sArg[r] = bi == 0x7fffffff ? 0 : bi;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) s.v[4 * i + j] = (e0 + j < a.V) ? __ldcg(row + e0 + j) : -INFINITY;
     }
   }
-  __syncwarp();
+}
 
+// Reduce one chunk and store its statistics.
+template <bool STOCH>
+__device__ __forceinline__ void reduce_slice(const Args& a, Slice& s) {
+  const int lane = threadIdx.x & 31;
+  const int64_t base = (int64_t)s.c * kChunk;
+  ChunkStat st;
+  if (STOCH) {
+    if (a.inv_t != 1.0f) {
+#pragma unroll
+      for (int i = 0; i < kPerLane; ++i) s.v[i] = KY_FMUL(s.v[i], a.inv_t);
+    }
+    // independent partial maxima and sums: max and integer addition give
+    // the same result in any order, and short chains keep the pipes busy
+    float m4[4] = {s.v[0], s.v[1], s.v[2], s.v[3]};
+#pragma unroll
+    for (int i = 4; i < kPerLane; ++i) m4[i & 3] = fmaxf(m4[i & 3], s.v[i]);
+    const float m = kyro::dev::warp_max(fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])));
+    unsigned long long e4[4] = {0ull, 0ull, 0ull, 0ull};
+#pragma unroll
+    for (int i = 0; i < kPerLane; ++i) e4[i & 3] += fix40_exp_fast(KY_FSUB(s.v[i], m));
+    st.m = m;
+    st.arg = 0;
+    st.E = warp_sum((e4[0] + e4[1]) + (e4[2] + e4[3]));
+    // e at the draft token, by the lane that holds it (s.v holds z * inv_t)
+    const int64_t xo = (int64_t)s.x - base;
+    if (s.x >= 0 && s.x < a.V && xo >= 0 && xo < kChunk && lane == (int)((xo >> 2) & 31)) {
+      const int q = (int)(((xo >> 7) << 2) | (xo & 3));
+      float z = s.v[0];
+#pragma unroll
+      for (int i = 1; i < kPerLane; ++i)
+        if (i == q) z = s.v[i];
+      a.ex[s.srow] = ky_exp(KY_FSUB(z, m));
+    }
+  } else {
+    float m = -INFINITY;
+    int arg = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < kPerLane; ++i)
+      if (s.v[i] > m) {
+        m = s.v[i];
+        arg = (int)(base + ((i >> 2) * 32 + lane) * 4 + (i & 3));
+      }
+    kyro::dev::warp_argmax(m, arg);
+    st.m = m;
+    st.arg = arg;
+    st.E = 0;
+  }
+  if (lane == 0) a.stats[(int64_t)s.srow * a.nchunks + s.c] = st;
+}
+
+// Persistent and grid-stride: warp w takes units w, w + W, w + 2W, ... (W =
+// warps in the grid), so neighbouring warps read neighbouring chunks.  Each
+// warp loads unit i+1 before it reduces unit i.
+template <bool VEC, bool STOCH>
+__global__ void __launch_bounds__(kThreads, kStatsMinCtas) accept_stats_kernel(Args a) {
+  const uint32_t stride = gridDim.x * kWarps;
+  uint32_t u = blockIdx.x * kWarps + (threadIdx.x >> 5);
+  if (u >= a.units) return;
+  Slice s0, s1;
+  load_slice<VEC>(a, u, s0);
+  while (true) {
+    uint32_t un = u + stride;
+    if (un < a.units) load_slice<VEC>(a, un, s1);
+    reduce_slice<STOCH>(a, s0);
+    if (un >= a.units) break;
+    u = un;
+    un = u + stride;
+    if (un < a.units) load_slice<VEC>(a, un, s0);
+    reduce_slice<STOCH>(a, s1);
+    if (un >= a.units) break;
+    u = un;
+  }
+}
+
+// ------------------------------------------------------------ decide kernel
+
+// Row normaliser (or argmax) of stats row srow, by one warp.
+__device__ __forceinline__ RowStat row_stat(const Args& a, int64_t srow) {
+  const int lane = threadIdx.x & 31;
+  const ChunkStat* st = a.stats + srow * a.nchunks;
+  RowStat rs;
+  rs.arg = 0;
+  rs.S = 0.0;
+  if (a.stoch) {
+    float M = -INFINITY;
+    for (int c = lane; c < a.nchunks; c += 32) M = fmaxf(M, st[c].m);
+    M = kyro::dev::warp_max(M);
+    double t = 0.0;
+    for (int c = lane; c < a.nchunks; c += 32) t = KY_DADD(t, ky_chunk_mass(st[c].E, st[c].m, M));
+    rs.M = M;
+    rs.S = warp_butterfly(t);
+  } else {
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int c = lane; c < a.nchunks; c += 32) {
+      const float m = st[c].m;
+      const int ai = st[c].arg;
+      if (m > best || (m == best && ai < bi)) {
+        best = m;
+        bi = ai;
+      }
+    }
+    kyro::dev::warp_argmax(best, bi);
+    rs.M = best;
+    rs.arg = bi == 0x7fffffff ? 0 : bi;
+  }
+  return rs;
+}
+
+// One CTA per sequence (per row for the sampler): the warps compute the row
+// statistics, then warp 0 runs the accept tests and writes the sequence's
+// accepted prefix and the row its last token is drawn from.
+__global__ void __launch_bounds__(kDecideWarps * 32) accept_decide_kernel(Args a) {
+  __shared__ RowStat rs[kMaxRows];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const int b = blockIdx.x;
+  for (int r = warp; r < a.R; r += nwarps) {
+    const RowStat s = row_stat(a, (int64_t)b * a.R + r);
+    if (lane == 0) rs[r] = s;
+  }
+  __syncthreads();
+  if (warp != 0) return;
   const int k = a.k;
   FinalRow fr;
   fr._pad = 0;
   if (a.sample) {
     // one row per "sequence": the draft sampler
-    const int64_t seq = a.seq_offset + b / a.pos_div;
-    const int pos = b % a.pos_div;
     if (lane == 0) {
+      const int64_t seq = a.seq_offset + b / a.pos_div;
+      const int pos = b % a.pos_div;
       fr.p_row = b;
       fr.p_stat = b;
       fr.q_row = -1;
@@ -327,246 +415,212 @@ __device__ void decide(const Args& a, int b, float* sM, double* sS, int* sArg) {
       fr.odd = ky_uniform_odd(a.seed, (uint32_t)seq, (uint32_t)pos, KY_STREAM_DRAFT, a.step);
       if (a.stoch) {
         fr.skip = 0;
-        fr.Mp = sM[0];
-        fr.Sp = sS[0];
+        fr.Mp = rs[0].M;
+        fr.Sp = rs[0].S;
       } else {
         fr.skip = 1;
         fr.Mp = 0.0f;
         fr.Sp = 1.0;
-        a.out_tokens[b] = sArg[0];
+        a.out_tokens[b] = rs[0].arg;
         if (a.out_probs) a.out_probs[b] = 1.0f;
       }
       a.final_rows[b] = fr;
     }
-  } else {
-    const uint32_t seq = (uint32_t)(a.seq_offset + b);
-    const int32_t* x = a.draft_tokens + (int64_t)b * k;
-    int first_reject = k;
-    for (int j0 = 0; j0 < k; j0 += 32) {
-      const int j = j0 + lane;
-      bool acc = true;
-      if (j < k) {
-        const int xj = x[j];
-        const bool ok = xj >= 0 && xj < a.V;
-        if (!ok) kyro::dev::flag(a.status, KYRO_DEV_BAD_TOKEN);
-        if (a.stoch) {
-          float p = 0.0f, q = 0.0f;
-          if (ok) {
-            const int cx = xj / kChunk;
-            const int64_t pr = (int64_t)b * a.R + j, qr = (int64_t)b * a.R + k + 1 + j;
-            p = KY_FMUL(__ldcg(&a.ex[pr]),
-                        ky_chunk_scale(__ldcg(&a.stats[pr * a.nchunks + cx].m), sM[j], sS[j]));
-            q = KY_FMUL(__ldcg(&a.ex[qr]),
-                        ky_chunk_scale(__ldcg(&a.stats[qr * a.nchunks + cx].m), sM[k + 1 + j],
-                                       sS[k + 1 + j]));
-          }
-          if (a.out_probs) {
-            a.out_probs[((int64_t)b * k + j) * 2 + 0] = p;
-            a.out_probs[((int64_t)b * k + j) * 2 + 1] = q;
-          }
-          const uint32_t odd = ky_uniform_odd(a.seed, seq, (uint32_t)j, KY_STREAM_ACCEPT, a.step);
-          acc = ok && ky_accept(odd, p, q);
-        } else {
-          acc = ok && sArg[j] == xj;
-        }
-      }
-      const unsigned rej = __ballot_sync(0xffffffffu, !acc);
-      if (first_reject == k && rej) first_reject = j0 + __ffs(rej) - 1;
-    }
-    const int aa = first_reject;
-    if (lane == 0) {
-      int32_t* toks = a.out_tokens + (int64_t)b * (k + 1);
-      for (int j = 0; j <= k; ++j) toks[j] = j < aa ? x[j] : -1;
-      a.out_accept_len[b] = aa;
-      fr.p_row = (int64_t)b * (k + 1) + aa;
-      fr.p_stat = (int64_t)b * a.R + aa;
-      fr.out_index = b * (k + 1) + aa;
-      fr.odd = ky_uniform_odd(a.seed, seq, (uint32_t)aa, KY_STREAM_RESAMPLE, a.step);
+    return;
+  }
+  const uint32_t seq = (uint32_t)(a.seq_offset + b);
+  const int32_t* x = a.draft_tokens + (int64_t)b * k;
+  const int64_t r0 = (int64_t)b * a.R;
+  // lane j runs accept test j (in rounds of 32)
+  int first_reject = k;
+  for (int j0 = 0; j0 < k; j0 += 32) {
+    const int j = j0 + lane;
+    bool acc = true;
+    if (j < k) {
+      const int xj = x[j];
+      const bool ok = xj >= 0 && xj < a.V;
+      if (!ok) kyro::dev::flag(a.status, KYRO_DEV_BAD_TOKEN);
       if (a.stoch) {
-        fr.skip = 0;
-        fr.Mp = sM[aa];
-        fr.Sp = sS[aa];
-        if (aa < k) {
-          fr.q_row = (int64_t)b * k + aa;
-          fr.q_stat = (int64_t)b * a.R + k + 1 + aa;
-          fr.Mq = sM[k + 1 + aa];
-          fr.Sq = sS[k + 1 + aa];
-        } else {
-          fr.q_row = -1;
-          fr.q_stat = -1;
-          fr.Mq = 0.0f;
-          fr.Sq = 1.0;
+        float p = 0.0f, q = 0.0f;
+        if (ok) {
+          const int cx = xj / kChunk;
+          p = KY_FMUL(a.ex[r0 + j],
+                      ky_chunk_scale(a.stats[(r0 + j) * a.nchunks + cx].m, rs[j].M, rs[j].S));
+          q = KY_FMUL(a.ex[r0 + k + 1 + j],
+                      ky_chunk_scale(a.stats[(r0 + k + 1 + j) * a.nchunks + cx].m,
+                                     rs[k + 1 + j].M, rs[k + 1 + j].S));
         }
-        a.out_num_tokens[b] = aa + 1;
+        if (a.out_probs) {
+          a.out_probs[((int64_t)b * k + j) * 2 + 0] = p;
+          a.out_probs[((int64_t)b * k + j) * 2 + 1] = q;
+        }
+        const uint32_t odd = ky_uniform_odd(a.seed, seq, (uint32_t)j, KY_STREAM_ACCEPT, a.step);
+        acc = ok && ky_accept(odd, p, q);
       } else {
-        fr.skip = 1;
-        fr.q_row = fr.q_stat = -1;
-        fr.Mp = fr.Mq = 0.0f;
-        fr.Sp = fr.Sq = 1.0;
-        if (aa == k && a.greedy_ref && k > 0) {
-          a.out_num_tokens[b] = k;
-        } else {
-          toks[aa] = sArg[aa];
-          a.out_num_tokens[b] = aa + 1;
-        }
-      }
-      a.final_rows[b] = fr;
-    }
-  }
-  if (lane == 0) {
-    __threadfence();
-    atomicExch(&a.ready[b], 1u);
-  }
-  __syncwarp();
-}
-
-// ------------------------------------------------------------ units
-
-template <bool VEC, bool STOCH>
-__device__ void stats_unit(const Args& a, int b, int local, float (&v)[kPerLane], float* sM,
-                           double* sS, int* sArg) {
-  const int lane = threadIdx.x & 31;
-  const int r = local / a.nchunks, c = local % a.nchunks;
-  const int64_t srow = (int64_t)b * a.R + r;
-  float m = -INFINITY;
-  int arg = 0x7fffffff;
-  if (STOCH) {
-    if (a.inv_t != 1.0f) {
-#pragma unroll
-      for (int i = 0; i < kPerLane; ++i) v[i] = KY_FMUL(v[i], a.inv_t);
-    }
-    // independent partial maxima and sums: max and integer addition give the
-    // same result in any order, and short chains keep the pipes busy
-    float m8[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) m8[j] = v[j];
-#pragma unroll
-    for (int i = 8; i < kPerLane; ++i) m8[i & 7] = fmaxf(m8[i & 7], v[i]);
-    m = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-              fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
-    m = kyro::dev::warp_max(m);
-    unsigned long long e4[4] = {0ull, 0ull, 0ull, 0ull};
-#pragma unroll
-    for (int i = 0; i < kPerLane; ++i) e4[i & 3] += ky_fix40_exp(KY_FSUB(v[i], m));
-    unsigned long long E = (e4[0] + e4[1]) + (e4[2] + e4[3]);
-    E = warp_sum(E);
-    if (lane == 0) {
-      ChunkStat s;
-      s.m = m;
-      s.arg = 0;
-      s.E = E;
-      a.stats[srow * a.nchunks + c] = s;
-      const int x = draft_token_of_row(a, b, r);
-      if (x >= (int64_t)c * kChunk && x < (int64_t)(c + 1) * kChunk && x < a.V) {
-        const float* rowp = stats_row_ptr(a, b, r);
-        a.ex[srow] = ky_exp(KY_FSUB(KY_FMUL(__ldg(rowp + x), a.inv_t), m));
+        acc = ok && rs[j].arg == xj;
       }
     }
+    const unsigned rej = __ballot_sync(0xffffffffu, !acc);
+    if (first_reject == k && rej) first_reject = j0 + __ffs(rej) - 1;
+  }
+  const int aa = first_reject;
+  if (lane != 0) return;
+  int32_t* toks = a.out_tokens + (int64_t)b * (k + 1);
+  for (int j = 0; j <= k; ++j) toks[j] = j < aa ? x[j] : -1;
+  a.out_accept_len[b] = aa;
+  fr.p_row = (int64_t)b * (k + 1) + aa;
+  fr.p_stat = r0 + aa;
+  fr.out_index = b * (k + 1) + aa;
+  fr.odd = ky_uniform_odd(a.seed, seq, (uint32_t)aa, KY_STREAM_RESAMPLE, a.step);
+  if (a.stoch) {
+    fr.skip = 0;
+    fr.Mp = rs[aa].M;
+    fr.Sp = rs[aa].S;
+    if (aa < k) {
+      fr.q_row = (int64_t)b * k + aa;
+      fr.q_stat = r0 + k + 1 + aa;
+      fr.Mq = rs[k + 1 + aa].M;
+      fr.Sq = rs[k + 1 + aa].S;
+    } else {
+      fr.q_row = -1;
+      fr.q_stat = -1;
+      fr.Mq = 0.0f;
+      fr.Sq = 1.0;
+    }
+    a.out_num_tokens[b] = aa + 1;
   } else {
-    const int64_t base = (int64_t)c * kChunk;
-#pragma unroll
-    for (int i = 0; i < kVecPerLane; ++i)
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        if (v[4 * i + j] > m) {
-          m = v[4 * i + j];
-          arg = (int)(base + (i * 32 + lane) * 4 + j);
-        }
-    kyro::dev::warp_argmax(m, arg);
-    if (lane == 0) {
-      ChunkStat s;
-      s.m = m;
-      s.arg = arg;
-      s.E = 0;
-      a.stats[srow * a.nchunks + c] = s;
+    fr.skip = 1;
+    fr.q_row = fr.q_stat = -1;
+    fr.Mp = fr.Mq = 0.0f;
+    fr.Sp = fr.Sq = 1.0;
+    if (aa == k && a.greedy_ref && k > 0) {
+      a.out_num_tokens[b] = k;
+    } else {
+      toks[aa] = rs[aa].arg;
+      a.out_num_tokens[b] = aa + 1;
     }
   }
-  // the warp that completes the sequence's last stats unit decides it
-  uint32_t last = 0;
-  if (lane == 0) {
-    __threadfence();
-    last = atomicAdd(&a.cnt_a[b], 1u) == (uint32_t)(a.ua - 1);
-  }
-  last = __shfl_sync(0xffffffffu, last, 0);
-  if (last) {
-    __threadfence();
-    decide(a, b, sM, sS, sArg);
-  }
+  a.final_rows[b] = fr;
 }
 
-// fix62 weights of 16 logits of one final unit
+// ------------------------------------------------------------ final kernel
+
+// Per-chunk factors of a final row: g62 = g_c * 2^62 of p (and of q for
+// the residual) at chunk c, and the chunk maxima.
+struct FinalScale {
+  float mp, gp62, mq, gq62;
+};
+
+__device__ __forceinline__ FinalScale final_scale(const Args& a, const FinalRow& fr, bool residual,
+                                                  int c) {
+  FinalScale s;
+  s.mp = a.stats[fr.p_stat * a.nchunks + c].m;
+  s.gp62 = ky_scale62(ky_chunk_scale(s.mp, fr.Mp, fr.Sp));
+  s.mq = 0.0f;
+  s.gq62 = 0.0f;
+  if (residual) {
+    s.mq = a.stats[fr.q_stat * a.nchunks + c].m;
+    s.gq62 = ky_scale62(ky_chunk_scale(s.mq, fr.Mq, fr.Sq));
+  }
+  return s;
+}
+
+// fix62 weights of the 4 logits at e0..e0+3 of a final row (entries past V
+// weigh 0).
 template <bool VEC>
-__device__ __forceinline__ void final_weights(const Args& a, const FinalRow& fr, bool residual,
-                                              int sub, unsigned long long (&w)[kSubVec * 4]) {
+__device__ __forceinline__ void weights4(const Args& a, const FinalRow& fr, bool residual,
+                                         const FinalScale& s, int64_t e0,
+                                         unsigned long long (&w)[4]) {
   const float* prow = a.plog + fr.p_row * a.V;
-  const int c = sub / kSubsPerChunk;
-  const ChunkStat* sp = a.stats + fr.p_stat * a.nchunks;
-  const float mp = __ldcg(&sp[c].m);
-  const float gp62 = ky_scale62(ky_chunk_scale(mp, fr.Mp, fr.Sp));
-  float zp[kSubVec * 4];
-  load_sub<VEC>(prow, a.V, sub, zp);
-  if (a.inv_t != 1.0f) {
+  float zp[4], zq[4];
+  if (VEC) {
+    float4 f = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+    if (e0 < a.V) f = __ldcg(reinterpret_cast<const float4*>(prow + e0));
+    zp[0] = f.x;
+    zp[1] = f.y;
+    zp[2] = f.z;
+    zp[3] = f.w;
+  } else {
 #pragma unroll
-    for (int i = 0; i < kSubVec * 4; ++i) zp[i] = KY_FMUL(zp[i], a.inv_t);
+    for (int j = 0; j < 4; ++j) zp[j] = (e0 + j < a.V) ? __ldcg(prow + e0 + j) : -INFINITY;
   }
   if (residual) {
     const float* qrow = a.qlog + fr.q_row * a.V;
-    const ChunkStat* sq = a.stats + fr.q_stat * a.nchunks;
-    const float mq = __ldcg(&sq[c].m);
-    const float gq62 = ky_scale62(ky_chunk_scale(mq, fr.Mq, fr.Sq));
-    float zq[kSubVec * 4];
-    load_sub<VEC>(qrow, a.V, sub, zq);
-    if (a.inv_t != 1.0f) {
+    if (VEC) {
+      float4 f = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+      if (e0 < a.V) f = __ldcg(reinterpret_cast<const float4*>(qrow + e0));
+      zq[0] = f.x;
+      zq[1] = f.y;
+      zq[2] = f.z;
+      zq[3] = f.w;
+    } else {
 #pragma unroll
-      for (int i = 0; i < kSubVec * 4; ++i) zq[i] = KY_FMUL(zq[i], a.inv_t);
+      for (int j = 0; j < 4; ++j) zq[j] = (e0 + j < a.V) ? __ldcg(qrow + e0 + j) : -INFINITY;
     }
+  }
 #pragma unroll
-    for (int i = 0; i < kSubVec * 4; ++i)
-      w[i] = ky_weight_residual(ky_exp(KY_FSUB(zp[i], mp)), gp62, ky_exp(KY_FSUB(zq[i], mq)),
-                                gq62);
-  } else {
-#pragma unroll
-    for (int i = 0; i < kSubVec * 4; ++i) w[i] = ky_weight_p(ky_exp(KY_FSUB(zp[i], mp)), gp62);
+  for (int j = 0; j < 4; ++j) {
+    float sp = zp[j];
+    if (a.inv_t != 1.0f) sp = KY_FMUL(sp, a.inv_t);
+    const float ep = ky_exp(KY_FSUB(sp, s.mp));
+    if (residual) {
+      float sq = zq[j];
+      if (a.inv_t != 1.0f) sq = KY_FMUL(sq, a.inv_t);
+      w[j] = ky_weight_residual(ep, s.gp62, ky_exp(KY_FSUB(sq, s.mq)), s.gq62);
+    } else {
+      w[j] = ky_weight_p(ep, s.gp62);
+    }
   }
 }
 
-// Locate the cut point of a final row once all its unit sums are in W.
+// Sum of the fix62 weights of chunk c of a final row over the whole warp.
 template <bool VEC>
-__device__ void final_search(const Args& a, int b, const FinalRow& fr) {
+__device__ __forceinline__ unsigned long long chunk_weight_sum(const Args& a, const FinalRow& fr,
+                                                               bool residual, int c) {
   const int lane = threadIdx.x & 31;
-  unsigned long long* W = a.W + (int64_t)b * a.nsub;
+  const FinalScale s = final_scale(a, fr, residual, c);
+  unsigned long long t = 0;
+#pragma unroll
+  for (int i = 0; i < kVec; ++i) {
+    unsigned long long w[4];
+    weights4<VEC>(a, fr, residual, s, (int64_t)c * kChunk + (i * 32 + lane) * 4, w);
+    t += (w[0] + w[1]) + (w[2] + w[3]);
+  }
+  return warp_sum(t);
+}
+
+// Locate the cut point of final row b once all its chunk sums are in W.
+template <bool VEC>
+__device__ __noinline__ void final_search(const Args& a, int b, const FinalRow& fr) {
+  const int lane = threadIdx.x & 31;
+  unsigned long long* W = a.W + (int64_t)b * a.nchunks;
   bool residual = fr.q_row >= 0;
   unsigned long long tot = 0;
-  for (int s = lane; s < a.nsub; s += 32) tot += __ldcg(&W[s]);
+  for (int s = lane; s < a.nchunks; s += 32) tot += __ldcg(&W[s]);
   tot = warp_sum(tot);
   if (residual && tot == 0) {
     // the residual has no mass: sample from p instead
     residual = false;
-    for (int s = 0; s < a.nsub; ++s) {
-      unsigned long long w[kSubVec * 4];
-      final_weights<VEC>(a, fr, false, s, w);
-      unsigned long long t = 0;
-#pragma unroll
-      for (int i = 0; i < kSubVec * 4; ++i) t += w[i];
-      t = warp_sum(t);
+    for (int s = 0; s < a.nchunks; ++s) {
+      const unsigned long long t = chunk_weight_sum<VEC>(a, fr, false, s);
       if (lane == 0) W[s] = t;
     }
     __syncwarp();
     __threadfence_block();
     tot = 0;
-    for (int s = lane; s < a.nsub; s += 32) tot += __ldcg(&W[s]);
+    for (int s = lane; s < a.nchunks; s += 32) tot += __ldcg(&W[s]);
     tot = warp_sum(tot);
   }
   int token = (int)a.V - 1;
   if (tot != 0) {
     unsigned long long T = ky_cdf_threshold(fr.odd, tot);
-    // find the unit whose inclusive prefix first reaches T
+    // find the chunk whose inclusive prefix first reaches T
     int sub = -1;
     unsigned long long base = 0;
-    for (int s0 = 0; s0 < a.nsub && sub < 0; s0 += 32) {
-      const unsigned long long ws = (s0 + lane < a.nsub) ? __ldcg(&W[s0 + lane]) : 0ull;
+    for (int s0 = 0; s0 < a.nchunks && sub < 0; s0 += 32) {
+      const unsigned long long ws = (s0 + lane < a.nchunks) ? __ldcg(&W[s0 + lane]) : 0ull;
       const unsigned long long inc = base + warp_inclusive(ws);
-      const unsigned hit = __ballot_sync(0xffffffffu, inc >= T && s0 + lane < a.nsub);
+      const unsigned hit = __ballot_sync(0xffffffffu, inc >= T && s0 + lane < a.nchunks);
       if (hit) {
         const int l = __ffs(hit) - 1;
         sub = s0 + l;
@@ -577,20 +631,21 @@ __device__ void final_search(const Args& a, int b, const FinalRow& fr) {
       }
     }
     if (sub >= 0) {
-      unsigned long long w[kSubVec * 4];
-      final_weights<VEC>(a, fr, residual, sub, w);
+      // scan the chunk: float4 groups in index order, lanes in order within
+      const FinalScale sc = final_scale(a, fr, residual, sub);
       unsigned long long cbase = 0;
       int found = -1;
-#pragma unroll
-      for (int i = 0; i < kSubVec; ++i) {
-        const unsigned long long s4 = w[4 * i] + w[4 * i + 1] + w[4 * i + 2] + w[4 * i + 3];
+      for (int i = 0; i < kVec; ++i) {
+        unsigned long long w[4];
+        weights4<VEC>(a, fr, residual, sc, (int64_t)sub * kChunk + (i * 32 + lane) * 4, w);
+        const unsigned long long s4 = (w[0] + w[1]) + (w[2] + w[3]);
         const unsigned long long inc = warp_inclusive(s4);
         unsigned long long C = cbase + inc - s4;
         int mine = -1;
         if (C < T && C + s4 >= T) {
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            C += w[4 * i + j];
+            C += w[j];
             if (mine < 0 && C >= T) mine = j;
           }
         }
@@ -598,7 +653,7 @@ __device__ void final_search(const Args& a, int b, const FinalRow& fr) {
         if (found < 0 && hit) {
           const int l = __ffs(hit) - 1;
           const int jj = __shfl_sync(0xffffffffu, mine, l);
-          found = sub * kSub + (i * 32 + l) * 4 + jj;
+          found = sub * kChunk + (i * 32 + l) * 4 + jj;
         }
         cbase += __shfl_sync(0xffffffffu, inc, 31);
       }
@@ -609,7 +664,7 @@ __device__ void final_search(const Args& a, int b, const FinalRow& fr) {
     a.out_tokens[fr.out_index] = token;
     if (a.sample && a.out_probs) {
       const int c = token / kChunk;
-      const float mp = __ldcg(&a.stats[fr.p_stat * a.nchunks + c].m);
+      const float mp = a.stats[fr.p_stat * a.nchunks + c].m;
       a.out_probs[fr.out_index] =
           KY_FMUL(ky_exp(KY_FSUB(KY_FMUL(__ldg(a.plog + fr.p_row * a.V + token), a.inv_t), mp)),
                   ky_chunk_scale(mp, fr.Mp, fr.Sp));
@@ -617,121 +672,25 @@ __device__ void final_search(const Args& a, int b, const FinalRow& fr) {
   }
 }
 
+// Weight sums: one warp per chunk of each sequence's chosen row.  Sequences
+// run in reverse, so the rows the stats kernel read last (the ones most
+// likely still in L2) come first.
 template <bool VEC>
-__device__ void final_unit(const Args& a, int b, int sub) {
-  const int lane = threadIdx.x & 31;
-  // wait (bounded) until the decide step of sequence b has published
-  uint32_t ok = 1;
-  if (lane == 0) {
-    volatile uint32_t* flag = a.ready + b;
-    if (*flag == 0) {
-      const long long t0 = clock64();
-      while (*flag == 0) {
-        __nanosleep(200);
-        if (clock64() - t0 > kyro::dev::kWaitBudgetCycles) {
-          ok = 0;
-          break;
-        }
-      }
-    }
-    __threadfence();
-  }
-  ok = __shfl_sync(0xffffffffu, ok, 0);
-  if (!ok) {
-    if (lane == 0) kyro::dev::flag(a.status, KYRO_DEV_WAIT_TIMEOUT);
-    return;
-  }
-  FinalRow fr;
-  {
-    const FinalRow* src = a.final_rows + b;
-    fr.p_row = __ldcg(&src->p_row);
-    fr.q_row = __ldcg(&src->q_row);
-    fr.p_stat = __ldcg(&src->p_stat);
-    fr.q_stat = __ldcg(&src->q_stat);
-    fr.Mp = __ldcg(&src->Mp);
-    fr.Mq = __ldcg(&src->Mq);
-    fr.Sp = __ldcg(&src->Sp);
-    fr.Sq = __ldcg(&src->Sq);
-    fr.odd = __ldcg(&src->odd);
-    fr.out_index = __ldcg(&src->out_index);
-    fr.skip = __ldcg(&src->skip);
-  }
+__global__ void __launch_bounds__(kThreads) accept_final_kernel(Args a) {
+  __shared__ Args sa;
+  if (threadIdx.x == 0) sa = a;
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int per_seq = (a.nchunks + kWarps - 1) / kWarps;
+  const int y = (int)(blockIdx.x / (unsigned)per_seq);
+  const int b = a.B - 1 - y;
+  const int c = (int)(blockIdx.x - (unsigned)y * per_seq) * kWarps + warp;
+  if (c >= a.nchunks) return;
+  FinalRow fr = a.final_rows[b];
   if (fr.skip) return;
-  unsigned long long w[kSubVec * 4];
-  final_weights<VEC>(a, fr, fr.q_row >= 0, sub, w);
-  unsigned long long t = 0;
-#pragma unroll
-  for (int i = 0; i < kSubVec * 4; ++i) t += w[i];
-  t = warp_sum(t);
-  uint32_t last = 0;
-  if (lane == 0) {
-    a.W[(int64_t)b * a.nsub + sub] = t;
-    __threadfence();
-    last = atomicAdd(&a.cnt_c[b], 1u) == (uint32_t)(a.uc - 1);
-  }
-  last = __shfl_sync(0xffffffffu, last, 0);
-  if (last) {
-    __threadfence();
-    final_search<VEC>(a, b, fr);
-  }
-}
-
-// ------------------------------------------------------------ the kernel
-
-struct UnitCursor {
-  long long next, end;
-};
-
-__device__ __forceinline__ long long take_unit(const Args& a, UnitCursor& cur) {
-  const int lane = threadIdx.x & 31;
-  if (cur.next >= cur.end) {
-    long long g = 0;
-    if (lane == 0) g = (long long)atomicAdd(a.queue, (unsigned long long)kBatch);
-    g = __shfl_sync(0xffffffffu, g, 0);
-    cur.next = g;
-    cur.end = g + kBatch;
-  }
-  return cur.next++;
-}
-
-template <bool VEC>
-__device__ __forceinline__ void prefetch(const Args& a, long long u, float (&buf)[kPerLane]) {
-  if (u >= a.total) return;
-  bool is_stats;
-  int seq, local;
-  unit_of(a, u, is_stats, seq, local);
-  if (!is_stats) return;
-  const int r = local / a.nchunks, c = local % a.nchunks;
-  load_chunk<VEC>(stats_row_ptr(a, seq, r), a.V, c, buf);
-}
-
-template <bool VEC, bool STOCH>
-__device__ __forceinline__ void run_unit(const Args& a, long long u, float (&buf)[kPerLane],
-                                         float* sM, double* sS, int* sArg) {
-  bool is_stats;
-  int seq, local;
-  unit_of(a, u, is_stats, seq, local);
-  if (is_stats)
-    stats_unit<VEC, STOCH>(a, seq, local, buf, sM, sS, sArg);
-  else
-    final_unit<VEC>(a, seq, local);
-}
-
-template <bool VEC, bool STOCH>
-__global__ void __launch_bounds__(kThreads, 3) accept_fused_kernel(Args a) {
-  __shared__ float sM_all[kWarps][kMaxRows];
-  __shared__ double sS_all[kWarps][kMaxRows];
-  __shared__ int sArg_all[kWarps][kMaxRows];
-  const int warp = threadIdx.x >> 5;
-  float* sM = sM_all[warp];
-  double* sS = sS_all[warp];
-  int* sArg = sArg_all[warp];
-  UnitCursor cur{0, 0};
-  float buf[kPerLane];
-  for (long long u = take_unit(a, cur); u < a.total; u = take_unit(a, cur)) {
-    prefetch<VEC>(a, u, buf);
-    run_unit<VEC, STOCH>(a, u, buf, sM, sS, sArg);
-  }
+  const unsigned long long t = chunk_weight_sum<VEC>(a, fr, fr.q_row >= 0, c);
+  if (lane == 0) a.W[(int64_t)b * a.nchunks + c] = t;
+  if (warp_last_of(&a.cnt_c[b], (uint32_t)(a.nchunks - 1))) final_search<VEC>(sa, b, fr);
 }
 
 // ------------------------------------------------------------ host side
@@ -743,49 +702,54 @@ bool use_vec(const void* a, const void* b, int64_t V) {
 template <bool VEC, bool STOCH>
 int resident_ctas(int num_sms) {
   int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, accept_fused_kernel<VEC, STOCH>,
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, accept_stats_kernel<VEC, STOCH>,
                                                     kThreads, 0) != cudaSuccess ||
       per_sm < 1)
     per_sm = 1;
   return num_sms * per_sm;
 }
 
-int launch(kyro_ctx* ctx, Args& a, const Workspace& ws, bool vec) {
-  cudaStream_t st = ctx->stream;
-  // the queue, the per-sequence counters and the ready flags start at zero
-  cudaError_t err = cudaMemsetAsync(ws.queue, 0, ws.counter_bytes, st);
-  if (err != cudaSuccess) return kyro::cuda_error(err, "cudaMemsetAsync(sampler counters)");
-  int resident;
-  if (vec && a.stoch)
-    resident = resident_ctas<true, true>(ctx->num_sms);
-  else if (vec)
-    resident = resident_ctas<true, false>(ctx->num_sms);
-  else if (a.stoch)
-    resident = resident_ctas<false, true>(ctx->num_sms);
-  else
-    resident = resident_ctas<false, false>(ctx->num_sms);
-  const long long useful = (a.total + kWarps * kBatch - 1) / (kWarps * kBatch);
-  const int grid = (int)(useful < resident ? useful : resident);
-  if (vec && a.stoch)
-    accept_fused_kernel<true, true><<<grid, kThreads, 0, st>>>(a);
-  else if (vec)
-    accept_fused_kernel<true, false><<<grid, kThreads, 0, st>>>(a);
-  else if (a.stoch)
-    accept_fused_kernel<false, true><<<grid, kThreads, 0, st>>>(a);
-  else
-    accept_fused_kernel<false, false><<<grid, kThreads, 0, st>>>(a);
-  return kyro::check_launch("accept_fused_kernel");
+template <bool VEC, bool STOCH>
+int launch_t(kyro_ctx* ctx, const Args& a) {
+  const long long need = ((long long)a.units + kWarps - 1) / kWarps;
+  const int resident = resident_ctas<VEC, STOCH>(ctx->num_sms);
+  const int grid = (int)(need < resident ? need : resident);
+  accept_stats_kernel<VEC, STOCH><<<grid, kThreads, 0, ctx->stream>>>(a);
+  KY_TRY(kyro::check_launch("accept_stats_kernel"));
+  const int dwarps = a.R < kDecideWarps ? a.R : kDecideWarps;
+  accept_decide_kernel<<<a.B, dwarps * 32, 0, ctx->stream>>>(a);
+  KY_TRY(kyro::check_launch("accept_decide_kernel"));
+  if (!STOCH) return KYRO_OK;  // greedy: the decide step wrote every token
+  const unsigned nfinal = (unsigned)a.B * (unsigned)((a.nchunks + kWarps - 1) / kWarps);
+  accept_final_kernel<VEC><<<nfinal, kThreads, 0, ctx->stream>>>(a);
+  return kyro::check_launch("accept_final_kernel");
 }
 
-void fill_workspace_args(Args& a, const Workspace& ws) {
+int launch(kyro_ctx* ctx, Args& a, const Workspace& ws, bool vec) {
+  // the last-arriver counters start at zero
+  if (a.stoch) {
+    cudaError_t err = cudaMemsetAsync(ws.cnt_c, 0, ws.counter_bytes, ctx->stream);
+    if (err != cudaSuccess) return kyro::cuda_error(err, "cudaMemsetAsync(sampler counters)");
+  }
+  if (vec && a.stoch) return launch_t<true, true>(ctx, a);
+  if (vec) return launch_t<true, false>(ctx, a);
+  if (a.stoch) return launch_t<false, true>(ctx, a);
+  return launch_t<false, false>(ctx, a);
+}
+
+void fill_common(Args& a, const Workspace& ws, int64_t V, int B, int R) {
+  a.V = V;
+  a.B = B;
+  a.R = R;
+  a.nchunks = (int)((V + kChunk - 1) / kChunk);
+  a.div_chunks = make_fastdiv((uint32_t)a.nchunks);
+  a.div_rows = make_fastdiv((uint32_t)R);
+  a.units = (uint32_t)((int64_t)B * R * a.nchunks);
   a.stats = ws.stats;
   a.ex = ws.ex;
   a.final_rows = ws.final_rows;
   a.W = ws.W;
-  a.cnt_a = ws.cnt_a;
   a.cnt_c = ws.cnt_c;
-  a.ready = ws.ready;
-  a.queue = ws.queue;
 }
 
 }  // namespace
@@ -797,8 +761,7 @@ size_t kyro_spec_accept_workspace_size(const kyro_accept_params* p) {
   const bool stoch = p->mode == KYRO_ACCEPT_STOCHASTIC && p->temperature > 0.0f;
   const int64_t R = stoch ? 2 * (int64_t)p->num_draft + 1 : (int64_t)p->num_draft + 1;
   const int64_t nchunks = (p->vocab + kChunk - 1) / kChunk;
-  const int64_t nsub = (p->vocab + kSub - 1) / kSub;
-  return carve(nullptr, p->batch, R, nchunks, nsub).bytes;
+  return carve(nullptr, p->batch, R, nchunks).bytes;
 }
 
 int kyro_spec_accept(kyro_ctx* ctx, const kyro_accept_params* p, const float* target_logits,
@@ -824,26 +787,21 @@ int kyro_spec_accept(kyro_ctx* ctx, const kyro_accept_params* p, const float* ta
   KY_REQUIRE(out_accept_len && out_tokens && out_num_tokens,
              "kyro_spec_accept: an output pointer is NULL");
   const int R = stoch ? 2 * k + 1 : k + 1;
-  const int nchunks = (int)((V + kChunk - 1) / kChunk);
-  const int nsub = (int)((V + kSub - 1) / kSub);
-  KY_REQUIRE((int64_t)B * R * nchunks < (1ll << 40), "kyro_spec_accept: batch too large");
-  const size_t need = carve(nullptr, B, R, nchunks, nsub).bytes;
+  const int64_t nchunks = (V + kChunk - 1) / kChunk;
+  KY_REQUIRE((int64_t)B * R * nchunks < (1ll << 31), "kyro_spec_accept: batch too large");
+  const size_t need = carve(nullptr, B, R, nchunks).bytes;
   if (workspace_bytes < need || !workspace)
     return kyro::set_error(KYRO_ERR_WORKSPACE, "kyro_spec_accept: workspace %zu < %zu bytes",
                            workspace_bytes, need);
   KY_REQUIRE((uintptr_t)workspace % 256 == 0,
              "kyro_spec_accept: workspace must be 256-byte aligned");
-  Workspace ws = carve(workspace, B, R, nchunks, nsub);
+  Workspace ws = carve(workspace, B, R, nchunks);
   Args a = {};
+  fill_common(a, ws, V, B, R);
   a.plog = target_logits;
   a.qlog = stoch ? draft_logits : nullptr;
   a.draft_tokens = draft_tokens;
-  a.B = B;
   a.k = k;
-  a.R = R;
-  a.V = V;
-  a.nchunks = nchunks;
-  a.nsub = nsub;
   a.inv_t = stoch ? ky_inv_temperature(p->temperature) : 1.0f;
   a.stoch = stoch;
   a.greedy_ref = p->mode == KYRO_ACCEPT_GREEDY_REF;
@@ -856,10 +814,6 @@ int kyro_spec_accept(kyro_ctx* ctx, const kyro_accept_params* p, const float* ta
   a.out_tokens = out_tokens;
   a.out_num_tokens = out_num_tokens;
   a.out_probs = stoch ? out_probs : nullptr;
-  fill_workspace_args(a, ws);
-  a.ua = R * nchunks;
-  a.uc = stoch ? nsub : 0;
-  a.total = (long long)B * (a.ua + a.uc);
   a.status = ctx->d_status;
   return launch(ctx, a, ws, use_vec(target_logits, a.qlog, V));
 }
@@ -868,8 +822,7 @@ size_t kyro_sample_workspace_size(const kyro_sample_params* p) {
   if (!p || p->batch < 0 || p->num_pos < 0 || p->vocab <= 0) return 0;
   const int64_t rows = (int64_t)p->batch * p->num_pos;
   const int64_t nchunks = (p->vocab + kChunk - 1) / kChunk;
-  const int64_t nsub = (p->vocab + kSub - 1) / kSub;
-  return carve(nullptr, rows, 1, nchunks, nsub).bytes;
+  return carve(nullptr, rows, 1, nchunks).bytes;
 }
 
 int kyro_sample_tokens(kyro_ctx* ctx, const kyro_sample_params* p, const float* logits,
@@ -883,29 +836,24 @@ int kyro_sample_tokens(kyro_ctx* ctx, const kyro_sample_params* p, const float* 
              "kyro_sample_tokens: vocab = %d", p->vocab);
   const int64_t rows = (int64_t)p->batch * p->num_pos;
   if (rows == 0) return KYRO_OK;
-  KY_REQUIRE(rows < (1ll << 30), "kyro_sample_tokens: too many rows");
-  KY_REQUIRE(logits && out_tokens, "kyro_sample_tokens: NULL logits or out_tokens");
   const int64_t V = p->vocab;
-  const int nchunks = (int)((V + kChunk - 1) / kChunk);
-  const int nsub = (int)((V + kSub - 1) / kSub);
-  const size_t need = carve(nullptr, rows, 1, nchunks, nsub).bytes;
+  const int64_t nchunks = (V + kChunk - 1) / kChunk;
+  KY_REQUIRE(rows * nchunks < (1ll << 31), "kyro_sample_tokens: too many rows");
+  KY_REQUIRE(logits && out_tokens, "kyro_sample_tokens: NULL logits or out_tokens");
+  const size_t need = carve(nullptr, rows, 1, nchunks).bytes;
   if (workspace_bytes < need || !workspace)
     return kyro::set_error(KYRO_ERR_WORKSPACE, "kyro_sample_tokens: workspace %zu < %zu bytes",
                            workspace_bytes, need);
   KY_REQUIRE((uintptr_t)workspace % 256 == 0,
              "kyro_sample_tokens: workspace must be 256-byte aligned");
-  Workspace ws = carve(workspace, rows, 1, nchunks, nsub);
+  Workspace ws = carve(workspace, rows, 1, nchunks);
   const bool stoch = p->temperature > 0.0f;
   Args a = {};
+  fill_common(a, ws, V, (int)rows, 1);
   a.plog = logits;
   a.qlog = nullptr;
   a.draft_tokens = nullptr;
-  a.B = (int)rows;
   a.k = 0;
-  a.R = 1;
-  a.V = V;
-  a.nchunks = nchunks;
-  a.nsub = nsub;
   a.inv_t = stoch ? ky_inv_temperature(p->temperature) : 1.0f;
   a.stoch = stoch;
   a.greedy_ref = 0;
@@ -916,10 +864,6 @@ int kyro_sample_tokens(kyro_ctx* ctx, const kyro_sample_params* p, const float* 
   a.seq_offset = p->seq_offset;
   a.out_tokens = out_tokens;
   a.out_probs = out_probs;
-  fill_workspace_args(a, ws);
-  a.ua = nchunks;
-  a.uc = stoch ? nsub : 0;
-  a.total = rows * (long long)(a.ua + a.uc);
   a.status = ctx->d_status;
   return launch(ctx, a, ws, use_vec(logits, nullptr, V));
 }
@@ -933,7 +877,7 @@ int kyro_sample_tokens(kyro_ctx* ctx, const kyro_sample_params* p, const float* 
 // present on every device that loads the library until the process exits.
 // In host code the array's name is only a stand-in, so the device address
 // is looked up once per device with cudaGetSymbolAddress while that device
-// is current, and that address is what the kernel receives.
+// is current, and that address is what the kernels receive.
 
 namespace {
 
