@@ -22,10 +22,12 @@
  *      fitted for this project by iterated weighted least squares on
  *      [-ln2/2, ln2/2] (max relative error 9.4e-8 before rounding).
  *      Inputs below -87 (and NaN) behave as -87; ky_exp(0) == 1 exactly.
- *   3. Exact fixed-point accumulation.  Softmax mass is summed as integers:
- *      fix40(e) = floor(e * 2^40) for e in [0,1] and fix62(w) = floor(w * 2^62)
- *      for w in [0,2).  Integer sums do not depend on the order in which a
- *      kernel adds them, so the inverse-CDF cut point is reproducible.
+ *   3. Fixed summation orders.  A chunk's softmax mass is an fp32 sum in one
+ *      prescribed tree (ky_chunk_sum), and a row's normaliser a double sum
+ *      in one prescribed butterfly, so a kernel that follows the same trees
+ *      gets the same bits.  Inverse-CDF weights are integers,
+ *      fix62(w) = floor(w * 2^62) for w in [0,2), whose sums do not depend
+ *      on the order in which a kernel adds them.
  *   4. The inverse-CDF threshold: with a uniform u = odd * 2^-24 and integer
  *      total mass W, the sampled index is the smallest i whose inclusive
  *      prefix C_i satisfies u*W <= C_i, i.e. C_i >= ceil(odd*W / 2^24).
@@ -213,18 +215,6 @@ KY_HD uint64_t ky_f2u64_rz(float v) {
 #endif
 }
 
-/* floor(e * 2^40) for e in [0, 1]; at most 2^40. */
-KY_HD uint64_t ky_fix40(float e) { return ky_f2u64_rz(KY_FMUL(e, 0x1p40f)); }
-
-/* floor(ky_exp(x) * 2^40), computed as floor(p * 2^(n+40)).  Equal to
- * ky_fix40(ky_exp(x)): the two differ only when ky_exp(x) is subnormal,
- * and then both are 0. */
-KY_HD uint64_t ky_fix40_exp(float x) {
-  uint32_t tb;
-  const float p = ky_exp_core(x, &tb);
-  return ky_f2u64_rz(KY_FMUL(p, ky_pow2_from_t(tb, 40u)));
-}
-
 /* floor(w * 2^62) for w in [0, 2). */
 KY_HD uint64_t ky_fix62(float w) { return ky_f2u64_rz(KY_FMUL(w, 0x1p62f)); }
 
@@ -243,9 +233,12 @@ KY_HD uint64_t ky_cdf_threshold(uint32_t odd, uint64_t W) {
  * without TP), and each shard into chunks of KY_CHUNK consecutive entries
  * starting at the shard start (the last chunk may be short).  With
  * s_i = z_i * inv_t:
- *   m_c = max_{i in c} s_i,  e_i = ky_exp(s_i - m_c),  E_c = sum fix40(e_i)
+ *   m_c = max_{i in c} s_i
+ *   e_i = ky_exp(s_i - m_c) at each of the chunk's KY_CHUNK positions; a
+ *         position past the shard end has s_i = -inf (so e_i = ky_exp(-87))
+ *   E_c = ky_chunk_sum(e_c)                   (fp32, the fixed tree below)
  *   M   = max_c m_c
- *   mass_c = E_c*2^-40 * ky_exp(m_c - M)                    (double)
+ *   mass_c = E_c * ky_exp(m_c - M)            (double)
  *   S_r = butterfly sum of the chunk masses of shard r:
  *           t[l] = sum of mass_c over c = l, l+32, l+64, ... (in that order,
  *                  starting from 0.0), l = 0..31;
@@ -261,12 +254,42 @@ KY_HD uint64_t ky_cdf_threshold(uint32_t odd, uint64_t W) {
  * chunk's statistics need no exchange between warps. */
 #define KY_CHUNK 512
 
+/* fp32 butterfly over 32 partial sums: for off = 16, 8, 4, 2, 1,
+ * t[l] = t[l] + t[l ^ off]; returns t[0] (every entry ends equal, since
+ * fp32 addition commutes). */
+KY_HD float ky_butterfly32f(float t[32]) {
+  for (int off = 16; off > 0; off >>= 1) {
+    float n[32];
+    for (int l = 0; l < 32; ++l) n[l] = KY_FADD(t[l], t[l ^ off]);
+    for (int l = 0; l < 32; ++l) t[l] = n[l];
+  }
+  return t[0];
+}
+
+/* The chunk sum E_c.  Position (i*32 + l)*4 + j of the chunk (i = 0..3,
+ * l = 0..31, j = 0..3) is term i of column j of lane l -- the float4 that
+ * lane l of a warp loads in step i.  Each lane adds its columns' terms in
+ * step order, then its four columns as (a0 + a1) + (a2 + a3), and the 32
+ * lane totals meet in ky_butterfly32f. */
+KY_HD float ky_chunk_sum(const float e[KY_CHUNK]) {
+  float lanes[32];
+  for (int l = 0; l < 32; ++l) {
+    float acc[4];
+    for (int j = 0; j < 4; ++j) {
+      acc[j] = 0.0f;
+      for (int i = 0; i < 4; ++i) acc[j] = KY_FADD(acc[j], e[(i * 32 + l) * 4 + j]);
+    }
+    lanes[l] = KY_FADD(KY_FADD(acc[0], acc[1]), KY_FADD(acc[2], acc[3]));
+  }
+  return ky_butterfly32f(lanes);
+}
+
 /* inv_t for temperature t > 0: (float)(1/(double)t); candle's `tensor / t`
  * (worker.rs:298) is an affine op multiplying by the reciprocal. */
 KY_HD float ky_inv_temperature(float t) { return (float)KY_DDIV(1.0, (double)t); }
 
-KY_HD double ky_chunk_mass(uint64_t E, float m_c, float M) {
-  return KY_DMUL((double)E * 0x1p-40, (double)ky_exp(KY_FSUB(m_c, M)));
+KY_HD double ky_chunk_mass(float E, float m_c, float M) {
+  return KY_DMUL((double)E, (double)ky_exp(KY_FSUB(m_c, M)));
 }
 
 KY_HD float ky_chunk_scale(float m_c, float M, double S) {

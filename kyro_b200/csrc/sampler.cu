@@ -7,16 +7,16 @@
 // to the host.  Everything here stays on the device and is batched.
 //
 // The normaliser contract of kyro_math.h makes every decision reproducible:
-// per-chunk maxima, ky_exp, exact integer (fix40) chunk masses, a fixed
-// butterfly combination in double, and integer (fix62) inverse-CDF weights.
-// Integer sums do not depend on how threads are arranged, so the parallel
-// kernels reproduce the sequential oracle bit for bit.
+// per-chunk maxima, ky_exp, chunk sums in one fixed fp32 tree (the lane
+// layout of a warp that holds the chunk), a fixed butterfly in double, and
+// integer (fix62) inverse-CDF weights.  The kernels follow exactly those
+// trees, so they reproduce the sequential oracle bit for bit.
 //
 // Three launches, none of which waits on another CTA:
 //   accept_stats_kernel   persistent, one warp per 512-entry chunk of every
 //                         row (target and draft), grid-stride.  A lane holds
 //                         16 logits in registers: chunk max (or argmax),
-//                         fix40 chunk mass, and e at the draft token.  Each
+//                         chunk sum, and e at the draft token.  Each
 //                         warp loads its next chunk while it reduces the
 //                         current one.  This kernel reads every logit once
 //                         and carries nearly all of the step's HBM traffic.
@@ -51,9 +51,10 @@ constexpr int kDecideWarps = 8;
 static_assert(kChunk == 512, "the kernels assume 16 logits per lane");
 
 struct ChunkStat {
-  float m;               // chunk max of s = z * inv_t (or of z, greedy)
-  int32_t arg;           // lowest index attaining m (greedy)
-  unsigned long long E;  // sum of fix40(ky_exp(s - m)) over the chunk
+  float m;      // chunk max of s = z * inv_t (or of z, greedy)
+  int32_t arg;  // lowest index attaining m (greedy)
+  float E;      // ky_chunk_sum of ky_exp(s - m) over the chunk
+  float _pad;
 };
 
 struct RowStat {
@@ -201,26 +202,31 @@ __device__ __forceinline__ bool warp_last_of(uint32_t* counter, uint32_t total_m
   return last != 0;
 }
 
-// ky_fix40_exp(x), bit for bit, in fewer instructions.  Scaling every
-// polynomial coefficient by 2^40 scales each round-to-nearest fma result by
-// exactly 2^40 (the values stay far from the subnormal and overflow ranges),
-// so p40 == 2^40 * p; and with t = 1.5*2^23 + n, bits(t) << 23 == n << 23
-// (mod 2^32), so adding it to bits(p40) multiplies by 2^n exactly (x >= -87
-// keeps n >= -126 and the product normal).  The contract's form is
-// floor(p * 2^(n+40)) with the same p and n.
-__device__ __forceinline__ unsigned long long fix40_exp_fast(float x) {
+// ky_exp(x), bit for bit, in fewer instructions.  With t = 1.5*2^23 + n,
+// bits(t) << 23 == n << 23 (mod 2^32), so adding it to the bits of the
+// polynomial value p multiplies p by 2^n exactly whenever p * 2^n is a
+// normal number -- and it always is: the clamp at -87 keeps n >= -126, and
+// n == -126 only for x < -86.989, where r > 0.336 and so p > 1.  The
+// contract's form computes the same product with an fp32 multiply.
+__device__ __forceinline__ float exp_fast(float x) {
   const float xc = fmaxf(x, -87.0f);
   const float t = __fmaf_rn(xc, KY_LOG2E, KY_RND_MAGIC);
   const float nf = __fsub_rn(t, KY_RND_MAGIC);
   const float r = __fmaf_rn(-nf, KY_LN2, xc);
-  float p = KY_EXP_C5 * 0x1p40f;
-  p = __fmaf_rn(p, r, KY_EXP_C4 * 0x1p40f);
-  p = __fmaf_rn(p, r, KY_EXP_C3 * 0x1p40f);
-  p = __fmaf_rn(p, r, KY_EXP_C2 * 0x1p40f);
-  p = __fmaf_rn(p, r, KY_EXP_C1 * 0x1p40f);
-  p = __fmaf_rn(p, r, KY_EXP_C0 * 0x1p40f);
-  const uint32_t bits = __float_as_uint(p) + (__float_as_uint(t) << 23);
-  return __float2ull_rz(__uint_as_float(bits));
+  float p = KY_EXP_C5;
+  p = __fmaf_rn(p, r, KY_EXP_C4);
+  p = __fmaf_rn(p, r, KY_EXP_C3);
+  p = __fmaf_rn(p, r, KY_EXP_C2);
+  p = __fmaf_rn(p, r, KY_EXP_C1);
+  p = __fmaf_rn(p, r, KY_EXP_C0);
+  return __uint_as_float(__float_as_uint(p) + (__float_as_uint(t) << 23));
+}
+
+// fp32 warp butterfly (the lanes' part of ky_chunk_sum)
+__device__ __forceinline__ float warp_butterfly_f(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
 }
 
 __device__ __forceinline__ const float* stats_row_ptr(const Args& a, int b, int r) {
@@ -292,12 +298,15 @@ __device__ __forceinline__ void reduce_slice(const Args& a, Slice& s) {
 #pragma unroll
     for (int i = 4; i < kPerLane; ++i) m4[i & 3] = fmaxf(m4[i & 3], s.v[i]);
     const float m = kyro::dev::warp_max(fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])));
-    unsigned long long e4[4] = {0ull, 0ull, 0ull, 0ull};
+    // ky_chunk_sum's tree: column j of this lane sums steps i = 0..3 in
+    // order, then (a0 + a1) + (a2 + a3), then the lane butterfly
+    float e4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-    for (int i = 0; i < kPerLane; ++i) e4[i & 3] += fix40_exp_fast(KY_FSUB(s.v[i], m));
+    for (int i = 0; i < kPerLane; ++i) e4[i & 3] = __fadd_rn(e4[i & 3], exp_fast(KY_FSUB(s.v[i], m)));
     st.m = m;
     st.arg = 0;
-    st.E = warp_sum((e4[0] + e4[1]) + (e4[2] + e4[3]));
+    st.E = warp_butterfly_f(__fadd_rn(__fadd_rn(e4[0], e4[1]), __fadd_rn(e4[2], e4[3])));
+    st._pad = 0.0f;
     // e at the draft token, by the lane that holds it (s.v holds z * inv_t)
     const int64_t xo = (int64_t)s.x - base;
     if (s.x >= 0 && s.x < a.V && xo >= 0 && xo < kChunk && lane == (int)((xo >> 2) & 31)) {
@@ -306,7 +315,7 @@ __device__ __forceinline__ void reduce_slice(const Args& a, Slice& s) {
 #pragma unroll
       for (int i = 1; i < kPerLane; ++i)
         if (i == q) z = s.v[i];
-      a.ex[s.srow] = ky_exp(KY_FSUB(z, m));
+      a.ex[s.srow] = exp_fast(KY_FSUB(z, m));
     }
   } else {
     float m = -INFINITY;
@@ -320,7 +329,8 @@ __device__ __forceinline__ void reduce_slice(const Args& a, Slice& s) {
     kyro::dev::warp_argmax(m, arg);
     st.m = m;
     st.arg = arg;
-    st.E = 0;
+    st.E = 0.0f;
+    st._pad = 0.0f;
   }
   if (lane == 0) a.stats[(int64_t)s.srow * a.nchunks + s.c] = st;
 }
@@ -351,37 +361,93 @@ __global__ void __launch_bounds__(kThreads, kStatsMinCtas) accept_stats_kernel(A
 
 // ------------------------------------------------------------ decide kernel
 
-// Row normaliser (or argmax) of stats row srow, by one warp.
+// Row normaliser (or argmax) of stats row srow, by one warp.  Lane l visits
+// chunks l, l+32, l+64, ... in that order (the contract's butterfly order);
+// loads go out eight at a time so that a pass costs one memory round trip
+// per 256 chunks.
 __device__ __forceinline__ RowStat row_stat(const Args& a, int64_t srow) {
   const int lane = threadIdx.x & 31;
   const ChunkStat* st = a.stats + srow * a.nchunks;
+  const int nc = a.nchunks;
   RowStat rs;
   rs.arg = 0;
   rs.S = 0.0;
   if (a.stoch) {
     float M = -INFINITY;
-    for (int c = lane; c < a.nchunks; c += 32) M = fmaxf(M, st[c].m);
+    for (int g = 0; g < nc; g += 256) {
+      float mm[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int c = g + j * 32 + lane;
+        mm[j] = c < nc ? st[c].m : -INFINITY;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) M = fmaxf(M, mm[j]);
+    }
     M = kyro::dev::warp_max(M);
     double t = 0.0;
-    for (int c = lane; c < a.nchunks; c += 32) t = KY_DADD(t, ky_chunk_mass(st[c].E, st[c].m, M));
+    for (int g = 0; g < nc; g += 256) {
+      float mm[8], ee[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int c = g + j * 32 + lane;
+        mm[j] = c < nc ? st[c].m : 0.0f;
+        ee[j] = c < nc ? st[c].E : 0.0f;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (g + j * 32 + lane < nc) t = KY_DADD(t, ky_chunk_mass(ee[j], mm[j], M));
+    }
     rs.M = M;
     rs.S = warp_butterfly(t);
   } else {
     float best = -INFINITY;
     int bi = 0x7fffffff;
-    for (int c = lane; c < a.nchunks; c += 32) {
-      const float m = st[c].m;
-      const int ai = st[c].arg;
-      if (m > best || (m == best && ai < bi)) {
-        best = m;
-        bi = ai;
+    for (int g = 0; g < nc; g += 256) {
+      float mm[8];
+      int aa[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int c = g + j * 32 + lane;
+        mm[j] = c < nc ? st[c].m : -INFINITY;
+        aa[j] = c < nc ? st[c].arg : 0x7fffffff;
       }
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (mm[j] > best || (mm[j] == best && aa[j] < bi)) {
+          best = mm[j];
+          bi = aa[j];
+        }
     }
     kyro::dev::warp_argmax(best, bi);
     rs.M = best;
     rs.arg = bi == 0x7fffffff ? 0 : bi;
   }
   return rs;
+}
+
+// What accept test j reads besides the row statistics: the draft token, e at
+// it in the target and the draft row, and those rows' chunk maxima there.
+struct TestInputs {
+  int x;
+  float ep, eq, mp, mq;
+};
+
+__device__ __forceinline__ TestInputs load_test(const Args& a, int b, int j) {
+  TestInputs t;
+  t.x = -1;
+  t.ep = t.eq = t.mp = t.mq = 0.0f;
+  if (j >= a.k) return t;
+  const int64_t r0 = (int64_t)b * a.R;
+  t.x = a.draft_tokens[(int64_t)b * a.k + j];
+  if (a.stoch && t.x >= 0 && t.x < a.V) {
+    const int cx = t.x / kChunk;
+    t.ep = a.ex[r0 + j];
+    t.eq = a.ex[r0 + a.k + 1 + j];
+    t.mp = a.stats[(r0 + j) * a.nchunks + cx].m;
+    t.mq = a.stats[(r0 + a.k + 1 + j) * a.nchunks + cx].m;
+  }
+  return t;
 }
 
 // One CTA per sequence (per row for the sampler): the warps compute the row
@@ -391,13 +457,20 @@ __global__ void __launch_bounds__(kDecideWarps * 32) accept_decide_kernel(Args a
   __shared__ RowStat rs[kMaxRows];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   const int b = blockIdx.x;
+  const int k = a.k;
+  // warp 0 fetches the test inputs (lane j: tests j and j + 32) before it
+  // joins the row statistics
+  TestInputs t0, t1;
+  if (warp == 0 && !a.sample) {
+    t0 = load_test(a, b, lane);
+    t1 = load_test(a, b, lane + 32);
+  }
   for (int r = warp; r < a.R; r += nwarps) {
     const RowStat s = row_stat(a, (int64_t)b * a.R + r);
     if (lane == 0) rs[r] = s;
   }
   __syncthreads();
   if (warp != 0) return;
-  const int k = a.k;
   FinalRow fr;
   fr._pad = 0;
   if (a.sample) {
@@ -429,26 +502,21 @@ __global__ void __launch_bounds__(kDecideWarps * 32) accept_decide_kernel(Args a
     return;
   }
   const uint32_t seq = (uint32_t)(a.seq_offset + b);
-  const int32_t* x = a.draft_tokens + (int64_t)b * k;
   const int64_t r0 = (int64_t)b * a.R;
   // lane j runs accept test j (in rounds of 32)
   int first_reject = k;
   for (int j0 = 0; j0 < k; j0 += 32) {
     const int j = j0 + lane;
+    const TestInputs& t = j0 == 0 ? t0 : t1;
     bool acc = true;
     if (j < k) {
-      const int xj = x[j];
-      const bool ok = xj >= 0 && xj < a.V;
+      const bool ok = t.x >= 0 && t.x < a.V;
       if (!ok) kyro::dev::flag(a.status, KYRO_DEV_BAD_TOKEN);
       if (a.stoch) {
         float p = 0.0f, q = 0.0f;
         if (ok) {
-          const int cx = xj / kChunk;
-          p = KY_FMUL(a.ex[r0 + j],
-                      ky_chunk_scale(a.stats[(r0 + j) * a.nchunks + cx].m, rs[j].M, rs[j].S));
-          q = KY_FMUL(a.ex[r0 + k + 1 + j],
-                      ky_chunk_scale(a.stats[(r0 + k + 1 + j) * a.nchunks + cx].m,
-                                     rs[k + 1 + j].M, rs[k + 1 + j].S));
+          p = KY_FMUL(t.ep, ky_chunk_scale(t.mp, rs[j].M, rs[j].S));
+          q = KY_FMUL(t.eq, ky_chunk_scale(t.mq, rs[k + 1 + j].M, rs[k + 1 + j].S));
         }
         if (a.out_probs) {
           a.out_probs[((int64_t)b * k + j) * 2 + 0] = p;
@@ -457,16 +525,21 @@ __global__ void __launch_bounds__(kDecideWarps * 32) accept_decide_kernel(Args a
         const uint32_t odd = ky_uniform_odd(a.seed, seq, (uint32_t)j, KY_STREAM_ACCEPT, a.step);
         acc = ok && ky_accept(odd, p, q);
       } else {
-        acc = ok && rs[j].arg == xj;
+        acc = ok && rs[j].arg == t.x;
       }
     }
     const unsigned rej = __ballot_sync(0xffffffffu, !acc);
     if (first_reject == k && rej) first_reject = j0 + __ffs(rej) - 1;
   }
   const int aa = first_reject;
-  if (lane != 0) return;
+  // lane j writes token slot j (and 32 + j): the accepted drafts, then -1
   int32_t* toks = a.out_tokens + (int64_t)b * (k + 1);
-  for (int j = 0; j <= k; ++j) toks[j] = j < aa ? x[j] : -1;
+  for (int j = lane; j <= k; j += 32) {
+    const TestInputs& t = j < 32 ? t0 : t1;
+    toks[j] = j < aa ? t.x : -1;
+  }
+  __syncwarp();
+  if (lane != 0) return;
   a.out_accept_len[b] = aa;
   fr.p_row = (int64_t)b * (k + 1) + aa;
   fr.p_stat = r0 + aa;
@@ -506,70 +579,70 @@ __global__ void __launch_bounds__(kDecideWarps * 32) accept_decide_kernel(Args a
 // ------------------------------------------------------------ final kernel
 
 // Per-chunk factors of a final row: g62 = g_c * 2^62 of p (and of q for
-// the residual) at chunk c, and the chunk maxima.
+// the residual) at chunk c, from the chunk maxima mp, mq.
 struct FinalScale {
   float mp, gp62, mq, gq62;
 };
 
-__device__ __forceinline__ FinalScale final_scale(const Args& a, const FinalRow& fr, bool residual,
-                                                  int c) {
+__device__ __forceinline__ FinalScale final_scale(const FinalRow& fr, bool residual, float mp,
+                                                  float mq) {
   FinalScale s;
-  s.mp = a.stats[fr.p_stat * a.nchunks + c].m;
-  s.gp62 = ky_scale62(ky_chunk_scale(s.mp, fr.Mp, fr.Sp));
-  s.mq = 0.0f;
-  s.gq62 = 0.0f;
-  if (residual) {
-    s.mq = a.stats[fr.q_stat * a.nchunks + c].m;
-    s.gq62 = ky_scale62(ky_chunk_scale(s.mq, fr.Mq, fr.Sq));
-  }
+  s.mp = mp;
+  s.gp62 = ky_scale62(ky_chunk_scale(mp, fr.Mp, fr.Sp));
+  s.mq = mq;
+  s.gq62 = residual ? ky_scale62(ky_chunk_scale(mq, fr.Mq, fr.Sq)) : 0.0f;
   return s;
 }
 
-// fix62 weights of the 4 logits at e0..e0+3 of a final row (entries past V
-// weigh 0).
+// 4 logits at e0..e0+3 of a row (entries past V read as -inf)
 template <bool VEC>
-__device__ __forceinline__ void weights4(const Args& a, const FinalRow& fr, bool residual,
-                                         const FinalScale& s, int64_t e0,
-                                         unsigned long long (&w)[4]) {
-  const float* prow = a.plog + fr.p_row * a.V;
-  float zp[4], zq[4];
+__device__ __forceinline__ float4 load4(const float* __restrict__ row, int64_t e0, int64_t V) {
   if (VEC) {
     float4 f = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-    if (e0 < a.V) f = __ldcg(reinterpret_cast<const float4*>(prow + e0));
-    zp[0] = f.x;
-    zp[1] = f.y;
-    zp[2] = f.z;
-    zp[3] = f.w;
-  } else {
-#pragma unroll
-    for (int j = 0; j < 4; ++j) zp[j] = (e0 + j < a.V) ? __ldcg(prow + e0 + j) : -INFINITY;
+    if (e0 < V) f = __ldcg(reinterpret_cast<const float4*>(row + e0));
+    return f;
   }
-  if (residual) {
-    const float* qrow = a.qlog + fr.q_row * a.V;
-    if (VEC) {
-      float4 f = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-      if (e0 < a.V) f = __ldcg(reinterpret_cast<const float4*>(qrow + e0));
-      zq[0] = f.x;
-      zq[1] = f.y;
-      zq[2] = f.z;
-      zq[3] = f.w;
-    } else {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) zq[j] = (e0 + j < a.V) ? __ldcg(qrow + e0 + j) : -INFINITY;
-    }
-  }
+  float4 f;
+  f.x = e0 + 0 < V ? __ldcg(row + e0 + 0) : -INFINITY;
+  f.y = e0 + 1 < V ? __ldcg(row + e0 + 1) : -INFINITY;
+  f.z = e0 + 2 < V ? __ldcg(row + e0 + 2) : -INFINITY;
+  f.w = e0 + 3 < V ? __ldcg(row + e0 + 3) : -INFINITY;
+  return f;
+}
+
+// fix62 weights of 4 logits of a final row: residual max(p - q, 0) or p.
+__device__ __forceinline__ void weights_of4(float inv_t, bool residual, const FinalScale& s,
+                                            float4 zp, float4 zq, unsigned long long (&w)[4]) {
+  const float p4[4] = {zp.x, zp.y, zp.z, zp.w};
+  const float q4[4] = {zq.x, zq.y, zq.z, zq.w};
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    float sp = zp[j];
-    if (a.inv_t != 1.0f) sp = KY_FMUL(sp, a.inv_t);
-    const float ep = ky_exp(KY_FSUB(sp, s.mp));
+    float sp = p4[j];
+    if (inv_t != 1.0f) sp = KY_FMUL(sp, inv_t);
+    const float ep = exp_fast(KY_FSUB(sp, s.mp));
     if (residual) {
-      float sq = zq[j];
-      if (a.inv_t != 1.0f) sq = KY_FMUL(sq, a.inv_t);
-      w[j] = ky_weight_residual(ep, s.gp62, ky_exp(KY_FSUB(sq, s.mq)), s.gq62);
+      float sq = q4[j];
+      if (inv_t != 1.0f) sq = KY_FMUL(sq, inv_t);
+      w[j] = ky_weight_residual(ep, s.gp62, exp_fast(KY_FSUB(sq, s.mq)), s.gq62);
     } else {
       w[j] = ky_weight_p(ep, s.gp62);
     }
+  }
+}
+
+// The 16 logits a lane owns in chunk c of the final row (p and, for the
+// residual, q), all loads issued together.
+template <bool VEC>
+__device__ __forceinline__ void load_final_chunk(const Args& a, const FinalRow& fr, bool residual,
+                                                 int c, float4 (&zp)[kVec], float4 (&zq)[kVec]) {
+  const int lane = threadIdx.x & 31;
+  const float* prow = a.plog + fr.p_row * a.V;
+  const float* qrow = residual ? a.qlog + fr.q_row * a.V : prow;
+#pragma unroll
+  for (int i = 0; i < kVec; ++i) {
+    const int64_t e0 = (int64_t)c * kChunk + (i * 32 + lane) * 4;
+    zp[i] = load4<VEC>(prow, e0, a.V);
+    zq[i] = residual ? load4<VEC>(qrow, e0, a.V) : zp[i];
   }
 }
 
@@ -577,13 +650,16 @@ __device__ __forceinline__ void weights4(const Args& a, const FinalRow& fr, bool
 template <bool VEC>
 __device__ __forceinline__ unsigned long long chunk_weight_sum(const Args& a, const FinalRow& fr,
                                                                bool residual, int c) {
-  const int lane = threadIdx.x & 31;
-  const FinalScale s = final_scale(a, fr, residual, c);
+  float4 zp[kVec], zq[kVec];
+  load_final_chunk<VEC>(a, fr, residual, c, zp, zq);
+  const float mp = a.stats[fr.p_stat * a.nchunks + c].m;
+  const float mq = residual ? a.stats[fr.q_stat * a.nchunks + c].m : 0.0f;
+  const FinalScale s = final_scale(fr, residual, mp, mq);
   unsigned long long t = 0;
 #pragma unroll
   for (int i = 0; i < kVec; ++i) {
     unsigned long long w[4];
-    weights4<VEC>(a, fr, residual, s, (int64_t)c * kChunk + (i * 32 + lane) * 4, w);
+    weights_of4(a.inv_t, residual, s, zp[i], zq[i], w);
     t += (w[0] + w[1]) + (w[2] + w[3]);
   }
   return warp_sum(t);
@@ -591,24 +667,34 @@ __device__ __forceinline__ unsigned long long chunk_weight_sum(const Args& a, co
 
 // Locate the cut point of final row b once all its chunk sums are in W.
 template <bool VEC>
-__device__ __noinline__ void final_search(const Args& a, int b, const FinalRow& fr) {
+__device__ __forceinline__ void final_search(const Args& a, int b, const FinalRow& fr) {
   const int lane = threadIdx.x & 31;
-  unsigned long long* W = a.W + (int64_t)b * a.nchunks;
+  const int nc = a.nchunks;
+  unsigned long long* W = a.W + (int64_t)b * nc;
   bool residual = fr.q_row >= 0;
   unsigned long long tot = 0;
-  for (int s = lane; s < a.nchunks; s += 32) tot += __ldcg(&W[s]);
+  for (int g = 0; g < nc; g += 256) {
+    unsigned long long ww[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = g + j * 32 + lane;
+      ww[j] = c < nc ? __ldcg(&W[c]) : 0ull;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) tot += ww[j];
+  }
   tot = warp_sum(tot);
   if (residual && tot == 0) {
     // the residual has no mass: sample from p instead
     residual = false;
-    for (int s = 0; s < a.nchunks; ++s) {
-      const unsigned long long t = chunk_weight_sum<VEC>(a, fr, false, s);
-      if (lane == 0) W[s] = t;
+    for (int c = 0; c < nc; ++c) {
+      const unsigned long long t = chunk_weight_sum<VEC>(a, fr, false, c);
+      if (lane == 0) W[c] = t;
     }
     __syncwarp();
     __threadfence_block();
     tot = 0;
-    for (int s = lane; s < a.nchunks; s += 32) tot += __ldcg(&W[s]);
+    for (int c = lane; c < nc; c += 32) tot += __ldcg(&W[c]);
     tot = warp_sum(tot);
   }
   int token = (int)a.V - 1;
@@ -617,10 +703,10 @@ __device__ __noinline__ void final_search(const Args& a, int b, const FinalRow& 
     // find the chunk whose inclusive prefix first reaches T
     int sub = -1;
     unsigned long long base = 0;
-    for (int s0 = 0; s0 < a.nchunks && sub < 0; s0 += 32) {
-      const unsigned long long ws = (s0 + lane < a.nchunks) ? __ldcg(&W[s0 + lane]) : 0ull;
+    for (int s0 = 0; s0 < nc && sub < 0; s0 += 32) {
+      const unsigned long long ws = (s0 + lane < nc) ? __ldcg(&W[s0 + lane]) : 0ull;
       const unsigned long long inc = base + warp_inclusive(ws);
-      const unsigned hit = __ballot_sync(0xffffffffu, inc >= T && s0 + lane < a.nchunks);
+      const unsigned hit = __ballot_sync(0xffffffffu, inc >= T && s0 + lane < nc);
       if (hit) {
         const int l = __ffs(hit) - 1;
         sub = s0 + l;
@@ -632,12 +718,17 @@ __device__ __noinline__ void final_search(const Args& a, int b, const FinalRow& 
     }
     if (sub >= 0) {
       // scan the chunk: float4 groups in index order, lanes in order within
-      const FinalScale sc = final_scale(a, fr, residual, sub);
+      float4 zp[kVec], zq[kVec];
+      load_final_chunk<VEC>(a, fr, residual, sub, zp, zq);
+      const float mp = a.stats[fr.p_stat * nc + sub].m;
+      const float mq = residual ? a.stats[fr.q_stat * nc + sub].m : 0.0f;
+      const FinalScale sc = final_scale(fr, residual, mp, mq);
       unsigned long long cbase = 0;
       int found = -1;
+#pragma unroll
       for (int i = 0; i < kVec; ++i) {
         unsigned long long w[4];
-        weights4<VEC>(a, fr, residual, sc, (int64_t)sub * kChunk + (i * 32 + lane) * 4, w);
+        weights_of4(a.inv_t, residual, sc, zp[i], zq[i], w);
         const unsigned long long s4 = (w[0] + w[1]) + (w[2] + w[3]);
         const unsigned long long inc = warp_inclusive(s4);
         unsigned long long C = cbase + inc - s4;
@@ -664,7 +755,7 @@ __device__ __noinline__ void final_search(const Args& a, int b, const FinalRow& 
     a.out_tokens[fr.out_index] = token;
     if (a.sample && a.out_probs) {
       const int c = token / kChunk;
-      const float mp = a.stats[fr.p_stat * a.nchunks + c].m;
+      const float mp = a.stats[fr.p_stat * nc + c].m;
       a.out_probs[fr.out_index] =
           KY_FMUL(ky_exp(KY_FSUB(KY_FMUL(__ldg(a.plog + fr.p_row * a.V + token), a.inv_t), mp)),
                   ky_chunk_scale(mp, fr.Mp, fr.Sp));
@@ -677,20 +768,17 @@ __device__ __noinline__ void final_search(const Args& a, int b, const FinalRow& 
 // likely still in L2) come first.
 template <bool VEC>
 __global__ void __launch_bounds__(kThreads) accept_final_kernel(Args a) {
-  __shared__ Args sa;
-  if (threadIdx.x == 0) sa = a;
-  __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int per_seq = (a.nchunks + kWarps - 1) / kWarps;
   const int y = (int)(blockIdx.x / (unsigned)per_seq);
   const int b = a.B - 1 - y;
   const int c = (int)(blockIdx.x - (unsigned)y * per_seq) * kWarps + warp;
   if (c >= a.nchunks) return;
-  FinalRow fr = a.final_rows[b];
+  const FinalRow fr = a.final_rows[b];
   if (fr.skip) return;
   const unsigned long long t = chunk_weight_sum<VEC>(a, fr, fr.q_row >= 0, c);
   if (lane == 0) a.W[(int64_t)b * a.nchunks + c] = t;
-  if (warp_last_of(&a.cnt_c[b], (uint32_t)(a.nchunks - 1))) final_search<VEC>(sa, b, fr);
+  if (warp_last_of(&a.cnt_c[b], (uint32_t)(a.nchunks - 1))) final_search<VEC>(a, b, fr);
 }
 
 // ------------------------------------------------------------ host side

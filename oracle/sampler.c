@@ -65,7 +65,7 @@ static void rowstat_init(ko_rowstat* st, const float* row, int32_t vocab, int32_
   st->m = (float*)malloc(sizeof(float) * (size_t)nc);
   st->g = (float*)malloc(sizeof(float) * (size_t)nc);
   st->g62 = (float*)malloc(sizeof(float) * (size_t)nc);
-  uint64_t* E = (uint64_t*)calloc((size_t)nc, sizeof(uint64_t));
+  float* E = (float*)malloc(sizeof(float) * (size_t)nc);
   /* chunk maxima */
   for (int32_t c = 0; c < nc; ++c) st->m[c] = -INFINITY;
   for (int32_t i = 0; i < vocab; ++i) {
@@ -73,11 +73,18 @@ static void rowstat_init(ko_rowstat* st, const float* row, int32_t vocab, int32_
     int32_t c = chunk_of(st, i);
     if (s > st->m[c]) st->m[c] = s;
   }
-  /* chunk masses */
-  for (int32_t i = 0; i < vocab; ++i) {
-    float s = KY_FMUL(row[i], inv_t);
-    int32_t c = chunk_of(st, i);
-    E[c] += ky_fix40_exp(KY_FSUB(s, st->m[c]));
+  /* chunk sums: every position of a chunk, -inf past the shard end */
+  for (int32_t r = 0; r < num_shards; ++r) {
+    for (int32_t lc = 0; lc < st->chunks_per_shard; ++lc) {
+      int32_t gc = r * st->chunks_per_shard + lc;
+      float e[KY_CHUNK];
+      for (int32_t p = 0; p < KY_CHUNK; ++p) {
+        int32_t local = lc * KY_CHUNK + p;
+        float s = local < st->shard_len ? KY_FMUL(row[r * st->shard_len + local], inv_t) : -INFINITY;
+        e[p] = ky_exp(KY_FSUB(s, st->m[gc]));
+      }
+      E[gc] = ky_chunk_sum(e);
+    }
   }
   float M = -INFINITY;
   for (int32_t c = 0; c < nc; ++c)
