@@ -229,6 +229,73 @@ __device__ __forceinline__ float warp_butterfly_f(float v) {
   return v;
 }
 
+// ---- packed pairs of fp32 (sm_100 .f32x2): each half rounds exactly as
+// the scalar round-to-nearest operation on it, so a pair computes the same
+// bits as two scalar evaluations with half the instructions.
+typedef unsigned long long f2_t;  // (lo, hi)
+
+__device__ __forceinline__ f2_t f2_pack(float lo, float hi) {
+  f2_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+
+__device__ __forceinline__ void f2_unpack(f2_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+
+__device__ __forceinline__ f2_t f2_fma(f2_t a, f2_t b, f2_t c) {
+  f2_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+__device__ __forceinline__ f2_t f2_add(f2_t a, f2_t b) {
+  f2_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+__device__ __forceinline__ f2_t f2_sub(f2_t a, f2_t b) {
+  f2_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+__device__ __forceinline__ f2_t f2_mul(f2_t a, f2_t b) {
+  f2_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// max of three (NaN inputs are ignored, as by fmaxf)
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// exp_fast of both halves.  fma(-nf, ln2, x) is written fma(nf, -ln2, x):
+// the product is exact inside the fma, so the sign can move to ln2.
+__device__ __forceinline__ f2_t exp_pair(f2_t x) {
+  float xl, xh;
+  f2_unpack(x, xl, xh);
+  const f2_t xc = f2_pack(fmaxf(xl, -87.0f), fmaxf(xh, -87.0f));
+  const f2_t t = f2_fma(xc, f2_pack(KY_LOG2E, KY_LOG2E), f2_pack(KY_RND_MAGIC, KY_RND_MAGIC));
+  const f2_t nf = f2_sub(t, f2_pack(KY_RND_MAGIC, KY_RND_MAGIC));
+  const f2_t r = f2_fma(nf, f2_pack(-KY_LN2, -KY_LN2), xc);
+  f2_t p = f2_fma(f2_pack(KY_EXP_C5, KY_EXP_C5), r, f2_pack(KY_EXP_C4, KY_EXP_C4));
+  p = f2_fma(p, r, f2_pack(KY_EXP_C3, KY_EXP_C3));
+  p = f2_fma(p, r, f2_pack(KY_EXP_C2, KY_EXP_C2));
+  p = f2_fma(p, r, f2_pack(KY_EXP_C1, KY_EXP_C1));
+  p = f2_fma(p, r, f2_pack(KY_EXP_C0, KY_EXP_C0));
+  float pl, ph, tl, th;
+  f2_unpack(p, pl, ph);
+  f2_unpack(t, tl, th);
+  return f2_pack(__uint_as_float(__float_as_uint(pl) + (__float_as_uint(tl) << 23)),
+                 __uint_as_float(__float_as_uint(ph) + (__float_as_uint(th) << 23)));
+}
+
 __device__ __forceinline__ const float* stats_row_ptr(const Args& a, int b, int r) {
   if (r <= a.k) return a.plog + ((int64_t)b * (a.k + 1) + r) * a.V;
   return a.qlog + ((int64_t)b * a.k + (r - a.k - 1)) * a.V;
@@ -264,6 +331,18 @@ __device__ __forceinline__ void load_slice(const Args& a, uint32_t u, Slice& s) 
   s.x = draft_token_of_row(a, b, r);
   const float* row = stats_row_ptr(a, b, r);
   const int64_t base = (int64_t)c * kChunk;
+  if (VEC && base + kChunk <= a.V) {
+    const float4* src = reinterpret_cast<const float4*>(row + base) + lane;
+#pragma unroll
+    for (int i = 0; i < kVec; ++i) {
+      const float4 f = __ldcg(src + i * 32);
+      s.v[4 * i + 0] = f.x;
+      s.v[4 * i + 1] = f.y;
+      s.v[4 * i + 2] = f.z;
+      s.v[4 * i + 3] = f.w;
+    }
+    return;
+  }
 #pragma unroll
   for (int i = 0; i < kVec; ++i) {
     const int64_t e0 = base + (i * 32 + lane) * 4;
@@ -288,24 +367,43 @@ __device__ __forceinline__ void reduce_slice(const Args& a, Slice& s) {
   const int64_t base = (int64_t)s.c * kChunk;
   ChunkStat st;
   if (STOCH) {
-    if (a.inv_t != 1.0f) {
+    // columns (0,1) and (2,3) of each float4 as packed pairs
+    f2_t z[2 * kVec];
 #pragma unroll
-      for (int i = 0; i < kPerLane; ++i) s.v[i] = KY_FMUL(s.v[i], a.inv_t);
+    for (int i = 0; i < kVec; ++i) {
+      z[2 * i] = f2_pack(s.v[4 * i], s.v[4 * i + 1]);
+      z[2 * i + 1] = f2_pack(s.v[4 * i + 2], s.v[4 * i + 3]);
     }
-    // independent partial maxima and sums: max and integer addition give
-    // the same result in any order, and short chains keep the pipes busy
-    float m4[4] = {s.v[0], s.v[1], s.v[2], s.v[3]};
+    if (a.inv_t != 1.0f) {
+      const f2_t it = f2_pack(a.inv_t, a.inv_t);
 #pragma unroll
-    for (int i = 4; i < kPerLane; ++i) m4[i & 3] = fmaxf(m4[i & 3], s.v[i]);
-    const float m = kyro::dev::warp_max(fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])));
+      for (int i = 0; i < 2 * kVec; ++i) z[i] = f2_mul(z[i], it);
+#pragma unroll
+      for (int i = 0; i < kVec; ++i) {
+        f2_unpack(z[2 * i], s.v[4 * i], s.v[4 * i + 1]);
+        f2_unpack(z[2 * i + 1], s.v[4 * i + 2], s.v[4 * i + 3]);
+      }
+    }
+    // the max is order-free: a tree of three-input maxima
+    const float* v = s.v;
+    const float m01 = max3(max3(v[0], v[1], v[2]), max3(v[3], v[4], v[5]), v[6]);
+    const float m02 = max3(max3(v[7], v[8], v[9]), max3(v[10], v[11], v[12]), v[13]);
+    const float m = kyro::dev::warp_max(max3(m01, m02, max3(v[14], v[15], -INFINITY)));
     // ky_chunk_sum's tree: column j of this lane sums steps i = 0..3 in
     // order, then (a0 + a1) + (a2 + a3), then the lane butterfly
-    float e4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    const f2_t m2 = f2_pack(m, m);
+    f2_t acc01 = f2_pack(0.0f, 0.0f), acc23 = f2_pack(0.0f, 0.0f);
 #pragma unroll
-    for (int i = 0; i < kPerLane; ++i) e4[i & 3] = __fadd_rn(e4[i & 3], exp_fast(KY_FSUB(s.v[i], m)));
+    for (int i = 0; i < kVec; ++i) {
+      acc01 = f2_add(acc01, exp_pair(f2_sub(z[2 * i], m2)));
+      acc23 = f2_add(acc23, exp_pair(f2_sub(z[2 * i + 1], m2)));
+    }
+    float a0, a1, a2, a3;
+    f2_unpack(acc01, a0, a1);
+    f2_unpack(acc23, a2, a3);
     st.m = m;
     st.arg = 0;
-    st.E = warp_butterfly_f(__fadd_rn(__fadd_rn(e4[0], e4[1]), __fadd_rn(e4[2], e4[3])));
+    st.E = warp_butterfly_f(__fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3)));
     st._pad = 0.0f;
     // e at the draft token, by the lane that holds it (s.v holds z * inv_t)
     const int64_t xo = (int64_t)s.x - base;
@@ -611,21 +709,35 @@ __device__ __forceinline__ float4 load4(const float* __restrict__ row, int64_t e
 }
 
 // fix62 weights of 4 logits of a final row: residual max(p - q, 0) or p.
+// Residual: each element's p and q exps form one packed pair; from p
+// alone, neighbouring elements pair up.
 __device__ __forceinline__ void weights_of4(float inv_t, bool residual, const FinalScale& s,
                                             float4 zp, float4 zq, unsigned long long (&w)[4]) {
   const float p4[4] = {zp.x, zp.y, zp.z, zp.w};
   const float q4[4] = {zq.x, zq.y, zq.z, zq.w};
+  if (residual) {
+    const f2_t mm = f2_pack(s.mp, s.mq);
+    const f2_t gg = f2_pack(s.gp62, s.gq62);
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    float sp = p4[j];
-    if (inv_t != 1.0f) sp = KY_FMUL(sp, inv_t);
-    const float ep = exp_fast(KY_FSUB(sp, s.mp));
-    if (residual) {
-      float sq = q4[j];
-      if (inv_t != 1.0f) sq = KY_FMUL(sq, inv_t);
-      w[j] = ky_weight_residual(ep, s.gp62, exp_fast(KY_FSUB(sq, s.mq)), s.gq62);
-    } else {
-      w[j] = ky_weight_p(ep, s.gp62);
+    for (int j = 0; j < 4; ++j) {
+      f2_t z = f2_pack(p4[j], q4[j]);
+      if (inv_t != 1.0f) z = f2_mul(z, f2_pack(inv_t, inv_t));
+      float wp, wq;
+      f2_unpack(f2_mul(exp_pair(f2_sub(z, mm)), gg), wp, wq);
+      const float d = __fsub_rn(wp, wq);
+      w[j] = d > 0.0f ? __float2ull_rz(d) : 0ull;
+    }
+  } else {
+    const f2_t mm = f2_pack(s.mp, s.mp);
+    const f2_t gg = f2_pack(s.gp62, s.gp62);
+#pragma unroll
+    for (int j = 0; j < 4; j += 2) {
+      f2_t z = f2_pack(p4[j], p4[j + 1]);
+      if (inv_t != 1.0f) z = f2_mul(z, f2_pack(inv_t, inv_t));
+      float w0, w1;
+      f2_unpack(f2_mul(exp_pair(f2_sub(z, mm)), gg), w0, w1);
+      w[j] = __float2ull_rz(w0);
+      w[j + 1] = __float2ull_rz(w1);
     }
   }
 }
