@@ -46,7 +46,9 @@ constexpr int kStatsMinCtas = 8;     // resident CTAs per SM the registers allow
 constexpr int kMaxChunks = 1024;     // V <= 524288
 constexpr int kMaxDraft = 64;
 constexpr int kMaxRows = 2 * kMaxDraft + 1;
-constexpr int kDecideWarps = 8;
+constexpr int kDecideWarps = 16;
+constexpr int kFinalPerWarp = 4;   // chunks per warp in the final kernel
+constexpr int kFinalPerCta = kWarps * kFinalPerWarp;
 
 static_assert(kChunk == 512, "the kernels assume 16 logits per lane");
 
@@ -127,7 +129,7 @@ struct Args {
 
 __host__ __device__ inline size_t align_up(size_t x) { return (x + 255) & ~size_t(255); }
 
-// Workspace: the counters first (zeroed before every launch), then the rest.
+// Workspace layout.  cnt_c is zeroed by the decide kernel of each call.
 struct Workspace {
   uint32_t* cnt_c;
   size_t counter_bytes;
@@ -159,15 +161,6 @@ Workspace carve(void* base, int64_t B, int64_t R, int64_t nchunks) {
 
 // ------------------------------------------------------------ primitives
 
-__device__ __forceinline__ uint32_t atomic_add_acq_rel(uint32_t* p, uint32_t v) {
-  uint32_t old;
-  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;"
-               : "=r"(old)
-               : "l"(p), "r"(v)
-               : "memory");
-  return old;
-}
-
 __device__ __forceinline__ unsigned long long warp_sum(unsigned long long v) {
   return kyro::dev::warp_sum_u64(v);
 }
@@ -187,19 +180,6 @@ __device__ __forceinline__ unsigned long long warp_inclusive(unsigned long long 
     if (lane >= o) v += t;
   }
   return v;
-}
-
-// Lane 0 counts this warp's contribution (release: lane 0's earlier writes
-// become visible first; acquire: the other contributors' writes are visible
-// afterwards).  True in every lane of the warp that made the count reach
-// `total_minus_one + 1`.
-__device__ __forceinline__ bool warp_last_of(uint32_t* counter, uint32_t total_minus_one) {
-  const int lane = threadIdx.x & 31;
-  uint32_t last = 0;
-  if (lane == 0) last = atomic_add_acq_rel(counter, 1u) == total_minus_one;
-  last = __shfl_sync(0xffffffffu, last, 0);
-  __syncwarp();
-  return last != 0;
 }
 
 // ky_exp(x), bit for bit, in fewer instructions.  With t = 1.5*2^23 + n,
@@ -273,6 +253,18 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
   return d;
+}
+
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialization may start before its predecessor ends; grid_dependency_wait
+// blocks until the predecessor grid has completed and its writes are
+// visible, and allow_dependents lets the next kernel begin launching.
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+__device__ __forceinline__ void allow_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 // exp_fast of both halves.  fma(-nf, ln2, x) is written fma(nf, -ln2, x):
@@ -438,6 +430,7 @@ __device__ __forceinline__ void reduce_slice(const Args& a, Slice& s) {
 // warp loads unit i+1 before it reduces unit i.
 template <bool VEC, bool STOCH>
 __global__ void __launch_bounds__(kThreads, kStatsMinCtas) accept_stats_kernel(Args a) {
+  allow_dependents();
   const uint32_t stride = gridDim.x * kWarps;
   uint32_t u = blockIdx.x * kWarps + (threadIdx.x >> 5);
   if (u >= a.units) return;
@@ -556,6 +549,9 @@ __global__ void __launch_bounds__(kDecideWarps * 32) accept_decide_kernel(Args a
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   const int b = blockIdx.x;
   const int k = a.k;
+  grid_dependency_wait();  // the chunk statistics are complete
+  allow_dependents();
+  if (threadIdx.x == 0) a.cnt_c[b] = 0;  // the final kernel's last-arriver count
   // warp 0 fetches the test inputs (lane j: tests j and j + 32) before it
   // joins the row statistics
   TestInputs t0, t1;
@@ -875,22 +871,37 @@ __device__ __forceinline__ void final_search(const Args& a, int b, const FinalRo
   }
 }
 
-// Weight sums: one warp per chunk of each sequence's chosen row.  Sequences
-// run in reverse, so the rows the stats kernel read last (the ones most
-// likely still in L2) come first.
+// Weight sums: a CTA covers kFinalPerCta chunks of one sequence's chosen
+// row, warp w the chunks w, w + 4, ... of them (neighbouring warps read
+// neighbouring chunks).  Sequences run in reverse, so the rows the stats
+// kernel read last (the ones most likely still in L2) come first.  The last
+// CTA of a row to finish locates the cut point.
 template <bool VEC>
 __global__ void __launch_bounds__(kThreads) accept_final_kernel(Args a) {
+  __shared__ int last_cta;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int per_seq = (a.nchunks + kWarps - 1) / kWarps;
+  const int per_seq = (a.nchunks + kFinalPerCta - 1) / kFinalPerCta;
   const int y = (int)(blockIdx.x / (unsigned)per_seq);
   const int b = a.B - 1 - y;
-  const int c = (int)(blockIdx.x - (unsigned)y * per_seq) * kWarps + warp;
-  if (c >= a.nchunks) return;
+  const int c0 = (int)(blockIdx.x - (unsigned)y * per_seq) * kFinalPerCta;
+  grid_dependency_wait();  // the decide kernel has written final_rows and zeroed cnt_c
   const FinalRow fr = a.final_rows[b];
-  if (fr.skip) return;
-  const unsigned long long t = chunk_weight_sum<VEC>(a, fr, fr.q_row >= 0, c);
-  if (lane == 0) a.W[(int64_t)b * a.nchunks + c] = t;
-  if (warp_last_of(&a.cnt_c[b], (uint32_t)(a.nchunks - 1))) final_search<VEC>(a, b, fr);
+  if (fr.skip) return;  // the same for the whole CTA
+  const bool residual = fr.q_row >= 0;
+#pragma unroll 1
+  for (int i = 0; i < kFinalPerWarp; ++i) {
+    const int c = c0 + i * kWarps + warp;
+    if (c >= a.nchunks) break;
+    const unsigned long long t = chunk_weight_sum<VEC>(a, fr, residual, c);
+    if (lane == 0) a.W[(int64_t)b * a.nchunks + c] = t;
+  }
+  if (lane == 0) __threadfence();  // this warp's sums are visible before the count
+  __syncthreads();
+  if (threadIdx.x == 0) last_cta = atomicAdd(&a.cnt_c[b], 1u) == (uint32_t)(per_seq - 1);
+  __syncthreads();
+  if (!last_cta || warp != 0) return;
+  __threadfence();  // every other CTA's sums are visible from here on
+  final_search<VEC>(a, b, fr);
 }
 
 // ------------------------------------------------------------ host side
@@ -909,6 +920,26 @@ int resident_ctas(int num_sms) {
   return num_sms * per_sm;
 }
 
+// Launch a kernel that may begin while its predecessor on the stream drains
+// (it calls grid_dependency_wait before it reads the predecessor's output).
+template <typename Kernel>
+int launch_dependent(Kernel kernel, unsigned grid, unsigned block, cudaStream_t stream,
+                     const Args& a, const char* name) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, a);
+  if (err != cudaSuccess) return kyro::cuda_error(err, name);
+  return KYRO_OK;
+}
+
 template <bool VEC, bool STOCH>
 int launch_t(kyro_ctx* ctx, const Args& a) {
   const long long need = ((long long)a.units + kWarps - 1) / kWarps;
@@ -917,20 +948,16 @@ int launch_t(kyro_ctx* ctx, const Args& a) {
   accept_stats_kernel<VEC, STOCH><<<grid, kThreads, 0, ctx->stream>>>(a);
   KY_TRY(kyro::check_launch("accept_stats_kernel"));
   const int dwarps = a.R < kDecideWarps ? a.R : kDecideWarps;
-  accept_decide_kernel<<<a.B, dwarps * 32, 0, ctx->stream>>>(a);
-  KY_TRY(kyro::check_launch("accept_decide_kernel"));
+  KY_TRY(launch_dependent(accept_decide_kernel, (unsigned)a.B, (unsigned)dwarps * 32, ctx->stream,
+                          a, "accept_decide_kernel"));
   if (!STOCH) return KYRO_OK;  // greedy: the decide step wrote every token
-  const unsigned nfinal = (unsigned)a.B * (unsigned)((a.nchunks + kWarps - 1) / kWarps);
-  accept_final_kernel<VEC><<<nfinal, kThreads, 0, ctx->stream>>>(a);
-  return kyro::check_launch("accept_final_kernel");
+  const unsigned nfinal = (unsigned)a.B * (unsigned)((a.nchunks + kFinalPerCta - 1) / kFinalPerCta);
+  return launch_dependent(accept_final_kernel<VEC>, nfinal, kThreads, ctx->stream, a,
+                          "accept_final_kernel");
 }
 
 int launch(kyro_ctx* ctx, Args& a, const Workspace& ws, bool vec) {
-  // the last-arriver counters start at zero
-  if (a.stoch) {
-    cudaError_t err = cudaMemsetAsync(ws.cnt_c, 0, ws.counter_bytes, ctx->stream);
-    if (err != cudaSuccess) return kyro::cuda_error(err, "cudaMemsetAsync(sampler counters)");
-  }
+  (void)ws;
   if (vec && a.stoch) return launch_t<true, true>(ctx, a);
   if (vec) return launch_t<true, false>(ctx, a);
   if (a.stoch) return launch_t<false, true>(ctx, a);
