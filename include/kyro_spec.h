@@ -284,6 +284,14 @@ int kyro_kv_write(kyro_ctx* ctx, const kyro_kv_params* p, int32_t num_new, int32
 int kyro_philox_uniforms(kyro_ctx* ctx, uint64_t seed, uint32_t seq, uint32_t pos0,
                          uint32_t stream, uint32_t step, int32_t n, float* out);
 
+/* Self-check of the sampler's arithmetic (test aid, no reference
+ * counterpart): the kernels evaluate the contract's ky_exp in two faster
+ * forms (exponent add; packed fp32x2 pairs).  This compares both with
+ * ky_exp on every fp32 input in [-100, 0] and on -inf / NaN, on the
+ * context's stream.  counts: device array of 2 u64, set to the number of
+ * mismatching inputs of each form (0 and 0 when the forms agree). */
+int kyro_selftest_exp(kyro_ctx* ctx, unsigned long long* counts);
+
 #ifdef __cplusplus
 }
 #endif

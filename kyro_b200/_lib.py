@@ -43,7 +43,7 @@ EXPORTS = (
     "kyro_sample_workspace_size",
     "kyro_sample_tokens", "kyro_verify_attention_workspace_size", "kyro_verify_attention",
     "kyro_kv_reserve", "kyro_kv_commit", "kyro_kv_commit_tree", "kyro_kv_write",
-    "kyro_philox_uniforms",
+    "kyro_philox_uniforms", "kyro_selftest_exp",
 )
 
 
@@ -115,6 +115,7 @@ def load():
                                           vp, vp, vp, vp]),
         "kyro_kv_write": (C.c_int, [vp, P(KVParams), i32, i32, i32, vp, vp, vp, vp, vp, vp]),
         "kyro_philox_uniforms": (C.c_int, [vp, u64, u32, u32, u32, u32, i32, vp]),
+        "kyro_selftest_exp": (C.c_int, [vp, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

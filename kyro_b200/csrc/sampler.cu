@@ -1097,6 +1097,56 @@ int kyro_sample_tokens(kyro_ctx* ctx, const kyro_sample_params* p, const float* 
 
 }  // extern "C"
 
+// ------------------------------------------------------------ exp self-check
+//
+// The kernels evaluate ky_exp through exp_fast and exp_pair.  This kernel
+// compares both with the contract's ky_exp on every fp32 x in [-100, 0]
+// (the bit patterns 0x80000000 .. 0xC2C80000) and on -inf and both NaN
+// signs, and counts the inputs whose bits differ.
+
+namespace {
+
+constexpr uint32_t kSelfFirst = 0x80000000u;  // -0.0f
+constexpr uint32_t kSelfLast = 0xC2C80000u;   // -100.0f
+constexpr uint64_t kSelfRange = (uint64_t)(kSelfLast - kSelfFirst) + 1;
+constexpr uint64_t kSelfCount = kSelfRange + 3;
+
+__device__ __forceinline__ float selftest_input(uint64_t i) {
+  if (i < kSelfRange) return __uint_as_float(kSelfFirst + (uint32_t)i);
+  const uint32_t special[3] = {0xFF800000u, 0x7FC00000u, 0xFFC00000u};
+  return __uint_as_float(special[i - kSelfRange]);
+}
+
+__global__ void __launch_bounds__(256) exp_selftest_kernel(unsigned long long* counts) {
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  unsigned long long bad_fast = 0, bad_pair = 0;
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < kSelfCount; i += stride) {
+    const float x = selftest_input(i), y = selftest_input(kSelfCount - 1 - i);
+    const uint32_t rx = __float_as_uint(ky_exp(x)), ry = __float_as_uint(ky_exp(y));
+    bad_fast += __float_as_uint(exp_fast(x)) != rx;
+    float px, py;
+    f2_unpack(exp_pair(f2_pack(x, y)), px, py);
+    bad_pair += (__float_as_uint(px) != rx) + (__float_as_uint(py) != ry);
+  }
+  bad_fast = warp_sum(bad_fast);
+  bad_pair = warp_sum(bad_pair);
+  if ((threadIdx.x & 31) == 0) {
+    if (bad_fast) atomicAdd(&counts[0], bad_fast);
+    if (bad_pair) atomicAdd(&counts[1], bad_pair);
+  }
+}
+
+}  // namespace
+
+extern "C" int kyro_selftest_exp(kyro_ctx* ctx, unsigned long long* counts) {
+  KY_TRY(kyro::enter(ctx));
+  KY_REQUIRE(counts, "kyro_selftest_exp: counts is NULL");
+  cudaError_t err = cudaMemsetAsync(counts, 0, 2 * sizeof(unsigned long long), ctx->stream);
+  if (err != cudaSuccess) return kyro::cuda_error(err, "cudaMemsetAsync(selftest counts)");
+  exp_selftest_kernel<<<ctx->num_sms * 8, 256, 0, ctx->stream>>>(counts);
+  return kyro::check_launch("exp_selftest_kernel");
+}
+
 // ------------------------------------------------------------ no-allocation entry point
 //
 // kyro_spec_accept_static serves callers that cannot allocate device memory

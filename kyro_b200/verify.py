@@ -286,3 +286,14 @@ def philox_uniforms(ctx: Context, seed: int, seq: int, pos0: int, stream: int, s
     check(_lib.load().kyro_philox_uniforms(ctx.handle, seed, seq, pos0, stream, step, n,
                                            _ptr(out)))
     return out
+
+
+def selftest_exp(ctx: Context) -> tuple:
+    """Mismatch counts of the kernels' two fast ky_exp forms against the
+    contract's ky_exp over every fp32 input in [-100, 0] (both 0 when the
+    kernels compute the contract's bits)."""
+    counts = torch.zeros(2, dtype=torch.int64, device=ctx.device)
+    ctx.bind_stream()
+    check(_lib.load().kyro_selftest_exp(ctx.handle, _ptr(counts)))
+    c = counts.cpu()
+    return int(c[0]), int(c[1])

@@ -166,3 +166,11 @@ def test_full_config1_accept_matches_oracle(ctx, oracle):
     # per-token acceptance probability E[min(1, p/q)]: BASELINE quotes ~0.6-0.8
     rate = np.minimum(1.0, oprobs[..., 0] / oprobs[..., 1]).mean()
     assert 0.5 < rate < 0.9, rate
+
+
+@pytest.mark.gpu
+def test_fast_exp_forms_match_contract(ctx):
+    """The exponent-add and packed fp32x2 forms the kernels use give ky_exp's
+    bits on every fp32 input in [-100, 0], -inf and NaN."""
+    from kyro_b200 import verify
+    assert verify.selftest_exp(ctx) == (0, 0)
