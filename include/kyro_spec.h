@@ -279,6 +279,37 @@ int kyro_kv_write(kyro_ctx* ctx, const kyro_kv_params* p, int32_t num_new, int32
                   const int64_t* block_table, const int64_t* context_lens, void* k_cache,
                   void* v_cache);
 
+/* ------------------------------------- tensor parallelism (vocab shards) */
+
+/* The lm_head / vocabulary dimension split over a tensor-parallel group as
+ * DistributedContext::shard_dim does it (src/distributed.rs:90-98): rank r
+ * holds vocabulary entries [r*V/R, (r+1)*V/R).  The reference's all_reduce
+ * (:61-79) is a stub; here a context joins its group through an NCCL
+ * communicator it creates from a unique id that the caller's launcher
+ * hands to every rank (rank 0 calls kyro_tp_unique_id).  NCCL is opened at
+ * run time: libnccl.so.2, or the path in the KYRO_NCCL_LIBRARY variable. */
+#define KYRO_TP_UNIQUE_ID_BYTES 128
+int kyro_tp_unique_id(void* out /* KYRO_TP_UNIQUE_ID_BYTES bytes */);
+/* Blocking: returns once all `world` ranks have joined. */
+int kyro_ctx_tp_init(kyro_ctx* ctx, const void* unique_id, int rank, int world);
+
+/* Vocabulary-sharded kyro_spec_accept: p->vocab is the FULL vocabulary V
+ * (divisible by the group size R); target_shard [B, k+1, V/R] and
+ * draft_shard [B, k, V/R] are this rank's columns; draft_tokens hold global
+ * ids.  Every rank passes identical params and gets identical outputs
+ * (accept lengths, tokens with global ids, p/q at the drafts), equal to
+ * kyro_spec_accept on the full rows.  Four small collectives on the
+ * context's stream: all-gathers of per-row maxima, per-row normaliser parts
+ * with the owner rank's values at the draft tokens, per-sequence weight
+ * totals, and an int32 max of the token id.  A rank that returns an error
+ * before its collectives leaves the others waiting in NCCL, so callers
+ * check arguments identically on every rank. */
+size_t kyro_spec_accept_tp_workspace_size(const kyro_accept_params* p, int world);
+int kyro_spec_accept_tp(kyro_ctx* ctx, const kyro_accept_params* p, const float* target_shard,
+                        const float* draft_shard, const int32_t* draft_tokens,
+                        int32_t* out_accept_len, int32_t* out_tokens, int32_t* out_num_tokens,
+                        float* out_probs, void* workspace, size_t workspace_bytes);
+
 /* Philox4x32-10 uniforms exactly as the kernels draw them (test aid):
  * out[i] = u for counter (seq, pos0 + i, stream, step), i < n. */
 int kyro_philox_uniforms(kyro_ctx* ctx, uint64_t seed, uint32_t seq, uint32_t pos0,

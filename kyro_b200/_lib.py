@@ -44,7 +44,11 @@ EXPORTS = (
     "kyro_sample_tokens", "kyro_verify_attention_workspace_size", "kyro_verify_attention",
     "kyro_kv_reserve", "kyro_kv_commit", "kyro_kv_commit_tree", "kyro_kv_write",
     "kyro_philox_uniforms", "kyro_selftest_exp",
+    "kyro_tp_unique_id", "kyro_ctx_tp_init", "kyro_spec_accept_tp_workspace_size",
+    "kyro_spec_accept_tp",
 )
+
+TP_UNIQUE_ID_BYTES = 128
 
 
 class AcceptParams(C.Structure):
@@ -116,6 +120,10 @@ def load():
         "kyro_kv_write": (C.c_int, [vp, P(KVParams), i32, i32, i32, vp, vp, vp, vp, vp, vp]),
         "kyro_philox_uniforms": (C.c_int, [vp, u64, u32, u32, u32, u32, i32, vp]),
         "kyro_selftest_exp": (C.c_int, [vp, vp]),
+        "kyro_tp_unique_id": (C.c_int, [vp]),
+        "kyro_ctx_tp_init": (C.c_int, [vp, vp, C.c_int, C.c_int]),
+        "kyro_spec_accept_tp_workspace_size": (C.c_size_t, [vp, C.c_int]),
+        "kyro_spec_accept_tp": (C.c_int, [vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, C.c_size_t]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

@@ -108,6 +108,9 @@ int kyro_ctx_create(int device, void* stream, kyro_ctx** out) {
   ctx->device = device;
   ctx->stream = (cudaStream_t)stream;
   ctx->num_sms = prop.multiProcessorCount;
+  ctx->nccl_comm = nullptr;
+  ctx->tp_rank = 0;
+  ctx->tp_world = 1;
   err = cudaMalloc(&ctx->d_status, 16);
   if (err != cudaSuccess) {
     delete ctx;
@@ -126,6 +129,7 @@ int kyro_ctx_create(int device, void* stream, kyro_ctx** out) {
 int kyro_ctx_destroy(kyro_ctx* ctx) {
   if (!ctx) return KYRO_OK;
   cudaSetDevice(ctx->device);
+  kyro::nccl::release(ctx);
   cudaFree(ctx->d_status);
   delete ctx;
   return KYRO_OK;

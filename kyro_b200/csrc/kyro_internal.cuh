@@ -17,6 +17,9 @@ struct kyro_ctx {
   cudaStream_t stream;
   uint32_t* d_status;  // KYRO_DEV_* bits, atomically OR-ed by kernels
   int num_sms;
+  // tensor-parallel group (kyro_ctx_tp_init); world 1 without one
+  void* nccl_comm;     // ncclComm_t
+  int tp_rank, tp_world;
 };
 
 namespace kyro {
@@ -29,6 +32,18 @@ int cuda_error(cudaError_t err, const char* what);
 int check_launch(const char* what);
 // Validate a context and make its device current.
 int enter(kyro_ctx* ctx);
+
+// NCCL, loaded at run time (nccl_comm.cu).  Collectives enqueue on the
+// context's stream over its tensor-parallel communicator.
+namespace nccl {
+// every rank receives the world * bytes concatenation of all ranks' `bytes`
+int all_gather(kyro_ctx* ctx, const void* send, void* recv, size_t bytes, const char* what);
+// element-wise max of int32 over the group
+int all_reduce_max_i32(kyro_ctx* ctx, const int32_t* send, int32_t* recv, size_t count,
+                       const char* what);
+// destroy the context's communicator (no-op without one)
+void release(kyro_ctx* ctx);
+}  // namespace nccl
 
 }  // namespace kyro
 

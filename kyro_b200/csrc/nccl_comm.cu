@@ -1,0 +1,142 @@
+// nccl_comm.cu -- the tensor-parallel group of a context.
+//
+// The reference's DistributedContext::all_reduce (src/distributed.rs:61-79)
+// is a stub that returns its input.  Here the vocabulary-sharded acceptance
+// step exchanges a few bytes per row over NCCL.  NCCL is opened at run time
+// (dlopen), so the library loads, and everything but the TP entry points
+// works, on a machine without it; the TP entry points fail with
+// KYRO_ERR_NCCL and a message naming the library they looked for.
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+
+#include "kyro_internal.cuh"
+
+namespace {
+
+struct NcclApi {
+  ncclResult_t (*GetUniqueId)(ncclUniqueId*);
+  ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int);
+  ncclResult_t (*CommDestroy)(ncclComm_t);
+  ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t);
+  ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                            cudaStream_t);
+  const char* (*GetErrorString)(ncclResult_t);
+};
+
+std::once_flag g_once;
+NcclApi g_api;
+bool g_ok = false;
+char g_why[512];
+
+void load_api() {
+  const char* path = std::getenv("KYRO_NCCL_LIBRARY");
+  if (!path || !*path) path = "libnccl.so.2";
+  void* h = dlopen(path, RTLD_NOW | RTLD_GLOBAL);
+  if (!h) {
+    snprintf(g_why, sizeof(g_why), "cannot open %s: %s", path, dlerror());
+    return;
+  }
+  bool ok = true;
+  auto sym = [&](const char* name) {
+    void* f = dlsym(h, name);
+    if (!f) ok = false;
+    return f;
+  };
+  g_api.GetUniqueId = (decltype(g_api.GetUniqueId))sym("ncclGetUniqueId");
+  g_api.CommInitRank = (decltype(g_api.CommInitRank))sym("ncclCommInitRank");
+  g_api.CommDestroy = (decltype(g_api.CommDestroy))sym("ncclCommDestroy");
+  g_api.AllGather = (decltype(g_api.AllGather))sym("ncclAllGather");
+  g_api.AllReduce = (decltype(g_api.AllReduce))sym("ncclAllReduce");
+  g_api.GetErrorString = (decltype(g_api.GetErrorString))sym("ncclGetErrorString");
+  if (!ok) {
+    snprintf(g_why, sizeof(g_why), "%s lacks an NCCL entry point", path);
+    return;
+  }
+  g_ok = true;
+}
+
+const NcclApi* api() {
+  std::call_once(g_once, load_api);
+  return g_ok ? &g_api : nullptr;
+}
+
+int nccl_error(ncclResult_t r, const char* what) {
+  const NcclApi* a = api();
+  return kyro::set_error(KYRO_ERR_NCCL, "%s: %s", what,
+                         a ? a->GetErrorString(r) : "NCCL error");
+}
+
+int need_api(const NcclApi** out, const char* what) {
+  *out = api();
+  if (!*out) return kyro::set_error(KYRO_ERR_NCCL, "%s: NCCL unavailable (%s)", what, g_why);
+  return KYRO_OK;
+}
+
+}  // namespace
+
+namespace kyro {
+namespace nccl {
+
+int all_gather(kyro_ctx* ctx, const void* send, void* recv, size_t bytes, const char* what) {
+  const NcclApi* a;
+  KY_TRY(need_api(&a, what));
+  const ncclResult_t r =
+      a->AllGather(send, recv, bytes, ncclUint8, (ncclComm_t)ctx->nccl_comm, ctx->stream);
+  return r == ncclSuccess ? KYRO_OK : nccl_error(r, what);
+}
+
+int all_reduce_max_i32(kyro_ctx* ctx, const int32_t* send, int32_t* recv, size_t count,
+                       const char* what) {
+  const NcclApi* a;
+  KY_TRY(need_api(&a, what));
+  const ncclResult_t r = a->AllReduce(send, recv, count, ncclInt32, ncclMax,
+                                      (ncclComm_t)ctx->nccl_comm, ctx->stream);
+  return r == ncclSuccess ? KYRO_OK : nccl_error(r, what);
+}
+
+void release(kyro_ctx* ctx) {
+  if (!ctx->nccl_comm) return;
+  const NcclApi* a = api();
+  if (a) a->CommDestroy((ncclComm_t)ctx->nccl_comm);
+  ctx->nccl_comm = nullptr;
+  ctx->tp_rank = 0;
+  ctx->tp_world = 1;
+}
+
+}  // namespace nccl
+}  // namespace kyro
+
+extern "C" int kyro_tp_unique_id(void* out) {
+  if (!out) return kyro::set_error(KYRO_ERR_INVALID_ARG, "kyro_tp_unique_id: out is NULL");
+  const NcclApi* a;
+  KY_TRY(need_api(&a, "kyro_tp_unique_id"));
+  static_assert(sizeof(ncclUniqueId) == KYRO_TP_UNIQUE_ID_BYTES, "NCCL unique id size");
+  ncclUniqueId id;
+  const ncclResult_t r = a->GetUniqueId(&id);
+  if (r != ncclSuccess) return nccl_error(r, "ncclGetUniqueId");
+  memcpy(out, &id, sizeof(id));
+  return KYRO_OK;
+}
+
+extern "C" int kyro_ctx_tp_init(kyro_ctx* ctx, const void* unique_id, int rank, int world) {
+  KY_TRY(kyro::enter(ctx));
+  KY_REQUIRE(unique_id, "kyro_ctx_tp_init: unique_id is NULL");
+  KY_REQUIRE(world >= 1 && rank >= 0 && rank < world, "kyro_ctx_tp_init: rank %d of %d", rank,
+             world);
+  KY_REQUIRE(!ctx->nccl_comm, "kyro_ctx_tp_init: the context already has a group");
+  const NcclApi* a;
+  KY_TRY(need_api(&a, "kyro_ctx_tp_init"));
+  ncclUniqueId id;
+  memcpy(&id, unique_id, sizeof(id));
+  ncclComm_t comm = nullptr;
+  const ncclResult_t r = a->CommInitRank(&comm, world, id, rank);
+  if (r != ncclSuccess) return nccl_error(r, "ncclCommInitRank");
+  ctx->nccl_comm = comm;
+  ctx->tp_rank = rank;
+  ctx->tp_world = world;
+  return KYRO_OK;
+}

@@ -96,6 +96,20 @@ __device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv& f) {
   return (__umulhi(n, f.m) + n) >> f.s;
 }
 
+// Tensor-parallel exchange records (one per row or per sequence and rank).
+struct TpRow1 {  // round 1: this rank's row max, or its argmax as a global id
+  float M;
+  int32_t arg;
+};
+struct TpRow2 {  // round 2: this rank's part of the normaliser under the
+  double S;      // global max; e and the chunk max at the draft token when
+  float ex;      // this rank holds the token, else 0
+  float mcx;
+};
+struct TpSeq3 {  // round 3: this rank's weight totals of the chosen row
+  unsigned long long w_res, w_p;
+};
+
 struct Args {
   const float* plog;            // target logits (accept) or the rows to sample
   const float* qlog;            // draft logits (stochastic accept) or null
@@ -125,6 +139,15 @@ struct Args {
   uint32_t* cnt_c;              // [B] finished weight sums per sequence
   uint32_t units;               // stats units: B * R * nchunks
   uint32_t* status;
+  // tensor parallelism (vocabulary shards): V above is this shard's width
+  int64_t V_global;             // the full vocabulary (V without a group)
+  int64_t vocab_offset;         // global id of this shard's entry 0
+  int tp_rank, tp_world;
+  TpRow1 *send1, *recv1;        // [B*R], [world][B*R]
+  TpRow2 *send2, *recv2;        // [B*R], [world][B*R]
+  TpSeq3 *send3, *recv3;        // [B], [world][B]
+  int32_t *send4, *recv4;       // [B]
+  unsigned long long* W2;       // [B][nchunks][2]: residual and p weight sums
 };
 
 __host__ __device__ inline size_t align_up(size_t x) { return (x + 255) & ~size_t(255); }
@@ -157,6 +180,46 @@ Workspace carve(void* base, int64_t B, int64_t R, int64_t nchunks) {
   off += align_up(sizeof(unsigned long long) * (size_t)(B * nchunks));
   w.bytes = off;
   return w;
+}
+
+// The tensor-parallel call's workspace: the single-GPU layout over this
+// rank's columns, then the exchange buffers and the paired chunk sums.
+struct TpWorkspace {
+  Workspace base;
+  TpRow1 *send1, *recv1;
+  TpRow2 *send2, *recv2;
+  TpSeq3 *send3, *recv3;
+  int32_t *send4, *recv4;
+  unsigned long long* W2;
+  size_t bytes;
+};
+
+TpWorkspace carve_tp(void* base, int64_t B, int64_t R, int64_t nchunks, int64_t world) {
+  TpWorkspace t;
+  t.base = carve(base, B, R, nchunks);
+  char* p = (char*)base;
+  size_t off = t.base.bytes;
+  const int64_t rows = B * R;
+  t.send1 = (TpRow1*)(p + off);
+  off += align_up(sizeof(TpRow1) * (size_t)rows);
+  t.recv1 = (TpRow1*)(p + off);
+  off += align_up(sizeof(TpRow1) * (size_t)(rows * world));
+  t.send2 = (TpRow2*)(p + off);
+  off += align_up(sizeof(TpRow2) * (size_t)rows);
+  t.recv2 = (TpRow2*)(p + off);
+  off += align_up(sizeof(TpRow2) * (size_t)(rows * world));
+  t.send3 = (TpSeq3*)(p + off);
+  off += align_up(sizeof(TpSeq3) * (size_t)B);
+  t.recv3 = (TpSeq3*)(p + off);
+  off += align_up(sizeof(TpSeq3) * (size_t)(B * world));
+  t.send4 = (int32_t*)(p + off);
+  off += align_up(sizeof(int32_t) * (size_t)B);
+  t.recv4 = (int32_t*)(p + off);
+  off += align_up(sizeof(int32_t) * (size_t)B);
+  t.W2 = (unsigned long long*)(p + off);
+  off += align_up(2 * sizeof(unsigned long long) * (size_t)(B * nchunks));
+  t.bytes = off;
+  return t;
 }
 
 // ------------------------------------------------------------ primitives
@@ -320,7 +383,8 @@ __device__ __forceinline__ void load_slice(const Args& a, uint32_t u, Slice& s) 
   const int r = (int)(srow - (uint32_t)b * (uint32_t)a.R);
   s.srow = srow;
   s.c = c;
-  s.x = draft_token_of_row(a, b, r);
+  const int xg = draft_token_of_row(a, b, r);  // global id, -1 for none
+  s.x = xg < 0 ? -1 : (int)(xg - a.vocab_offset);
   const float* row = stats_row_ptr(a, b, r);
   const int64_t base = (int64_t)c * kChunk;
   if (VEC && base + kChunk <= a.V) {
@@ -541,30 +605,14 @@ __device__ __forceinline__ TestInputs load_test(const Args& a, int b, int j) {
   return t;
 }
 
-// One CTA per sequence (per row for the sampler): the warps compute the row
-// statistics, then warp 0 runs the accept tests and writes the sequence's
-// accepted prefix and the row its last token is drawn from.
-__global__ void __launch_bounds__(kDecideWarps * 32) accept_decide_kernel(Args a) {
-  __shared__ RowStat rs[kMaxRows];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
-  const int b = blockIdx.x;
+// Warp 0 of a sequence's CTA: the k accept tests (lane j runs test j), the
+// accepted prefix, and the descriptor of the row the last token is drawn
+// from.  rs holds the sequence's row statistics; t0 / t1 the inputs of
+// tests lane and lane + 32.
+__device__ __forceinline__ void decide_sequence(const Args& a, int b, const RowStat* rs,
+                                                const TestInputs& t0, const TestInputs& t1) {
+  const int lane = threadIdx.x & 31;
   const int k = a.k;
-  grid_dependency_wait();  // the chunk statistics are complete
-  allow_dependents();
-  if (threadIdx.x == 0) a.cnt_c[b] = 0;  // the final kernel's last-arriver count
-  // warp 0 fetches the test inputs (lane j: tests j and j + 32) before it
-  // joins the row statistics
-  TestInputs t0, t1;
-  if (warp == 0 && !a.sample) {
-    t0 = load_test(a, b, lane);
-    t1 = load_test(a, b, lane + 32);
-  }
-  for (int r = warp; r < a.R; r += nwarps) {
-    const RowStat s = row_stat(a, (int64_t)b * a.R + r);
-    if (lane == 0) rs[r] = s;
-  }
-  __syncthreads();
-  if (warp != 0) return;
   FinalRow fr;
   fr._pad = 0;
   if (a.sample) {
@@ -604,7 +652,7 @@ __global__ void __launch_bounds__(kDecideWarps * 32) accept_decide_kernel(Args a
     const TestInputs& t = j0 == 0 ? t0 : t1;
     bool acc = true;
     if (j < k) {
-      const bool ok = t.x >= 0 && t.x < a.V;
+      const bool ok = t.x >= 0 && t.x < a.V_global;
       if (!ok) kyro::dev::flag(a.status, KYRO_DEV_BAD_TOKEN);
       if (a.stoch) {
         float p = 0.0f, q = 0.0f;
@@ -670,6 +718,31 @@ __global__ void __launch_bounds__(kDecideWarps * 32) accept_decide_kernel(Args a
   a.final_rows[b] = fr;
 }
 
+// One CTA per sequence (per row for the sampler): the warps compute the row
+// statistics, then warp 0 runs the accept tests and writes the sequence's
+// accepted prefix and the row its last token is drawn from.
+__global__ void __launch_bounds__(kDecideWarps * 32) accept_decide_kernel(Args a) {
+  __shared__ RowStat rs[kMaxRows];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const int b = blockIdx.x;
+  grid_dependency_wait();  // the chunk statistics are complete
+  allow_dependents();
+  if (threadIdx.x == 0) a.cnt_c[b] = 0;  // the final kernel's last-arriver count
+  // warp 0 fetches the test inputs (lane j: tests j and j + 32) before it
+  // joins the row statistics
+  TestInputs t0, t1;
+  if (warp == 0 && !a.sample) {
+    t0 = load_test(a, b, lane);
+    t1 = load_test(a, b, lane + 32);
+  }
+  for (int r = warp; r < a.R; r += nwarps) {
+    const RowStat s = row_stat(a, (int64_t)b * a.R + r);
+    if (lane == 0) rs[r] = s;
+  }
+  __syncthreads();
+  if (warp == 0) decide_sequence(a, b, rs, t0, t1);
+}
+
 // ------------------------------------------------------------ final kernel
 
 // Per-chunk factors of a final row: g62 = g_c * 2^62 of p (and of q for
@@ -708,7 +781,8 @@ __device__ __forceinline__ float4 load4(const float* __restrict__ row, int64_t e
 // Residual: each element's p and q exps form one packed pair; from p
 // alone, neighbouring elements pair up.
 __device__ __forceinline__ void weights_of4(float inv_t, bool residual, const FinalScale& s,
-                                            float4 zp, float4 zq, unsigned long long (&w)[4]) {
+                                            float4 zp, float4 zq, unsigned long long (&w)[4],
+                                            unsigned long long* wp_out = nullptr) {
   const float p4[4] = {zp.x, zp.y, zp.z, zp.w};
   const float q4[4] = {zq.x, zq.y, zq.z, zq.w};
   if (residual) {
@@ -722,6 +796,7 @@ __device__ __forceinline__ void weights_of4(float inv_t, bool residual, const Fi
       f2_unpack(f2_mul(exp_pair(f2_sub(z, mm)), gg), wp, wq);
       const float d = __fsub_rn(wp, wq);
       w[j] = d > 0.0f ? __float2ull_rz(d) : 0ull;
+      if (wp_out) wp_out[j] = __float2ull_rz(wp);  // ky_weight_p of the same e_p
     }
   } else {
     const f2_t mm = f2_pack(s.mp, s.mp);
@@ -734,6 +809,10 @@ __device__ __forceinline__ void weights_of4(float inv_t, bool residual, const Fi
       f2_unpack(f2_mul(exp_pair(f2_sub(z, mm)), gg), w0, w1);
       w[j] = __float2ull_rz(w0);
       w[j + 1] = __float2ull_rz(w1);
+      if (wp_out) {
+        wp_out[j] = w[j];
+        wp_out[j + 1] = w[j + 1];
+      }
     }
   }
 }
@@ -773,6 +852,88 @@ __device__ __forceinline__ unsigned long long chunk_weight_sum(const Args& a, co
   return warp_sum(t);
 }
 
+// Both sums of chunk c over the warp: the weights the row samples from
+// (residual or p) and the p weights alone (the residual's fallback).
+template <bool VEC>
+__device__ __forceinline__ void chunk_weight_sums2(const Args& a, const FinalRow& fr, bool residual,
+                                                   int c, unsigned long long& t_w,
+                                                   unsigned long long& t_p) {
+  float4 zp[kVec], zq[kVec];
+  load_final_chunk<VEC>(a, fr, residual, c, zp, zq);
+  const float mp = a.stats[fr.p_stat * a.nchunks + c].m;
+  const float mq = residual ? a.stats[fr.q_stat * a.nchunks + c].m : 0.0f;
+  const FinalScale s = final_scale(fr, residual, mp, mq);
+  unsigned long long tw = 0, tp = 0;
+#pragma unroll
+  for (int i = 0; i < kVec; ++i) {
+    unsigned long long w[4], wp[4];
+    weights_of4(a.inv_t, residual, s, zp[i], zq[i], w, wp);
+    tw += (w[0] + w[1]) + (w[2] + w[3]);
+    tp += (wp[0] + wp[1]) + (wp[2] + wp[3]);
+  }
+  t_w = warp_sum(tw);
+  t_p = warp_sum(tp);
+}
+
+// The entry (an index into this row's columns) whose inclusive weight
+// prefix first reaches T, 1 <= T <= the sum of the chunk sums W[c * wstride]
+// (-1 if it does not): find the chunk by a prefix scan over the chunk sums,
+// then scan the chunk's float4 groups in index order, lanes in order within.
+template <bool VEC>
+__device__ __forceinline__ int cut_index(const Args& a, const FinalRow& fr, bool residual,
+                                         const unsigned long long* W, int wstride,
+                                         unsigned long long T) {
+  const int lane = threadIdx.x & 31;
+  const int nc = a.nchunks;
+  int sub = -1;
+  unsigned long long base = 0;
+  for (int s0 = 0; s0 < nc && sub < 0; s0 += 32) {
+    const unsigned long long ws = (s0 + lane < nc) ? __ldcg(&W[(int64_t)(s0 + lane) * wstride]) : 0ull;
+    const unsigned long long inc = base + warp_inclusive(ws);
+    const unsigned hit = __ballot_sync(0xffffffffu, inc >= T && s0 + lane < nc);
+    if (hit) {
+      const int l = __ffs(hit) - 1;
+      sub = s0 + l;
+      const unsigned long long before = __shfl_sync(0xffffffffu, inc - ws, l);
+      T -= before;
+    } else {
+      base = __shfl_sync(0xffffffffu, inc, 31);
+    }
+  }
+  if (sub < 0) return -1;
+  float4 zp[kVec], zq[kVec];
+  load_final_chunk<VEC>(a, fr, residual, sub, zp, zq);
+  const float mp = a.stats[fr.p_stat * nc + sub].m;
+  const float mq = residual ? a.stats[fr.q_stat * nc + sub].m : 0.0f;
+  const FinalScale sc = final_scale(fr, residual, mp, mq);
+  unsigned long long cbase = 0;
+  int found = -1;
+#pragma unroll
+  for (int i = 0; i < kVec; ++i) {
+    unsigned long long w[4];
+    weights_of4(a.inv_t, residual, sc, zp[i], zq[i], w);
+    const unsigned long long s4 = (w[0] + w[1]) + (w[2] + w[3]);
+    const unsigned long long inc = warp_inclusive(s4);
+    unsigned long long C = cbase + inc - s4;
+    int mine = -1;
+    if (C < T && C + s4 >= T) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        C += w[j];
+        if (mine < 0 && C >= T) mine = j;
+      }
+    }
+    const unsigned hit = __ballot_sync(0xffffffffu, mine >= 0);
+    if (found < 0 && hit) {
+      const int l = __ffs(hit) - 1;
+      const int jj = __shfl_sync(0xffffffffu, mine, l);
+      found = sub * kChunk + (i * 32 + l) * 4 + jj;
+    }
+    cbase += __shfl_sync(0xffffffffu, inc, 31);
+  }
+  return found;
+}
+
 // Locate the cut point of final row b once all its chunk sums are in W.
 template <bool VEC>
 __device__ __forceinline__ void final_search(const Args& a, int b, const FinalRow& fr) {
@@ -807,57 +968,8 @@ __device__ __forceinline__ void final_search(const Args& a, int b, const FinalRo
   }
   int token = (int)a.V - 1;
   if (tot != 0) {
-    unsigned long long T = ky_cdf_threshold(fr.odd, tot);
-    // find the chunk whose inclusive prefix first reaches T
-    int sub = -1;
-    unsigned long long base = 0;
-    for (int s0 = 0; s0 < nc && sub < 0; s0 += 32) {
-      const unsigned long long ws = (s0 + lane < nc) ? __ldcg(&W[s0 + lane]) : 0ull;
-      const unsigned long long inc = base + warp_inclusive(ws);
-      const unsigned hit = __ballot_sync(0xffffffffu, inc >= T && s0 + lane < nc);
-      if (hit) {
-        const int l = __ffs(hit) - 1;
-        sub = s0 + l;
-        const unsigned long long before = __shfl_sync(0xffffffffu, inc - ws, l);
-        T -= before;
-      } else {
-        base = __shfl_sync(0xffffffffu, inc, 31);
-      }
-    }
-    if (sub >= 0) {
-      // scan the chunk: float4 groups in index order, lanes in order within
-      float4 zp[kVec], zq[kVec];
-      load_final_chunk<VEC>(a, fr, residual, sub, zp, zq);
-      const float mp = a.stats[fr.p_stat * nc + sub].m;
-      const float mq = residual ? a.stats[fr.q_stat * nc + sub].m : 0.0f;
-      const FinalScale sc = final_scale(fr, residual, mp, mq);
-      unsigned long long cbase = 0;
-      int found = -1;
-#pragma unroll
-      for (int i = 0; i < kVec; ++i) {
-        unsigned long long w[4];
-        weights_of4(a.inv_t, residual, sc, zp[i], zq[i], w);
-        const unsigned long long s4 = (w[0] + w[1]) + (w[2] + w[3]);
-        const unsigned long long inc = warp_inclusive(s4);
-        unsigned long long C = cbase + inc - s4;
-        int mine = -1;
-        if (C < T && C + s4 >= T) {
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            C += w[j];
-            if (mine < 0 && C >= T) mine = j;
-          }
-        }
-        const unsigned hit = __ballot_sync(0xffffffffu, mine >= 0);
-        if (found < 0 && hit) {
-          const int l = __ffs(hit) - 1;
-          const int jj = __shfl_sync(0xffffffffu, mine, l);
-          found = sub * kChunk + (i * 32 + l) * 4 + jj;
-        }
-        cbase += __shfl_sync(0xffffffffu, inc, 31);
-      }
-      if (found >= 0) token = found;
-    }
+    const int found = cut_index<VEC>(a, fr, residual, W, 1, ky_cdf_threshold(fr.odd, tot));
+    if (found >= 0) token = found;
   }
   if (lane == 0) {
     a.out_tokens[fr.out_index] = token;
@@ -875,8 +987,10 @@ __device__ __forceinline__ void final_search(const Args& a, int b, const FinalRo
 // row, warp w the chunks w, w + 4, ... of them (neighbouring warps read
 // neighbouring chunks).  Sequences run in reverse, so the rows the stats
 // kernel read last (the ones most likely still in L2) come first.  The last
-// CTA of a row to finish locates the cut point.
-template <bool VEC>
+// CTA of a row to finish locates the cut point -- or, under tensor
+// parallelism (TP), sums this rank's residual and p weights for the
+// exchange that precedes the search.
+template <bool VEC, bool TP>
 __global__ void __launch_bounds__(kThreads) accept_final_kernel(Args a) {
   __shared__ int last_cta;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -892,8 +1006,17 @@ __global__ void __launch_bounds__(kThreads) accept_final_kernel(Args a) {
   for (int i = 0; i < kFinalPerWarp; ++i) {
     const int c = c0 + i * kWarps + warp;
     if (c >= a.nchunks) break;
-    const unsigned long long t = chunk_weight_sum<VEC>(a, fr, residual, c);
-    if (lane == 0) a.W[(int64_t)b * a.nchunks + c] = t;
+    if (TP) {
+      unsigned long long tw, tp;
+      chunk_weight_sums2<VEC>(a, fr, residual, c, tw, tp);
+      if (lane == 0) {
+        a.W2[((int64_t)b * a.nchunks + c) * 2 + 0] = tw;
+        a.W2[((int64_t)b * a.nchunks + c) * 2 + 1] = tp;
+      }
+    } else {
+      const unsigned long long t = chunk_weight_sum<VEC>(a, fr, residual, c);
+      if (lane == 0) a.W[(int64_t)b * a.nchunks + c] = t;
+    }
   }
   if (lane == 0) __threadfence();  // this warp's sums are visible before the count
   __syncthreads();
@@ -901,7 +1024,223 @@ __global__ void __launch_bounds__(kThreads) accept_final_kernel(Args a) {
   __syncthreads();
   if (!last_cta || warp != 0) return;
   __threadfence();  // every other CTA's sums are visible from here on
-  final_search<VEC>(a, b, fr);
+  if (!TP) {
+    final_search<VEC>(a, b, fr);
+    return;
+  }
+  unsigned long long tw = 0, tp = 0;
+  for (int c = lane; c < a.nchunks; c += 32) {
+    tw += __ldcg(&a.W2[((int64_t)b * a.nchunks + c) * 2 + 0]);
+    tp += __ldcg(&a.W2[((int64_t)b * a.nchunks + c) * 2 + 1]);
+  }
+  tw = warp_sum(tw);
+  tp = warp_sum(tp);
+  if (lane == 0) a.send3[b] = TpSeq3{tw, tp};
+}
+
+// ------------------------------------------------------------ tensor parallelism
+//
+// Vocabulary shards (DistributedContext::shard_dim, src/distributed.rs:90-98):
+// each rank runs the stats kernel on its own columns, then
+//   accept_tp_max_kernel    row maxima (argmax, greedy)         -> all-gather 1
+//   accept_tp_sum_kernel    normaliser parts under the global
+//                           max, owner values at the drafts     -> all-gather 2
+//   accept_tp_decide_kernel the decision, the same on every rank
+//   accept_final_kernel<TP> this rank's weight totals            -> all-gather 3
+//   accept_tp_search_kernel the owner rank finds the token      -> int32 max 4
+//   accept_tp_write_kernel  every rank writes it
+// Ranks contribute to sums through all-gathers and add the parts in rank
+// order, so every rank computes the contract's rank-ordered sums.
+
+// Row max of stats row srow over this rank's chunks (one warp).
+__device__ __forceinline__ float row_max(const Args& a, int64_t srow) {
+  const int lane = threadIdx.x & 31;
+  const ChunkStat* st = a.stats + srow * a.nchunks;
+  float M = -INFINITY;
+  for (int g = 0; g < a.nchunks; g += 256) {
+    float mm[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = g + j * 32 + lane;
+      mm[j] = c < a.nchunks ? st[c].m : -INFINITY;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) M = fmaxf(M, mm[j]);
+  }
+  return kyro::dev::warp_max(M);
+}
+
+// This rank's butterfly part of the normaliser of stats row srow under the
+// global row max M (one warp; lane l adds chunks l, l+32, ... in order).
+__device__ __forceinline__ double row_sum_part(const Args& a, int64_t srow, float M) {
+  const int lane = threadIdx.x & 31;
+  const ChunkStat* st = a.stats + srow * a.nchunks;
+  double t = 0.0;
+  for (int g = 0; g < a.nchunks; g += 256) {
+    float mm[8], ee[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = g + j * 32 + lane;
+      mm[j] = c < a.nchunks ? st[c].m : 0.0f;
+      ee[j] = c < a.nchunks ? st[c].E : 0.0f;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (g + j * 32 + lane < a.nchunks) t = KY_DADD(t, ky_chunk_mass(ee[j], mm[j], M));
+  }
+  return warp_butterfly(t);
+}
+
+__device__ __forceinline__ float global_row_max(const Args& a, int64_t srow) {
+  const int64_t rows = (int64_t)a.B * a.R;
+  float M = -INFINITY;
+  for (int q = 0; q < a.tp_world; ++q) M = fmaxf(M, a.recv1[q * rows + srow].M);
+  return M;
+}
+
+// One CTA per sequence, one warp per row.
+__global__ void __launch_bounds__(kDecideWarps * 32) accept_tp_max_kernel(Args a) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const int b = blockIdx.x;
+  grid_dependency_wait();
+  for (int r = warp; r < a.R; r += nwarps) {
+    const int64_t srow = (int64_t)b * a.R + r;
+    TpRow1 v;
+    if (a.stoch) {
+      v.M = row_max(a, srow);
+      v.arg = 0;
+    } else {
+      const RowStat rs = row_stat(a, srow);
+      v.M = rs.M;
+      v.arg = (int32_t)(rs.arg + a.vocab_offset);
+    }
+    if (lane == 0) a.send1[srow] = v;
+  }
+}
+
+// One CTA per sequence, one warp per row (stochastic mode only).
+__global__ void __launch_bounds__(kDecideWarps * 32) accept_tp_sum_kernel(Args a) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const int b = blockIdx.x;
+  for (int r = warp; r < a.R; r += nwarps) {
+    const int64_t srow = (int64_t)b * a.R + r;
+    const float M = global_row_max(a, srow);
+    TpRow2 v;
+    v.S = row_sum_part(a, srow, M);
+    v.ex = 0.0f;
+    v.mcx = 0.0f;
+    const int xg = draft_token_of_row(a, b, r);
+    const int64_t xl = (int64_t)xg - a.vocab_offset;
+    if (xg >= 0 && xg < a.V_global && xl >= 0 && xl < a.V) {
+      v.ex = a.ex[srow];
+      v.mcx = a.stats[srow * a.nchunks + xl / kChunk].m;
+    }
+    if (lane == 0) a.send2[srow] = v;
+  }
+}
+
+// The inputs of accept test j from the rank that holds the draft token.
+__device__ __forceinline__ TestInputs tp_test(const Args& a, int b, int j) {
+  TestInputs t;
+  t.x = -1;
+  t.ep = t.eq = t.mp = t.mq = 0.0f;
+  if (j >= a.k) return t;
+  t.x = a.draft_tokens[(int64_t)b * a.k + j];
+  if (a.stoch && t.x >= 0 && t.x < a.V_global) {
+    const int64_t rows = (int64_t)a.B * a.R;
+    const int owner = (int)(t.x / a.V);
+    const TpRow2 pr = a.recv2[owner * rows + (int64_t)b * a.R + j];
+    const TpRow2 qr = a.recv2[owner * rows + (int64_t)b * a.R + a.k + 1 + j];
+    t.ep = pr.ex;
+    t.mp = pr.mcx;
+    t.eq = qr.ex;
+    t.mq = qr.mcx;
+  }
+  return t;
+}
+
+// One CTA per sequence: global row statistics from the exchanged parts,
+// then the same decision as accept_decide_kernel.
+__global__ void __launch_bounds__(kDecideWarps * 32) accept_tp_decide_kernel(Args a) {
+  __shared__ RowStat rs[kMaxRows];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int b = blockIdx.x;
+  const int64_t rows = (int64_t)a.B * a.R;
+  if (threadIdx.x == 0) a.cnt_c[b] = 0;
+  for (int r = threadIdx.x; r < a.R; r += blockDim.x) {
+    const int64_t srow = (int64_t)b * a.R + r;
+    RowStat v;
+    v.S = 0.0;
+    v.arg = 0;
+    if (a.stoch) {
+      v.M = global_row_max(a, srow);
+      for (int q = 0; q < a.tp_world; ++q) v.S = KY_DADD(v.S, a.recv2[q * rows + srow].S);
+    } else {
+      // shards are contiguous: the first strict maximum in rank order is the
+      // lowest global index among equal maxima
+      v.M = a.recv1[srow].M;
+      v.arg = a.recv1[srow].arg;
+      for (int q = 1; q < a.tp_world; ++q) {
+        const TpRow1 o = a.recv1[q * rows + srow];
+        if (o.M > v.M) {
+          v.M = o.M;
+          v.arg = o.arg;
+        }
+      }
+    }
+    rs[r] = v;
+  }
+  __syncthreads();
+  if (warp != 0) return;
+  const TestInputs t0 = tp_test(a, b, lane), t1 = tp_test(a, b, lane + 32);
+  decide_sequence(a, b, rs, t0, t1);
+}
+
+// One warp per sequence: the global threshold from the exchanged totals;
+// the rank whose columns hold it finds the token, the others offer -1.
+template <bool VEC>
+__global__ void __launch_bounds__(kThreads) accept_tp_search_kernel(Args a) {
+  const int lane = threadIdx.x & 31;
+  const int b = blockIdx.x * kWarps + (threadIdx.x >> 5);
+  if (b >= a.B) return;
+  const FinalRow fr = a.final_rows[b];
+  int token = -1;
+  if (!fr.skip) {
+    unsigned long long tot_w = 0, tot_p = 0;
+    for (int q = 0; q < a.tp_world; ++q) {
+      tot_w += a.recv3[(int64_t)q * a.B + b].w_res;
+      tot_p += a.recv3[(int64_t)q * a.B + b].w_p;
+    }
+    // the residual, or p when there is none (bonus) or it has no mass
+    const bool residual = fr.q_row >= 0 && tot_w != 0;
+    const unsigned long long tot = residual ? tot_w : tot_p;
+    if (tot == 0) {
+      if (a.tp_rank == a.tp_world - 1) token = (int)(a.V_global - 1);
+    } else {
+      const unsigned long long T = ky_cdf_threshold(fr.odd, tot);
+      unsigned long long before = 0;
+      for (int q = 0; q < a.tp_rank; ++q) {
+        const TpSeq3 v = a.recv3[(int64_t)q * a.B + b];
+        before += residual ? v.w_res : v.w_p;
+      }
+      const TpSeq3 mine = a.recv3[(int64_t)a.tp_rank * a.B + b];
+      const unsigned long long m = residual ? mine.w_res : mine.w_p;
+      if (T > before && T - before <= m) {
+        const int local = cut_index<VEC>(a, fr, residual,
+                                         a.W2 + (int64_t)b * a.nchunks * 2 + (residual ? 0 : 1), 2,
+                                         T - before);
+        if (local >= 0) token = (int)(local + a.vocab_offset);
+      }
+    }
+  }
+  if (lane == 0) a.send4[b] = token;
+}
+
+__global__ void accept_tp_write_kernel(Args a) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= a.B) return;
+  const FinalRow fr = a.final_rows[b];
+  if (!fr.skip) a.out_tokens[fr.out_index] = a.recv4[b];
 }
 
 // ------------------------------------------------------------ host side
@@ -952,7 +1291,7 @@ int launch_t(kyro_ctx* ctx, const Args& a) {
                           a, "accept_decide_kernel"));
   if (!STOCH) return KYRO_OK;  // greedy: the decide step wrote every token
   const unsigned nfinal = (unsigned)a.B * (unsigned)((a.nchunks + kFinalPerCta - 1) / kFinalPerCta);
-  return launch_dependent(accept_final_kernel<VEC>, nfinal, kThreads, ctx->stream, a,
+  return launch_dependent(accept_final_kernel<VEC, false>, nfinal, kThreads, ctx->stream, a,
                           "accept_final_kernel");
 }
 
@@ -962,6 +1301,43 @@ int launch(kyro_ctx* ctx, Args& a, const Workspace& ws, bool vec) {
   if (vec) return launch_t<true, false>(ctx, a);
   if (a.stoch) return launch_t<false, true>(ctx, a);
   return launch_t<false, false>(ctx, a);
+}
+
+// The tensor-parallel sequence (kernels and collectives on the context's
+// stream; every rank issues the same collectives in the same order).
+template <bool VEC, bool STOCH>
+int launch_tp(kyro_ctx* ctx, const Args& a) {
+  const int64_t rows = (int64_t)a.B * a.R;
+  const long long need = ((long long)a.units + kWarps - 1) / kWarps;
+  const int resident = resident_ctas<VEC, STOCH>(ctx->num_sms);
+  const int grid = (int)(need < resident ? need : resident);
+  accept_stats_kernel<VEC, STOCH><<<grid, kThreads, 0, ctx->stream>>>(a);
+  KY_TRY(kyro::check_launch("accept_stats_kernel"));
+  const unsigned dthreads = 32u * (unsigned)(a.R < kDecideWarps ? a.R : kDecideWarps);
+  KY_TRY(launch_dependent(accept_tp_max_kernel, (unsigned)a.B, dthreads, ctx->stream, a,
+                          "accept_tp_max_kernel"));
+  KY_TRY(kyro::nccl::all_gather(ctx, a.send1, a.recv1, sizeof(TpRow1) * rows,
+                                "kyro_spec_accept_tp: row maxima"));
+  if (STOCH) {
+    accept_tp_sum_kernel<<<a.B, dthreads, 0, ctx->stream>>>(a);
+    KY_TRY(kyro::check_launch("accept_tp_sum_kernel"));
+    KY_TRY(kyro::nccl::all_gather(ctx, a.send2, a.recv2, sizeof(TpRow2) * rows,
+                                  "kyro_spec_accept_tp: normaliser parts"));
+  }
+  accept_tp_decide_kernel<<<a.B, dthreads, 0, ctx->stream>>>(a);
+  KY_TRY(kyro::check_launch("accept_tp_decide_kernel"));
+  if (!STOCH) return KYRO_OK;  // greedy: the decide step wrote every token
+  const unsigned nfinal = (unsigned)a.B * (unsigned)((a.nchunks + kFinalPerCta - 1) / kFinalPerCta);
+  KY_TRY(launch_dependent(accept_final_kernel<VEC, true>, nfinal, kThreads, ctx->stream, a,
+                          "accept_final_kernel"));
+  KY_TRY(kyro::nccl::all_gather(ctx, a.send3, a.recv3, sizeof(TpSeq3) * (size_t)a.B,
+                                "kyro_spec_accept_tp: weight totals"));
+  accept_tp_search_kernel<VEC><<<(a.B + kWarps - 1) / kWarps, kThreads, 0, ctx->stream>>>(a);
+  KY_TRY(kyro::check_launch("accept_tp_search_kernel"));
+  KY_TRY(kyro::nccl::all_reduce_max_i32(ctx, a.send4, a.recv4, (size_t)a.B,
+                                        "kyro_spec_accept_tp: token"));
+  accept_tp_write_kernel<<<(a.B + 127) / 128, 128, 0, ctx->stream>>>(a);
+  return kyro::check_launch("accept_tp_write_kernel");
 }
 
 void fill_common(Args& a, const Workspace& ws, int64_t V, int B, int R) {
@@ -977,6 +1353,10 @@ void fill_common(Args& a, const Workspace& ws, int64_t V, int B, int R) {
   a.final_rows = ws.final_rows;
   a.W = ws.W;
   a.cnt_c = ws.cnt_c;
+  a.V_global = V;
+  a.vocab_offset = 0;
+  a.tp_rank = 0;
+  a.tp_world = 1;
 }
 
 }  // namespace
@@ -1093,6 +1473,96 @@ int kyro_sample_tokens(kyro_ctx* ctx, const kyro_sample_params* p, const float* 
   a.out_probs = out_probs;
   a.status = ctx->d_status;
   return launch(ctx, a, ws, use_vec(logits, nullptr, V));
+}
+
+size_t kyro_spec_accept_tp_workspace_size(const kyro_accept_params* p, int world) {
+  if (!p || world < 1 || p->batch < 0 || p->num_draft < 0 || p->vocab <= 0 ||
+      p->vocab % world != 0)
+    return 0;
+  const bool stoch = p->mode == KYRO_ACCEPT_STOCHASTIC && p->temperature > 0.0f;
+  const int64_t R = stoch ? 2 * (int64_t)p->num_draft + 1 : (int64_t)p->num_draft + 1;
+  const int64_t nchunks = (p->vocab / world + kChunk - 1) / kChunk;
+  return carve_tp(nullptr, p->batch, R, nchunks, world).bytes;
+}
+
+int kyro_spec_accept_tp(kyro_ctx* ctx, const kyro_accept_params* p, const float* target_shard,
+                        const float* draft_shard, const int32_t* draft_tokens,
+                        int32_t* out_accept_len, int32_t* out_tokens, int32_t* out_num_tokens,
+                        float* out_probs, void* workspace, size_t workspace_bytes) {
+  KY_TRY(kyro::enter(ctx));
+  KY_REQUIRE(p, "kyro_spec_accept_tp: params is NULL");
+  const int world = ctx->tp_world;
+  if (world == 1)  // no group: the single-GPU call on the full rows
+    return kyro_spec_accept(ctx, p, target_shard, draft_shard, draft_tokens, out_accept_len,
+                            out_tokens, out_num_tokens, out_probs, workspace, workspace_bytes);
+  KY_REQUIRE(ctx->nccl_comm, "kyro_spec_accept_tp: the context has no group");
+  KY_REQUIRE(p->batch >= 0, "kyro_spec_accept_tp: batch = %d", p->batch);
+  KY_REQUIRE(p->num_draft >= 0 && p->num_draft <= kMaxDraft,
+             "kyro_spec_accept_tp: num_draft = %d (0..%d)", p->num_draft, kMaxDraft);
+  KY_REQUIRE(p->vocab > 0 && p->vocab % world == 0 &&
+                 (int64_t)(p->vocab / world) <= (int64_t)kMaxChunks * kChunk,
+             "kyro_spec_accept_tp: vocab = %d over %d ranks (a multiple of the group size, "
+             "at most %d per rank)",
+             p->vocab, world, kMaxChunks * kChunk);
+  KY_REQUIRE(p->mode >= 0 && p->mode <= 2, "kyro_spec_accept_tp: mode = %d", p->mode);
+  if (p->batch == 0) return KYRO_OK;
+  const bool stoch = p->mode == KYRO_ACCEPT_STOCHASTIC && p->temperature > 0.0f;
+  const int B = p->batch, k = p->num_draft;
+  const int64_t V = p->vocab, Vl = V / world;
+  KY_REQUIRE(target_shard, "kyro_spec_accept_tp: target_shard is NULL");
+  KY_REQUIRE(k == 0 || draft_tokens, "kyro_spec_accept_tp: draft_tokens is NULL");
+  KY_REQUIRE(!stoch || k == 0 || draft_shard,
+             "kyro_spec_accept_tp: stochastic mode needs draft_shard");
+  KY_REQUIRE(out_accept_len && out_tokens && out_num_tokens,
+             "kyro_spec_accept_tp: an output pointer is NULL");
+  const int R = stoch ? 2 * k + 1 : k + 1;
+  const int64_t nchunks = (Vl + kChunk - 1) / kChunk;
+  KY_REQUIRE((int64_t)B * R * nchunks < (1ll << 31) && (int64_t)B * R * world < (1ll << 31),
+             "kyro_spec_accept_tp: batch too large");
+  const size_t need = carve_tp(nullptr, B, R, nchunks, world).bytes;
+  if (workspace_bytes < need || !workspace)
+    return kyro::set_error(KYRO_ERR_WORKSPACE, "kyro_spec_accept_tp: workspace %zu < %zu bytes",
+                           workspace_bytes, need);
+  KY_REQUIRE((uintptr_t)workspace % 256 == 0,
+             "kyro_spec_accept_tp: workspace must be 256-byte aligned");
+  const TpWorkspace ws = carve_tp(workspace, B, R, nchunks, world);
+  Args a = {};
+  fill_common(a, ws.base, Vl, B, R);
+  a.plog = target_shard;
+  a.qlog = stoch ? draft_shard : nullptr;
+  a.draft_tokens = draft_tokens;
+  a.k = k;
+  a.inv_t = stoch ? ky_inv_temperature(p->temperature) : 1.0f;
+  a.stoch = stoch;
+  a.greedy_ref = p->mode == KYRO_ACCEPT_GREEDY_REF;
+  a.sample = 0;
+  a.pos_div = 1;
+  a.seed = p->seed;
+  a.step = p->step;
+  a.seq_offset = p->seq_offset;
+  a.out_accept_len = out_accept_len;
+  a.out_tokens = out_tokens;
+  a.out_num_tokens = out_num_tokens;
+  a.out_probs = stoch ? out_probs : nullptr;
+  a.status = ctx->d_status;
+  a.V_global = V;
+  a.vocab_offset = (int64_t)ctx->tp_rank * Vl;
+  a.tp_rank = ctx->tp_rank;
+  a.tp_world = world;
+  a.send1 = ws.send1;
+  a.recv1 = ws.recv1;
+  a.send2 = ws.send2;
+  a.recv2 = ws.recv2;
+  a.send3 = ws.send3;
+  a.recv3 = ws.recv3;
+  a.send4 = ws.send4;
+  a.recv4 = ws.recv4;
+  a.W2 = ws.W2;
+  const bool vec = use_vec(target_shard, a.qlog, Vl);
+  if (vec && stoch) return launch_tp<true, true>(ctx, a);
+  if (vec) return launch_tp<true, false>(ctx, a);
+  if (stoch) return launch_tp<false, true>(ctx, a);
+  return launch_tp<false, false>(ctx, a);
 }
 
 }  // extern "C"

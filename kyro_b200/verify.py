@@ -72,6 +72,17 @@ class Context:
             self._ws = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
         return self._ws
 
+    def tp_init(self, unique_id: bytes, rank: int, world: int):
+        """Join a tensor-parallel group (kyro_ctx_tp_init); blocks until all
+        `world` ranks have joined.  unique_id comes from tp_unique_id() on
+        rank 0, passed to the others by the caller's launcher."""
+        if len(unique_id) != _lib.TP_UNIQUE_ID_BYTES:
+            raise ValueError(f"unique_id must be {_lib.TP_UNIQUE_ID_BYTES} bytes")
+        buf = C.create_string_buffer(bytes(unique_id), _lib.TP_UNIQUE_ID_BYTES)
+        with torch.cuda.device(self.index):
+            check(_lib.load().kyro_ctx_tp_init(self._h, buf, rank, world))
+        self.tp_rank, self.tp_world = rank, world
+
     def device_status(self, clear: bool = True) -> int:
         flags = C.c_uint32(0)
         check(_lib.load().kyro_ctx_device_status(self._h, C.byref(flags), int(clear)))
@@ -125,6 +136,47 @@ def spec_accept(ctx: Context, target_logits: torch.Tensor, draft_logits: Optiona
     check(L.kyro_spec_accept(ctx.handle, C.byref(p), _ptr(target_logits), _ptr(draft_logits),
                              _ptr(draft_tokens), _ptr(acc), _ptr(toks), _ptr(num), _ptr(probs),
                              _ptr(ws), ws.numel()))
+    return acc, toks, num, probs
+
+
+def tp_unique_id() -> bytes:
+    """An NCCL unique id for kyro_ctx_tp_init (call on rank 0)."""
+    buf = C.create_string_buffer(_lib.TP_UNIQUE_ID_BYTES)
+    check(_lib.load().kyro_tp_unique_id(buf))
+    return buf.raw
+
+
+def spec_accept_tp(ctx: Context, target_shard: torch.Tensor, draft_shard: Optional[torch.Tensor],
+                   draft_tokens: torch.Tensor, vocab: int, mode: int = ACCEPT_STOCHASTIC,
+                   temperature: float = 1.0, seed: int = 0, step: int = 0, seq_offset: int = 0,
+                   want_probs: bool = False):
+    """kyro_spec_accept_tp: this rank's vocabulary columns, target_shard fp32
+    [B,k+1,V/R] and draft_shard fp32 [B,k,V/R]; draft_tokens int32 [B,k]
+    hold global ids; vocab is the full V.  Every rank returns the same
+    (accept_len [B], tokens [B,k+1], num_tokens [B], probs [B,k,2] or None)."""
+    dev = ctx.device
+    _need(target_shard, "target_shard", torch.float32, dev, 3)
+    B, k1, _ = target_shard.shape
+    k = k1 - 1
+    _need(draft_tokens, "draft_tokens", torch.int32, dev)
+    if draft_shard is not None:
+        _need(draft_shard, "draft_shard", torch.float32, dev, 3)
+    acc = torch.empty(B, dtype=torch.int32, device=dev)
+    toks = torch.empty(B, k + 1, dtype=torch.int32, device=dev)
+    num = torch.empty(B, dtype=torch.int32, device=dev)
+    probs = torch.empty(B, k, 2, dtype=torch.float32, device=dev) if want_probs else None
+    p = AcceptParams(B, k, vocab, mode, float(temperature), step & 0xFFFFFFFF,
+                     seed & 0xFFFFFFFFFFFFFFFF, seq_offset)
+    L = _lib.load()
+    world = getattr(ctx, "tp_world", 1)
+    need = L.kyro_spec_accept_tp_workspace_size(C.byref(p), world)
+    if need == 0:
+        raise ValueError(f"vocab {vocab} does not split over {world} ranks")
+    ws = ctx.workspace(need)
+    ctx.bind_stream()
+    check(L.kyro_spec_accept_tp(ctx.handle, C.byref(p), _ptr(target_shard), _ptr(draft_shard),
+                                _ptr(draft_tokens), _ptr(acc), _ptr(toks), _ptr(num),
+                                _ptr(probs), _ptr(ws), ws.numel()))
     return acc, toks, num, probs
 
 
