@@ -65,6 +65,21 @@ void ko_spec_accept(int32_t batch, int32_t k, int32_t vocab, int32_t mode, float
                     const int32_t* draft_tokens, int32_t* out_accept_len, int32_t* out_tokens,
                     int32_t* out_num_tokens, float* out_probs, int32_t nthreads);
 
+/* One rank's pieces of a vocabulary-sharded row (its contiguous columns,
+ * len entries): the shard's row max; its butterfly part of the normaliser
+ * under the global max M; e and the chunk max at one of its entries; its
+ * residual (q_shard != NULL) and p weight totals under the global row
+ * statistics; and the entry where its weights first reach T. */
+float ko_tp_row_max(const float* shard, int32_t len, float temperature);
+double ko_tp_row_sum_part(const float* shard, int32_t len, float temperature, float M);
+void ko_tp_entry(const float* shard, int32_t len, float temperature, int32_t idx, float* e,
+                 float* m_c);
+void ko_tp_weight_totals(const float* p_shard, const float* q_shard, int32_t len,
+                         float temperature, float Mp, double Sp, float Mq, double Sq,
+                         uint64_t* w_res, uint64_t* w_p);
+int32_t ko_tp_cut(const float* p_shard, const float* q_shard, int32_t len, float temperature,
+                  float Mp, double Sp, float Mq, double Sq, int32_t residual, uint64_t T);
+
 /* Paged multi-query attention in double precision.
  * q bf16 bits [B, nq, Hq, D]; caches bf16 bits [NB, Hkv, bs, D];
  * out fp32 [B, nq, Hq, D]; tree_mask may be NULL (chain). */

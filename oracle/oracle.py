@@ -56,6 +56,15 @@ def _declare(L):
     L.ko_sample_tokens.argtypes = [i32, i32, i32, f32, u64, u32, i64, vp, vp, vp, i32]
     L.ko_spec_accept.argtypes = [i32, i32, i32, i32, f32, u64, u32, i64, i32, vp, vp, vp, vp, vp,
                                  vp, vp, i32]
+    f64 = C.c_double
+    L.ko_tp_row_max.argtypes = [vp, i32, f32]
+    L.ko_tp_row_max.restype = f32
+    L.ko_tp_row_sum_part.argtypes = [vp, i32, f32, f32]
+    L.ko_tp_row_sum_part.restype = f64
+    L.ko_tp_entry.argtypes = [vp, i32, f32, i32, vp, vp]
+    L.ko_tp_weight_totals.argtypes = [vp, vp, i32, f32, f32, f64, f32, f64, vp, vp]
+    L.ko_tp_cut.argtypes = [vp, vp, i32, f32, f32, f64, f32, f64, i32, u64]
+    L.ko_tp_cut.restype = i32
     L.ko_paged_attention.argtypes = [i32, i32, i32, i32, i32, i32, i32, f32, vp, vp, vp, vp, vp,
                                      vp, vp, i32]
     L.ko_kv_reserve.argtypes = [i32, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp]
@@ -114,6 +123,46 @@ def spec_accept(target_logits, draft_logits, draft_tokens, mode=MODE_STOCHASTIC,
     lib().ko_spec_accept(B, k, V, mode, temperature, seed, step, seq_offset, num_shards, _p(tg),
                          _p(dr), _p(dt), _p(acc), _p(toks), _p(num), _p(probs), nthreads)
     return acc, toks, num, probs
+
+
+# ---- one rank's pieces of a vocabulary-sharded row (test infrastructure for
+# the tensor-parallel exchange; rank order combination happens in the caller)
+
+def _f32row(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def tp_row_max(shard, temperature: float) -> float:
+    r = _f32row(shard)
+    return float(lib().ko_tp_row_max(_p(r), r.size, temperature))
+
+
+def tp_row_sum_part(shard, temperature: float, M: float) -> float:
+    r = _f32row(shard)
+    return float(lib().ko_tp_row_sum_part(_p(r), r.size, temperature, M))
+
+
+def tp_entry(shard, temperature: float, idx: int):
+    r = _f32row(shard)
+    e, m = C.c_float(), C.c_float()
+    lib().ko_tp_entry(_p(r), r.size, temperature, idx, C.byref(e), C.byref(m))
+    return e.value, m.value
+
+
+def tp_weight_totals(p_shard, q_shard, temperature, Mp, Sp, Mq, Sq):
+    p = _f32row(p_shard)
+    q = None if q_shard is None else _f32row(q_shard)
+    a, b = C.c_uint64(), C.c_uint64()
+    lib().ko_tp_weight_totals(_p(p), _p(q), p.size, temperature, Mp, Sp, Mq, Sq, C.byref(a),
+                              C.byref(b))
+    return a.value, b.value
+
+
+def tp_cut(p_shard, q_shard, temperature, Mp, Sp, Mq, Sq, residual: bool, T: int) -> int:
+    p = _f32row(p_shard)
+    q = None if q_shard is None else _f32row(q_shard)
+    return int(lib().ko_tp_cut(_p(p), _p(q), p.size, temperature, Mp, Sp, Mq, Sq, int(residual),
+                               T))
 
 
 def paged_attention(q_bits, k_bits, v_bits, block_table, context_lens, block_size, scale=None,

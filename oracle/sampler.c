@@ -167,6 +167,133 @@ void ko_softmax_row(const float* row, int32_t vocab, int32_t num_shards, float t
 }
 
 /* ------------------------------------------------------------------ */
+/* one rank's columns under tensor parallelism                          */
+/* ------------------------------------------------------------------ */
+/* The pieces each rank of a vocabulary-sharded group computes on its own
+ * columns (a contiguous shard, chunks starting at the shard start; the
+ * shard rule of src/distributed.rs:90-98).  Combined across ranks in rank
+ * order they give exactly the num_shards statistics of rowstat_init. */
+
+/* chunk maxima and sums of one shard */
+static int32_t shard_chunks(const float* shard, int32_t len, float inv_t, float** m_out,
+                            float** E_out) {
+  ko_rowstat st;
+  rowstat_init(&st, shard, len, 1, inv_t);
+  int32_t nc = st.chunks_per_shard;
+  float* E = (float*)malloc(sizeof(float) * (size_t)nc);
+  for (int32_t c = 0; c < nc; ++c) {
+    float e[KY_CHUNK];
+    for (int32_t p = 0; p < KY_CHUNK; ++p) {
+      int32_t i = c * KY_CHUNK + p;
+      float s = i < len ? KY_FMUL(shard[i], inv_t) : -INFINITY;
+      e[p] = ky_exp(KY_FSUB(s, st.m[c]));
+    }
+    E[c] = ky_chunk_sum(e);
+  }
+  float* m = (float*)malloc(sizeof(float) * (size_t)nc);
+  memcpy(m, st.m, sizeof(float) * (size_t)nc);
+  rowstat_free(&st);
+  *m_out = m;
+  *E_out = E;
+  return nc;
+}
+
+float ko_tp_row_max(const float* shard, int32_t len, float temperature) {
+  float *m, *E;
+  int32_t nc = shard_chunks(shard, len, ky_inv_temperature(temperature), &m, &E);
+  float M = -INFINITY;
+  for (int32_t c = 0; c < nc; ++c)
+    if (m[c] > M) M = m[c];
+  free(m);
+  free(E);
+  return M;
+}
+
+double ko_tp_row_sum_part(const float* shard, int32_t len, float temperature, float M) {
+  float *m, *E;
+  int32_t nc = shard_chunks(shard, len, ky_inv_temperature(temperature), &m, &E);
+  double t[32];
+  for (int32_t l = 0; l < 32; ++l) {
+    t[l] = 0.0;
+    for (int32_t c = l; c < nc; c += 32) t[l] = KY_DADD(t[l], ky_chunk_mass(E[c], m[c], M));
+  }
+  free(m);
+  free(E);
+  return ky_butterfly32(t);
+}
+
+void ko_tp_entry(const float* shard, int32_t len, float temperature, int32_t idx, float* e,
+                 float* m_c) {
+  float inv_t = ky_inv_temperature(temperature);
+  float *m, *E;
+  shard_chunks(shard, len, inv_t, &m, &E);
+  *m_c = m[idx / KY_CHUNK];
+  *e = ky_exp(KY_FSUB(KY_FMUL(shard[idx], inv_t), *m_c));
+  free(m);
+  free(E);
+}
+
+/* Weights of the shard under the global row statistics (Mp, Sp) of p and
+ * (Mq, Sq) of q; q_shard NULL samples from p.  w[i] = residual (or p)
+ * weight, wp[i] = p weight. */
+static void shard_weights(const float* p_shard, const float* q_shard, int32_t len, float inv_t,
+                          float Mp, double Sp, float Mq, double Sq, uint64_t* w, uint64_t* wp) {
+  float *mp, *Ep, *mq = NULL, *Eq = NULL;
+  shard_chunks(p_shard, len, inv_t, &mp, &Ep);
+  if (q_shard) shard_chunks(q_shard, len, inv_t, &mq, &Eq);
+  for (int32_t i = 0; i < len; ++i) {
+    int32_t c = i / KY_CHUNK;
+    float ep = ky_exp(KY_FSUB(KY_FMUL(p_shard[i], inv_t), mp[c]));
+    float gp62 = ky_scale62(ky_chunk_scale(mp[c], Mp, Sp));
+    wp[i] = ky_weight_p(ep, gp62);
+    if (q_shard) {
+      float eq = ky_exp(KY_FSUB(KY_FMUL(q_shard[i], inv_t), mq[c]));
+      w[i] = ky_weight_residual(ep, gp62, eq, ky_scale62(ky_chunk_scale(mq[c], Mq, Sq)));
+    } else {
+      w[i] = wp[i];
+    }
+  }
+  free(mp);
+  free(Ep);
+  free(mq);
+  free(Eq);
+}
+
+void ko_tp_weight_totals(const float* p_shard, const float* q_shard, int32_t len,
+                         float temperature, float Mp, double Sp, float Mq, double Sq,
+                         uint64_t* w_res, uint64_t* w_p) {
+  uint64_t* w = (uint64_t*)malloc(sizeof(uint64_t) * (size_t)len);
+  uint64_t* wp = (uint64_t*)malloc(sizeof(uint64_t) * (size_t)len);
+  shard_weights(p_shard, q_shard, len, ky_inv_temperature(temperature), Mp, Sp, Mq, Sq, w, wp);
+  uint64_t a = 0, b = 0;
+  for (int32_t i = 0; i < len; ++i) {
+    a += w[i];
+    b += wp[i];
+  }
+  *w_res = a;
+  *w_p = b;
+  free(w);
+  free(wp);
+}
+
+int32_t ko_tp_cut(const float* p_shard, const float* q_shard, int32_t len, float temperature,
+                  float Mp, double Sp, float Mq, double Sq, int32_t residual, uint64_t T) {
+  uint64_t* w = (uint64_t*)malloc(sizeof(uint64_t) * (size_t)len);
+  uint64_t* wp = (uint64_t*)malloc(sizeof(uint64_t) * (size_t)len);
+  shard_weights(p_shard, q_shard, len, ky_inv_temperature(temperature), Mp, Sp, Mq, Sq, w, wp);
+  const uint64_t* use = residual ? w : wp;
+  int32_t found = -1;
+  uint64_t C = 0;
+  for (int32_t i = 0; i < len && found < 0; ++i) {
+    C += use[i];
+    if (C >= T) found = i;
+  }
+  free(w);
+  free(wp);
+  return found;
+}
+
+/* ------------------------------------------------------------------ */
 /* draft sampler                                                        */
 /* ------------------------------------------------------------------ */
 typedef struct {
