@@ -508,6 +508,151 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_tp(args):
+    """Config 3: vocabulary-sharded acceptance (kyro_spec_accept_tp) over the
+    N ranks of one tensor-parallel group, plus KV reserve/commit on a
+    32768-block table.  Total work is fixed as N grows (strong scaling):
+    each rank holds V/N columns of the same [256, 9 | 8, V] logits."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from kyro_b200.verify import (Context, kv_commit, kv_reserve, spec_accept_tp,
+                                  tp_unique_id)
+    from kyro_b200.workloads import CONFIG3, paged_state
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    cfg = CONFIG3
+    B, k, V, T = cfg.batch, cfg.k, cfg.vocab, cfg.temperature
+    if V % world:
+        raise SystemExit(f"vocab {V} does not split over {world} ranks")
+    Vs = V // world
+    ctx = Context(local)
+    if world > 1:
+        uid = torch.zeros(128, dtype=torch.uint8, device=dev)
+        if rank == 0:
+            uid.copy_(torch.frombuffer(bytearray(tp_unique_id()), dtype=torch.uint8))
+        dist.broadcast(uid, 0)
+        ctx.tp_init(bytes(uid.cpu().numpy().tobytes()), rank, world)
+
+    def shard(r):  # rank r's columns of the (never materialised) full logits
+        g = torch.Generator(device=dev).manual_seed(5000 + r)
+        t = torch.randn(B, k + 1, Vs, generator=g, device=dev) * cfg.logit_std
+        d = t[:, :k, :] + torch.randn(B, k, Vs, generator=g, device=dev) * cfg.draft_noise
+        return t.contiguous(), d.contiguous()
+
+    tgt, drf = shard(rank)
+    # draft tokens sampled from the full draft rows (rank 0 regenerates every
+    # shard once, before the timed region) and broadcast
+    drafts = torch.zeros(B, k, dtype=torch.int32, device=dev)
+    if rank == 0:
+        full = torch.cat([shard(r)[1] for r in range(world)], dim=2)
+        g = torch.Generator(device=dev).manual_seed(6000)
+        probs = torch.softmax(full.reshape(B * k, V) / T, dim=1)
+        drafts.copy_(torch.multinomial(probs, 1, generator=g).reshape(B, k).int())
+        del full, probs
+    if world > 1:
+        dist.broadcast(drafts, 0)
+    st = paged_state(cfg, dev, seed=7000, fill_cache=False)
+    snap = {n: getattr(st, n).clone() for n in
+            ("block_table", "context_lens", "free_stack", "free_top", "ref_counts")}
+    nq = k + 1
+    ok = torch.empty(B, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    ev = []
+
+    def step(i, timed):
+        for n, t in snap.items():
+            getattr(st, n).copy_(t, non_blocking=True)
+        kv_reserve(ctx, nq, st.block_table, st.context_lens, st.free_stack, st.free_top,
+                   st.ref_counts, cfg.block_size, out_ok=ok)
+        if timed:
+            e0 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+        acc, _, _, _ = spec_accept_tp(ctx, tgt, drf, drafts, V, temperature=T, seed=0, step=i)
+        if timed:
+            e1 = torch.cuda.Event(enable_timing=True)
+            e1.record(stream)
+            ev.append((e0, e1))
+        kv_commit(ctx, nq, acc, st.block_table, st.context_lens, st.free_stack, st.free_top,
+                  st.ref_counts, cfg.block_size)
+        return acc
+
+    for i in range(args.warmup):
+        step(i, False)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = None
+    if rank == 0:
+        try:
+            clocks = NvmlClockSampler(local)
+        except Exception:
+            clocks = ClockSampler(local)
+        clocks.start()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    accs = []
+    for i in range(args.warmup, args.warmup + args.steps):
+        accs.append(step(i, True))
+    t1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop() if clocks else None
+    ms = t0.elapsed_time(t1)
+    acc_ms = float(np.mean([a.elapsed_time(b) for a, b in ev]))
+    if world > 1:
+        t = torch.tensor([ms, acc_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, acc_ms = float(t[0]), float(t[1])
+    status = ctx.device_status()
+    if status:
+        raise SystemExit(f"device status word 0x{status:x} after the timed region")
+    rate = float(torch.stack(accs).float().mean().item()) / k
+    peak, peak_kind = load_peaks()
+    rank_bytes = (2 * k + 1) * B * Vs * 4  # every logit of this rank's columns once
+    achieved = rank_bytes / (acc_ms * 1e-3) / 1e9
+    if rank == 0:
+        line = {
+            "metric": "TP spec-accept verified positions/s (config 3)", "unit": UNIT,
+            "value": B * nq * args.steps / (ms * 1e-3), "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded; BASELINE config 3 shapes and distributions)",
+            "config": {"workload": "config3: vocabulary-sharded acceptance (B 256, k 8, "
+                                   f"V 128256 over {world} ranks, T 0.8) + KV reserve/commit "
+                                   "on a 32768-block table",
+                       "global_batch": B, "k": k, "vocab": V, "columns_per_rank": Vs,
+                       "parallelism": f"tp{world} (vocabulary)",
+                       "l2": f"{rank_bytes / 1e9:.2f} GB of logits per rank per step"},
+            "roofline": {"bound": "hbm", "kernel": "kyro_spec_accept_tp (per rank)",
+                         "achieved": achieved, "peak": peak, "peak_kind": peak_kind,
+                         "unit": "GB/s", "frac": achieved / peak, "traffic": None},
+            "accept_ms": acc_ms, "acceptance_rate": rate,
+            "gpu_launches": (2 + (7 if world > 1 else 3)) * args.steps,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -521,11 +666,16 @@ def main():
                     help="wall time the cpu_baseline leg repeats whole-batch steps for")
     ap.add_argument("--no-e2e", action="store_true",
                     help="skip the host-buffer leg (profiling runs)")
+    ap.add_argument("--config", choices=["1", "3"], default="1",
+                    help="1: chain verify step (the headline); 3: vocabulary-sharded "
+                         "acceptance over the N ranks of one TP group")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         raise SystemExit("--warmup must be >= 3")
     if args.impl == "reference":
         run_reference(args)
+    elif args.config == "3":
+        run_tp(args)
     else:
         run_ours(args)
 

@@ -51,6 +51,12 @@ class ChainConfig:
 
 CONFIG0 = dict(batch=8, k=4, vocab=32000)
 CONFIG1 = ChainConfig()
+# Config 3: vocabulary-sharded acceptance and KV commit on a 32768-block
+# table (the table only: a one-head, 8-wide cache keeps the K/V arrays small;
+# contexts U[256, 1800] fit 256 sequences plus growth in the pool).
+CONFIG3 = ChainConfig(batch=256, k=8, num_heads=1, num_kv_heads=1, head_dim=8,
+                      num_blocks=32768, ctx_min=256, ctx_max=1800, vocab=128256,
+                      temperature=0.8, headroom_tokens=128)
 
 
 def accept_inputs(batch: int, k: int, vocab: int, device, seed: int = 0, std: float = 3.0,
