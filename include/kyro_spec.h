@@ -279,6 +279,47 @@ int kyro_kv_write(kyro_ctx* ctx, const kyro_kv_params* p, int32_t num_new, int32
                   const int64_t* block_table, const int64_t* context_lens, void* k_cache,
                   void* v_cache);
 
+/* ------------------------------------------------- tree acceptance */
+
+/* Verification of a draft tree instead of a chain.  The reference has no
+ * tree path; the rule is multi-candidate rejection sampling (SpecInfer,
+ * Miao et al. 2023) with the arithmetic of kyro_math.h: at each node the
+ * children are tried in index order against the target / draft
+ * distributions of their parent, each rejection replaces p by
+ * norm(max(p - q, 0)), an accepted child becomes the next node, and when
+ * every child is rejected (or the node is a leaf) one token is drawn from
+ * the current p.  Greedy modes accept the first child whose token is the
+ * target's argmax and otherwise emit the argmax (speculative.rs:314-323 per
+ * node). */
+typedef struct kyro_tree_params {
+  int32_t batch;       /* B                                                */
+  int32_t num_nodes;   /* N <= 64, BFS order, node 0 = the root            */
+  int32_t vocab;       /* V                                                */
+  int32_t mode;        /* KYRO_ACCEPT_*                                    */
+  float temperature;
+  uint32_t step;       /* Philox counter word 3                            */
+  uint64_t seed;       /* Philox key                                       */
+  int64_t seq_offset;  /* global index of sequence 0                       */
+} kyro_tree_params;
+
+size_t kyro_spec_accept_tree_workspace_size(const kyro_tree_params* p);
+
+/*   target_logits fp32 [B, N, V]  the target's next-token logits at node n
+ *   draft_logits  fp32 [B, N, V]  the draft's, which node n's children were
+ *                                 sampled from (NULL in greedy modes)
+ *   node_tokens   int32 [B, N]    the token of node n (the root's is unused)
+ *   parents       int32 [B, N]    parent of node n; -1 for the root; a
+ *                                 parent precedes its children
+ * Outputs: out_path [B, N] the accepted nodes, root first, -1 padded (the
+ * path kyro_kv_commit_tree takes); out_path_len [B]; out_tokens [B, N] the
+ * emitted tokens (the path's tokens after the root, then the drawn one),
+ * -1 padded; out_num_tokens [B] (== out_path_len). */
+int kyro_spec_accept_tree(kyro_ctx* ctx, const kyro_tree_params* p, const float* target_logits,
+                          const float* draft_logits, const int32_t* node_tokens,
+                          const int32_t* parents, int32_t* out_path, int32_t* out_path_len,
+                          int32_t* out_tokens, int32_t* out_num_tokens, void* workspace,
+                          size_t workspace_bytes);
+
 /* ------------------------------------- tensor parallelism (vocab shards) */
 
 /* The lm_head / vocabulary dimension split over a tensor-parallel group as

@@ -45,7 +45,7 @@ EXPORTS = (
     "kyro_kv_reserve", "kyro_kv_commit", "kyro_kv_commit_tree", "kyro_kv_write",
     "kyro_philox_uniforms", "kyro_selftest_exp",
     "kyro_tp_unique_id", "kyro_ctx_tp_init", "kyro_spec_accept_tp_workspace_size",
-    "kyro_spec_accept_tp",
+    "kyro_spec_accept_tp", "kyro_spec_accept_tree_workspace_size", "kyro_spec_accept_tree",
 )
 
 TP_UNIQUE_ID_BYTES = 128
@@ -53,6 +53,12 @@ TP_UNIQUE_ID_BYTES = 128
 
 class AcceptParams(C.Structure):
     _fields_ = [("batch", C.c_int32), ("num_draft", C.c_int32), ("vocab", C.c_int32),
+                ("mode", C.c_int32), ("temperature", C.c_float), ("step", C.c_uint32),
+                ("seed", C.c_uint64), ("seq_offset", C.c_int64)]
+
+
+class TreeParams(C.Structure):
+    _fields_ = [("batch", C.c_int32), ("num_nodes", C.c_int32), ("vocab", C.c_int32),
                 ("mode", C.c_int32), ("temperature", C.c_float), ("step", C.c_uint32),
                 ("seed", C.c_uint64), ("seq_offset", C.c_int64)]
 
@@ -121,6 +127,9 @@ def load():
         "kyro_philox_uniforms": (C.c_int, [vp, u64, u32, u32, u32, u32, i32, vp]),
         "kyro_selftest_exp": (C.c_int, [vp, vp]),
         "kyro_tp_unique_id": (C.c_int, [vp]),
+        "kyro_spec_accept_tree_workspace_size": (C.c_size_t, [vp]),
+        "kyro_spec_accept_tree": (C.c_int, [vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp,
+                                            C.c_size_t]),
         "kyro_ctx_tp_init": (C.c_int, [vp, vp, C.c_int, C.c_int]),
         "kyro_spec_accept_tp_workspace_size": (C.c_size_t, [vp, C.c_int]),
         "kyro_spec_accept_tp": (C.c_int, [vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, C.c_size_t]),

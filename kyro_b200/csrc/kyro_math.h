@@ -60,6 +60,7 @@
 #define KY_FDIV(a, b) __fdiv_rn((a), (b))
 #define KY_DMUL(a, b) __dmul_rn((a), (b))
 #define KY_DADD(a, b) __dadd_rn((a), (b))
+#define KY_DSUB(a, b) __dsub_rn((a), (b))
 #define KY_DDIV(a, b) __ddiv_rn((a), (b))
 #else
 #define KY_FMAF(a, b, c) fmaf((a), (b), (c))
@@ -69,6 +70,7 @@
 #define KY_FDIV(a, b) ((float)(a) / (float)(b))
 #define KY_DMUL(a, b) ((double)(a) * (double)(b))
 #define KY_DADD(a, b) ((double)(a) + (double)(b))
+#define KY_DSUB(a, b) ((double)(a) - (double)(b))
 #define KY_DDIV(a, b) ((double)(a) / (double)(b))
 #endif
 
@@ -326,6 +328,60 @@ KY_HD uint64_t ky_weight_p(float e, float g62) { return ky_f2u64_rz(KY_FMUL(e, g
 KY_HD uint64_t ky_weight_residual(float ep, float g62p, float eq, float g62q) {
   const float d = KY_FSUB(KY_FMUL(ep, g62p), KY_FMUL(eq, g62q));
   return d > 0.0f ? ky_f2u64_rz(d) : 0ull;
+}
+
+/* ------------------------------------------------------------------ */
+/* tree verification                                                    */
+/* ------------------------------------------------------------------ */
+/* Multi-candidate rejection sampling over a draft tree (SpecInfer, Miao et
+ * al. 2023).  At a node with target distribution p and draft distribution
+ * q (the contract's fp32 p_i and q_i, widened to double), the children are
+ * tried in index order; child c with token x is accepted iff
+ * u_c < p_j(x) / q(x) (double division), where j children have been
+ * rejected so far and
+ *   p_0(i) = p_i,
+ *   p_{j+1}(i) = max(p_j(i) - q_i, 0) / R_j   with   R_j = sum_i max(p_j(i) - q_i, 0),
+ * and p_{j+1} = p_j when R_j == 0 (then p_j == q and the next child is
+ * accepted).  R_j is summed in one fixed tree: each 512-entry chunk by
+ * ky_chunk_sum_d (ky_chunk_sum's tree in double; entries past V are 0),
+ * the chunk sums by the 32-lane butterfly of the normaliser (chunks
+ * c = l, l+32, ... into lane l, then ky_butterfly32).  A node whose
+ * children are all rejected draws from p_J, a leaf from p_0, with integer
+ * weights floor(p_J(i) * 2^62) and the chain's inverse-CDF threshold. */
+
+KY_HD double ky_tree_step(double p, double q, double R) {
+  if (R == 0.0) return p;
+  const double d = KY_DSUB(p, q);
+  return d > 0.0 ? KY_DDIV(d, R) : 0.0;
+}
+
+/* max(p - q, 0), the term of R_j */
+KY_HD double ky_tree_excess(double p, double q) {
+  const double d = KY_DSUB(p, q);
+  return d > 0.0 ? d : 0.0;
+}
+
+/* ky_chunk_sum's lane tree in double */
+KY_HD double ky_chunk_sum_d(const double e[KY_CHUNK]) {
+  double lanes[32];
+  for (int l = 0; l < 32; ++l) {
+    double acc[4];
+    for (int j = 0; j < 4; ++j) {
+      acc[j] = 0.0;
+      for (int i = 0; i < 4; ++i) acc[j] = KY_DADD(acc[j], e[(i * 32 + l) * 4 + j]);
+    }
+    lanes[l] = KY_DADD(KY_DADD(acc[0], acc[1]), KY_DADD(acc[2], acc[3]));
+  }
+  return ky_butterfly32(lanes);
+}
+
+/* floor(w * 2^62) for a probability w in [0, 1] */
+KY_HD uint64_t ky_weight_d(double w) {
+#if defined(__CUDA_ARCH__)
+  return __double2ull_rz(KY_DMUL(w, 0x1p62));
+#else
+  return (uint64_t)(w * 0x1p62);
+#endif
 }
 
 #endif /* KYRO_MATH_H */

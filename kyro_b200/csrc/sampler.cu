@@ -148,6 +148,14 @@ struct Args {
   TpSeq3 *send3, *recv3;        // [B], [world][B]
   int32_t *send4, *recv4;       // [B]
   unsigned long long* W2;       // [B][nchunks][2]: residual and p weight sums
+  // tree verification: rows per sequence are k+1 = N target rows, then
+  // q_rows draft rows (k for the chain)
+  int q_rows;
+  int tree;
+  const int32_t* node_tokens;   // [B, N]
+  const int32_t* parents;       // [B, N]
+  int32_t* out_path;            // [B, N]
+  int32_t* out_path_len;        // [B]
 };
 
 __host__ __device__ inline size_t align_up(size_t x) { return (x + 255) & ~size_t(255); }
@@ -353,11 +361,11 @@ __device__ __forceinline__ f2_t exp_pair(f2_t x) {
 
 __device__ __forceinline__ const float* stats_row_ptr(const Args& a, int b, int r) {
   if (r <= a.k) return a.plog + ((int64_t)b * (a.k + 1) + r) * a.V;
-  return a.qlog + ((int64_t)b * a.k + (r - a.k - 1)) * a.V;
+  return a.qlog + ((int64_t)b * a.q_rows + (r - a.k - 1)) * a.V;
 }
 
 __device__ __forceinline__ int draft_token_of_row(const Args& a, int b, int r) {
-  if (a.sample) return -1;
+  if (a.sample || a.tree) return -1;
   if (r < a.k) return a.draft_tokens[(int64_t)b * a.k + r];
   if (r > a.k) return a.draft_tokens[(int64_t)b * a.k + (r - a.k - 1)];
   return -1;
@@ -1243,6 +1251,272 @@ __global__ void accept_tp_write_kernel(Args a) {
   if (!fr.skip) a.out_tokens[fr.out_index] = a.recv4[b];
 }
 
+// ------------------------------------------------------------ tree verification
+//
+// Multi-candidate rejection sampling over a BFS-ordered draft tree
+// (SpecInfer), as kyro_math.h states it: one CTA walks one sequence's tree.
+// Every node row's chunk statistics come from the stats kernel; a rejection
+// costs one CTA-wide pass over the node's target and draft rows that sums
+// R_j in the contract's tree (warps own chunks, warp 0 combines them), and
+// the final draw sums integer weights per chunk and scans one chunk.
+
+constexpr int kTreeThreads = 1024;
+constexpr int kTreeWarps = kTreeThreads / 32;
+constexpr int kMaxNodes = 64;
+
+struct TreeShared {
+  float mP[kMaxChunks], gP[kMaxChunks], mQ[kMaxChunks], gQ[kMaxChunks];
+  double csum[kMaxChunks];  // chunk sums of R_j, or (as u64) of the weights
+  double R[kMaxNodes];
+  int ch[kMaxNodes];
+  int nch, node, accepted, token, done;
+};
+
+// The contract's p_i and q_i of 4 entries at e0 (fp32, then widened), and
+// p_nr after nr residual steps; entries past V are marked invalid.
+template <bool VEC>
+__device__ __forceinline__ void tree_values4(const Args& a, const TreeShared& sh,
+                                             const float* prow, const float* qrow, int c,
+                                             int64_t e0, int nr, double (&pd)[4],
+                                             double (&qd)[4], bool (&ok)[4]) {
+  const float4 zp = load4<VEC>(prow, e0, a.V);
+  const float4 zq = load4<VEC>(qrow, e0, a.V);
+  const float p4[4] = {zp.x, zp.y, zp.z, zp.w};
+  const float q4[4] = {zq.x, zq.y, zq.z, zq.w};
+  const f2_t mm = f2_pack(sh.mP[c], sh.mQ[c]);
+  const f2_t gg = f2_pack(sh.gP[c], sh.gQ[c]);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    f2_t z = f2_pack(p4[j], q4[j]);
+    if (a.inv_t != 1.0f) z = f2_mul(z, f2_pack(a.inv_t, a.inv_t));
+    float pf, qf;
+    f2_unpack(f2_mul(exp_pair(f2_sub(z, mm)), gg), pf, qf);
+    ok[j] = e0 + j < a.V;
+    qd[j] = (double)qf;
+    double v = (double)pf;
+    for (int r = 0; r < nr; ++r) v = ky_tree_step(v, qd[j], sh.R[r]);
+    pd[j] = v;
+  }
+}
+
+template <bool VEC, bool STOCH>
+__global__ void __launch_bounds__(kTreeThreads) accept_tree_kernel(Args a) {
+  __shared__ TreeShared sh;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int b = blockIdx.x;
+  const int N = a.k + 1;
+  const int nc = a.nchunks;
+  const uint32_t seq = (uint32_t)(a.seq_offset + b);
+  const int32_t* tok = a.node_tokens + (int64_t)b * N;
+  const int32_t* par = a.parents + (int64_t)b * N;
+  grid_dependency_wait();  // the chunk statistics are complete
+  for (int n = threadIdx.x; n < N; n += kTreeThreads) {
+    a.out_path[(int64_t)b * N + n] = -1;
+    a.out_tokens[(int64_t)b * N + n] = -1;
+  }
+  int plen = 1, ntok = 0;  // thread 0's counts
+  if (threadIdx.x == 0) {
+    sh.node = 0;
+    sh.done = 0;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) a.out_path[(int64_t)b * N] = 0;
+  while (!sh.done) {
+    const int node = sh.node;
+    if (threadIdx.x == 0) {
+      int m = 0;
+      for (int c = node + 1; c < N; ++c)
+        if (par[c] == node) sh.ch[m++] = c;
+      sh.nch = m;
+      sh.accepted = -1;
+    }
+    if (!STOCH) {
+      if (warp == 0) {
+        const RowStat rs = row_stat(a, (int64_t)b * a.R + node);
+        if (lane == 0) sh.token = rs.arg;
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        for (int i = 0; i < sh.nch && sh.accepted < 0; ++i)
+          if (tok[sh.ch[i]] == sh.token) sh.accepted = sh.ch[i];
+      }
+      __syncthreads();
+    } else {
+      // row statistics of the node's target (warp 0) and draft (warp 1) rows
+      if (warp < 2) {
+        const RowStat rs = row_stat(a, (int64_t)b * a.R + (warp == 0 ? node : N + node));
+        if (lane == 0) {
+          if (warp == 0) {
+            sh.R[kMaxNodes - 1] = rs.S;  // parked until the chunk factors are made
+            sh.mP[0] = rs.M;
+          } else {
+            sh.csum[0] = rs.S;
+            sh.mQ[0] = rs.M;
+          }
+        }
+      }
+      __syncthreads();
+      const float Mp = sh.mP[0], Mq = sh.mQ[0];
+      const double Sp = sh.R[kMaxNodes - 1], Sq = sh.csum[0];
+      __syncthreads();
+      const ChunkStat* stp = a.stats + ((int64_t)b * a.R + node) * nc;
+      const ChunkStat* stq = a.stats + ((int64_t)b * a.R + N + node) * nc;
+      for (int c = threadIdx.x; c < nc; c += kTreeThreads) {
+        const float mp = stp[c].m, mq = stq[c].m;
+        sh.mP[c] = mp;
+        sh.gP[c] = ky_chunk_scale(mp, Mp, Sp);
+        sh.mQ[c] = mq;
+        sh.gQ[c] = ky_chunk_scale(mq, Mq, Sq);
+      }
+      __syncthreads();
+      const float* prow = stats_row_ptr(a, b, node);
+      const float* qrow = stats_row_ptr(a, b, N + node);
+      int nr = 0;
+      for (int i = 0; i < sh.nch; ++i) {
+        const int c = sh.ch[i];
+        if (threadIdx.x == 0) {
+          const int x = tok[c];
+          if (x >= 0 && x < a.V) {
+            const int cx = x / kChunk;
+            float sp = prow[x], sq = qrow[x];
+            if (a.inv_t != 1.0f) {
+              sp = KY_FMUL(sp, a.inv_t);
+              sq = KY_FMUL(sq, a.inv_t);
+            }
+            const double qx = (double)KY_FMUL(exp_fast(KY_FSUB(sq, sh.mQ[cx])), sh.gQ[cx]);
+            double px = (double)KY_FMUL(exp_fast(KY_FSUB(sp, sh.mP[cx])), sh.gP[cx]);
+            for (int r = 0; r < nr; ++r) px = ky_tree_step(px, qx, sh.R[r]);
+            const double u =
+                (double)ky_odd_to_float(ky_uniform_odd(a.seed, seq, (uint32_t)c, KY_STREAM_ACCEPT,
+                                                       a.step));
+            if (u < KY_DDIV(px, qx)) sh.accepted = c;
+          } else {
+            kyro::dev::flag(a.status, KYRO_DEV_BAD_TOKEN);
+          }
+        }
+        __syncthreads();
+        if (sh.accepted >= 0) break;
+        // rejected: R_nr over the vocabulary in the contract's tree
+        for (int cc = warp; cc < nc; cc += kTreeWarps) {
+          double acc[4] = {0.0, 0.0, 0.0, 0.0};
+#pragma unroll
+          for (int g = 0; g < kVec; ++g) {
+            double pd[4], qd[4];
+            bool ok[4];
+            tree_values4<VEC>(a, sh, prow, qrow, cc,
+                              (int64_t)cc * kChunk + (g * 32 + lane) * 4, nr, pd, qd, ok);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              acc[j] = KY_DADD(acc[j], ok[j] ? ky_tree_excess(pd[j], qd[j]) : 0.0);
+          }
+          const double t =
+              warp_butterfly(KY_DADD(KY_DADD(acc[0], acc[1]), KY_DADD(acc[2], acc[3])));
+          if (lane == 0) sh.csum[cc] = t;
+        }
+        __syncthreads();
+        if (warp == 0) {
+          double t = 0.0;
+          for (int cc = lane; cc < nc; cc += 32) t = KY_DADD(t, sh.csum[cc]);
+          t = warp_butterfly(t);
+          if (lane == 0) sh.R[nr] = t;
+        }
+        __syncthreads();
+        ++nr;
+      }
+      if (sh.accepted < 0) {
+        // draw from p_nr: integer weights, chunk sums, then one chunk's scan
+        unsigned long long* wsum = reinterpret_cast<unsigned long long*>(sh.csum);
+        for (int cc = warp; cc < nc; cc += kTreeWarps) {
+          unsigned long long t = 0;
+#pragma unroll
+          for (int g = 0; g < kVec; ++g) {
+            double pd[4], qd[4];
+            bool ok[4];
+            tree_values4<VEC>(a, sh, prow, qrow, cc,
+                              (int64_t)cc * kChunk + (g * 32 + lane) * 4, nr, pd, qd, ok);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) t += ok[j] ? ky_weight_d(pd[j]) : 0ull;
+          }
+          t = warp_sum(t);
+          if (lane == 0) wsum[cc] = t;
+        }
+        __syncthreads();
+        if (warp == 0) {
+          unsigned long long tot = 0;
+          for (int cc = lane; cc < nc; cc += 32) tot += wsum[cc];
+          tot = warp_sum(tot);
+          int token = (int)a.V - 1;
+          if (tot != 0) {
+            unsigned long long T = ky_cdf_threshold(
+                ky_uniform_odd(a.seed, seq, (uint32_t)node, KY_STREAM_RESAMPLE, a.step), tot);
+            int sub = -1;
+            unsigned long long base = 0;
+            for (int s0 = 0; s0 < nc && sub < 0; s0 += 32) {
+              const unsigned long long ws = s0 + lane < nc ? wsum[s0 + lane] : 0ull;
+              const unsigned long long inc = base + warp_inclusive(ws);
+              const unsigned hit = __ballot_sync(0xffffffffu, inc >= T && s0 + lane < nc);
+              if (hit) {
+                const int l = __ffs(hit) - 1;
+                sub = s0 + l;
+                T -= __shfl_sync(0xffffffffu, inc - ws, l);
+              } else {
+                base = __shfl_sync(0xffffffffu, inc, 31);
+              }
+            }
+            if (sub >= 0) {
+              unsigned long long cbase = 0;
+              int found = -1;
+              for (int g = 0; g < kVec; ++g) {
+                double pd[4], qd[4];
+                bool ok[4];
+                tree_values4<VEC>(a, sh, prow, qrow, sub,
+                                  (int64_t)sub * kChunk + (g * 32 + lane) * 4, nr, pd, qd, ok);
+                unsigned long long w[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) w[j] = ok[j] ? ky_weight_d(pd[j]) : 0ull;
+                const unsigned long long s4 = (w[0] + w[1]) + (w[2] + w[3]);
+                const unsigned long long inc = warp_inclusive(s4);
+                unsigned long long C = cbase + inc - s4;
+                int mine = -1;
+                if (C < T && C + s4 >= T) {
+#pragma unroll
+                  for (int j = 0; j < 4; ++j) {
+                    C += w[j];
+                    if (mine < 0 && C >= T) mine = j;
+                  }
+                }
+                const unsigned hit = __ballot_sync(0xffffffffu, mine >= 0);
+                if (found < 0 && hit) {
+                  const int l = __ffs(hit) - 1;
+                  found = sub * kChunk + (g * 32 + l) * 4 + __shfl_sync(0xffffffffu, mine, l);
+                }
+                cbase += __shfl_sync(0xffffffffu, inc, 31);
+              }
+              if (found >= 0) token = found;
+            }
+          }
+          if (lane == 0) sh.token = token;
+        }
+        __syncthreads();
+      }
+    }
+    if (threadIdx.x == 0) {
+      const int c = sh.accepted;
+      if (c >= 0) {
+        a.out_path[(int64_t)b * N + plen++] = c;
+        a.out_tokens[(int64_t)b * N + ntok++] = tok[c];
+        sh.node = c;
+      } else {
+        a.out_tokens[(int64_t)b * N + ntok++] = sh.token;
+        sh.done = 1;
+        a.out_path_len[b] = plen;
+        a.out_num_tokens[b] = ntok;
+      }
+    }
+    __syncthreads();
+  }
+}
+
 // ------------------------------------------------------------ host side
 
 bool use_vec(const void* a, const void* b, int64_t V) {
@@ -1357,6 +1631,8 @@ void fill_common(Args& a, const Workspace& ws, int64_t V, int B, int R) {
   a.vocab_offset = 0;
   a.tp_rank = 0;
   a.tp_world = 1;
+  a.q_rows = 0;
+  a.tree = 0;
 }
 
 }  // namespace
@@ -1409,6 +1685,7 @@ int kyro_spec_accept(kyro_ctx* ctx, const kyro_accept_params* p, const float* ta
   a.qlog = stoch ? draft_logits : nullptr;
   a.draft_tokens = draft_tokens;
   a.k = k;
+  a.q_rows = k;
   a.inv_t = stoch ? ky_inv_temperature(p->temperature) : 1.0f;
   a.stoch = stoch;
   a.greedy_ref = p->mode == KYRO_ACCEPT_GREEDY_REF;
@@ -1532,6 +1809,7 @@ int kyro_spec_accept_tp(kyro_ctx* ctx, const kyro_accept_params* p, const float*
   a.qlog = stoch ? draft_shard : nullptr;
   a.draft_tokens = draft_tokens;
   a.k = k;
+  a.q_rows = k;
   a.inv_t = stoch ? ky_inv_temperature(p->temperature) : 1.0f;
   a.stoch = stoch;
   a.greedy_ref = p->mode == KYRO_ACCEPT_GREEDY_REF;
@@ -1563,6 +1841,103 @@ int kyro_spec_accept_tp(kyro_ctx* ctx, const kyro_accept_params* p, const float*
   if (vec) return launch_tp<true, false>(ctx, a);
   if (stoch) return launch_tp<false, true>(ctx, a);
   return launch_tp<false, false>(ctx, a);
+}
+
+size_t kyro_spec_accept_tree_workspace_size(const kyro_tree_params* p) {
+  if (!p || p->batch < 0 || p->num_nodes < 1 || p->vocab <= 0) return 0;
+  const bool stoch = p->mode == KYRO_ACCEPT_STOCHASTIC && p->temperature > 0.0f;
+  const int64_t R = stoch ? 2 * (int64_t)p->num_nodes : (int64_t)p->num_nodes;
+  const int64_t nchunks = (p->vocab + kChunk - 1) / kChunk;
+  return carve(nullptr, p->batch, R, nchunks).bytes;
+}
+
+int kyro_spec_accept_tree(kyro_ctx* ctx, const kyro_tree_params* p, const float* target_logits,
+                          const float* draft_logits, const int32_t* node_tokens,
+                          const int32_t* parents, int32_t* out_path, int32_t* out_path_len,
+                          int32_t* out_tokens, int32_t* out_num_tokens, void* workspace,
+                          size_t workspace_bytes) {
+  KY_TRY(kyro::enter(ctx));
+  KY_REQUIRE(p, "kyro_spec_accept_tree: params is NULL");
+  KY_REQUIRE(p->batch >= 0, "kyro_spec_accept_tree: batch = %d", p->batch);
+  KY_REQUIRE(p->num_nodes >= 1 && p->num_nodes <= kMaxNodes,
+             "kyro_spec_accept_tree: num_nodes = %d (1..%d)", p->num_nodes, kMaxNodes);
+  KY_REQUIRE(p->vocab > 0 && (int64_t)p->vocab <= (int64_t)kMaxChunks * kChunk,
+             "kyro_spec_accept_tree: vocab = %d (1..%d)", p->vocab, kMaxChunks * kChunk);
+  KY_REQUIRE(p->mode >= 0 && p->mode <= 2, "kyro_spec_accept_tree: mode = %d", p->mode);
+  if (p->batch == 0) return KYRO_OK;
+  const bool stoch = p->mode == KYRO_ACCEPT_STOCHASTIC && p->temperature > 0.0f;
+  const int B = p->batch, N = p->num_nodes;
+  const int64_t V = p->vocab;
+  KY_REQUIRE(target_logits && node_tokens && parents,
+             "kyro_spec_accept_tree: target_logits, node_tokens and parents are required");
+  KY_REQUIRE(!stoch || draft_logits, "kyro_spec_accept_tree: stochastic mode needs draft_logits");
+  KY_REQUIRE(out_path && out_path_len && out_tokens && out_num_tokens,
+             "kyro_spec_accept_tree: an output pointer is NULL");
+  const int R = stoch ? 2 * N : N;
+  const int64_t nchunks = (V + kChunk - 1) / kChunk;
+  KY_REQUIRE((int64_t)B * R * nchunks < (1ll << 31), "kyro_spec_accept_tree: batch too large");
+  const size_t need = carve(nullptr, B, R, nchunks).bytes;
+  if (workspace_bytes < need || !workspace)
+    return kyro::set_error(KYRO_ERR_WORKSPACE, "kyro_spec_accept_tree: workspace %zu < %zu bytes",
+                           workspace_bytes, need);
+  KY_REQUIRE((uintptr_t)workspace % 256 == 0,
+             "kyro_spec_accept_tree: workspace must be 256-byte aligned");
+  Workspace ws = carve(workspace, B, R, nchunks);
+  Args a = {};
+  fill_common(a, ws, V, B, R);
+  a.plog = target_logits;
+  a.qlog = stoch ? draft_logits : nullptr;
+  a.k = N - 1;
+  a.q_rows = stoch ? N : 0;
+  a.tree = 1;
+  a.inv_t = stoch ? ky_inv_temperature(p->temperature) : 1.0f;
+  a.stoch = stoch;
+  a.seed = p->seed;
+  a.step = p->step;
+  a.seq_offset = p->seq_offset;
+  a.node_tokens = node_tokens;
+  a.parents = parents;
+  a.out_path = out_path;
+  a.out_path_len = out_path_len;
+  a.out_tokens = out_tokens;
+  a.out_num_tokens = out_num_tokens;
+  a.status = ctx->d_status;
+  const bool vec = use_vec(target_logits, a.qlog, V);
+  const long long units = (long long)a.units;
+  if (vec && stoch) {
+    const int resident = resident_ctas<true, true>(ctx->num_sms);
+    const long long need_ctas = (units + kWarps - 1) / kWarps;
+    accept_stats_kernel<true, true><<<(int)(need_ctas < resident ? need_ctas : resident),
+                                      kThreads, 0, ctx->stream>>>(a);
+    KY_TRY(kyro::check_launch("accept_stats_kernel"));
+    return launch_dependent(accept_tree_kernel<true, true>, (unsigned)B, kTreeThreads, ctx->stream,
+                            a, "accept_tree_kernel");
+  }
+  if (vec) {
+    const int resident = resident_ctas<true, false>(ctx->num_sms);
+    const long long need_ctas = (units + kWarps - 1) / kWarps;
+    accept_stats_kernel<true, false><<<(int)(need_ctas < resident ? need_ctas : resident),
+                                       kThreads, 0, ctx->stream>>>(a);
+    KY_TRY(kyro::check_launch("accept_stats_kernel"));
+    return launch_dependent(accept_tree_kernel<true, false>, (unsigned)B, kTreeThreads,
+                            ctx->stream, a, "accept_tree_kernel");
+  }
+  if (stoch) {
+    const int resident = resident_ctas<false, true>(ctx->num_sms);
+    const long long need_ctas = (units + kWarps - 1) / kWarps;
+    accept_stats_kernel<false, true><<<(int)(need_ctas < resident ? need_ctas : resident),
+                                       kThreads, 0, ctx->stream>>>(a);
+    KY_TRY(kyro::check_launch("accept_stats_kernel"));
+    return launch_dependent(accept_tree_kernel<false, true>, (unsigned)B, kTreeThreads,
+                            ctx->stream, a, "accept_tree_kernel");
+  }
+  const int resident = resident_ctas<false, false>(ctx->num_sms);
+  const long long need_ctas = (units + kWarps - 1) / kWarps;
+  accept_stats_kernel<false, false><<<(int)(need_ctas < resident ? need_ctas : resident),
+                                      kThreads, 0, ctx->stream>>>(a);
+  KY_TRY(kyro::check_launch("accept_stats_kernel"));
+  return launch_dependent(accept_tree_kernel<false, false>, (unsigned)B, kTreeThreads, ctx->stream,
+                          a, "accept_tree_kernel");
 }
 
 }  // extern "C"

@@ -139,6 +139,37 @@ def spec_accept(ctx: Context, target_logits: torch.Tensor, draft_logits: Optiona
     return acc, toks, num, probs
 
 
+def spec_accept_tree(ctx: Context, target_logits: torch.Tensor,
+                     draft_logits: Optional[torch.Tensor], node_tokens: torch.Tensor,
+                     parents: torch.Tensor, mode: int = ACCEPT_STOCHASTIC,
+                     temperature: float = 1.0, seed: int = 0, step: int = 0,
+                     seq_offset: int = 0):
+    """kyro_spec_accept_tree.  target/draft logits fp32 [B,N,V]; node_tokens
+    and parents int32 [B,N] (BFS order, parents[:,0] == -1).  Returns
+    (path [B,N], path_len [B], tokens [B,N], num_tokens [B])."""
+    from ._lib import TreeParams
+    dev = ctx.device
+    _need(target_logits, "target_logits", torch.float32, dev, 3)
+    B, N, V = target_logits.shape
+    _need(node_tokens, "node_tokens", torch.int32, dev, 2)
+    _need(parents, "parents", torch.int32, dev, 2)
+    if draft_logits is not None:
+        _need(draft_logits, "draft_logits", torch.float32, dev, 3)
+    path = torch.empty(B, N, dtype=torch.int32, device=dev)
+    plen = torch.empty(B, dtype=torch.int32, device=dev)
+    toks = torch.empty(B, N, dtype=torch.int32, device=dev)
+    num = torch.empty(B, dtype=torch.int32, device=dev)
+    p = TreeParams(B, N, V, mode, float(temperature), step & 0xFFFFFFFF,
+                   seed & 0xFFFFFFFFFFFFFFFF, seq_offset)
+    L = _lib.load()
+    ws = ctx.workspace(L.kyro_spec_accept_tree_workspace_size(C.byref(p)))
+    ctx.bind_stream()
+    check(L.kyro_spec_accept_tree(ctx.handle, C.byref(p), _ptr(target_logits), _ptr(draft_logits),
+                                  _ptr(node_tokens), _ptr(parents), _ptr(path), _ptr(plen),
+                                  _ptr(toks), _ptr(num), _ptr(ws), ws.numel()))
+    return path, plen, toks, num
+
+
 def tp_unique_id() -> bytes:
     """An NCCL unique id for kyro_ctx_tp_init (call on rank 0)."""
     buf = C.create_string_buffer(_lib.TP_UNIQUE_ID_BYTES)

@@ -141,3 +141,39 @@ def chain_bytes_per_step(context_lens: np.ndarray, cfg: ChainConfig) -> dict:
     qo = 2 * cfg.batch * cfg.num_query * cfg.num_heads * cfg.head_dim * 2
     logits = cfg.batch * (2 * cfg.k + 1) * cfg.vocab * 4
     return {"attention": kv + qo, "accept": logits, "total": kv + qo + logits}
+
+
+def bfs_tree(num_nodes: int = 64, branching=(4, 4, 4)) -> np.ndarray:
+    """Parents of a BFS-ordered draft tree: node 0 is the root, each level
+    gives every node of the previous level `branching[d]` children, and the
+    tree is cut at num_nodes (config 2: 4, 4, 4 cut to 64 = 1 + 4 + 16 + 43)."""
+    parents = [-1]
+    level = [0]
+    for br in branching:
+        nxt = []
+        for u in level:
+            for _ in range(br):
+                if len(parents) == num_nodes:
+                    break
+                parents.append(u)
+                nxt.append(len(parents) - 1)
+        level = nxt
+    return np.asarray(parents[:num_nodes], dtype=np.int32)
+
+
+def tree_inputs(batch: int, parents: np.ndarray, vocab: int, seed: int = 0,
+                std: float = 3.0, noise: float = 1.0, temperature: float = 1.0):
+    """Target logits z ~ N(0, std^2) per (seq, node, vocab), draft logits
+    z + N(0, noise^2), and node tokens: each child's token sampled from its
+    parent's draft distribution softmax(draft / T) (numpy, seeded)."""
+    rng = np.random.default_rng(seed)
+    N = parents.size
+    tgt = (rng.standard_normal((batch, N, vocab)) * std).astype(np.float32)
+    drf = (tgt + rng.standard_normal((batch, N, vocab)) * noise).astype(np.float32)
+    tok = np.zeros((batch, N), dtype=np.int32)
+    for b in range(batch):
+        for n in range(1, N):
+            z = drf[b, parents[n]].astype(np.float64) / temperature
+            q = np.exp(z - z.max())
+            tok[b, n] = rng.choice(vocab, p=q / q.sum())
+    return tgt, drf, tok

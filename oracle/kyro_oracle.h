@@ -65,6 +65,18 @@ void ko_spec_accept(int32_t batch, int32_t k, int32_t vocab, int32_t mode, float
                     const int32_t* draft_tokens, int32_t* out_accept_len, int32_t* out_tokens,
                     int32_t* out_num_tokens, float* out_probs, int32_t nthreads);
 
+/* Tree acceptance: node n of sequence b has token node_tokens[b][n], parent
+ * parents[b][n] (-1 for the root, node 0; parents precede children), and
+ * target / draft next-token logits rows [b][n][V].  Outputs: the accepted
+ * path (node ids, root first, -1 padded) [B, N], its length [B], the
+ * emitted tokens [B, N] (-1 padded) and their count [B]. */
+void ko_spec_accept_tree(int32_t batch, int32_t num_nodes, int32_t vocab, int32_t mode,
+                         float temperature, uint64_t seed, uint32_t step, int64_t seq_offset,
+                         const float* target_logits, const float* draft_logits,
+                         const int32_t* node_tokens, const int32_t* parents, int32_t* out_path,
+                         int32_t* out_path_len, int32_t* out_tokens, int32_t* out_num_tokens,
+                         int32_t nthreads);
+
 /* One rank's pieces of a vocabulary-sharded row (its contiguous columns,
  * len entries): the shard's row max; its butterfly part of the normaliser
  * under the global max M; e and the chunk max at one of its entries; its

@@ -56,6 +56,8 @@ def _declare(L):
     L.ko_sample_tokens.argtypes = [i32, i32, i32, f32, u64, u32, i64, vp, vp, vp, i32]
     L.ko_spec_accept.argtypes = [i32, i32, i32, i32, f32, u64, u32, i64, i32, vp, vp, vp, vp, vp,
                                  vp, vp, i32]
+    L.ko_spec_accept_tree.argtypes = [i32, i32, i32, i32, f32, u64, u32, i64, vp, vp, vp, vp, vp,
+                                      vp, vp, vp, i32]
     f64 = C.c_double
     L.ko_tp_row_max.argtypes = [vp, i32, f32]
     L.ko_tp_row_max.restype = f32
@@ -123,6 +125,25 @@ def spec_accept(target_logits, draft_logits, draft_tokens, mode=MODE_STOCHASTIC,
     lib().ko_spec_accept(B, k, V, mode, temperature, seed, step, seq_offset, num_shards, _p(tg),
                          _p(dr), _p(dt), _p(acc), _p(toks), _p(num), _p(probs), nthreads)
     return acc, toks, num, probs
+
+
+def spec_accept_tree(target_logits, draft_logits, node_tokens, parents, mode=MODE_STOCHASTIC,
+                     temperature=1.0, seed=0, step=0, seq_offset=0, nthreads=1):
+    """Tree acceptance; target/draft logits [B, N, V] fp32, node_tokens and
+    parents [B, N] int32.  Returns (path [B,N], path_len [B], tokens [B,N],
+    num_tokens [B])."""
+    tg = np.ascontiguousarray(target_logits, dtype=np.float32)
+    B, N, V = tg.shape
+    dr = None if draft_logits is None else np.ascontiguousarray(draft_logits, dtype=np.float32)
+    nt = np.ascontiguousarray(node_tokens, dtype=np.int32).reshape(B, N)
+    pa = np.ascontiguousarray(parents, dtype=np.int32).reshape(B, N)
+    path = np.empty((B, N), dtype=np.int32)
+    plen = np.empty(B, dtype=np.int32)
+    toks = np.empty((B, N), dtype=np.int32)
+    num = np.empty(B, dtype=np.int32)
+    lib().ko_spec_accept_tree(B, N, V, mode, temperature, seed, step, seq_offset, _p(tg), _p(dr),
+                              _p(nt), _p(pa), _p(path), _p(plen), _p(toks), _p(num), nthreads)
+    return path, plen, toks, num
 
 
 # ---- one rank's pieces of a vocabulary-sharded row (test infrastructure for

@@ -525,3 +525,153 @@ void ko_spec_accept(int32_t batch, int32_t k, int32_t vocab, int32_t mode, float
   run_parallel(jobs, sizeof(accept_job), batch, nt, accept_thread, accept_set_range);
   free(jobs);
 }
+
+/* ------------------------------------------------------------------ */
+/* tree acceptance                                                      */
+/* ------------------------------------------------------------------ */
+/* Multi-candidate rejection sampling over a BFS-ordered draft tree
+ * (SpecInfer, Miao et al. 2023), as kyro_math.h states it.  The reference
+ * has no tree code; the greedy variant accepts the first child whose token
+ * is the target's argmax (speculative.rs:314-323 applied per node). */
+
+/* p_j(i): p_i after j residual steps */
+static double tree_pj(const ko_rowstat* P, const ko_rowstat* Q, const double* R, int32_t nr,
+                      int32_t i) {
+  double v = (double)rowstat_p(P, i);
+  const double q = (double)rowstat_p(Q, i);
+  for (int32_t j = 0; j < nr; ++j) v = ky_tree_step(v, q, R[j]);
+  return v;
+}
+
+/* R_nr = sum_i max(p_nr(i) - q_i, 0) in the contract's tree */
+static double tree_residual_sum(const ko_rowstat* P, const ko_rowstat* Q, const double* R,
+                                int32_t nr, int32_t V) {
+  int32_t nc = (V + KY_CHUNK - 1) / KY_CHUNK;
+  double t[32];
+  for (int32_t l = 0; l < 32; ++l) t[l] = 0.0;
+  for (int32_t c = 0; c < nc; ++c) {
+    double e[KY_CHUNK];
+    for (int32_t p = 0; p < KY_CHUNK; ++p) {
+      int32_t i = c * KY_CHUNK + p;
+      e[p] = i < V ? ky_tree_excess(tree_pj(P, Q, R, nr, i), (double)rowstat_p(Q, i)) : 0.0;
+    }
+    t[c % 32] = KY_DADD(t[c % 32], ky_chunk_sum_d(e));
+  }
+  return ky_butterfly32(t);
+}
+
+typedef struct {
+  int32_t batch, num_nodes, vocab, greedy;
+  float temperature;
+  uint64_t seed;
+  uint32_t step;
+  int64_t seq_offset;
+  const float* target;
+  const float* draft;
+  const int32_t* node_tokens;
+  const int32_t* parents;
+  int32_t* out_path;
+  int32_t* out_path_len;
+  int32_t* out_tokens;
+  int32_t* out_num_tokens;
+  int32_t b0, b1;
+} tree_job;
+
+static void tree_one(const tree_job* J, int32_t b, uint64_t* w) {
+  const int32_t N = J->num_nodes, V = J->vocab;
+  const float inv_t = ky_inv_temperature(J->temperature);
+  const float* tgt = J->target + (size_t)b * N * V;
+  const float* drf = J->draft + (size_t)b * N * V;
+  const int32_t* tok = J->node_tokens + (size_t)b * N;
+  const int32_t* par = J->parents + (size_t)b * N;
+  int32_t* path = J->out_path + (size_t)b * N;
+  int32_t* toks = J->out_tokens + (size_t)b * N;
+  const uint32_t seq = (uint32_t)(J->seq_offset + b);
+  for (int32_t n = 0; n < N; ++n) path[n] = toks[n] = -1;
+  int32_t node = 0, plen = 1, ntok = 0;
+  path[0] = 0;
+  for (;;) {
+    int32_t ch[64], nch = 0;
+    for (int32_t c = node + 1; c < N; ++c)
+      if (par[c] == node) ch[nch++] = c;
+    int32_t accepted = -1;
+    if (J->greedy) {
+      const int32_t top = argmax_row(tgt + (size_t)node * V, V);
+      for (int32_t i = 0; i < nch && accepted < 0; ++i)
+        if (tok[ch[i]] == top) accepted = ch[i];
+      if (accepted < 0) {
+        toks[ntok++] = top;
+        break;
+      }
+    } else {
+      ko_rowstat P, Q;
+      rowstat_init(&P, tgt + (size_t)node * V, V, 1, inv_t);
+      rowstat_init(&Q, drf + (size_t)node * V, V, 1, inv_t);
+      double R[64];
+      int32_t nr = 0;
+      for (int32_t i = 0; i < nch; ++i) {
+        const int32_t c = ch[i], x = tok[c];
+        if (x >= 0 && x < V) {
+          const double px = tree_pj(&P, &Q, R, nr, x);
+          const double qx = (double)rowstat_p(&Q, x);
+          const double u =
+              (double)ky_odd_to_float(ky_uniform_odd(J->seed, seq, (uint32_t)c, KY_STREAM_ACCEPT,
+                                                     J->step));
+          if (u < KY_DDIV(px, qx)) {
+            accepted = c;
+            break;
+          }
+        }
+        R[nr] = tree_residual_sum(&P, &Q, R, nr, V);
+        ++nr;
+      }
+      if (accepted < 0) {
+        for (int32_t i = 0; i < V; ++i) w[i] = ky_weight_d(tree_pj(&P, &Q, R, nr, i));
+        const uint32_t odd =
+            ky_uniform_odd(J->seed, seq, (uint32_t)node, KY_STREAM_RESAMPLE, J->step);
+        toks[ntok++] = inverse_cdf(w, V, odd);
+      }
+      rowstat_free(&P);
+      rowstat_free(&Q);
+      if (accepted < 0) break;
+    }
+    path[plen++] = accepted;
+    toks[ntok++] = tok[accepted];
+    node = accepted;
+  }
+  J->out_path_len[b] = plen;
+  J->out_num_tokens[b] = ntok;
+}
+
+static void* tree_thread(void* arg) {
+  const tree_job* J = (const tree_job*)arg;
+  uint64_t* w = (uint64_t*)malloc(sizeof(uint64_t) * (size_t)J->vocab);
+  for (int32_t b = J->b0; b < J->b1; ++b) tree_one(J, b, w);
+  free(w);
+  return NULL;
+}
+
+static void tree_set_range(void* j, int32_t b0, int32_t b1) {
+  ((tree_job*)j)->b0 = b0;
+  ((tree_job*)j)->b1 = b1;
+}
+
+void ko_spec_accept_tree(int32_t batch, int32_t num_nodes, int32_t vocab, int32_t mode,
+                         float temperature, uint64_t seed, uint32_t step, int64_t seq_offset,
+                         const float* target_logits, const float* draft_logits,
+                         const int32_t* node_tokens, const int32_t* parents, int32_t* out_path,
+                         int32_t* out_path_len, int32_t* out_tokens, int32_t* out_num_tokens,
+                         int32_t nthreads) {
+  int32_t nt = nthreads < 1 ? 1 : nthreads;
+  tree_job* jobs = (tree_job*)calloc((size_t)nt, sizeof(tree_job));
+  const int32_t greedy = !(mode == KO_MODE_STOCHASTIC && temperature > 0.0f);
+  for (int32_t t = 0; t < nt; ++t) {
+    tree_job J = {batch,        num_nodes,     vocab,       greedy,        temperature,
+                  seed,         step,          seq_offset,  target_logits, draft_logits,
+                  node_tokens,  parents,       out_path,    out_path_len,  out_tokens,
+                  out_num_tokens, 0,           0};
+    jobs[t] = J;
+  }
+  run_parallel(jobs, sizeof(tree_job), batch, nt, tree_thread, tree_set_range);
+  free(jobs);
+}

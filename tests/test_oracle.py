@@ -127,6 +127,72 @@ def test_stochastic_rule_emits_target_distribution(oracle):
     assert abs(rate - np.minimum(p, q).sum()) < 4 * math.sqrt(0.25 / N)
 
 
+def _star_tree(n_children):
+    """root (node 0) with n_children leaf children"""
+    par = np.full(n_children + 1, -1, dtype=np.int32)
+    par[1:] = 0
+    return par
+
+
+def test_tree_rule_emits_target_distribution(oracle):
+    """Multi-candidate rejection sampling (SpecInfer, Miao et al. 2023): with
+    children drawn i.i.d. from q, the first emitted token is distributed as
+    p at the root, whatever q is -- whether a child is accepted or the final
+    residual is sampled."""
+    V, N, C = 8, 120_000, 4
+    rng = np.random.default_rng(11)
+    zt = (rng.standard_normal(V) * 1.5).astype(np.float32)
+    zd = (zt + rng.standard_normal(V) * 1.5).astype(np.float32)
+    nodes = C + 1
+    tgt = np.broadcast_to(zt[None, None], (N, nodes, V)).copy()
+    drf = np.broadcast_to(zd[None, None], (N, nodes, V)).copy()
+    par = np.broadcast_to(_star_tree(C)[None], (N, nodes)).copy()
+    q = oracle.softmax_row(zd)
+    p = oracle.softmax_row(zt)
+    tok = np.zeros((N, nodes), dtype=np.int32)
+    tok[:, 1:] = rng.choice(V, size=(N, C), p=q / q.sum())
+    path, plen, toks, num = oracle.spec_accept_tree(tgt, drf, tok, par, seed=5, nthreads=8)
+    counts = np.bincount(toks[:, 0], minlength=V)
+    expected = p * N
+    chi2 = ((counts - expected) ** 2 / expected).sum()
+    assert chi2 < 35.0, (chi2, counts, expected)  # dof 7: p ~ 1e-5
+    # more candidates accept more often than one
+    assert (plen == 2).mean() > np.minimum(p, q).sum()
+
+
+def test_tree_walk_structure(oracle):
+    """Paths follow parent links from the root; emitted tokens are the path's
+    node tokens then one sampled token; identical models accept the first
+    child at every level down to a leaf, which adds the bonus token."""
+    B, V = 4, 600
+    rng = np.random.default_rng(12)
+    par = np.array([-1, 0, 0, 1, 1, 2, 3], dtype=np.int32)  # depth 3 along 0-1-3-6
+    N = par.size
+    z = (rng.standard_normal((B, N, V)) * 3).astype(np.float32)
+    tok = rng.integers(0, V, size=(B, N)).astype(np.int32)
+    pars = np.broadcast_to(par[None], (B, N)).copy()
+    path, plen, toks, num = oracle.spec_accept_tree(z, z + 1.0, tok, pars, seed=2)
+    for b in range(B):
+        L = plen[b]
+        assert path[b, 0] == 0 and num[b] == L
+        for i in range(1, L):
+            assert par[path[b, i]] == path[b, i - 1]
+            assert toks[b, i - 1] == tok[b, path[b, i]]
+        assert (path[b, L:] == -1).all() and (toks[b, num[b]:] == -1).all()
+    # identical target and draft: every first child is accepted (p/q == 1)
+    for b in range(B):
+        tok[b, 1] = rng.integers(0, V)
+    path, plen, toks, num = oracle.spec_accept_tree(z, z, tok, pars, seed=4)
+    assert (plen == 4).all() and (path[:, :4] == [0, 1, 3, 6]).all()
+    # greedy: the first child whose token is the argmax
+    top0 = z[:, 0].argmax(axis=1)
+    tok2 = tok.copy()
+    tok2[:, 1] = (top0 + 1) % V
+    tok2[:, 2] = top0
+    path, plen, toks, num = oracle.spec_accept_tree(z, None, tok2, pars, mode=oracle.MODE_GREEDY)
+    assert (path[:, 1] == 2).all() and (toks[:, 0] == top0).all()
+
+
 def test_stochastic_identical_models_accept_everything(oracle):
     V, B, k = 64, 32, 4
     rng = np.random.default_rng(2)
