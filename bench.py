@@ -508,6 +508,154 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_tree(args):
+    """Config 2: tree verification.  Per step and GPU (batch-sharded, no
+    collective): KV reserve and write of the 64 tree nodes, paged attention
+    of 64 query heads over 8 KV heads (context 8192) under the ancestor mask,
+    multi-candidate acceptance over vocabulary 32000, and the tree commit of
+    the accepted path."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from kyro_b200.verify import (Context, kv_commit_tree, kv_reserve, kv_write,
+                                  spec_accept_tree, verify_attention)
+    from kyro_b200.workloads import CONFIG2, bfs_tree, paged_state, tree_mask_bits
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    cfg = CONFIG2
+    B, N, V = cfg.batch, cfg.num_query, cfg.vocab
+    ctx = Context(local)
+    st = paged_state(cfg, dev, seed=8000 + rank)
+    par = bfs_tree(N)
+    pars = torch.from_numpy(np.broadcast_to(par[None], (B, N)).copy()).to(dev)
+    mask = torch.from_numpy(np.broadcast_to(tree_mask_bits(par)[None], (B, N)).copy()).to(dev)
+    g = torch.Generator(device=dev).manual_seed(8100 + rank)
+    tgt = torch.randn(B, N, V, generator=g, device=dev) * cfg.logit_std
+    drf = tgt + torch.randn(B, N, V, generator=g, device=dev) * cfg.draft_noise
+    # each child's token sampled from its parent's draft distribution
+    tok = torch.zeros(B, N, dtype=torch.int32, device=dev)
+    q = torch.softmax(drf[:, torch.from_numpy(par[1:]).long().to(dev), :] / cfg.temperature, dim=2)
+    tok[:, 1:] = torch.multinomial(q.reshape(-1, V), 1, generator=g).reshape(B, N - 1).int()
+    del q
+    k_new = torch.randn(B, N, cfg.num_kv_heads, cfg.head_dim, generator=g, device=dev,
+                        dtype=torch.bfloat16)
+    v_new = torch.randn_like(k_new)
+    attn_out = torch.empty_like(st.q)
+    ok = torch.empty(B, dtype=torch.int32, device=dev)
+    snap = {n: getattr(st, n).clone() for n in
+            ("block_table", "context_lens", "free_stack", "free_top", "ref_counts")}
+    stream = torch.cuda.current_stream(dev)
+    ev = {"attention": [], "accept": []}
+
+    def step(i, timed):
+        for n, t in snap.items():
+            getattr(st, n).copy_(t, non_blocking=True)
+        kv_reserve(ctx, N, st.block_table, st.context_lens, st.free_stack, st.free_top,
+                   st.ref_counts, cfg.block_size, out_ok=ok)
+        kv_write(ctx, k_new, v_new, st.block_table, st.context_lens, st.k_cache, st.v_cache,
+                 cfg.block_size)
+        if timed:
+            e0 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+        verify_attention(ctx, st.q, st.k_cache, st.v_cache, st.block_table, st.context_lens,
+                         tree_mask=mask, out=attn_out)
+        if timed:
+            e1 = torch.cuda.Event(enable_timing=True)
+            e1.record(stream)
+        path, plen, _, _ = spec_accept_tree(ctx, tgt, drf, tok, pars, temperature=cfg.temperature,
+                                            seed=0, step=i, seq_offset=rank * B)
+        if timed:
+            e2 = torch.cuda.Event(enable_timing=True)
+            e2.record(stream)
+            ev["attention"].append((e0, e1))
+            ev["accept"].append((e1, e2))
+        kv_commit_tree(ctx, N, path, plen, [st.k_cache], [st.v_cache], st.block_table,
+                       st.context_lens, st.free_stack, st.free_top, st.ref_counts, cfg.block_size)
+        return plen
+
+    for i in range(args.warmup):
+        step(i, False)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = None
+    if rank == 0:
+        try:
+            clocks = NvmlClockSampler(local)
+        except Exception:
+            clocks = ClockSampler(local)
+        clocks.start()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    plens = []
+    for i in range(args.warmup, args.warmup + args.steps):
+        plens.append(step(i, True))
+    t1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop() if clocks else None
+    ms = t0.elapsed_time(t1)
+    att_ms = float(np.mean([a.elapsed_time(b) for a, b in ev["attention"]]))
+    acc_ms = float(np.mean([a.elapsed_time(b) for a, b in ev["accept"]]))
+    if world > 1:
+        t = torch.tensor([ms, att_ms, acc_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, att_ms, acc_ms = float(t[0]), float(t[1]), float(t[2])
+    status = ctx.device_status()
+    if status:
+        raise SystemExit(f"device status word 0x{status:x} after the timed region")
+    peak, peak_kind = load_peaks()
+    kv_bytes = B * (cfg.ctx_max + N) * 2 * cfg.num_kv_heads * cfg.head_dim * 2
+    flops = 4.0 * B * cfg.num_heads * N * cfg.head_dim * (cfg.ctx_max + N)
+    acc_bytes = 2 * B * N * V * 4
+    mean_path = float(torch.stack(plens).float().mean().item())
+    if rank == 0:
+        line = {
+            "metric": "spec-verify tree nodes/s (config 2)", "unit": "verified tree nodes/s",
+            "value": B * N * world * args.steps / (ms * 1e-3), "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded; BASELINE config 2 shapes and distributions)",
+            "config": {"workload": "config2: tree verify (paged attention under a 64-node "
+                                   "ancestor mask + multi-candidate acceptance + tree commit), "
+                                   "Hq64/Hkv8/D128 bf16, ctx 8192, tree 4,4,4 cut to 64, "
+                                   "V 32000 fp32, T 1.0",
+                       "batch_per_gpu": B, "global_batch": B * world, "nodes": N,
+                       "parallelism": f"batch-sharded x{world} (no collective)"},
+            "kernels": {
+                "attention": {"ms": att_ms, "kv_bytes": kv_bytes, "flops": flops,
+                              "GBps": kv_bytes / (att_ms * 1e-3) / 1e9,
+                              "hbm_frac": kv_bytes / (att_ms * 1e-3) / 1e9 / peak,
+                              "TFLOPs": flops / (att_ms * 1e-3) / 1e12},
+                "accept": {"ms": acc_ms, "bytes": acc_bytes,
+                           "GBps": acc_bytes / (acc_ms * 1e-3) / 1e9,
+                           "hbm_frac": acc_bytes / (acc_ms * 1e-3) / 1e9 / peak},
+            },
+            "mean_path_len": mean_path,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def run_tp(args):
     """Config 3: vocabulary-sharded acceptance (kyro_spec_accept_tp) over the
     N ranks of one tensor-parallel group, plus KV reserve/commit on a
@@ -666,14 +814,16 @@ def main():
                     help="wall time the cpu_baseline leg repeats whole-batch steps for")
     ap.add_argument("--no-e2e", action="store_true",
                     help="skip the host-buffer leg (profiling runs)")
-    ap.add_argument("--config", choices=["1", "3"], default="1",
-                    help="1: chain verify step (the headline); 3: vocabulary-sharded "
-                         "acceptance over the N ranks of one TP group")
+    ap.add_argument("--config", choices=["1", "2", "3"], default="1",
+                    help="1: chain verify step (the headline); 2: tree verify step; "
+                         "3: vocabulary-sharded acceptance over the N ranks of one TP group")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         raise SystemExit("--warmup must be >= 3")
     if args.impl == "reference":
         run_reference(args)
+    elif args.config == "2":
+        run_tree(args)
     elif args.config == "3":
         run_tp(args)
     else:

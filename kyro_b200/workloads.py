@@ -51,6 +51,12 @@ class ChainConfig:
 
 CONFIG0 = dict(batch=8, k=4, vocab=32000)
 CONFIG1 = ChainConfig()
+# Config 2: tree verification, 64 query heads over 8 KV heads, context 8192,
+# a 64-node tree (k + 1 = 64 positions), vocabulary 32000.
+CONFIG2 = ChainConfig(batch=32, k=63, num_heads=64, num_kv_heads=8, head_dim=128,
+                      num_blocks=17408, ctx_min=8192, ctx_max=8192, vocab=32000,
+                      temperature=1.0, headroom_tokens=128)
+
 # Config 3: vocabulary-sharded acceptance and KV commit on a 32768-block
 # table (the table only: a one-head, 8-wide cache keeps the K/V arrays small;
 # contexts U[256, 1800] fit 256 sequences plus growth in the pool).
@@ -177,3 +183,18 @@ def tree_inputs(batch: int, parents: np.ndarray, vocab: int, seed: int = 0,
             q = np.exp(z - z.max())
             tok[b, n] = rng.choice(vocab, p=q / q.sum())
     return tgt, drf, tok
+
+
+def tree_mask_bits(parents: np.ndarray) -> np.ndarray:
+    """uint64-as-int64 ancestor masks: bit i of mask[j] is set iff node i is
+    node j or one of its ancestors."""
+    N = parents.size
+    mask = np.zeros(N, dtype=np.uint64)
+    for j in range(N):
+        bits = np.uint64(0)
+        n = j
+        while n >= 0:
+            bits |= np.uint64(1) << np.uint64(n)
+            n = int(parents[n])
+        mask[j] = bits
+    return mask.view(np.int64)
