@@ -555,6 +555,11 @@ int kyro_verify_attention(kyro_ctx* ctx, const kyro_attn_params* p, const void* 
                  (uintptr_t)q % 16 == 0,
              "kyro_verify_attention: q and the caches must be 16-byte aligned");
   KY_REQUIRE(pl.a.B <= 65535, "kyro_verify_attention: batch %d > 65535", pl.a.B);
+  // enough query rows per KV head to fill 128-row tensor-core tiles (draft
+  // trees): the tcgen05 kernel, which needs no workspace
+  if (kyro::tree_attention_eligible(p))
+    return kyro::tree_attention_launch(ctx, p, q, k_cache, v_cache, block_table, context_lens,
+                                       tree_mask, out);
   const size_t need = ws_bytes(pl);
   if (need > 0 && (workspace_bytes < need || !workspace))
     return kyro::set_error(KYRO_ERR_WORKSPACE, "kyro_verify_attention: workspace %zu < %zu bytes",

@@ -60,7 +60,7 @@ const char* kyro_kernel_names(void) {
          "accept_tp_max_kernel;accept_tp_sum_kernel;accept_tp_decide_kernel;"
          "accept_tp_search_kernel;accept_tp_write_kernel;verify_attention_kernel;"
          "kv_reserve_kernel;kv_commit_kernel;kv_tree_move_kernel;kv_write_kernel;"
-         "philox_uniforms_kernel;exp_selftest_kernel";
+         "philox_uniforms_kernel;exp_selftest_kernel;tree_attention_tc_kernel";
 }
 
 size_t kyro_last_error(char* buf, size_t len) {

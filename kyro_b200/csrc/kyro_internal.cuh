@@ -33,6 +33,13 @@ int check_launch(const char* what);
 // Validate a context and make its device current.
 int enter(kyro_ctx* ctx);
 
+// Tensor-core attention for many query rows per KV head (tree_attention.cu):
+// whether a shape fills its 128-row tiles, and the launch.
+bool tree_attention_eligible(const kyro_attn_params* p);
+int tree_attention_launch(kyro_ctx* ctx, const kyro_attn_params* p, const void* q,
+                          const void* k_cache, const void* v_cache, const int64_t* block_table,
+                          const int64_t* context_lens, const uint64_t* tree_mask, void* out);
+
 // NCCL, loaded at run time (nccl_comm.cu).  Collectives enqueue on the
 // context's stream over its tensor-parallel communicator.
 namespace nccl {

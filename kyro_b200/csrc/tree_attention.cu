@@ -1,0 +1,568 @@
+// tree_attention.cu -- K1 for many query rows per KV head (tree
+// verification), on the sm_100 tensor cores: tcgen05.mma with the score and
+// output accumulators in tensor memory (TMEM).
+//
+// Replaces PagedAttention::forward (src/model/attention_kernel.rs:22-136) for
+// the tree case: N draft-tree nodes x (Hq/Hkv) query heads share each KV
+// head, 512 rows for config 2, which fill 128-row MMA tiles.  The chain case
+// (24 rows) stays on the mma.sync kernel of attention.cu.
+//
+// One CTA = (two 128-row query tiles, one KV head, one sequence).  Rows are
+// ordered node-major: row r = node_local * group + head_in_group, so a Q
+// tile is a TMA box of (128/group nodes) x (group heads) x 128 dims.  The
+// two tiles share every K/V load.  Per 128-token KV tile j (8 paged blocks):
+//   warp 0 (producer)  TMA loads of K_j and V_j into a 2-stage ring (128-byte
+//                      swizzle, no multicast; a 16-token block is one box
+//                      per 64-column slab)
+//   warp 1 (MMA)       S_h = Q_h K_j^T into tile h's TMEM score buffer, and
+//                      after tile h's softmax O_h += P_h V_j with P read
+//                      from TMEM (the TS form) and V from shared memory
+//                      (MN-major).  The order S0 S1 | O0 S0' | O1 S1' | ...
+//                      lets one tile's softmax run while the other tile's
+//                      MMAs do (ping-pong).
+//   warps 4-7, 8-11    the softmax of tile 0 and of tile 1, one query row
+//                      per thread (its TMEM lane): mask, online max and sum,
+//                      P = exp2(s - m) written back over the scores as bf16,
+//                      and the O rescale when the running max grows by more
+//                      than 2^8
+// The output is O / l, written as bf16.  Every wait is bounded; a wait that
+// runs out sets KYRO_DEV_WAIT_TIMEOUT, and the CTA still waits (bounded)
+// for its own copies and MMAs before it frees its TMEM.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_bf16.h>
+
+#include <mutex>
+
+#include "kyro_internal.cuh"
+#include "ptx.cuh"
+
+namespace {
+
+constexpr int kBS = 16;                       // tokens per paged block
+constexpr int kD = 128;                       // head dim
+constexpr int kTM = 128;                      // query rows per CTA
+constexpr int kTN = 128;                      // KV tokens per tile
+constexpr int kTileBlocks = kTN / kBS;        // 8
+constexpr int kTcThreads = 384;
+constexpr int kTilesPerCta = 2;
+constexpr uint32_t kSlab = 128 * 128;         // one 64-column slab of a 128-row tile
+constexpr uint32_t kTile = 2 * kSlab;         // 128 rows x 128 bf16
+constexpr uint32_t kOffQ = 0;                 // Q tile h at h * kTile
+constexpr uint32_t kOffStage = 2 * kTile;     // stage s: K at +s*2*kTile, V after it
+constexpr uint32_t kTilesBytes = 2 * kTile + 2 * 2 * kTile;  // 2 Q tiles + 2 stages of K, V
+constexpr uint32_t kSmemTc = kTilesBytes + 256 + 1024;       // + barriers, alignment slack
+constexpr uint32_t kTmemCols = 512;           // S_h at h*128, O_h at 256 + h*128
+constexpr uint32_t kColO = 256;
+constexpr long long kTcWaitBudget = 2000000000ll;
+
+struct TcArgs {
+  int B, nq, hq, hkv, group, max_blocks, num_blocks;
+  float scale_log2;
+};
+
+// ---------------------------------------------------------------- tcgen05
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// D[tmem] (+)= A[smem] * B[smem]
+__device__ __forceinline__ void umma_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
+                                        uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+// D[tmem] (+)= A[tmem] * B[smem]
+__device__ __forceinline__ void umma_ts(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc,
+                                        uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+      "r"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+// arrive on `bar` when every tcgen05.mma this thread issued so far is done
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
+      "%30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, "
+      "%29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld_wait() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptors (tcgen05 format: version 1, 128-byte
+// swizzle).  K-major (rows of 64 contiguous bf16 along K): the stride between
+// 8-row groups is 1024 B and the leading offset is unused (16 B).  MN-major
+// (64 contiguous bf16 along N): the leading offset steps between 64-column
+// slabs along N, the stride between 8-row groups along K.
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;  // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor of kind::f16: bf16 A and B, fp32 accumulate,
+// M = 128, N = 128; b_mn selects an MN-major B.
+__host__ __device__ constexpr uint32_t idesc_bf16(bool b_mn) {
+  return (1u << 4)              // D fp32
+         | (1u << 7)            // A bf16
+         | (1u << 10)           // B bf16
+         | ((b_mn ? 1u : 0u) << 16)
+         | ((uint32_t)(kTN >> 3) << 17)   // N = 128
+         | ((uint32_t)(kTM >> 4) << 24);  // M = 128
+}
+
+__device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, int* err, uint32_t* status) {
+  if (kyro::ptx::mbar_wait_bounded(bar, parity, kTcWaitBudget)) return true;
+  *(volatile int*)err = 1;
+  kyro::dev::flag(status, KYRO_DEV_WAIT_TIMEOUT);
+  return false;
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+tree_attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
+                         const __grid_constant__ CUtensorMap tmK,
+                         const __grid_constant__ CUtensorMap tmV, TcArgs a,
+                         const int64_t* __restrict__ block_table,
+                         const int64_t* __restrict__ context_lens,
+                         const uint64_t* __restrict__ tree_mask, __nv_bfloat16* __restrict__ out,
+                         uint32_t* status) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = kyro::ptx::smem_addr(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw);
+  const uint32_t bar0 = base + kTilesBytes;
+  auto q_full = [&]() { return bar0; };
+  auto kv_full = [&](int s) { return bar0 + 8u * (1 + s); };
+  auto kv_empty = [&](int s) { return bar0 + 8u * (3 + s); };
+  auto s_full = [&](int h) { return bar0 + 8u * (5 + h); };
+  auto p_full = [&](int h) { return bar0 + 8u * (7 + h); };
+  auto o_done = [&](int h) { return bar0 + 8u * (9 + h); };
+  const uint32_t mma_done = bar0 + 8u * 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + kTilesBytes + 128);
+  int* err = reinterpret_cast<int*>(gbase + kTilesBytes + 132);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kvh = blockIdx.y, b = blockIdx.z;
+  const int64_t ctx = context_lens[b];
+  const int64_t T = ctx + a.nq;
+  if (ctx < 0 || (T + kBS - 1) / kBS > a.max_blocks) {
+    if (threadIdx.x == 0 && blockIdx.x == 0 && kvh == 0)
+      kyro::dev::flag(status, KYRO_DEV_BAD_LENGTH);
+    return;
+  }
+  const int nblk = (int)((T + kBS - 1) / kBS);
+  const int ntiles = (int)((T + kTN - 1) / kTN);
+  const int nodes_per_tile = kTM / a.group;
+  const int mt0 = blockIdx.x * kTilesPerCta;             // first 128-row tile of this CTA
+  const int mtiles = a.nq * a.group / kTM;
+  const int ntq = mtiles - mt0 < kTilesPerCta ? mtiles - mt0 : kTilesPerCta;  // 1 or 2
+
+  if (threadIdx.x == 0) {
+    kyro::ptx::mbar_init(q_full(), 1);
+    for (int i = 0; i < 2; ++i) {
+      kyro::ptx::mbar_init(kv_full(i), 1);
+      kyro::ptx::mbar_init(kv_empty(i), 1);
+      kyro::ptx::mbar_init(s_full(i), 1);
+      kyro::ptx::mbar_init(p_full(i), 128);
+      kyro::ptx::mbar_init(o_done(i), 1);
+    }
+    kyro::ptx::mbar_init(mma_done, 1);
+    *err = 0;
+    kyro::ptx::fence_barrier_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(kyro::ptx::smem_addr(tmem_slot), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------ producer (one thread)
+    if (lane == 0) {
+      kyro::ptx::prefetch_tensormap(&tmQ);
+      kyro::ptx::prefetch_tensormap(&tmK);
+      kyro::ptx::prefetch_tensormap(&tmV);
+      kyro::ptx::mbar_arrive_expect_tx(q_full(), (uint32_t)ntq * kTile);
+      for (int h = 0; h < ntq; ++h) {
+        const int32_t qz = (int32_t)((int64_t)b * a.nq + (mt0 + h) * nodes_per_tile);
+        const uint32_t qd = base + kOffQ + (uint32_t)h * kTile;
+        kyro::ptx::tma_load_3d(qd, &tmQ, 0, kvh * a.group, qz, q_full());
+        kyro::ptx::tma_load_3d(qd + kSlab, &tmQ, 64, kvh * a.group, qz, q_full());
+      }
+      const int64_t* bt = block_table + (int64_t)b * a.max_blocks;
+      // a tile's 8 block ids are loaded together, one tile ahead of use
+      int64_t ids[kTileBlocks];
+      auto fetch_ids = [&](int j) {
+#pragma unroll
+        for (int i = 0; i < kTileBlocks; ++i) {
+          const int tb = j * kTileBlocks + i;
+          ids[i] = __ldg(&bt[tb < nblk ? tb : 0]);  // blocks past the end: any block, masked
+        }
+      };
+      fetch_ids(0);
+      int issued = 0;
+      for (int j = 0; j < ntiles; ++j) {
+        const int s = j & 1;
+        int64_t cur[kTileBlocks];
+#pragma unroll
+        for (int i = 0; i < kTileBlocks; ++i) cur[i] = ids[i];
+        if (j + 1 < ntiles) fetch_ids(j + 1);
+        if (j >= 2 && !wait_bar(kv_empty(s), ((j - 2) >> 1) & 1, err, status)) break;
+        if (*(volatile int*)err) break;
+        kyro::ptx::mbar_arrive_expect_tx(kv_full(s), 2 * kTile);
+        const uint32_t ks = base + kOffStage + (uint32_t)s * 2 * kTile;
+        const uint32_t vs = ks + kTile;
+#pragma unroll
+        for (int i = 0; i < kTileBlocks; ++i) {
+          int64_t bid = cur[i];
+          if (bid < 0 || bid >= a.num_blocks) {
+            kyro::dev::flag(status, KYRO_DEV_BAD_BLOCK);
+            bid = 0;
+          }
+          const int32_t z = (int32_t)(bid * a.hkv + kvh);
+          const uint32_t off = (uint32_t)i * kBS * 128;
+          kyro::ptx::tma_load_3d(ks + off, &tmK, 0, 0, z, kv_full(s));
+          kyro::ptx::tma_load_3d(ks + kSlab + off, &tmK, 64, 0, z, kv_full(s));
+          kyro::ptx::tma_load_3d(vs + off, &tmV, 0, 0, z, kv_full(s));
+          kyro::ptx::tma_load_3d(vs + kSlab + off, &tmV, 64, 0, z, kv_full(s));
+        }
+        ++issued;
+      }
+      // every copy this thread started has landed before the CTA moves on
+      wait_bar(q_full(), 0, err, status);
+      for (int j = issued - 2 < 0 ? 0 : issued - 2; j < issued; ++j)
+        wait_bar(kv_full(j & 1), (j >> 1) & 1, err, status);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------ MMA issuer (one thread)
+    if (lane == 0) {
+      constexpr uint32_t idS = idesc_bf16(false), idO = idesc_bf16(true);
+      auto s_mma = [&](int h, int j) {
+        const uint32_t ks = base + kOffStage + (uint32_t)(j & 1) * 2 * kTile;
+        const uint32_t qs = base + kOffQ + (uint32_t)h * kTile;
+#pragma unroll
+        for (int k = 0; k < kD / 16; ++k) {
+          const uint32_t koff = (uint32_t)(k >> 2) * kSlab + (uint32_t)(k & 3) * 32;
+          umma_ss(tmem + (uint32_t)h * 128, desc_sw128(qs + koff, 16, 1024),
+                  desc_sw128(ks + koff, 16, 1024), idS, k > 0 ? 1u : 0u);
+        }
+        umma_commit(s_full(h));
+      };
+      auto o_mma = [&](int h, int j) -> bool {
+        if (!wait_bar(p_full(h), j & 1, err, status)) return false;
+        tc_fence_after();
+        const uint32_t vs = base + kOffStage + (uint32_t)(j & 1) * 2 * kTile + kTile;
+#pragma unroll
+        for (int k = 0; k < kTN / 16; ++k) {
+          const uint64_t bd = desc_sw128(vs + (uint32_t)k * 16 * 128, kSlab, 1024);
+          umma_ts(tmem + kColO + (uint32_t)h * 128, tmem + (uint32_t)h * 128 + (uint32_t)k * 8,
+                  bd, idO, (j > 0 || k > 0) ? 1u : 0u);
+        }
+        umma_commit(o_done(h));
+        return true;
+      };
+      bool ok = wait_bar(q_full(), 0, err, status) && wait_bar(kv_full(0), 0, err, status);
+      if (ok) {
+        tc_fence_after();
+        for (int h = 0; h < ntq; ++h) s_mma(h, 0);
+      }
+      for (int j = 0; ok && j < ntiles; ++j) {
+        const bool more = j + 1 < ntiles;
+        for (int h = 0; ok && h < ntq; ++h) {
+          if (!o_mma(h, j)) {
+            ok = false;
+            break;
+          }
+          if (h == ntq - 1) umma_commit(kv_empty(j & 1));  // K_j, V_j no longer read
+          if (more) {
+            if (h == 0) {
+              if (!wait_bar(kv_full((j + 1) & 1), ((j + 1) >> 1) & 1, err, status)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+            }
+            s_mma(h, j + 1);  // overwrites P_h of tile j, consumed by the O MMA above
+          }
+        }
+      }
+      // every MMA issued above is complete before TMEM is released
+      umma_commit(mma_done);
+      wait_bar(mma_done, 0, err, status);
+    }
+    __syncwarp();
+  } else if (warp >= 4 && (warp - 4) / 4 < ntq) {
+    // ------------------------------------------------ softmax of tile h, one row per thread
+    const int h = (warp - 4) / 4;
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const int node = (mt0 + h) * nodes_per_tile + row / a.group;
+    const int g = row % a.group;
+    const uint64_t mask = tree_mask ? tree_mask[(int64_t)b * a.nq + node] : 0ull;
+    auto visible = [&](int64_t t) -> bool {
+      if (t < ctx) return true;
+      if (t >= T) return false;
+      const int i = (int)(t - ctx);
+      return tree_mask ? ((mask >> i) & 1ull) != 0 : i <= node;
+    };
+    const uint32_t sc = tmem + lane_base + (uint32_t)h * 128;
+    const uint32_t oc = tmem + lane_base + kColO + (uint32_t)h * 128;
+    float m_used = -INFINITY, l = 0.0f;
+    bool ok = true;
+    for (int j = 0; j < ntiles; ++j) {
+      if (!wait_bar(s_full(h), j & 1, err, status)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int64_t t0 = (int64_t)j * kTN;
+      const bool whole = t0 + kTN <= ctx;
+      // the row's 128 scores: four loads in flight, one wait
+      uint32_t r[128];
+      tmem_ld32(sc + 0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+      tmem_ld32(sc + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+      tmem_ld32(sc + 64, *reinterpret_cast<uint32_t(*)[32]>(&r[64]));
+      tmem_ld32(sc + 96, *reinterpret_cast<uint32_t(*)[32]>(&r[96]));
+      tmem_ld_wait();
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int i = 0; i < 128; ++i) {
+        float s = __uint_as_float(r[i]) * a.scale_log2;
+        if (!whole && !visible(t0 + i)) s = -INFINITY;
+        r[i] = __float_as_uint(s);
+        mx4[i & 3] = fmaxf(mx4[i & 3], s);
+      }
+      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+      const float m_new = fmaxf(m_used, mx);
+      bool need = false;
+      if (j == 0) {
+        m_used = m_new;
+      } else {
+        need = m_new > m_used + 8.0f;
+      }
+      if (__any_sync(0xffffffffu, need)) {
+        // S_h of tile j was issued after O_h of tile j-1, so O_h is final
+        // for tile j-1 by now; the wait only confirms it
+        if (!wait_bar(o_done(h), (j - 1) & 1, err, status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const float alpha = need ? kyro::ptx::fast_exp2(m_used - m_new) : 1.0f;
+        if (need) {
+          m_used = m_new;
+          l *= alpha;
+        }
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld32(oc + c * 32, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(oc + c * 32, o);
+        }
+        tmem_st_wait();
+      }
+      const float ref = m_used == -INFINITY ? 0.0f : m_used;
+      float l4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float p0 = kyro::ptx::fast_exp2(__uint_as_float(r[c * 32 + 2 * i]) - ref);
+          const float p1 = kyro::ptx::fast_exp2(__uint_as_float(r[c * 32 + 2 * i + 1]) - ref);
+          l4[i & 3] += p0 + p1;
+          pk[i] = kyro::ptx::pack_bf16x2(p0, p1);
+        }
+        tmem_st16(sc + c * 16, pk);  // P over the scores (all read above)
+      }
+      l += (l4[0] + l4[1]) + (l4[2] + l4[3]);
+      tmem_st_wait();
+      tc_fence_before();
+      kyro::ptx::mbar_arrive(p_full(h));
+    }
+    if (ok && ntiles > 0 && wait_bar(o_done(h), (ntiles - 1) & 1, err, status)) {
+      tc_fence_after();
+      const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+      __nv_bfloat16* orow =
+          out + (((int64_t)b * a.nq + node) * a.hq + (int64_t)kvh * a.group + g) * kD;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o[32];
+        tmem_ld32(oc + c * 32, o);
+        tmem_ld_wait();
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          pk[i] = kyro::ptx::pack_bf16x2(__uint_as_float(o[2 * i]) * inv,
+                                         __uint_as_float(o[2 * i + 1]) * inv);
+        uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+        for (int v = 0; v < 4; ++v)
+          dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 2) tmem_dealloc(tmem, kTmemCols);
+}
+
+// ---------------------------------------------------------------- host side
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 3-D bf16 map with 128-byte swizzle: dims (innermost first), strides of the
+// outer two dims in bytes, box (64, box1, box2).
+int make_map3(CUtensorMap* map, const void* ptr, uint64_t d0, uint64_t d1, uint64_t d2,
+              uint64_t s1, uint64_t s2, uint32_t box1, uint32_t box2) {
+  auto enc = encode_fn();
+  if (!enc) return kyro::set_error(KYRO_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {s1, s2};
+  cuuint32_t box[3] = {64, box1, box2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims,
+                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return kyro::set_error(KYRO_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return KYRO_OK;
+}
+
+}  // namespace
+
+namespace kyro {
+
+// The shapes this kernel takes: head_dim 128, 16-token blocks, and query
+// rows that fill 128-row tiles node-major (group divides 128, and the tree
+// size is a multiple of 128/group).
+bool tree_attention_eligible(const kyro_attn_params* p) {
+  if (!p || p->head_dim != kD || p->block_size != kBS || p->num_kv_heads <= 0) return false;
+  if (p->num_heads % p->num_kv_heads) return false;
+  const int group = p->num_heads / p->num_kv_heads;
+  if (group > kTM || kTM % group) return false;
+  const int npt = kTM / group;
+  return p->num_query >= npt && p->num_query % npt == 0 && p->num_query <= 64;
+}
+
+int tree_attention_launch(kyro_ctx* ctx, const kyro_attn_params* p, const void* q,
+                          const void* k_cache, const void* v_cache, const int64_t* block_table,
+                          const int64_t* context_lens, const uint64_t* tree_mask, void* out) {
+  const int group = p->num_heads / p->num_kv_heads;
+  KY_REQUIRE((uintptr_t)q % 16 == 0 && (uintptr_t)k_cache % 16 == 0 &&
+                 (uintptr_t)v_cache % 16 == 0 && (uintptr_t)out % 16 == 0,
+             "kyro_verify_attention: q, caches and out must be 16-byte aligned");
+  CUtensorMap mq, mk, mv;
+  // Q [B*nq nodes][Hq heads][128]: box (64, group heads, 128/group nodes)
+  KY_TRY(make_map3(&mq, q, kD, (uint64_t)p->num_heads, (uint64_t)p->batch * p->num_query,
+                   (uint64_t)kD * 2, (uint64_t)p->num_heads * kD * 2, (uint32_t)group,
+                   (uint32_t)(kTM / group)));
+  // K, V [blocks*Hkv][16 tokens][128]: box (64, 16, 1)
+  const uint64_t rows = (uint64_t)p->num_blocks * p->num_kv_heads;
+  KY_TRY(make_map3(&mk, k_cache, kD, kBS, rows, (uint64_t)kD * 2, (uint64_t)kBS * kD * 2, kBS, 1));
+  KY_TRY(make_map3(&mv, v_cache, kD, kBS, rows, (uint64_t)kD * 2, (uint64_t)kBS * kD * 2, kBS, 1));
+  TcArgs a;
+  a.B = p->batch;
+  a.nq = p->num_query;
+  a.hq = p->num_heads;
+  a.hkv = p->num_kv_heads;
+  a.group = group;
+  a.max_blocks = p->max_blocks_per_seq;
+  a.num_blocks = p->num_blocks;
+  const float scale = p->scale > 0.0f ? p->scale : 1.0f / sqrtf((float)kD);
+  a.scale_log2 = scale * 1.4426950408889634f;
+  static std::once_flag attr_once;
+  std::call_once(attr_once, [] {
+    cudaFuncSetAttribute(tree_attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         kSmemTc);
+  });
+  const int mtiles = p->num_query * group / kTM;
+  const dim3 grid((unsigned)((mtiles + kTilesPerCta - 1) / kTilesPerCta),
+                  (unsigned)p->num_kv_heads, (unsigned)p->batch);
+  tree_attention_tc_kernel<<<grid, kTcThreads, kSmemTc, ctx->stream>>>(
+      mq, mk, mv, a, block_table, context_lens, tree_mask, (__nv_bfloat16*)out, ctx->d_status);
+  return kyro::check_launch("tree_attention_tc_kernel");
+}
+
+}  // namespace kyro
