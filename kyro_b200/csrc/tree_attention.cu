@@ -48,9 +48,13 @@ constexpr int kTcThreads = 384;
 constexpr int kTilesPerCta = 2;
 constexpr uint32_t kSlab = 128 * 128;         // one 64-column slab of a 128-row tile
 constexpr uint32_t kTile = 2 * kSlab;         // 128 rows x 128 bf16
-constexpr uint32_t kOffQ = 0;                 // Q tile h at h * kTile
-constexpr uint32_t kOffStage = 2 * kTile;     // stage s: K at +s*2*kTile, V after it
-constexpr uint32_t kTilesBytes = 2 * kTile + 2 * 2 * kTile;  // 2 Q tiles + 2 stages of K, V
+// K and V tiles share one ring of kSlots buffers, filled in the order
+// K_0 V_0 K_1 V_1 ... (item n: K_{n/2} for even n, V_{n/2} for odd n) and
+// released in the same order, so about two tiles of loads stay in flight
+constexpr int kSlots = 5;
+constexpr uint32_t kOffQ = 0;                                // Q tile h at h * kTile
+constexpr uint32_t kOffRing = 2 * kTile;                     // slot s at + s * kTile
+constexpr uint32_t kTilesBytes = kOffRing + kSlots * kTile;  // 224 KB
 constexpr uint32_t kSmemTc = kTilesBytes + 256 + 1024;       // + barriers, alignment slack
 constexpr uint32_t kTmemCols = 512;           // S_h at h*128, O_h at 256 + h*128
 constexpr uint32_t kColO = 256;
@@ -170,6 +174,71 @@ __host__ __device__ constexpr uint32_t idesc_bf16(bool b_mn) {
          | ((uint32_t)(kTM >> 4) << 24);  // M = 128
 }
 
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Maximum of a row's 128 scores (raw units): four max3 chains.
+__device__ __forceinline__ float row_max128(const uint32_t (&r)[128]) {
+  float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < 128; i += 8) {
+    m0 = fmax3(m0, __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
+    m1 = fmax3(m1, __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
+    m2 = fmax3(m2, __uint_as_float(r[i + 4]), __uint_as_float(r[i + 5]));
+    m3 = fmax3(m3, __uint_as_float(r[i + 6]), __uint_as_float(r[i + 7]));
+  }
+  return fmax3(fmax3(m0, m1, m2), m3, -INFINITY);
+}
+
+// 2^x on the FMA pipe, for a share of the probabilities so that the
+// special-function unit is not the only exp2 engine.  x is rounded to
+// n + f with |f| <= 1/2 (the 1.5 * 2^23 addition), 2^f is a degree-3
+// polynomial fitted here for minimum relative error on [-1/2, 1/2]
+// (7.5e-5, far below the bf16 rounding of P), and n is added to the
+// exponent field.  x is clamped at -120 so the result stays normal; such
+// terms (< 2^-119 against a row maximum of 1) vanish in bf16 sums.
+__device__ __forceinline__ float exp2_poly(float x) {
+  x = fmaxf(x, -120.0f);
+  const float t = x + 12582912.0f;
+  const float f = x - (t - 12582912.0f);
+  float p = fmaf(0.0551716685f, f, 0.2426111251f);
+  p = fmaf(p, f, 0.6932609677f);
+  p = fmaf(p, f, 0.9999280572f);
+  return __int_as_float(__float_as_int(p) + ((__float_as_int(t) - 0x4B400000) << 23));
+}
+
+// Pairs of probabilities per 16 whose exp2 runs on the FMA pipe.
+constexpr int kPolyPairs = 0;
+
+// P = 2^(s * sl2 - m) for half kHalf of a row's 128 scores (64 tokens),
+// written as bf16 pairs over those scores in TMEM; returns their sum.  With
+// kPoly (tiles without masked scores) kPolyPairs of every 16 pairs use
+// exp2_poly.
+template <bool kPoly, int kHalf>
+__device__ __forceinline__ float exp_store(const uint32_t (&r)[128], float sl2, float nref,
+                                           uint32_t sc) {
+  float l4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+  for (int c = 2 * kHalf; c < 2 * kHalf + 2; ++c) {
+    uint32_t pk[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float x0 = fmaf(__uint_as_float(r[c * 32 + 2 * i]), sl2, nref);
+      const float x1 = fmaf(__uint_as_float(r[c * 32 + 2 * i + 1]), sl2, nref);
+      const bool poly = kPoly && ((i * kPolyPairs) % 16) < kPolyPairs;
+      const float p0 = poly ? exp2_poly(x0) : kyro::ptx::fast_exp2(x0);
+      const float p1 = poly ? exp2_poly(x1) : kyro::ptx::fast_exp2(x1);
+      l4[i & 3] += p0 + p1;
+      pk[i] = kyro::ptx::pack_bf16x2(p0, p1);
+    }
+    tmem_st16(sc + c * 16, pk);  // P over the scores (all read before)
+  }
+  return (l4[0] + l4[1]) + (l4[2] + l4[3]);
+}
+
 __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, int* err, uint32_t* status) {
   if (kyro::ptx::mbar_wait_bounded(bar, parity, kTcWaitBudget)) return true;
   *(volatile int*)err = 1;
@@ -191,14 +260,19 @@ tree_attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
   uint8_t* gbase = smem_raw + (base - raw);
   const uint32_t bar0 = base + kTilesBytes;
   auto q_full = [&]() { return bar0; };
-  auto kv_full = [&](int s) { return bar0 + 8u * (1 + s); };
-  auto kv_empty = [&](int s) { return bar0 + 8u * (3 + s); };
-  auto s_full = [&](int h) { return bar0 + 8u * (5 + h); };
-  auto p_full = [&](int h) { return bar0 + 8u * (7 + h); };
-  auto o_done = [&](int h) { return bar0 + 8u * (9 + h); };
-  const uint32_t mma_done = bar0 + 8u * 11;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + kTilesBytes + 128);
-  int* err = reinterpret_cast<int*>(gbase + kTilesBytes + 132);
+  auto slot_full = [&](int s) { return bar0 + 8u * (1 + s); };
+  auto slot_empty = [&](int s) { return bar0 + 8u * (1 + kSlots + s); };
+  auto s_full = [&](int h) { return bar0 + 8u * (1 + 2 * kSlots + h); };
+  // P of tile h reaches the MMA warp in two halves of 64 tokens
+  auto p_full = [&](int h, int half) { return bar0 + 8u * (3 + 2 * kSlots + 2 * h + half); };
+  auto o_done = [&](int h) { return bar0 + 8u * (7 + 2 * kSlots + h); };
+  const uint32_t mma_done = bar0 + 8u * (9 + 2 * kSlots);
+  // ring item n lives in slot n % kSlots; its fill is that slot's phase n / kSlots
+  auto item_slot = [](int n) { return n % kSlots; };
+  auto item_parity = [](int n) { return (uint32_t)((n / kSlots) & 1); };
+  auto item_addr = [&](int n) { return base + kOffRing + (uint32_t)(n % kSlots) * kTile; };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + kTilesBytes + 240);
+  int* err = reinterpret_cast<int*>(gbase + kTilesBytes + 244);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kvh = blockIdx.y, b = blockIdx.z;
@@ -218,11 +292,14 @@ tree_attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
 
   if (threadIdx.x == 0) {
     kyro::ptx::mbar_init(q_full(), 1);
+    for (int i = 0; i < kSlots; ++i) {
+      kyro::ptx::mbar_init(slot_full(i), 1);
+      kyro::ptx::mbar_init(slot_empty(i), 1);
+    }
     for (int i = 0; i < 2; ++i) {
-      kyro::ptx::mbar_init(kv_full(i), 1);
-      kyro::ptx::mbar_init(kv_empty(i), 1);
       kyro::ptx::mbar_init(s_full(i), 1);
-      kyro::ptx::mbar_init(p_full(i), 128);
+      kyro::ptx::mbar_init(p_full(i, 0), 128);
+      kyro::ptx::mbar_init(p_full(i, 1), 128);
       kyro::ptx::mbar_init(o_done(i), 1);
     }
     kyro::ptx::mbar_init(mma_done, 1);
@@ -261,39 +338,49 @@ tree_attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
           ids[i] = __ldg(&bt[tb < nblk ? tb : 0]);  // blocks past the end: any block, masked
         }
       };
-      fetch_ids(0);
-      int issued = 0;
-      for (int j = 0; j < ntiles; ++j) {
-        const int s = j & 1;
-        int64_t cur[kTileBlocks];
-#pragma unroll
-        for (int i = 0; i < kTileBlocks; ++i) cur[i] = ids[i];
-        if (j + 1 < ntiles) fetch_ids(j + 1);
-        if (j >= 2 && !wait_bar(kv_empty(s), ((j - 2) >> 1) & 1, err, status)) break;
-        if (*(volatile int*)err) break;
-        kyro::ptx::mbar_arrive_expect_tx(kv_full(s), 2 * kTile);
-        const uint32_t ks = base + kOffStage + (uint32_t)s * 2 * kTile;
-        const uint32_t vs = ks + kTile;
+      auto load_item = [&](int n, const int64_t (&bids)[kTileBlocks]) {
+        const CUtensorMap* map = (n & 1) ? &tmV : &tmK;
+        const uint32_t dst = item_addr(n), bar = slot_full(item_slot(n));
+        kyro::ptx::mbar_arrive_expect_tx(bar, kTile);
 #pragma unroll
         for (int i = 0; i < kTileBlocks; ++i) {
-          int64_t bid = cur[i];
+          int64_t bid = bids[i];
           if (bid < 0 || bid >= a.num_blocks) {
             kyro::dev::flag(status, KYRO_DEV_BAD_BLOCK);
             bid = 0;
           }
           const int32_t z = (int32_t)(bid * a.hkv + kvh);
           const uint32_t off = (uint32_t)i * kBS * 128;
-          kyro::ptx::tma_load_3d(ks + off, &tmK, 0, 0, z, kv_full(s));
-          kyro::ptx::tma_load_3d(ks + kSlab + off, &tmK, 64, 0, z, kv_full(s));
-          kyro::ptx::tma_load_3d(vs + off, &tmV, 0, 0, z, kv_full(s));
-          kyro::ptx::tma_load_3d(vs + kSlab + off, &tmV, 64, 0, z, kv_full(s));
+          kyro::ptx::tma_load_3d(dst + off, map, 0, 0, z, bar);
+          kyro::ptx::tma_load_3d(dst + kSlab + off, map, 64, 0, z, bar);
         }
-        ++issued;
+      };
+      fetch_ids(0);
+      int issued = 0;  // ring items
+      for (int j = 0; j < ntiles; ++j) {
+        int64_t cur[kTileBlocks];
+#pragma unroll
+        for (int i = 0; i < kTileBlocks; ++i) cur[i] = ids[i];
+        if (j + 1 < ntiles) fetch_ids(j + 1);
+        bool stop = false;
+        for (int n = 2 * j; n < 2 * j + 2; ++n) {
+          if (n >= kSlots && !wait_bar(slot_empty(item_slot(n)), item_parity(n - kSlots), err, status)) {
+            stop = true;
+            break;
+          }
+          if (*(volatile int*)err) {
+            stop = true;
+            break;
+          }
+          load_item(n, cur);
+          ++issued;
+        }
+        if (stop) break;
       }
       // every copy this thread started has landed before the CTA moves on
       wait_bar(q_full(), 0, err, status);
-      for (int j = issued - 2 < 0 ? 0 : issued - 2; j < issued; ++j)
-        wait_bar(kv_full(j & 1), (j >> 1) & 1, err, status);
+      for (int n = issued - kSlots < 0 ? 0 : issued - kSlots; n < issued; ++n)
+        wait_bar(slot_full(item_slot(n)), item_parity(n), err, status);
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -301,7 +388,7 @@ tree_attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
     if (lane == 0) {
       constexpr uint32_t idS = idesc_bf16(false), idO = idesc_bf16(true);
       auto s_mma = [&](int h, int j) {
-        const uint32_t ks = base + kOffStage + (uint32_t)(j & 1) * 2 * kTile;
+        const uint32_t ks = item_addr(2 * j);
         const uint32_t qs = base + kOffQ + (uint32_t)h * kTile;
 #pragma unroll
         for (int k = 0; k < kD / 16; ++k) {
@@ -310,21 +397,28 @@ tree_attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                   desc_sw128(ks + koff, 16, 1024), idS, k > 0 ? 1u : 0u);
         }
         umma_commit(s_full(h));
+        if (h == ntq - 1) umma_commit(slot_empty(item_slot(2 * j)));  // K_j no longer read
       };
       auto o_mma = [&](int h, int j) -> bool {
-        if (!wait_bar(p_full(h), j & 1, err, status)) return false;
-        tc_fence_after();
-        const uint32_t vs = base + kOffStage + (uint32_t)(j & 1) * 2 * kTile + kTile;
+        const uint32_t vs = item_addr(2 * j + 1);
+        for (int half = 0; half < 2; ++half) {
+          if (!wait_bar(p_full(h, half), j & 1, err, status)) return false;
+          if (half == 0 && h == 0 &&
+              !wait_bar(slot_full(item_slot(2 * j + 1)), item_parity(2 * j + 1), err, status))
+            return false;
+          tc_fence_after();
 #pragma unroll
-        for (int k = 0; k < kTN / 16; ++k) {
-          const uint64_t bd = desc_sw128(vs + (uint32_t)k * 16 * 128, kSlab, 1024);
-          umma_ts(tmem + kColO + (uint32_t)h * 128, tmem + (uint32_t)h * 128 + (uint32_t)k * 8,
-                  bd, idO, (j > 0 || k > 0) ? 1u : 0u);
+          for (int k = 4 * half; k < 4 * half + 4; ++k) {
+            const uint64_t bd = desc_sw128(vs + (uint32_t)k * 16 * 128, kSlab, 1024);
+            umma_ts(tmem + kColO + (uint32_t)h * 128, tmem + (uint32_t)h * 128 + (uint32_t)k * 8,
+                    bd, idO, (j > 0 || k > 0) ? 1u : 0u);
+          }
         }
         umma_commit(o_done(h));
+        if (h == ntq - 1) umma_commit(slot_empty(item_slot(2 * j + 1)));  // V_j no longer read
         return true;
       };
-      bool ok = wait_bar(q_full(), 0, err, status) && wait_bar(kv_full(0), 0, err, status);
+      bool ok = wait_bar(q_full(), 0, err, status) && wait_bar(slot_full(0), 0, err, status);
       if (ok) {
         tc_fence_after();
         for (int h = 0; h < ntq; ++h) s_mma(h, 0);
@@ -336,10 +430,10 @@ tree_attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
             ok = false;
             break;
           }
-          if (h == ntq - 1) umma_commit(kv_empty(j & 1));  // K_j, V_j no longer read
           if (more) {
             if (h == 0) {
-              if (!wait_bar(kv_full((j + 1) & 1), ((j + 1) >> 1) & 1, err, status)) {
+              const int nk = 2 * (j + 1);
+              if (!wait_bar(slot_full(item_slot(nk)), item_parity(nk), err, status)) {
                 ok = false;
                 break;
               }
@@ -362,13 +456,22 @@ tree_attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     const int node = (mt0 + h) * nodes_per_tile + row / a.group;
     const int g = row % a.group;
-    const uint64_t mask = tree_mask ? tree_mask[(int64_t)b * a.nq + node] : 0ull;
-    auto visible = [&](int64_t t) -> bool {
-      if (t < ctx) return true;
-      if (t >= T) return false;
-      const int i = (int)(t - ctx);
-      return tree_mask ? ((mask >> i) & 1ull) != 0 : i <= node;
+    // bit i: the row sees draft node i (its ancestors and itself under a
+    // tree mask, nodes 0..node for a chain); nothing at or past nq
+    uint64_t tbits = tree_mask ? tree_mask[(int64_t)b * a.nq + node]
+                               : (node >= 63 ? ~0ull : (1ull << (node + 1)) - 1ull);
+    if (a.nq < 64) tbits &= (1ull << a.nq) - 1ull;
+    // visibility of tokens tw .. tw+31: the context below ctx, then tbits
+    auto vis_word = [&](int64_t tw) -> uint32_t {
+      const int64_t d = ctx - tw;
+      const uint32_t wc = d >= 32 ? 0xffffffffu : d <= 0 ? 0u : ((1u << (uint32_t)d) - 1u);
+      const int64_t rel = tw - ctx;
+      uint32_t wt = 0;
+      if (rel >= 0 && rel < 64) wt = (uint32_t)(tbits >> rel);
+      else if (rel < 0 && rel > -32) wt = (uint32_t)(tbits << (uint32_t)(-rel));
+      return wc | wt;
     };
+    const float sl2 = a.scale_log2;
     const uint32_t sc = tmem + lane_base + (uint32_t)h * 128;
     const uint32_t oc = tmem + lane_base + kColO + (uint32_t)h * 128;
     float m_used = -INFINITY, l = 0.0f;
@@ -380,7 +483,7 @@ tree_attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
       }
       tc_fence_after();
       const int64_t t0 = (int64_t)j * kTN;
-      const bool whole = t0 + kTN <= ctx;
+      const bool whole = t0 + kTN <= ctx;  // no masked score in the tile
       // the row's 128 scores: four loads in flight, one wait
       uint32_t r[128];
       tmem_ld32(sc + 0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
@@ -388,16 +491,16 @@ tree_attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
       tmem_ld32(sc + 64, *reinterpret_cast<uint32_t(*)[32]>(&r[64]));
       tmem_ld32(sc + 96, *reinterpret_cast<uint32_t(*)[32]>(&r[96]));
       tmem_ld_wait();
-      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      if (!whole) {
+        uint32_t vis[4];
 #pragma unroll
-      for (int i = 0; i < 128; ++i) {
-        float s = __uint_as_float(r[i]) * a.scale_log2;
-        if (!whole && !visible(t0 + i)) s = -INFINITY;
-        r[i] = __float_as_uint(s);
-        mx4[i & 3] = fmaxf(mx4[i & 3], s);
+        for (int w = 0; w < 4; ++w) vis[w] = vis_word(t0 + 32 * w);
+#pragma unroll
+        for (int i = 0; i < 128; ++i)
+          if (!((vis[i >> 5] >> (i & 31)) & 1u)) r[i] = 0xff800000u;  // -inf
       }
-      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
-      const float m_new = fmaxf(m_used, mx);
+      // scores stay raw; the log2 scale enters the max and the exp2 argument
+      const float m_new = fmaxf(m_used, row_max128(r) * sl2);
       bool need = false;
       if (j == 0) {
         m_used = m_new;
@@ -428,24 +531,16 @@ tree_attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
         }
         tmem_st_wait();
       }
-      const float ref = m_used == -INFINITY ? 0.0f : m_used;
-      float l4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float p0 = kyro::ptx::fast_exp2(__uint_as_float(r[c * 32 + 2 * i]) - ref);
-          const float p1 = kyro::ptx::fast_exp2(__uint_as_float(r[c * 32 + 2 * i + 1]) - ref);
-          l4[i & 3] += p0 + p1;
-          pk[i] = kyro::ptx::pack_bf16x2(p0, p1);
-        }
-        tmem_st16(sc + c * 16, pk);  // P over the scores (all read above)
-      }
-      l += (l4[0] + l4[1]) + (l4[2] + l4[3]);
+      const float nref = m_used == -INFINITY ? 0.0f : -m_used;
+      // the first 64 tokens' P goes to the MMA warp while the rest is computed
+      l += whole ? exp_store<true, 0>(r, sl2, nref, sc) : exp_store<false, 0>(r, sl2, nref, sc);
       tmem_st_wait();
       tc_fence_before();
-      kyro::ptx::mbar_arrive(p_full(h));
+      kyro::ptx::mbar_arrive(p_full(h, 0));
+      l += whole ? exp_store<true, 1>(r, sl2, nref, sc) : exp_store<false, 1>(r, sl2, nref, sc);
+      tmem_st_wait();
+      tc_fence_before();
+      kyro::ptx::mbar_arrive(p_full(h, 1));
     }
     if (ok && ntiles > 0 && wait_bar(o_done(h), (ntiles - 1) & 1, err, status)) {
       tc_fence_after();
