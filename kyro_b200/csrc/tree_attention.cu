@@ -7,27 +7,38 @@
 // head, 512 rows for config 2, which fill 128-row MMA tiles.  The chain case
 // (24 rows) stays on the mma.sync kernel of attention.cu.
 //
-// One CTA = (two 128-row query tiles, one KV head, one sequence).  Rows are
-// ordered node-major: row r = node_local * group + head_in_group, so a Q
-// tile is a TMA box of (128/group nodes) x (group heads) x 128 dims.  The
-// two tiles share every K/V load.  Per 128-token KV tile j (8 paged blocks):
-//   warp 0 (producer)  TMA loads of K_j and V_j into a 2-stage ring (128-byte
-//                      swizzle, no multicast; a 16-token block is one box
-//                      per 64-column slab)
-//   warp 1 (MMA)       S_h = Q_h K_j^T into tile h's TMEM score buffer, and
-//                      after tile h's softmax O_h += P_h V_j with P read
-//                      from TMEM (the TS form) and V from shared memory
-//                      (MN-major).  The order S0 S1 | O0 S0' | O1 S1' | ...
-//                      lets one tile's softmax run while the other tile's
-//                      MMAs do (ping-pong).
-//   warps 4-7, 8-11    the softmax of tile 0 and of tile 1, one query row
-//                      per thread (its TMEM lane): mask, online max and sum,
-//                      P = exp2(s - m) written back over the scores as bf16,
-//                      and the O rescale when the running max grows by more
-//                      than 2^8
+// A cluster of two CTAs (an SM pair) = (four 128-row query tiles, one KV
+// head, one sequence).  Rows are ordered node-major: row r = node_local *
+// group + head_in_group, so a Q tile is a TMA box of (128/group nodes) x
+// (group heads) x 128 dims.  CTA `rank` of pair p holds tiles 4p + 2h + rank
+// (h = 0, 1); the pair's MMAs are tcgen05.mma.cta_group::2 with M = 256, one
+// instruction covering tile h of both CTAs, which runs about 1.5x faster per
+// SM than two M = 128 instructions.  For S = Q K^T each CTA holds 64 of a
+// KV tile's 128 tokens of K, for O += P V all 128 tokens of one 64-dim slab
+// of V, so every K/V byte is loaded once per (sequence, KV head).  Per
+// 128-token KV tile j (8 paged blocks):
+//   warps 0-3, 4-7     the softmax of tile 0 and of tile 1, one query row
+//                      per thread (its TMEM lane, so warp w reads lanes
+//                      32*(w%4)..): mask, online max and sum, P = exp2(s - m)
+//                      written back over the scores as bf16 in two 64-token
+//                      halves, and the O rescale when the running max grows
+//                      by more than 2^8.  A row's scores are read from TMEM
+//                      twice (all 128 for the maximum, then 64 at a time),
+//                      which keeps a thread within 168 registers.
+//   warp 8 (producer)  TMA loads of this CTA's half of K_j and V_j into a
+//                      ring of 16 KB slots (128-byte swizzle, no multicast;
+//                      the .cta_group::2 form completes them on the leader
+//                      CTA's barrier, which expects both halves)
+//   warp 9 (MMA)       in the leader only: S_h = Q_h K_j^T, and after each
+//                      half of tile h's softmax (both CTAs) O_h += P_h V_j
+//                      with P read from TMEM and V from shared memory
+//                      (MN-major).  The order S0 S1 | O0 S0' | O1 S1' lets
+//                      one tile's softmax run while the other's MMAs do.
+//                      Commits reach both CTAs' barriers (multicast commit).
+//                      Warp 9 of each CTA also owns the pair's TMEM.
 // The output is O / l, written as bf16.  Every wait is bounded; a wait that
-// runs out sets KYRO_DEV_WAIT_TIMEOUT, and the CTA still waits (bounded)
-// for its own copies and MMAs before it frees its TMEM.
+// runs out sets KYRO_DEV_WAIT_TIMEOUT, and both CTAs still wait (bounded)
+// for the leader's MMAs before they free TMEM.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_bf16.h>
@@ -44,18 +55,22 @@ constexpr int kD = 128;                       // head dim
 constexpr int kTM = 128;                      // query rows per CTA
 constexpr int kTN = 128;                      // KV tokens per tile
 constexpr int kTileBlocks = kTN / kBS;        // 8
-constexpr int kTcThreads = 384;
+constexpr int kTcThreads = 320;
+constexpr int kProducerWarp = 8, kMmaWarp = 9;
 constexpr int kTilesPerCta = 2;
 constexpr uint32_t kSlab = 128 * 128;         // one 64-column slab of a 128-row tile
 constexpr uint32_t kTile = 2 * kSlab;         // 128 rows x 128 bf16
-// K and V tiles share one ring of kSlots buffers, filled in the order
+constexpr uint32_t kItem = 16384;             // one CTA's half of a K or V tile
+constexpr uint32_t kKSlab = 64 * 128;         // 64 tokens x 64 dims of K
+// K and V halves share one ring of kSlots buffers, filled in the order
 // K_0 V_0 K_1 V_1 ... (item n: K_{n/2} for even n, V_{n/2} for odd n) and
-// released in the same order, so about two tiles of loads stay in flight
-constexpr int kSlots = 5;
-constexpr uint32_t kOffQ = 0;                                // Q tile h at h * kTile
-constexpr uint32_t kOffRing = 2 * kTile;                     // slot s at + s * kTile
-constexpr uint32_t kTilesBytes = kOffRing + kSlots * kTile;  // 224 KB
-constexpr uint32_t kSmemTc = kTilesBytes + 256 + 1024;       // + barriers, alignment slack
+// released in the same order.  The ring comes first and the Q tiles after
+// it, so every operand read stays inside the allocation.
+constexpr int kSlots = 10;
+constexpr uint32_t kOffRing = 0;                             // slot s at s * kItem
+constexpr uint32_t kOffQ = kSlots * kItem;                   // Q tile h at + h * kTile
+constexpr uint32_t kTilesBytes = kOffQ + 2 * kTile;          // 224 KB
+constexpr uint32_t kSmemTc = kTilesBytes + 512 + 1024;       // + barriers, alignment slack
 constexpr uint32_t kTmemCols = 512;           // S_h at h*128, O_h at 256 + h*128
 constexpr uint32_t kColO = 256;
 constexpr long long kTcWaitBudget = 2000000000ll;
@@ -66,48 +81,87 @@ struct TcArgs {
 };
 
 // ---------------------------------------------------------------- tcgen05
-__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
-               "r"(ncols)
-               : "memory");
-}
-__device__ __forceinline__ void tmem_relinquish() {
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
-               : "memory");
-}
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
 __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
-// D[tmem] (+)= A[smem] * B[smem]
-__device__ __forceinline__ void umma_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
-                                        uint32_t acc) {
+// ---------------------------------------------------------------- CTA pair
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" :::
+                   "memory");
+}
+// The leader CTA's (rank 0) copy of a shared-memory object, as a
+// shared::cluster address.
+__device__ __forceinline__ uint32_t leader_addr(uint32_t local) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(r) : "r"(local));
+  return r;
+}
+// Arrive on a barrier of either CTA of the pair (default semantics, release
+// at CTA scope).  TMEM written before it is ordered by tcgen05.wait::st and
+// tcgen05.fence::before_thread_sync, and the MMA issued after the matching
+// wait by tcgen05.fence::after_thread_sync; a cluster-scope release here
+// costs about a thousand cycles per arrive and orders nothing more.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+// 3-D tile load into this CTA's shared memory that completes on a barrier of
+// either CTA of the pair (.cta_group::2; no multicast).
+__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap* map, int32_t x,
+                                                 int32_t y, int32_t z, uint32_t cluster_bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(cluster_bar)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_alloc2(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish2() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc2(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+// D (+)= A[smem] * B[smem] over the pair: each CTA supplies its 128 rows of A
+// and half of B's N columns at the same shared-memory offsets.
+__device__ __forceinline__ void umma2_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
+                                         uint32_t acc) {
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
       "l"(a), "l"(b), "r"(idesc), "r"(acc)
       : "memory");
 }
-// D[tmem] (+)= A[tmem] * B[smem]
-__device__ __forceinline__ void umma_ts(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc,
-                                        uint32_t acc) {
+// D (+)= A[tmem] * B[smem] over the pair (A: each CTA's own TMEM rows).
+__device__ __forceinline__ void umma2_ts(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc,
+                                         uint32_t acc) {
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
       "r"(a), "l"(b), "r"(idesc), "r"(acc)
       : "memory");
 }
-// arrive on `bar` when every tcgen05.mma this thread issued so far is done
-__device__ __forceinline__ void umma_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   bar)
-               : "memory");
+// Arrive on `bar` in both CTAs when every MMA issued so far is done.
+__device__ __forceinline__ void umma2_commit_both(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 "
+      "[%0], %1;" ::"r"(bar),
+      "h"((uint16_t)3)
+      : "memory");
 }
+
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
@@ -164,14 +218,14 @@ __device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr, uint32_t lbo, uin
 }
 
 // Instruction descriptor of kind::f16: bf16 A and B, fp32 accumulate,
-// M = 128, N = 128; b_mn selects an MN-major B.
+// M = 256 (a CTA pair), N = 128; b_mn selects an MN-major B.
 __host__ __device__ constexpr uint32_t idesc_bf16(bool b_mn) {
   return (1u << 4)              // D fp32
          | (1u << 7)            // A bf16
          | (1u << 10)           // B bf16
          | ((b_mn ? 1u : 0u) << 16)
          | ((uint32_t)(kTN >> 3) << 17)   // N = 128
-         | ((uint32_t)(kTM >> 4) << 24);  // M = 128
+         | ((uint32_t)((2 * kTM) >> 4) << 24);  // M = 256
 }
 
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
@@ -213,28 +267,28 @@ __device__ __forceinline__ float exp2_poly(float x) {
 // Pairs of probabilities per 16 whose exp2 runs on the FMA pipe.
 constexpr int kPolyPairs = 0;
 
-// P = 2^(s * sl2 - m) for half kHalf of a row's 128 scores (64 tokens),
-// written as bf16 pairs over those scores in TMEM; returns their sum.  With
-// kPoly (tiles without masked scores) kPolyPairs of every 16 pairs use
-// exp2_poly.
-template <bool kPoly, int kHalf>
-__device__ __forceinline__ float exp_store(const uint32_t (&r)[128], float sl2, float nref,
-                                           uint32_t sc) {
+// P = 2^(s * sl2 - m) for 64 scores (one half of a row's tile), written as
+// bf16 pairs over the first 32 of their TMEM columns at pc; returns their
+// sum.  With kPoly (tiles without masked scores) kPolyPairs of every 16
+// pairs use exp2_poly.
+template <bool kPoly>
+__device__ __forceinline__ float exp_half(const uint32_t (&q)[64], float sl2, float nref,
+                                          uint32_t pc) {
   float l4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-  for (int c = 2 * kHalf; c < 2 * kHalf + 2; ++c) {
+  for (int c = 0; c < 2; ++c) {
     uint32_t pk[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
-      const float x0 = fmaf(__uint_as_float(r[c * 32 + 2 * i]), sl2, nref);
-      const float x1 = fmaf(__uint_as_float(r[c * 32 + 2 * i + 1]), sl2, nref);
+      const float x0 = fmaf(__uint_as_float(q[c * 32 + 2 * i]), sl2, nref);
+      const float x1 = fmaf(__uint_as_float(q[c * 32 + 2 * i + 1]), sl2, nref);
       const bool poly = kPoly && ((i * kPolyPairs) % 16) < kPolyPairs;
       const float p0 = poly ? exp2_poly(x0) : kyro::ptx::fast_exp2(x0);
       const float p1 = poly ? exp2_poly(x1) : kyro::ptx::fast_exp2(x1);
       l4[i & 3] += p0 + p1;
       pk[i] = kyro::ptx::pack_bf16x2(p0, p1);
     }
-    tmem_st16(sc + c * 16, pk);  // P over the scores (all read before)
+    tmem_st16(pc + c * 16, pk);
   }
   return (l4[0] + l4[1]) + (l4[2] + l4[3]);
 }
@@ -246,7 +300,7 @@ __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, int* err
   return false;
 }
 
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
 tree_attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                          const __grid_constant__ CUtensorMap tmK,
                          const __grid_constant__ CUtensorMap tmV, TcArgs a,
@@ -259,26 +313,30 @@ tree_attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* gbase = smem_raw + (base - raw);
   const uint32_t bar0 = base + kTilesBytes;
+  // leader-side barriers (only the leader's copies are used): Q and ring
+  // slots filled (both CTAs' bytes), P halves written (both CTAs' threads)
   auto q_full = [&]() { return bar0; };
   auto slot_full = [&](int s) { return bar0 + 8u * (1 + s); };
-  auto slot_empty = [&](int s) { return bar0 + 8u * (1 + kSlots + s); };
-  auto s_full = [&](int h) { return bar0 + 8u * (1 + 2 * kSlots + h); };
-  // P of tile h reaches the MMA warp in two halves of 64 tokens
-  auto p_full = [&](int h, int half) { return bar0 + 8u * (3 + 2 * kSlots + 2 * h + half); };
+  auto p_full = [&](int h, int half) { return bar0 + 8u * (1 + kSlots + 2 * h + half); };
+  // barriers of both CTAs, signalled by multicast commits of the leader's MMAs
+  auto slot_empty = [&](int s) { return bar0 + 8u * (5 + kSlots + s); };
+  auto s_full = [&](int h) { return bar0 + 8u * (5 + 2 * kSlots + h); };
   auto o_done = [&](int h) { return bar0 + 8u * (7 + 2 * kSlots + h); };
   const uint32_t mma_done = bar0 + 8u * (9 + 2 * kSlots);
   // ring item n lives in slot n % kSlots; its fill is that slot's phase n / kSlots
   auto item_slot = [](int n) { return n % kSlots; };
   auto item_parity = [](int n) { return (uint32_t)((n / kSlots) & 1); };
-  auto item_addr = [&](int n) { return base + kOffRing + (uint32_t)(n % kSlots) * kTile; };
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + kTilesBytes + 240);
-  int* err = reinterpret_cast<int*>(gbase + kTilesBytes + 244);
+  auto item_addr = [&](int n) { return base + kOffRing + (uint32_t)(n % kSlots) * kItem; };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + kTilesBytes + 480);
+  int* err = reinterpret_cast<int*>(gbase + kTilesBytes + 484);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();  // 0: the leader, which issues the MMAs
+  const int pair = blockIdx.x >> 1;
   const int kvh = blockIdx.y, b = blockIdx.z;
   const int64_t ctx = context_lens[b];
   const int64_t T = ctx + a.nq;
-  if (ctx < 0 || (T + kBS - 1) / kBS > a.max_blocks) {
+  if (ctx < 0 || (T + kBS - 1) / kBS > a.max_blocks) {  // the same decision in both CTAs
     if (threadIdx.x == 0 && blockIdx.x == 0 && kvh == 0)
       kyro::dev::flag(status, KYRO_DEV_BAD_LENGTH);
     return;
@@ -286,9 +344,12 @@ tree_attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
   const int nblk = (int)((T + kBS - 1) / kBS);
   const int ntiles = (int)((T + kTN - 1) / kTN);
   const int nodes_per_tile = kTM / a.group;
-  const int mt0 = blockIdx.x * kTilesPerCta;             // first 128-row tile of this CTA
   const int mtiles = a.nq * a.group / kTM;
-  const int ntq = mtiles - mt0 < kTilesPerCta ? mtiles - mt0 : kTilesPerCta;  // 1 or 2
+  // the pair's query tiles: 4*pair + 2*h + rank for h < ntq; a CTA whose
+  // tile h lies past mtiles computes padding rows and writes nothing for them
+  const int left = (mtiles - 4 * pair + 1) / 2;
+  const int ntq = left < kTilesPerCta ? left : kTilesPerCta;  // 1 or 2
+  auto tile_of = [&](int h) { return 4 * pair + 2 * h + (int)rank; };
 
   if (threadIdx.x == 0) {
     kyro::ptx::mbar_init(q_full(), 1);
@@ -298,35 +359,39 @@ tree_attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
     }
     for (int i = 0; i < 2; ++i) {
       kyro::ptx::mbar_init(s_full(i), 1);
-      kyro::ptx::mbar_init(p_full(i, 0), 128);
-      kyro::ptx::mbar_init(p_full(i, 1), 128);
+      kyro::ptx::mbar_init(p_full(i, 0), 256);
+      kyro::ptx::mbar_init(p_full(i, 1), 256);
       kyro::ptx::mbar_init(o_done(i), 1);
     }
     kyro::ptx::mbar_init(mma_done, 1);
     *err = 0;
     kyro::ptx::fence_barrier_init();
   }
-  if (warp == 2) {
-    tmem_alloc(kyro::ptx::smem_addr(tmem_slot), kTmemCols);
-    tmem_relinquish();
+  if (warp == kMmaWarp) {
+    tmem_alloc2(kyro::ptx::smem_addr(tmem_slot), kTmemCols);
+    tmem_relinquish2();
   }
   tc_fence_before();
   __syncthreads();
+  cluster_sync();  // both CTAs' barriers exist before either signals the other
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
-    // ------------------------------------------------ producer (one thread)
+  if (warp == kProducerWarp) {
+    // ------------------------------------------------ producer (one thread per CTA)
     if (lane == 0) {
       kyro::ptx::prefetch_tensormap(&tmQ);
       kyro::ptx::prefetch_tensormap(&tmK);
       kyro::ptx::prefetch_tensormap(&tmV);
-      kyro::ptx::mbar_arrive_expect_tx(q_full(), (uint32_t)ntq * kTile);
+      // every load completes on the leader's barrier, which expects both CTAs' bytes
+      const uint32_t lq = leader_addr(q_full());
+      if (rank == 0) kyro::ptx::mbar_arrive_expect_tx(q_full(), 2u * (uint32_t)ntq * kTile);
       for (int h = 0; h < ntq; ++h) {
-        const int32_t qz = (int32_t)((int64_t)b * a.nq + (mt0 + h) * nodes_per_tile);
+        // a padding tile reads some other rows (or the zero fill past the end)
+        const int32_t qz = (int32_t)((int64_t)b * a.nq + tile_of(h) * nodes_per_tile);
         const uint32_t qd = base + kOffQ + (uint32_t)h * kTile;
-        kyro::ptx::tma_load_3d(qd, &tmQ, 0, kvh * a.group, qz, q_full());
-        kyro::ptx::tma_load_3d(qd + kSlab, &tmQ, 64, kvh * a.group, qz, q_full());
+        tma_load_3d_pair(qd, &tmQ, 0, kvh * a.group, qz, lq);
+        tma_load_3d_pair(qd + kSlab, &tmQ, 64, kvh * a.group, qz, lq);
       }
       const int64_t* bt = block_table + (int64_t)b * a.max_blocks;
       // a tile's 8 block ids are loaded together, one tile ahead of use
@@ -338,25 +403,34 @@ tree_attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
           ids[i] = __ldg(&bt[tb < nblk ? tb : 0]);  // blocks past the end: any block, masked
         }
       };
+      auto zrow = [&](int64_t bid) -> int32_t {
+        if (bid < 0 || bid >= a.num_blocks) {
+          kyro::dev::flag(status, KYRO_DEV_BAD_BLOCK);
+          bid = 0;
+        }
+        return (int32_t)(bid * a.hkv + kvh);
+      };
+      // item 2j: this CTA's 64 tokens of K_j (both 64-dim slabs, 8 KB each);
+      // item 2j+1: all 128 tokens of V_j in this CTA's 64-dim slab
       auto load_item = [&](int n, const int64_t (&bids)[kTileBlocks]) {
-        const CUtensorMap* map = (n & 1) ? &tmV : &tmK;
-        const uint32_t dst = item_addr(n), bar = slot_full(item_slot(n));
-        kyro::ptx::mbar_arrive_expect_tx(bar, kTile);
+        const uint32_t dst = item_addr(n), lb = leader_addr(slot_full(item_slot(n)));
+        if (rank == 0) kyro::ptx::mbar_arrive_expect_tx(slot_full(item_slot(n)), 2u * kItem);
+        if ((n & 1) == 0) {
 #pragma unroll
-        for (int i = 0; i < kTileBlocks; ++i) {
-          int64_t bid = bids[i];
-          if (bid < 0 || bid >= a.num_blocks) {
-            kyro::dev::flag(status, KYRO_DEV_BAD_BLOCK);
-            bid = 0;
+          for (int i = 0; i < kTileBlocks / 2; ++i) {
+            const int32_t z = zrow(bids[(kTileBlocks / 2) * rank + i]);
+            const uint32_t off = (uint32_t)i * kBS * 128;
+            tma_load_3d_pair(dst + off, &tmK, 0, 0, z, lb);
+            tma_load_3d_pair(dst + kKSlab + off, &tmK, 64, 0, z, lb);
           }
-          const int32_t z = (int32_t)(bid * a.hkv + kvh);
-          const uint32_t off = (uint32_t)i * kBS * 128;
-          kyro::ptx::tma_load_3d(dst + off, map, 0, 0, z, bar);
-          kyro::ptx::tma_load_3d(dst + kSlab + off, map, 64, 0, z, bar);
+        } else {
+#pragma unroll
+          for (int i = 0; i < kTileBlocks; ++i)
+            tma_load_3d_pair(dst + (uint32_t)i * kBS * 128, &tmV, 64 * (int32_t)rank, 0,
+                             zrow(bids[i]), lb);
         }
       };
       fetch_ids(0);
-      int issued = 0;  // ring items
       for (int j = 0; j < ntiles; ++j) {
         int64_t cur[kTileBlocks];
 #pragma unroll
@@ -373,31 +447,27 @@ tree_attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
             break;
           }
           load_item(n, cur);
-          ++issued;
         }
         if (stop) break;
       }
-      // every copy this thread started has landed before the CTA moves on
-      wait_bar(q_full(), 0, err, status);
-      for (int n = issued - kSlots < 0 ? 0 : issued - kSlots; n < issued; ++n)
-        wait_bar(slot_full(item_slot(n)), item_parity(n), err, status);
     }
     __syncwarp();
-  } else if (warp == 1) {
-    // ------------------------------------------------ MMA issuer (one thread)
-    if (lane == 0) {
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------ MMA issuer (the leader's one thread)
+    if (rank == 0 && lane == 0) {
       constexpr uint32_t idS = idesc_bf16(false), idO = idesc_bf16(true);
       auto s_mma = [&](int h, int j) {
         const uint32_t ks = item_addr(2 * j);
         const uint32_t qs = base + kOffQ + (uint32_t)h * kTile;
 #pragma unroll
         for (int k = 0; k < kD / 16; ++k) {
-          const uint32_t koff = (uint32_t)(k >> 2) * kSlab + (uint32_t)(k & 3) * 32;
-          umma_ss(tmem + (uint32_t)h * 128, desc_sw128(qs + koff, 16, 1024),
-                  desc_sw128(ks + koff, 16, 1024), idS, k > 0 ? 1u : 0u);
+          const uint32_t qoff = (uint32_t)(k >> 2) * kSlab + (uint32_t)(k & 3) * 32;
+          const uint32_t koff = (uint32_t)(k >> 2) * kKSlab + (uint32_t)(k & 3) * 32;
+          umma2_ss(tmem + (uint32_t)h * 128, desc_sw128(qs + qoff, 16, 1024),
+                   desc_sw128(ks + koff, 16, 1024), idS, k > 0 ? 1u : 0u);
         }
-        umma_commit(s_full(h));
-        if (h == ntq - 1) umma_commit(slot_empty(item_slot(2 * j)));  // K_j no longer read
+        umma2_commit_both(s_full(h));
+        if (h == ntq - 1) umma2_commit_both(slot_empty(item_slot(2 * j)));  // K_j no longer read
       };
       auto o_mma = [&](int h, int j) -> bool {
         const uint32_t vs = item_addr(2 * j + 1);
@@ -410,12 +480,12 @@ tree_attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
 #pragma unroll
           for (int k = 4 * half; k < 4 * half + 4; ++k) {
             const uint64_t bd = desc_sw128(vs + (uint32_t)k * 16 * 128, kSlab, 1024);
-            umma_ts(tmem + kColO + (uint32_t)h * 128, tmem + (uint32_t)h * 128 + (uint32_t)k * 8,
-                    bd, idO, (j > 0 || k > 0) ? 1u : 0u);
+            umma2_ts(tmem + kColO + (uint32_t)h * 128, tmem + (uint32_t)h * 128 + (uint32_t)k * 8,
+                     bd, idO, (j > 0 || k > 0) ? 1u : 0u);
           }
         }
-        umma_commit(o_done(h));
-        if (h == ntq - 1) umma_commit(slot_empty(item_slot(2 * j + 1)));  // V_j no longer read
+        umma2_commit_both(o_done(h));
+        if (h == ntq - 1) umma2_commit_both(slot_empty(item_slot(2 * j + 1)));  // V_j no longer read
         return true;
       };
       bool ok = wait_bar(q_full(), 0, err, status) && wait_bar(slot_full(0), 0, err, status);
@@ -443,18 +513,19 @@ tree_attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
           }
         }
       }
-      // every MMA issued above is complete before TMEM is released
-      umma_commit(mma_done);
-      wait_bar(mma_done, 0, err, status);
+      // every MMA issued above is complete before either CTA frees TMEM
+      umma2_commit_both(mma_done);
     }
+    if (lane == 0) wait_bar(mma_done, 0, err, status);
     __syncwarp();
-  } else if (warp >= 4 && (warp - 4) / 4 < ntq) {
+  } else if (warp < 8 && warp / 4 < ntq) {
     // ------------------------------------------------ softmax of tile h, one row per thread
-    const int h = (warp - 4) / 4;
+    const int h = warp / 4;
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-    const int node = (mt0 + h) * nodes_per_tile + row / a.group;
+    const bool real = tile_of(h) < mtiles;  // padding rows take part but write nothing
+    const int node = real ? tile_of(h) * nodes_per_tile + row / a.group : 0;
     const int g = row % a.group;
     // bit i: the row sees draft node i (its ancestors and itself under a
     // tree mask, nodes 0..node for a chain); nothing at or past nq
@@ -474,6 +545,8 @@ tree_attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
     const float sl2 = a.scale_log2;
     const uint32_t sc = tmem + lane_base + (uint32_t)h * 128;
     const uint32_t oc = tmem + lane_base + kColO + (uint32_t)h * 128;
+    // P halves are reported on the leader's barriers
+    const uint32_t pf0 = leader_addr(p_full(h, 0)), pf1 = leader_addr(p_full(h, 1));
     float m_used = -INFINITY, l = 0.0f;
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
@@ -484,15 +557,15 @@ tree_attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
       tc_fence_after();
       const int64_t t0 = (int64_t)j * kTN;
       const bool whole = t0 + kTN <= ctx;  // no masked score in the tile
-      // the row's 128 scores: four loads in flight, one wait
+      // first pass: the row's 128 scores for the maximum (four loads in flight)
       uint32_t r[128];
       tmem_ld32(sc + 0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
       tmem_ld32(sc + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
       tmem_ld32(sc + 64, *reinterpret_cast<uint32_t(*)[32]>(&r[64]));
       tmem_ld32(sc + 96, *reinterpret_cast<uint32_t(*)[32]>(&r[96]));
       tmem_ld_wait();
+      uint32_t vis[4] = {~0u, ~0u, ~0u, ~0u};
       if (!whole) {
-        uint32_t vis[4];
 #pragma unroll
         for (int w = 0; w < 4; ++w) vis[w] = vis_word(t0 + 32 * w);
 #pragma unroll
@@ -532,17 +605,28 @@ tree_attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
         tmem_st_wait();
       }
       const float nref = m_used == -INFINITY ? 0.0f : -m_used;
-      // the first 64 tokens' P goes to the MMA warp while the rest is computed
-      l += whole ? exp_store<true, 0>(r, sl2, nref, sc) : exp_store<false, 0>(r, sl2, nref, sc);
-      tmem_st_wait();
-      tc_fence_before();
-      kyro::ptx::mbar_arrive(p_full(h, 0));
-      l += whole ? exp_store<true, 1>(r, sl2, nref, sc) : exp_store<false, 1>(r, sl2, nref, sc);
-      tmem_st_wait();
-      tc_fence_before();
-      kyro::ptx::mbar_arrive(p_full(h, 1));
+      // second pass, 64 tokens at a time: the first half's P goes to the MMA
+      // warp while the second half is computed.  P of tokens 64*half.. lands
+      // on score columns 32*half.., which this thread has already read.
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t q[64];
+        tmem_ld32(sc + 64 * half, *reinterpret_cast<uint32_t(*)[32]>(&q[0]));
+        tmem_ld32(sc + 64 * half + 32, *reinterpret_cast<uint32_t(*)[32]>(&q[32]));
+        tmem_ld_wait();
+        if (!whole) {
+#pragma unroll
+          for (int i = 0; i < 64; ++i)
+            if (!((vis[2 * half + (i >> 5)] >> (i & 31)) & 1u)) q[i] = 0xff800000u;
+        }
+        const uint32_t pc = sc + 32 * half;
+        l += whole ? exp_half<true>(q, sl2, nref, pc) : exp_half<false>(q, sl2, nref, pc);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive_cluster(half == 0 ? pf0 : pf1);
+      }
     }
-    if (ok && ntiles > 0 && wait_bar(o_done(h), (ntiles - 1) & 1, err, status)) {
+    if (ok && real && ntiles > 0 && wait_bar(o_done(h), (ntiles - 1) & 1, err, status)) {
       tc_fence_after();
       const float inv = l > 0.0f ? 1.0f / l : 0.0f;
       __nv_bfloat16* orow =
@@ -564,10 +648,13 @@ tree_attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
       }
     }
   }
+  // neither CTA leaves (or frees TMEM) while the leader's MMAs may still
+  // read the other's shared memory or TMEM, or its commits may still arrive
   tc_fence_before();
   __syncthreads();
+  cluster_sync();
   tc_fence_after();
-  if (warp == 2) tmem_dealloc(tmem, kTmemCols);
+  if (warp == kMmaWarp) tmem_dealloc2(tmem, kTmemCols);
 }
 
 // ---------------------------------------------------------------- host side
@@ -653,8 +740,9 @@ int tree_attention_launch(kyro_ctx* ctx, const kyro_attn_params* p, const void* 
                          kSmemTc);
   });
   const int mtiles = p->num_query * group / kTM;
-  const dim3 grid((unsigned)((mtiles + kTilesPerCta - 1) / kTilesPerCta),
-                  (unsigned)p->num_kv_heads, (unsigned)p->batch);
+  // CTA pairs (the kernel's cluster shape), each covering four query tiles
+  const dim3 grid((unsigned)(2 * ((mtiles + 3) / 4)), (unsigned)p->num_kv_heads,
+                  (unsigned)p->batch);
   tree_attention_tc_kernel<<<grid, kTcThreads, kSmemTc, ctx->stream>>>(
       mq, mk, mv, a, block_table, context_lens, tree_mask, (__nv_bfloat16*)out, ctx->d_status);
   return kyro::check_launch("tree_attention_tc_kernel");
