@@ -47,8 +47,11 @@ struct Geo {
   static constexpr int kRingBytes = kWarps * kWarpRing;
   static constexpr int kQStride = D + 8;              // padded bf16 row stride of the Q tile
   static constexpr int kQBytes = kMaxCols * kQStride * 2;
-  // tree merge: two warps' (O, m, l) at a time
-  static constexpr int kMergeBytes = 2 * (D * kMaxCols + 2 * kMaxCols) * 4;
+  // tree merge: two warps' (O, m, l) at a time; O as [col][D + 4] floats,
+  // so a warp's accumulator fragment (8 dims x 4 column pairs) hits 32
+  // different banks
+  static constexpr int kMoStride = D + 4;
+  static constexpr int kMergeBytes = 2 * (kMaxCols * kMoStride + 2 * kMaxCols) * 4;
   static constexpr int kFinalBytes = (kMaxSplits * kMaxCols + kMaxCols) * 4;
   static_assert(kMergeBytes + kFinalBytes <= kRingBytes, "merge areas reuse the ring");
   static constexpr int kSmemBytes =
@@ -131,8 +134,23 @@ verify_attention_kernel(const __nv_bfloat16* __restrict__ q,
   const uint32_t ring_s = kyro::ptx::smem_addr(ring);
   const uint32_t q_s = ring_s + G::kRingBytes;
 
-  // ---- block ids of this split, Q rows, column masks
+  // ---- this warp's first blocks go out straight from the block table, so
+  // their latency overlaps the setup below
   const int64_t* bt = block_table + (int64_t)b * a.max_blocks + blk0;
+  const int nmy = nb > warp ? (nb - warp + kWarps - 1) / kWarps : 0;
+  const uint32_t wring0 = kyro::ptx::smem_addr(smem) + warp * G::kWarpRing;
+#pragma unroll
+  for (int p = 0; p < NS - 1; ++p) {
+    if (p < nmy) {
+      int64_t phys = bt[p * kWarps + warp];
+      if (phys < 0 || phys >= a.num_blocks) phys = 0;  // flagged below
+      load_block<D>(wring0 + p * kSlotBytes, k_base, v_base, (phys * a.hkv + kvh) * kTileBytes,
+                    lane);
+    }
+    kyro::ptx::cp_async_commit();
+  }
+
+  // ---- block ids of this split, Q rows, column masks
   for (int i = tid; i < nb; i += kThreads) {
     int64_t phys = bt[i];
     if (phys < 0 || phys >= a.num_blocks) {
@@ -162,17 +180,12 @@ verify_attention_kernel(const __nv_bfloat16* __restrict__ q,
   }
   __syncthreads();
 
-  // ---- this warp's blocks: w, w + 4, w + 8, ... of the split
-  const int nmy = nb > warp ? (nb - warp + kWarps - 1) / kWarps : 0;
+  // ---- this warp's blocks: w, w + 4, w + 8, ... of the split (the first
+  // NS-1 already in flight)
   const uint32_t wring = ring_s + warp * G::kWarpRing;
   auto tile_off = [&](int i) -> int64_t {
     return ((int64_t)ids[i * kWarps + warp] * a.hkv + kvh) * kTileBytes;
   };
-#pragma unroll
-  for (int p = 0; p < NS - 1; ++p) {
-    if (p < nmy) load_block<D>(wring + p * kSlotBytes, k_base, v_base, tile_off(p), lane);
-    kyro::ptx::cp_async_commit();
-  }
 
   float o[kMT][NT][4];
   float m_run[NT][2], l_run[NT][2];
@@ -307,10 +320,11 @@ verify_attention_kernel(const __nv_bfloat16* __restrict__ q,
 
   // ---- merge the four warps: (2,3) into (0,1), then 1 into 0
   float* mo = reinterpret_cast<float*>(ring);           // [2][d][col]
-  float* mm = mo + 2 * kD * kMaxCols;                   // [2][col]
+  constexpr int kMoStride = G::kMoStride;
+  float* mm = mo + 2 * kMaxCols * kMoStride;            // [2][col]
   float* ml = mm + 2 * kMaxCols;                        // [2][col]
   auto publish = [&](int slot) {
-    float* wo = mo + slot * kD * kMaxCols;
+    float* wo = mo + slot * kMaxCols * kMoStride;
 #pragma unroll
     for (int mt = 0; mt < kMT; ++mt)
 #pragma unroll
@@ -319,7 +333,7 @@ verify_attention_kernel(const __nv_bfloat16* __restrict__ q,
         for (int e = 0; e < 4; ++e) {
           const int d = mt * 16 + (lane >> 2) + (e >> 1) * 8;
           const int col = nt * 8 + 2 * (lane & 3) + (e & 1);
-          wo[d * kMaxCols + col] = o[mt][nt][e];
+          wo[col * kMoStride + d] = o[mt][nt][e];
         }
     if (lane < 4) {
 #pragma unroll
@@ -333,7 +347,7 @@ verify_attention_kernel(const __nv_bfloat16* __restrict__ q,
     }
   };
   auto absorb = [&](int slot) {
-    const float* wo = mo + slot * kD * kMaxCols;
+    const float* wo = mo + slot * kMaxCols * kMoStride;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -349,8 +363,8 @@ verify_attention_kernel(const __nv_bfloat16* __restrict__ q,
 #pragma unroll
         for (int mt = 0; mt < kMT; ++mt) {
           const int d = mt * 16 + (lane >> 2);
-          o[mt][nt][c] = o[mt][nt][c] * fa + wo[d * kMaxCols + col] * fb;
-          o[mt][nt][c + 2] = o[mt][nt][c + 2] * fa + wo[(d + 8) * kMaxCols + col] * fb;
+          o[mt][nt][c] = o[mt][nt][c] * fa + wo[col * kMoStride + d] * fb;
+          o[mt][nt][c + 2] = o[mt][nt][c + 2] * fa + wo[col * kMoStride + d + 8] * fb;
         }
       }
   };
@@ -371,7 +385,7 @@ verify_attention_kernel(const __nv_bfloat16* __restrict__ q,
   float* pml = part_ml + item * a.max_splits * (kMaxCols * 2);
   for (int i = tid; i < ncols * kD; i += kThreads) {
     const int col = i / kD, d = i % kD;
-    const float O = mo[d * kMaxCols + col];
+    const float O = mo[col * kMoStride + d];
     const float L = ml[col];
     if (single) {
       const int r = col0 + col, j = r / a.group, gi = r % a.group;
@@ -413,14 +427,28 @@ verify_attention_kernel(const __nv_bfloat16* __restrict__ q,
     finv[col] = L > 0.0f ? 1.0f / L : 0.0f;
   }
   __syncthreads();
-  for (int i = tid; i < ncols * kD; i += kThreads) {
-    const int col = i / kD, d = i % kD;
-    float O = 0.0f;
-    for (int sp = 0; sp < nsplit; ++sp)
-      O += fscale[sp * kMaxCols + col] * __ldcg(&po[(sp * kMaxCols + col) * kD + d]);
+  // four dims per thread per step; the splits' loads are independent, so
+  // several are in flight at once
+#pragma unroll 2
+  for (int i4 = tid; i4 < ncols * (kD / 4); i4 += kThreads) {
+    const int col = i4 / (kD / 4), d4 = (i4 % (kD / 4)) * 4;
+    float4 O = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll 4
+    for (int sp = 0; sp < nsplit; ++sp) {
+      const float f = fscale[sp * kMaxCols + col];
+      const float4 v =
+          __ldcg(reinterpret_cast<const float4*>(&po[(sp * kMaxCols + col) * kD + d4]));
+      O.x += f * v.x;
+      O.y += f * v.y;
+      O.z += f * v.z;
+      O.w += f * v.w;
+    }
+    const float inv = finv[col];
     const int r = col0 + col, j = r / a.group, gi = r % a.group;
     const int h = kvh * a.group + gi;
-    out[(((int64_t)b * a.nq + j) * a.hq + h) * kD + d] = __float2bfloat16(O * finv[col]);
+    *reinterpret_cast<uint2*>(&out[(((int64_t)b * a.nq + j) * a.hq + h) * kD + d4]) =
+        make_uint2(kyro::ptx::pack_bf16x2(O.x * inv, O.y * inv),
+                   kyro::ptx::pack_bf16x2(O.z * inv, O.w * inv));
   }
   if (tid == 0) tickets[item] = 0;
 }
