@@ -47,13 +47,16 @@ struct Geo {
   static constexpr int kRingBytes = kWarps * kWarpRing;
   static constexpr int kQStride = D + 8;              // padded bf16 row stride of the Q tile
   static constexpr int kQBytes = kMaxCols * kQStride * 2;
-  // tree merge: two warps' (O, m, l) at a time; O as [col][D + 4] floats,
-  // so a warp's accumulator fragment (8 dims x 4 column pairs) hits 32
-  // different banks
+  // warp merge: the four warps' (O, m, l), merge factors and the merged
+  // (m, l), over the ring and the Q tile (both free by then).  O is stored
+  // [col][D + 4] so a warp's accumulator fragment (8 dims x 4 column pairs)
+  // hits 32 different banks.
   static constexpr int kMoStride = D + 4;
-  static constexpr int kMergeBytes = 2 * (kMaxCols * kMoStride + 2 * kMaxCols) * 4;
+  static constexpr int kMergeBytes =
+      (kWarps * kMaxCols * kMoStride + 3 * kWarps * kMaxCols + 2 * kMaxCols) * 4;
   static constexpr int kFinalBytes = (kMaxSplits * kMaxCols + kMaxCols) * 4;
-  static_assert(kMergeBytes + kFinalBytes <= kRingBytes, "merge areas reuse the ring");
+  static_assert(kMergeBytes <= kRingBytes + kQBytes, "the warp merge reuses the ring and Q tile");
+  static_assert(kFinalBytes <= kRingBytes, "the split merge reuses the ring");
   static constexpr int kSmemBytes =
       kRingBytes + kQBytes + kMaxCols * 8 + kMaxSplitBlocks * 4 + 16;
 };
@@ -112,6 +115,15 @@ verify_attention_kernel(const __nv_bfloat16* __restrict__ q,
   const int b = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
+  // this warp's first block ids load together with the context length (the
+  // split's start does not depend on it); entries past the table row are
+  // not read
+  const int64_t* bt = block_table + (int64_t)b * a.max_blocks + (int64_t)split * a.split_blocks;
+  int64_t first_ids[NS - 1];
+#pragma unroll
+  for (int p = 0; p < NS - 1; ++p)
+    first_ids[p] = split * a.split_blocks + p * kWarps + warp < a.max_blocks ? bt[p * kWarps + warp]
+                                                                             : 0;
   const int64_t ctx = context_lens[b];
   const int64_t total = ctx + a.nq;
   if (ctx < 0 || (total + kBS - 1) / kBS > a.max_blocks) {
@@ -134,15 +146,14 @@ verify_attention_kernel(const __nv_bfloat16* __restrict__ q,
   const uint32_t ring_s = kyro::ptx::smem_addr(ring);
   const uint32_t q_s = ring_s + G::kRingBytes;
 
-  // ---- this warp's first blocks go out straight from the block table, so
-  // their latency overlaps the setup below
-  const int64_t* bt = block_table + (int64_t)b * a.max_blocks + blk0;
+  // ---- this warp's first blocks go out before the setup below, so their
+  // latency overlaps it
   const int nmy = nb > warp ? (nb - warp + kWarps - 1) / kWarps : 0;
   const uint32_t wring0 = kyro::ptx::smem_addr(smem) + warp * G::kWarpRing;
 #pragma unroll
   for (int p = 0; p < NS - 1; ++p) {
     if (p < nmy) {
-      int64_t phys = bt[p * kWarps + warp];
+      int64_t phys = first_ids[p];
       if (phys < 0 || phys >= a.num_blocks) phys = 0;  // flagged below
       load_block<D>(wring0 + p * kSlotBytes, k_base, v_base, (phys * a.hkv + kvh) * kTileBytes,
                     lane);
@@ -318,13 +329,18 @@ verify_attention_kernel(const __nv_bfloat16* __restrict__ q,
     }
   __syncthreads();  // the ring is free
 
-  // ---- merge the four warps: (2,3) into (0,1), then 1 into 0
-  float* mo = reinterpret_cast<float*>(ring);           // [2][d][col]
+  // ---- merge the four warps in one pass: each publishes its state, the
+  // first ncols threads form the per-column factors, then every thread
+  // combines four dims at a time
   constexpr int kMoStride = G::kMoStride;
-  float* mm = mo + 2 * kMaxCols * kMoStride;            // [2][col]
-  float* ml = mm + 2 * kMaxCols;                        // [2][col]
-  auto publish = [&](int slot) {
-    float* wo = mo + slot * kMaxCols * kMoStride;
+  float* mo = reinterpret_cast<float*>(ring);           // [warp][col][kMoStride]
+  float* mm = mo + kWarps * kMaxCols * kMoStride;       // [warp][col]
+  float* ml = mm + kWarps * kMaxCols;                   // [warp][col]
+  float* mf = ml + kWarps * kMaxCols;                   // [warp][col] merge factors
+  float* mM = mf + kWarps * kMaxCols;                   // [col] merged max
+  float* mL = mM + kMaxCols;                            // [col] merged sum
+  {
+    float* wo = mo + warp * kMaxCols * kMoStride;
 #pragma unroll
     for (int mt = 0; mt < kMT; ++mt)
 #pragma unroll
@@ -341,61 +357,57 @@ verify_attention_kernel(const __nv_bfloat16* __restrict__ q,
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           const int col = nt * 8 + 2 * lane + c;
-          mm[slot * kMaxCols + col] = m_run[nt][c];
-          ml[slot * kMaxCols + col] = l_run[nt][c];
+          mm[warp * kMaxCols + col] = m_run[nt][c];
+          ml[warp * kMaxCols + col] = l_run[nt][c];
         }
     }
-  };
-  auto absorb = [&](int slot) {
-    const float* wo = mo + slot * kMaxCols * kMoStride;
+  }
+  __syncthreads();
+  if (tid < ncols) {
+    float M = -INFINITY;
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
+    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, mm[w * kMaxCols + tid]);
+    const float Mu = M == -INFINITY ? 0.0f : M;
+    float L = 0.0f;
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        const int col = nt * 8 + 2 * (lane & 3) + c;
-        const float mo_ = mm[slot * kMaxCols + col], lo_ = ml[slot * kMaxCols + col];
-        const float M = fmaxf(m_run[nt][c], mo_);
-        const float Mu = M == -INFINITY ? 0.0f : M;
-        const float fa = kyro::ptx::fast_exp2(m_run[nt][c] - Mu);
-        const float fb = kyro::ptx::fast_exp2(mo_ - Mu);
-        l_run[nt][c] = l_run[nt][c] * fa + lo_ * fb;
-        m_run[nt][c] = M;
-#pragma unroll
-        for (int mt = 0; mt < kMT; ++mt) {
-          const int d = mt * 16 + (lane >> 2);
-          o[mt][nt][c] = o[mt][nt][c] * fa + wo[col * kMoStride + d] * fb;
-          o[mt][nt][c + 2] = o[mt][nt][c + 2] * fa + wo[col * kMoStride + d + 8] * fb;
-        }
-      }
-  };
-  if (warp >= 2) publish(warp - 2);
-  __syncthreads();
-  if (warp < 2) absorb(warp);
-  __syncthreads();
-  if (warp == 1) publish(0);
-  __syncthreads();
-  if (warp == 0) absorb(0);
-  __syncthreads();
-  if (warp == 0) publish(0);  // the CTA's merged state, for the writers below
+    for (int w = 0; w < kWarps; ++w) {
+      const float f = kyro::ptx::fast_exp2(mm[w * kMaxCols + tid] - Mu);
+      mf[w * kMaxCols + tid] = f;
+      L += f * ml[w * kMaxCols + tid];
+    }
+    mM[tid] = M;
+    mL[tid] = L;
+  }
   __syncthreads();
 
   const bool single = nsplit == 1;
   const int64_t item = ((int64_t)b * a.hkv + kvh) * a.ngroups + grp;
   float* po = part_o + item * a.max_splits * (kMaxCols * kD);
   float* pml = part_ml + item * a.max_splits * (kMaxCols * 2);
-  for (int i = tid; i < ncols * kD; i += kThreads) {
-    const int col = i / kD, d = i % kD;
-    const float O = mo[col * kMoStride + d];
-    const float L = ml[col];
+  for (int i4 = tid; i4 < ncols * (kD / 4); i4 += kThreads) {
+    const int col = i4 / (kD / 4), d4 = (i4 % (kD / 4)) * 4;
+    float4 O = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const float f = mf[w * kMaxCols + col];
+      const float4 v = *reinterpret_cast<const float4*>(&mo[(w * kMaxCols + col) * kMoStride + d4]);
+      O.x += f * v.x;
+      O.y += f * v.y;
+      O.z += f * v.z;
+      O.w += f * v.w;
+    }
+    const float L = mL[col];
     if (single) {
+      const float inv = L > 0.0f ? 1.0f / L : 0.0f;
       const int r = col0 + col, j = r / a.group, gi = r % a.group;
       const int h = kvh * a.group + gi;
-      out[(((int64_t)b * a.nq + j) * a.hq + h) * kD + d] =
-          __float2bfloat16(L > 0.0f ? O / L : 0.0f);
+      *reinterpret_cast<uint2*>(&out[(((int64_t)b * a.nq + j) * a.hq + h) * kD + d4]) =
+          make_uint2(kyro::ptx::pack_bf16x2(O.x * inv, O.y * inv),
+                     kyro::ptx::pack_bf16x2(O.z * inv, O.w * inv));
     } else {
-      po[(split * kMaxCols + col) * kD + d] = O;
-      if (d == 0) {
-        pml[(split * kMaxCols + col) * 2 + 0] = mm[col];
+      *reinterpret_cast<float4*>(&po[(split * kMaxCols + col) * kD + d4]) = O;
+      if (d4 == 0) {
+        pml[(split * kMaxCols + col) * 2 + 0] = mM[col];
         pml[(split * kMaxCols + col) * 2 + 1] = L;
       }
     }
@@ -412,7 +424,7 @@ verify_attention_kernel(const __nv_bfloat16* __restrict__ q,
   __syncthreads();
   if (!*sh_last) return;
   __threadfence();
-  float* fscale = reinterpret_cast<float*>(ring + G::kMergeBytes);  // [split][col]
+  float* fscale = reinterpret_cast<float*>(ring);  // [split][col] (the warp merge is done)
   float* finv = fscale + kMaxSplits * kMaxCols;                    // [col]
   for (int col = tid; col < ncols; col += kThreads) {
     float M = -INFINITY;
