@@ -65,6 +65,7 @@ struct AttnArgs {
   int B, nq, hq, hkv, group, rows, ngroups, max_blocks, num_blocks, split_blocks, max_splits;
   float scale_log2;
   int d;
+  uint32_t epoch;  // nonzero, new on every call: split tickets of older calls count as zero
 };
 
 // byte offset of (token row, 16-byte chunk along D) inside a swizzled tile:
@@ -101,7 +102,8 @@ verify_attention_kernel(const __nv_bfloat16* __restrict__ q,
                         const int64_t* __restrict__ context_lens,
                         const uint64_t* __restrict__ tree_mask, __nv_bfloat16* __restrict__ out,
                         float* __restrict__ part_o, float* __restrict__ part_ml,
-                        uint32_t* __restrict__ tickets, AttnArgs a, uint32_t* status) {
+                        unsigned long long* __restrict__ tickets, AttnArgs a,
+                        uint32_t* status) {
   extern __shared__ __align__(128) uint8_t smem[];
   using G = Geo<D, NS>;
   constexpr int kD = D;
@@ -114,6 +116,10 @@ verify_attention_kernel(const __nv_bfloat16* __restrict__ q,
   const int grp = blockIdx.y % a.ngroups;
   const int b = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // launched behind the stream's previous kernel (programmatic dependent
+  // launch): nothing is read or written before it has completed
+  kyro::dev::pdl_wait();
+  kyro::dev::pdl_trigger();
 
   // this warp's first block ids load together with the context length (the
   // split's start does not depend on it); entries past the table row are
@@ -417,9 +423,19 @@ verify_attention_kernel(const __nv_bfloat16* __restrict__ q,
   // ---- the last split of this (sequence, KV head, row group) merges all splits
   __syncthreads();
   if (tid == 0) {
+    // a ticket is (epoch << 32 | splits done); a ticket left by an earlier
+    // call carries another epoch and counts as zero
     __threadfence();
-    const uint32_t t = atomicAdd(&tickets[item], 1u);
-    *sh_last = (t == (uint32_t)nsplit - 1);
+    unsigned long long cur = *(volatile unsigned long long*)&tickets[item];
+    uint32_t done;
+    for (;;) {
+      done = (uint32_t)(cur >> 32) == a.epoch ? (uint32_t)cur + 1u : 1u;
+      const unsigned long long nw = ((unsigned long long)a.epoch << 32) | done;
+      const unsigned long long prev = atomicCAS(&tickets[item], cur, nw);
+      if (prev == cur) break;
+      cur = prev;
+    }
+    *sh_last = done == (uint32_t)nsplit;
   }
   __syncthreads();
   if (!*sh_last) return;
@@ -462,7 +478,6 @@ verify_attention_kernel(const __nv_bfloat16* __restrict__ q,
         make_uint2(kyro::ptx::pack_bf16x2(O.x * inv, O.y * inv),
                    kyro::ptx::pack_bf16x2(O.z * inv, O.w * inv));
   }
-  if (tid == 0) tickets[item] = 0;
 }
 
 // ------------------------------------------------------------------ host
@@ -534,7 +549,7 @@ int plan(const kyro_attn_params* p, int num_sms, Plan* out) {
   const int64_t items = groups * (a.max_splits > 1 ? a.max_splits : 0);
   pl.part_o_bytes = (size_t)items * kMaxCols * p->head_dim * 4;
   pl.part_ml_bytes = (size_t)items * kMaxCols * 2 * 4;
-  pl.ticket_bytes = a.max_splits > 1 ? (size_t)groups * 4 : 0;
+  pl.ticket_bytes = a.max_splits > 1 ? (size_t)groups * 8 : 0;
   *out = pl;
   return KYRO_OK;
 }
@@ -548,19 +563,19 @@ size_t ws_bytes(const Plan& pl) {
 template <int NT, int D>
 void launch(const Plan& pl, dim3 grid, cudaStream_t st, const void* q, const void* kc,
             const void* vc, const int64_t* bt, const int64_t* cl, const uint64_t* tm, void* out,
-            float* po, float* pml, uint32_t* tk, uint32_t* status) {
+            float* po, float* pml, unsigned long long* tk, uint32_t* status) {
   constexpr int smem = Geo<D, kStages>::kSmemBytes;
   cudaFuncSetAttribute(verify_attention_kernel<NT, D, kStages>,
                        cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  verify_attention_kernel<NT, D, kStages><<<grid, kThreads, smem, st>>>(
-      (const __nv_bfloat16*)q, (const uint8_t*)kc, (const uint8_t*)vc, bt, cl, tm,
-      (__nv_bfloat16*)out, po, pml, tk, pl.a, status);
+  kyro::launch_pdl(verify_attention_kernel<NT, D, kStages>, grid, dim3(kThreads), smem, st,
+                   "verify_attention_kernel", (const __nv_bfloat16*)q, (const uint8_t*)kc,
+                   (const uint8_t*)vc, bt, cl, tm, (__nv_bfloat16*)out, po, pml, tk, pl.a, status);
 }
 
 template <int D>
 void launch_d(const Plan& pl, dim3 grid, cudaStream_t st, const void* q, const void* kc,
               const void* vc, const int64_t* bt, const int64_t* cl, const uint64_t* tm,
-              void* out, float* po, float* pml, uint32_t* tk, uint32_t* status) {
+              void* out, float* po, float* pml, unsigned long long* tk, uint32_t* status) {
   switch (pl.nt) {
     case 1: launch<1, D>(pl, grid, st, q, kc, vc, bt, cl, tm, out, po, pml, tk, status); break;
     case 2: launch<2, D>(pl, grid, st, q, kc, vc, bt, cl, tm, out, po, pml, tk, status); break;
@@ -608,14 +623,19 @@ int kyro_verify_attention(kyro_ctx* ctx, const kyro_attn_params* p, const void* 
              "kyro_verify_attention: workspace must be 256-byte aligned");
   float* po = (float*)workspace;
   float* pml = (float*)((char*)workspace + align256(pl.part_o_bytes));
-  uint32_t* tk = (uint32_t*)((char*)workspace + align256(pl.part_o_bytes) +
-                             align256(pl.part_ml_bytes));
+  unsigned long long* tk = (unsigned long long*)((char*)workspace + align256(pl.part_o_bytes) +
+                                                 align256(pl.part_ml_bytes));
   dim3 grid((unsigned)pl.a.max_splits, (unsigned)(pl.a.hkv * pl.a.ngroups), (unsigned)pl.a.B);
   cudaStream_t st = ctx->stream;
-  if (pl.ticket_bytes) {
-    // split tickets start at zero; the merging split also resets its ticket
+  // split tickets carry the call's epoch, so one workspace needs zeroing
+  // only the first time this context sees it (a zeroed ticket holds epoch 0,
+  // which no call uses)
+  if (++ctx->attn_epoch == 0) ctx->attn_epoch = 1;
+  pl.a.epoch = ctx->attn_epoch;
+  if (pl.ticket_bytes && workspace != ctx->attn_ws_zeroed) {
     cudaError_t err = cudaMemsetAsync(tk, 0, pl.ticket_bytes, st);
     if (err != cudaSuccess) return kyro::cuda_error(err, "cudaMemsetAsync(attention tickets)");
+    ctx->attn_ws_zeroed = workspace;
   }
   if (p->head_dim == 128)
     launch_d<128>(pl, grid, st, q, k_cache, v_cache, block_table, context_lens, tree_mask, out, po,

@@ -114,6 +114,8 @@ int kyro_ctx_create(int device, void* stream, kyro_ctx** out) {
   ctx->nccl_comm = nullptr;
   ctx->tp_rank = 0;
   ctx->tp_world = 1;
+  ctx->attn_epoch = 0;
+  ctx->attn_ws_zeroed = nullptr;
   err = cudaMalloc(&ctx->d_status, 16);
   if (err != cudaSuccess) {
     delete ctx;

@@ -63,6 +63,8 @@ kv_reserve_kernel(int B, int bs, int max_blocks, int num_blocks, int num_new,
                   uint32_t* status) {
   __shared__ int sh[72];
   __shared__ int sh_top, sh_fast;
+  kyro::dev::pdl_wait();
+  kyro::dev::pdl_trigger();
   if (threadIdx.x == 0) {
     int t = *free_top;
     if (t < 0 || t > num_blocks) {
@@ -151,6 +153,8 @@ kv_commit_kernel(int B, int bs, int max_blocks, int num_blocks, int num_new,
                  int32_t* __restrict__ ref_counts, uint32_t* status) {
   __shared__ int sh[72];
   __shared__ int sh_top, sh_fast;
+  kyro::dev::pdl_wait();
+  kyro::dev::pdl_trigger();
   if (threadIdx.x == 0) {
     int t = *free_top;
     if (t < 0 || t > num_blocks) {
@@ -311,6 +315,8 @@ kv_write_kernel(int num_new, int hkv, int d, int bs, int max_blocks, int num_blo
                 const int64_t* __restrict__ block_table, const int64_t* __restrict__ context_lens,
                 uint8_t* __restrict__ k_cache, uint8_t* __restrict__ v_cache, uint32_t* status) {
   const int b = blockIdx.x, j = blockIdx.y;
+  kyro::dev::pdl_wait();
+  kyro::dev::pdl_trigger();
   const int64_t ctx = context_lens[b];
   const int64_t pos = ctx + j;
   if (ctx < 0 || pos / bs >= max_blocks) {
@@ -354,11 +360,10 @@ int kyro_kv_reserve(kyro_ctx* ctx, const kyro_kv_params* p, int32_t num_new,
   if (p->batch == 0) return KYRO_OK;
   KY_REQUIRE(block_table && context_lens && free_stack && free_top && ref_counts,
              "kyro_kv_reserve: a required pointer is NULL");
-  kv_reserve_kernel<<<1, kTile, 0, ctx->stream>>>(p->batch, p->block_size, p->max_blocks_per_seq,
-                                                  p->num_blocks, num_new, block_table,
-                                                  context_lens, free_stack, free_top, ref_counts,
-                                                  out_ok, ctx->d_status);
-  return kyro::check_launch("kv_reserve_kernel");
+  return kyro::launch_pdl(kv_reserve_kernel, dim3(1), dim3(kTile), 0, ctx->stream,
+                          "kv_reserve_kernel", p->batch, p->block_size, p->max_blocks_per_seq,
+                          p->num_blocks, num_new, block_table, context_lens,
+                          (const int32_t*)free_stack, free_top, ref_counts, out_ok, ctx->d_status);
 }
 
 int kyro_kv_commit(kyro_ctx* ctx, const kyro_kv_params* p, int32_t num_new,
@@ -370,11 +375,10 @@ int kyro_kv_commit(kyro_ctx* ctx, const kyro_kv_params* p, int32_t num_new,
   if (p->batch == 0) return KYRO_OK;
   KY_REQUIRE(accept_len && block_table && context_lens && free_stack && free_top && ref_counts,
              "kyro_kv_commit: a required pointer is NULL");
-  kv_commit_kernel<<<1, kTile, 0, ctx->stream>>>(p->batch, p->block_size, p->max_blocks_per_seq,
-                                                 p->num_blocks, num_new, accept_len, nullptr,
-                                                 block_table, context_lens, free_stack, free_top,
-                                                 ref_counts, ctx->d_status);
-  return kyro::check_launch("kv_commit_kernel");
+  return kyro::launch_pdl(kv_commit_kernel, dim3(1), dim3(kTile), 0, ctx->stream,
+                          "kv_commit_kernel", p->batch, p->block_size, p->max_blocks_per_seq,
+                          p->num_blocks, num_new, accept_len, (const int32_t*)nullptr, block_table,
+                          context_lens, free_stack, free_top, ref_counts, ctx->d_status);
 }
 
 int kyro_kv_write(kyro_ctx* ctx, const kyro_kv_params* p, int32_t num_new, int32_t num_kv_heads,
@@ -393,11 +397,11 @@ int kyro_kv_write(kyro_ctx* ctx, const kyro_kv_params* p, int32_t num_new, int32
                  (uintptr_t)k_cache % 16 == 0 && (uintptr_t)v_cache % 16 == 0,
              "kyro_kv_write: tensors must be 16-byte aligned");
   dim3 grid((unsigned)p->batch, (unsigned)num_new);
-  kv_write_kernel<<<grid, 256, 0, ctx->stream>>>(
-      num_new, num_kv_heads, head_dim, p->block_size, p->max_blocks_per_seq, p->num_blocks,
-      (const uint4*)k_new, (const uint4*)v_new, block_table, context_lens, (uint8_t*)k_cache,
-      (uint8_t*)v_cache, ctx->d_status);
-  return kyro::check_launch("kv_write_kernel");
+  return kyro::launch_pdl(kv_write_kernel, grid, dim3(256), 0, ctx->stream, "kv_write_kernel",
+                          (int)num_new, (int)num_kv_heads, (int)head_dim, p->block_size,
+                          p->max_blocks_per_seq, p->num_blocks, (const uint4*)k_new,
+                          (const uint4*)v_new, block_table, context_lens, (uint8_t*)k_cache,
+                          (uint8_t*)v_cache, ctx->d_status);
 }
 
 int kyro_kv_commit_tree(kyro_ctx* ctx, const kyro_kv_params* p, int32_t num_nodes,

@@ -9,6 +9,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <string>
+#include <utility>
 
 #include "../../include/kyro_spec.h"
 
@@ -20,6 +21,10 @@ struct kyro_ctx {
   // tensor-parallel group (kyro_ctx_tp_init); world 1 without one
   void* nccl_comm;     // ncclComm_t
   int tp_rank, tp_world;
+  // verify attention's split tickets: a per-call epoch, and the last
+  // workspace whose tickets this context has zeroed
+  uint32_t attn_epoch;
+  const void* attn_ws_zeroed;
 };
 
 namespace kyro {
@@ -67,10 +72,39 @@ void release(kyro_ctx* ctx);
 
 // ---------------------------------------------------------------- device
 namespace kyro {
+// Launch `kernel` with programmatic stream serialization (see dev::pdl_wait).
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+               const char* name, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  if (err != cudaSuccess) return cuda_error(err, name);
+  return KYRO_OK;
+}
+
 namespace dev {
 
 __device__ __forceinline__ void flag(uint32_t* status, uint32_t bits) {
   if (status) atomicOr(status, bits);
+}
+
+// Programmatic dependent launch.  A kernel started with launch_pdl may run
+// while its predecessor on the stream drains; pdl_wait blocks until that
+// grid has completed and its writes are visible, so it comes before the
+// kernel reads or writes anything a predecessor may touch.  pdl_trigger
+// lets the next kernel begin launching.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 __device__ __forceinline__ float warp_max(float v) {

@@ -1007,6 +1007,7 @@ __global__ void __launch_bounds__(kThreads) accept_final_kernel(Args a) {
   const int b = a.B - 1 - y;
   const int c0 = (int)(blockIdx.x - (unsigned)y * per_seq) * kFinalPerCta;
   grid_dependency_wait();  // the decide kernel has written final_rows and zeroed cnt_c
+  allow_dependents();      // the stream's next kernel (e.g. the KV commit) may start launching
   const FinalRow fr = a.final_rows[b];
   if (fr.skip) return;  // the same for the whole CTA
   const bool residual = fr.q_row >= 0;
