@@ -169,6 +169,39 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
+class KvStateSnapshot:
+    """The KV bookkeeping tensors of a PagedState (block table, context
+    lengths, free stack and top, ref counts) moved into one device buffer,
+    with a copy of their starting values.  Every timed step starts from the
+    same state, and resetting it is one device-to-device copy."""
+
+    NAMES = ("block_table", "context_lens", "free_stack", "free_top", "ref_counts")
+
+    def __init__(self, st):
+        import torch
+        layout, off = [], 0
+        for n in self.NAMES:
+            t = getattr(st, n)
+            nbytes = t.numel() * t.element_size()
+            layout.append((n, off, nbytes, t.dtype, tuple(t.shape)))
+            off += (nbytes + 255) // 256 * 256
+        self.buf = torch.empty(off, dtype=torch.uint8, device=st.block_table.device)
+        self._views = {}
+        for n, o, nb, dt, sh in layout:
+            v = self.buf[o:o + nb].view(dt).view(sh)
+            v.copy_(getattr(st, n))
+            setattr(st, n, v)
+            self._views[n] = (o, nb, dt, sh)
+        self.snap = self.buf.clone()
+
+    def restore(self):
+        self.buf.copy_(self.snap, non_blocking=True)
+
+    def initial(self, name):
+        o, nb, dt, sh = self._views[name]
+        return self.snap[o:o + nb].view(dt).view(sh)
+
+
 # --------------------------------------------------------------------- ours
 def run_ours(args):
     import torch
@@ -218,13 +251,9 @@ def run_ours(args):
     stream = torch.cuda.current_stream(dev)
     ev = {n: [] for n in ("attention", "accept")}
     # every step starts from the same KV state, so each step sees the same
-    # context lengths; the restore is four device-to-device copies (~0.5 MB)
-    snap = {n: getattr(st, n).clone() for n in
-            ("block_table", "context_lens", "free_stack", "free_top", "ref_counts")}
-
-    def restore():
-        for n, t in snap.items():
-            getattr(st, n).copy_(t, non_blocking=True)
+    # context lengths; the reset is one device-to-device copy (~0.5 MB)
+    kvsnap = KvStateSnapshot(st)
+    restore = kvsnap.restore
 
     def step(i, timed):
         restore()
@@ -292,7 +321,7 @@ def run_ours(args):
         raise SystemExit(f"device status word 0x{status:x} after the timed region")
 
     # algorithmic bytes per step, from the context lengths every step starts from
-    per = [chain_bytes_per_step(snap["context_lens"].cpu().numpy(), cfg)]
+    per = [chain_bytes_per_step(kvsnap.initial("context_lens").cpu().numpy(), cfg)]
     att_ms = np.mean([a.elapsed_time(b) for a, b in ev["attention"]])
     acc_ms = np.mean([a.elapsed_time(b) for a, b in ev["accept"]])
     att_bytes = float(np.mean([p["attention"] for p in per]))
@@ -552,14 +581,12 @@ def run_tree(args):
     v_new = torch.randn_like(k_new)
     attn_out = torch.empty_like(st.q)
     ok = torch.empty(B, dtype=torch.int32, device=dev)
-    snap = {n: getattr(st, n).clone() for n in
-            ("block_table", "context_lens", "free_stack", "free_top", "ref_counts")}
+    kvsnap = KvStateSnapshot(st)
     stream = torch.cuda.current_stream(dev)
     ev = {"attention": [], "accept": []}
 
     def step(i, timed):
-        for n, t in snap.items():
-            getattr(st, n).copy_(t, non_blocking=True)
+        kvsnap.restore()
         kv_reserve(ctx, N, st.block_table, st.context_lens, st.free_stack, st.free_top,
                    st.ref_counts, cfg.block_size, out_ok=ok)
         kv_write(ctx, k_new, v_new, st.block_table, st.context_lens, st.k_cache, st.v_cache,
@@ -711,16 +738,14 @@ def run_tp(args):
     if world > 1:
         dist.broadcast(drafts, 0)
     st = paged_state(cfg, dev, seed=7000, fill_cache=False)
-    snap = {n: getattr(st, n).clone() for n in
-            ("block_table", "context_lens", "free_stack", "free_top", "ref_counts")}
+    kvsnap = KvStateSnapshot(st)
     nq = k + 1
     ok = torch.empty(B, dtype=torch.int32, device=dev)
     stream = torch.cuda.current_stream(dev)
     ev = []
 
     def step(i, timed):
-        for n, t in snap.items():
-            getattr(st, n).copy_(t, non_blocking=True)
+        kvsnap.restore()
         kv_reserve(ctx, nq, st.block_table, st.context_lens, st.free_stack, st.free_top,
                    st.ref_counts, cfg.block_size, out_ok=ok)
         if timed:
