@@ -263,24 +263,36 @@ def run_ours(args):
                  cfg.block_size)
         if timed:
             e0 = torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
+            e0.record()
         verify_attention(ctx, st.q, st.k_cache, st.v_cache, st.block_table, st.context_lens,
                          out=attn_out, workspace=ws_attn)
         if timed:
             e1 = torch.cuda.Event(enable_timing=True)
-            e1.record(stream)
+            e1.record()
         spec_accept(ctx, tgt, drf, drafts, temperature=cfg.temperature, seed=0, step=i,
                     seq_offset=seq_offset, out=(acc, toks, num, None), workspace=ws_acc)
         if timed:
             e2 = torch.cuda.Event(enable_timing=True)
-            e2.record(stream)
+            e2.record()
             ev["attention"].append((e0, e1))
             ev["accept"].append((e1, e2))
         kv_commit(ctx, nq, acc, st.block_table, st.context_lens, st.free_stack, st.free_top,
                   st.ref_counts, cfg.block_size)
 
-    for i in range(args.warmup):
-        step(i, False)
+    # the step runs on a side stream as a CUDA graph (captured once after the
+    # warm-up steps); the library context is bound to that stream
+    side = torch.cuda.Stream(dev)
+    graph = None
+    with torch.cuda.stream(side):
+        ctx.bind_stream()
+        for i in range(args.warmup):
+            step(i, False)
+        if not args.no_graph:
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=side):
+                step(args.warmup, False)
+            for _ in range(3):
+                graph.replay()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -303,15 +315,27 @@ def run_ours(args):
         dist.barrier()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
-    t0.record(stream)
-    for i in range(args.warmup, args.warmup + args.steps):
-        step(i, True)
-    t1.record(stream)
+    with torch.cuda.stream(side):
+        t0.record(side)
+        for i in range(args.warmup, args.warmup + args.steps):
+            if graph is not None:
+                graph.replay()
+            else:
+                step(i, False)
+        t1.record(side)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     clk = clocks.stop() if clocks else None
     ms = t0.elapsed_time(t1)
+    # per-kernel times from separate steps with events around attention and
+    # acceptance (events between kernels would perturb the timed steps)
+    with torch.cuda.stream(side):
+        for i in range(10):
+            step(args.warmup + args.steps + i, True)
+    torch.cuda.synchronize()
+    del graph
+    ctx.bind_stream()  # back to the default stream for the end-to-end run
     if world > 1:
         tms = torch.tensor([ms], dtype=torch.float64, device=dev)
         dist.all_reduce(tms, op=dist.ReduceOp.MAX)
@@ -337,8 +361,8 @@ def run_ours(args):
     value = units / (ms * 1e-3)
     step_bytes = att_bytes + acc_bytes
     # kv_reserve, kv_write, verify_attention, accept_stats, accept_decide,
-    # accept_final, kv_commit (the attention split counters are cleared by a
-    # driver memset, not a kernel of this library)
+    # accept_final, kv_commit (the attention split counters are zeroed by a
+    # driver memset only the first time a workspace is used)
     launches_per_step = 7
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -358,6 +382,7 @@ def run_ours(args):
                        "frac": acc_bytes / (acc_ms * 1e-3) / 1e9 / peak},
             "step_frac_of_hbm": step_bytes / (ms / args.steps * 1e-3) / 1e9 / peak,
         },
+        "timing": "CUDA graph replays of the step" if not args.no_graph else "stream launches",
         "acceptance_rate": float(acc.float().mean().item() / cfg.k),
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clk,
@@ -837,6 +862,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="wall time the cpu_baseline leg repeats whole-batch steps for")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="time config 1 as plain launches instead of CUDA graph replays")
     ap.add_argument("--no-e2e", action="store_true",
                     help="skip the host-buffer leg (profiling runs)")
     ap.add_argument("--config", choices=["1", "2", "3"], default="1",

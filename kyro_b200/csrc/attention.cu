@@ -26,6 +26,8 @@
 // to the workspace and the split that finishes last (atomic ticket) merges.
 #include <cuda_bf16.h>
 
+#include <mutex>
+
 #include "kyro_internal.cuh"
 #include "ptx.cuh"
 
@@ -423,8 +425,9 @@ verify_attention_kernel(const __nv_bfloat16* __restrict__ q,
   // ---- the last split of this (sequence, KV head, row group) merges all splits
   __syncthreads();
   if (tid == 0) {
-    // a ticket is (epoch << 32 | splits done); a ticket left by an earlier
-    // call carries another epoch and counts as zero
+    // a ticket is (epoch << 32 | splits done); the merging split zeroes it,
+    // and a ticket of another epoch (a workspace that held other data)
+    // counts as zero
     __threadfence();
     unsigned long long cur = *(volatile unsigned long long*)&tickets[item];
     uint32_t done;
@@ -478,6 +481,8 @@ verify_attention_kernel(const __nv_bfloat16* __restrict__ q,
         make_uint2(kyro::ptx::pack_bf16x2(O.x * inv, O.y * inv),
                    kyro::ptx::pack_bf16x2(O.z * inv, O.w * inv));
   }
+  // back to zero for the next call (a replayed graph reuses its epoch)
+  if (tid == 0) tickets[item] = 0ull;
 }
 
 // ------------------------------------------------------------------ host
@@ -565,8 +570,11 @@ void launch(const Plan& pl, dim3 grid, cudaStream_t st, const void* q, const voi
             const void* vc, const int64_t* bt, const int64_t* cl, const uint64_t* tm, void* out,
             float* po, float* pml, unsigned long long* tk, uint32_t* status) {
   constexpr int smem = Geo<D, kStages>::kSmemBytes;
-  cudaFuncSetAttribute(verify_attention_kernel<NT, D, kStages>,
-                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  static std::once_flag attr_once;  // one host call per kernel, never inside a graph capture
+  std::call_once(attr_once, [] {
+    cudaFuncSetAttribute(verify_attention_kernel<NT, D, kStages>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  });
   kyro::launch_pdl(verify_attention_kernel<NT, D, kStages>, grid, dim3(kThreads), smem, st,
                    "verify_attention_kernel", (const __nv_bfloat16*)q, (const uint8_t*)kc,
                    (const uint8_t*)vc, bt, cl, tm, (__nv_bfloat16*)out, po, pml, tk, pl.a, status);

@@ -1526,11 +1526,15 @@ bool use_vec(const void* a, const void* b, int64_t V) {
 
 template <bool VEC, bool STOCH>
 int resident_ctas(int num_sms) {
-  int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, accept_stats_kernel<VEC, STOCH>,
-                                                    kThreads, 0) != cudaSuccess ||
-      per_sm < 1)
-    per_sm = 1;
+  // one occupancy query per kernel (not repeated inside a graph capture)
+  static int per_sm = 0;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, accept_stats_kernel<VEC, STOCH>,
+                                                      kThreads, 0) != cudaSuccess ||
+        per_sm < 1)
+      per_sm = 1;
+  });
   return num_sms * per_sm;
 }
 
