@@ -56,7 +56,7 @@ struct Geo {
   static constexpr int kMoStride = D + 4;
   static constexpr int kMergeBytes =
       (kWarps * kMaxCols * kMoStride + 3 * kWarps * kMaxCols + 2 * kMaxCols) * 4;
-  static constexpr int kFinalBytes = (kMaxSplits * kMaxCols + kMaxCols) * 4;
+  static constexpr int kFinalBytes = (3 * kMaxSplits * kMaxCols + kMaxCols) * 4;
   static_assert(kMergeBytes <= kRingBytes + kQBytes, "the warp merge reuses the ring and Q tile");
   static_assert(kFinalBytes <= kRingBytes, "the split merge reuses the ring");
   static constexpr int kSmemBytes =
@@ -132,6 +132,31 @@ verify_attention_kernel(const __nv_bfloat16* __restrict__ q,
   for (int p = 0; p < NS - 1; ++p)
     first_ids[p] = split * a.split_blocks + p * kWarps + warp < a.max_blocks ? bt[p * kWarps + warp]
                                                                              : 0;
+  // the rest of the split's block ids (entries tid, tid + kThreads of the
+  // split's span of the table row) and the CTA's Q rows do not depend on the
+  // context length either: they load in the same round trip
+  constexpr int kIdsPerThread = kMaxSplitBlocks / kThreads;
+  constexpr int kQPerThread = kMaxCols * (D / 8) / kThreads;
+  const int span = min(a.split_blocks, a.max_blocks - split * a.split_blocks);
+  int64_t my_ids[kIdsPerThread];
+#pragma unroll
+  for (int j = 0; j < kIdsPerThread; ++j)
+    my_ids[j] = tid + j * kThreads < span ? bt[tid + j * kThreads] : 0;
+  const int col0 = grp * kMaxCols;
+  const int ncols = min(kMaxCols, a.rows - col0);
+  uint4 my_q[kQPerThread];
+#pragma unroll
+  for (int j = 0; j < kQPerThread; ++j) {
+    const int i = tid + j * kThreads;
+    const int col = i / (D / 8), ch = i % (D / 8);
+    my_q[j] = make_uint4(0, 0, 0, 0);
+    if (col < ncols) {
+      const int r = col0 + col, jq = r / a.group, gi = r % a.group;
+      const int h = kvh * a.group + gi;
+      my_q[j] =
+          *reinterpret_cast<const uint4*>(q + (((int64_t)b * a.nq + jq) * a.hq + h) * D + ch * 8);
+    }
+  }
   const int64_t ctx = context_lens[b];
   const int64_t total = ctx + a.nq;
   if (ctx < 0 || (total + kBS - 1) / kBS > a.max_blocks) {
@@ -143,8 +168,6 @@ verify_attention_kernel(const __nv_bfloat16* __restrict__ q,
   if (split >= nsplit) return;
   const int blk0 = split * a.split_blocks;
   const int nb = min(nblk, blk0 + a.split_blocks) - blk0;
-  const int col0 = grp * kMaxCols;
-  const int ncols = min(kMaxCols, a.rows - col0);
 
   uint8_t* ring = smem;
   uint8_t* qtile = ring + G::kRingBytes;
@@ -169,24 +192,24 @@ verify_attention_kernel(const __nv_bfloat16* __restrict__ q,
     kyro::ptx::cp_async_commit();
   }
 
-  // ---- block ids of this split, Q rows, column masks
-  for (int i = tid; i < nb; i += kThreads) {
-    int64_t phys = bt[i];
-    if (phys < 0 || phys >= a.num_blocks) {
-      kyro::dev::flag(status, KYRO_DEV_BAD_BLOCK);
-      phys = 0;
+  // ---- block ids of this split, Q rows, column masks into shared memory
+#pragma unroll
+  for (int j = 0; j < kIdsPerThread; ++j) {
+    const int i = tid + j * kThreads;
+    if (i < nb) {
+      int64_t phys = my_ids[j];
+      if (phys < 0 || phys >= a.num_blocks) {
+        kyro::dev::flag(status, KYRO_DEV_BAD_BLOCK);
+        phys = 0;
+      }
+      ids[i] = (int32_t)phys;
     }
-    ids[i] = (int32_t)phys;
   }
-  for (int i = tid; i < kMaxCols * (kD / 8); i += kThreads) {
+#pragma unroll
+  for (int j = 0; j < kQPerThread; ++j) {
+    const int i = tid + j * kThreads;
     const int col = i / (kD / 8), ch = i % (kD / 8);
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (col < ncols) {
-      const int r = col0 + col, j = r / a.group, gi = r % a.group;
-      const int h = kvh * a.group + gi;
-      v = *reinterpret_cast<const uint4*>(q + (((int64_t)b * a.nq + j) * a.hq + h) * kD + ch * 8);
-    }
-    *reinterpret_cast<uint4*>(qtile + col * kQStride * 2 + ch * 16) = v;
+    *reinterpret_cast<uint4*>(qtile + col * kQStride * 2 + ch * 16) = my_q[j];
   }
   for (int col = tid; col < kMaxCols; col += kThreads) {
     uint64_t m = 0;
@@ -443,17 +466,21 @@ verify_attention_kernel(const __nv_bfloat16* __restrict__ q,
   __syncthreads();
   if (!*sh_last) return;
   __threadfence();
-  float* fscale = reinterpret_cast<float*>(ring);  // [split][col] (the warp merge is done)
-  float* finv = fscale + kMaxSplits * kMaxCols;                    // [col]
+  // every split's (m, l) per column, copied in one parallel pass
+  float* sml = reinterpret_cast<float*>(ring);                    // [split][col][2]
+  float* fscale = sml + kMaxSplits * kMaxCols * 2;                // [split][col]
+  float* finv = fscale + kMaxSplits * kMaxCols;                   // [col]
+  for (int i = tid; i < nsplit * kMaxCols * 2; i += kThreads) sml[i] = __ldcg(&pml[i]);
+  __syncthreads();
   for (int col = tid; col < ncols; col += kThreads) {
     float M = -INFINITY;
-    for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, __ldcg(&pml[(sp * kMaxCols + col) * 2]));
+    for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, sml[(sp * kMaxCols + col) * 2]);
     const float Mu = M == -INFINITY ? 0.0f : M;
     float L = 0.0f;
     for (int sp = 0; sp < nsplit; ++sp) {
-      const float f = kyro::ptx::fast_exp2(__ldcg(&pml[(sp * kMaxCols + col) * 2]) - Mu);
+      const float f = kyro::ptx::fast_exp2(sml[(sp * kMaxCols + col) * 2] - Mu);
       fscale[sp * kMaxCols + col] = f;
-      L += f * __ldcg(&pml[(sp * kMaxCols + col) * 2 + 1]);
+      L += f * sml[(sp * kMaxCols + col) * 2 + 1];
     }
     finv[col] = L > 0.0f ? 1.0f / L : 0.0f;
   }
