@@ -39,6 +39,7 @@ constexpr int kThreads = kWarps * 32;
 constexpr int kMaxCols = 32;          // query rows per work item
 constexpr int kMaxSplitBlocks = 256;  // KV blocks per work item
 constexpr int kMaxSplits = 64;        // work items per (sequence, KV head, row group)
+constexpr float kLazyRescale = 8.0f;  // log2 headroom before a column's running max moves
 
 // Shared-memory geometry for head_dim D (64 or 128) and NS ring stages.
 template <int D, int NS>
@@ -281,8 +282,7 @@ verify_attention_kernel(const __nv_bfloat16* __restrict__ q,
     const int64_t tok0 = (int64_t)blk * kBS;
     const bool need_mask = tok0 + kBS > ctx;
     const int trow = lane >> 2;
-    float alpha[NT][2];
-    bool moved = false;
+    bool over = false;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
@@ -296,37 +296,54 @@ verify_attention_kernel(const __nv_bfloat16* __restrict__ q,
           if (!ok) v = -INFINITY;
         }
         sc[nt][e] = v;
+        over |= v > m_run[nt][e & 1] + kLazyRescale;
       }
+    }
+    // The running max of a column moves only when a score passes it by more
+    // than kLazyRescale (log2 units), so P stays below 2^kLazyRescale; most
+    // blocks skip the column reductions and the O rescale.
+    if (__any_sync(0xffffffffu, over)) {
+      float alpha[NT][2];
+      bool moved = false;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          float cm = fmaxf(sc[nt][c], sc[nt][c + 2]);
+          cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 4));
+          cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 8));
+          cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 16));
+          const float m_new = fmaxf(m_run[nt][c], cm);
+          const float m_use = m_new == -INFINITY ? 0.0f : m_new;
+          alpha[nt][c] = kyro::ptx::fast_exp2(m_run[nt][c] - m_use);
+          moved |= m_new != m_run[nt][c];
+          l_run[nt][c] *= alpha[nt][c];
+          m_run[nt][c] = m_new;
+        }
+      // rescale O only when some running max moved (alpha == 1 otherwise)
+      if (__any_sync(0xffffffffu, moved)) {
+#pragma unroll
+        for (int mt = 0; mt < kMT; ++mt)
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            o[mt][nt][0] *= alpha[nt][0];
+            o[mt][nt][1] *= alpha[nt][1];
+            o[mt][nt][2] *= alpha[nt][0];
+            o[mt][nt][3] *= alpha[nt][1];
+          }
+      }
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
-        float cm = fmaxf(sc[nt][c], sc[nt][c + 2]);
-        cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 4));
-        cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 8));
-        cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 16));
-        const float m_new = fmaxf(m_run[nt][c], cm);
-        const float m_use = m_new == -INFINITY ? 0.0f : m_new;
-        alpha[nt][c] = kyro::ptx::fast_exp2(m_run[nt][c] - m_use);
-        moved |= m_new != m_run[nt][c];
+        const float m_use = m_run[nt][c] == -INFINITY ? 0.0f : m_run[nt][c];
         const float p0 = kyro::ptx::fast_exp2(sc[nt][c] - m_use);
         const float p1 = kyro::ptx::fast_exp2(sc[nt][c + 2] - m_use);
         sc[nt][c] = p0;
         sc[nt][c + 2] = p1;
-        l_run[nt][c] = l_run[nt][c] * alpha[nt][c] + p0 + p1;
-        m_run[nt][c] = m_new;
+        l_run[nt][c] += p0 + p1;
       }
-    }
-    // rescale O only when some running max moved (alpha == 1 otherwise)
-    if (__any_sync(0xffffffffu, moved)) {
-#pragma unroll
-      for (int mt = 0; mt < kMT; ++mt)
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          o[mt][nt][0] *= alpha[nt][0];
-          o[mt][nt][1] *= alpha[nt][1];
-          o[mt][nt][2] *= alpha[nt][0];
-          o[mt][nt][3] *= alpha[nt][1];
-        }
-    }
     // P^T fragment (tokens x cols) -> B operand (k = tokens, n = cols)
     uint32_t pb[NT][2];
 #pragma unroll
