@@ -1518,6 +1518,331 @@ __global__ void __launch_bounds__(kTreeThreads) accept_tree_kernel(Args a) {
   }
 }
 
+// ------------------------------------------------------------ clustered tree walk
+//
+// The stochastic walk of accept_tree_kernel on a cluster of kTreeC CTAs per
+// sequence.  CTA `rank` owns chunks [rank * cpc, rank * cpc + cpc) of the
+// vocabulary and keeps their p (fp64, the current residual p_nr) and q (fp32,
+// exact in fp64) in shared memory, so a residual step costs one division per
+// entry instead of the whole chain from p_0.  Every CTA takes the same
+// decisions from the same inputs in the same order (row statistics, child
+// tests, thresholds); per-chunk sums cross the cluster through distributed
+// shared memory (double-buffered, one cluster barrier per exchange) and each
+// CTA adds them in the contract's order (chunks l, l+32, ... into lane l,
+// then the butterfly), so all ranks hold bit-identical R_j.  Rank 0 writes
+// the path, the CTA owning the drawn token's chunk writes that token.
+
+constexpr int kTreeCMaxChunks = 32;  // chunks per CTA (one warp each)
+
+__device__ __forceinline__ uint32_t tc_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t tc_size() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void tc_cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" :::
+                   "memory");
+}
+// A 64-bit word of CTA `rank`'s shared memory at this CTA's offset `local`.
+__device__ __forceinline__ unsigned long long tc_ld_remote(const void* local, uint32_t rank) {
+  uint32_t la = (uint32_t)__cvta_generic_to_shared(local), ra;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(la), "r"(rank));
+  unsigned long long v;
+  asm volatile("ld.shared::cluster.u64 %0, [%1];" : "=l"(v) : "r"(ra) : "memory");
+  return v;
+}
+
+struct TreeClusterShared {
+  float mP[kTreeCMaxChunks], gP[kTreeCMaxChunks], mQ[kTreeCMaxChunks], gQ[kTreeCMaxChunks];
+  unsigned long long xsum[2][kTreeCMaxChunks];  // exchanged chunk sums (f64 bits or u64)
+  double R[kMaxNodes];
+  int ch[kMaxNodes];
+  float Mp, Mq;
+  double Sp, Sq;
+  int nch, node, accepted, token, done, sub;
+  unsigned long long T;
+};
+
+template <bool VEC>
+__global__ void __launch_bounds__(kTreeThreads) accept_tree_cluster_kernel(Args a, int cpc) {
+  extern __shared__ __align__(16) uint8_t tree_smem[];
+  TreeClusterShared& sh = *reinterpret_cast<TreeClusterShared*>(tree_smem);
+  double* pv = reinterpret_cast<double*>(tree_smem + ((sizeof(TreeClusterShared) + 15) & ~size_t(15)));
+  float* qv = reinterpret_cast<float*>(pv + (size_t)cpc * kChunk);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t rank = tc_rank(), C = tc_size();
+  const int b = (int)(blockIdx.x / C);
+  const int N = a.k + 1;
+  const int nc = a.nchunks;
+  const int c0 = (int)rank * cpc;
+  const int ncc = max(0, min(nc, c0 + cpc) - c0);  // chunks of this CTA
+  const uint32_t seq = (uint32_t)(a.seq_offset + b);
+  const int32_t* tok = a.node_tokens + (int64_t)b * N;
+  const int32_t* par = a.parents + (int64_t)b * N;
+  grid_dependency_wait();  // the chunk statistics are complete
+  if (rank == 0)
+    for (int n = threadIdx.x; n < N; n += kTreeThreads) {
+      a.out_path[(int64_t)b * N + n] = -1;
+      a.out_tokens[(int64_t)b * N + n] = -1;
+    }
+  int plen = 1, ntok = 0, xbuf = 0;  // thread 0's counts; the exchange buffer (uniform)
+  if (threadIdx.x == 0) {
+    sh.node = 0;
+    sh.done = 0;
+  }
+  __syncthreads();
+  if (rank == 0 && threadIdx.x == 0) a.out_path[(int64_t)b * N] = 0;
+  // sums of all chunks from their owners, in the contract's lane order
+  auto gather_f64 = [&](int buf) -> double {
+    double t = 0.0;
+    for (int cc = lane; cc < nc; cc += 32)
+      t = KY_DADD(t, __longlong_as_double((long long)tc_ld_remote(&sh.xsum[buf][cc % cpc],
+                                                                   (uint32_t)(cc / cpc))));
+    return warp_butterfly(t);
+  };
+  // a path visits at most N nodes; every CTA of the cluster takes the same
+  // number of steps
+  for (int walk = 0; walk <= N && !sh.done; ++walk) {
+    const int node = sh.node;
+    if (threadIdx.x == 0) {
+      int m = 0;
+      for (int c = node + 1; c < N; ++c)
+        if (par[c] == node) sh.ch[m++] = c;
+      sh.nch = m;
+      sh.accepted = -1;
+    }
+    // row statistics of the node's target (warp 0) and draft (warp 1) rows
+    if (warp < 2) {
+      const RowStat rs = row_stat(a, (int64_t)b * a.R + (warp == 0 ? node : N + node));
+      if (lane == 0) {
+        if (warp == 0) {
+          sh.Mp = rs.M;
+          sh.Sp = rs.S;
+        } else {
+          sh.Mq = rs.M;
+          sh.Sq = rs.S;
+        }
+      }
+    }
+    __syncthreads();
+    const ChunkStat* stp = a.stats + ((int64_t)b * a.R + node) * nc;
+    const ChunkStat* stq = a.stats + ((int64_t)b * a.R + N + node) * nc;
+    if ((int)threadIdx.x < ncc) {
+      const int c = c0 + threadIdx.x;
+      const float mp = stp[c].m, mq = stq[c].m;
+      sh.mP[threadIdx.x] = mp;
+      sh.gP[threadIdx.x] = ky_chunk_scale(mp, sh.Mp, sh.Sp);
+      sh.mQ[threadIdx.x] = mq;
+      sh.gQ[threadIdx.x] = ky_chunk_scale(mq, sh.Mq, sh.Sq);
+    }
+    __syncthreads();
+    const float* prow = stats_row_ptr(a, b, node);
+    const float* qrow = stats_row_ptr(a, b, N + node);
+    // p_0 and q of this CTA's entries (entries past V hold 0, which adds 0
+    // to every sum below)
+    if (warp < ncc) {
+      const int cc = c0 + warp;
+      const f2_t mm = f2_pack(sh.mP[warp], sh.mQ[warp]);
+      const f2_t gg = f2_pack(sh.gP[warp], sh.gQ[warp]);
+#pragma unroll
+      for (int g = 0; g < kVec; ++g) {
+        const int64_t e0 = (int64_t)cc * kChunk + (g * 32 + lane) * 4;
+        const float4 zp = load4<VEC>(prow, e0, a.V);
+        const float4 zq = load4<VEC>(qrow, e0, a.V);
+        const float p4[4] = {zp.x, zp.y, zp.z, zp.w};
+        const float q4[4] = {zq.x, zq.y, zq.z, zq.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          f2_t z = f2_pack(p4[j], q4[j]);
+          if (a.inv_t != 1.0f) z = f2_mul(z, f2_pack(a.inv_t, a.inv_t));
+          float pf, qf;
+          f2_unpack(f2_mul(exp_pair(f2_sub(z, mm)), gg), pf, qf);
+          const bool ok = e0 + j < a.V;
+          const int idx = warp * kChunk + (g * 32 + lane) * 4 + j;
+          pv[idx] = ok ? (double)pf : 0.0;
+          qv[idx] = ok ? qf : 0.0f;
+        }
+      }
+    }
+    __syncthreads();
+    int nr = 0;
+    for (int i = 0; i < sh.nch; ++i) {
+      const int c = sh.ch[i];
+      if (threadIdx.x == 0) {
+        const int x = tok[c];
+        if (x >= 0 && x < a.V) {
+          const int cx = x / kChunk;
+          const float mpx = stp[cx].m, mqx = stq[cx].m;
+          float sp = prow[x], sq = qrow[x];
+          if (a.inv_t != 1.0f) {
+            sp = KY_FMUL(sp, a.inv_t);
+            sq = KY_FMUL(sq, a.inv_t);
+          }
+          const double qx =
+              (double)KY_FMUL(exp_fast(KY_FSUB(sq, mqx)), ky_chunk_scale(mqx, sh.Mq, sh.Sq));
+          double px =
+              (double)KY_FMUL(exp_fast(KY_FSUB(sp, mpx)), ky_chunk_scale(mpx, sh.Mp, sh.Sp));
+          for (int r = 0; r < nr; ++r) px = ky_tree_step(px, qx, sh.R[r]);
+          const double u =
+              (double)ky_odd_to_float(ky_uniform_odd(a.seed, seq, (uint32_t)c, KY_STREAM_ACCEPT,
+                                                     a.step));
+          if (u < KY_DDIV(px, qx)) sh.accepted = c;
+        } else if (rank == 0) {
+          kyro::dev::flag(a.status, KYRO_DEV_BAD_TOKEN);
+        }
+      }
+      __syncthreads();
+      if (sh.accepted >= 0) break;
+      // rejected: p_nr from the stored p_{nr-1}, then R_nr = sum max(p_nr - q, 0)
+      if (warp < ncc) {
+        double acc[4] = {0.0, 0.0, 0.0, 0.0};
+#pragma unroll
+        for (int g = 0; g < kVec; ++g)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int idx = warp * kChunk + (g * 32 + lane) * 4 + j;
+            double p = pv[idx];
+            const double q = (double)qv[idx];
+            if (nr > 0) {
+              p = ky_tree_step(p, q, sh.R[nr - 1]);
+              pv[idx] = p;
+            }
+            acc[j] = KY_DADD(acc[j], ky_tree_excess(p, q));
+          }
+        const double t = warp_butterfly(KY_DADD(KY_DADD(acc[0], acc[1]), KY_DADD(acc[2], acc[3])));
+        if (lane == 0) sh.xsum[xbuf][warp] = (unsigned long long)__double_as_longlong(t);
+      }
+      tc_cluster_sync();
+      if (warp == 0) {
+        const double t = gather_f64(xbuf);
+        if (lane == 0) sh.R[nr] = t;
+      }
+      xbuf ^= 1;
+      __syncthreads();
+      ++nr;
+    }
+    if (sh.accepted < 0) {
+      // draw from p_nr: integer weights, chunk sums, then one chunk's scan
+      if (warp < ncc) {
+        unsigned long long t = 0;
+#pragma unroll
+        for (int g = 0; g < kVec; ++g)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int idx = warp * kChunk + (g * 32 + lane) * 4 + j;
+            double p = pv[idx];
+            if (nr > 0) {
+              p = ky_tree_step(p, (double)qv[idx], sh.R[nr - 1]);
+              pv[idx] = p;
+            }
+            t += ky_weight_d(p);
+          }
+        t = warp_sum(t);
+        if (lane == 0) sh.xsum[xbuf][warp] = t;
+      }
+      tc_cluster_sync();
+      if (warp == 0) {
+        unsigned long long tot = 0;
+        for (int cc = lane; cc < nc; cc += 32)
+          tot += tc_ld_remote(&sh.xsum[xbuf][cc % cpc], (uint32_t)(cc / cpc));
+        tot = warp_sum(tot);
+        int sub = -1;
+        unsigned long long T = 0;
+        if (tot != 0) {
+          T = ky_cdf_threshold(
+              ky_uniform_odd(a.seed, seq, (uint32_t)node, KY_STREAM_RESAMPLE, a.step), tot);
+          unsigned long long base = 0;
+          for (int s0 = 0; s0 < nc && sub < 0; s0 += 32) {
+            const unsigned long long ws =
+                s0 + lane < nc ? tc_ld_remote(&sh.xsum[xbuf][(s0 + lane) % cpc],
+                                              (uint32_t)((s0 + lane) / cpc))
+                               : 0ull;
+            const unsigned long long inc = base + warp_inclusive(ws);
+            const unsigned hit = __ballot_sync(0xffffffffu, inc >= T && s0 + lane < nc);
+            if (hit) {
+              const int l = __ffs(hit) - 1;
+              sub = s0 + l;
+              T -= __shfl_sync(0xffffffffu, inc - ws, l);
+            } else {
+              base = __shfl_sync(0xffffffffu, inc, 31);
+            }
+          }
+        }
+        if (lane == 0) {
+          sh.sub = sub;
+          sh.T = T;
+        }
+      }
+      __syncthreads();
+      // the token: in the cut chunk by its owner, V - 1 when p_nr has no mass
+      const int sub = sh.sub;
+      const uint32_t owner = sub >= 0 ? (uint32_t)(sub / cpc) : 0u;
+      if (warp == 0 && rank == owner) {
+        int token = (int)a.V - 1;
+        if (sub >= 0) {
+          const unsigned long long T = sh.T;
+          const int w = sub - c0;
+          unsigned long long cbase = 0;
+          int found = -1;
+          for (int g = 0; g < kVec; ++g) {
+            unsigned long long wj[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              wj[j] = ky_weight_d(pv[w * kChunk + (g * 32 + lane) * 4 + j]);
+            const unsigned long long s4 = (wj[0] + wj[1]) + (wj[2] + wj[3]);
+            const unsigned long long inc = warp_inclusive(s4);
+            unsigned long long Cc = cbase + inc - s4;
+            int mine = -1;
+            if (Cc < T && Cc + s4 >= T) {
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                Cc += wj[j];
+                if (mine < 0 && Cc >= T) mine = j;
+              }
+            }
+            const unsigned hit = __ballot_sync(0xffffffffu, mine >= 0);
+            if (found < 0 && hit) {
+              const int l = __ffs(hit) - 1;
+              found = sub * kChunk + (g * 32 + l) * 4 + __shfl_sync(0xffffffffu, mine, l);
+            }
+            cbase += __shfl_sync(0xffffffffu, inc, 31);
+          }
+          if (found >= 0) token = found;
+        }
+        if (lane == 0) a.out_tokens[(int64_t)b * N + ntok] = token;
+      }
+      xbuf ^= 1;
+    }
+    if (threadIdx.x == 0) {
+      const int c = sh.accepted;
+      if (c >= 0) {
+        if (rank == 0) {
+          a.out_path[(int64_t)b * N + plen] = c;
+          a.out_tokens[(int64_t)b * N + ntok] = tok[c];
+        }
+        ++plen;
+        ++ntok;
+        sh.node = c;
+      } else {
+        ++ntok;
+        sh.done = 1;
+        if (rank == 0) {
+          a.out_path_len[b] = plen;
+          a.out_num_tokens[b] = ntok;
+        }
+      }
+    }
+    __syncthreads();
+  }
+  // no CTA leaves while another may still read its shared memory
+  tc_cluster_sync();
+}
+
 // ------------------------------------------------------------ host side
 
 bool use_vec(const void* a, const void* b, int64_t V) {
@@ -1556,6 +1881,41 @@ int launch_dependent(Kernel kernel, unsigned grid, unsigned block, cudaStream_t 
   const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, a);
   if (err != cudaSuccess) return kyro::cuda_error(err, name);
   return KYRO_OK;
+}
+
+// The clustered tree walk: clusters of 4 CTAs (up to 64 chunks) or 8 (up to
+// 256), each CTA holding its chunks' p and q in shared memory.  Returns
+// false when the vocabulary is too large for it.
+template <bool VEC>
+bool launch_tree_cluster(int B, const Args& a, cudaStream_t stream, int* rc) {
+  const int nc = a.nchunks;
+  if (nc > 8 * kTreeCMaxChunks) return false;
+  const int C = nc <= 4 * 16 ? 4 : 8;
+  const int cpc = (nc + C - 1) / C;
+  const size_t smem = ((sizeof(TreeClusterShared) + 15) & ~size_t(15)) +
+                      (size_t)cpc * kChunk * (sizeof(double) + sizeof(float));
+  static std::once_flag once;  // one host call per kernel, never inside a graph capture
+  std::call_once(once, [] {
+    cudaFuncSetAttribute(accept_tree_cluster_kernel<VEC>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  });
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(B * C));
+  cfg.blockDim = dim3(kTreeThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, accept_tree_cluster_kernel<VEC>, a, cpc);
+  *rc = err == cudaSuccess ? KYRO_OK : kyro::cuda_error(err, "accept_tree_cluster_kernel");
+  return true;
 }
 
 template <bool VEC, bool STOCH>
@@ -1915,6 +2275,8 @@ int kyro_spec_accept_tree(kyro_ctx* ctx, const kyro_tree_params* p, const float*
     accept_stats_kernel<true, true><<<(int)(need_ctas < resident ? need_ctas : resident),
                                       kThreads, 0, ctx->stream>>>(a);
     KY_TRY(kyro::check_launch("accept_stats_kernel"));
+    int rc = KYRO_OK;
+    if (launch_tree_cluster<true>(B, a, ctx->stream, &rc)) return rc;
     return launch_dependent(accept_tree_kernel<true, true>, (unsigned)B, kTreeThreads, ctx->stream,
                             a, "accept_tree_kernel");
   }
@@ -1933,6 +2295,8 @@ int kyro_spec_accept_tree(kyro_ctx* ctx, const kyro_tree_params* p, const float*
     accept_stats_kernel<false, true><<<(int)(need_ctas < resident ? need_ctas : resident),
                                        kThreads, 0, ctx->stream>>>(a);
     KY_TRY(kyro::check_launch("accept_stats_kernel"));
+    int rc = KYRO_OK;
+    if (launch_tree_cluster<false>(B, a, ctx->stream, &rc)) return rc;
     return launch_dependent(accept_tree_kernel<false, true>, (unsigned)B, kTreeThreads,
                             ctx->stream, a, "accept_tree_kernel");
   }
