@@ -535,7 +535,32 @@ __device__ __forceinline__ RowStat row_stat(const Args& a, int64_t srow) {
   RowStat rs;
   rs.arg = 0;
   rs.S = 0.0;
-  if (a.stoch) {
+  if (a.stoch && nc <= 256) {
+    // one round trip: the lane's chunk maxima and sums stay in registers
+    // between the maximum and the normaliser
+    float mm[8], ee[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = j * 32 + lane;
+      mm[j] = -INFINITY;
+      ee[j] = 0.0f;
+      if (c < nc) {
+        const ChunkStat cs = st[c];
+        mm[j] = cs.m;
+        ee[j] = cs.E;
+      }
+    }
+    float M = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) M = fmaxf(M, mm[j]);
+    M = kyro::dev::warp_max(M);
+    double t = 0.0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (j * 32 + lane < nc) t = KY_DADD(t, ky_chunk_mass(ee[j], mm[j], M));
+    rs.M = M;
+    rs.S = warp_butterfly(t);
+  } else if (a.stoch) {
     float M = -INFINITY;
     for (int g = 0; g < nc; g += 256) {
       float mm[8];
@@ -895,8 +920,23 @@ __device__ __forceinline__ int cut_index(const Args& a, const FinalRow& fr, bool
   const int nc = a.nchunks;
   int sub = -1;
   unsigned long long base = 0;
+  // up to 256 chunk sums load in one round trip, then the scan runs on them
+  unsigned long long wr[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int c = j * 32 + lane;
+    wr[j] = (c < nc && nc <= 256) ? __ldcg(&W[(int64_t)c * wstride]) : 0ull;
+  }
   for (int s0 = 0; s0 < nc && sub < 0; s0 += 32) {
-    const unsigned long long ws = (s0 + lane < nc) ? __ldcg(&W[(int64_t)(s0 + lane) * wstride]) : 0ull;
+    unsigned long long ws;
+    if (nc <= 256) {
+      ws = 0ull;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (j * 32 == s0) ws = wr[j];
+    } else {
+      ws = (s0 + lane < nc) ? __ldcg(&W[(int64_t)(s0 + lane) * wstride]) : 0ull;
+    }
     const unsigned long long inc = base + warp_inclusive(ws);
     const unsigned hit = __ballot_sync(0xffffffffu, inc >= T && s0 + lane < nc);
     if (hit) {
