@@ -37,6 +37,8 @@ sys.path.insert(0, ROOT)
 
 METRIC = "spec-verify tokens/s (attn+accept)"
 UNIT = "verified positions/s"
+# untimed steps after the timed region that carry CUDA events around the kernels
+PER_KERNEL_STEPS = 10
 
 
 def workload_desc(cfg, n):
@@ -331,7 +333,7 @@ def run_ours(args):
     # per-kernel times from separate steps with events around attention and
     # acceptance (events between kernels would perturb the timed steps)
     with torch.cuda.stream(side):
-        for i in range(10):
+        for i in range(PER_KERNEL_STEPS):
             step(args.warmup + args.steps + i, True)
     torch.cuda.synchronize()
     del graph
@@ -655,13 +657,18 @@ def run_tree(args):
     t0.record(stream)
     plens = []
     for i in range(args.warmup, args.warmup + args.steps):
-        plens.append(step(i, True))
+        plens.append(step(i, False))
     t1.record(stream)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     clk = clocks.stop() if clocks else None
     ms = t0.elapsed_time(t1)
+    # per-kernel times from separate steps, so that no event sits between the
+    # chained launches of the timed ones
+    for i in range(args.warmup + args.steps, args.warmup + args.steps + PER_KERNEL_STEPS):
+        step(i, True)
+    torch.cuda.synchronize()
     att_ms = float(np.mean([a.elapsed_time(b) for a, b in ev["attention"]]))
     acc_ms = float(np.mean([a.elapsed_time(b) for a, b in ev["accept"]]))
     if world > 1:
@@ -805,13 +812,16 @@ def run_tp(args):
     t0.record(stream)
     accs = []
     for i in range(args.warmup, args.warmup + args.steps):
-        accs.append(step(i, True))
+        accs.append(step(i, False))
     t1.record(stream)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     clk = clocks.stop() if clocks else None
     ms = t0.elapsed_time(t1)
+    for i in range(args.warmup + args.steps, args.warmup + args.steps + PER_KERNEL_STEPS):
+        step(i, True)
+    torch.cuda.synchronize()
     acc_ms = float(np.mean([a.elapsed_time(b) for a, b in ev]))
     if world > 1:
         t = torch.tensor([ms, acc_ms], dtype=torch.float64, device=dev)
