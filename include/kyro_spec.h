@@ -243,6 +243,24 @@ int kyro_kv_reserve(kyro_ctx* ctx, const kyro_kv_params* p, int32_t num_new,
                     int64_t* block_table, const int64_t* context_lens, int32_t* free_stack,
                     int32_t* free_top, int32_t* ref_counts, int32_t* out_ok);
 
+/* kyro_kv_reserve_cow: kyro_kv_reserve for block tables that share prefix
+ * blocks.  allocate_with_prefix (block_manager.rs:53-105) hands a request the
+ * radix cache's blocks with ref_count += 1 (:60-63), so a sequence's last,
+ * partly filled block can be shared; growing into it would overwrite the
+ * other holders' tokens.  Here, in sequence order, such a sequence first
+ * pops a fresh block (ref_count 1) for it, the shared block's ref_count drops
+ * by one, its table entry is replaced, and every slot of the block is copied
+ * in each of the num_layers K and V caches (copy-on-write); then its new
+ * blocks are popped as kyro_kv_reserve does.  A sequence that cannot get all
+ * of its blocks gets none (out_ok[b] = 0).  out_cow int32 [B, 2] receives the
+ * (shared, fresh) pair of each sequence, or (-1, -1).  k_caches / v_caches
+ * are host arrays of device pointers as in kyro_kv_commit_tree. */
+int kyro_kv_reserve_cow(kyro_ctx* ctx, const kyro_kv_params* p, int32_t num_new,
+                        int32_t num_layers, void* const* k_caches, void* const* v_caches,
+                        int32_t num_kv_heads, int32_t head_dim, int64_t* block_table,
+                        const int64_t* context_lens, int32_t* free_stack, int32_t* free_top,
+                        int32_t* ref_counts, int32_t* out_ok, int32_t* out_cow);
+
 /* kyro_kv_commit: after verification keep accept_len[b] + 1 of the num_new
  * reserved slots (the last accepted token plus the accepted drafts),
  * advance context_lens, and release the blocks that now lie wholly beyond
@@ -278,6 +296,31 @@ int kyro_kv_write(kyro_ctx* ctx, const kyro_kv_params* p, int32_t num_new, int32
                   int32_t head_dim, const void* k_new, const void* v_new,
                   const int64_t* block_table, const int64_t* context_lens, void* k_cache,
                   void* v_cache);
+
+/* kyro_rope_kv_write: the steps between the q/k/v projections and attention
+ * in LlamaAttention::forward (src/model/llama.rs:73-82) for the num_new new
+ * tokens of every sequence: rotary position embedding of the query and key
+ * heads (RotaryEmbedding::apply, src/model/layers.rs:37-61, with
+ * inv_freq[i] = 1 / rope_theta^(2i/head_dim) as in :26-33; llama.rs:45 uses
+ * theta 10000), then the rotated keys and the values stored in the paged
+ * slots context_lens[b] + j as kyro_kv_write does (append_kv), and the
+ * rotated queries written to q_out (which may be q itself).  Token j of
+ * sequence b is rotated at position context_lens[b] + pos_offsets[j]
+ * (the reference's index + i, layers.rs:45); pos_offsets NULL means j, and a
+ * draft tree passes each node's depth.
+ *   q       bf16 [B, num_new, num_heads, head_dim]     (q_proj, reshaped :73)
+ *   k_new   bf16 [B, num_new, num_kv_heads, head_dim]  (k_proj, :74)
+ *   v_new   bf16 [B, num_new, num_kv_heads, head_dim]  (v_proj, :75)
+ *   q_out   bf16 [B, num_new, num_heads, head_dim]
+ *   k_cache, v_cache bf16 [num_blocks, num_kv_heads, block_size, head_dim]
+ * head_dim is a multiple of 16 and at most 256.  Each rotated element is
+ * x*cos + (-/+)x'*sin with each product and the sum rounded to fp32 (the
+ * reference's broadcast_mul and add), then rounded to bf16. */
+int kyro_rope_kv_write(kyro_ctx* ctx, const kyro_kv_params* p, int32_t num_new,
+                       int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
+                       float rope_theta, const int32_t* pos_offsets, const void* q,
+                       const void* k_new, const void* v_new, const int64_t* block_table,
+                       const int64_t* context_lens, void* q_out, void* k_cache, void* v_cache);
 
 /* ------------------------------------------------- tree acceptance */
 

@@ -42,8 +42,8 @@ EXPORTS = (
     "kyro_spec_accept_workspace_size", "kyro_spec_accept", "kyro_spec_accept_static",
     "kyro_sample_workspace_size",
     "kyro_sample_tokens", "kyro_verify_attention_workspace_size", "kyro_verify_attention",
-    "kyro_kv_reserve", "kyro_kv_commit", "kyro_kv_commit_tree", "kyro_kv_write",
-    "kyro_philox_uniforms", "kyro_selftest_exp",
+    "kyro_kv_reserve", "kyro_kv_reserve_cow", "kyro_kv_commit", "kyro_kv_commit_tree", "kyro_kv_write",
+    "kyro_rope_kv_write", "kyro_philox_uniforms", "kyro_selftest_exp",
     "kyro_tp_unique_id", "kyro_ctx_tp_init", "kyro_spec_accept_tp_workspace_size",
     "kyro_spec_accept_tp", "kyro_spec_accept_tree_workspace_size", "kyro_spec_accept_tree",
 )
@@ -121,9 +121,13 @@ def load():
                                             sz]),
         "kyro_kv_reserve": (C.c_int, [vp, P(KVParams), i32, vp, vp, vp, vp, vp, vp]),
         "kyro_kv_commit": (C.c_int, [vp, P(KVParams), i32, vp, vp, vp, vp, vp, vp]),
+        "kyro_kv_reserve_cow": (C.c_int, [vp, P(KVParams), i32, i32, vp, vp, i32, i32, vp, vp, vp,
+                                          vp, vp, vp, vp]),
         "kyro_kv_commit_tree": (C.c_int, [vp, P(KVParams), i32, vp, vp, i32, vp, vp, i32, i32, vp,
                                           vp, vp, vp, vp]),
         "kyro_kv_write": (C.c_int, [vp, P(KVParams), i32, i32, i32, vp, vp, vp, vp, vp, vp]),
+        "kyro_rope_kv_write": (C.c_int, [vp, P(KVParams), i32, i32, i32, i32, C.c_float, vp, vp,
+                                         vp, vp, vp, vp, vp, vp, vp]),
         "kyro_philox_uniforms": (C.c_int, [vp, u64, u32, u32, u32, u32, i32, vp]),
         "kyro_selftest_exp": (C.c_int, [vp, vp]),
         "kyro_tp_unique_id": (C.c_int, [vp]),

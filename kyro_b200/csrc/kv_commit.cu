@@ -17,6 +17,8 @@
 // (the pool runs out inside the tile, or a released block is shared), the
 // tile is done by one thread in batch order, which is the reference's
 // semantics exactly.
+#include <cmath>
+
 #include "kyro_internal.cuh"
 
 namespace {
@@ -55,12 +57,20 @@ __device__ int block_exclusive_scan(int v, int* sh, int* total) {
   return sh[32 + warp] + inc - v;
 }
 
+// COW (copy-on-write): a sequence whose last block is partly filled and
+// shared (ref count > 1, a prefix held by the radix cache or another
+// request, block_manager.rs:60-63) gets a fresh block for it before its new
+// blocks; the shared block's ref count drops by one and the pair (shared,
+// fresh) goes to cow[b] for the copy kernel (-1, -1 when there is none).  A
+// tile with such a sequence takes the one-thread path, so that sequences
+// sharing one block see each other's decrements in batch order.
+template <bool COW>
 __global__ void __launch_bounds__(kTile)
 kv_reserve_kernel(int B, int bs, int max_blocks, int num_blocks, int num_new,
                   int64_t* __restrict__ block_table, const int64_t* __restrict__ context_lens,
                   const int32_t* __restrict__ free_stack, int32_t* __restrict__ free_top,
                   int32_t* __restrict__ ref_counts, int32_t* __restrict__ out_ok,
-                  uint32_t* status) {
+                  int32_t* __restrict__ cow, uint32_t* status) {
   __shared__ int sh[72];
   __shared__ int sh_top, sh_fast;
   kyro::dev::pdl_wait();
@@ -77,7 +87,7 @@ kv_reserve_kernel(int B, int bs, int max_blocks, int num_blocks, int num_new,
   for (int base = 0; base < B; base += kTile) {
     const int b = base + threadIdx.x;
     int64_t have = 0, need = 0;
-    bool fits_table = true;
+    bool fits_table = true, shared_last = false;
     if (b < B) {
       const int64_t len = context_lens[b];
       have = blocks_for(len, bs);
@@ -85,13 +95,19 @@ kv_reserve_kernel(int B, int bs, int max_blocks, int num_blocks, int num_new,
       need = want - have;
       fits_table = len >= 0 && want <= max_blocks;
       if (!fits_table) kyro::dev::flag(status, KYRO_DEV_BAD_LENGTH);
+      if constexpr (COW) {
+        if (fits_table && len % bs != 0) {
+          const int64_t old = block_table[(int64_t)b * max_blocks + have - 1];
+          shared_last = old >= 0 && old < num_blocks && ref_counts[old] > 1;
+        }
+      }
     }
     int total;
     const int off = block_exclusive_scan(fits_table ? (int)need : 0, sh, &total);
     const int top = sh_top;
     if (threadIdx.x == 0) sh_fast = 1;
     __syncthreads();
-    if (b < B && !fits_table) sh_fast = 0;
+    if (b < B && (!fits_table || shared_last)) sh_fast = 0;
     __syncthreads();
     const bool fast = sh_fast && total <= top;
     if (fast) {
@@ -106,6 +122,10 @@ kv_reserve_kernel(int B, int bs, int max_blocks, int num_blocks, int num_new,
           block_table[(int64_t)b * max_blocks + have + i] = blk;
         }
         if (out_ok) out_ok[b] = 1;
+        if constexpr (COW) {
+          cow[2 * b] = -1;
+          cow[2 * b + 1] = -1;
+        }
       }
       __syncthreads();
       if (threadIdx.x == 0) sh_top = top - total;
@@ -119,10 +139,33 @@ kv_reserve_kernel(int B, int bs, int max_blocks, int num_blocks, int num_new,
           const int64_t len = context_lens[bb];
           const int64_t h = blocks_for(len, bs);
           const int64_t w = blocks_for(len + num_new, bs);
-          const int64_t n = w - h;
-          if (len < 0 || w > max_blocks || n > t) {
+          int64_t n = w - h;
+          int64_t old = -1;
+          if constexpr (COW) {
+            cow[2 * bb] = -1;
+            cow[2 * bb + 1] = -1;
+            if (len >= 0 && w <= max_blocks && len % bs != 0) {
+              const int64_t o = block_table[(int64_t)bb * max_blocks + h - 1];
+              if (o >= 0 && o < num_blocks && ref_counts[o] > 1) old = o;
+            }
+          }
+          if (len < 0 || w > max_blocks || n + (old >= 0) > t) {
             if (out_ok) out_ok[bb] = 0;
             continue;
+          }
+          if constexpr (COW) {
+            if (old >= 0) {
+              const int32_t blk = free_stack[--t];
+              if (blk < 0 || blk >= num_blocks) {
+                kyro::dev::flag(status, KYRO_DEV_BAD_BLOCK);
+              } else {
+                ref_counts[blk] = 1;
+                ref_counts[old] -= 1;
+                block_table[(int64_t)bb * max_blocks + h - 1] = blk;
+                cow[2 * bb] = (int32_t)old;
+                cow[2 * bb + 1] = blk;
+              }
+            }
           }
           for (int64_t i = 0; i < n; ++i) {
             const int32_t blk = free_stack[--t];
@@ -308,6 +351,22 @@ kv_tree_move_kernel(CachePtrs caches, int nlayers, int num_nodes, int hkv, int d
   }
 }
 
+// grid (B, 2 * layers): the copy half of a copy-on-write reserve -- every
+// slot of the shared block cow[2b] into the fresh block cow[2b+1], in one
+// layer's K or V cache.
+__global__ void __launch_bounds__(256)
+kv_block_copy_kernel(CachePtrs caches, int nlayers, int hkv, int d, int bs, int num_blocks,
+                     const int32_t* __restrict__ cow) {
+  const int b = blockIdx.x, which = blockIdx.y;
+  const int32_t src = cow[2 * b], dst = cow[2 * b + 1];
+  if (src < 0 || dst < 0 || src >= num_blocks || dst >= num_blocks) return;
+  uint8_t* cache = caches.p[which < nlayers ? which : kMaxLayerPtrs + (which - nlayers)];
+  const int64_t n16 = (int64_t)hkv * bs * d * 2 / 16;
+  const uint4* s = reinterpret_cast<const uint4*>(cache) + (int64_t)src * n16;
+  uint4* t = reinterpret_cast<uint4*>(cache) + (int64_t)dst * n16;
+  for (int64_t i = threadIdx.x; i < n16; i += blockDim.x) t[i] = s[i];
+}
+
 // grid (B, num_new): one CTA copies the K and V rows of one new token.
 __global__ void __launch_bounds__(256)
 kv_write_kernel(int num_new, int hkv, int d, int bs, int max_blocks, int num_blocks,
@@ -338,6 +397,118 @@ kv_write_kernel(int num_new, int hkv, int d, int bs, int max_blocks, int num_blo
   }
 }
 
+// Rotary position embedding of the new tokens, fused with the paged K/V
+// store (LlamaAttention::forward, src/model/llama.rs:77-82, then append_kv).
+// RotaryEmbedding::apply (src/model/layers.rs:37-61) rotates the two halves
+// of every head: y[i] = x[i]*cos(f_i) - x[i+D/2]*sin(f_i) and y[i+D/2] =
+// x[i+D/2]*cos(f_i) + x[i]*sin(f_i), with f_i = pos * inv_freq[i] in fp32
+// and inv_freq[i] = (float)(1 / theta^(2i/D)) formed in double (:26-33).
+// Each product and the sum round to fp32 separately, as the reference's
+// broadcast_mul / add do; cos and sin are those of the fp32 angle, rounded
+// to fp32 (evaluated in double, so they are the correctly rounded values in
+// all but vanishingly rare cases).
+constexpr int kRopeMaxHalf = 128;  // head_dim <= 256
+
+struct RopeArgs {
+  int num_new, hq, hkv, d, bs, max_blocks, num_blocks;
+  float inv_freq[kRopeMaxHalf];
+};
+
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+__device__ __forceinline__ uint32_t bf16_pack(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// grid (B, num_new): one CTA rotates the query and key heads of one new
+// token, writes the queries to q_out and the rotated keys and the values to
+// the token's paged slot.
+__global__ void __launch_bounds__(256)
+rope_kv_write_kernel(RopeArgs a, const int32_t* __restrict__ pos_offsets,
+                     const uint4* q /* q_out may alias it */,
+                     const uint4* __restrict__ k_new, const uint4* __restrict__ v_new,
+                     const int64_t* __restrict__ block_table,
+                     const int64_t* __restrict__ context_lens, uint4* q_out, uint8_t* k_cache,
+                     uint8_t* v_cache, uint32_t* status) {
+  __shared__ float cs[kRopeMaxHalf], sn[kRopeMaxHalf];
+  const int b = blockIdx.x, j = blockIdx.y;
+  kyro::dev::pdl_wait();
+  kyro::dev::pdl_trigger();
+  const int64_t ctx = context_lens[b];
+  const int64_t pos = ctx + j;  // the cache slot
+  const int half = a.d / 2;
+  // the rotary position: (index + i) as f32 (layers.rs:45), index = the
+  // sequence's cached length, i = the token's offset (its depth in a tree)
+  const float pf = (float)(ctx + (pos_offsets ? pos_offsets[j] : j));
+  for (int i = threadIdx.x; i < half; i += blockDim.x) {
+    const float f = __fmul_rn(pf, a.inv_freq[i]);
+    double sd, cd;
+    sincos((double)f, &sd, &cd);
+    cs[i] = (float)cd;
+    sn[i] = (float)sd;
+  }
+  bool slot_ok = ctx >= 0 && pos / a.bs < a.max_blocks;
+  int64_t blk = -1;
+  if (slot_ok) {
+    blk = block_table[(int64_t)b * a.max_blocks + pos / a.bs];
+    if (blk < 0 || blk >= a.num_blocks) {
+      if (threadIdx.x == 0) kyro::dev::flag(status, KYRO_DEV_BAD_BLOCK);
+      slot_ok = false;
+    }
+  } else if (threadIdx.x == 0) {
+    kyro::dev::flag(status, KYRO_DEV_BAD_LENGTH);
+  }
+  __syncthreads();
+  const int hv = half / 8;         // 16-byte pieces per half row
+  const int row16 = a.d / 8;       // 16-byte pieces per row
+  const int64_t tok = (int64_t)b * a.num_new + j;
+  const int nrot = (a.hq + a.hkv) * hv;
+  for (int it = threadIdx.x; it < nrot; it += blockDim.x) {
+    const int h = it / hv, c = it - h * hv;
+    const bool is_q = h < a.hq;
+    if (!is_q && !slot_ok) continue;
+    const uint4* src = is_q ? q + (tok * a.hq + h) * row16
+                            : k_new + (tok * a.hkv + (h - a.hq)) * row16;
+    const uint4 x1 = src[c], x2 = src[hv + c];
+    const uint32_t w1[4] = {x1.x, x1.y, x1.z, x1.w};
+    const uint32_t w2[4] = {x2.x, x2.y, x2.z, x2.w};
+    uint32_t y1[4], y2[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int i0 = c * 8 + 2 * e;
+      const float a0 = bf16_lo(w1[e]), a1 = bf16_hi(w1[e]);
+      const float b0 = bf16_lo(w2[e]), b1 = bf16_hi(w2[e]);
+      const float c0 = cs[i0], c1 = cs[i0 + 1], s0 = sn[i0], s1 = sn[i0 + 1];
+      y1[e] = bf16_pack(__fadd_rn(__fmul_rn(a0, c0), __fmul_rn(-b0, s0)),
+                        __fadd_rn(__fmul_rn(a1, c1), __fmul_rn(-b1, s1)));
+      y2[e] = bf16_pack(__fadd_rn(__fmul_rn(b0, c0), __fmul_rn(a0, s0)),
+                        __fadd_rn(__fmul_rn(b1, c1), __fmul_rn(a1, s1)));
+    }
+    const uint4 o1 = make_uint4(y1[0], y1[1], y1[2], y1[3]);
+    const uint4 o2 = make_uint4(y2[0], y2[1], y2[2], y2[3]);
+    if (is_q) {
+      uint4* dst = q_out + (tok * a.hq + h) * row16;
+      dst[c] = o1;
+      dst[hv + c] = o2;
+    } else {
+      uint4* dst = reinterpret_cast<uint4*>(
+          k_cache + (((blk * a.hkv + (h - a.hq)) * a.bs + pos % a.bs) * a.d) * 2);
+      dst[c] = o1;
+      dst[hv + c] = o2;
+    }
+  }
+  if (!slot_ok) return;
+  for (int it = threadIdx.x; it < a.hkv * row16; it += blockDim.x) {
+    const int h = it / row16, c = it - h * row16;
+    uint4* dst = reinterpret_cast<uint4*>(
+        v_cache + (((blk * a.hkv + h) * a.bs + pos % a.bs) * a.d) * 2);
+    dst[c] = v_new[(tok * a.hkv + h) * row16 + c];
+  }
+}
+
 int check_kv(const kyro_kv_params* p, const char* fn) {
   KY_REQUIRE(p, "%s: params is NULL", fn);
   KY_REQUIRE(p->batch >= 0, "%s: batch = %d", fn, p->batch);
@@ -360,10 +531,11 @@ int kyro_kv_reserve(kyro_ctx* ctx, const kyro_kv_params* p, int32_t num_new,
   if (p->batch == 0) return KYRO_OK;
   KY_REQUIRE(block_table && context_lens && free_stack && free_top && ref_counts,
              "kyro_kv_reserve: a required pointer is NULL");
-  return kyro::launch_pdl(kv_reserve_kernel, dim3(1), dim3(kTile), 0, ctx->stream,
+  return kyro::launch_pdl(kv_reserve_kernel<false>, dim3(1), dim3(kTile), 0, ctx->stream,
                           "kv_reserve_kernel", p->batch, p->block_size, p->max_blocks_per_seq,
                           p->num_blocks, num_new, block_table, context_lens,
-                          (const int32_t*)free_stack, free_top, ref_counts, out_ok, ctx->d_status);
+                          (const int32_t*)free_stack, free_top, ref_counts, out_ok,
+                          (int32_t*)nullptr, ctx->d_status);
 }
 
 int kyro_kv_commit(kyro_ctx* ctx, const kyro_kv_params* p, int32_t num_new,
@@ -446,6 +618,89 @@ int kyro_kv_commit_tree(kyro_ctx* ctx, const kyro_kv_params* p, int32_t num_node
                                                  block_table, context_lens, free_stack, free_top,
                                                  ref_counts, ctx->d_status);
   return kyro::check_launch("kv_commit_kernel");
+}
+
+int kyro_rope_kv_write(kyro_ctx* ctx, const kyro_kv_params* p, int32_t num_new,
+                       int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
+                       float rope_theta, const int32_t* pos_offsets, const void* q,
+                       const void* k_new, const void* v_new, const int64_t* block_table,
+                       const int64_t* context_lens, void* q_out, void* k_cache, void* v_cache) {
+  KY_TRY(kyro::enter(ctx));
+  KY_TRY(check_kv(p, "kyro_rope_kv_write"));
+  KY_REQUIRE(num_new >= 0 && num_new <= 65535, "kyro_rope_kv_write: num_new = %d", num_new);
+  KY_REQUIRE(num_heads > 0 && num_kv_heads > 0 && num_heads % num_kv_heads == 0,
+             "kyro_rope_kv_write: num_heads %d num_kv_heads %d", num_heads, num_kv_heads);
+  KY_REQUIRE(head_dim > 0 && head_dim % 16 == 0 && head_dim / 2 <= kRopeMaxHalf,
+             "kyro_rope_kv_write: head_dim %d (a multiple of 16, at most %d)", head_dim,
+             2 * kRopeMaxHalf);
+  KY_REQUIRE(rope_theta > 0.0f, "kyro_rope_kv_write: rope_theta = %g", (double)rope_theta);
+  if (p->batch == 0 || num_new == 0) return KYRO_OK;
+  KY_REQUIRE(q && k_new && v_new && block_table && context_lens && q_out && k_cache && v_cache,
+             "kyro_rope_kv_write: a required pointer is NULL");
+  KY_REQUIRE((uintptr_t)q % 16 == 0 && (uintptr_t)k_new % 16 == 0 && (uintptr_t)v_new % 16 == 0 &&
+                 (uintptr_t)q_out % 16 == 0 && (uintptr_t)k_cache % 16 == 0 &&
+                 (uintptr_t)v_cache % 16 == 0,
+             "kyro_rope_kv_write: tensors must be 16-byte aligned");
+  RopeArgs a;
+  a.num_new = num_new;
+  a.hq = num_heads;
+  a.hkv = num_kv_heads;
+  a.d = head_dim;
+  a.bs = p->block_size;
+  a.max_blocks = p->max_blocks_per_seq;
+  a.num_blocks = p->num_blocks;
+  // RotaryEmbedding::new (layers.rs:26-33): 1 / theta^(2i/D) in double, then fp32
+  for (int i = 0; i < kRopeMaxHalf; ++i)
+    a.inv_freq[i] = i < head_dim / 2
+                        ? (float)(1.0 / std::pow((double)rope_theta, 2.0 * i / head_dim))
+                        : 0.0f;
+  dim3 grid((unsigned)p->batch, (unsigned)num_new);
+  return kyro::launch_pdl(rope_kv_write_kernel, grid, dim3(256), 0, ctx->stream,
+                          "rope_kv_write_kernel", a, pos_offsets, (const uint4*)q,
+                          (const uint4*)k_new, (const uint4*)v_new, block_table, context_lens,
+                          (uint4*)q_out, (uint8_t*)k_cache, (uint8_t*)v_cache, ctx->d_status);
+}
+
+int kyro_kv_reserve_cow(kyro_ctx* ctx, const kyro_kv_params* p, int32_t num_new,
+                        int32_t num_layers, void* const* k_caches, void* const* v_caches,
+                        int32_t num_kv_heads, int32_t head_dim, int64_t* block_table,
+                        const int64_t* context_lens, int32_t* free_stack, int32_t* free_top,
+                        int32_t* ref_counts, int32_t* out_ok, int32_t* out_cow) {
+  KY_TRY(kyro::enter(ctx));
+  KY_TRY(check_kv(p, "kyro_kv_reserve_cow"));
+  KY_REQUIRE(num_new >= 0, "kyro_kv_reserve_cow: num_new = %d", num_new);
+  KY_REQUIRE(num_layers >= 0, "kyro_kv_reserve_cow: num_layers = %d", num_layers);
+  KY_REQUIRE(num_kv_heads > 0 && head_dim > 0 && (head_dim * 2) % 16 == 0,
+             "kyro_kv_reserve_cow: num_kv_heads %d head_dim %d (head_dim*2 must be a multiple "
+             "of 16)",
+             num_kv_heads, head_dim);
+  if (p->batch == 0) return KYRO_OK;
+  KY_REQUIRE(block_table && context_lens && free_stack && free_top && ref_counts && out_cow,
+             "kyro_kv_reserve_cow: a required pointer is NULL");
+  KY_REQUIRE(num_layers == 0 || (k_caches && v_caches), "kyro_kv_reserve_cow: cache arrays NULL");
+  KY_REQUIRE(p->batch <= 2147483647 / 2, "kyro_kv_reserve_cow: batch too large");
+  for (int i = 0; i < num_layers; ++i)
+    KY_REQUIRE(k_caches[i] && v_caches[i] && (uintptr_t)k_caches[i] % 16 == 0 &&
+                   (uintptr_t)v_caches[i] % 16 == 0,
+               "kyro_kv_reserve_cow: layer %d cache pointer NULL or not 16-byte aligned", i);
+  KY_TRY(kyro::launch_pdl(kv_reserve_kernel<true>, dim3(1), dim3(kTile), 0, ctx->stream,
+                          "kv_reserve_kernel", p->batch, p->block_size, p->max_blocks_per_seq,
+                          p->num_blocks, num_new, block_table, context_lens,
+                          (const int32_t*)free_stack, free_top, ref_counts, out_ok, out_cow,
+                          ctx->d_status));
+  for (int l0 = 0; l0 < num_layers; l0 += kMaxLayerPtrs) {
+    const int nl = min(kMaxLayerPtrs, num_layers - l0);
+    CachePtrs cp = {};
+    for (int i = 0; i < nl; ++i) {
+      cp.p[i] = (uint8_t*)k_caches[l0 + i];
+      cp.p[kMaxLayerPtrs + i] = (uint8_t*)v_caches[l0 + i];
+    }
+    dim3 grid((unsigned)p->batch, (unsigned)(2 * nl));
+    kv_block_copy_kernel<<<grid, 256, 0, ctx->stream>>>(cp, nl, num_kv_heads, head_dim,
+                                                        p->block_size, p->num_blocks, out_cow);
+    KY_TRY(kyro::check_launch("kv_block_copy_kernel"));
+  }
+  return KYRO_OK;
 }
 
 }  // extern "C"

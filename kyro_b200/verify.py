@@ -341,6 +341,35 @@ def kv_commit_tree(ctx: Context, num_nodes: int, path: torch.Tensor, path_len: t
                                           _ptr(ref_counts)))
 
 
+def kv_reserve_cow(ctx: Context, num_new: int, k_caches: Sequence[torch.Tensor],
+                   v_caches: Sequence[torch.Tensor], block_table, context_lens, free_stack,
+                   free_top, ref_counts, block_size: int):
+    """kyro_kv_reserve_cow (in place): kv_reserve, except that a sequence whose
+    last block is partly filled and shared gets a private copy of it first
+    (every layer's K/V).  Returns (ok [B] int32, cow [B, 2] int32: the
+    (shared, fresh) block pair or -1)."""
+    _check_kv_state(ctx, block_table, context_lens, free_stack, free_top, ref_counts)
+    if len(k_caches) != len(v_caches):
+        raise ValueError("k_caches and v_caches differ in length")
+    for c in list(k_caches) + list(v_caches):
+        _need(c, "cache", torch.bfloat16, ctx.device, 4)
+    nl = len(k_caches)
+    kp = (C.c_void_p * max(nl, 1))(*[c.data_ptr() for c in k_caches])
+    vp = (C.c_void_p * max(nl, 1))(*[c.data_ptr() for c in v_caches])
+    hkv = k_caches[0].shape[1] if nl else 1
+    d = k_caches[0].shape[3] if nl else 8
+    B = block_table.shape[0]
+    ok = torch.empty(B, dtype=torch.int32, device=ctx.device)
+    cow = torch.empty(B, 2, dtype=torch.int32, device=ctx.device)
+    p = _kv_params(block_table, block_size, ref_counts.numel())
+    ctx.bind_stream()
+    check(_lib.load().kyro_kv_reserve_cow(ctx.handle, C.byref(p), num_new, nl,
+                                          C.cast(kp, C.c_void_p), C.cast(vp, C.c_void_p), hkv, d,
+                                          _ptr(block_table), _ptr(context_lens), _ptr(free_stack),
+                                          _ptr(free_top), _ptr(ref_counts), _ptr(ok), _ptr(cow)))
+    return ok, cow
+
+
 def kv_write(ctx: Context, k_new: torch.Tensor, v_new: torch.Tensor, block_table, context_lens,
              k_cache: torch.Tensor, v_cache: torch.Tensor, block_size: int):
     """kyro_kv_write: k_new / v_new bf16 [B, num_new, Hkv, D] into the paged
@@ -360,6 +389,46 @@ def kv_write(ctx: Context, k_new: torch.Tensor, v_new: torch.Tensor, block_table
     check(_lib.load().kyro_kv_write(ctx.handle, C.byref(p), n, hkv, d, _ptr(k_new), _ptr(v_new),
                                     _ptr(block_table), _ptr(context_lens), _ptr(k_cache),
                                     _ptr(v_cache)))
+
+
+def rope_kv_write(ctx: Context, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
+                  block_table, context_lens, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                  block_size: int, theta: float = 10000.0, pos_offsets=None,
+                  q_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """kyro_rope_kv_write: rotary embedding of q [B, n, Hq, D] and k_new
+    [B, n, Hkv, D] (bf16) at positions context_lens[b] + pos_offsets[j]
+    (default j), rotated keys and the values into the paged slots
+    context_lens[b] + j, rotated queries into q_out (default a new tensor;
+    q itself is allowed)."""
+    dev = ctx.device
+    _need(q, "q", torch.bfloat16, dev, 4)
+    _need(k_new, "k_new", torch.bfloat16, dev, 4)
+    _need(v_new, "v_new", torch.bfloat16, dev, 4)
+    _need(k_cache, "k_cache", torch.bfloat16, dev, 4)
+    _need(v_cache, "v_cache", torch.bfloat16, dev, 4)
+    _need(block_table, "block_table", torch.int64, dev, 2)
+    _need(context_lens, "context_lens", torch.int64, dev, 1)
+    B, n, hq, d = q.shape
+    hkv = k_new.shape[2]
+    if (tuple(k_new.shape) != (B, n, hkv, d) or tuple(v_new.shape) != (B, n, hkv, d)
+            or k_cache.shape[1] != hkv or k_cache.shape[3] != d):
+        raise ValueError("q / k_new / v_new / cache shapes disagree")
+    if q_out is None:
+        q_out = torch.empty_like(q)
+    _need(q_out, "q_out", torch.bfloat16, dev, 4)
+    if tuple(q_out.shape) != tuple(q.shape):
+        raise ValueError("q_out shape disagrees with q")
+    if pos_offsets is not None:
+        _need(pos_offsets, "pos_offsets", torch.int32, dev, 1)
+        if pos_offsets.numel() != n:
+            raise ValueError("pos_offsets needs one entry per new token")
+    p = _kv_params(block_table, block_size, k_cache.shape[0])
+    ctx.bind_stream()
+    check(_lib.load().kyro_rope_kv_write(
+        ctx.handle, C.byref(p), n, hq, hkv, d, float(theta),
+        None if pos_offsets is None else _ptr(pos_offsets), _ptr(q), _ptr(k_new), _ptr(v_new),
+        _ptr(block_table), _ptr(context_lens), _ptr(q_out), _ptr(k_cache), _ptr(v_cache)))
+    return q_out
 
 
 def philox_uniforms(ctx: Context, seed: int, seq: int, pos0: int, stream: int, step: int,

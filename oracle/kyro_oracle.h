@@ -106,6 +106,12 @@ void ko_kv_reserve(int32_t batch, int32_t bs, int32_t max_blocks, int32_t num_bl
                    int32_t num_new, int64_t* block_table, const int64_t* context_lens,
                    int32_t* free_stack, int32_t* free_top, int32_t* ref_counts,
                    int32_t* out_ok);
+/* kv_reserve with copy-on-write of a shared, partly filled last block */
+void ko_kv_reserve_cow(int32_t batch, int32_t bs, int32_t max_blocks, int32_t num_blocks,
+                       int32_t num_new, int32_t num_layers, uint16_t* const* k_caches,
+                       uint16_t* const* v_caches, int32_t hkv, int32_t d, int64_t* block_table,
+                       const int64_t* context_lens, int32_t* free_stack, int32_t* free_top,
+                       int32_t* ref_counts, int32_t* out_ok, int32_t* cow);
 void ko_kv_commit(int32_t batch, int32_t bs, int32_t max_blocks, int32_t num_blocks,
                   int32_t num_new, const int32_t* accept_len, int64_t* block_table,
                   int64_t* context_lens, int32_t* free_stack, int32_t* free_top,
@@ -114,6 +120,13 @@ void ko_kv_write(int32_t batch, int32_t bs, int32_t max_blocks, int32_t num_bloc
                  int32_t num_new, int32_t hkv, int32_t d, const uint16_t* k_new,
                  const uint16_t* v_new, const int64_t* block_table, const int64_t* context_lens,
                  uint16_t* k_cache, uint16_t* v_cache);
+/* rotary position embedding (layers.rs:37-61) + paged K/V store */
+void ko_rope_kv_write(int32_t batch, int32_t bs, int32_t max_blocks, int32_t num_blocks,
+                      int32_t num_new, int32_t hq, int32_t hkv, int32_t d, float theta,
+                      const int32_t* pos_offsets, const uint16_t* q, const uint16_t* k_new,
+                      const uint16_t* v_new, const int64_t* block_table,
+                      const int64_t* context_lens, uint16_t* q_out, uint16_t* k_cache,
+                      uint16_t* v_cache);
 void ko_kv_commit_tree(int32_t batch, int32_t bs, int32_t max_blocks, int32_t num_blocks,
                        int32_t num_nodes, const int32_t* path, const int32_t* path_len,
                        int32_t num_layers, uint16_t* const* k_caches, uint16_t* const* v_caches,

@@ -70,8 +70,12 @@ def _declare(L):
     L.ko_paged_attention.argtypes = [i32, i32, i32, i32, i32, i32, i32, f32, vp, vp, vp, vp, vp,
                                      vp, vp, i32]
     L.ko_kv_reserve.argtypes = [i32, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp]
+    L.ko_kv_reserve_cow.argtypes = [i32, i32, i32, i32, i32, i32, vp, vp, i32, i32, vp, vp, vp,
+                                    vp, vp, vp, vp]
     L.ko_kv_commit.argtypes = [i32, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp]
     L.ko_kv_write.argtypes = [i32, i32, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp]
+    L.ko_rope_kv_write.argtypes = [i32, i32, i32, i32, i32, i32, i32, i32, f32, vp, vp, vp, vp,
+                                   vp, vp, vp, vp, vp]
     L.ko_kv_commit_tree.argtypes = [i32, i32, i32, i32, i32, vp, vp, i32, vp, vp, i32, i32, vp,
                                     vp, vp, vp, vp]
 
@@ -214,6 +218,25 @@ def kv_reserve(num_new, block_table, context_lens, free_stack, free_top, ref_cou
     return ok
 
 
+def kv_reserve_cow(num_new, k_caches, v_caches, block_table, context_lens, free_stack,
+                   free_top, ref_counts, block_size):
+    """kv_reserve with copy-on-write of shared, partly filled last blocks; in
+    place on numpy arrays and the uint16 caches [NB,Hkv,bs,D] of every layer.
+    Returns (ok [B], cow [B, 2])."""
+    B, maxb = block_table.shape
+    ok = np.empty(B, dtype=np.int32)
+    cow = np.empty((B, 2), dtype=np.int32)
+    L = len(k_caches)
+    kp = (C.c_void_p * max(L, 1))(*[c.ctypes.data for c in k_caches])
+    vp = (C.c_void_p * max(L, 1))(*[c.ctypes.data for c in v_caches])
+    hkv, d = (k_caches[0].shape[1], k_caches[0].shape[3]) if L else (1, 8)
+    lib().ko_kv_reserve_cow(B, block_size, maxb, ref_counts.size, num_new, L,
+                            C.cast(kp, C.c_void_p), C.cast(vp, C.c_void_p), hkv, d,
+                            _p(block_table), _p(context_lens), _p(free_stack), _p(free_top),
+                            _p(ref_counts), _p(ok), _p(cow))
+    return ok, cow
+
+
 def kv_commit(num_new, accept_len, block_table, context_lens, free_stack, free_top, ref_counts,
               block_size):
     B, maxb = block_table.shape
@@ -246,3 +269,23 @@ def kv_write(k_new, v_new, block_table, context_lens, k_cache, v_cache, block_si
     lib().ko_kv_write(B, block_size, block_table.shape[1], k_cache.shape[0], n, hkv, d, _p(kn),
                       _p(vn), _p(np.ascontiguousarray(block_table)),
                       _p(np.ascontiguousarray(context_lens)), _p(k_cache), _p(v_cache))
+
+
+def rope_kv_write(q, k_new, v_new, block_table, context_lens, k_cache, v_cache, block_size,
+                  theta=10000.0, pos_offsets=None):
+    """Rotary embedding of q and k (layers.rs:37-61) + paged K/V store.
+    q uint16 [B, n, Hq, D], k_new / v_new uint16 [B, n, Hkv, D]; returns the
+    rotated q; the caches are modified in place."""
+    B, n, hq, d = q.shape
+    hkv = k_new.shape[2]
+    qq = np.ascontiguousarray(q, dtype=np.uint16)
+    kn = np.ascontiguousarray(k_new, dtype=np.uint16)
+    vn = np.ascontiguousarray(v_new, dtype=np.uint16)
+    q_out = np.empty_like(qq)
+    po = None if pos_offsets is None else np.ascontiguousarray(pos_offsets, dtype=np.int32)
+    lib().ko_rope_kv_write(B, block_size, block_table.shape[1], k_cache.shape[0], n, hq, hkv, d,
+                           float(theta), None if po is None else _p(po), _p(qq), _p(kn), _p(vn),
+                           _p(np.ascontiguousarray(block_table)),
+                           _p(np.ascontiguousarray(context_lens)), _p(q_out), _p(k_cache),
+                           _p(v_cache))
+    return q_out

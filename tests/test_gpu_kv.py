@@ -155,3 +155,100 @@ def test_kv_write_matches_oracle(ctx, oracle):
     oracle.kv_write(bf16_bits(kn), bf16_bits(vn), dev["block_table"].cpu().numpy(),
                     dev["context_lens"].cpu().numpy(), hk, hv, bs)
     assert np.array_equal(bf16_bits(kc), hk) and np.array_equal(bf16_bits(vc), hv)
+
+
+@pytest.mark.parametrize("theta,tree,inplace", [(10000.0, False, False), (500000.0, True, True)])
+def test_rope_kv_write_matches_oracle(ctx, oracle, theta, tree, inplace):
+    """Rotary embedding of the new tokens' q and k (layers.rs:37-61) fused with
+    the paged store: q_out and both caches bit-identical to the oracle."""
+    from kyro_b200.verify import kv_reserve, rope_kv_write
+    from kyro_b200.workloads import bf16_bits
+    rng = np.random.default_rng(5)
+    B, NB, bs, hq, hkv, d, n = 9, 1024, 16, 32, 8, 128, 6
+    lens = rng.integers(0, 700, B)
+    dev = _device_state(rng, NB, B, 64, bs, lens, ctx.device)
+    kv_reserve(ctx, n, dev["block_table"], dev["context_lens"], dev["free_stack"],
+               dev["free_top"], dev["ref_counts"], bs)
+    kc = torch.randn(NB, hkv, bs, d, device=ctx.device).to(torch.bfloat16)
+    vc = torch.randn(NB, hkv, bs, d, device=ctx.device).to(torch.bfloat16)
+    q = (torch.randn(B, n, hq, d, device=ctx.device) * 3).to(torch.bfloat16)
+    kn = torch.randn(B, n, hkv, d, device=ctx.device).to(torch.bfloat16)
+    vn = torch.randn(B, n, hkv, d, device=ctx.device).to(torch.bfloat16)
+    offs = np.array([0, 1, 1, 2, 2, 3], np.int32) if tree else None
+    hq_bits, hk, hv = bf16_bits(q), bf16_bits(kc), bf16_bits(vc)
+    want_q = oracle.rope_kv_write(hq_bits, bf16_bits(kn), bf16_bits(vn),
+                                  dev["block_table"].cpu().numpy(),
+                                  dev["context_lens"].cpu().numpy(), hk, hv, bs, theta=theta,
+                                  pos_offsets=offs)
+    po = None if offs is None else torch.from_numpy(offs).to(ctx.device)
+    out = rope_kv_write(ctx, q, kn, vn, dev["block_table"], dev["context_lens"], kc, vc, bs,
+                        theta=theta, pos_offsets=po, q_out=q if inplace else None)
+    assert ctx.device_status() == 0
+    assert np.array_equal(bf16_bits(out), want_q)
+    assert np.array_equal(bf16_bits(kc), hk) and np.array_equal(bf16_bits(vc), hv)
+
+
+def test_rope_kv_write_position_zero_is_identity(ctx):
+    """At position 0 (empty context, first token) the rotation is the identity
+    (the reference's RotaryEmbedding test applies it at index 0)."""
+    from kyro_b200.verify import rope_kv_write
+    bs, NB, hq, hkv, d = 16, 8, 4, 4, 64
+    table = torch.tensor([[0, 1]], dtype=torch.int64, device=ctx.device)
+    lens = torch.zeros(1, dtype=torch.int64, device=ctx.device)
+    x = torch.randn(1, 1, hq, d, device=ctx.device).to(torch.bfloat16)
+    kc = torch.zeros(NB, hkv, bs, d, device=ctx.device, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    out = rope_kv_write(ctx, x, x, x, table, lens, kc, vc, bs)
+    assert torch.equal(out, x) and torch.equal(kc[0, :, 0], x[0, 0]) and torch.equal(vc[0, :, 0], x[0, 0])
+
+
+@pytest.mark.parametrize("B,NB,free_left", [(40, 2048, None), (1500, 60000, None), (40, 2048, 9)])
+def test_reserve_cow_matches_oracle(ctx, oracle, B, NB, free_left):
+    """Copy-on-write reserve against the oracle: groups of sequences share
+    prefix blocks (ref count = holders), some ending in a partly filled
+    block; tables, ref counts, free list, ok / cow pairs and both layers'
+    caches must match exactly (one-thread tiles where a shared tail occurs,
+    parallel tiles elsewhere, and a pool that runs dry)."""
+    from kyro_b200.verify import kv_reserve_cow
+    rng = np.random.default_rng(21)
+    bs, maxb, hkv, d, n_new, layers = 16, 48, 2, 64, 6, 2
+    free = rng.permutation(NB).astype(np.int32)
+    top = NB
+    table = np.full((B, maxb), -1, np.int64)
+    refs = np.zeros(NB, np.int32)
+    lens = np.zeros(B, np.int64)
+    b = 0
+    while b < B:
+        # a group of 1..3 holders of one prefix; only some groups start in the first tile
+        g = int(rng.integers(1, 4)) if (b < 1024 or B < 1024 or rng.random() < 0.02) else 1
+        g = min(g, B - b)
+        plen = int(rng.integers(1, 300))
+        nblk = -(-plen // bs)
+        blks = [free[top - 1 - i] for i in range(nblk)]
+        top -= nblk
+        for m in range(g):
+            table[b + m, :nblk] = blks
+            lens[b + m] = plen
+        refs[blks] += g
+        b += g
+    if free_left is not None:
+        top = free_left
+    st = {"block_table": table, "context_lens": lens, "free_stack": free,
+          "free_top": np.array([top], np.int32), "ref_counts": refs}
+    dev = {k: torch.from_numpy(v.copy()).to(ctx.device) for k, v in st.items()}
+    host = {k: v.copy() for k, v in st.items()}
+    kc = [torch.randn(NB, hkv, bs, d, device=ctx.device).to(torch.bfloat16) for _ in range(layers)]
+    vc = [torch.randn(NB, hkv, bs, d, device=ctx.device).to(torch.bfloat16) for _ in range(layers)]
+    from kyro_b200.workloads import bf16_bits
+    hk = [bf16_bits(t) for t in kc]
+    hv = [bf16_bits(t) for t in vc]
+    ok, cow = kv_reserve_cow(ctx, n_new, kc, vc, dev["block_table"], dev["context_lens"],
+                             dev["free_stack"], dev["free_top"], dev["ref_counts"], bs)
+    hok, hcow = oracle.kv_reserve_cow(n_new, hk, hv, host["block_table"], host["context_lens"],
+                                      host["free_stack"], host["free_top"], host["ref_counts"], bs)
+    assert ctx.device_status() == 0
+    assert (hcow[:, 0] >= 0).any()  # the case exercises copy-on-write
+    assert np.array_equal(ok.cpu().numpy(), hok) and np.array_equal(cow.cpu().numpy(), hcow)
+    _assert_same(dev, host)
+    for t, h in zip(kc + vc, hk + hv):
+        assert np.array_equal(bf16_bits(t), h)

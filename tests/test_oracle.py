@@ -377,3 +377,133 @@ def test_tree_commit_moves_path_rows(oracle):
     # blocks wholly beyond the kept length went back to the free list
     released = sum((bt0[b] >= 0).sum() - (bt[b] >= 0).sum() for b in range(B))
     assert top[0] == top0 + released
+
+
+def _bf16_to_f32(bits):
+    return (np.asarray(bits, np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def _f32_to_bf16(x):
+    u = np.asarray(x, np.float32).view(np.uint32).astype(np.uint64)
+    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+def _rope_state(rng, B, n, hq, hkv, d, bs, NB):
+    maxb = 64
+    lens = rng.integers(0, 700, B).astype(np.int64)
+    table = np.full((B, maxb), -1, np.int64)
+    perm = rng.permutation(NB)
+    k = 0
+    for b in range(B):
+        for i in range(-(-(int(lens[b]) + n) // bs)):
+            table[b, i] = perm[k]
+            k += 1
+    bits = lambda *s: _f32_to_bf16(rng.standard_normal(s).astype(np.float32))
+    return lens, table, bits(B, n, hq, d), bits(B, n, hkv, d), bits(B, n, hkv, d), maxb
+
+
+def test_rope_reference_known_answer(oracle):
+    """layers.rs:82-89 applies RotaryEmbedding (dim 64) to ones at index 0:
+    at position 0 cos = 1 and sin = 0, so the rotation returns its input."""
+    B, n, hq, hkv, d, bs, NB = 1, 1, 4, 4, 64, 16, 4
+    ones = np.full((B, n, hq, d), 0x3F80, np.uint16)  # bf16 1.0
+    table = np.array([[0, 1, 2, 3]], np.int64)
+    kc = np.zeros((NB, hkv, bs, d), np.uint16)
+    vc = np.zeros_like(kc)
+    q_out = oracle.rope_kv_write(ones, ones, ones, table, np.zeros(1, np.int64), kc, vc, bs)
+    assert q_out.shape == ones.shape and np.array_equal(q_out, ones)
+    assert np.array_equal(kc[0, :, 0, :], ones[0, 0]) and np.array_equal(vc[0, :, 0, :], ones[0, 0])
+
+
+@pytest.mark.parametrize("theta,offsets", [(10000.0, None), (500000.0, None), (10000.0, "tree")])
+def test_rope_oracle_vs_float64(oracle, theta, offsets):
+    """The oracle's rotation (fp32 products and sums, bf16 out) against a
+    float64 evaluation of RotaryEmbedding::apply (layers.rs:37-61) at the
+    same fp32 angles: within one bf16 rounding step; the paged slots hold
+    the rotated keys and the unchanged values."""
+    rng = np.random.default_rng(11)
+    B, n, hq, hkv, d, bs, NB = 5, 6, 8, 2, 128, 16, 400
+    lens, table, q, k, v, maxb = _rope_state(rng, B, n, hq, hkv, d, bs, NB)
+    po = None if offsets is None else np.array([0, 1, 1, 2, 2, 2], np.int32)
+    kc = np.zeros((NB, hkv, bs, d), np.uint16)
+    vc = np.zeros_like(kc)
+    q_out = oracle.rope_kv_write(q, k, v, table, lens, kc, vc, bs, theta=theta, pos_offsets=po)
+    half = d // 2
+    inv = (1.0 / np.power(np.float64(theta), 2.0 * np.arange(half) / d)).astype(np.float32)
+
+    def rot(x_bits, b, j):
+        off = j if po is None else int(po[j])
+        ang = (np.float32(lens[b] + off) * inv).astype(np.float64)  # fp32 product
+        c, s = np.cos(ang), np.sin(ang)
+        x = _bf16_to_f32(x_bits).astype(np.float64)
+        x1, x2 = x[..., :half], x[..., half:]
+        return np.concatenate([x1 * c - x2 * s, x2 * c + x1 * s], axis=-1)
+
+    for b in range(B):
+        for j in range(n):
+            want = rot(q[b, j], b, j)
+            got = _bf16_to_f32(q_out[b, j]).astype(np.float64)
+            assert np.all(np.abs(got - want) <= 2.0 ** -7 * np.abs(want) + 1e-6)
+            pos = lens[b] + j
+            blk = table[b, pos // bs]
+            wk = rot(k[b, j], b, j)
+            gk = _bf16_to_f32(kc[blk, :, pos % bs, :]).astype(np.float64)
+            assert np.all(np.abs(gk - wk) <= 2.0 ** -7 * np.abs(wk) + 1e-6)
+            assert np.array_equal(vc[blk, :, pos % bs, :], v[b, j])
+
+
+def _shared_prefix_pool(rng, n, maxb, bs, hkv, d, layers):
+    """Four sequences: 0 and 1 hold the same prefix blocks (ref 2, the last
+    one partly filled), 2 shares only full blocks with them, 3 is private."""
+    bt, cl, fs, top, rc = _fresh_pool(n, 4, maxb)
+    fs[:] = rng.permutation(n).astype(np.int32)
+    _prefill(bt, cl, fs, top, rc, bs, [10, 0, 0, 7])
+    bt[1, :3] = bt[0, :3]
+    cl[1] = 10
+    bt[2, :2] = bt[0, :2]
+    cl[2] = 8
+    rc[bt[0, :3]] += 1
+    rc[bt[0, :2]] += 1
+    kc = [rng.integers(0, 65535, (n, hkv, bs, d), dtype=np.uint16) for _ in range(layers)]
+    vc = [rng.integers(0, 65535, (n, hkv, bs, d), dtype=np.uint16) for _ in range(layers)]
+    return bt, cl, fs, top, rc, kc, vc
+
+
+def test_reserve_cow_copies_shared_tail_block(oracle):
+    """Copy-on-write at a shared, partly filled last block (prefix sharing,
+    block_manager.rs:60-63): sequence 0 gets a private copy (the shared
+    block's ref drops to 1), so sequence 1 -- now its only holder -- keeps
+    it; full shared blocks and private tails are left alone."""
+    rng = np.random.default_rng(12)
+    n, maxb, bs, hkv, d = 64, 16, 4, 2, 8
+    bt, cl, fs, top, rc, kc, vc = _shared_prefix_pool(rng, n, maxb, bs, hkv, d, 2)
+    shared = int(bt[0, 2])
+    before = [(k.copy(), v.copy()) for k, v in zip(kc, vc)]
+    held0 = set(bt[bt >= 0].tolist())
+    top0 = int(top[0])
+    ok, cow = oracle.kv_reserve_cow(3, kc, vc, bt, cl, fs, top, rc, bs)
+    assert ok.tolist() == [1, 1, 1, 1]
+    fresh = int(fs[top0 - 1])  # the COW block is popped first
+    assert cow.tolist() == [[shared, fresh], [-1, -1], [-1, -1], [-1, -1]]
+    assert bt[0, 2] == fresh and bt[1, 2] == shared and rc[shared] == 1 and rc[fresh] == 1
+    for (k0, v0), k1, v1 in zip(before, kc, vc):
+        assert np.array_equal(k1[fresh], k0[shared]) and np.array_equal(v1[fresh], v0[shared])
+        assert np.array_equal(k1[shared], k0[shared])
+    # every block is held once per reference: the table's multiset matches ref counts
+    held = bt[bt >= 0]
+    counts = np.bincount(held, minlength=n)
+    assert (counts[held] == rc[held]).all()
+    assert len(set(held.tolist()) - held0) + int(top[0]) == top0
+
+
+def test_reserve_cow_out_of_blocks(oracle):
+    """A sequence that cannot get its COW block and its new blocks gets
+    nothing, and the shared block keeps its ref count."""
+    rng = np.random.default_rng(13)
+    n, maxb, bs, hkv, d = 64, 16, 4, 2, 8
+    bt, cl, fs, top, rc, kc, vc = _shared_prefix_pool(rng, n, maxb, bs, hkv, d, 1)
+    shared = int(bt[0, 2])
+    top[0] = 1  # one free block: sequences 0 and 1 need two each (COW + one new)
+    ok, cow = oracle.kv_reserve_cow(3, kc, vc, bt, cl, fs, top, rc, bs)
+    assert ok.tolist() == [0, 0, 1, 0] and (cow == -1).all()
+    assert rc[shared] == 2 and bt[0, 2] == shared and bt[1, 2] == shared and top[0] == 0
