@@ -210,8 +210,8 @@ def run_ours(args):
     import torch.distributed as dist
 
     from kyro_b200 import _lib
-    from kyro_b200.verify import (Context, kv_commit, kv_reserve, kv_write, sample_tokens,
-                                  spec_accept, verify_attention)
+    from kyro_b200.verify import (Context, kv_commit, kv_reserve, kv_write, rope_kv_write,
+                                  sample_tokens, spec_accept, verify_attention)
     from kyro_b200.workloads import CONFIG1, accept_inputs, chain_bytes_per_step, paged_state
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -335,7 +335,25 @@ def run_ours(args):
     with torch.cuda.stream(side):
         for i in range(PER_KERNEL_STEPS):
             step(args.warmup + args.steps + i, True)
+        # the fused rotary embedding + paged K/V store on the step's new tokens
+        # (kyro_rope_kv_write, the alternative to kv_write for un-rotated
+        # projections), timed back to back: its ~9 MB stay in L2
+        restore()
+        kv_reserve(ctx, nq, st.block_table, st.context_lens, st.free_stack, st.free_top,
+                   st.ref_counts, cfg.block_size, out_ok=ok)
+        q_rot = torch.empty_like(st.q)
+        for _ in range(3):
+            rope_kv_write(ctx, st.q, k_new, v_new, st.block_table, st.context_lens, st.k_cache,
+                          st.v_cache, cfg.block_size, q_out=q_rot)
+        r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        r0.record()
+        for _ in range(20):
+            rope_kv_write(ctx, st.q, k_new, v_new, st.block_table, st.context_lens, st.k_cache,
+                          st.v_cache, cfg.block_size, q_out=q_rot)
+        r1.record()
     torch.cuda.synchronize()
+    rope_us = r0.elapsed_time(r1) / 20 * 1e3
+    rope_bytes = 2.0 * q_rot.numel() * 2 + 4.0 * k_new.numel() * 2
     del graph
     ctx.bind_stream()  # back to the default stream for the end-to-end run
     if world > 1:
@@ -383,6 +401,9 @@ def run_ours(args):
                        "GBps": acc_bytes / (acc_ms * 1e-3) / 1e9,
                        "frac": acc_bytes / (acc_ms * 1e-3) / 1e9 / peak},
             "step_frac_of_hbm": step_bytes / (ms / args.steps * 1e-3) / 1e9 / peak,
+            "rope_kv_write": {"us": rope_us, "bytes": rope_bytes,
+                              "GBps": rope_bytes / (rope_us * 1e-6) / 1e9,
+                              "note": "outside the step; back-to-back launches, L2-resident"},
         },
         "timing": "CUDA graph replays of the step" if not args.no_graph else "stream launches",
         "acceptance_rate": float(acc.float().mean().item() / cfg.k),

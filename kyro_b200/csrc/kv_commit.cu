@@ -408,6 +408,8 @@ kv_write_kernel(int num_new, int hkv, int d, int bs, int max_blocks, int num_blo
 // to fp32 (evaluated in double, so they are the correctly rounded values in
 // all but vanishingly rare cases).
 constexpr int kRopeMaxHalf = 128;  // head_dim <= 256
+constexpr int kRopeThreads = 256;
+constexpr int kRopePrefetch = 2;   // rotation pieces per thread loaded before the angles
 
 struct RopeArgs {
   int num_new, hq, hkv, d, bs, max_blocks, num_blocks;
@@ -426,7 +428,7 @@ __device__ __forceinline__ uint32_t bf16_pack(float lo, float hi) {
 // grid (B, num_new): one CTA rotates the query and key heads of one new
 // token, writes the queries to q_out and the rotated keys and the values to
 // the token's paged slot.
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(kRopeThreads)
 rope_kv_write_kernel(RopeArgs a, const int32_t* __restrict__ pos_offsets,
                      const uint4* q /* q_out may alias it */,
                      const uint4* __restrict__ k_new, const uint4* __restrict__ v_new,
@@ -437,44 +439,65 @@ rope_kv_write_kernel(RopeArgs a, const int32_t* __restrict__ pos_offsets,
   const int b = blockIdx.x, j = blockIdx.y;
   kyro::dev::pdl_wait();
   kyro::dev::pdl_trigger();
+  const int half = a.d / 2;
+  const int hv = half / 8;    // 16-byte pieces per half row
+  const int row16 = a.d / 8;  // 16-byte pieces per row
+  const int64_t tok = (int64_t)b * a.num_new + j;
+  const int nrot = (a.hq + a.hkv) * hv;
+  const int nv = a.hkv * row16;
+  // the inputs do not depend on the position: their loads go out first, and
+  // the angles are computed while they are in flight
+  uint4 x1[kRopePrefetch], x2[kRopePrefetch], xv;
+#pragma unroll
+  for (int u = 0; u < kRopePrefetch; ++u) {
+    const int it = threadIdx.x + u * blockDim.x;
+    if (it < nrot) {
+      const int h = it / hv, c = it - h * hv;
+      const uint4* src = h < a.hq ? q + (tok * a.hq + h) * row16
+                                  : k_new + (tok * a.hkv + (h - a.hq)) * row16;
+      x1[u] = src[c];
+      x2[u] = src[hv + c];
+    }
+  }
+  if (threadIdx.x < nv) xv = v_new[tok * nv + threadIdx.x];
   const int64_t ctx = context_lens[b];
   const int64_t pos = ctx + j;  // the cache slot
-  const int half = a.d / 2;
   // the rotary position: (index + i) as f32 (layers.rs:45), index = the
   // sequence's cached length, i = the token's offset (its depth in a tree)
   const float pf = (float)(ctx + (pos_offsets ? pos_offsets[j] : j));
+  bool slot_ok = ctx >= 0 && pos / a.bs < a.max_blocks;
+  int64_t blk = -1;
+  if (slot_ok) blk = block_table[(int64_t)b * a.max_blocks + pos / a.bs];
   for (int i = threadIdx.x; i < half; i += blockDim.x) {
-    const float f = __fmul_rn(pf, a.inv_freq[i]);
     double sd, cd;
-    sincos((double)f, &sd, &cd);
+    sincos((double)__fmul_rn(pf, a.inv_freq[i]), &sd, &cd);
     cs[i] = (float)cd;
     sn[i] = (float)sd;
   }
-  bool slot_ok = ctx >= 0 && pos / a.bs < a.max_blocks;
-  int64_t blk = -1;
-  if (slot_ok) {
-    blk = block_table[(int64_t)b * a.max_blocks + pos / a.bs];
-    if (blk < 0 || blk >= a.num_blocks) {
-      if (threadIdx.x == 0) kyro::dev::flag(status, KYRO_DEV_BAD_BLOCK);
-      slot_ok = false;
-    }
-  } else if (threadIdx.x == 0) {
+  if (slot_ok && (blk < 0 || blk >= a.num_blocks)) {
+    if (threadIdx.x == 0) kyro::dev::flag(status, KYRO_DEV_BAD_BLOCK);
+    slot_ok = false;
+  } else if (!slot_ok && threadIdx.x == 0) {
     kyro::dev::flag(status, KYRO_DEV_BAD_LENGTH);
   }
   __syncthreads();
-  const int hv = half / 8;         // 16-byte pieces per half row
-  const int row16 = a.d / 8;       // 16-byte pieces per row
-  const int64_t tok = (int64_t)b * a.num_new + j;
-  const int nrot = (a.hq + a.hkv) * hv;
-  for (int it = threadIdx.x; it < nrot; it += blockDim.x) {
+  for (int it = threadIdx.x, u = 0; it < nrot; it += blockDim.x, ++u) {
     const int h = it / hv, c = it - h * hv;
     const bool is_q = h < a.hq;
     if (!is_q && !slot_ok) continue;
-    const uint4* src = is_q ? q + (tok * a.hq + h) * row16
-                            : k_new + (tok * a.hkv + (h - a.hq)) * row16;
-    const uint4 x1 = src[c], x2 = src[hv + c];
-    const uint32_t w1[4] = {x1.x, x1.y, x1.z, x1.w};
-    const uint32_t w2[4] = {x2.x, x2.y, x2.z, x2.w};
+    uint4 v1, v2;
+    if (u < kRopePrefetch) {
+      // static register indexing: u is 0 or 1 here
+      v1 = u == 0 ? x1[0] : x1[kRopePrefetch - 1];
+      v2 = u == 0 ? x2[0] : x2[kRopePrefetch - 1];
+    } else {
+      const uint4* src = is_q ? q + (tok * a.hq + h) * row16
+                              : k_new + (tok * a.hkv + (h - a.hq)) * row16;
+      v1 = src[c];
+      v2 = src[hv + c];
+    }
+    const uint32_t w1[4] = {v1.x, v1.y, v1.z, v1.w};
+    const uint32_t w2[4] = {v2.x, v2.y, v2.z, v2.w};
     uint32_t y1[4], y2[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
@@ -489,23 +512,18 @@ rope_kv_write_kernel(RopeArgs a, const int32_t* __restrict__ pos_offsets,
     }
     const uint4 o1 = make_uint4(y1[0], y1[1], y1[2], y1[3]);
     const uint4 o2 = make_uint4(y2[0], y2[1], y2[2], y2[3]);
-    if (is_q) {
-      uint4* dst = q_out + (tok * a.hq + h) * row16;
-      dst[c] = o1;
-      dst[hv + c] = o2;
-    } else {
-      uint4* dst = reinterpret_cast<uint4*>(
-          k_cache + (((blk * a.hkv + (h - a.hq)) * a.bs + pos % a.bs) * a.d) * 2);
-      dst[c] = o1;
-      dst[hv + c] = o2;
-    }
+    uint4* dst = is_q ? q_out + (tok * a.hq + h) * row16
+                      : reinterpret_cast<uint4*>(
+                            k_cache + (((blk * a.hkv + (h - a.hq)) * a.bs + pos % a.bs) * a.d) * 2);
+    dst[c] = o1;
+    dst[hv + c] = o2;
   }
   if (!slot_ok) return;
-  for (int it = threadIdx.x; it < a.hkv * row16; it += blockDim.x) {
+  for (int it = threadIdx.x; it < nv; it += blockDim.x) {
     const int h = it / row16, c = it - h * row16;
     uint4* dst = reinterpret_cast<uint4*>(
         v_cache + (((blk * a.hkv + h) * a.bs + pos % a.bs) * a.d) * 2);
-    dst[c] = v_new[(tok * a.hkv + h) * row16 + c];
+    dst[c] = it == threadIdx.x ? xv : v_new[tok * nv + it];
   }
 }
 
@@ -655,7 +673,7 @@ int kyro_rope_kv_write(kyro_ctx* ctx, const kyro_kv_params* p, int32_t num_new,
                         ? (float)(1.0 / std::pow((double)rope_theta, 2.0 * i / head_dim))
                         : 0.0f;
   dim3 grid((unsigned)p->batch, (unsigned)num_new);
-  return kyro::launch_pdl(rope_kv_write_kernel, grid, dim3(256), 0, ctx->stream,
+  return kyro::launch_pdl(rope_kv_write_kernel, grid, dim3(kRopeThreads), 0, ctx->stream,
                           "rope_kv_write_kernel", a, pos_offsets, (const uint4*)q,
                           (const uint4*)k_new, (const uint4*)v_new, block_table, context_lens,
                           (uint4*)q_out, (uint8_t*)k_cache, (uint8_t*)v_cache, ctx->d_status);
