@@ -374,8 +374,15 @@ int kyro_spec_accept_tree(kyro_ctx* ctx, const kyro_tree_params* p, const float*
  * run time: libnccl.so.2, or the path in the KYRO_NCCL_LIBRARY variable. */
 #define KYRO_TP_UNIQUE_ID_BYTES 128
 int kyro_tp_unique_id(void* out /* KYRO_TP_UNIQUE_ID_BYTES bytes */);
-/* Blocking: returns once all `world` ranks have joined. */
+/* Blocking: returns once all `world` ranks have joined.  With 2..8 ranks on
+ * distinct GPUs that can map each other's memory (CUDA IPC over NVLink), the
+ * sampler's exchange rounds then run as peer-memory stores with per-sender
+ * flags instead of NCCL collectives; KYRO_TP_TRANSPORT=nccl in the
+ * environment keeps NCCL.  The group agrees on one transport. */
 int kyro_ctx_tp_init(kyro_ctx* ctx, const void* unique_id, int rank, int world);
+/* The transport of the context's exchange rounds: 0 no group, 1 NCCL,
+ * 2 NVLink peer memory. */
+int kyro_ctx_tp_transport(kyro_ctx* ctx);
 
 /* Vocabulary-sharded kyro_spec_accept: p->vocab is the FULL vocabulary V
  * (divisible by the group size R); target_shard [B, k+1, V/R] and

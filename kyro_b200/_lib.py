@@ -44,7 +44,8 @@ EXPORTS = (
     "kyro_sample_tokens", "kyro_verify_attention_workspace_size", "kyro_verify_attention",
     "kyro_kv_reserve", "kyro_kv_reserve_cow", "kyro_kv_commit", "kyro_kv_commit_tree", "kyro_kv_write",
     "kyro_rope_kv_write", "kyro_philox_uniforms", "kyro_selftest_exp",
-    "kyro_tp_unique_id", "kyro_ctx_tp_init", "kyro_spec_accept_tp_workspace_size",
+    "kyro_tp_unique_id", "kyro_ctx_tp_init", "kyro_ctx_tp_transport",
+    "kyro_spec_accept_tp_workspace_size",
     "kyro_spec_accept_tp", "kyro_spec_accept_tree_workspace_size", "kyro_spec_accept_tree",
 )
 
@@ -135,6 +136,7 @@ def load():
         "kyro_spec_accept_tree": (C.c_int, [vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp,
                                             C.c_size_t]),
         "kyro_ctx_tp_init": (C.c_int, [vp, vp, C.c_int, C.c_int]),
+        "kyro_ctx_tp_transport": (C.c_int, [vp]),
         "kyro_spec_accept_tp_workspace_size": (C.c_size_t, [vp, C.c_int]),
         "kyro_spec_accept_tp": (C.c_int, [vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, C.c_size_t]),
     }

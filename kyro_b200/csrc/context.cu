@@ -60,7 +60,7 @@ const char* kyro_kernel_names(void) {
          "accept_tp_max_kernel;accept_tp_sum_kernel;accept_tp_decide_kernel;"
          "accept_tp_search_kernel;accept_tp_write_kernel;verify_attention_kernel;"
          "kv_reserve_kernel;kv_commit_kernel;kv_tree_move_kernel;kv_write_kernel;rope_kv_write_kernel;kv_block_copy_kernel;"
-         "philox_uniforms_kernel;exp_selftest_kernel;tree_attention_tc_kernel";
+         "philox_uniforms_kernel;exp_selftest_kernel;tree_attention_tc_kernel;peer_exchange_kernel";
 }
 
 size_t kyro_last_error(char* buf, size_t len) {
@@ -116,6 +116,9 @@ int kyro_ctx_create(int device, void* stream, kyro_ctx** out) {
   ctx->tp_world = 1;
   ctx->attn_epoch = 0;
   ctx->attn_ws_zeroed = nullptr;
+  ctx->xchg_ready = false;
+  ctx->xchg_local = nullptr;
+  for (int r = 0; r < KYRO_MAX_TP_WORLD; ++r) ctx->xchg_peer[r] = nullptr;
   err = cudaMalloc(&ctx->d_status, 16);
   if (err != cudaSuccess) {
     delete ctx;

@@ -13,6 +13,8 @@
 
 #include "../../include/kyro_spec.h"
 
+#define KYRO_MAX_TP_WORLD 8
+
 struct kyro_ctx {
   int device;
   cudaStream_t stream;
@@ -25,6 +27,11 @@ struct kyro_ctx {
   // workspace whose tickets this context has zeroed
   uint32_t attn_epoch;
   const void* attn_ws_zeroed;
+  // the sharded sampler's exchange rounds over NVLink peer memory
+  // (peer_exchange.cu): this rank's region and every rank's mapping of it
+  bool xchg_ready;
+  uint8_t* xchg_local;
+  uint8_t* xchg_peer[KYRO_MAX_TP_WORLD];
 };
 
 namespace kyro {
@@ -53,9 +60,24 @@ int all_gather(kyro_ctx* ctx, const void* send, void* recv, size_t bytes, const 
 // element-wise max of int32 over the group
 int all_reduce_max_i32(kyro_ctx* ctx, const int32_t* send, int32_t* recv, size_t count,
                        const char* what);
+// element-wise min of int32 over the group
+int all_reduce_min_i32(kyro_ctx* ctx, const int32_t* send, int32_t* recv, size_t count,
+                       const char* what);
 // destroy the context's communicator (no-op without one)
 void release(kyro_ctx* ctx);
 }  // namespace nccl
+
+// The sharded sampler's exchange rounds over NVLink peer memory
+// (peer_exchange.cu), with NCCL as the transport when the ranks cannot map
+// each other's memory or KYRO_TP_TRANSPORT=nccl.
+namespace xchg {
+// map every rank's exchange region (collective over the context's group)
+int init(kyro_ctx* ctx);
+void release(kyro_ctx* ctx);
+int all_gather(kyro_ctx* ctx, const void* send, void* recv, size_t bytes, const char* what);
+int all_reduce_max_i32(kyro_ctx* ctx, const int32_t* send, int32_t* recv, size_t count,
+                       const char* what);
+}  // namespace xchg
 
 }  // namespace kyro
 

@@ -98,7 +98,17 @@ int all_reduce_max_i32(kyro_ctx* ctx, const int32_t* send, int32_t* recv, size_t
   return r == ncclSuccess ? KYRO_OK : nccl_error(r, what);
 }
 
+int all_reduce_min_i32(kyro_ctx* ctx, const int32_t* send, int32_t* recv, size_t count,
+                       const char* what) {
+  const NcclApi* a;
+  KY_TRY(need_api(&a, what));
+  const ncclResult_t r = a->AllReduce(send, recv, count, ncclInt32, ncclMin,
+                                      (ncclComm_t)ctx->nccl_comm, ctx->stream);
+  return r == ncclSuccess ? KYRO_OK : nccl_error(r, what);
+}
+
 void release(kyro_ctx* ctx) {
+  xchg::release(ctx);
   if (!ctx->nccl_comm) return;
   const NcclApi* a = api();
   if (a) a->CommDestroy((ncclComm_t)ctx->nccl_comm);
@@ -138,5 +148,10 @@ extern "C" int kyro_ctx_tp_init(kyro_ctx* ctx, const void* unique_id, int rank, 
   ctx->nccl_comm = comm;
   ctx->tp_rank = rank;
   ctx->tp_world = world;
-  return KYRO_OK;
+  return kyro::xchg::init(ctx);
+}
+
+extern "C" int kyro_ctx_tp_transport(kyro_ctx* ctx) {
+  if (!ctx || !ctx->nccl_comm) return 0;
+  return ctx->xchg_ready ? 2 : 1;
 }

@@ -1995,12 +1995,12 @@ int launch_tp(kyro_ctx* ctx, const Args& a) {
   const unsigned dthreads = 32u * (unsigned)(a.R < kDecideWarps ? a.R : kDecideWarps);
   KY_TRY(launch_dependent(accept_tp_max_kernel, (unsigned)a.B, dthreads, ctx->stream, a,
                           "accept_tp_max_kernel"));
-  KY_TRY(kyro::nccl::all_gather(ctx, a.send1, a.recv1, sizeof(TpRow1) * rows,
+  KY_TRY(kyro::xchg::all_gather(ctx, a.send1, a.recv1, sizeof(TpRow1) * rows,
                                 "kyro_spec_accept_tp: row maxima"));
   if (STOCH) {
     accept_tp_sum_kernel<<<a.B, dthreads, 0, ctx->stream>>>(a);
     KY_TRY(kyro::check_launch("accept_tp_sum_kernel"));
-    KY_TRY(kyro::nccl::all_gather(ctx, a.send2, a.recv2, sizeof(TpRow2) * rows,
+    KY_TRY(kyro::xchg::all_gather(ctx, a.send2, a.recv2, sizeof(TpRow2) * rows,
                                   "kyro_spec_accept_tp: normaliser parts"));
   }
   accept_tp_decide_kernel<<<a.B, dthreads, 0, ctx->stream>>>(a);
@@ -2009,11 +2009,11 @@ int launch_tp(kyro_ctx* ctx, const Args& a) {
   const unsigned nfinal = (unsigned)a.B * (unsigned)((a.nchunks + kFinalPerCta - 1) / kFinalPerCta);
   KY_TRY(launch_dependent(accept_final_kernel<VEC, true>, nfinal, kThreads, ctx->stream, a,
                           "accept_final_kernel"));
-  KY_TRY(kyro::nccl::all_gather(ctx, a.send3, a.recv3, sizeof(TpSeq3) * (size_t)a.B,
+  KY_TRY(kyro::xchg::all_gather(ctx, a.send3, a.recv3, sizeof(TpSeq3) * (size_t)a.B,
                                 "kyro_spec_accept_tp: weight totals"));
   accept_tp_search_kernel<VEC><<<(a.B + kWarps - 1) / kWarps, kThreads, 0, ctx->stream>>>(a);
   KY_TRY(kyro::check_launch("accept_tp_search_kernel"));
-  KY_TRY(kyro::nccl::all_reduce_max_i32(ctx, a.send4, a.recv4, (size_t)a.B,
+  KY_TRY(kyro::xchg::all_reduce_max_i32(ctx, a.send4, a.recv4, (size_t)a.B,
                                         "kyro_spec_accept_tp: token"));
   accept_tp_write_kernel<<<(a.B + 127) / 128, 128, 0, ctx->stream>>>(a);
   return kyro::check_launch("accept_tp_write_kernel");

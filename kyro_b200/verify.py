@@ -83,6 +83,12 @@ class Context:
             check(_lib.load().kyro_ctx_tp_init(self._h, buf, rank, world))
         self.tp_rank, self.tp_world = rank, world
 
+    @property
+    def tp_transport(self) -> str:
+        """The exchange rounds' transport: "none", "nccl" or "peer" (NVLink
+        peer memory)."""
+        return ("none", "nccl", "peer")[_lib.load().kyro_ctx_tp_transport(self._h)]
+
     def device_status(self, clear: bool = True) -> int:
         flags = C.c_uint32(0)
         check(_lib.load().kyro_ctx_device_status(self._h, C.byref(flags), int(clear)))

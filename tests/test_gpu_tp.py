@@ -35,7 +35,9 @@ def _inputs(B, k, V, seed):
     return tgt.contiguous(), drf.contiguous()
 
 
-def _rank_main(rank, world, q_id, q_out, cases):
+def _rank_main(rank, world, q_id, q_out, cases, transport="peer"):
+    if transport == "nccl":
+        os.environ["KYRO_TP_TRANSPORT"] = "nccl"
     sys.path.insert(0, ROOT)
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
@@ -50,6 +52,8 @@ def _rank_main(rank, world, q_id, q_out, cases):
         else:
             uid = q_id.get(timeout=120)
         ctx.tp_init(uid, rank, world)
+        if ctx.tp_transport != transport:
+            raise RuntimeError(f"transport {ctx.tp_transport}, expected {transport}")
         dev = torch.device("cuda", rank)
         results = []
         for (B, k, V, mode, T, seed) in cases:
@@ -79,7 +83,10 @@ def _rank_main(rank, world, q_id, q_out, cases):
         ctx.close()
 
 
-def test_vocab_sharded_accept_matches_oracle():
+@pytest.mark.parametrize("transport", ["peer", "nccl"])
+def test_vocab_sharded_accept_matches_oracle(transport):
+    """Both transports of the exchange rounds: NVLink peer-memory stores with
+    per-sender flags (the default on B200 nodes) and NCCL collectives."""
     n = torch.cuda.device_count() if torch.cuda.is_available() else 0
     if n < 2:
         pytest.skip("needs two GPUs")
@@ -87,7 +94,7 @@ def test_vocab_sharded_accept_matches_oracle():
     import torch.multiprocessing as mp
     mpc = mp.get_context("spawn")
     q_id, q_out = mpc.Queue(), mpc.Queue()
-    procs = [mpc.Process(target=_rank_main, args=(r, world, q_id, q_out, CASES))
+    procs = [mpc.Process(target=_rank_main, args=(r, world, q_id, q_out, CASES, transport))
              for r in range(world)]
     for p in procs:
         p.start()
