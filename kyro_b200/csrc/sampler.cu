@@ -751,9 +751,10 @@ __device__ __forceinline__ void decide_sequence(const Args& a, int b, const RowS
   a.final_rows[b] = fr;
 }
 
-// One CTA per sequence (per row for the sampler): the warps compute the row
-// statistics, then warp 0 runs the accept tests and writes the sequence's
-// accepted prefix and the row its last token is drawn from.
+// One CTA per sequence (per row for the sampler): warp 0 loads the accept
+// tests' inputs while the other warps compute the row statistics, then warp
+// 0 runs the tests and writes the sequence's accepted prefix and the row its
+// last token is drawn from.
 __global__ void __launch_bounds__(kDecideWarps * 32) accept_decide_kernel(Args a) {
   __shared__ RowStat rs[kMaxRows];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
@@ -761,16 +762,20 @@ __global__ void __launch_bounds__(kDecideWarps * 32) accept_decide_kernel(Args a
   grid_dependency_wait();  // the chunk statistics are complete
   allow_dependents();
   if (threadIdx.x == 0) a.cnt_c[b] = 0;  // the final kernel's last-arriver count
-  // warp 0 fetches the test inputs (lane j: tests j and j + 32) before it
-  // joins the row statistics
+  // warp 0 fetches the test inputs (lane j: tests j and j + 32)
   TestInputs t0, t1;
   if (warp == 0 && !a.sample) {
     t0 = load_test(a, b, lane);
     t1 = load_test(a, b, lane + 32);
   }
-  for (int r = warp; r < a.R; r += nwarps) {
-    const RowStat s = row_stat(a, (int64_t)b * a.R + r);
-    if (lane == 0) rs[r] = s;
+  // the other warps take the rows, so that the test inputs' two dependent
+  // loads run beside the row statistics
+  const int w0 = (a.sample || nwarps == 1) ? 0 : 1;
+  if (warp >= w0) {
+    for (int r = warp - w0; r < a.R; r += nwarps - w0) {
+      const RowStat s = row_stat(a, (int64_t)b * a.R + r);
+      if (lane == 0) rs[r] = s;
+    }
   }
   __syncthreads();
   if (warp == 0) decide_sequence(a, b, rs, t0, t1);
@@ -1965,7 +1970,7 @@ int launch_t(kyro_ctx* ctx, const Args& a) {
   const int grid = (int)(need < resident ? need : resident);
   accept_stats_kernel<VEC, STOCH><<<grid, kThreads, 0, ctx->stream>>>(a);
   KY_TRY(kyro::check_launch("accept_stats_kernel"));
-  const int dwarps = a.R < kDecideWarps ? a.R : kDecideWarps;
+  const int dwarps = min(a.R + (a.sample ? 0 : 1), kDecideWarps);
   KY_TRY(launch_dependent(accept_decide_kernel, (unsigned)a.B, (unsigned)dwarps * 32, ctx->stream,
                           a, "accept_decide_kernel"));
   if (!STOCH) return KYRO_OK;  // greedy: the decide step wrote every token
