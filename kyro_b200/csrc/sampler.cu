@@ -1157,6 +1157,7 @@ __global__ void __launch_bounds__(kDecideWarps * 32) accept_tp_max_kernel(Args a
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   const int b = blockIdx.x;
   grid_dependency_wait();
+  allow_dependents();
   for (int r = warp; r < a.R; r += nwarps) {
     const int64_t srow = (int64_t)b * a.R + r;
     TpRow1 v;
@@ -1176,6 +1177,8 @@ __global__ void __launch_bounds__(kDecideWarps * 32) accept_tp_max_kernel(Args a
 __global__ void __launch_bounds__(kDecideWarps * 32) accept_tp_sum_kernel(Args a) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   const int b = blockIdx.x;
+  grid_dependency_wait();  // round 1 has landed
+  allow_dependents();
   for (int r = warp; r < a.R; r += nwarps) {
     const int64_t srow = (int64_t)b * a.R + r;
     const float M = global_row_max(a, srow);
@@ -1220,6 +1223,8 @@ __global__ void __launch_bounds__(kDecideWarps * 32) accept_tp_decide_kernel(Arg
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int b = blockIdx.x;
   const int64_t rows = (int64_t)a.B * a.R;
+  grid_dependency_wait();  // the last exchange round has landed
+  allow_dependents();
   if (threadIdx.x == 0) a.cnt_c[b] = 0;
   for (int r = threadIdx.x; r < a.R; r += blockDim.x) {
     const int64_t srow = (int64_t)b * a.R + r;
@@ -1256,6 +1261,8 @@ template <bool VEC>
 __global__ void __launch_bounds__(kThreads) accept_tp_search_kernel(Args a) {
   const int lane = threadIdx.x & 31;
   const int b = blockIdx.x * kWarps + (threadIdx.x >> 5);
+  grid_dependency_wait();  // round 3 has landed
+  allow_dependents();
   if (b >= a.B) return;
   const FinalRow fr = a.final_rows[b];
   int token = -1;
@@ -1292,6 +1299,8 @@ __global__ void __launch_bounds__(kThreads) accept_tp_search_kernel(Args a) {
 
 __global__ void accept_tp_write_kernel(Args a) {
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  grid_dependency_wait();  // round 4 has landed
+  allow_dependents();
   if (b >= a.B) return;
   const FinalRow fr = a.final_rows[b];
   if (!fr.skip) a.out_tokens[fr.out_index] = a.recv4[b];
@@ -2003,25 +2012,25 @@ int launch_tp(kyro_ctx* ctx, const Args& a) {
   KY_TRY(kyro::xchg::all_gather(ctx, a.send1, a.recv1, sizeof(TpRow1) * rows,
                                 "kyro_spec_accept_tp: row maxima"));
   if (STOCH) {
-    accept_tp_sum_kernel<<<a.B, dthreads, 0, ctx->stream>>>(a);
-    KY_TRY(kyro::check_launch("accept_tp_sum_kernel"));
+    KY_TRY(launch_dependent(accept_tp_sum_kernel, (unsigned)a.B, dthreads, ctx->stream, a,
+                            "accept_tp_sum_kernel"));
     KY_TRY(kyro::xchg::all_gather(ctx, a.send2, a.recv2, sizeof(TpRow2) * rows,
                                   "kyro_spec_accept_tp: normaliser parts"));
   }
-  accept_tp_decide_kernel<<<a.B, dthreads, 0, ctx->stream>>>(a);
-  KY_TRY(kyro::check_launch("accept_tp_decide_kernel"));
+  KY_TRY(launch_dependent(accept_tp_decide_kernel, (unsigned)a.B, dthreads, ctx->stream, a,
+                          "accept_tp_decide_kernel"));
   if (!STOCH) return KYRO_OK;  // greedy: the decide step wrote every token
   const unsigned nfinal = (unsigned)a.B * (unsigned)((a.nchunks + kFinalPerCta - 1) / kFinalPerCta);
   KY_TRY(launch_dependent(accept_final_kernel<VEC, true>, nfinal, kThreads, ctx->stream, a,
                           "accept_final_kernel"));
   KY_TRY(kyro::xchg::all_gather(ctx, a.send3, a.recv3, sizeof(TpSeq3) * (size_t)a.B,
                                 "kyro_spec_accept_tp: weight totals"));
-  accept_tp_search_kernel<VEC><<<(a.B + kWarps - 1) / kWarps, kThreads, 0, ctx->stream>>>(a);
-  KY_TRY(kyro::check_launch("accept_tp_search_kernel"));
+  KY_TRY(launch_dependent(accept_tp_search_kernel<VEC>, (unsigned)((a.B + kWarps - 1) / kWarps),
+                          kThreads, ctx->stream, a, "accept_tp_search_kernel"));
   KY_TRY(kyro::xchg::all_reduce_max_i32(ctx, a.send4, a.recv4, (size_t)a.B,
                                         "kyro_spec_accept_tp: token"));
-  accept_tp_write_kernel<<<(a.B + 127) / 128, 128, 0, ctx->stream>>>(a);
-  return kyro::check_launch("accept_tp_write_kernel");
+  return launch_dependent(accept_tp_write_kernel, (unsigned)((a.B + 127) / 128), 128u,
+                          ctx->stream, a, "accept_tp_write_kernel");
 }
 
 void fill_common(Args& a, const Workspace& ws, int64_t V, int B, int R) {
