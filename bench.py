@@ -736,6 +736,176 @@ def run_tree(args):
         dist.destroy_process_group()
 
 
+class _EventTimer:
+    """Sums CUDA-event intervals per name over the current stream."""
+
+    def __init__(self, stream):
+        import torch
+        self.torch, self.stream, self.open, self.pairs = torch, stream, {}, {}
+
+    def begin(self, name):
+        e = self.torch.cuda.Event(enable_timing=True)
+        e.record(self.stream)
+        self.open[name] = e
+
+    def end(self, name):
+        e = self.torch.cuda.Event(enable_timing=True)
+        e.record(self.stream)
+        self.pairs.setdefault(name, []).append((self.open.pop(name), e))
+
+    def ms(self, name, per):
+        return sum(a.elapsed_time(b) for a, b in self.pairs.get(name, [])) / per
+
+
+def run_e2e_model(args):
+    """Config 4: the end-to-end batched speculative step over a random-init
+    16-layer Llama target and a 2-layer draft (kyro_b200/e2e_model.py).
+    512 requests in total, split over the N ranks (strong scaling, no
+    collective); every step drafts k = 4 tokens per request, verifies k + 1
+    positions through the target, accepts, and commits, with the contexts
+    growing from step to step.  Timed as CUDA graph replays of one step."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from kyro_b200.e2e_model import CONFIG4, CONFIG4_SHAPE, SpecModels, SpecStep, context_lengths
+    from kyro_b200.verify import Context
+    from kyro_b200.workloads import ChainConfig, paged_state
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    cfg, shape = CONFIG4, CONFIG4_SHAPE
+    if cfg.requests % world:
+        raise SystemExit(f"{cfg.requests} requests do not split over {world} ranks")
+    B = cfg.requests // world
+    lens = context_lengths(cfg, seed=0)[rank * B:(rank + 1) * B]
+    bs, k = cfg.block_size, cfg.k
+    grow = (k + 1) * (args.warmup + args.steps + PER_KERNEL_STEPS + 8)
+    need_blocks = int(sum(-(-(int(c) + grow) // bs) for c in lens))
+    kvcfg = ChainConfig(batch=B, k=k, num_heads=1, num_kv_heads=1, head_dim=8,
+                        num_blocks=need_blocks + 256, ctx_min=1, ctx_max=cfg.ctx_max,
+                        headroom_tokens=grow)
+    kv = paged_state(kvcfg, dev, seed=4000 + rank, ctx_lens=lens, num_query=1, fill_cache=False)
+    del kv.k_cache, kv.v_cache, kv.q
+    models = SpecModels(shape, cfg, kvcfg.num_blocks, dev, seed=4100)
+    ctx_t, ctx_d = Context(local), Context(local)
+    spec = SpecStep(models, ctx_t, ctx_d, kv, seed=0, seq_offset=rank * B)
+    side = torch.cuda.Stream(dev)
+    graph = None
+    with torch.cuda.stream(side):
+        for i in range(args.warmup):
+            spec(i)
+        if not args.no_graph:
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=side):
+                spec(args.warmup)
+    torch.cuda.synchronize()
+    lens0 = kv.context_lens.cpu().numpy().copy()
+    if world > 1:
+        dist.barrier()
+    clocks = None
+    if rank == 0:
+        try:
+            clocks = NvmlClockSampler(local)
+        except Exception:
+            clocks = ClockSampler(local)
+        clocks.start()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(side):
+        t0.record(side)
+        for i in range(args.warmup, args.warmup + args.steps):
+            if graph is not None:
+                graph.replay()
+            else:
+                spec(i)
+        t1.record(side)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop() if clocks else None
+    ms = t0.elapsed_time(t1)
+    lens1 = kv.context_lens.cpu().numpy().copy()
+    emitted = float(lens1.sum() - lens0.sum())  # accept_len + 1 per request and step
+    # per-kernel times from eager steps with events around the parts
+    timer = _EventTimer(side)
+    with torch.cuda.stream(side):
+        lens_k = kv.context_lens.cpu().numpy().copy()
+        for i in range(PER_KERNEL_STEPS):
+            spec(args.warmup + args.steps + i, timer=timer)
+    torch.cuda.synchronize()
+    del graph
+    status = ctx_t.device_status() | ctx_d.device_status()
+    if status:
+        raise SystemExit(f"device status word 0x{status:x} after the timed region")
+    part = {n: timer.ms(n, PER_KERNEL_STEPS) for n in ("draft", "target", "attention", "accept")}
+    vals = [ms, emitted] + [part[n] for n in ("draft", "target", "attention", "accept")]
+    if world > 1:
+        t = torch.tensor(vals[:1] + vals[2:], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e = torch.tensor([emitted], dtype=torch.float64, device=dev)
+        dist.all_reduce(e, op=dist.ReduceOp.SUM)
+        ms, emitted = float(t[0]), float(e[0])
+        part = dict(zip(("draft", "target", "attention", "accept"), [float(x) for x in t[1:]]))
+    peak, peak_kind = load_peaks()
+    # target verify attention, all 16 layers of one step: K and V of every
+    # cached token plus the k + 1 new ones, and Q and O (bf16)
+    kv_tok = 2 * shape.kv_heads * shape.head_dim * 2
+    att_bytes = float(shape.layers * ((lens_k + k + 1).sum() * kv_tok
+                                      + 2 * B * (k + 1) * shape.heads * shape.head_dim * 2))
+    acc_bytes = float((2 * k + 1) * shape.vocab * 4 * B)
+    att_gbs = att_bytes / (part["attention"] * 1e-3) / 1e9
+    acc_gbs = acc_bytes / (part["accept"] * 1e-3) / 1e9
+    if rank == 0:
+        line = {
+            "metric": "spec-decode verified positions/s, end-to-end step (config 4)",
+            "unit": "verified positions/s",
+            "value": cfg.requests * (k + 1) * args.steps / (ms * 1e-3), "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded random-init weights; BASELINE config 4 shapes; "
+                    "lognormal contexts with sigma 1.0 assumed)",
+            "config": {"workload": "config4: end-to-end speculative step, 16-layer Llama target "
+                                   "(hidden 2048, 32/8 heads, D 64, FFN 8192, V 128256, bf16) + "
+                                   "2-layer draft, k 4, T 0.7, 512 requests, ctx lognormal "
+                                   "(median 1024, max 16384)",
+                       "requests": cfg.requests, "requests_per_gpu": B,
+                       "parallelism": f"batch-sharded x{world} (no collective)",
+                       "l2": "inputs larger than L2 (~30 GB of K/V per GPU at N=1)"},
+            "emitted_tokens_per_s": emitted / (ms * 1e-3),
+            "mean_emitted_per_request_step": emitted / (cfg.requests * args.steps),
+            "roofline": {"bound": "hbm", "kernel": "verify_attention_kernel (16 target layers)",
+                         "achieved": att_gbs, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                         "frac": att_gbs / peak, "traffic": None},
+            "parts_ms_per_step": part,
+            "kernels": {
+                "target_attention": {"ms": part["attention"], "algorithmic_bytes": att_bytes,
+                                     "GBps": att_gbs, "frac": att_gbs / peak},
+                "accept": {"ms": part["accept"], "algorithmic_bytes": acc_bytes,
+                           "GBps": acc_gbs, "frac": acc_gbs / peak},
+            },
+            "timing": "stream launches" if args.no_graph else "CUDA graph replays of the step",
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    ctx_t.close()
+    ctx_d.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def run_tp(args):
     """Config 3: vocabulary-sharded acceptance (kyro_spec_accept_tp) over the
     N ranks of one tensor-parallel group, plus KV reserve/commit on a
@@ -897,9 +1067,10 @@ def main():
                     help="time config 1 as plain launches instead of CUDA graph replays")
     ap.add_argument("--no-e2e", action="store_true",
                     help="skip the host-buffer leg (profiling runs)")
-    ap.add_argument("--config", choices=["1", "2", "3"], default="1",
+    ap.add_argument("--config", choices=["1", "2", "3", "4"], default="1",
                     help="1: chain verify step (the headline); 2: tree verify step; "
-                         "3: vocabulary-sharded acceptance over the N ranks of one TP group")
+                         "3: vocabulary-sharded acceptance over the N ranks of one TP group; "
+                         "4: end-to-end speculative step of a 16-layer Llama + 2-layer draft")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         raise SystemExit("--warmup must be >= 3")
@@ -909,6 +1080,8 @@ def main():
         run_tree(args)
     elif args.config == "3":
         run_tp(args)
+    elif args.config == "4":
+        run_e2e_model(args)
     else:
         run_ours(args)
 
