@@ -531,7 +531,10 @@ verify_attention_kernel(const __nv_bfloat16* __restrict__ q,
 
 // ------------------------------------------------------------------ host
 
-constexpr int kStages = 2;
+// ring stages per warp: a D = 64 block is half the bytes of a D = 128 one,
+// so it keeps more blocks in flight for the same bytes in flight
+template <int D>
+constexpr int stages_for() { return D == 64 ? 2 : 2; }
 
 struct Plan {
   AttnArgs a;
@@ -613,6 +616,7 @@ template <int NT, int D>
 void launch(const Plan& pl, dim3 grid, cudaStream_t st, const void* q, const void* kc,
             const void* vc, const int64_t* bt, const int64_t* cl, const uint64_t* tm, void* out,
             float* po, float* pml, unsigned long long* tk, uint32_t* status) {
+  constexpr int kStages = stages_for<D>();
   constexpr int smem = Geo<D, kStages>::kSmemBytes;
   static std::once_flag attr_once;  // one host call per kernel, never inside a graph capture
   std::call_once(attr_once, [] {
