@@ -48,6 +48,7 @@ def _oracle(oracle, st, cfg, mask):
     (8, 8, 128, 1, [1, 33, 300]),                     # MHA, one query
     (64, 8, 128, 8, [40, 700]),                       # 64 rows per KV head: two row groups
     (32, 8, 64, 5, [10, 500]),                        # head_dim 64
+    (32, 8, 64, 1, [0, 2, 47, 48, 49, 1700]),         # head_dim 64, one query (the draft)
     (16, 2, 128, 3, [255, 256, 257]),
 ])
 def test_chain_attention_matches_oracle(ctx, oracle, hq, hkv, d, nq, lens):
@@ -60,10 +61,10 @@ def test_chain_attention_matches_oracle(ctx, oracle, hq, hkv, d, nq, lens):
     assert ctx.device_status() == 0
 
 
-@pytest.mark.parametrize("split", [4, 8, 16, 0])
-def test_split_kv_merge(ctx, oracle, split):
+@pytest.mark.parametrize("d,split", [(128, 4), (128, 8), (128, 16), (128, 0), (64, 7), (64, 0)])
+def test_split_kv_merge(ctx, oracle, d, split):
     from kyro_b200.verify import verify_attention
-    cfg, st, _ = _setup(ctx, 32, 8, 128, 6, [3000, 47, 1500, 4096], seed=7)
+    cfg, st, _ = _setup(ctx, 32, 8, d, 6, [3000, 47, 1500, 4096], seed=7)
     out = verify_attention(ctx, st.q, st.k_cache, st.v_cache, st.block_table, st.context_lens,
                            kv_split_blocks=split)
     ref = _oracle(oracle, st, cfg, None)
