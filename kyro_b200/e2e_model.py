@@ -64,9 +64,11 @@ class E2EConfig:
     ctx_max: int = 16384
     block_size: int = 16
     draft_layers: int = 2
-    # KV blocks per attention work item: contexts range from tens of tokens to
-    # 16384, so short items keep the longest sequences from trailing the grid
-    kv_split_blocks: int = 64
+    # KV blocks per attention work item (0: the library's plan, 256 here).
+    # The grid spans the block table's width, so short items mostly launch
+    # empty CTAs: measured 445 us at 64 blocks against 308 us at 256 for the
+    # target's 5 query rows
+    kv_split_blocks: int = 0
 
 
 CONFIG4 = E2EConfig()
@@ -128,9 +130,10 @@ class SpecModels:
 
     def forward(self, ctx: Context, layers: Layers, kc: List[torch.Tensor], vc: List[torch.Tensor],
                 tokens: torch.Tensor, block_table: torch.Tensor, lens: torch.Tensor,
-                ws_attn: torch.Tensor, timer=None) -> torch.Tensor:
-        """tokens int64 [B, n] at positions lens[b] + j -> bf16 logits [B, n, V].
-        Each layer stores its new K/V rows into slots lens[b] + j."""
+                ws_attn: torch.Tensor, logits: torch.Tensor, timer=None) -> torch.Tensor:
+        """tokens int64 [B, n] at positions lens[b] + j -> fp32 logits, written
+        by the lm_head GEMM into `logits` (contiguous [B * n, V]) and returned
+        as [B, n, V].  Each layer stores its new K/V rows into slots lens[b] + j."""
         s = self.shape
         B, n = tokens.shape
         hq, hkv, d = s.heads, s.kv_heads, s.head_dim
@@ -154,7 +157,8 @@ class SpecModels:
             gu = torch.matmul(h, layers.wgu[i])
             x = x + torch.matmul(F.silu(gu[..., :s.ffn]) * gu[..., s.ffn:], layers.wdown[i])
         h = F.rms_norm(x, (s.hidden,), self.final_norm, s.eps)
-        return torch.matmul(h, self.lm_head)
+        torch.mm(h.view(B * n, s.hidden), self.lm_head, out_dtype=torch.float32, out=logits)
+        return logits.view(B, n, s.vocab)
 
 
 class SpecStep:
@@ -177,6 +181,7 @@ class SpecStep:
         self.toks = torch.empty(B, k + 1, dtype=torch.int32, device=dev)
         self.num = torch.empty(B, dtype=torch.int32, device=dev)
         self.tokens_in = torch.empty(B, k + 1, dtype=torch.int64, device=dev)
+        self.dlog = torch.empty(B, V, dtype=torch.float32, device=dev)  # one draft position
         from . import _lib
         import ctypes as C
         from .verify import attn_params
@@ -199,6 +204,7 @@ class SpecStep:
 
     def __call__(self, step: int, timer=None):
         m, kv, cfg, k = self.m, self.kv, self.m.cfg, self.k
+        V = m.shape.vocab
         bs = cfg.block_size
         kv_reserve(self.ctx_t, k + 1, kv.block_table, kv.context_lens, kv.free_stack, kv.free_top,
                    kv.ref_counts, bs, out_ok=self.ok)
@@ -210,7 +216,7 @@ class SpecStep:
         for i in range(k):
             torch.add(kv.context_lens, i, out=self.d_lens)
             logits = m.forward(self.ctx_d, m.draft, m.d_k, m.d_v, tok, kv.block_table, self.d_lens,
-                               self.ws_d).float()  # [B, 1, V] fp32
+                               self.ws_d, self.dlog)  # [B, 1, V] fp32
             t, _ = sample_tokens(self.ctx_d, logits, cfg.temperature, seed=self.seed,
                                  step=step * k + i, seq_offset=self.seq_offset,
                                  workspace=self.ws_smp)
@@ -222,9 +228,8 @@ class SpecStep:
             timer.begin("target")
         self.tokens_in[:, 0] = self.last
         self.tokens_in[:, 1:] = self.drafts
-        logits = m.forward(self.ctx_t, m.target, m.t_k, m.t_v, self.tokens_in, kv.block_table,
-                           kv.context_lens, self.ws_t, timer=timer)
-        self.tgt.copy_(logits)
+        m.forward(self.ctx_t, m.target, m.t_k, m.t_v, self.tokens_in, kv.block_table,
+                  kv.context_lens, self.ws_t, self.tgt.view(self.B * (k + 1), V), timer=timer)
         if timer is not None:
             timer.end("target")
             timer.begin("accept")
