@@ -783,6 +783,11 @@ def run_e2e_model(args):
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
     cfg, shape = CONFIG4, CONFIG4_SHAPE
+    if args.requests or args.target_layers:
+        # a smaller case of the same step, for profiler captures (not a bench line)
+        import dataclasses
+        cfg = dataclasses.replace(cfg, requests=args.requests or cfg.requests)
+        shape = dataclasses.replace(shape, layers=args.target_layers or shape.layers)
     if cfg.requests % world:
         raise SystemExit(f"{cfg.requests} requests do not split over {world} ranks")
     B = cfg.requests // world
@@ -881,6 +886,8 @@ def run_e2e_model(args):
                                    "2-layer draft, k 4, T 0.7, 512 requests, ctx lognormal "
                                    "(median 1024, max 16384)",
                        "requests": cfg.requests, "requests_per_gpu": B,
+                       "target_layers": shape.layers,
+                       "reduced_for_profiling": bool(args.requests or args.target_layers),
                        "parallelism": f"batch-sharded x{world} (no collective)",
                        "l2": "inputs larger than L2 (~30 GB of K/V per GPU at N=1)"},
             "emitted_tokens_per_s": emitted / (ms * 1e-3),
@@ -1067,6 +1074,10 @@ def main():
                     help="time config 1 as plain launches instead of CUDA graph replays")
     ap.add_argument("--no-e2e", action="store_true",
                     help="skip the host-buffer leg (profiling runs)")
+    ap.add_argument("--requests", type=int, default=0,
+                    help="config 4 only: requests in all (default 512; smaller for profiling)")
+    ap.add_argument("--target-layers", type=int, default=0,
+                    help="config 4 only: target layers (default 16; fewer for profiling)")
     ap.add_argument("--config", choices=["1", "2", "3", "4"], default="1",
                     help="1: chain verify step (the headline); 2: tree verify step; "
                          "3: vocabulary-sharded acceptance over the N ranks of one TP group; "
