@@ -855,23 +855,28 @@ def run_e2e_model(args):
     if status:
         raise SystemExit(f"device status word 0x{status:x} after the timed region")
     part = {n: timer.ms(n, PER_KERNEL_STEPS) for n in ("draft", "target", "attention", "accept")}
-    vals = [ms, emitted] + [part[n] for n in ("draft", "target", "attention", "accept")]
-    if world > 1:
-        t = torch.tensor(vals[:1] + vals[2:], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e = torch.tensor([emitted], dtype=torch.float64, device=dev)
-        dist.all_reduce(e, op=dist.ReduceOp.SUM)
-        ms, emitted = float(t[0]), float(e[0])
-        part = dict(zip(("draft", "target", "attention", "accept"), [float(x) for x in t[1:]]))
-    peak, peak_kind = load_peaks()
-    # target verify attention, all 16 layers of one step: K and V of every
+    # target verify attention, all layers of one step: K and V of every
     # cached token plus the k + 1 new ones, and Q and O (bf16)
     kv_tok = 2 * shape.kv_heads * shape.head_dim * 2
     att_bytes = float(shape.layers * ((lens_k + k + 1).sum() * kv_tok
                                       + 2 * B * (k + 1) * shape.heads * shape.head_dim * 2))
     acc_bytes = float((2 * k + 1) * shape.vocab * 4 * B)
-    att_gbs = att_bytes / (part["attention"] * 1e-3) / 1e9
-    acc_gbs = acc_bytes / (part["accept"] * 1e-3) / 1e9
+    att_ms, acc_ms = part["attention"], part["accept"]
+    if world > 1:
+        # step time and part times: max over ranks; kernel bandwidth: every
+        # rank's bytes over every rank's time (ranks hold unequal contexts)
+        t = torch.tensor([ms] + [part[n] for n in ("draft", "target", "attention", "accept")],
+                         dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        sums = torch.tensor([emitted, att_bytes, att_ms, acc_bytes, acc_ms], dtype=torch.float64,
+                            device=dev)
+        dist.all_reduce(sums, op=dist.ReduceOp.SUM)
+        ms = float(t[0])
+        part = dict(zip(("draft", "target", "attention", "accept"), [float(x) for x in t[1:]]))
+        emitted, att_bytes, att_ms, acc_bytes, acc_ms = [float(x) for x in sums]
+    peak, peak_kind = load_peaks()
+    att_gbs = att_bytes / (att_ms * 1e-3) / 1e9
+    acc_gbs = acc_bytes / (acc_ms * 1e-3) / 1e9
     if rank == 0:
         line = {
             "metric": "spec-decode verified positions/s, end-to-end step (config 4)",
@@ -897,9 +902,10 @@ def run_e2e_model(args):
                          "frac": att_gbs / peak, "traffic": None},
             "parts_ms_per_step": part,
             "kernels": {
-                "target_attention": {"ms": part["attention"], "algorithmic_bytes": att_bytes,
+                # means over ranks (one rank's figures at N = 1)
+                "target_attention": {"ms": att_ms / world, "algorithmic_bytes": att_bytes / world,
                                      "GBps": att_gbs, "frac": att_gbs / peak},
-                "accept": {"ms": part["accept"], "algorithmic_bytes": acc_bytes,
+                "accept": {"ms": acc_ms / world, "algorithmic_bytes": acc_bytes / world,
                            "GBps": acc_gbs, "frac": acc_gbs / peak},
             },
             "timing": "stream launches" if args.no_graph else "CUDA graph replays of the step",
