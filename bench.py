@@ -877,6 +877,11 @@ def run_e2e_model(args):
     peak, peak_kind = load_peaks()
     att_gbs = att_bytes / (att_ms * 1e-3) / 1e9
     acc_gbs = acc_bytes / (acc_ms * 1e-3) / 1e9
+    # DRAM bytes of one target attention launch: a capture of a 128-request
+    # case scaled by this launch's algorithmic bytes (traffic follows them)
+    small = load_traffic().get("verify_attention_kernel_config4_small")
+    traffic4 = (small["dram_bytes"] / small["algorithmic_bytes"] * att_bytes / world / shape.layers
+                if small else None)
     if rank == 0:
         line = {
             "metric": "spec-decode verified positions/s, end-to-end step (config 4)",
@@ -899,7 +904,7 @@ def run_e2e_model(args):
             "mean_emitted_per_request_step": emitted / (cfg.requests * args.steps),
             "roofline": {"bound": "hbm", "kernel": "verify_attention_kernel (16 target layers)",
                          "achieved": att_gbs, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
-                         "frac": att_gbs / peak, "traffic": None},
+                         "frac": att_gbs / peak, "traffic": traffic4},
             "parts_ms_per_step": part,
             "kernels": {
                 # means over ranks (one rank's figures at N = 1)
