@@ -326,6 +326,13 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
   return d;
 }
 
+// min of three; NaN if any input is NaN
+__device__ __forceinline__ float min3_nan(float a, float b, float c) {
+  float d;
+  asm("min.NaN.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 // Programmatic dependent launch: a kernel launched with programmatic stream
 // serialization may start before its predecessor ends; grid_dependency_wait
 // blocks until the predecessor grid has completed and its writes are
@@ -340,10 +347,13 @@ __device__ __forceinline__ void allow_dependents() {
 
 // exp_fast of both halves.  fma(-nf, ln2, x) is written fma(nf, -ln2, x):
 // the product is exact inside the fma, so the sign can move to ln2.
+// CLAMP = false is for arguments already known to be >= -87 (and not NaN),
+// where the clamp is the identity.
+template <bool CLAMP = true>
 __device__ __forceinline__ f2_t exp_pair(f2_t x) {
   float xl, xh;
   f2_unpack(x, xl, xh);
-  const f2_t xc = f2_pack(fmaxf(xl, -87.0f), fmaxf(xh, -87.0f));
+  const f2_t xc = CLAMP ? f2_pack(fmaxf(xl, -87.0f), fmaxf(xh, -87.0f)) : x;
   const f2_t t = f2_fma(xc, f2_pack(KY_LOG2E, KY_LOG2E), f2_pack(KY_RND_MAGIC, KY_RND_MAGIC));
   const f2_t nf = f2_sub(t, f2_pack(KY_RND_MAGIC, KY_RND_MAGIC));
   const f2_t r = f2_fma(nf, f2_pack(-KY_LN2, -KY_LN2), xc);
@@ -457,10 +467,27 @@ __device__ __forceinline__ void reduce_slice(const Args& a, Slice& s) {
     // order, then (a0 + a1) + (a2 + a3), then the lane butterfly
     const f2_t m2 = f2_pack(m, m);
     f2_t acc01 = f2_pack(0.0f, 0.0f), acc23 = f2_pack(0.0f, 0.0f);
+    // ky_exp clamps its argument at -87.  When the chunk's smallest entry
+    // already gives z - m >= -87 (fsub is monotonic, so one check covers
+    // every entry; -inf, NaN and an all -inf chunk fail it), the clamp is
+    // the identity and the warp skips it.  The vote keeps the branch uniform.
+    const float lmin = min3_nan(min3_nan(min3_nan(v[0], v[1], v[2]), min3_nan(v[3], v[4], v[5]),
+                                         min3_nan(v[6], v[7], v[8])),
+                                min3_nan(min3_nan(v[9], v[10], v[11]),
+                                         min3_nan(v[12], v[13], v[14]), v[15]),
+                                v[15]);
+    if (__all_sync(0xffffffffu, KY_FSUB(lmin, m) >= -87.0f)) {
 #pragma unroll
-    for (int i = 0; i < kVec; ++i) {
-      acc01 = f2_add(acc01, exp_pair(f2_sub(z[2 * i], m2)));
-      acc23 = f2_add(acc23, exp_pair(f2_sub(z[2 * i + 1], m2)));
+      for (int i = 0; i < kVec; ++i) {
+        acc01 = f2_add(acc01, exp_pair<false>(f2_sub(z[2 * i], m2)));
+        acc23 = f2_add(acc23, exp_pair<false>(f2_sub(z[2 * i + 1], m2)));
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < kVec; ++i) {
+        acc01 = f2_add(acc01, exp_pair(f2_sub(z[2 * i], m2)));
+        acc23 = f2_add(acc23, exp_pair(f2_sub(z[2 * i + 1], m2)));
+      }
     }
     float a0, a1, a2, a3;
     f2_unpack(acc01, a0, a1);

@@ -68,6 +68,31 @@ def test_stochastic_accept_matches_oracle(ctx, oracle, B, k, V, T, seed):
     assert ctx.device_status() == 0
 
 
+@pytest.mark.parametrize("std", [25.0, 60.0])
+def test_wide_logits_and_minus_inf_match_oracle(ctx, oracle, std):
+    """Logit spreads above 87 within a chunk, and -inf entries, take the
+    clamped exponential; chunks within 87 of their max skip the clamp.  Both
+    must give the contract's bits."""
+    from kyro_b200.verify import spec_accept
+    from kyro_b200.workloads import accept_inputs
+    B, k, V, T, seed = 6, 4, 32000, 1.0, 11
+    tgt, drf = accept_inputs(B, k, V, ctx.device, seed=seed, std=std, noise=std / 3)
+    g = torch.Generator(device=ctx.device).manual_seed(seed)
+    holes = torch.rand(B, 1, V, generator=g, device=ctx.device) < 0.002
+    tgt = tgt.masked_fill(holes, float("-inf")).contiguous()
+    drf = drf.masked_fill(holes[:, :, :V].expand(B, k, V), float("-inf")).contiguous()
+    drafts = _sample_drafts(ctx, oracle, drf, T, seed)
+    acc, toks, num, probs = spec_accept(ctx, tgt, drf, drafts, temperature=T, seed=seed,
+                                        want_probs=True)
+    oacc, otoks, onum, oprobs = oracle.spec_accept(_np(tgt), _np(drf), _np(drafts),
+                                                   temperature=T, seed=seed, step=0,
+                                                   nthreads=NTHREADS)
+    assert np.array_equal(_np(acc), oacc)
+    assert np.array_equal(_np(toks), otoks)
+    assert np.array_equal(_np(probs), oprobs)
+    assert ctx.device_status() == 0
+
+
 def test_probabilities_match_torch_softmax(ctx, oracle):
     """probabilities within 1e-5 relative (fp32) of softmax(z / T)."""
     from kyro_b200.verify import spec_accept
