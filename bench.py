@@ -1,27 +1,45 @@
 """Benchmark of the speculative verify step on B200.
 
-One step = one verify pass over a batch of 64 sequences per GPU, the
-workload BASELINE.json's metric is quoted on (config 1):
-  kv_reserve (k+1 slots) -> kv_write (new K/V rows) -> verify attention
-  (Llama-3-8B layer: Hq 32, Hkv 8, D 128, bf16 paged KV, block 16,
-  context ~ U[512, 4096]) -> acceptance sampling (k = 5, V = 128256, fp32,
-  T = 1.0) -> kv_commit.
-Contexts grow by the committed tokens from step to step, as in decoding.
+One step = one batched verify pass over 64 sequences per GPU, the workload
+BASELINE.json's metric is quoted on (config 1), run by
+kyro_b200.step.VerifyStep:
+  kv_reserve (k+1 slots) -> rope_kv_write (RoPE of the new q/k rows at
+  context_len + j, paged store of the new K/V) -> verify attention
+  (Llama-3-8B layer: Hq 32, Hkv 8, D 128, bf16 paged KV, block 16, context
+  ~ U[512, 4096]) -> acceptance sampling (k = 5, V = 128256, fp32, T = 1.0)
+  -> kv_commit.
+Every timed step first restores the KV bookkeeping state (one device copy),
+so every step sees the same context lengths; the step is captured once as
+a CUDA graph and replayed, so every replay also reuses the Philox step
+number of the capture (the work and its timing do not depend on the draws).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 N > 1 runs under torchrun, one rank per GPU; sequences are sharded by
 rank (weak scaling, no collective on the data path).  `value` is verified
 positions per second over all ranks, device-timed with CUDA events, max
-over ranks.  `e2e` is the same metric through the C ABI with host buffers:
-each step copies its inputs from pinned host memory and reads its results
-back.  `--impl reference` times the CPU restatement of the reference path
-(oracle/, the reference itself is Rust and cannot be built here) on the
-host cores.
+over ranks.  `e2e` is the same metric through the public step API with host
+buffers: each step copies its inputs from pinned host memory and reads its
+results back.  `--impl reference` times the CPU restatement of the
+reference path (oracle/; the reference itself is Rust and cannot be built
+here) on the host cores.
+
+Besides the headline, the default run adds (outside the headline's timed
+region, each timed on its own):
+  config0   acceptance only (B 8, k 4, V 32000): launch-bound
+  config2   the tree verify step (64-node tree, context 8192)
+  tp_accept config 3's vocabulary-sharded acceptance (B 256, k 8,
+            V 128256 over the N ranks as one tensor-parallel group, both
+            exchange transports), after a bit-exact check of the sharded
+            kernels against tests/golden/tp_accept_golden.json; at N = 1 the
+            single-GPU acceptance of the same rows (the strong-scaling base)
+  per_rank  every rank's context tokens, bytes and kernel times (N > 1)
 """
 from __future__ import annotations
 
 import argparse
+import ctypes as C
+import datetime
 import json
 import os
 import statistics
@@ -39,13 +57,14 @@ METRIC = "spec-verify tokens/s (attn+accept)"
 UNIT = "verified positions/s"
 # untimed steps after the timed region that carry CUDA events around the kernels
 PER_KERNEL_STEPS = 10
+TP_GOLDEN = os.path.join(ROOT, "tests", "golden", "tp_accept_golden.json")
 
 
 def workload_desc(cfg, n):
     return {
-        "workload": "config1: chain verify (paged attention + accept + KV commit), Llama-3-8B "
-                    "layer Hq32/Hkv8/D128 bf16 KV block16, ctx U[512,4096], k=5 (+1), "
-                    "V=128256 fp32, T=1.0",
+        "workload": "config1: chain verify (RoPE + paged KV store, paged attention, accept, KV "
+                    "commit), Llama-3-8B layer Hq32/Hkv8/D128 bf16 KV block16, ctx U[512,4096], "
+                    "k=5 (+1), V=128256 fp32, T=1.0",
         "batch_per_gpu": cfg.batch, "global_batch": cfg.batch * n, "k": cfg.k,
         "vocab": cfg.vocab, "kv_blocks_per_gpu": cfg.num_blocks,
         "parallelism": f"batch-sharded x{n} (no collective)",
@@ -171,6 +190,57 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
+def start_clocks(rank, local):
+    """The clock sampler of rank 0 (None elsewhere), on the physical GPU."""
+    if rank != 0:
+        return None
+    phys = local
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    if vis:
+        ids = [v.strip() for v in vis.split(",")]
+        if local < len(ids) and ids[local].isdigit():
+            phys = int(ids[local])
+    try:
+        clocks = NvmlClockSampler(phys)
+    except Exception:
+        clocks = ClockSampler(phys)
+    clocks.start()
+    return clocks
+
+
+def bind_numa_local(local):
+    """Restrict this process to the CPUs next to its GPU (read from sysfs
+    through the GPU's PCI bus id), so that pinned host buffers allocated
+    afterwards land on the GPU's NUMA node.  Returns (node, cpu count) or
+    None when the topology is not available."""
+    try:
+        import pynvml
+        pynvml.nvmlInit()
+        h = pynvml.nvmlDeviceGetHandleByIndex(local)
+        bus = pynvml.nvmlDeviceGetPciInfo(h).busId
+        bus = bus.decode() if isinstance(bus, bytes) else bus
+        dev = "/sys/bus/pci/devices/" + bus.lower()[-12:]
+        with open(dev + "/local_cpulist") as f:
+            spec = f.read().strip()
+        cpus = set()
+        for part in spec.split(","):
+            lo, _, hi = part.partition("-")
+            cpus.update(range(int(lo), int(hi or lo) + 1))
+        cpus &= os.sched_getaffinity(0)
+        if not cpus:
+            return None
+        os.sched_setaffinity(0, cpus)
+        node = -1
+        try:
+            with open(dev + "/numa_node") as f:
+                node = int(f.read().strip())
+        except Exception:
+            pass
+        return {"numa_node": node, "cpus": len(cpus)}
+    except Exception:
+        return None
+
+
 class KvStateSnapshot:
     """The KV bookkeeping tensors of a PagedState (block table, context
     lengths, free stack and top, ref counts) moved into one device buffer,
@@ -204,27 +274,71 @@ class KvStateSnapshot:
         return self.snap[o:o + nb].view(dt).view(sh)
 
 
-# --------------------------------------------------------------------- ours
-def run_ours(args):
+def kv_of(st):
+    from kyro_b200.step import KVState
+    return KVState(st.block_table, st.context_lens, st.free_stack, st.free_top, st.ref_counts,
+                   st.k_cache, st.v_cache)
+
+
+def init_ranks(args, timeout_s=120):
+    """(world, rank, local, device), with the NCCL process group up for N > 1."""
     import torch
     import torch.distributed as dist
-
-    from kyro_b200 import _lib
-    from kyro_b200.verify import (Context, kv_commit, kv_reserve, kv_write, rope_kv_write,
-                                  sample_tokens, spec_accept, verify_attention)
-    from kyro_b200.workloads import CONFIG1, accept_inputs, chain_bytes_per_step, paged_state
-
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
     torch.cuda.set_device(local)
-    if world > 1:
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
     dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=timeout_s),
+                                device_id=dev)
+    return world, rank, local, dev
+
+
+def max_over_ranks(vals, world, dev):
+    import torch
+    import torch.distributed as dist
+    if world == 1:
+        return [float(v) for v in vals]
+    t = torch.tensor([float(v) for v in vals], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(x) for x in t.cpu()]
+
+
+def gather_rows(vals, world, dev):
+    """Every rank's row of floats, on every rank: [world][len(vals)]."""
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([float(v) for v in vals], dtype=torch.float64, device=dev)
+    if world == 1:
+        return [t.cpu().tolist()]
+    out = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [o.cpu().tolist() for o in out]
+
+
+def acceptance_stats(acc, k):
+    """(mean accepted fraction a/k, per-token acceptance rate): the second
+    counts accepted drafts over accept tests run (a test runs at every
+    position up to the first rejection)."""
+    a = acc.detach().cpu().numpy().astype(np.int64)
+    tests = np.where(a < k, a + 1, k)
+    return float(a.mean() / k) if k else 0.0, float(a.sum() / max(1, tests.sum()))
+
+
+# --------------------------------------------------------------------- ours
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    from kyro_b200.step import VerifyStep
+    from kyro_b200.verify import Context, sample_tokens
+    from kyro_b200.workloads import CONFIG1, accept_inputs, chain_bytes_per_step, paged_state
+
+    world, rank, local, dev = init_ranks(args)
+    numa = bind_numa_local(local)
     cfg = CONFIG1
     ctx = Context(local)
     seq_offset = rank * cfg.batch
@@ -237,49 +351,18 @@ def run_ours(args):
                         dtype=torch.bfloat16)
     v_new = torch.randn(cfg.batch, nq, cfg.num_kv_heads, cfg.head_dim, generator=g, device=dev,
                         dtype=torch.bfloat16)
-    attn_out = torch.empty_like(st.q)
-    acc = torch.empty(cfg.batch, dtype=torch.int32, device=dev)
-    toks = torch.empty(cfg.batch, nq, dtype=torch.int32, device=dev)
-    num = torch.empty(cfg.batch, dtype=torch.int32, device=dev)
-    ok = torch.empty(cfg.batch, dtype=torch.int32, device=dev)
-    L = _lib.load()
-    from kyro_b200.verify import attn_params
-    import ctypes as C
-    from kyro_b200._lib import AcceptParams
-    ws_attn = torch.empty(max(256, L.kyro_verify_attention_workspace_size(
-        C.byref(attn_params(st.q, st.k_cache, st.block_table)))), dtype=torch.uint8, device=dev)
-    ws_acc = torch.empty(max(256, L.kyro_spec_accept_workspace_size(C.byref(AcceptParams(
-        cfg.batch, cfg.k, cfg.vocab, 0, cfg.temperature, 0, 0, 0)))), dtype=torch.uint8, device=dev)
-    stream = torch.cuda.current_stream(dev)
-    ev = {n: [] for n in ("attention", "accept")}
     # every step starts from the same KV state, so each step sees the same
     # context lengths; the reset is one device-to-device copy (~0.5 MB)
     kvsnap = KvStateSnapshot(st)
-    restore = kvsnap.restore
+    kv = kv_of(st)
+    vstep = VerifyStep(ctx, cfg.batch, cfg.k, cfg.num_heads, kv, cfg.vocab, cfg.block_size,
+                       temperature=cfg.temperature, seed=0, seq_offset=seq_offset,
+                       rope_theta=10000.0)
+    ev = {}
 
-    def step(i, timed):
-        restore()
-        kv_reserve(ctx, nq, st.block_table, st.context_lens, st.free_stack, st.free_top,
-                   st.ref_counts, cfg.block_size, out_ok=ok)
-        kv_write(ctx, k_new, v_new, st.block_table, st.context_lens, st.k_cache, st.v_cache,
-                 cfg.block_size)
-        if timed:
-            e0 = torch.cuda.Event(enable_timing=True)
-            e0.record()
-        verify_attention(ctx, st.q, st.k_cache, st.v_cache, st.block_table, st.context_lens,
-                         out=attn_out, workspace=ws_attn)
-        if timed:
-            e1 = torch.cuda.Event(enable_timing=True)
-            e1.record()
-        spec_accept(ctx, tgt, drf, drafts, temperature=cfg.temperature, seed=0, step=i,
-                    seq_offset=seq_offset, out=(acc, toks, num, None), workspace=ws_acc)
-        if timed:
-            e2 = torch.cuda.Event(enable_timing=True)
-            e2.record()
-            ev["attention"].append((e0, e1))
-            ev["accept"].append((e1, e2))
-        kv_commit(ctx, nq, acc, st.block_table, st.context_lens, st.free_stack, st.free_top,
-                  st.ref_counts, cfg.block_size)
+    def step(i, events=None):
+        kvsnap.restore()
+        return vstep(kv, st.q, k_new, v_new, tgt, drf, drafts, step=i, events=events)
 
     # the step runs on a side stream as a CUDA graph (captured once after the
     # warm-up steps); the library context is bound to that stream
@@ -288,30 +371,17 @@ def run_ours(args):
     with torch.cuda.stream(side):
         ctx.bind_stream()
         for i in range(args.warmup):
-            step(i, False)
+            step(i)
         if not args.no_graph:
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph, stream=side):
-                step(args.warmup, False)
+                step(args.warmup)
             for _ in range(3):
                 graph.replay()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    phys = local
-    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
-    if vis:
-        ids = [v.strip() for v in vis.split(",")]
-        if local < len(ids) and ids[local].isdigit():
-            phys = int(ids[local])
-    clocks = None
-    if rank == 0:
-        try:
-            clocks = NvmlClockSampler(phys)
-        except Exception:
-            clocks = ClockSampler(phys)
-    if clocks:
-        clocks.start()
+    clocks = start_clocks(rank, local)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -323,53 +393,34 @@ def run_ours(args):
             if graph is not None:
                 graph.replay()
             else:
-                step(i, False)
+                step(i)
         t1.record(side)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     clk = clocks.stop() if clocks else None
-    ms = t0.elapsed_time(t1)
+    ms_rank = t0.elapsed_time(t1)
     # per-kernel times from separate steps with events around attention and
     # acceptance (events between kernels would perturb the timed steps)
     with torch.cuda.stream(side):
         for i in range(PER_KERNEL_STEPS):
-            step(args.warmup + args.steps + i, True)
-        # the fused rotary embedding + paged K/V store on the step's new tokens
-        # (kyro_rope_kv_write, the alternative to kv_write for un-rotated
-        # projections), timed back to back: its ~9 MB stay in L2
-        restore()
-        kv_reserve(ctx, nq, st.block_table, st.context_lens, st.free_stack, st.free_top,
-                   st.ref_counts, cfg.block_size, out_ok=ok)
-        q_rot = torch.empty_like(st.q)
-        for _ in range(3):
-            rope_kv_write(ctx, st.q, k_new, v_new, st.block_table, st.context_lens, st.k_cache,
-                          st.v_cache, cfg.block_size, q_out=q_rot)
-        r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        r0.record()
-        for _ in range(20):
-            rope_kv_write(ctx, st.q, k_new, v_new, st.block_table, st.context_lens, st.k_cache,
-                          st.v_cache, cfg.block_size, q_out=q_rot)
-        r1.record()
+            _, _, acc, _, _ = step(args.warmup + args.steps + i, events=ev)
     torch.cuda.synchronize()
-    rope_us = r0.elapsed_time(r1) / 20 * 1e3
-    rope_bytes = 2.0 * q_rot.numel() * 2 + 4.0 * k_new.numel() * 2
     del graph
     ctx.bind_stream()  # back to the default stream for the end-to-end run
-    if world > 1:
-        tms = torch.tensor([ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(tms, op=dist.ReduceOp.MAX)
-        ms = float(tms.item())
     status = ctx.device_status()
     if status:
         raise SystemExit(f"device status word 0x{status:x} after the timed region")
 
     # algorithmic bytes per step, from the context lengths every step starts from
-    per = [chain_bytes_per_step(kvsnap.initial("context_lens").cpu().numpy(), cfg)]
-    att_ms = np.mean([a.elapsed_time(b) for a, b in ev["attention"]])
-    acc_ms = np.mean([a.elapsed_time(b) for a, b in ev["accept"]])
-    att_bytes = float(np.mean([p["attention"] for p in per]))
-    acc_bytes = float(np.mean([p["accept"] for p in per]))
+    lens0 = kvsnap.initial("context_lens").cpu().numpy()
+    per = chain_bytes_per_step(lens0, cfg, rope=True)
+    att_ms = float(np.mean([a.elapsed_time(b) for a, b in ev["attention"]]))
+    acc_ms = float(np.mean([a.elapsed_time(b) for a, b in ev["accept"]]))
+    rows = gather_rows([rank, int(lens0.sum()), per["attention"], per["accept"], att_ms, acc_ms,
+                        ms_rank / args.steps], world, dev)
+    ms = max(r[6] for r in rows) * args.steps
+    att_bytes, acc_bytes = float(per["attention"]), float(per["accept"])
     peak, peak_kind = load_peaks()
     traffic = load_traffic()
     if att_ms >= acc_ms:
@@ -379,11 +430,8 @@ def run_ours(args):
     achieved = dbytes / (dms * 1e-3) / 1e9
     units = cfg.batch * nq * world * args.steps
     value = units / (ms * 1e-3)
-    step_bytes = att_bytes + acc_bytes
-    # kv_reserve, kv_write, verify_attention, accept_stats, accept_decide,
-    # accept_final, kv_commit (the attention split counters are zeroed by a
-    # driver memset only the first time a workspace is used)
-    launches_per_step = 7
+    step_bytes = float(per["total"])
+    frac_acc, per_token = acceptance_stats(acc, cfg.k)
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
@@ -400,50 +448,51 @@ def run_ours(args):
             "accept": {"ms": acc_ms, "algorithmic_bytes": acc_bytes,
                        "GBps": acc_bytes / (acc_ms * 1e-3) / 1e9,
                        "frac": acc_bytes / (acc_ms * 1e-3) / 1e9 / peak},
+            "step_algorithmic_bytes": step_bytes,
             "step_frac_of_hbm": step_bytes / (ms / args.steps * 1e-3) / 1e9 / peak,
-            "rope_kv_write": {"us": rope_us, "bytes": rope_bytes,
-                              "GBps": rope_bytes / (rope_us * 1e-6) / 1e9,
-                              "note": "outside the step; back-to-back launches, L2-resident"},
         },
         "timing": "CUDA graph replays of the step" if not args.no_graph else "stream launches",
-        "acceptance_rate": float(acc.float().mean().item() / cfg.k),
-        "gpu_launches": launches_per_step * args.steps,
+        "mean_accepted_fraction": frac_acc,
+        "per_token_acceptance": per_token,
+        "gpu_launches": vstep.launches() * args.steps,
         "clocks": clk,
     }
+    if world > 1:
+        slow = max(rows, key=lambda r: r[6])
+        line["per_rank"] = {
+            "fields": ["rank", "context_tokens", "attention_bytes", "accept_bytes", "attention_ms",
+                       "accept_ms", "step_ms"],
+            "rows": rows,
+            "slowest_rank": int(slow[0]), "slowest_context_tokens": int(slow[1]),
+            "note": "each rank draws its own contexts (seed 1000 + rank); the job's step time is "
+                    "the slowest rank's"}
+        line["config"]["attention_bytes_all_ranks"] = sum(r[2] for r in rows)
     if not args.no_e2e:
-        line["e2e"] = run_e2e(args, ctx, cfg, st, tgt, drf, drafts, k_new, v_new, seq_offset,
-                              world, dist if world > 1 else None, dev, restore)
+        line["e2e"] = run_e2e(args, ctx, cfg, st, kv, vstep, tgt, drf, drafts, k_new, v_new,
+                              world, dev, kvsnap.restore, numa)
+    if not args.no_extras:
+        line["extras"] = run_extras(args, ctx, world, rank, local, dev)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cfg, st, tgt, drf, drafts, k_new, v_new, args)
     if rank == 0:
         print(json.dumps(line), flush=True)
+    ctx.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
 
 
-def _attn_splits(st, cfg):
-    import ctypes as C
-    from kyro_b200 import _lib
-    from kyro_b200.verify import attn_params
-    p = attn_params(st.q, st.k_cache, st.block_table)
-    return _lib.load().kyro_verify_attention_workspace_size(C.byref(p)) > 0
-
-
-def run_e2e(args, ctx, cfg, st, tgt, drf, drafts, k_new, v_new, seq_offset, world, dist, dev,
-            restore):
-    """The same step through the C ABI with host buffers: inputs copied from
-    pinned host memory each step, results read back each step."""
+def run_e2e(args, ctx, cfg, st, kv, vstep, tgt, drf, drafts, k_new, v_new, world, dev, restore,
+            numa):
+    """The same step through the public step API with host buffers: inputs
+    copied from pinned host memory each step, results read back each step."""
     import torch
-    from kyro_b200.verify import kv_commit, kv_reserve, kv_write, spec_accept, verify_attention
-    nq = cfg.num_query
     h = {n: t.cpu().pin_memory() for n, t in
          dict(q=st.q, k_new=k_new, v_new=v_new, tgt=tgt, drf=drf, drafts=drafts).items()}
     d = {n: torch.empty_like(t, device=dev) for n, t in h.items()}
+    nq = cfg.num_query
     out_h = {n: torch.empty(s, dtype=torch.int32).pin_memory()
              for n, s in dict(acc=(cfg.batch,), toks=(cfg.batch, nq), num=(cfg.batch,)).items()}
-    out_d = {n: torch.empty(t.shape, dtype=torch.int32, device=dev) for n, t in out_h.items()}
-    attn_out = torch.empty_like(st.q)
     stream = torch.cuda.current_stream(dev)
     h2d = sum(t.numel() * t.element_size() for t in h.values())
     d2h = sum(t.numel() * t.element_size() for t in out_h.values())
@@ -453,24 +502,17 @@ def run_e2e(args, ctx, cfg, st, tgt, drf, drafts, k_new, v_new, seq_offset, worl
         restore()
         for n in h:
             d[n].copy_(h[n], non_blocking=True)
-        kv_reserve(ctx, nq, st.block_table, st.context_lens, st.free_stack, st.free_top,
-                   st.ref_counts, cfg.block_size)
-        kv_write(ctx, d["k_new"], d["v_new"], st.block_table, st.context_lens, st.k_cache,
-                 st.v_cache, cfg.block_size)
-        verify_attention(ctx, d["q"], st.k_cache, st.v_cache, st.block_table, st.context_lens,
-                         out=attn_out)
-        spec_accept(ctx, d["tgt"], d["drf"], d["drafts"], temperature=cfg.temperature, seed=0,
-                    step=1000 + i, seq_offset=seq_offset,
-                    out=(out_d["acc"], out_d["toks"], out_d["num"], None))
-        kv_commit(ctx, nq, out_d["acc"], st.block_table, st.context_lens, st.free_stack,
-                  st.free_top, st.ref_counts, cfg.block_size)
-        for n in out_h:
-            out_h[n].copy_(out_d[n], non_blocking=True)
+        _, _, acc, toks, num = vstep(kv, d["q"], d["k_new"], d["v_new"], d["tgt"], d["drf"],
+                                     d["drafts"], step=1000 + i)
+        out_h["acc"].copy_(acc, non_blocking=True)
+        out_h["toks"].copy_(toks, non_blocking=True)
+        out_h["num"].copy_(num, non_blocking=True)
         stream.synchronize()  # the caller reads the emitted tokens
 
     step(0)
     torch.cuda.synchronize()
-    if dist:
+    if world > 1:
+        import torch.distributed as dist
         dist.barrier()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
@@ -479,139 +521,83 @@ def run_e2e(args, ctx, cfg, st, tgt, drf, drafts, k_new, v_new, seq_offset, worl
         step(1 + i)
     t1.record(stream)
     torch.cuda.synchronize()
-    ms = t0.elapsed_time(t1)
-    if dist:
-        tms = torch.tensor([ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(tms, op=dist.ReduceOp.MAX)
-        ms = float(tms.item())
+    ms_rank = t0.elapsed_time(t1)
+    rows = gather_rows([ms_rank / steps, h2d / (ms_rank / steps * 1e-3) / 1e9], world, dev)
+    ms = max(r[0] for r in rows) * steps
     value = cfg.batch * nq * world * steps / (ms * 1e-3)
-    return {"value": value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "steps": steps, "ms_per_step": ms / steps}
+    out = {"value": value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+           "steps": steps, "ms_per_step": ms / steps,
+           "h2d_GBps_per_rank": [r[1] for r in rows],
+           "h2d_GBps_all_ranks": h2d * world / (ms / steps * 1e-3) / 1e9,
+           "limit": "the logits (366 MB per step and rank) cross the host link and host memory; "
+                    "with N ranks the host's memory bandwidth is shared",
+           "host_binding": numa}
+    return out
 
 
-# ------------------------------------------------------------------ CPU side
-def _cpu_step(O, cfg, inp, seqs, step, nthreads):
-    """The reference path's verify step on host cores for the sequences in
-    `seqs`: KV write, attention, acceptance, commit (oracle restatement)."""
-    sel = np.asarray(seqs)
-    nq = cfg.num_query
-    bt, cl = inp["bt"][sel].copy(), inp["cl"][sel].copy()
-    fs, top, rc = inp["fs"].copy(), inp["top"].copy(), inp["rc"].copy()
-    O.kv_reserve(nq, bt, cl, fs, top, rc, cfg.block_size)
-    O.kv_write(inp["k_new"][sel], inp["v_new"][sel], bt, cl, inp["kc"], inp["vc"],
-               cfg.block_size)
-    O.paged_attention(inp["q"][sel], inp["kc"], inp["vc"], bt, cl, cfg.block_size,
-                      nthreads=nthreads)
-    acc, _, _, _ = O.spec_accept(inp["tgt"][sel], inp["drf"][sel], inp["drafts"][sel],
-                                 temperature=cfg.temperature, seed=0, step=step,
-                                 nthreads=nthreads)
-    O.kv_commit(nq, acc, bt, cl, fs, top, rc, cfg.block_size)
+# ------------------------------------------------------------------ extras
+def run_extras(args, ctx, world, rank, local, dev):
+    """Configs 0, 2 and 3 on the same ranks, each with its own short timed
+    region (max over ranks).  Every rank takes the same collective steps."""
+    out = {}
+    out["config0"] = extra_config0(ctx, world, dev)
+    out["config2"] = tree_measure(ctx, world, rank, dev, steps=args.extra_steps, warmup=3)
+    out["tp_accept"] = tp_measure(world, rank, local, dev, steps=args.extra_steps, warmup=3)
+    return out
 
 
-def _host_inputs(st, tgt, drf, drafts, k_new, v_new):
-    from kyro_b200.workloads import bf16_bits
-    return {"q": bf16_bits(st.q), "kc": bf16_bits(st.k_cache), "vc": bf16_bits(st.v_cache),
-            "bt": st.block_table.cpu().numpy(), "cl": st.context_lens.cpu().numpy(),
-            "fs": st.free_stack.cpu().numpy(), "top": st.free_top.cpu().numpy(),
-            "rc": st.ref_counts.cpu().numpy(), "tgt": tgt.cpu().numpy(),
-            "drf": drf.cpu().numpy(), "drafts": drafts.cpu().numpy(),
-            "k_new": bf16_bits(k_new), "v_new": bf16_bits(v_new)}
-
-
-def cpu_baseline(cfg, st, tgt, drf, drafts, k_new, v_new, args):
-    """The oracle's verify step over the whole config-1 batch on the host
-    cores, repeated for about ten seconds."""
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle as O
-    O.build()
-    inp = _host_inputs(st, tgt, drf, drafts, k_new, v_new)
-    nthreads = os.cpu_count() or 1
-    seqs = list(range(cfg.batch))
-    done, t0 = 0, time.perf_counter()
-    while True:
-        _cpu_step(O, cfg, inp, seqs, done, nthreads)
-        done += 1
-        dt = time.perf_counter() - t0
-        if dt > args.cpu_seconds or done >= 50:
-            break
-    return {"value": done * len(seqs) * cfg.num_query / dt, "unit": UNIT, "cores": nthreads,
-            "kind": "port",
-            "sample": f"{done} verify steps over the full config-1 batch ({cfg.batch} sequences: "
-                      f"kv write + attention + accept + commit), {dt:.1f} s"}
-
-
-def run_reference(args):
-    """CPU restatement of the reference path on the host cores, same config."""
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
-        return
+def extra_config0(ctx, world, dev, steps=200):
+    """Config 0: acceptance only (B 8, k 4, V 32000, T 1.0), CUDA graph
+    replays.  9.2 MB per call: launch-bound, reported as such."""
     import torch
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle as O
-    O.build()
-    from kyro_b200.workloads import CONFIG1, accept_inputs, paged_state
-    cfg = CONFIG1
-    st = paged_state(cfg, "cpu", seed=1000)
-    tgt, drf = accept_inputs(cfg.batch, cfg.k, cfg.vocab, "cpu", seed=2000)
-    drafts, _ = O.sample_tokens(drf.numpy(), cfg.temperature, seed=0, nthreads=os.cpu_count())
-    g = torch.Generator().manual_seed(3000)
-    shape = (cfg.batch, cfg.num_query, cfg.num_kv_heads, cfg.head_dim)
-    k_new = torch.randn(shape, generator=g).to(torch.bfloat16)
-    v_new = torch.randn(shape, generator=g).to(torch.bfloat16)
-    inp = _host_inputs(st, tgt, drf, torch.from_numpy(drafts), k_new, v_new)
-    nthreads = os.cpu_count() or 1
-    sample = min(cfg.batch, args.cpu_sample)
-    for i in range(args.warmup):
-        _cpu_step(O, cfg, inp, list(range(sample)), i, nthreads)
-    times = []
-    for i in range(args.steps):
-        seqs = [(i * sample + j) % cfg.batch for j in range(sample)]
-        t = time.perf_counter()
-        _cpu_step(O, cfg, inp, seqs, args.warmup + i, nthreads)
-        times.append(time.perf_counter() - t)
-    total = sum(times)
-    value = sample * cfg.num_query * args.steps / total
-    line = {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": total / args.steps * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
-        "data": "synthetic (seeded; BASELINE config 1 shapes and distributions)",
-        "config": workload_desc(cfg, 1), "impl": "reference",
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": nthreads, "kind": "port",
-                         "sample": f"{sample} of {cfg.batch} config-1 sequences per step"},
-        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }
-    print(json.dumps(line), flush=True)
+    from kyro_b200.verify import sample_tokens, spec_accept
+    from kyro_b200.workloads import CONFIG0, accept_inputs
+    B, k, V = CONFIG0["batch"], CONFIG0["k"], CONFIG0["vocab"]
+    tgt, drf = accept_inputs(B, k, V, dev, seed=0)
+    drafts, _ = sample_tokens(ctx, drf, 1.0, seed=0)
+    acc = torch.empty(B, dtype=torch.int32, device=dev)
+    toks = torch.empty(B, k + 1, dtype=torch.int32, device=dev)
+    num = torch.empty(B, dtype=torch.int32, device=dev)
+    side = torch.cuda.Stream(dev)
+    with torch.cuda.stream(side):
+        ctx.bind_stream()
+        for i in range(3):
+            spec_accept(ctx, tgt, drf, drafts, seed=0, step=i, out=(acc, toks, num, None))
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            for i in range(10):  # ten calls per replay
+                spec_accept(ctx, tgt, drf, drafts, seed=0, step=i, out=(acc, toks, num, None))
+        graph.replay()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(side):
+        t0.record(side)
+        for _ in range(steps // 10):
+            graph.replay()
+        t1.record(side)
+    torch.cuda.synchronize()
+    del graph
+    ctx.bind_stream()
+    us = max_over_ranks([t0.elapsed_time(t1) / steps * 1e3], world, dev)[0]
+    bytes_ = (2 * k + 1) * V * 4 * B
+    return {"workload": "config0: acceptance only, B 8, k 4, V 32000, T 1.0 (per rank)",
+            "us_per_call": us, "positions_per_s": B * (k + 1) * world / (us * 1e-6),
+            "GBps": bytes_ / (us * 1e-6) / 1e9, "algorithmic_bytes": bytes_,
+            "timing": "CUDA graph of 10 back-to-back calls, max over ranks",
+            "bound": "launch latency (9.2 MB per call)"}
 
 
-def run_tree(args):
-    """Config 2: tree verification.  Per step and GPU (batch-sharded, no
-    collective): KV reserve and write of the 64 tree nodes, paged attention
-    of 64 query heads over 8 KV heads (context 8192) under the ancestor mask,
-    multi-candidate acceptance over vocabulary 32000, and the tree commit of
-    the accepted path."""
-    import datetime
-
+def tree_measure(ctx, world, rank, dev, steps, warmup):
+    """Config 2 on this rank (batch-sharded): KV reserve and write of the 64
+    tree nodes, paged attention of 64 query heads over 8 KV heads (context
+    8192) under the ancestor mask, multi-candidate acceptance over vocabulary
+    32000, and the tree commit of the accepted path."""
     import torch
-    import torch.distributed as dist
-
-    from kyro_b200.verify import (Context, kv_commit_tree, kv_reserve, kv_write,
-                                  spec_accept_tree, verify_attention)
+    from kyro_b200.verify import (kv_commit_tree, kv_reserve, kv_write, spec_accept_tree,
+                                  verify_attention)
     from kyro_b200.workloads import CONFIG2, bfs_tree, paged_state, tree_mask_bits
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world != args.gpus:
-        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     cfg = CONFIG2
     B, N, V = cfg.batch, cfg.num_query, cfg.vocab
-    ctx = Context(local)
     st = paged_state(cfg, dev, seed=8000 + rank)
     par = bfs_tree(N)
     pars = torch.from_numpy(np.broadcast_to(par[None], (B, N)).copy()).to(dev)
@@ -632,6 +618,7 @@ def run_tree(args):
     kvsnap = KvStateSnapshot(st)
     stream = torch.cuda.current_stream(dev)
     ev = {"attention": [], "accept": []}
+    ctx.bind_stream()
 
     def step(i, timed):
         kvsnap.restore()
@@ -658,79 +645,343 @@ def run_tree(args):
                        st.context_lens, st.free_stack, st.free_top, st.ref_counts, cfg.block_size)
         return plen
 
-    for i in range(args.warmup):
+    for i in range(warmup):
         step(i, False)
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    clocks = None
-    if rank == 0:
-        try:
-            clocks = NvmlClockSampler(local)
-        except Exception:
-            clocks = ClockSampler(local)
-        clocks.start()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record(stream)
-    plens = []
-    for i in range(args.warmup, args.warmup + args.steps):
-        plens.append(step(i, False))
+    plens = [step(i, False) for i in range(warmup, warmup + steps)]
     t1.record(stream)
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    clk = clocks.stop() if clocks else None
     ms = t0.elapsed_time(t1)
     # per-kernel times from separate steps, so that no event sits between the
     # chained launches of the timed ones
-    for i in range(args.warmup + args.steps, args.warmup + args.steps + PER_KERNEL_STEPS):
+    for i in range(warmup + steps, warmup + steps + PER_KERNEL_STEPS):
         step(i, True)
     torch.cuda.synchronize()
     att_ms = float(np.mean([a.elapsed_time(b) for a, b in ev["attention"]]))
     acc_ms = float(np.mean([a.elapsed_time(b) for a, b in ev["accept"]]))
-    if world > 1:
-        t = torch.tensor([ms, att_ms, acc_ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, att_ms, acc_ms = float(t[0]), float(t[1]), float(t[2])
+    ms, att_ms, acc_ms = max_over_ranks([ms, att_ms, acc_ms], world, dev)
     status = ctx.device_status()
     if status:
-        raise SystemExit(f"device status word 0x{status:x} after the timed region")
-    peak, peak_kind = load_peaks()
+        raise SystemExit(f"device status word 0x{status:x} after the config-2 steps")
+    peak, _ = load_peaks()
     kv_bytes = B * (cfg.ctx_max + N) * 2 * cfg.num_kv_heads * cfg.head_dim * 2
     flops = 4.0 * B * cfg.num_heads * N * cfg.head_dim * (cfg.ctx_max + N)
     acc_bytes = 2 * B * N * V * 4
-    mean_path = float(torch.stack(plens).float().mean().item())
+    tpk = None
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            tpk = float(json.load(f)["bf16_tflops"])
+    except Exception:
+        tpk = 1590.0
+    return {
+        "workload": "config2: tree verify (paged attention under a 64-node ancestor mask + "
+                    "multi-candidate acceptance + tree commit), Hq64/Hkv8/D128 bf16, ctx 8192, "
+                    "tree 4,4,4 cut to 64, V 32000 fp32, T 1.0, B 32 per rank",
+        "nodes_per_s": B * N * world * steps / (ms * 1e-3), "ms_per_step": ms / steps,
+        "steps": steps, "mean_path_len": float(torch.stack(plens).float().mean().item()),
+        "attention": {"ms": att_ms, "TFLOPs": flops / (att_ms * 1e-3) / 1e12,
+                      "tensor_frac_of_burst": flops / (att_ms * 1e-3) / 1e12 / tpk,
+                      "kv_GBps": kv_bytes / (att_ms * 1e-3) / 1e9, "flops": flops},
+        "accept": {"ms": acc_ms, "bytes": acc_bytes, "GBps": acc_bytes / (acc_ms * 1e-3) / 1e9,
+                   "hbm_frac": acc_bytes / (acc_ms * 1e-3) / 1e9 / peak},
+        "timing": "stream launches, max over ranks",
+    }
+
+
+def _tp_parity(ctx, world, rank, dev):
+    """The sharded kernels on this group against the oracle's outputs for
+    num_shards = world (tests/golden/tp_accept_golden.json): True iff every
+    case matches bit for bit on this rank."""
+    import torch
+    from kyro_b200.verify import spec_accept, spec_accept_tp
+    sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
+    from make_tp_golden import inputs
+    with open(TP_GOLDEN) as f:
+        fixture = json.load(f)
+    ok = True
+    for case in fixture["cases"]:
+        B, k, V, mode, T, seed = (case[n] for n in ("B", "k", "V", "mode", "T", "seed"))
+        want = case["shards"].get(str(world))
+        if want is None:
+            return None
+        tgt, drf = inputs(B, k, V, seed)
+        Vs = V // world
+        ts = torch.from_numpy(tgt[:, :, rank * Vs:(rank + 1) * Vs].copy()).to(dev)
+        ds = torch.from_numpy(drf[:, :, rank * Vs:(rank + 1) * Vs].copy()).to(dev)
+        drafts = torch.tensor(case["drafts"], dtype=torch.int32).reshape(B, k).to(dev)
+        if world == 1:
+            acc, toks, num, probs = spec_accept(ctx, ts, ds if mode == 0 else None, drafts,
+                                                mode=mode, temperature=T, seed=seed,
+                                                want_probs=mode == 0)
+        else:
+            acc, toks, num, probs = spec_accept_tp(ctx, ts, ds if mode == 0 else None, drafts, V,
+                                                   mode=mode, temperature=T, seed=seed,
+                                                   want_probs=mode == 0)
+        torch.cuda.synchronize(dev)
+        ok &= acc.cpu().tolist() == want["accept_len"]
+        ok &= toks.cpu().tolist() == want["tokens"]
+        ok &= num.cpu().tolist() == want["num_tokens"]
+        if mode == 0:
+            ok &= probs.cpu().numpy().view(np.uint32).tolist() == want["probs_bits"]
+    return bool(ok)
+
+
+def tp_measure(world, rank, local, dev, steps, warmup):
+    """Config 3 over the N ranks as one tensor-parallel group: parity against
+    the golden fixture, then the timed step (acceptance of B 256 x k 8 over
+    V 128256 split N ways, plus KV reserve/commit on a 32768-block table) for
+    each exchange transport.  At N = 1: the single-GPU acceptance of the
+    same rows."""
+    import torch
+    import torch.distributed as dist
+    from kyro_b200.verify import Context, kv_commit, kv_reserve, spec_accept_tp, tp_unique_id
+    from kyro_b200.workloads import CONFIG3, paged_state
+    cfg = CONFIG3
+    B, k, V, T = cfg.batch, cfg.k, cfg.vocab, cfg.temperature
+    Vs = V // world
+    transports = ["single"] if world == 1 else ["peer", "nccl"]
+    res = {"workload": f"config3: vocabulary-sharded acceptance (B 256, k 8, V 128256 over "
+                       f"{world} rank(s), T 0.8) + KV reserve/commit on a 32768-block table",
+           "columns_per_rank": Vs, "scaling": "strong (the same rows split over the ranks)"}
+
+    def shard(r):  # rank r's columns of the (never materialised) full logits
+        g = torch.Generator(device=dev).manual_seed(5000 + r)
+        t = torch.randn(B, k + 1, Vs, generator=g, device=dev) * cfg.logit_std
+        d = t[:, :k, :] + torch.randn(B, k, Vs, generator=g, device=dev) * cfg.draft_noise
+        return t.contiguous(), d.contiguous()
+
+    tgt, drf = shard(rank)
+    drafts = torch.zeros(B, k, dtype=torch.int32, device=dev)
     if rank == 0:
-        line = {
+        full = torch.cat([shard(r)[1] for r in range(world)], dim=2)
+        g = torch.Generator(device=dev).manual_seed(6000)
+        probs = torch.softmax(full.reshape(B * k, V) / T, dim=1)
+        drafts.copy_(torch.multinomial(probs, 1, generator=g).reshape(B, k).int())
+        del full, probs
+    if world > 1:
+        dist.broadcast(drafts, 0)
+    st = paged_state(cfg, dev, seed=7000, fill_cache=False)
+    kvsnap = KvStateSnapshot(st)
+    nq = k + 1
+    ok = torch.empty(B, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    peak, _ = load_peaks()
+    rank_bytes = (2 * k + 1) * B * Vs * 4
+    for tr in transports:
+        prev = os.environ.get("KYRO_TP_TRANSPORT")
+        ctx = Context(local)
+        try:
+            if world > 1:
+                if tr == "nccl":
+                    os.environ["KYRO_TP_TRANSPORT"] = "nccl"
+                uid = torch.zeros(128, dtype=torch.uint8, device=dev)
+                if rank == 0:
+                    uid.copy_(torch.frombuffer(bytearray(tp_unique_id()), dtype=torch.uint8))
+                dist.broadcast(uid, 0)
+                ctx.tp_init(bytes(uid.cpu().numpy().tobytes()), rank, world)
+        finally:
+            if prev is None:
+                os.environ.pop("KYRO_TP_TRANSPORT", None)
+            else:
+                os.environ["KYRO_TP_TRANSPORT"] = prev
+        got = ctx.tp_transport if world > 1 else "none"
+        parity = _tp_parity(ctx, world, rank, dev)
+        # every rank's verdict, combined with a collective all ranks take
+        flags = torch.tensor([0 if parity is None else (1 if parity else 2)], device=dev)
+        if world > 1:
+            dist.all_reduce(flags, op=dist.ReduceOp.MAX)
+        parity_ok = {0: None, 1: True, 2: False}[int(flags.item())]
+        ev = []
+
+        def step(i, timed):
+            kvsnap.restore()
+            kv_reserve(ctx, nq, st.block_table, st.context_lens, st.free_stack, st.free_top,
+                       st.ref_counts, cfg.block_size, out_ok=ok)
+            if timed:
+                e0 = torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+            acc, _, _, _ = spec_accept_tp(ctx, tgt, drf, drafts, V, temperature=T, seed=0, step=i)
+            if timed:
+                e1 = torch.cuda.Event(enable_timing=True)
+                e1.record(stream)
+                ev.append((e0, e1))
+            kv_commit(ctx, nq, acc, st.block_table, st.context_lens, st.free_stack, st.free_top,
+                      st.ref_counts, cfg.block_size)
+            return acc
+
+        ctx.bind_stream()
+        for i in range(warmup):
+            step(i, False)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for i in range(warmup, warmup + steps):
+            acc = step(i, False)
+        t1.record(stream)
+        torch.cuda.synchronize()
+        ms = t0.elapsed_time(t1)
+        for i in range(PER_KERNEL_STEPS):
+            step(warmup + steps + i, True)
+        torch.cuda.synchronize()
+        acc_ms = float(np.mean([a.elapsed_time(b) for a, b in ev]))
+        ms, acc_ms = max_over_ranks([ms, acc_ms], world, dev)
+        status = ctx.device_status()
+        ctx.close()
+        if world > 1:
+            dist.barrier()
+        res[tr] = {"transport": got, "parity_ok": parity_ok, "ms_per_step": ms / steps,
+                   "accept_ms": acc_ms, "positions_per_s": B * nq * steps / (ms * 1e-3),
+                   "per_rank_GBps": rank_bytes / (acc_ms * 1e-3) / 1e9,
+                   "frac_hbm_per_rank": rank_bytes / (acc_ms * 1e-3) / 1e9 / peak,
+                   "device_status": status}
+    res["parity_ok"] = all(res[t]["parity_ok"] for t in transports)
+    return res
+
+
+# ------------------------------------------------------------------ CPU side
+def _host_inputs(st, tgt, drf, drafts, k_new, v_new):
+    from kyro_b200.workloads import bf16_bits
+    return {"q": bf16_bits(st.q), "k_cache": bf16_bits(st.k_cache),
+            "v_cache": bf16_bits(st.v_cache), "block_table": st.block_table.cpu().numpy(),
+            "context_lens": st.context_lens.cpu().numpy(), "free_stack": st.free_stack.cpu().numpy(),
+            "free_top": st.free_top.cpu().numpy(), "ref_counts": st.ref_counts.cpu().numpy(),
+            "tgt": tgt.cpu().numpy(), "drf": drf.cpu().numpy(), "drafts": drafts.cpu().numpy(),
+            "k_new": bf16_bits(k_new), "v_new": bf16_bits(v_new)}
+
+
+def _cpu_step(O, cfg, inp, seqs, step, nthreads):
+    """The reference path's verify step on host cores for the sequences in
+    `seqs` (oracle restatement, composed as the GPU step is)."""
+    sel = np.asarray(seqs)
+    state = {"block_table": inp["block_table"][sel].copy(),
+             "context_lens": inp["context_lens"][sel].copy(),
+             "free_stack": inp["free_stack"].copy(), "free_top": inp["free_top"].copy(),
+             "ref_counts": inp["ref_counts"].copy(), "k_cache": inp["k_cache"],
+             "v_cache": inp["v_cache"]}
+    O.verify_step(state, inp["q"][sel], inp["k_new"][sel], inp["v_new"][sel], inp["tgt"][sel],
+                  inp["drf"][sel], inp["drafts"][sel], cfg.block_size,
+                  temperature=cfg.temperature, seed=0, step=step, rope_theta=10000.0,
+                  nthreads=nthreads)
+
+
+def cpu_baseline(cfg, st, tgt, drf, drafts, k_new, v_new, args):
+    """The oracle's verify step over the whole config-1 batch on the host
+    cores, repeated for about ten seconds."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    O.build()
+    inp = _host_inputs(st, tgt, drf, drafts, k_new, v_new)
+    nthreads = len(os.sched_getaffinity(0)) or 1
+    seqs = list(range(cfg.batch))
+    done, t0 = 0, time.perf_counter()
+    while True:
+        _cpu_step(O, cfg, inp, seqs, done, nthreads)
+        done += 1
+        dt = time.perf_counter() - t0
+        if dt > args.cpu_seconds or done >= 50:
+            break
+    return {"value": done * len(seqs) * cfg.num_query / dt, "unit": UNIT, "cores": nthreads,
+            "kind": "port",
+            "sample": f"{done} verify steps over the full config-1 batch ({cfg.batch} sequences: "
+                      f"RoPE + kv write + attention + accept + commit), {dt:.1f} s"}
+
+
+def run_reference(args):
+    """CPU restatement of the reference path on the host cores, same config."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import torch
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    O.build()
+    from kyro_b200.workloads import CONFIG1, accept_inputs, paged_state
+    cfg = CONFIG1
+    st = paged_state(cfg, "cpu", seed=1000)
+    tgt, drf = accept_inputs(cfg.batch, cfg.k, cfg.vocab, "cpu", seed=2000)
+    nthreads = os.cpu_count() or 1
+    drafts, _ = O.sample_tokens(drf.numpy(), cfg.temperature, seed=0, nthreads=nthreads)
+    g = torch.Generator().manual_seed(3000)
+    shape = (cfg.batch, cfg.num_query, cfg.num_kv_heads, cfg.head_dim)
+    k_new = torch.randn(shape, generator=g).to(torch.bfloat16)
+    v_new = torch.randn(shape, generator=g).to(torch.bfloat16)
+    inp = _host_inputs(st, tgt, drf, torch.from_numpy(drafts), k_new, v_new)
+    sample = min(cfg.batch, args.cpu_sample)
+    for i in range(args.warmup):
+        _cpu_step(O, cfg, inp, list(range(sample)), i, nthreads)
+    times = []
+    for i in range(args.steps):
+        seqs = [(i * sample + j) % cfg.batch for j in range(sample)]
+        t = time.perf_counter()
+        _cpu_step(O, cfg, inp, seqs, args.warmup + i, nthreads)
+        times.append(time.perf_counter() - t)
+    total = sum(times)
+    value = sample * cfg.num_query * args.steps / total
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": total / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic (seeded; BASELINE config 1 shapes and distributions)",
+        "config": workload_desc(cfg, 1), "impl": "reference",
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": nthreads, "kind": "port",
+                         "sample": f"{sample} of {cfg.batch} config-1 sequences per step"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------- standalone configs
+def run_tree(args):
+    """--config 2: the tree verify step alone, with its own JSON line."""
+    import torch.distributed as dist
+    from kyro_b200.verify import Context
+    world, rank, local, dev = init_ranks(args)
+    ctx = Context(local)
+    clocks = start_clocks(rank, local)
+    r = tree_measure(ctx, world, rank, dev, steps=args.steps, warmup=args.warmup)
+    clk = clocks.stop() if clocks else None
+    if rank == 0:
+        print(json.dumps({
             "metric": "spec-verify tree nodes/s (config 2)", "unit": "verified tree nodes/s",
-            "value": B * N * world * args.steps / (ms * 1e-3), "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "value": r["nodes_per_s"], "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded; BASELINE config 2 shapes and distributions)",
-            "config": {"workload": "config2: tree verify (paged attention under a 64-node "
-                                   "ancestor mask + multi-candidate acceptance + tree commit), "
-                                   "Hq64/Hkv8/D128 bf16, ctx 8192, tree 4,4,4 cut to 64, "
-                                   "V 32000 fp32, T 1.0",
-                       "batch_per_gpu": B, "global_batch": B * world, "nodes": N,
-                       "parallelism": f"batch-sharded x{world} (no collective)"},
-            "kernels": {
-                "attention": {"ms": att_ms, "kv_bytes": kv_bytes, "flops": flops,
-                              "GBps": kv_bytes / (att_ms * 1e-3) / 1e9,
-                              "hbm_frac": kv_bytes / (att_ms * 1e-3) / 1e9 / peak,
-                              "TFLOPs": flops / (att_ms * 1e-3) / 1e12},
-                "accept": {"ms": acc_ms, "bytes": acc_bytes,
-                           "GBps": acc_bytes / (acc_ms * 1e-3) / 1e9,
-                           "hbm_frac": acc_bytes / (acc_ms * 1e-3) / 1e9 / peak},
-            },
-            "mean_path_len": mean_path,
-            "clocks": clk,
-        }
-        print(json.dumps(line), flush=True)
+            "config": {"workload": r["workload"], "parallelism": f"batch-sharded x{world}"},
+            "kernels": {"attention": r["attention"], "accept": r["accept"]},
+            "mean_path_len": r["mean_path_len"], "clocks": clk}), flush=True)
     ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_tp(args):
+    """--config 3: the vocabulary-sharded acceptance alone, with its own line."""
+    import torch.distributed as dist
+    world, rank, local, dev = init_ranks(args)
+    if 128256 % world:
+        raise SystemExit(f"vocab 128256 does not split over {world} ranks")
+    clocks = start_clocks(rank, local)
+    r = tp_measure(world, rank, local, dev, steps=args.steps, warmup=args.warmup)
+    clk = clocks.stop() if clocks else None
+    if rank == 0:
+        best = min((r[t] for t in ("single", "peer", "nccl") if t in r),
+                   key=lambda x: x["ms_per_step"])
+        print(json.dumps({
+            "metric": "TP spec-accept verified positions/s (config 3)", "unit": UNIT,
+            "value": best["positions_per_s"], "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": best["ms_per_step"], "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded; BASELINE config 3 shapes and distributions)",
+            "config": {"workload": r["workload"], "parallelism": f"tp{world} (vocabulary)"},
+            "tp_accept": r, "clocks": clk}), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -764,8 +1015,6 @@ def run_e2e_model(args):
     collective); every step drafts k = 4 tokens per request, verifies k + 1
     positions through the target, accepts, and commits, with the contexts
     growing from step to step.  Timed as CUDA graph replays of one step."""
-    import datetime
-
     import torch
     import torch.distributed as dist
 
@@ -773,15 +1022,7 @@ def run_e2e_model(args):
     from kyro_b200.verify import Context
     from kyro_b200.workloads import ChainConfig, paged_state
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world != args.gpus:
-        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    world, rank, local, dev = init_ranks(args, timeout_s=300)
     cfg, shape = CONFIG4, CONFIG4_SHAPE
     if args.requests or args.target_layers:
         # a smaller case of the same step, for profiler captures (not a bench line)
@@ -816,13 +1057,7 @@ def run_e2e_model(args):
     lens0 = kv.context_lens.cpu().numpy().copy()
     if world > 1:
         dist.barrier()
-    clocks = None
-    if rank == 0:
-        try:
-            clocks = NvmlClockSampler(local)
-        except Exception:
-            clocks = ClockSampler(local)
-        clocks.start()
+    clocks = start_clocks(rank, local)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -924,152 +1159,6 @@ def run_e2e_model(args):
         dist.destroy_process_group()
 
 
-def run_tp(args):
-    """Config 3: vocabulary-sharded acceptance (kyro_spec_accept_tp) over the
-    N ranks of one tensor-parallel group, plus KV reserve/commit on a
-    32768-block table.  Total work is fixed as N grows (strong scaling):
-    each rank holds V/N columns of the same [256, 9 | 8, V] logits."""
-    import datetime
-
-    import torch
-    import torch.distributed as dist
-
-    from kyro_b200.verify import (Context, kv_commit, kv_reserve, spec_accept_tp,
-                                  tp_unique_id)
-    from kyro_b200.workloads import CONFIG3, paged_state
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world != args.gpus:
-        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    cfg = CONFIG3
-    B, k, V, T = cfg.batch, cfg.k, cfg.vocab, cfg.temperature
-    if V % world:
-        raise SystemExit(f"vocab {V} does not split over {world} ranks")
-    Vs = V // world
-    ctx = Context(local)
-    if world > 1:
-        uid = torch.zeros(128, dtype=torch.uint8, device=dev)
-        if rank == 0:
-            uid.copy_(torch.frombuffer(bytearray(tp_unique_id()), dtype=torch.uint8))
-        dist.broadcast(uid, 0)
-        ctx.tp_init(bytes(uid.cpu().numpy().tobytes()), rank, world)
-
-    def shard(r):  # rank r's columns of the (never materialised) full logits
-        g = torch.Generator(device=dev).manual_seed(5000 + r)
-        t = torch.randn(B, k + 1, Vs, generator=g, device=dev) * cfg.logit_std
-        d = t[:, :k, :] + torch.randn(B, k, Vs, generator=g, device=dev) * cfg.draft_noise
-        return t.contiguous(), d.contiguous()
-
-    tgt, drf = shard(rank)
-    # draft tokens sampled from the full draft rows (rank 0 regenerates every
-    # shard once, before the timed region) and broadcast
-    drafts = torch.zeros(B, k, dtype=torch.int32, device=dev)
-    if rank == 0:
-        full = torch.cat([shard(r)[1] for r in range(world)], dim=2)
-        g = torch.Generator(device=dev).manual_seed(6000)
-        probs = torch.softmax(full.reshape(B * k, V) / T, dim=1)
-        drafts.copy_(torch.multinomial(probs, 1, generator=g).reshape(B, k).int())
-        del full, probs
-    if world > 1:
-        dist.broadcast(drafts, 0)
-    st = paged_state(cfg, dev, seed=7000, fill_cache=False)
-    kvsnap = KvStateSnapshot(st)
-    nq = k + 1
-    ok = torch.empty(B, dtype=torch.int32, device=dev)
-    stream = torch.cuda.current_stream(dev)
-    ev = []
-
-    def step(i, timed):
-        kvsnap.restore()
-        kv_reserve(ctx, nq, st.block_table, st.context_lens, st.free_stack, st.free_top,
-                   st.ref_counts, cfg.block_size, out_ok=ok)
-        if timed:
-            e0 = torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-        acc, _, _, _ = spec_accept_tp(ctx, tgt, drf, drafts, V, temperature=T, seed=0, step=i)
-        if timed:
-            e1 = torch.cuda.Event(enable_timing=True)
-            e1.record(stream)
-            ev.append((e0, e1))
-        kv_commit(ctx, nq, acc, st.block_table, st.context_lens, st.free_stack, st.free_top,
-                  st.ref_counts, cfg.block_size)
-        return acc
-
-    for i in range(args.warmup):
-        step(i, False)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    clocks = None
-    if rank == 0:
-        try:
-            clocks = NvmlClockSampler(local)
-        except Exception:
-            clocks = ClockSampler(local)
-        clocks.start()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    t0.record(stream)
-    accs = []
-    for i in range(args.warmup, args.warmup + args.steps):
-        accs.append(step(i, False))
-    t1.record(stream)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    clk = clocks.stop() if clocks else None
-    ms = t0.elapsed_time(t1)
-    for i in range(args.warmup + args.steps, args.warmup + args.steps + PER_KERNEL_STEPS):
-        step(i, True)
-    torch.cuda.synchronize()
-    acc_ms = float(np.mean([a.elapsed_time(b) for a, b in ev]))
-    if world > 1:
-        t = torch.tensor([ms, acc_ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, acc_ms = float(t[0]), float(t[1])
-    status = ctx.device_status()
-    if status:
-        raise SystemExit(f"device status word 0x{status:x} after the timed region")
-    rate = float(torch.stack(accs).float().mean().item()) / k
-    peak, peak_kind = load_peaks()
-    rank_bytes = (2 * k + 1) * B * Vs * 4  # every logit of this rank's columns once
-    achieved = rank_bytes / (acc_ms * 1e-3) / 1e9
-    if rank == 0:
-        line = {
-            "metric": "TP spec-accept verified positions/s (config 3)", "unit": UNIT,
-            "value": B * nq * args.steps / (ms * 1e-3), "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded; BASELINE config 3 shapes and distributions)",
-            "config": {"workload": "config3: vocabulary-sharded acceptance (B 256, k 8, "
-                                   f"V 128256 over {world} ranks, T 0.8) + KV reserve/commit "
-                                   "on a 32768-block table",
-                       "global_batch": B, "k": k, "vocab": V, "columns_per_rank": Vs,
-                       "parallelism": f"tp{world} (vocabulary)",
-                       "l2": f"{rank_bytes / 1e9:.2f} GB of logits per rank per step"},
-            "roofline": {"bound": "hbm", "kernel": "kyro_spec_accept_tp (per rank)",
-                         "achieved": achieved, "peak": peak, "peak_kind": peak_kind,
-                         "unit": "GB/s", "frac": achieved / peak, "traffic": None},
-            "accept_ms": acc_ms, "acceptance_rate": rate,
-            "gpu_launches": (2 + (7 if world > 1 else 3)) * args.steps,
-            "clocks": clk,
-        }
-        print(json.dumps(line), flush=True)
-    ctx.close()
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-
-
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1085,6 +1174,10 @@ def main():
                     help="time config 1 as plain launches instead of CUDA graph replays")
     ap.add_argument("--no-e2e", action="store_true",
                     help="skip the host-buffer leg (profiling runs)")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the config 0 / 2 / 3 measurements after the headline")
+    ap.add_argument("--extra-steps", type=int, default=20,
+                    help="timed steps of each extra configuration")
     ap.add_argument("--requests", type=int, default=0,
                     help="config 4 only: requests in all (default 512; smaller for profiling)")
     ap.add_argument("--target-layers", type=int, default=0,

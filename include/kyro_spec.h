@@ -142,7 +142,10 @@ int kyro_spec_accept(kyro_ctx* ctx, const kyro_accept_params* p, const float* ta
  *     rejected with KYRO_ERR_WORKSPACE before anything is launched.
  *   - The first call on a device looks up the buffer's device address (a
  *     host-side runtime query, no allocation); make that first call before
- *     capturing a stream into a CUDA graph.
+ *     capturing a stream into a CUDA graph.  The address is kept until the
+ *     next kyro_ctx_create on that device: a device reset moves the array
+ *     and ends every context, so the first call through a new context looks
+ *     it up again.
  *   - Every call on a device shares the one buffer and its counters are
  *     cleared at the start of each call: calls that overlap on the GPU
  *     (different streams, or different contexts on one device) race. */
@@ -157,14 +160,18 @@ int kyro_spec_accept_static(kyro_ctx* ctx, const kyro_accept_params* p,
  * argmax.  Replaces the draft loop's argmax (src/speculative.rs:229-241)
  * with on-device sampling.
  *   logits fp32 [B, num_pos, V] -> out_tokens int32 [B, num_pos]
- *   out_probs fp32 [B, num_pos] optional: q(token). */
+ *   out_probs fp32 [B, num_pos] optional: q(token).
+ * seq_stride: logits rows from sequence b's first row to sequence b+1's;
+ * 0 means num_pos (dense rows).  A draft loop that writes position i's
+ * logits straight into column i of a [B, k, V] buffer samples it with
+ * num_pos 1 and seq_stride k. */
 typedef struct kyro_sample_params {
   int32_t batch;
   int32_t num_pos;
   int32_t vocab;
   float temperature;
   uint32_t step;
-  uint32_t _pad;
+  uint32_t seq_stride;
   uint64_t seed;
   int64_t seq_offset;
 } kyro_sample_params;
@@ -388,8 +395,12 @@ int kyro_ctx_tp_transport(kyro_ctx* ctx);
  * (divisible by the group size R); target_shard [B, k+1, V/R] and
  * draft_shard [B, k, V/R] are this rank's columns; draft_tokens hold global
  * ids.  Every rank passes identical params and gets identical outputs
- * (accept lengths, tokens with global ids, p/q at the drafts), equal to
- * kyro_spec_accept on the full rows.  Four small collectives on the
+ * (accept lengths, tokens with global ids, p/q at the drafts).  The
+ * normaliser contract is then taken over R shards (chunks start at each
+ * shard's first column; shard sums add in rank order), so the outputs equal
+ * the CPU restatement with num_shards = R bit for bit; they can differ from
+ * kyro_spec_accept on the full rows in the last bits of p and q, and so in
+ * a decision whose test lands within those bits.  Four small collectives on the
  * context's stream: all-gathers of per-row maxima, per-row normaliser parts
  * with the owner rank's values at the draft tokens, per-sequence weight
  * totals, and an int32 max of the token id.  A rank that returns an error

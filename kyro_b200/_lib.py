@@ -66,7 +66,7 @@ class TreeParams(C.Structure):
 
 class SampleParams(C.Structure):
     _fields_ = [("batch", C.c_int32), ("num_pos", C.c_int32), ("vocab", C.c_int32),
-                ("temperature", C.c_float), ("step", C.c_uint32), ("_pad", C.c_uint32),
+                ("temperature", C.c_float), ("step", C.c_uint32), ("seq_stride", C.c_uint32),
                 ("seed", C.c_uint64), ("seq_offset", C.c_int64)]
 
 

@@ -46,21 +46,31 @@ class PagedAttention:
                 tree_mask: Optional[torch.Tensor] = None, kv_split_blocks: int = 0):
         if key_cache.shape[1] != self.num_kv_heads or key_cache.shape[2] != self.block_size:
             raise ValueError("key_cache must be [num_blocks, num_kv_heads, block_size, head_dim]")
+        # The paged caches are the big operands: a dtype conversion here
+        # would copy the whole cache on every call, so only bf16 caches are
+        # taken (the reference's KVCacheManager holds f16,
+        # src/model/kv_cache.rs:55-56; convert such a cache once, up front).
+        for name, c in (("key_cache", key_cache), ("value_cache", value_cache)):
+            if c.dtype != torch.bfloat16:
+                raise TypeError(f"{name} must be bfloat16, got {c.dtype} (the verify kernel reads "
+                                "bf16 caches; convert the cache once, not per call)")
+            if not c.is_contiguous():
+                raise ValueError(f"{name} must be contiguous")
         ctx = self._context(query.device)
+        # queries are small ([B, n, Hq, D]); they are converted when needed
         q = query.to(torch.bfloat16)
-        kc = key_cache.to(torch.bfloat16)
-        vc = value_cache.to(torch.bfloat16)
+        kc, vc = key_cache, value_cache
         bt = block_table.to(torch.int64).contiguous()
         cl = context_lens.to(torch.int64).contiguous()
         if q.dim() == 3:
             # reference decode layout: the query is the last cached token
             empty = cl <= 0
             cl_q = torch.clamp(cl - 1, min=0)
-            out = verify_attention(ctx, q.unsqueeze(1).contiguous(), kc.contiguous(),
-                                   vc.contiguous(), bt, cl_q, kv_split_blocks=kv_split_blocks)
+            out = verify_attention(ctx, q.unsqueeze(1).contiguous(), kc, vc, bt, cl_q,
+                                   kv_split_blocks=kv_split_blocks)
             out = out.squeeze(1).float()
             return torch.where(empty[:, None, None], torch.zeros_like(out), out)
-        return verify_attention(ctx, q.contiguous(), kc.contiguous(), vc.contiguous(), bt, cl,
-                                tree_mask=tree_mask, kv_split_blocks=kv_split_blocks)
+        return verify_attention(ctx, q.contiguous(), kc, vc, bt, cl, tree_mask=tree_mask,
+                                kv_split_blocks=kv_split_blocks)
 
     __call__ = forward

@@ -21,9 +21,11 @@
 // so the query rows (24 for GQA 4 x 6 positions) sit in the N dimension in
 // 8-wide tiles without padding to 16; movmatrix turns P^T into the B
 // operand.  Online softmax runs per query column in the log2 domain.  The
-// four warps' states merge in shared memory (a two-round tree); when a
-// sequence needs more than one split, each split writes its partial state
-// to the workspace and the split that finishes last (atomic ticket) merges.
+// four warps' states merge in shared memory in one pass (each warp
+// publishes its (O, m, l), per-column factors are formed once, then every
+// thread combines four dims at a time); when a sequence needs more than one
+// split, each split writes its partial state to the workspace and the split
+// that finishes last (an epoch-tagged atomic ticket) merges them.
 #include <cuda_bf16.h>
 
 #include <mutex>

@@ -107,6 +107,8 @@ int kyro_ctx_create(int device, void* stream, kyro_ctx** out) {
                            "kyro_ctx_create: device %d is sm_%d%d; this library is built for "
                            "sm_100a (B200) only",
                            device, prop.major, prop.minor);
+  // the device may have been reset since an earlier context was made on it
+  kyro::static_scratch_forget(device);
   kyro_ctx* ctx = new kyro_ctx();
   ctx->device = device;
   ctx->stream = (cudaStream_t)stream;

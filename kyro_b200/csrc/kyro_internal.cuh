@@ -44,6 +44,9 @@ int cuda_error(cudaError_t err, const char* what);
 int check_launch(const char* what);
 // Validate a context and make its device current.
 int enter(kyro_ctx* ctx);
+// Drop the cached device address of kyro_spec_accept_static's scratch array
+// on `device` (sampler.cu), so that the next call looks it up again.
+void static_scratch_forget(int device);
 
 // Tensor-core attention for many query rows per KV head (tree_attention.cu):
 // whether a shape fills its 128-row tiles, and the launch.
@@ -71,8 +74,11 @@ void release(kyro_ctx* ctx);
 // (peer_exchange.cu), with NCCL as the transport when the ranks cannot map
 // each other's memory or KYRO_TP_TRANSPORT=nccl.
 namespace xchg {
-// map every rank's exchange region (collective over the context's group)
-int init(kyro_ctx* ctx);
+// bytes of the device buffer init() exchanges its setup records through
+size_t setup_bytes(int world);
+// map every rank's exchange region (collective over the context's group);
+// `dh` holds setup_bytes(world) bytes of device memory
+int init(kyro_ctx* ctx, uint8_t* dh);
 void release(kyro_ctx* ctx);
 int all_gather(kyro_ctx* ctx, const void* send, void* recv, size_t bytes, const char* what);
 int all_reduce_max_i32(kyro_ctx* ctx, const int32_t* send, int32_t* recv, size_t count,

@@ -19,8 +19,11 @@
  *      operations only (round-to-nearest fma/mul/add and integer ops), so
  *      host and device produce the same bits.  Reduction x = n*ln2 + r,
  *      |r| <= ln2/2, then a degree-5 polynomial whose coefficients were
- *      fitted for this project by iterated weighted least squares on
- *      [-ln2/2, ln2/2] (max relative error 9.4e-8 before rounding).
+ *      fitted for this project by iterated weighted least squares
+ *      (Lawson's algorithm on the relative error over [-ln2/2, ln2/2],
+ *      c0 fixed at 1, stopped early and rounded to fp32; max relative error
+ *      9.3e-8 before rounding).  oracle/exp_poly.py restates the fit and
+ *      checks these constants.
  *      Inputs below -87 (and NaN) behave as -87; ky_exp(0) == 1 exactly.
  *   3. Fixed summation orders.  A chunk's softmax mass is an fp32 sum in one
  *      prescribed tree (ky_chunk_sum), and a row's normaliser a double sum

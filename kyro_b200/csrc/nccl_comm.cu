@@ -140,15 +140,27 @@ extern "C" int kyro_ctx_tp_init(kyro_ctx* ctx, const void* unique_id, int rank, 
   KY_REQUIRE(!ctx->nccl_comm, "kyro_ctx_tp_init: the context already has a group");
   const NcclApi* a;
   KY_TRY(need_api(&a, "kyro_ctx_tp_init"));
+  // The peer-exchange setup's device buffer is allocated before the group
+  // forms: a failure here returns before the first collective, like an
+  // argument error, and nothing after it can skip one of the setup's
+  // collectives that the other ranks take.
+  uint8_t* dh = nullptr;
+  const cudaError_t err = cudaMalloc(&dh, kyro::xchg::setup_bytes(world));
+  if (err != cudaSuccess) return kyro::cuda_error(err, "cudaMalloc(peer exchange setup)");
   ncclUniqueId id;
   memcpy(&id, unique_id, sizeof(id));
   ncclComm_t comm = nullptr;
   const ncclResult_t r = a->CommInitRank(&comm, world, id, rank);
-  if (r != ncclSuccess) return nccl_error(r, "ncclCommInitRank");
+  if (r != ncclSuccess) {
+    cudaFree(dh);
+    return nccl_error(r, "ncclCommInitRank");
+  }
   ctx->nccl_comm = comm;
   ctx->tp_rank = rank;
   ctx->tp_world = world;
-  return kyro::xchg::init(ctx);
+  const int st = kyro::xchg::init(ctx, dh);
+  cudaFree(dh);
+  return st;
 }
 
 extern "C" int kyro_ctx_tp_transport(kyro_ctx* ctx) {

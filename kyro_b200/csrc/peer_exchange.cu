@@ -155,7 +155,9 @@ struct SetupRec {
   int32_t pad[11];
 };
 
-int init(kyro_ctx* ctx) {
+size_t setup_bytes(int world) { return sizeof(SetupRec) * (size_t)(world + 1) + 64; }
+
+int init(kyro_ctx* ctx, uint8_t* dh) {
   ctx->xchg_ready = false;
   ctx->xchg_local = nullptr;
   for (int r = 0; r < KYRO_MAX_TP_WORLD; ++r) ctx->xchg_peer[r] = nullptr;
@@ -182,21 +184,18 @@ int init(kyro_ctx* ctx) {
                   cudaIpcGetMemHandle(&mine.handle, local) != cudaSuccess))
     mine.ok = 0;
   cudaGetLastError();
-  uint8_t* dh = nullptr;
-  cudaError_t err = cudaMalloc(&dh, sizeof(SetupRec) * (world + 1) + 64);
-  if (err != cudaSuccess) {
-    if (local) cudaFree(local);
-    return cuda_error(err, "cudaMalloc(peer exchange setup)");
-  }
-  // the setup's collectives run on a private stream, synchronously
+  // The setup's collectives run synchronously on a private stream, or on the
+  // context's own stream if no stream can be made.  `dh` (the exchange
+  // records) was allocated by the caller before the group formed, so no
+  // local failure from here on skips a collective.
   cudaStream_t saved = ctx->stream, s = nullptr;
-  err = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
-  if (err != cudaSuccess) {
-    cudaFree(dh);
-    if (local) cudaFree(local);
-    return cuda_error(err, "cudaStreamCreate(peer exchange setup)");
+  const bool own_stream = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) == cudaSuccess;
+  if (!own_stream) {
+    cudaGetLastError();
+    s = saved;
   }
   ctx->stream = s;
+  cudaError_t err;
   uint8_t* d_mine = dh + sizeof(SetupRec) * world;
   cudaMemcpy(d_mine, &mine, sizeof(mine), cudaMemcpyHostToDevice);
   int st = nccl::all_gather(ctx, d_mine, dh, sizeof(SetupRec), "peer exchange setup");
@@ -239,8 +238,7 @@ int init(kyro_ctx* ctx) {
     if (st == KYRO_OK) cudaMemcpy(&agreed, dh + 16, 4, cudaMemcpyDeviceToHost);
   }
   ctx->stream = saved;
-  cudaStreamDestroy(s);
-  cudaFree(dh);
+  if (own_stream) cudaStreamDestroy(s);
   if (st != KYRO_OK || !agreed) {
     for (int r = 0; r < world; ++r)
       if (r != ctx->tp_rank && ctx->xchg_peer[r]) cudaIpcCloseMemHandle(ctx->xchg_peer[r]);

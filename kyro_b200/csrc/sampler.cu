@@ -125,6 +125,7 @@ struct Args {
   int greedy_ref;
   int sample;                   // draft-sampler call
   int pos_div;                  // sampler: Philox seq = r / pos_div, pos = r % pos_div
+  int64_t seq_rows;             // sampler: logits rows from one sequence to the next (>= pos_div)
   uint64_t seed;
   uint32_t step;
   int64_t seq_offset;
@@ -369,7 +370,13 @@ __device__ __forceinline__ f2_t exp_pair(f2_t x) {
                  __uint_as_float(__float_as_uint(ph) + (__float_as_uint(th) << 23)));
 }
 
+// The logits row of sampler row b (sequence b / pos_div, position b % pos_div).
+__device__ __forceinline__ int64_t sample_row(const Args& a, int b) {
+  return (int64_t)(b / a.pos_div) * a.seq_rows + b % a.pos_div;
+}
+
 __device__ __forceinline__ const float* stats_row_ptr(const Args& a, int b, int r) {
+  if (a.sample) return a.plog + sample_row(a, b) * a.V;
   if (r <= a.k) return a.plog + ((int64_t)b * (a.k + 1) + r) * a.V;
   return a.qlog + ((int64_t)b * a.q_rows + (r - a.k - 1)) * a.V;
 }
@@ -680,7 +687,7 @@ __device__ __forceinline__ void decide_sequence(const Args& a, int b, const RowS
     if (lane == 0) {
       const int64_t seq = a.seq_offset + b / a.pos_div;
       const int pos = b % a.pos_div;
-      fr.p_row = b;
+      fr.p_row = sample_row(a, b);
       fr.p_stat = b;
       fr.q_row = -1;
       fr.q_stat = -1;
@@ -2137,6 +2144,7 @@ int kyro_spec_accept(kyro_ctx* ctx, const kyro_accept_params* p, const float* ta
   a.greedy_ref = p->mode == KYRO_ACCEPT_GREEDY_REF;
   a.sample = 0;
   a.pos_div = 1;
+  a.seq_rows = 1;
   a.seed = p->seed;
   a.step = p->step;
   a.seq_offset = p->seq_offset;
@@ -2170,6 +2178,8 @@ int kyro_sample_tokens(kyro_ctx* ctx, const kyro_sample_params* p, const float* 
   const int64_t nchunks = (V + kChunk - 1) / kChunk;
   KY_REQUIRE(rows * nchunks < (1ll << 31), "kyro_sample_tokens: too many rows");
   KY_REQUIRE(logits && out_tokens, "kyro_sample_tokens: NULL logits or out_tokens");
+  KY_REQUIRE(p->seq_stride == 0 || p->seq_stride >= (uint32_t)p->num_pos,
+             "kyro_sample_tokens: seq_stride %u < num_pos %d", p->seq_stride, p->num_pos);
   const size_t need = carve(nullptr, rows, 1, nchunks).bytes;
   if (workspace_bytes < need || !workspace)
     return kyro::set_error(KYRO_ERR_WORKSPACE, "kyro_sample_tokens: workspace %zu < %zu bytes",
@@ -2189,6 +2199,7 @@ int kyro_sample_tokens(kyro_ctx* ctx, const kyro_sample_params* p, const float* 
   a.greedy_ref = 0;
   a.sample = 1;
   a.pos_div = p->num_pos;
+  a.seq_rows = p->seq_stride ? (int64_t)p->seq_stride : (int64_t)p->num_pos;
   a.seed = p->seed;
   a.step = p->step;
   a.seq_offset = p->seq_offset;
@@ -2261,6 +2272,7 @@ int kyro_spec_accept_tp(kyro_ctx* ctx, const kyro_accept_params* p, const float*
   a.greedy_ref = p->mode == KYRO_ACCEPT_GREEDY_REF;
   a.sample = 0;
   a.pos_div = 1;
+  a.seq_rows = 1;
   a.seed = p->seed;
   a.step = p->step;
   a.seq_offset = p->seq_offset;
@@ -2475,6 +2487,17 @@ int static_scratch(int device, void** out) {
 }
 
 }  // namespace
+
+// A device reset (cudaDeviceReset, or the primary context torn down and made
+// again) moves the array, so the cached address must not outlive it.  A
+// reset also ends every kyro_ctx on the device, and any later call needs a
+// new one: kyro_ctx_create calls this, and the next static call looks the
+// address up again.
+void kyro::static_scratch_forget(int device) {
+  if (device < 0 || device >= kMaxDevices) return;
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  g_static_ptr[device] = nullptr;
+}
 
 extern "C" int kyro_spec_accept_static(kyro_ctx* ctx, const kyro_accept_params* p,
                                        const float* target_logits, const float* draft_logits,

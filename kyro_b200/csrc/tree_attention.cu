@@ -329,6 +329,7 @@ tree_attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
   auto item_addr = [&](int n) { return base + kOffRing + (uint32_t)(n % kSlots) * kItem; };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + kTilesBytes + 480);
   int* err = reinterpret_cast<int*>(gbase + kTilesBytes + 484);
+  int* issued_out = reinterpret_cast<int*>(gbase + kTilesBytes + 488);  // the producer's count
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_rank();  // 0: the leader, which issues the MMAs
@@ -365,6 +366,7 @@ tree_attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
     }
     kyro::ptx::mbar_init(mma_done, 1);
     *err = 0;
+    *issued_out = 0;
     kyro::ptx::fence_barrier_init();
   }
   if (warp == kMmaWarp) {
@@ -431,6 +433,7 @@ tree_attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
         }
       };
       fetch_ids(0);
+      int issued = 0;  // ring items whose loads this CTA has issued
       for (int j = 0; j < ntiles; ++j) {
         int64_t cur[kTileBlocks];
 #pragma unroll
@@ -447,9 +450,11 @@ tree_attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
             break;
           }
           load_item(n, cur);
+          issued = n + 1;
         }
         if (stop) break;
       }
+      *issued_out = issued;
     }
     __syncwarp();
   } else if (warp == kMmaWarp) {
@@ -494,6 +499,11 @@ tree_attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
         for (int h = 0; h < ntq; ++h) s_mma(h, 0);
       }
       for (int j = 0; ok && j < ntiles; ++j) {
+        // a timeout recorded by another warp of this CTA: issue nothing more
+        if (*(volatile int*)err) {
+          ok = false;
+          break;
+        }
         const bool more = j + 1 < ntiles;
         for (int h = 0; ok && h < ntq; ++h) {
           if (!o_mma(h, j)) {
@@ -651,6 +661,17 @@ tree_attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
   // neither CTA leaves (or frees TMEM) while the leader's MMAs may still
   // read the other's shared memory or TMEM, or its commits may still arrive
   tc_fence_before();
+  __syncthreads();
+  // After a timeout the consumers may have stopped before the last loads
+  // landed.  The leader's slot barriers count both CTAs' bytes, so the
+  // leader waits (bounded) for every item still in the ring, while the
+  // cluster barrier below keeps the peer resident: no CTA leaves while a
+  // bulk copy may still write its shared memory.
+  if (rank == 0 && warp == kProducerWarp && lane == 0 && *(volatile int*)err) {
+    const int issued = *(volatile int*)issued_out;
+    for (int n = issued > kSlots ? issued - kSlots : 0; n < issued; ++n)
+      kyro::ptx::mbar_wait_bounded(slot_full(item_slot(n)), item_parity(n), kTcWaitBudget);
+  }
   __syncthreads();
   cluster_sync();
   tc_fence_after();

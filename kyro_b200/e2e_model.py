@@ -132,8 +132,10 @@ class SpecModels:
                 tokens: torch.Tensor, block_table: torch.Tensor, lens: torch.Tensor,
                 ws_attn: torch.Tensor, logits: torch.Tensor, timer=None) -> torch.Tensor:
         """tokens int64 [B, n] at positions lens[b] + j -> fp32 logits, written
-        by the lm_head GEMM into `logits` (contiguous [B * n, V]) and returned
-        as [B, n, V].  Each layer stores its new K/V rows into slots lens[b] + j."""
+        by the lm_head GEMM into `logits` and returned as [B, n, V].  `logits`
+        is [B * n, V], contiguous, or (n == 1) a [B, V] view with unit column
+        stride, such as column i of a [B, k, V] buffer, which the GEMM writes
+        in place.  Each layer stores its new K/V rows into slots lens[b] + j."""
         s = self.shape
         B, n = tokens.shape
         hq, hkv, d = s.heads, s.kv_heads, s.head_dim
@@ -158,7 +160,9 @@ class SpecModels:
             x = x + torch.matmul(F.silu(gu[..., :s.ffn]) * gu[..., s.ffn:], layers.wdown[i])
         h = F.rms_norm(x, (s.hidden,), self.final_norm, s.eps)
         torch.mm(h.view(B * n, s.hidden), self.lm_head, out_dtype=torch.float32, out=logits)
-        return logits.view(B, n, s.vocab)
+        if logits.is_contiguous():
+            return logits.view(B, n, s.vocab)
+        return logits.unsqueeze(1)  # [B, 1, V], rows k * V apart
 
 
 class SpecStep:
@@ -181,7 +185,6 @@ class SpecStep:
         self.toks = torch.empty(B, k + 1, dtype=torch.int32, device=dev)
         self.num = torch.empty(B, dtype=torch.int32, device=dev)
         self.tokens_in = torch.empty(B, k + 1, dtype=torch.int64, device=dev)
-        self.dlog = torch.empty(B, V, dtype=torch.float32, device=dev)  # one draft position
         from . import _lib
         import ctypes as C
         from .verify import attn_params
@@ -215,12 +218,13 @@ class SpecStep:
         tok = self.last.view(-1, 1)
         for i in range(k):
             torch.add(kv.context_lens, i, out=self.d_lens)
+            # the lm_head GEMM writes position i's logits straight into
+            # column i of the [B, k, V] draft buffer that acceptance reads
             logits = m.forward(self.ctx_d, m.draft, m.d_k, m.d_v, tok, kv.block_table, self.d_lens,
-                               self.ws_d, self.dlog)  # [B, 1, V] fp32
+                               self.ws_d, self.drf[:, i])  # [B, 1, V] fp32, rows k * V apart
             t, _ = sample_tokens(self.ctx_d, logits, cfg.temperature, seed=self.seed,
                                  step=step * k + i, seq_offset=self.seq_offset,
                                  workspace=self.ws_smp)
-            self.drf[:, i].copy_(logits[:, 0])
             self.drafts[:, i] = t[:, 0]
             tok = t.long()
         if timer is not None:

@@ -219,14 +219,30 @@ def spec_accept_tp(ctx: Context, target_shard: torch.Tensor, draft_shard: Option
 
 def sample_tokens(ctx: Context, logits: torch.Tensor, temperature: float, seed: int = 0,
                   step: int = 0, seq_offset: int = 0, workspace: Optional[torch.Tensor] = None):
-    """kyro_sample_tokens.  logits fp32 [B,P,V] -> (tokens int32 [B,P], probs fp32 [B,P])."""
+    """kyro_sample_tokens.  logits fp32 [B,P,V] -> (tokens int32 [B,P], probs fp32 [B,P]).
+
+    The rows of one sequence must be dense ([P, V] contiguous), but the
+    sequences may sit further apart: logits[:, i:i+1] of a [B, k, V] buffer
+    is taken as it is (seq_stride k), without a copy."""
     dev = ctx.device
-    _need(logits, "logits", torch.float32, dev, 3)
+    if not isinstance(logits, torch.Tensor):
+        raise TypeError("logits must be a torch.Tensor")
+    if logits.dim() != 3:
+        raise ValueError(f"logits must have 3 dims, got shape {tuple(logits.shape)}")
     B, P, V = logits.shape
+    st = logits.stride()
+    seq_stride = 0
+    if not logits.is_contiguous():
+        if st[2] != 1 or (P > 1 and st[1] != V) or st[0] % V or st[0] // V < P:
+            raise ValueError("logits rows must be dense within a sequence "
+                             f"(strides {st} for shape {tuple(logits.shape)})")
+        seq_stride = st[0] // V
+    if logits.dtype != torch.float32 or logits.device != dev:
+        raise TypeError(f"logits must be float32 on {dev}")
     toks = torch.empty(B, P, dtype=torch.int32, device=dev)
     probs = torch.empty(B, P, dtype=torch.float32, device=dev)
-    p = SampleParams(B, P, V, float(temperature), step & 0xFFFFFFFF, 0, seed & 0xFFFFFFFFFFFFFFFF,
-                     seq_offset)
+    p = SampleParams(B, P, V, float(temperature), step & 0xFFFFFFFF, seq_stride,
+                     seed & 0xFFFFFFFFFFFFFFFF, seq_offset)
     L = _lib.load()
     need = L.kyro_sample_workspace_size(C.byref(p))
     ws = workspace if workspace is not None else ctx.workspace(need)

@@ -289,3 +289,44 @@ def rope_kv_write(q, k_new, v_new, block_table, context_lens, k_cache, v_cache, 
                            _p(np.ascontiguousarray(context_lens)), _p(q_out), _p(k_cache),
                            _p(v_cache))
     return q_out
+
+
+def verify_step(state: dict, q, k_new, v_new, target_logits, draft_logits, draft_tokens,
+                block_size, mode=MODE_STOCHASTIC, temperature=1.0, seed=0, step=0,
+                seq_offset=0, rope_theta=None, nthreads=1):
+    """One batched verify step, composed from the restatements above in the
+    order SpeculativeDecoder::step runs it (src/speculative.rs:342-353) with
+    the paged cache of the verify path:
+
+      kv_reserve (k + 1 slots, BlockManager::allocate semantics)
+      -> rope_kv_write (rope_theta given: RoPE at context_len + j, llama.rs:73-82)
+         or kv_write (append_kv, kv_cache.rs:49-75) of the new K/V rows
+      -> paged attention of the k + 1 query rows (attention_kernel.rs:22-136)
+      -> acceptance (verify_drafts, speculative.rs:286-339, or the
+         stochastic rule) -> kv_commit of accept_len + 1 slots.
+
+    `state` holds numpy arrays block_table, context_lens, free_stack,
+    free_top, ref_counts and the uint16 caches k_cache, v_cache; all are
+    modified in place.  q / k_new / v_new are uint16 bf16 bit patterns.
+    Returns dict(attention fp32 [B, k+1, Hq, D], ok, accept_len, tokens,
+    num_tokens, probs)."""
+    nq = np.asarray(target_logits).shape[1]
+    s = state
+    ok = kv_reserve(nq, s["block_table"], s["context_lens"], s["free_stack"], s["free_top"],
+                    s["ref_counts"], block_size)
+    if rope_theta is not None:
+        qq = rope_kv_write(q, k_new, v_new, s["block_table"], s["context_lens"], s["k_cache"],
+                           s["v_cache"], block_size, theta=rope_theta)
+    else:
+        kv_write(k_new, v_new, s["block_table"], s["context_lens"], s["k_cache"], s["v_cache"],
+                 block_size)
+        qq = q
+    att = paged_attention(qq, s["k_cache"], s["v_cache"], s["block_table"], s["context_lens"],
+                          block_size, nthreads=nthreads)
+    acc, toks, num, probs = spec_accept(target_logits, draft_logits, draft_tokens, mode=mode,
+                                        temperature=temperature, seed=seed, step=step,
+                                        seq_offset=seq_offset, nthreads=nthreads)
+    kv_commit(nq, acc, s["block_table"], s["context_lens"], s["free_stack"], s["free_top"],
+              s["ref_counts"], block_size)
+    return {"attention": att, "ok": ok, "accept_len": acc, "tokens": toks, "num_tokens": num,
+            "probs": probs}

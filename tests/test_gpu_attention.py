@@ -88,7 +88,7 @@ def test_reference_layout_cases(ctx):
     for hkv, ctx_len, fill in [(2, 0, 0.0), (8, 8, 1.0), (8, 24, 1.0)]:
         attn = PagedAttention(16, 8, 64, hkv, ctx=ctx)
         q = torch.full((1, 8, 64), fill, device=ctx.device)
-        kc = torch.full((4, hkv, 16, 64), fill, device=ctx.device)
+        kc = torch.full((4, hkv, 16, 64), fill, device=ctx.device, dtype=torch.bfloat16)
         bt = torch.zeros(1, 4, dtype=torch.int64, device=ctx.device)
         cl = torch.full((1,), ctx_len, dtype=torch.int64, device=ctx.device)
         out = attn.forward(q, kc, kc, bt, cl)

@@ -199,3 +199,27 @@ def test_fast_exp_forms_match_contract(ctx):
     bits on every fp32 input in [-100, 0], -inf and NaN."""
     from kyro_b200 import verify
     assert verify.selftest_exp(ctx) == (0, 0)
+
+
+@pytest.mark.parametrize("k,V,T", [(4, 32000, 0.7), (5, 4099, 1.0), (3, 1000, 0.0)])
+def test_sampler_reads_strided_sequences(ctx, oracle, k, V, T):
+    """Column i of a [B, k, V] draft buffer, sampled in place (seq_stride k),
+    gives the tokens and probabilities of the same rows copied out densely,
+    and both match the oracle."""
+    from kyro_b200.verify import sample_tokens
+    from kyro_b200.workloads import accept_inputs
+    B = 6
+    _, drf = accept_inputs(B, k, V, ctx.device, seed=40 + k)
+    for i in range(k):
+        col = drf[:, i:i + 1]
+        assert not col.is_contiguous() or k == 1
+        toks, probs = sample_tokens(ctx, col, T, seed=3, step=i, seq_offset=5)
+        dense = col.contiguous()
+        dtoks, dprobs = sample_tokens(ctx, dense, T, seed=3, step=i, seq_offset=5)
+        otoks, oprobs = oracle.sample_tokens(_np(dense), T, seed=3, step=i, seq_offset=5,
+                                             nthreads=NTHREADS)
+        assert torch.equal(toks, dtoks) and torch.equal(probs, dprobs)
+        assert np.array_equal(_np(toks), otoks)
+        if T > 0:
+            assert np.array_equal(_np(probs), oprobs)
+    assert ctx.device_status() == 0

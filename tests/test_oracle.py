@@ -4,10 +4,12 @@ property of the published rejection-sampling rule."""
 import json
 import math
 import os
+import sys
 
 import numpy as np
 import pytest
 
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "reference_known_answers.json")
 
 
@@ -48,6 +50,20 @@ def test_exp_accuracy(oracle):
     assert oracle.exp(0.0) == 1.0
     # below -87 (and -inf) behaves as -87
     assert oracle.exp(-87.5) == oracle.exp(-87.0) == oracle.exp(float("-inf")) < 2e-38
+
+
+def test_exp_polynomial_constants():
+    """The committed ky_exp coefficients: c0 is 1 (so ky_exp(0) == 1), the
+    fit's relative error before rounding is the stated 9.3e-8, and the fit
+    restated by oracle/exp_poly.py lands within that error class."""
+    import exp_poly
+    c = exp_poly.committed()
+    assert c[0] == 1.0
+    err = exp_poly.max_rel_error(c)
+    assert err < 9.4e-8
+    refit = exp_poly.lawson_fit()
+    assert exp_poly.max_rel_error(refit) < 1e-7
+    assert max(abs(a - b) / abs(b) for a, b in zip(refit[1:], c[1:])) < 1e-3
 
 
 @pytest.mark.parametrize("V,shards", [(7, 1), (2048, 1), (32000, 1), (128256, 1), (128256, 2),
@@ -507,3 +523,18 @@ def test_reserve_cow_out_of_blocks(oracle):
     ok, cow = oracle.kv_reserve_cow(3, kc, vc, bt, cl, fs, top, rc, bs)
     assert ok.tolist() == [0, 0, 1, 0] and (cow == -1).all()
     assert rc[shared] == 2 and bt[0, 2] == shared and bt[1, 2] == shared and top[0] == 0
+
+
+def test_tp_golden_fixture_matches_oracle(oracle):
+    """tests/golden/tp_accept_golden.json (read by bench.py --gpus N to check
+    the sharded kernels) holds exactly the oracle's outputs at 1, 2, 4 and 8
+    shards."""
+    import json
+    sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
+    import make_tp_golden as G
+    with open(G.OUT) as f:
+        fixture = json.load(f)
+    assert [tuple(c[n] for n in ("B", "k", "V", "mode", "T", "seed")) for c in fixture["cases"]] \
+        == [tuple(c) for c in G.CASES]
+    for case in fixture["cases"]:
+        assert case["shards"] == G.expected(oracle, case)
