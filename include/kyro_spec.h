@@ -68,6 +68,17 @@ int kyro_ctx_set_stream(kyro_ctx* ctx, void* stream);
 /* Synchronise the context's stream, return the device status word in
  * *out_flags (KYRO_DEV_* bits) and clear it when `clear` != 0. */
 int kyro_ctx_device_status(kyro_ctx* ctx, uint32_t* out_flags, int clear);
+/* Bound, in milliseconds (1..600000), of every wait this context makes on
+ * another rank: a device-side wait for a peer's flag in the exchange rounds
+ * sets KYRO_DEV_WAIT_TIMEOUT and returns when it runs out, and the host
+ * watchdog aborts an NCCL collective that has not completed within it (the
+ * group's TP calls then return KYRO_ERR_TIMEOUT).  The role of the
+ * reference's request deadlines (src/scheduler/continuous_batching.rs:
+ * 83-100), for the step's collectives.  A new context takes
+ * KYRO_WAIT_TIMEOUT_MS from the environment, else 2000.  After a timeout
+ * the ranks' exchange state no longer agrees: destroy the context and form
+ * the group again. */
+int kyro_ctx_set_wait_timeout(kyro_ctx* ctx, uint32_t ms);
 /* Copy the calling thread's last error message into buf (NUL-terminated);
  * returns the full message length. */
 size_t kyro_last_error(char* buf, size_t len);
@@ -390,6 +401,31 @@ int kyro_ctx_tp_init(kyro_ctx* ctx, const void* unique_id, int rank, int world);
 /* The transport of the context's exchange rounds: 0 no group, 1 NCCL,
  * 2 NVLink peer memory. */
 int kyro_ctx_tp_transport(kyro_ctx* ctx);
+
+/* Failure injection and self-tests of the bounded waits.  No counterpart in
+ * the reference, whose failure handling is host-side (deadlines,
+ * src/scheduler/continuous_batching.rs:83-100; worker errors logged,
+ * src/main.rs:146-148).  None of them faults or hangs a GPU.
+ *
+ * kyro_ctx_tp_inject_skip: this rank skips its next `rounds` peer-memory
+ * exchange rounds while staying alive (it neither stores its payload nor
+ * raises its flags), so its peers' waits run into the wait bound.  Only for
+ * contexts whose exchange runs on peer memory.
+ *
+ * kyro_selftest_exchange_timeout: on one GPU, runs the exchange kernel as a
+ * one-rank group over `region` (>= 4096 bytes of device memory, 256-byte
+ * aligned, cleared by the call) with the round skipped, so it waits for a
+ * flag that nothing sets; after the wait bound it sets
+ * KYRO_DEV_WAIT_TIMEOUT and returns, leaving the context usable.
+ *
+ * kyro_selftest_watchdog: the host watchdog that guards NCCL collectives,
+ * run on the caller's probe: arms `poll` with a bound of timeout_ms and
+ * blocks until poll(user) returns nonzero (KYRO_OK) or the bound passes and
+ * on_abort(user) has run once (KYRO_ERR_TIMEOUT).  Needs no GPU. */
+int kyro_ctx_tp_inject_skip(kyro_ctx* ctx, int32_t rounds);
+int kyro_selftest_exchange_timeout(kyro_ctx* ctx, void* region, size_t region_bytes);
+int kyro_selftest_watchdog(uint32_t timeout_ms, int (*poll)(void* user),
+                           void (*on_abort)(void* user), void* user);
 
 /* Vocabulary-sharded kyro_spec_accept: p->vocab is the FULL vocabulary V
  * (divisible by the group size R); target_shard [B, k+1, V/R] and

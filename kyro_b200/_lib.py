@@ -45,11 +45,17 @@ EXPORTS = (
     "kyro_kv_reserve", "kyro_kv_reserve_cow", "kyro_kv_commit", "kyro_kv_commit_tree", "kyro_kv_write",
     "kyro_rope_kv_write", "kyro_philox_uniforms", "kyro_selftest_exp",
     "kyro_tp_unique_id", "kyro_ctx_tp_init", "kyro_ctx_tp_transport",
+    "kyro_ctx_set_wait_timeout", "kyro_ctx_tp_inject_skip", "kyro_selftest_exchange_timeout",
+    "kyro_selftest_watchdog",
     "kyro_spec_accept_tp_workspace_size",
     "kyro_spec_accept_tp", "kyro_spec_accept_tree_workspace_size", "kyro_spec_accept_tree",
 )
 
 TP_UNIQUE_ID_BYTES = 128
+
+# callback types of kyro_selftest_watchdog
+POLL_FN = C.CFUNCTYPE(C.c_int, C.c_void_p)
+ABORT_FN = C.CFUNCTYPE(None, C.c_void_p)
 
 
 class AcceptParams(C.Structure):
@@ -137,6 +143,10 @@ def load():
                                             C.c_size_t]),
         "kyro_ctx_tp_init": (C.c_int, [vp, vp, C.c_int, C.c_int]),
         "kyro_ctx_tp_transport": (C.c_int, [vp]),
+        "kyro_ctx_set_wait_timeout": (C.c_int, [vp, u32]),
+        "kyro_ctx_tp_inject_skip": (C.c_int, [vp, i32]),
+        "kyro_selftest_exchange_timeout": (C.c_int, [vp, vp, sz]),
+        "kyro_selftest_watchdog": (C.c_int, [u32, POLL_FN, ABORT_FN, vp]),
         "kyro_spec_accept_tp_workspace_size": (C.c_size_t, [vp, C.c_int]),
         "kyro_spec_accept_tp": (C.c_int, [vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, C.c_size_t]),
     }

@@ -2,6 +2,7 @@
 // Philox test aid.  The context plays the part of the per-worker state the
 // reference keeps in Worker (src/worker.rs:13-38): the device it runs on and
 // the stream its kernels go to.
+#include <cstdlib>
 #include <mutex>
 
 #include "kyro_internal.cuh"
@@ -29,6 +30,16 @@ int check_launch(const char* what) {
   cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) return cuda_error(err, what);
   return KYRO_OK;
+}
+
+uint64_t default_wait_ns() {
+  const char* e = std::getenv("KYRO_WAIT_TIMEOUT_MS");
+  if (e && *e) {
+    char* end = nullptr;
+    const unsigned long v = std::strtoul(e, &end, 10);
+    if (end && *end == '\0' && v >= 1 && v <= 600000) return (uint64_t)v * 1000000ull;
+  }
+  return 2000000000ull;  // 2 s
 }
 
 int enter(kyro_ctx* ctx) {
@@ -121,6 +132,10 @@ int kyro_ctx_create(int device, void* stream, kyro_ctx** out) {
   ctx->xchg_ready = false;
   ctx->xchg_local = nullptr;
   for (int r = 0; r < KYRO_MAX_TP_WORLD; ++r) ctx->xchg_peer[r] = nullptr;
+  ctx->xchg_skip_rounds = 0;
+  ctx->wait_ns = kyro::default_wait_ns();
+  ctx->watchdog = nullptr;
+  ctx->tp_aborted = 0;
   err = cudaMalloc(&ctx->d_status, 16);
   if (err != cudaSuccess) {
     delete ctx;
@@ -142,6 +157,13 @@ int kyro_ctx_destroy(kyro_ctx* ctx) {
   kyro::nccl::release(ctx);
   cudaFree(ctx->d_status);
   delete ctx;
+  return KYRO_OK;
+}
+
+int kyro_ctx_set_wait_timeout(kyro_ctx* ctx, uint32_t ms) {
+  if (!ctx) return kyro::set_error(KYRO_ERR_INVALID_ARG, "null kyro_ctx");
+  KY_REQUIRE(ms >= 1 && ms <= 600000, "kyro_ctx_set_wait_timeout: %u ms (1..600000)", ms);
+  ctx->wait_ns = (uint64_t)ms * 1000000ull;
   return KYRO_OK;
 }
 

@@ -32,6 +32,14 @@ struct kyro_ctx {
   bool xchg_ready;
   uint8_t* xchg_local;
   uint8_t* xchg_peer[KYRO_MAX_TP_WORLD];
+  int xchg_skip_rounds;  // fault injection: exchange rounds this rank skips
+  // bound of every device-side wait on another rank, and of the host
+  // watchdog on NCCL collectives (kyro_ctx_set_wait_timeout)
+  uint64_t wait_ns;
+  // host watchdog of the NCCL collectives (nccl_comm.cu); set once it has
+  // aborted the communicator, after which TP calls fail
+  void* watchdog;
+  volatile int tp_aborted;
 };
 
 namespace kyro {
@@ -44,6 +52,8 @@ int cuda_error(cudaError_t err, const char* what);
 int check_launch(const char* what);
 // Validate a context and make its device current.
 int enter(kyro_ctx* ctx);
+// The wait bound a new context starts with: KYRO_WAIT_TIMEOUT_MS, else 2 s.
+uint64_t default_wait_ns();
 // Drop the cached device address of kyro_spec_accept_static's scratch array
 // on `device` (sampler.cu), so that the next call looks it up again.
 void static_scratch_forget(int device);
@@ -68,6 +78,9 @@ int all_reduce_min_i32(kyro_ctx* ctx, const int32_t* send, int32_t* recv, size_t
                        const char* what);
 // destroy the context's communicator (no-op without one)
 void release(kyro_ctx* ctx);
+// put the collectives enqueued so far under the context's host watchdog
+// (NCCL transport only; a no-op otherwise and during stream capture)
+void watch(kyro_ctx* ctx);
 }  // namespace nccl
 
 // The sharded sampler's exchange rounds over NVLink peer memory

@@ -14,6 +14,7 @@
 #include <mutex>
 
 #include "kyro_internal.cuh"
+#include "watchdog.h"
 
 namespace {
 
@@ -21,6 +22,7 @@ struct NcclApi {
   ncclResult_t (*GetUniqueId)(ncclUniqueId*);
   ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int);
   ncclResult_t (*CommDestroy)(ncclComm_t);
+  ncclResult_t (*CommAbort)(ncclComm_t);
   ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t);
   ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                             cudaStream_t);
@@ -49,6 +51,7 @@ void load_api() {
   g_api.GetUniqueId = (decltype(g_api.GetUniqueId))sym("ncclGetUniqueId");
   g_api.CommInitRank = (decltype(g_api.CommInitRank))sym("ncclCommInitRank");
   g_api.CommDestroy = (decltype(g_api.CommDestroy))sym("ncclCommDestroy");
+  g_api.CommAbort = (decltype(g_api.CommAbort))sym("ncclCommAbort");
   g_api.AllGather = (decltype(g_api.AllGather))sym("ncclAllGather");
   g_api.AllReduce = (decltype(g_api.AllReduce))sym("ncclAllReduce");
   g_api.GetErrorString = (decltype(g_api.GetErrorString))sym("ncclGetErrorString");
@@ -76,10 +79,84 @@ int need_api(const NcclApi** out, const char* what) {
   return KYRO_OK;
 }
 
+// The context's host watchdog over its NCCL collectives: a ring of CUDA
+// events, one recorded after each sharded call's collectives; a call whose
+// event has not completed within the context's wait bound gets the
+// communicator aborted (ncclCommAbort ends the stuck collectives), and the
+// context's TP calls fail from then on.
+constexpr int kWatchEvents = 64;
+
+struct NcclWatch {
+  kyro_ctx* ctx;
+  cudaEvent_t ev[kWatchEvents];
+  int next;
+  kyro::Watchdog* wd;
+};
+
+int watch_poll(void* user, void* probe) {
+  (void)user;
+  return cudaEventQuery((cudaEvent_t)probe) != cudaErrorNotReady;
+}
+
+void watch_abort(void* user) {
+  NcclWatch* w = (NcclWatch*)user;
+  const NcclApi* a = api();
+  if (a && w->ctx->nccl_comm) a->CommAbort((ncclComm_t)w->ctx->nccl_comm);
+  w->ctx->tp_aborted = 1;
+}
+
+void watch_setup(void* user) { cudaSetDevice(((NcclWatch*)user)->ctx->device); }
+
+int start_watch(kyro_ctx* ctx) {
+  NcclWatch* w = new NcclWatch();
+  w->ctx = ctx;
+  w->next = 0;
+  for (int i = 0; i < kWatchEvents; ++i) {
+    const cudaError_t err = cudaEventCreateWithFlags(&w->ev[i], cudaEventDisableTiming);
+    if (err != cudaSuccess) {
+      for (int j = 0; j < i; ++j) cudaEventDestroy(w->ev[j]);
+      delete w;
+      return kyro::cuda_error(err, "cudaEventCreate(NCCL watchdog)");
+    }
+  }
+  w->wd = new kyro::Watchdog(watch_poll, watch_abort, watch_setup, w);
+  ctx->watchdog = w;
+  return KYRO_OK;
+}
+
+void stop_watch(kyro_ctx* ctx) {
+  NcclWatch* w = (NcclWatch*)ctx->watchdog;
+  if (!w) return;
+  delete w->wd;  // joins the thread
+  for (int i = 0; i < kWatchEvents; ++i) cudaEventDestroy(w->ev[i]);
+  delete w;
+  ctx->watchdog = nullptr;
+}
+
 }  // namespace
 
 namespace kyro {
 namespace nccl {
+
+void watch(kyro_ctx* ctx) {
+  NcclWatch* w = (NcclWatch*)ctx->watchdog;
+  if (!w) return;
+  // a captured graph's replays run outside these calls: not watched
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(ctx->stream, &cs) != cudaSuccess ||
+      cs != cudaStreamCaptureStatusNone) {
+    cudaGetLastError();
+    return;
+  }
+  cudaEvent_t ev = w->ev[w->next % kWatchEvents];
+  if (w->wd->pending((void*)ev)) return;  // 64 calls still in flight: this one goes unwatched
+  ++w->next;
+  if (cudaEventRecord(ev, ctx->stream) != cudaSuccess) {
+    cudaGetLastError();
+    return;
+  }
+  w->wd->arm((void*)ev, ctx->wait_ns);
+}
 
 int all_gather(kyro_ctx* ctx, const void* send, void* recv, size_t bytes, const char* what) {
   const NcclApi* a;
@@ -108,10 +185,12 @@ int all_reduce_min_i32(kyro_ctx* ctx, const int32_t* send, int32_t* recv, size_t
 }
 
 void release(kyro_ctx* ctx) {
+  stop_watch(ctx);
   xchg::release(ctx);
   if (!ctx->nccl_comm) return;
   const NcclApi* a = api();
-  if (a) a->CommDestroy((ncclComm_t)ctx->nccl_comm);
+  // an aborted communicator is already gone
+  if (a && !ctx->tp_aborted) a->CommDestroy((ncclComm_t)ctx->nccl_comm);
   ctx->nccl_comm = nullptr;
   ctx->tp_rank = 0;
   ctx->tp_world = 1;
@@ -158,9 +237,43 @@ extern "C" int kyro_ctx_tp_init(kyro_ctx* ctx, const void* unique_id, int rank, 
   ctx->nccl_comm = comm;
   ctx->tp_rank = rank;
   ctx->tp_world = world;
-  const int st = kyro::xchg::init(ctx, dh);
+  int st = kyro::xchg::init(ctx, dh);
   cudaFree(dh);
+  // collectives that stay on NCCL get the host watchdog
+  if (st == KYRO_OK && !ctx->xchg_ready) st = start_watch(ctx);
   return st;
+}
+
+// The watchdog alone, on the host, with the caller's probe and abort hook:
+// arms one probe with a bound of timeout_ms and blocks until the probe
+// reports completion (KYRO_OK) or the bound passes and the abort hook has
+// run once (KYRO_ERR_TIMEOUT).  Needs no GPU.
+namespace {
+struct SelftestHooks {
+  int (*poll)(void*);
+  void (*on_abort)(void*);
+  void* user;
+};
+int selftest_poll(void* u, void*) { return ((SelftestHooks*)u)->poll(((SelftestHooks*)u)->user); }
+void selftest_abort(void* u) { ((SelftestHooks*)u)->on_abort(((SelftestHooks*)u)->user); }
+}  // namespace
+
+extern "C" int kyro_selftest_watchdog(uint32_t timeout_ms, int (*poll)(void* user),
+                                      void (*on_abort)(void* user), void* user) {
+  KY_REQUIRE(poll && on_abort, "kyro_selftest_watchdog: poll and on_abort are required");
+  KY_REQUIRE(timeout_ms >= 1 && timeout_ms <= 600000, "kyro_selftest_watchdog: %u ms",
+             timeout_ms);
+  SelftestHooks hooks{poll, on_abort, user};
+  bool fired;
+  {
+    kyro::Watchdog wd(selftest_poll, selftest_abort, nullptr, &hooks);
+    wd.arm(&hooks, (uint64_t)timeout_ms * 1000000ull);
+    fired = wd.wait_idle();
+  }
+  if (fired)
+    return kyro::set_error(KYRO_ERR_TIMEOUT, "kyro_selftest_watchdog: the probe did not complete "
+                                             "within %u ms; the abort hook ran", timeout_ms);
+  return KYRO_OK;
 }
 
 extern "C" int kyro_ctx_tp_transport(kyro_ctx* ctx) {

@@ -12,19 +12,27 @@
 // peers' flags on its own.
 //
 // Region of one rank:
-//   [0, 64 * 8)        flag[p]: the last round whose payload peer p has
-//                      completed in this region (64-byte apart)
-//   [512, 520)         this rank's round counter
+//   [0, 64 * 2 * 8)    flag[p][s]: the last round of parity s whose payload
+//                      peer p has completed in this region (64 bytes apart)
+//   [2048, 2056)       this rank's round counter
 //   [4096, 4096+2H)    two halves (round parity) of world slots, slot p
 //                      holding peer p's payload of the current round
 // Rounds are numbered on the device (the counter), so a captured CUDA graph
 // replays with fresh numbers.  A slot of parity s is written again only in
 // round s + 2, which a sender starts after it has seen the receiver's flag
 // of round s + 1, raised after the receiver's round-s kernel had finished
-// reading the slot.
+// reading the slot.  Flags are kept per parity for the same reason: a peer
+// can be one round ahead (it finishes round s as soon as this rank's flag
+// lands, then raises its round-(s+1) flag), but never two, so a wait on the
+// parity-s flag sees round s or nothing, and a peer that skipped round s
+// cannot satisfy it with its next round's flag.
 //
-// Every wait is bounded: a flag that does not arrive within ~2 s sets
-// KYRO_DEV_WAIT_TIMEOUT in the status word and the kernel returns.
+// Every wait is bounded: a flag that does not arrive within the context's
+// wait bound (kyro_ctx_set_wait_timeout; 2 s unless KYRO_WAIT_TIMEOUT_MS
+// says otherwise) sets KYRO_DEV_WAIT_TIMEOUT in the status word and the
+// kernel returns.  After a timeout the ranks' round counters no longer
+// agree and a late peer may still write into a slot that will be reused,
+// so the context must be destroyed and the group formed again.
 #include <cstdlib>
 #include <cstring>
 
@@ -34,10 +42,16 @@ namespace {
 
 constexpr size_t kCtlBytes = 4096;
 constexpr size_t kFlagStride = 64;
-constexpr size_t kSeqOffset = 512;
+constexpr size_t kSeqOffset = 2048;
+static_assert(2 * KYRO_MAX_TP_WORLD * kFlagStride <= kSeqOffset, "flags overlap the counter");
+
+// flag[p][s] of a region
+__device__ __forceinline__ unsigned long long* flag_of(uint8_t* region, int p, unsigned long long seq) {
+  return reinterpret_cast<unsigned long long*>(region + ((size_t)p * 2 + (size_t)(seq & 1ull)) *
+                                                             kFlagStride);
+}
 constexpr size_t kHalfBytes = size_t(4) << 20;  // one parity half: world slots of one round
 constexpr int kXchgThreads = 512;
-constexpr long long kWaitNs = 2000000000ll;  // bound of a wait on a peer's flag
 
 struct Peers {
   uint8_t* p[KYRO_MAX_TP_WORLD];  // every rank's region, mapped here (own: local)
@@ -81,9 +95,16 @@ __device__ __forceinline__ void copy_words(uint8_t* dst, const uint8_t* src, siz
 // One cluster of `world` CTAs; CTA p talks to rank p.  mode 0: recv gets the
 // world * bytes concatenation of every rank's payload (slot order = rank
 // order).  mode 1: recv[i] = max over ranks of the int32 payload element i.
+// A wait for a peer's flag gives up after wait_ns nanoseconds.  skip is
+// fault injection for the tests (always 0 otherwise): 1 makes this rank
+// skip the round towards its peers while staying alive (it neither stores
+// its payload in their regions nor raises their flags, so a peer waiting
+// for them runs into its bound); 2 skips its own slot as well, so that a
+// one-rank group waits for a flag that nothing sets.
 __global__ void __launch_bounds__(kXchgThreads)
 peer_exchange_kernel(Peers peers, int rank, int world, const uint8_t* __restrict__ send,
-                     uint8_t* __restrict__ recv, size_t bytes, int mode, uint32_t* status) {
+                     uint8_t* __restrict__ recv, size_t bytes, int mode, uint32_t* status,
+                     unsigned long long wait_ns, int skip) {
   const int p = blockIdx.x;  // == the CTA's rank in the cluster (the grid is one cluster)
   uint8_t* own = peers.p[rank];
   unsigned long long* ctr = reinterpret_cast<unsigned long long*>(own + kSeqOffset);
@@ -95,20 +116,20 @@ peer_exchange_kernel(Peers peers, int rank, int world, const uint8_t* __restrict
   const size_t half = (seq & 1ull) * kHalfBytes;
   // this rank's payload into rank p's slot `rank`
   const size_t stride = (bytes + 15) & ~size_t(15);  // slots start 16-byte aligned
-  copy_words(peers.p[p] + kCtlBytes + half + (size_t)rank * stride, send, bytes);
+  const bool send_p = skip == 0 || (skip == 1 && p == rank);
+  if (send_p) copy_words(peers.p[p] + kCtlBytes + half + (size_t)rank * stride, send, bytes);
   __threadfence_system();
   __syncthreads();
   __shared__ int timed_out;
   if (threadIdx.x == 0) {
     timed_out = 0;
-    st_release_sys(reinterpret_cast<unsigned long long*>(peers.p[p] + (size_t)rank * kFlagStride),
-                   seq);
-    // rank p's payload for this round has landed here once its flag reads seq
-    const unsigned long long* flag =
-        reinterpret_cast<const unsigned long long*>(own + (size_t)p * kFlagStride);
+    if (send_p) st_release_sys(flag_of(peers.p[p], rank, seq), seq);
+    // rank p's payload for this round has landed here once its flag of this
+    // round's parity reads seq
+    const unsigned long long* flag = flag_of(own, p, seq);
     const unsigned long long t0 = globaltimer();
     while (ld_acquire_sys(flag) < seq) {
-      if (globaltimer() - t0 > (unsigned long long)kWaitNs) {
+      if (globaltimer() - t0 > wait_ns) {
         kyro::dev::flag(status, KYRO_DEV_WAIT_TIMEOUT);
         timed_out = 1;
         break;
@@ -263,6 +284,11 @@ void release(kyro_ctx* ctx) {
 
 static int launch(kyro_ctx* ctx, const void* send, void* recv, size_t bytes, int mode,
                   const char* what) {
+  int skip = 0;
+  if (ctx->xchg_skip_rounds > 0) {  // fault injection: this rank skips the round
+    --ctx->xchg_skip_rounds;
+    skip = 1;
+  }
   Peers peers = {};
   for (int r = 0; r < ctx->tp_world; ++r) peers.p[r] = ctx->xchg_peer[r];
   cudaLaunchConfig_t cfg = {};
@@ -280,7 +306,8 @@ static int launch(kyro_ctx* ctx, const void* send, void* recv, size_t bytes, int
   cfg.numAttrs = 2;
   const cudaError_t err =
       cudaLaunchKernelEx(&cfg, peer_exchange_kernel, peers, ctx->tp_rank, ctx->tp_world,
-                         (const uint8_t*)send, (uint8_t*)recv, bytes, mode, ctx->d_status);
+                         (const uint8_t*)send, (uint8_t*)recv, bytes, mode, ctx->d_status,
+                         (unsigned long long)ctx->wait_ns, skip);
   if (err != cudaSuccess) return cuda_error(err, what);
   return KYRO_OK;
 }
@@ -310,3 +337,44 @@ int all_reduce_max_i32(kyro_ctx* ctx, const int32_t* send, int32_t* recv, size_t
 
 }  // namespace xchg
 }  // namespace kyro
+
+// ---------------------------------------------------------------- self-test
+//
+// The exchange kernel's bounded wait, run on one GPU: a one-rank "group"
+// over a caller-given region, with the round skipped, so the kernel waits
+// for a flag that nothing sets.  It must give up after the context's wait
+// bound, set KYRO_DEV_WAIT_TIMEOUT and return; the context stays usable.
+extern "C" int kyro_selftest_exchange_timeout(kyro_ctx* ctx, void* region, size_t region_bytes) {
+  KY_TRY(kyro::enter(ctx));
+  KY_REQUIRE(region && region_bytes >= kCtlBytes && (uintptr_t)region % 256 == 0,
+             "kyro_selftest_exchange_timeout: region must be 256-byte aligned and hold %zu bytes",
+             kCtlBytes);
+  cudaError_t err = cudaMemsetAsync(region, 0, kCtlBytes, ctx->stream);
+  if (err != cudaSuccess) return kyro::cuda_error(err, "cudaMemsetAsync(self-test region)");
+  Peers peers = {};
+  peers.p[0] = (uint8_t*)region;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(kXchgThreads);
+  cfg.stream = ctx->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  err = cudaLaunchKernelEx(&cfg, peer_exchange_kernel, peers, 0, 1, (const uint8_t*)nullptr,
+                           (uint8_t*)nullptr, (size_t)0, 0, ctx->d_status,
+                           (unsigned long long)ctx->wait_ns, 2);
+  if (err != cudaSuccess) return kyro::cuda_error(err, "peer_exchange_kernel (self-test)");
+  return KYRO_OK;
+}
+
+extern "C" int kyro_ctx_tp_inject_skip(kyro_ctx* ctx, int32_t rounds) {
+  if (!ctx) return kyro::set_error(KYRO_ERR_INVALID_ARG, "null kyro_ctx");
+  KY_REQUIRE(rounds >= 0, "kyro_ctx_tp_inject_skip: rounds = %d", rounds);
+  KY_REQUIRE(ctx->xchg_ready, "kyro_ctx_tp_inject_skip: the context's exchange is not on peer memory");
+  ctx->xchg_skip_rounds = rounds;
+  return KYRO_OK;
+}

@@ -2230,6 +2230,11 @@ int kyro_spec_accept_tp(kyro_ctx* ctx, const kyro_accept_params* p, const float*
     return kyro_spec_accept(ctx, p, target_shard, draft_shard, draft_tokens, out_accept_len,
                             out_tokens, out_num_tokens, out_probs, workspace, workspace_bytes);
   KY_REQUIRE(ctx->nccl_comm, "kyro_spec_accept_tp: the context has no group");
+  if (ctx->tp_aborted)
+    return kyro::set_error(KYRO_ERR_TIMEOUT,
+                           "kyro_spec_accept_tp: a collective of this group exceeded the wait "
+                           "bound and the group was aborted; destroy the context and form the "
+                           "group again");
   KY_REQUIRE(p->batch >= 0, "kyro_spec_accept_tp: batch = %d", p->batch);
   KY_REQUIRE(p->num_draft >= 0 && p->num_draft <= kMaxDraft,
              "kyro_spec_accept_tp: num_draft = %d (0..%d)", p->num_draft, kMaxDraft);
@@ -2295,10 +2300,13 @@ int kyro_spec_accept_tp(kyro_ctx* ctx, const kyro_accept_params* p, const float*
   a.recv4 = ws.recv4;
   a.W2 = ws.W2;
   const bool vec = use_vec(target_shard, a.qlog, Vl);
-  if (vec && stoch) return launch_tp<true, true>(ctx, a);
-  if (vec) return launch_tp<true, false>(ctx, a);
-  if (stoch) return launch_tp<false, true>(ctx, a);
-  return launch_tp<false, false>(ctx, a);
+  int st;
+  if (vec && stoch) st = launch_tp<true, true>(ctx, a);
+  else if (vec) st = launch_tp<true, false>(ctx, a);
+  else if (stoch) st = launch_tp<false, true>(ctx, a);
+  else st = launch_tp<false, false>(ctx, a);
+  if (st == KYRO_OK) kyro::nccl::watch(ctx);
+  return st;
 }
 
 size_t kyro_spec_accept_tree_workspace_size(const kyro_tree_params* p) {

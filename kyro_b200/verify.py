@@ -89,6 +89,15 @@ class Context:
         peer memory)."""
         return ("none", "nccl", "peer")[_lib.load().kyro_ctx_tp_transport(self._h)]
 
+    def set_wait_timeout(self, ms: int):
+        """Bound of this context's waits on other ranks (kyro_ctx_set_wait_timeout)."""
+        check(_lib.load().kyro_ctx_set_wait_timeout(self._h, int(ms)))
+
+    def inject_skip(self, rounds: int = 1):
+        """Fault injection: this rank skips its next `rounds` peer-memory
+        exchange rounds (kyro_ctx_tp_inject_skip)."""
+        check(_lib.load().kyro_ctx_tp_inject_skip(self._h, int(rounds)))
+
     def device_status(self, clear: bool = True) -> int:
         flags = C.c_uint32(0)
         check(_lib.load().kyro_ctx_device_status(self._h, C.byref(flags), int(clear)))

@@ -9,6 +9,7 @@ for num_shards = R, bit for bit.  Skipped with fewer than two GPUs.
 """
 import os
 import sys
+import time
 
 import numpy as np
 import pytest
@@ -120,3 +121,74 @@ def test_vocab_sharded_accept_matches_oracle(transport):
             assert np.array_equal(num, rnum), (rank, case)
             if probs is not None:
                 assert np.array_equal(probs, rprobs), (rank, case)
+
+
+def _skip_rank_main(rank, world, q_id, q_out):
+    """Both ranks join a peer-memory group; rank 1 skips its first exchange
+    round towards rank 0 (it stays alive and runs the rest of the call), so
+    rank 0's first round must run into its 100 ms bound, flag
+    KYRO_DEV_WAIT_TIMEOUT and return instead of hanging."""
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    sys.path.insert(0, ROOT)
+    from kyro_b200 import _lib
+    from kyro_b200.verify import Context, spec_accept_tp, tp_unique_id
+    torch.cuda.set_device(rank)
+    ctx = Context(rank)
+    try:
+        if rank == 0:
+            uid = tp_unique_id()
+            q_id.put(uid)
+        else:
+            uid = q_id.get(timeout=120)
+        ctx.tp_init(uid, rank, world)
+        if ctx.tp_transport != "peer":
+            raise RuntimeError(f"transport {ctx.tp_transport}")
+        # rank 0 gives up after 100 ms; rank 1's later rounds wait about that
+        # long for rank 0 and keep a bound well above it
+        ctx.set_wait_timeout(100 if rank == 0 else 3000)
+        B, k, V = 4, 3, 32000
+        tgt, drf = _inputs(B, k, V, 1)
+        Vs = V // world
+        dev = torch.device("cuda", rank)
+        ts = tgt[:, :, rank * Vs:(rank + 1) * Vs].contiguous().to(dev)
+        ds = drf[:, :, rank * Vs:(rank + 1) * Vs].contiguous().to(dev)
+        drafts = torch.zeros(B, k, dtype=torch.int32, device=dev)
+        if rank == 1:
+            ctx.inject_skip(1)
+        t0 = time.monotonic()
+        spec_accept_tp(ctx, ts, ds, drafts, V, seed=1)
+        status = ctx.device_status(clear=True)
+        q_out.put((rank, status, time.monotonic() - t0, None))
+    except Exception as e:
+        q_out.put((rank, None, None, repr(e)))
+    finally:
+        ctx.close()
+
+
+def test_skipped_round_times_out_on_the_peer():
+    n = torch.cuda.device_count() if torch.cuda.is_available() else 0
+    if n < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    from kyro_b200._lib import DEV_WAIT_TIMEOUT
+    mpc = mp.get_context("spawn")
+    q_id, q_out = mpc.Queue(), mpc.Queue()
+    procs = [mpc.Process(target=_skip_rank_main, args=(r, 2, q_id, q_out)) for r in range(2)]
+    for p in procs:
+        p.start()
+    outs = {}
+    try:
+        for _ in range(2):
+            rank, status, dt, err = q_out.get(timeout=300)
+            outs[rank] = (status, dt, err)
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    for rank in (0, 1):
+        assert outs[rank][2] is None, outs
+    assert outs[0][0] & DEV_WAIT_TIMEOUT, outs
+    assert outs[0][1] < 10.0, outs
+    # rank 1 skipped its own stores, but rank 0 raised every flag it waited for
+    assert not (outs[1][0] & DEV_WAIT_TIMEOUT), outs
