@@ -2,6 +2,8 @@
 // Philox test aid.  The context plays the part of the per-worker state the
 // reference keeps in Worker (src/worker.rs:13-38): the device it runs on and
 // the stream its kernels go to.
+#include <atomic>
+#include <chrono>
 #include <cstdlib>
 #include <mutex>
 
@@ -67,7 +69,7 @@ extern "C" {
 int kyro_version(void) { return KYRO_VERSION; }
 
 const char* kyro_kernel_names(void) {
-  return "accept_stats_kernel;accept_decide_kernel;accept_final_kernel;accept_tree_kernel;accept_tree_cluster_kernel;"
+  return "accept_stats_kernel;accept_decide_kernel;accept_final_kernel;accept_wave_kernel;accept_tree_kernel;accept_tree_cluster_kernel;"
          "accept_tp_max_kernel;accept_tp_sum_kernel;accept_tp_decide_kernel;"
          "accept_tp_search_kernel;accept_tp_write_kernel;verify_attention_kernel;"
          "kv_reserve_kernel;kv_commit_kernel;kv_tree_move_kernel;kv_write_kernel;rope_kv_write_kernel;kv_block_copy_kernel;"
@@ -129,6 +131,12 @@ int kyro_ctx_create(int device, void* stream, kyro_ctx** out) {
   ctx->tp_world = 1;
   ctx->attn_epoch = 0;
   ctx->attn_ws_zeroed = nullptr;
+  {
+    // a salt per context: tags of different contexts differ
+    static std::atomic<uint32_t> contexts{0};
+    const uint64_t t = (uint64_t)std::chrono::steady_clock::now().time_since_epoch().count();
+    ctx->pipe_salt = (uint32_t)(t ^ (t >> 32)) ^ (0x9E3779B9u * (contexts.fetch_add(1) + 1u));
+  }
   ctx->xchg_ready = false;
   ctx->xchg_local = nullptr;
   for (int r = 0; r < KYRO_MAX_TP_WORLD; ++r) ctx->xchg_peer[r] = nullptr;
@@ -136,12 +144,15 @@ int kyro_ctx_create(int device, void* stream, kyro_ctx** out) {
   ctx->wait_ns = kyro::default_wait_ns();
   ctx->watchdog = nullptr;
   ctx->tp_aborted = 0;
-  err = cudaMalloc(&ctx->d_status, 16);
+  // one allocation: the status word, then the acceptance pipeline's counts
+  constexpr size_t kCtxBytes = 256 + 4 * KYRO_PIPE_COUNTS;
+  err = cudaMalloc(&ctx->d_status, kCtxBytes);
   if (err != cudaSuccess) {
     delete ctx;
     return kyro::cuda_error(err, "cudaMalloc(status word)");
   }
-  err = cudaMemset(ctx->d_status, 0, 16);
+  ctx->d_pipe_counts = ctx->d_status + 64;
+  err = cudaMemset(ctx->d_status, 0, kCtxBytes);
   if (err != cudaSuccess) {
     cudaFree(ctx->d_status);
     delete ctx;
@@ -183,6 +194,18 @@ int kyro_ctx_device_status(kyro_ctx* ctx, uint32_t* out_flags, int clear) {
   if (clear) {
     err = cudaMemset(ctx->d_status, 0, 4);
     if (err != cudaSuccess) return kyro::cuda_error(err, "clear status word");
+    // a wait that gave up may have left a call unfinished: move the
+    // acceptance pipeline to a new generation (a new tag) with no sequence
+    // counted
+    if (flags & KYRO_DEV_WAIT_TIMEOUT) {
+      uint32_t counts[2];
+      err = cudaMemcpy(counts, ctx->d_pipe_counts, 8, cudaMemcpyDeviceToHost);
+      if (err != cudaSuccess) return kyro::cuda_error(err, "read pipeline counts");
+      counts[0] += 1u;
+      counts[1] = 0u;
+      err = cudaMemcpy(ctx->d_pipe_counts, counts, 8, cudaMemcpyHostToDevice);
+      if (err != cudaSuccess) return kyro::cuda_error(err, "reset pipeline counts");
+    }
   }
   if (out_flags) *out_flags = flags;
   return KYRO_OK;

@@ -14,6 +14,8 @@
 #include "../../include/kyro_spec.h"
 
 #define KYRO_MAX_TP_WORLD 8
+// counts of the acceptance pipeline kept in each context (sampler.cu)
+#define KYRO_PIPE_COUNTS 128
 
 struct kyro_ctx {
   int device;
@@ -27,6 +29,11 @@ struct kyro_ctx {
   // workspace whose tickets this context has zeroed
   uint32_t attn_epoch;
   const void* attn_ws_zeroed;
+  // the acceptance pipeline's generation count and finished-sequence
+  // count (device words owned by the context; sampler.cu), and the salt
+  // of its record tags
+  uint32_t* d_pipe_counts;
+  uint32_t pipe_salt;
   // the sharded sampler's exchange rounds over NVLink peer memory
   // (peer_exchange.cu): this rank's region and every rank's mapping of it
   bool xchg_ready;

@@ -12,7 +12,10 @@
 // integer (fix62) inverse-CDF weights.  The kernels follow exactly those
 // trees, so they reproduce the sequential oracle bit for bit.
 //
-// Three launches, none of which waits on another CTA:
+// Three launches (the chain acceptance chains them: the decide and final
+// kernels start while their predecessor drains and wait for the tagged
+// records they read, see "chained acceptance"; the other callers wait for
+// the whole predecessor grid):
 //   accept_stats_kernel   persistent, one warp per 512-entry chunk of every
 //                         row (target and draft), grid-stride.  A lane holds
 //                         16 logits in registers: chunk max (or argmax),
@@ -30,6 +33,7 @@
 //
 // This file is compiled with --fmad=false; the shared arithmetic also uses
 // explicit round-to-nearest intrinsics.
+#include <algorithm>
 #include <mutex>
 
 #include "kyro_internal.cuh"
@@ -52,12 +56,29 @@ constexpr int kFinalPerCta = kWarps * kFinalPerWarp;
 
 static_assert(kChunk == 512, "the kernels assume 16 logits per lane");
 
+// A chunk's statistics, stored as two 64-bit words that each carry a tag in
+// their high half: (m, tag) and (E or arg, tag).  Each word is written and
+// read as one 64-bit access, so a reader that sees the tag sees the value
+// stored with it.  The chained acceptance tags every record with its call's
+// tag and its decide kernel waits for those tags (see "chained acceptance");
+// the other launches write tag 0, which no chained call uses.
 struct ChunkStat {
-  float m;      // chunk max of s = z * inv_t (or of z, greedy)
-  int32_t arg;  // lowest index attaining m (greedy)
-  float E;      // ky_chunk_sum of ky_exp(s - m) over the chunk
-  float _pad;
+  float m;        // chunk max of s = z * inv_t (or of z, greedy)
+  uint32_t tag;
+  float E;        // ky_chunk_sum of ky_exp(s - m) (stochastic); the bits of
+                  // the lowest index attaining m (greedy)
+  uint32_t tag2;
 };
+
+__host__ __device__ inline int32_t stat_arg(const ChunkStat& c) {
+#if defined(__CUDA_ARCH__)
+  return __float_as_int(c.E);
+#else
+  int32_t v;
+  memcpy(&v, &c.E, 4);
+  return v;
+#endif
+}
 
 struct RowStat {
   float M;      // row max
@@ -134,7 +155,15 @@ struct Args {
   int32_t* out_num_tokens;
   float* out_probs;             // accept: [B,k,2] (p,q); sampler: [rows]
   ChunkStat* stats;             // [B*R][nchunks]
-  float* ex;                    // [B*R] e at the draft token
+  unsigned long long* ex;       // [B*R] (e at the draft token, tag) as one 64-bit word
+  uint32_t* final_ready;        // [B] the call's tag once final_rows[b] is written (poll)
+  // Chained acceptance (poll != 0): the decide and final kernels start
+  // while their predecessor drains and wait for the records they read
+  // instead of the whole grid (see "chained acceptance" below)
+  int poll;
+  const uint32_t* gen;          // the context's generation count
+  uint32_t* done;               // sequences finished in this call
+  uint32_t salt;                // the context's tag salt
   FinalRow* final_rows;         // [B]
   unsigned long long* W;        // [B][nchunks] weight sums of the chosen rows
   uint32_t* cnt_c;              // [B] finished weight sums per sequence
@@ -166,7 +195,8 @@ struct Workspace {
   uint32_t* cnt_c;
   size_t counter_bytes;
   ChunkStat* stats;
-  float* ex;
+  unsigned long long* ex;
+  uint32_t* final_ready;
   FinalRow* final_rows;
   unsigned long long* W;
   size_t bytes;
@@ -181,8 +211,10 @@ Workspace carve(void* base, int64_t B, int64_t R, int64_t nchunks) {
   w.counter_bytes = off;
   w.stats = (ChunkStat*)(p + off);
   off += align_up(sizeof(ChunkStat) * (size_t)(B * R * nchunks));
-  w.ex = (float*)(p + off);
-  off += align_up(sizeof(float) * (size_t)(B * R));
+  w.ex = (unsigned long long*)(p + off);
+  off += align_up(sizeof(unsigned long long) * (size_t)(B * R));
+  w.final_ready = (uint32_t*)(p + off);
+  off += align_up(sizeof(uint32_t) * (size_t)B);
   w.final_rows = (FinalRow*)(p + off);
   off += align_up(sizeof(FinalRow) * (size_t)B);
   w.W = (unsigned long long*)(p + off);
@@ -375,6 +407,33 @@ __device__ __forceinline__ int64_t sample_row(const Args& a, int b) {
   return (int64_t)(b / a.pos_div) * a.seq_rows + b % a.pos_div;
 }
 
+// Chunk statistics, e values and final-row descriptors can be produced by a
+// kernel that is still running (the chained acceptance), so they are read
+// with ld.global.cg: from L2, never from a possibly stale L1 line.
+__device__ __forceinline__ ChunkStat ld_stat(const ChunkStat* p) {
+  unsigned long long lo, hi;
+  asm volatile("ld.global.cg.v2.u64 {%0, %1}, [%2];" : "=l"(lo), "=l"(hi) : "l"(p) : "memory");
+  ChunkStat s;
+  s.m = __uint_as_float((uint32_t)lo);
+  s.tag = (uint32_t)(lo >> 32);
+  s.E = __uint_as_float((uint32_t)hi);
+  s.tag2 = (uint32_t)(hi >> 32);
+  return s;
+}
+
+// Both words of a chunk record, each one 64-bit store.
+__device__ __forceinline__ void st_stat(ChunkStat* p, float m, float e, uint32_t tag) {
+  const unsigned long long lo = (unsigned long long)__float_as_uint(m) | ((unsigned long long)tag << 32);
+  const unsigned long long hi = (unsigned long long)__float_as_uint(e) | ((unsigned long long)tag << 32);
+  asm volatile("st.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(lo), "l"(hi) : "memory");
+}
+
+__device__ __forceinline__ float ld_ex(const Args& a, int64_t srow) {
+  return __uint_as_float((uint32_t)__ldcg(&a.ex[srow]));
+}
+
+__device__ __forceinline__ float ld_m(const ChunkStat* p) { return __ldcg(&p->m); }
+
 __device__ __forceinline__ const float* stats_row_ptr(const Args& a, int b, int r) {
   if (a.sample) return a.plog + sample_row(a, b) * a.V;
   if (r <= a.k) return a.plog + ((int64_t)b * (a.k + 1) + r) * a.V;
@@ -386,6 +445,159 @@ __device__ __forceinline__ int draft_token_of_row(const Args& a, int b, int r) {
   if (r < a.k) return a.draft_tokens[(int64_t)b * a.k + r];
   if (r > a.k) return a.draft_tokens[(int64_t)b * a.k + (r - a.k - 1)];
   return -1;
+}
+
+// ------------------------------------------------------------ chained acceptance
+//
+// The chain acceptance's three kernels (stats, decide, final) run with
+// programmatic dependent launch: a kernel's CTAs become resident while its
+// predecessor drains.  Instead of waiting for the whole predecessor grid,
+// they wait for the records they read: every chunk record and every e value
+// carries the call's tag in each 64-bit word it is stored in, and a decide
+// CTA publishes its final-row descriptor with a tagged flag (release /
+// acquire).  So the decide step of a sequence starts as soon as its rows'
+// records are in, overlapping the tail of the stats pass, and a final CTA
+// as soon as its sequence is decided.  Every wait is for a kernel whose CTAs
+// have all been resident since before the waiting CTA launched (a dependent
+// grid launches only after every CTA of its predecessor has started), so
+// every wait ends; each is also bounded (KYRO_DEV_WAIT_TIMEOUT).  Each kernel
+// still calls griddepcontrol.wait before it exits, so it never completes
+// before its predecessor.
+//
+// The tag of a call is a hash of a per-context salt and a generation count
+// on the device, read by every CTA at its start; the call's last finished
+// sequence advances the count, so every call, and every replay of a
+// captured graph, has a new tag, and a record left by an earlier call,
+// another context or other data does not match it (a hash collision aside,
+// about 2^-32 per record).
+
+constexpr long long kChainWaitNs = 1000000000ll;
+
+__device__ __forceinline__ uint32_t chain_tag(uint32_t gen, uint32_t salt) {
+  // murmur3's finaliser: a bijection, so distinct generations give distinct tags
+  uint32_t h = gen ^ salt;
+  h ^= h >> 16;
+  h *= 0x85ebca6bu;
+  h ^= h >> 13;
+  h *= 0xc2b2ae35u;
+  h ^= h >> 16;
+  return h == 0u ? 1u : h;  // tag 0 belongs to the unchained launches
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ unsigned long long chain_clock() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ uint32_t call_tag(const Args& a) {
+  return a.poll ? chain_tag(ld_acquire_gpu32(a.gen), a.salt) : 0u;
+}
+
+__device__ __forceinline__ bool stat_tagged(const ChunkStat* p, uint32_t tag) {
+  const ChunkStat c = ld_stat(p);
+  return c.tag == tag && c.tag2 == tag;
+}
+
+// The whole warp waits until every chunk record of stats row srow carries
+// `tag` (bounded).  Lane l watches chunks l, l + 32, ...; its loads go out
+// together, then only the records still missing are polled again.
+__device__ __forceinline__ void wait_row(const Args& a, int64_t srow, uint32_t tag) {
+  const int lane = threadIdx.x & 31;
+  const ChunkStat* st = a.stats + srow * a.nchunks;
+  const unsigned long long t0 = chain_clock();
+  for (int g = 0; g < a.nchunks; g += 256) {
+    unsigned missing = 0;  // bit j: chunk g + j*32 + lane not yet tagged
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = g + j * 32 + lane;
+      if (c < a.nchunks && !stat_tagged(st + c, tag)) missing |= 1u << j;
+    }
+    while (__any_sync(0xffffffffu, missing != 0)) {
+      if (chain_clock() - t0 > (unsigned long long)kChainWaitNs) {
+        if (lane == 0) kyro::dev::flag(a.status, KYRO_DEV_WAIT_TIMEOUT);
+        return;
+      }
+      __nanosleep(256);
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if ((missing >> j) & 1u)
+          if (stat_tagged(st + g + j * 32 + lane, tag)) missing &= ~(1u << j);
+    }
+  }
+}
+
+// Lane j waits for what accept test j reads (the draft token's e in the
+// target and the draft row, and those chunks' records), bounded.  A draft
+// token outside the vocabulary has none (and the test reads none).
+__device__ __forceinline__ void wait_tests(const Args& a, int b, uint32_t tag) {
+  const int lane = threadIdx.x & 31;
+  const unsigned long long t0 = chain_clock();
+  const int64_t r0 = (int64_t)b * a.R;
+  for (int j = lane; j < a.k; j += 32) {
+    const int x = a.draft_tokens[(int64_t)b * a.k + j];
+    if (x < 0 || x >= a.V) continue;
+    const int cx = x / kChunk;
+    for (int side = 0; side < 2; ++side) {
+      const int64_t srow = side == 0 ? r0 + j : r0 + a.k + 1 + j;
+      while ((uint32_t)(__ldcg(&a.ex[srow]) >> 32) != tag ||
+             !stat_tagged(a.stats + srow * a.nchunks + cx, tag)) {
+        if (chain_clock() - t0 > (unsigned long long)kChainWaitNs) {
+          kyro::dev::flag(a.status, KYRO_DEV_WAIT_TIMEOUT);
+          break;
+        }
+        __nanosleep(256);
+      }
+    }
+  }
+  __syncwarp();
+}
+
+__device__ __forceinline__ FinalRow ld_final_row(const FinalRow* g) {
+  FinalRow fr;
+  fr.p_row = __ldcg(&g->p_row);
+  fr.q_row = __ldcg(&g->q_row);
+  fr.p_stat = __ldcg(&g->p_stat);
+  fr.q_stat = __ldcg(&g->q_stat);
+  fr.Mp = __ldcg(&g->Mp);
+  fr.Mq = __ldcg(&g->Mq);
+  fr.Sp = __ldcg(&g->Sp);
+  fr.Sq = __ldcg(&g->Sq);
+  fr.odd = __ldcg(&g->odd);
+  fr.out_index = __ldcg(&g->out_index);
+  fr.skip = __ldcg(&g->skip);
+  fr._pad = 0;
+  return fr;
+}
+
+// One thread waits until a 32-bit word reads `tag` (bounded).
+__device__ __forceinline__ void wait_flag(const Args& a, const uint32_t* word, uint32_t tag) {
+  if (ld_acquire_gpu32(word) == tag) return;
+  const unsigned long long t0 = chain_clock();
+  while (ld_acquire_gpu32(word) != tag) {
+    if (chain_clock() - t0 > (unsigned long long)kChainWaitNs) {
+      kyro::dev::flag(a.status, KYRO_DEV_WAIT_TIMEOUT);
+      return;
+    }
+    __nanosleep(256);
+  }
+}
+
+// One more finished sequence; the call's last one advances the generation,
+// which gives the next call its tag.  One thread.
+__device__ __forceinline__ void chain_seq_done(const Args& a) {
+  __threadfence();
+  if (atomicAdd(a.done, 1u) == (uint32_t)(a.B - 1)) {
+    *a.done = 0u;
+    __threadfence();
+    atomicAdd(const_cast<uint32_t*>(a.gen), 1u);
+  }
 }
 
 // ------------------------------------------------------------ stats kernel
@@ -443,7 +655,7 @@ __device__ __forceinline__ void load_slice(const Args& a, uint32_t u, Slice& s) 
 
 // Reduce one chunk and store its statistics.
 template <bool STOCH>
-__device__ __forceinline__ void reduce_slice(const Args& a, Slice& s) {
+__device__ __forceinline__ void reduce_slice(const Args& a, Slice& s, uint32_t tag) {
   const int lane = threadIdx.x & 31;
   const int64_t base = (int64_t)s.c * kChunk;
   ChunkStat st;
@@ -500,9 +712,7 @@ __device__ __forceinline__ void reduce_slice(const Args& a, Slice& s) {
     f2_unpack(acc01, a0, a1);
     f2_unpack(acc23, a2, a3);
     st.m = m;
-    st.arg = 0;
     st.E = warp_butterfly_f(__fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3)));
-    st._pad = 0.0f;
     // e at the draft token, by the lane that holds it (s.v holds z * inv_t)
     const int64_t xo = (int64_t)s.x - base;
     if (s.x >= 0 && s.x < a.V && xo >= 0 && xo < kChunk && lane == (int)((xo >> 2) & 31)) {
@@ -511,7 +721,8 @@ __device__ __forceinline__ void reduce_slice(const Args& a, Slice& s) {
 #pragma unroll
       for (int i = 1; i < kPerLane; ++i)
         if (i == q) z = s.v[i];
-      a.ex[s.srow] = exp_fast(KY_FSUB(z, m));
+      a.ex[s.srow] = (unsigned long long)__float_as_uint(exp_fast(KY_FSUB(z, m))) |
+                     ((unsigned long long)tag << 32);
     }
   } else {
     float m = -INFINITY;
@@ -524,11 +735,9 @@ __device__ __forceinline__ void reduce_slice(const Args& a, Slice& s) {
       }
     kyro::dev::warp_argmax(m, arg);
     st.m = m;
-    st.arg = arg;
-    st.E = 0.0f;
-    st._pad = 0.0f;
+    st.E = __int_as_float(arg);
   }
-  if (lane == 0) a.stats[(int64_t)s.srow * a.nchunks + s.c] = st;
+  if (lane == 0) st_stat(a.stats + (int64_t)s.srow * a.nchunks + s.c, st.m, st.E, tag);
 }
 
 // Persistent and grid-stride: warp w takes units w, w + W, w + 2W, ... (W =
@@ -537,6 +746,7 @@ __device__ __forceinline__ void reduce_slice(const Args& a, Slice& s) {
 template <bool VEC, bool STOCH>
 __global__ void __launch_bounds__(kThreads, kStatsMinCtas) accept_stats_kernel(Args a) {
   allow_dependents();
+  const uint32_t tag = call_tag(a);
   const uint32_t stride = gridDim.x * kWarps;
   uint32_t u = blockIdx.x * kWarps + (threadIdx.x >> 5);
   if (u >= a.units) return;
@@ -545,12 +755,12 @@ __global__ void __launch_bounds__(kThreads, kStatsMinCtas) accept_stats_kernel(A
   while (true) {
     uint32_t un = u + stride;
     if (un < a.units) load_slice<VEC>(a, un, s1);
-    reduce_slice<STOCH>(a, s0);
+    reduce_slice<STOCH>(a, s0, tag);
     if (un >= a.units) break;
     u = un;
     un = u + stride;
     if (un < a.units) load_slice<VEC>(a, un, s0);
-    reduce_slice<STOCH>(a, s1);
+    reduce_slice<STOCH>(a, s1, tag);
     if (un >= a.units) break;
     u = un;
   }
@@ -579,7 +789,7 @@ __device__ __forceinline__ RowStat row_stat(const Args& a, int64_t srow) {
       mm[j] = -INFINITY;
       ee[j] = 0.0f;
       if (c < nc) {
-        const ChunkStat cs = st[c];
+        const ChunkStat cs = ld_stat(st + c);
         mm[j] = cs.m;
         ee[j] = cs.E;
       }
@@ -601,7 +811,7 @@ __device__ __forceinline__ RowStat row_stat(const Args& a, int64_t srow) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const int c = g + j * 32 + lane;
-        mm[j] = c < nc ? st[c].m : -INFINITY;
+        mm[j] = c < nc ? ld_m(st + c) : -INFINITY;
       }
 #pragma unroll
       for (int j = 0; j < 8; ++j) M = fmaxf(M, mm[j]);
@@ -613,8 +823,9 @@ __device__ __forceinline__ RowStat row_stat(const Args& a, int64_t srow) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const int c = g + j * 32 + lane;
-        mm[j] = c < nc ? st[c].m : 0.0f;
-        ee[j] = c < nc ? st[c].E : 0.0f;
+        const ChunkStat cs = ld_stat(st + (c < nc ? c : 0));
+        mm[j] = c < nc ? cs.m : 0.0f;
+        ee[j] = c < nc ? cs.E : 0.0f;
       }
 #pragma unroll
       for (int j = 0; j < 8; ++j)
@@ -631,8 +842,9 @@ __device__ __forceinline__ RowStat row_stat(const Args& a, int64_t srow) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const int c = g + j * 32 + lane;
-        mm[j] = c < nc ? st[c].m : -INFINITY;
-        aa[j] = c < nc ? st[c].arg : 0x7fffffff;
+        const ChunkStat cs = ld_stat(st + (c < nc ? c : 0));
+        mm[j] = c < nc ? cs.m : -INFINITY;
+        aa[j] = c < nc ? stat_arg(cs) : 0x7fffffff;
       }
 #pragma unroll
       for (int j = 0; j < 8; ++j)
@@ -664,10 +876,10 @@ __device__ __forceinline__ TestInputs load_test(const Args& a, int b, int j) {
   t.x = a.draft_tokens[(int64_t)b * a.k + j];
   if (a.stoch && t.x >= 0 && t.x < a.V) {
     const int cx = t.x / kChunk;
-    t.ep = a.ex[r0 + j];
-    t.eq = a.ex[r0 + a.k + 1 + j];
-    t.mp = a.stats[(r0 + j) * a.nchunks + cx].m;
-    t.mq = a.stats[(r0 + a.k + 1 + j) * a.nchunks + cx].m;
+    t.ep = ld_ex(a, r0 + j);
+    t.eq = ld_ex(a, r0 + a.k + 1 + j);
+    t.mp = ld_m(&a.stats[(r0 + j) * a.nchunks + cx]);
+    t.mq = ld_m(&a.stats[(r0 + a.k + 1 + j) * a.nchunks + cx]);
   }
   return t;
 }
@@ -793,12 +1005,14 @@ __global__ void __launch_bounds__(kDecideWarps * 32) accept_decide_kernel(Args a
   __shared__ RowStat rs[kMaxRows];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   const int b = blockIdx.x;
-  grid_dependency_wait();  // the chunk statistics are complete
+  const uint32_t tag = call_tag(a);
+  if (!a.poll) grid_dependency_wait();  // the chunk statistics are complete
   allow_dependents();
   if (threadIdx.x == 0) a.cnt_c[b] = 0;  // the final kernel's last-arriver count
   // warp 0 fetches the test inputs (lane j: tests j and j + 32)
   TestInputs t0, t1;
   if (warp == 0 && !a.sample) {
+    if (a.poll && a.stoch) wait_tests(a, b, tag);
     t0 = load_test(a, b, lane);
     t1 = load_test(a, b, lane + 32);
   }
@@ -807,12 +1021,27 @@ __global__ void __launch_bounds__(kDecideWarps * 32) accept_decide_kernel(Args a
   const int w0 = (a.sample || nwarps == 1) ? 0 : 1;
   if (warp >= w0) {
     for (int r = warp - w0; r < a.R; r += nwarps - w0) {
+      if (a.poll) wait_row(a, (int64_t)b * a.R + r, tag);
       const RowStat s = row_stat(a, (int64_t)b * a.R + r);
       if (lane == 0) rs[r] = s;
     }
   }
   __syncthreads();
-  if (warp == 0) decide_sequence(a, b, rs, t0, t1);
+  if (warp == 0) {
+    decide_sequence(a, b, rs, t0, t1);
+    __syncwarp();
+    if (a.poll && lane == 0) {
+      if (a.stoch) {
+        // the descriptor, the zeroed count and the tokens before the flag
+        __threadfence();
+        asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(a.final_ready + b), "r"(tag)
+                     : "memory");
+      } else {
+        chain_seq_done(a);  // greedy: the decision wrote every token
+      }
+    }
+  }
+  if (a.poll) grid_dependency_wait();  // complete only after the stats kernel
 }
 
 // ------------------------------------------------------------ final kernel
@@ -911,8 +1140,8 @@ __device__ __forceinline__ unsigned long long chunk_weight_sum(const Args& a, co
                                                                bool residual, int c) {
   float4 zp[kVec], zq[kVec];
   load_final_chunk<VEC>(a, fr, residual, c, zp, zq);
-  const float mp = a.stats[fr.p_stat * a.nchunks + c].m;
-  const float mq = residual ? a.stats[fr.q_stat * a.nchunks + c].m : 0.0f;
+  const float mp = ld_m(&a.stats[fr.p_stat * a.nchunks + c]);
+  const float mq = residual ? ld_m(&a.stats[fr.q_stat * a.nchunks + c]) : 0.0f;
   const FinalScale s = final_scale(fr, residual, mp, mq);
   unsigned long long t = 0;
 #pragma unroll
@@ -932,8 +1161,8 @@ __device__ __forceinline__ void chunk_weight_sums2(const Args& a, const FinalRow
                                                    unsigned long long& t_p) {
   float4 zp[kVec], zq[kVec];
   load_final_chunk<VEC>(a, fr, residual, c, zp, zq);
-  const float mp = a.stats[fr.p_stat * a.nchunks + c].m;
-  const float mq = residual ? a.stats[fr.q_stat * a.nchunks + c].m : 0.0f;
+  const float mp = ld_m(&a.stats[fr.p_stat * a.nchunks + c]);
+  const float mq = residual ? ld_m(&a.stats[fr.q_stat * a.nchunks + c]) : 0.0f;
   const FinalScale s = final_scale(fr, residual, mp, mq);
   unsigned long long tw = 0, tp = 0;
 #pragma unroll
@@ -990,8 +1219,8 @@ __device__ __forceinline__ int cut_index(const Args& a, const FinalRow& fr, bool
   if (sub < 0) return -1;
   float4 zp[kVec], zq[kVec];
   load_final_chunk<VEC>(a, fr, residual, sub, zp, zq);
-  const float mp = a.stats[fr.p_stat * nc + sub].m;
-  const float mq = residual ? a.stats[fr.q_stat * nc + sub].m : 0.0f;
+  const float mp = ld_m(&a.stats[fr.p_stat * nc + sub]);
+  const float mq = residual ? ld_m(&a.stats[fr.q_stat * nc + sub]) : 0.0f;
   const FinalScale sc = final_scale(fr, residual, mp, mq);
   unsigned long long cbase = 0;
   int found = -1;
@@ -1062,7 +1291,7 @@ __device__ __forceinline__ void final_search(const Args& a, int b, const FinalRo
     a.out_tokens[fr.out_index] = token;
     if (a.sample && a.out_probs) {
       const int c = token / kChunk;
-      const float mp = a.stats[fr.p_stat * nc + c].m;
+      const float mp = ld_m(&a.stats[fr.p_stat * nc + c]);
       a.out_probs[fr.out_index] =
           KY_FMUL(ky_exp(KY_FSUB(KY_FMUL(__ldg(a.plog + fr.p_row * a.V + token), a.inv_t), mp)),
                   ky_chunk_scale(mp, fr.Mp, fr.Sp));
@@ -1085,10 +1314,23 @@ __global__ void __launch_bounds__(kThreads) accept_final_kernel(Args a) {
   const int y = (int)(blockIdx.x / (unsigned)per_seq);
   const int b = a.B - 1 - y;
   const int c0 = (int)(blockIdx.x - (unsigned)y * per_seq) * kFinalPerCta;
-  grid_dependency_wait();  // the decide kernel has written final_rows and zeroed cnt_c
+  __shared__ FinalRow sh_fr;
+  if (a.poll) {
+    // this sequence's decision is published (its descriptor, the zeroed count)
+    if (threadIdx.x == 0) {
+      wait_flag(a, a.final_ready + b, call_tag(a));
+      sh_fr = ld_final_row(a.final_rows + b);
+    }
+    __syncthreads();
+  } else {
+    grid_dependency_wait();  // the decide kernel has written final_rows and zeroed cnt_c
+  }
   allow_dependents();      // the stream's next kernel (e.g. the KV commit) may start launching
-  const FinalRow fr = a.final_rows[b];
-  if (fr.skip) return;  // the same for the whole CTA
+  const FinalRow fr = a.poll ? sh_fr : a.final_rows[b];
+  if (fr.skip) {  // the same for the whole CTA
+    if (a.poll) grid_dependency_wait();
+    return;
+  }
   const bool residual = fr.q_row >= 0;
 #pragma unroll 1
   for (int i = 0; i < kFinalPerWarp; ++i) {
@@ -1110,10 +1352,17 @@ __global__ void __launch_bounds__(kThreads) accept_final_kernel(Args a) {
   __syncthreads();
   if (threadIdx.x == 0) last_cta = atomicAdd(&a.cnt_c[b], 1u) == (uint32_t)(per_seq - 1);
   __syncthreads();
-  if (!last_cta || warp != 0) return;
+  if (!last_cta || warp != 0) {
+    if (a.poll) grid_dependency_wait();  // complete only after the decide kernel
+    return;
+  }
   __threadfence();  // every other CTA's sums are visible from here on
   if (!TP) {
     final_search<VEC>(a, b, fr);
+    if (a.poll) {
+      if (lane == 0) chain_seq_done(a);
+      grid_dependency_wait();
+    }
     return;
   }
   unsigned long long tw = 0, tp = 0;
@@ -1223,7 +1472,7 @@ __global__ void __launch_bounds__(kDecideWarps * 32) accept_tp_sum_kernel(Args a
     const int xg = draft_token_of_row(a, b, r);
     const int64_t xl = (int64_t)xg - a.vocab_offset;
     if (xg >= 0 && xg < a.V_global && xl >= 0 && xl < a.V) {
-      v.ex = a.ex[srow];
+      v.ex = ld_ex(a, srow);
       v.mcx = a.stats[srow * a.nchunks + xl / kChunk].m;
     }
     if (lane == 0) a.send2[srow] = v;
@@ -2077,6 +2326,7 @@ void fill_common(Args& a, const Workspace& ws, int64_t V, int B, int R) {
   a.units = (uint32_t)((int64_t)B * R * a.nchunks);
   a.stats = ws.stats;
   a.ex = ws.ex;
+  a.final_ready = ws.final_ready;
   a.final_rows = ws.final_rows;
   a.W = ws.W;
   a.cnt_c = ws.cnt_c;
@@ -2153,6 +2403,11 @@ int kyro_spec_accept(kyro_ctx* ctx, const kyro_accept_params* p, const float* ta
   a.out_num_tokens = out_num_tokens;
   a.out_probs = stoch ? out_probs : nullptr;
   a.status = ctx->d_status;
+  // chained: the decide and final kernels wait for tagged records
+  a.poll = 1;
+  a.gen = ctx->d_pipe_counts;
+  a.done = ctx->d_pipe_counts + 1;
+  a.salt = ctx->pipe_salt;
   return launch(ctx, a, ws, use_vec(target_logits, a.qlog, V));
 }
 

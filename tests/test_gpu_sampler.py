@@ -223,3 +223,46 @@ def test_sampler_reads_strided_sequences(ctx, oracle, k, V, T):
         if T > 0:
             assert np.array_equal(_np(probs), oprobs)
     assert ctx.device_status() == 0
+
+
+def test_accept_graph_replays_match_oracle(ctx, oracle):
+    """kyro_spec_accept captured once in a CUDA graph and replayed on new
+    inputs copied into the captured buffers: every replay must give the
+    oracle's decisions.  (The acceptance kernel tags its records per call
+    from a device-side count, so a replay must not read an earlier replay's
+    records.)"""
+    from kyro_b200.verify import spec_accept
+    from kyro_b200.workloads import accept_inputs
+    B, k, V, T = 24, 5, 128256, 1.0
+    tgt, drf = accept_inputs(B, k, V, ctx.device, seed=90)
+    drafts = torch.zeros(B, k, dtype=torch.int32, device=ctx.device)
+    acc = torch.empty(B, dtype=torch.int32, device=ctx.device)
+    toks = torch.empty(B, k + 1, dtype=torch.int32, device=ctx.device)
+    num = torch.empty(B, dtype=torch.int32, device=ctx.device)
+    ws = torch.empty(64 << 20, dtype=torch.uint8, device=ctx.device)
+    side = torch.cuda.Stream(ctx.device)
+    with torch.cuda.stream(side):
+        spec_accept(ctx, tgt, drf, drafts, temperature=T, seed=3, out=(acc, toks, num, None),
+                    workspace=ws)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side):
+            spec_accept(ctx, tgt, drf, drafts, temperature=T, seed=3,
+                        out=(acc, toks, num, None), workspace=ws)
+    torch.cuda.synchronize()
+    for rep in range(4):
+        t2, d2 = accept_inputs(B, k, V, ctx.device, seed=91 + rep)
+        dr = oracle.sample_tokens(_np(d2), T, seed=rep, nthreads=NTHREADS)[0]
+        tgt.copy_(t2)
+        drf.copy_(d2)
+        drafts.copy_(torch.from_numpy(dr))
+        with torch.cuda.stream(side):
+            g.replay()
+        torch.cuda.synchronize()
+        oacc, otoks, onum, _ = oracle.spec_accept(_np(t2), _np(d2), dr, temperature=T, seed=3,
+                                                  nthreads=NTHREADS)
+        assert np.array_equal(_np(acc), oacc), rep
+        assert np.array_equal(_np(toks), otoks), rep
+        assert np.array_equal(_np(num), onum), rep
+    del g
+    ctx.bind_stream()
+    assert ctx.device_status() == 0
