@@ -658,6 +658,7 @@ int kyro_verify_attention(kyro_ctx* ctx, const kyro_attn_params* p, const void* 
                           const void* k_cache, const void* v_cache, const int64_t* block_table,
                           const int64_t* context_lens, const uint64_t* tree_mask, void* out,
                           void* workspace, size_t workspace_bytes) {
+  KY_NVTX("kyro_verify_attention");
   KY_TRY(kyro::enter(ctx));
   Plan pl;
   // plan with the SM count the workspace size was computed for, so that

@@ -543,6 +543,7 @@ extern "C" {
 int kyro_kv_reserve(kyro_ctx* ctx, const kyro_kv_params* p, int32_t num_new,
                     int64_t* block_table, const int64_t* context_lens, int32_t* free_stack,
                     int32_t* free_top, int32_t* ref_counts, int32_t* out_ok) {
+  KY_NVTX("kyro_kv_reserve");
   KY_TRY(kyro::enter(ctx));
   KY_TRY(check_kv(p, "kyro_kv_reserve"));
   KY_REQUIRE(num_new >= 0, "kyro_kv_reserve: num_new = %d", num_new);
@@ -559,6 +560,7 @@ int kyro_kv_reserve(kyro_ctx* ctx, const kyro_kv_params* p, int32_t num_new,
 int kyro_kv_commit(kyro_ctx* ctx, const kyro_kv_params* p, int32_t num_new,
                    const int32_t* accept_len, int64_t* block_table, int64_t* context_lens,
                    int32_t* free_stack, int32_t* free_top, int32_t* ref_counts) {
+  KY_NVTX("kyro_kv_commit");
   KY_TRY(kyro::enter(ctx));
   KY_TRY(check_kv(p, "kyro_kv_commit"));
   KY_REQUIRE(num_new >= 0, "kyro_kv_commit: num_new = %d", num_new);
@@ -575,6 +577,7 @@ int kyro_kv_write(kyro_ctx* ctx, const kyro_kv_params* p, int32_t num_new, int32
                   int32_t head_dim, const void* k_new, const void* v_new,
                   const int64_t* block_table, const int64_t* context_lens, void* k_cache,
                   void* v_cache) {
+  KY_NVTX("kyro_kv_write");
   KY_TRY(kyro::enter(ctx));
   KY_TRY(check_kv(p, "kyro_kv_write"));
   KY_REQUIRE(num_new >= 0 && num_new <= 65535, "kyro_kv_write: num_new = %d", num_new);
@@ -599,6 +602,7 @@ int kyro_kv_commit_tree(kyro_ctx* ctx, const kyro_kv_params* p, int32_t num_node
                         void* const* k_caches, void* const* v_caches, int32_t num_kv_heads,
                         int32_t head_dim, int64_t* block_table, int64_t* context_lens,
                         int32_t* free_stack, int32_t* free_top, int32_t* ref_counts) {
+  KY_NVTX("kyro_kv_commit_tree");
   KY_TRY(kyro::enter(ctx));
   KY_TRY(check_kv(p, "kyro_kv_commit_tree"));
   KY_REQUIRE(num_nodes >= 1 && num_nodes <= 64, "kyro_kv_commit_tree: num_nodes = %d (1..64)",
@@ -643,6 +647,7 @@ int kyro_rope_kv_write(kyro_ctx* ctx, const kyro_kv_params* p, int32_t num_new,
                        float rope_theta, const int32_t* pos_offsets, const void* q,
                        const void* k_new, const void* v_new, const int64_t* block_table,
                        const int64_t* context_lens, void* q_out, void* k_cache, void* v_cache) {
+  KY_NVTX("kyro_rope_kv_write");
   KY_TRY(kyro::enter(ctx));
   KY_TRY(check_kv(p, "kyro_rope_kv_write"));
   KY_REQUIRE(num_new >= 0 && num_new <= 65535, "kyro_rope_kv_write: num_new = %d", num_new);
@@ -684,6 +689,7 @@ int kyro_kv_reserve_cow(kyro_ctx* ctx, const kyro_kv_params* p, int32_t num_new,
                         int32_t num_kv_heads, int32_t head_dim, int64_t* block_table,
                         const int64_t* context_lens, int32_t* free_stack, int32_t* free_top,
                         int32_t* ref_counts, int32_t* out_ok, int32_t* out_cow) {
+  KY_NVTX("kyro_kv_reserve_cow");
   KY_TRY(kyro::enter(ctx));
   KY_TRY(check_kv(p, "kyro_kv_reserve_cow"));
   KY_REQUIRE(num_new >= 0, "kyro_kv_reserve_cow: num_new = %d", num_new);

@@ -13,6 +13,12 @@
 
 #include "../../include/kyro_spec.h"
 
+// NVTX (header-only v3): each entry point that enqueues work marks its host
+// span with a named range, so a timeline tool shows the verify step's K1 /
+// K2 / K3 calls beside their kernels.  Without a tool attached a range is
+// one predicted branch.
+#include <nvtx3/nvToolsExt.h>
+
 #define KYRO_MAX_TP_WORLD 8
 // counts of the acceptance pipeline kept in each context (sampler.cu)
 #define KYRO_PIPE_COUNTS 128
@@ -106,6 +112,16 @@ int all_reduce_max_i32(kyro_ctx* ctx, const int32_t* send, int32_t* recv, size_t
 }  // namespace xchg
 
 }  // namespace kyro
+
+namespace kyro {
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange&) = delete;
+  NvtxRange& operator=(const NvtxRange&) = delete;
+};
+}  // namespace kyro
+#define KY_NVTX(name) kyro::NvtxRange ky_nvtx_range_(name)
 
 #define KY_REQUIRE(cond, ...)                                       \
   do {                                                              \

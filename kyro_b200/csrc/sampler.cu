@@ -2354,6 +2354,7 @@ int kyro_spec_accept(kyro_ctx* ctx, const kyro_accept_params* p, const float* ta
                      const float* draft_logits, const int32_t* draft_tokens,
                      int32_t* out_accept_len, int32_t* out_tokens, int32_t* out_num_tokens,
                      float* out_probs, void* workspace, size_t workspace_bytes) {
+  KY_NVTX("kyro_spec_accept");
   KY_TRY(kyro::enter(ctx));
   KY_REQUIRE(p, "kyro_spec_accept: params is NULL");
   KY_REQUIRE(p->batch >= 0, "kyro_spec_accept: batch = %d", p->batch);
@@ -2421,6 +2422,7 @@ size_t kyro_sample_workspace_size(const kyro_sample_params* p) {
 int kyro_sample_tokens(kyro_ctx* ctx, const kyro_sample_params* p, const float* logits,
                        int32_t* out_tokens, float* out_probs, void* workspace,
                        size_t workspace_bytes) {
+  KY_NVTX("kyro_sample_tokens");
   KY_TRY(kyro::enter(ctx));
   KY_REQUIRE(p, "kyro_sample_tokens: params is NULL");
   KY_REQUIRE(p->batch >= 0 && p->num_pos >= 0, "kyro_sample_tokens: batch %d num_pos %d",
@@ -2478,6 +2480,7 @@ int kyro_spec_accept_tp(kyro_ctx* ctx, const kyro_accept_params* p, const float*
                         const float* draft_shard, const int32_t* draft_tokens,
                         int32_t* out_accept_len, int32_t* out_tokens, int32_t* out_num_tokens,
                         float* out_probs, void* workspace, size_t workspace_bytes) {
+  KY_NVTX("kyro_spec_accept_tp");
   KY_TRY(kyro::enter(ctx));
   KY_REQUIRE(p, "kyro_spec_accept_tp: params is NULL");
   const int world = ctx->tp_world;
@@ -2577,6 +2580,7 @@ int kyro_spec_accept_tree(kyro_ctx* ctx, const kyro_tree_params* p, const float*
                           const int32_t* parents, int32_t* out_path, int32_t* out_path_len,
                           int32_t* out_tokens, int32_t* out_num_tokens, void* workspace,
                           size_t workspace_bytes) {
+  KY_NVTX("kyro_spec_accept_tree");
   KY_TRY(kyro::enter(ctx));
   KY_REQUIRE(p, "kyro_spec_accept_tree: params is NULL");
   KY_REQUIRE(p->batch >= 0, "kyro_spec_accept_tree: batch = %d", p->batch);
@@ -2767,6 +2771,7 @@ extern "C" int kyro_spec_accept_static(kyro_ctx* ctx, const kyro_accept_params* 
                                        const int32_t* draft_tokens, int32_t* out_accept_len,
                                        int32_t* out_tokens, int32_t* out_num_tokens,
                                        float* out_probs) {
+  KY_NVTX("kyro_spec_accept_static");
   KY_TRY(kyro::enter(ctx));
   KY_REQUIRE(p, "kyro_spec_accept_static: params is NULL");
   const size_t need = kyro_spec_accept_workspace_size(p);
