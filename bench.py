@@ -3,11 +3,13 @@
 One step = one batched verify pass over 64 sequences per GPU, the workload
 BASELINE.json's metric is quoted on (config 1), run by
 kyro_b200.step.VerifyStep:
-  kv_reserve (k+1 slots) -> rope_kv_write (RoPE of the new q/k rows at
-  context_len + j, paged store of the new K/V) -> verify attention
-  (Llama-3-8B layer: Hq 32, Hkv 8, D 128, bf16 paged KV, block 16, context
-  ~ U[512, 4096]) -> acceptance sampling (k = 5, V = 128256, fp32, T = 1.0)
-  -> kv_commit.
+  rope_kv_write (RoPE of the new q/k rows at context_len + j, paged store
+  of the new K/V) -> verify attention (Llama-3-8B layer: Hq 32, Hkv 8,
+  D 128, bf16 paged KV, block 16, context ~ U[512, 4096]) -> acceptance
+  sampling (k = 5, V = 128256, fp32, T = 1.0) -> kv_commit of the accepted
+  slots and kv_reserve of the next step's k+1 slots (the decode-loop form:
+  kyro_spec_accept_commit runs the commit beside the acceptance's final
+  pass and the reserve in the same launch as the commit).
 Every timed step first restores the KV bookkeeping state (one device copy),
 so every step sees the same context lengths; the step is captured once as
 a CUDA graph and replayed, so every replay also reuses the Philox step
@@ -351,8 +353,14 @@ def run_ours(args):
                         dtype=torch.bfloat16)
     v_new = torch.randn(cfg.batch, nq, cfg.num_kv_heads, cfg.head_dim, generator=g, device=dev,
                         dtype=torch.bfloat16)
-    # every step starts from the same KV state, so each step sees the same
-    # context lengths; the reset is one device-to-device copy (~0.5 MB)
+    # The decode-loop form of the step: the commit also reserves the next
+    # step's k + 1 slots (kyro_spec_accept_commit), so the state every step
+    # starts from has its slots reserved.  Every step starts from that same
+    # state, so each step sees the same context lengths; the reset is one
+    # device-to-device copy (~0.5 MB).
+    from kyro_b200.verify import kv_reserve
+    kv_reserve(ctx, nq, st.block_table, st.context_lens, st.free_stack, st.free_top,
+               st.ref_counts, cfg.block_size)
     kvsnap = KvStateSnapshot(st)
     kv = kv_of(st)
     vstep = VerifyStep(ctx, cfg.batch, cfg.k, cfg.num_heads, kv, cfg.vocab, cfg.block_size,
@@ -362,7 +370,8 @@ def run_ours(args):
 
     def step(i, events=None):
         kvsnap.restore()
-        return vstep(kv, st.q, k_new, v_new, tgt, drf, drafts, step=i, events=events)
+        return vstep(kv, st.q, k_new, v_new, tgt, drf, drafts, step=i, events=events,
+                     reserve=False, reserve_next=nq)
 
     # the step runs on a side stream as a CUDA graph (captured once after the
     # warm-up steps); the library context is bound to that stream
@@ -454,7 +463,7 @@ def run_ours(args):
         "timing": "CUDA graph replays of the step" if not args.no_graph else "stream launches",
         "mean_accepted_fraction": frac_acc,
         "per_token_acceptance": per_token,
-        "gpu_launches": vstep.launches() * args.steps,
+        "gpu_launches": vstep.launches(reserve=False) * args.steps,
         "clocks": clk,
     }
     if world > 1:
@@ -503,7 +512,8 @@ def run_e2e(args, ctx, cfg, st, kv, vstep, tgt, drf, drafts, k_new, v_new, world
         for n in h:
             d[n].copy_(h[n], non_blocking=True)
         _, _, acc, toks, num = vstep(kv, d["q"], d["k_new"], d["v_new"], d["tgt"], d["drf"],
-                                     d["drafts"], step=1000 + i)
+                                     d["drafts"], step=1000 + i, reserve=False,
+                                     reserve_next=cfg.num_query)
         out_h["acc"].copy_(acc, non_blocking=True)
         out_h["toks"].copy_(toks, non_blocking=True)
         out_h["num"].copy_(num, non_blocking=True)

@@ -289,6 +289,25 @@ int kyro_kv_commit(kyro_ctx* ctx, const kyro_kv_params* p, int32_t num_new,
                    const int32_t* accept_len, int64_t* block_table, int64_t* context_lens,
                    int32_t* free_stack, int32_t* free_top, int32_t* ref_counts);
 
+/* kyro_spec_accept_commit: kyro_spec_accept, then kyro_kv_commit of the
+ * accepted slots and, when num_new_next > 0, kyro_kv_reserve of the next
+ * step's num_new_next slots, in one call.  The end of
+ * SpeculativeDecoder::step (src/speculative.rs:342-353) in a decode loop,
+ * where every step reserves right after it commits.  The commit needs only
+ * the accept lengths, so it runs beside the acceptance's final pass
+ * instead of after it, and the commit and the reserve are one launch.
+ * Results equal kyro_spec_accept followed by kyro_kv_commit (num_new) and
+ * kyro_kv_reserve (num_new_next); kv->batch must equal p->batch, and
+ * out_ok (may be NULL) gets the reserve's per-sequence result. */
+int kyro_spec_accept_commit(kyro_ctx* ctx, const kyro_accept_params* p,
+                            const float* target_logits, const float* draft_logits,
+                            const int32_t* draft_tokens, int32_t* out_accept_len,
+                            int32_t* out_tokens, int32_t* out_num_tokens, float* out_probs,
+                            void* workspace, size_t workspace_bytes, const kyro_kv_params* kv,
+                            int32_t num_new, int32_t num_new_next, int64_t* block_table,
+                            int64_t* context_lens, int32_t* free_stack, int32_t* free_top,
+                            int32_t* ref_counts, int32_t* out_ok);
+
 /* kyro_kv_commit_tree: tree verification wrote node n's K/V at position
  * context_len + n.  For the accepted root-to-leaf path path[b][0..len-1]
  * (path[b][0] == 0), move node path[b][i]'s K/V rows to position

@@ -40,6 +40,7 @@ EXPORTS = (
     "kyro_ctx_create", "kyro_ctx_destroy", "kyro_ctx_set_stream", "kyro_ctx_device_status",
     "kyro_last_error", "kyro_status_string", "kyro_version", "kyro_kernel_names",
     "kyro_spec_accept_workspace_size", "kyro_spec_accept", "kyro_spec_accept_static",
+    "kyro_spec_accept_commit",
     "kyro_sample_workspace_size",
     "kyro_sample_tokens", "kyro_verify_attention_workspace_size", "kyro_verify_attention",
     "kyro_kv_reserve", "kyro_kv_reserve_cow", "kyro_kv_commit", "kyro_kv_commit_tree", "kyro_kv_write",
@@ -121,6 +122,8 @@ def load():
         "kyro_spec_accept_workspace_size": (sz, [P(AcceptParams)]),
         "kyro_spec_accept": (C.c_int, [vp, P(AcceptParams), vp, vp, vp, vp, vp, vp, vp, vp, sz]),
         "kyro_spec_accept_static": (C.c_int, [vp, P(AcceptParams), vp, vp, vp, vp, vp, vp, vp]),
+        "kyro_spec_accept_commit": (C.c_int, [vp, P(AcceptParams), vp, vp, vp, vp, vp, vp, vp, vp,
+                                              sz, P(KVParams), i32, i32, vp, vp, vp, vp, vp, vp]),
         "kyro_sample_workspace_size": (sz, [P(SampleParams)]),
         "kyro_sample_tokens": (C.c_int, [vp, P(SampleParams), vp, vp, vp, vp, sz]),
         "kyro_verify_attention_workspace_size": (sz, [P(AttnParams)]),

@@ -8,15 +8,17 @@
 // never rolls back.  The verify step needs both: reserve k+1 slots before
 // the target forward, keep the accepted ones after, release the rest.
 //
-// Both operations run as one CTA that walks the batch in tiles of
-// kTile sequences.  Within a tile, per-sequence block counts go through a
-// block-wide exclusive scan, which gives every sequence the same stack
+// Both operations run as one CTA that walks the batch in tiles of one
+// sequence per thread (up to kTile).  Within a tile, per-sequence block
+// counts go through a block-wide exclusive scan, which gives every sequence
+// the same stack
 // positions a sequential loop in batch order would: sequence b pops
 // free_stack[top-1-off_b-i] for its i-th block and pushes released block i
 // at free_stack[top+off_b+i].  When the fast path's preconditions fail
 // (the pool runs out inside the tile, or a released block is shared), the
 // tile is done by one thread in batch order, which is the reference's
 // semantics exactly.
+#include <algorithm>
 #include <cmath>
 
 #include "kyro_internal.cuh"
@@ -29,9 +31,10 @@ __device__ __forceinline__ int64_t blocks_for(int64_t tokens, int bs) {
   return (tokens + bs - 1) / bs;
 }
 
-// Block-wide exclusive scan of an int over kTile threads (1024).
+// Block-wide exclusive scan of an int over the block's threads (a multiple
+// of 32, at most kTile).
 __device__ int block_exclusive_scan(int v, int* sh, int* total) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   int inc = v;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -42,7 +45,7 @@ __device__ int block_exclusive_scan(int v, int* sh, int* total) {
   if (lane == 31) sh[warp] = inc;
   __syncthreads();
   if (warp == 0) {
-    int w = sh[lane];
+    int w = lane < nwarps ? sh[lane] : 0;
     int wi = w;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -65,16 +68,16 @@ __device__ int block_exclusive_scan(int v, int* sh, int* total) {
 // tile with such a sequence takes the one-thread path, so that sequences
 // sharing one block see each other's decrements in batch order.
 template <bool COW>
-__global__ void __launch_bounds__(kTile)
-kv_reserve_kernel(int B, int bs, int max_blocks, int num_blocks, int num_new,
-                  int64_t* __restrict__ block_table, const int64_t* __restrict__ context_lens,
-                  const int32_t* __restrict__ free_stack, int32_t* __restrict__ free_top,
-                  int32_t* __restrict__ ref_counts, int32_t* __restrict__ out_ok,
-                  int32_t* __restrict__ cow, uint32_t* status) {
+__device__ __forceinline__ void reserve_body(int B, int bs, int max_blocks, int num_blocks,
+                                             int num_new, int64_t* __restrict__ block_table,
+                                             const int64_t* __restrict__ context_lens,
+                                             const int32_t* __restrict__ free_stack,
+                                             int32_t* __restrict__ free_top,
+                                             int32_t* __restrict__ ref_counts,
+                                             int32_t* __restrict__ out_ok,
+                                             int32_t* __restrict__ cow, uint32_t* status) {
   __shared__ int sh[72];
   __shared__ int sh_top, sh_fast;
-  kyro::dev::pdl_wait();
-  kyro::dev::pdl_trigger();
   if (threadIdx.x == 0) {
     int t = *free_top;
     if (t < 0 || t > num_blocks) {
@@ -84,7 +87,7 @@ kv_reserve_kernel(int B, int bs, int max_blocks, int num_blocks, int num_new,
     sh_top = t;
   }
   __syncthreads();
-  for (int base = 0; base < B; base += kTile) {
+  for (int base = 0; base < B; base += (int)blockDim.x) {
     const int b = base + threadIdx.x;
     int64_t have = 0, need = 0;
     bool fits_table = true, shared_last = false;
@@ -134,7 +137,7 @@ kv_reserve_kernel(int B, int bs, int max_blocks, int num_blocks, int num_new,
       __syncthreads();
       if (threadIdx.x == 0) {
         int t = top;
-        const int end = min(B, base + kTile);
+        const int end = min(B, base + (int)blockDim.x);
         for (int bb = base; bb < end; ++bb) {
           const int64_t len = context_lens[bb];
           const int64_t h = blocks_for(len, bs);
@@ -184,20 +187,34 @@ kv_reserve_kernel(int B, int bs, int max_blocks, int num_blocks, int num_new,
     }
   }
   if (threadIdx.x == 0) *free_top = sh_top;
+  __syncthreads();
+}
+
+template <bool COW>
+__global__ void __launch_bounds__(kTile)
+kv_reserve_kernel(int B, int bs, int max_blocks, int num_blocks, int num_new,
+                  int64_t* __restrict__ block_table, const int64_t* __restrict__ context_lens,
+                  const int32_t* __restrict__ free_stack, int32_t* __restrict__ free_top,
+                  int32_t* __restrict__ ref_counts, int32_t* __restrict__ out_ok,
+                  int32_t* __restrict__ cow, uint32_t* status) {
+  kyro::dev::pdl_wait();
+  kyro::dev::pdl_trigger();
+  reserve_body<COW>(B, bs, max_blocks, num_blocks, num_new, block_table, context_lens, free_stack,
+                    free_top, ref_counts, out_ok, cow, status);
 }
 
 // accept_len[b] (accepted drafts) or path_len[b] (accepted path length
 // including the root) gives the number of reserved slots to keep.
-__global__ void __launch_bounds__(kTile)
-kv_commit_kernel(int B, int bs, int max_blocks, int num_blocks, int num_new,
-                 const int32_t* __restrict__ accept_len, const int32_t* __restrict__ path_len,
-                 int64_t* __restrict__ block_table, int64_t* __restrict__ context_lens,
-                 int32_t* __restrict__ free_stack, int32_t* __restrict__ free_top,
-                 int32_t* __restrict__ ref_counts, uint32_t* status) {
+__device__ __forceinline__ void commit_body(int B, int bs, int max_blocks, int num_blocks,
+                                            int num_new, const int32_t* __restrict__ accept_len,
+                                            const int32_t* __restrict__ path_len,
+                                            int64_t* __restrict__ block_table,
+                                            int64_t* __restrict__ context_lens,
+                                            int32_t* __restrict__ free_stack,
+                                            int32_t* __restrict__ free_top,
+                                            int32_t* __restrict__ ref_counts, uint32_t* status) {
   __shared__ int sh[72];
   __shared__ int sh_top, sh_fast;
-  kyro::dev::pdl_wait();
-  kyro::dev::pdl_trigger();
   if (threadIdx.x == 0) {
     int t = *free_top;
     if (t < 0 || t > num_blocks) {
@@ -207,7 +224,7 @@ kv_commit_kernel(int B, int bs, int max_blocks, int num_blocks, int num_new,
     sh_top = t;
   }
   __syncthreads();
-  for (int base = 0; base < B; base += kTile) {
+  for (int base = 0; base < B; base += (int)blockDim.x) {
     const int b = base + threadIdx.x;
     int64_t len = 0, keep = 0, had = 0, new_len = 0;
     bool active = false;
@@ -261,7 +278,7 @@ kv_commit_kernel(int B, int bs, int max_blocks, int num_blocks, int num_new,
       __syncthreads();
       if (threadIdx.x == 0) {
         int t = top;
-        const int end = min(B, base + kTile);
+        const int end = min(B, base + (int)blockDim.x);
         for (int bb = base; bb < end; ++bb) {
           const int a = accept_len ? accept_len[bb] : (path_len ? path_len[bb] - 1 : -1);
           const int64_t l0 = context_lens[bb];
@@ -290,6 +307,42 @@ kv_commit_kernel(int B, int bs, int max_blocks, int num_blocks, int num_new,
     }
   }
   if (threadIdx.x == 0) *free_top = sh_top;
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(kTile)
+kv_commit_kernel(int B, int bs, int max_blocks, int num_blocks, int num_new,
+                 const int32_t* __restrict__ accept_len, const int32_t* __restrict__ path_len,
+                 int64_t* __restrict__ block_table, int64_t* __restrict__ context_lens,
+                 int32_t* __restrict__ free_stack, int32_t* __restrict__ free_top,
+                 int32_t* __restrict__ ref_counts, uint32_t* status) {
+  kyro::dev::pdl_wait();
+  kyro::dev::pdl_trigger();
+  commit_body(B, bs, max_blocks, num_blocks, num_new, accept_len, path_len, block_table,
+              context_lens, free_stack, free_top, ref_counts, status);
+}
+
+// The commit of this step's slots, then the reserve of num_new_next slots
+// for the next step, in one launch: a decoding loop always reserves right
+// after it commits.  The two phases run in the same CTA, in the same order
+// as kv_commit_kernel followed by kv_reserve_kernel.  Launched between the
+// acceptance's decide and final kernels (kyro_spec_accept_commit): it lets
+// the final kernel launch before it waits for the accept lengths, since the
+// final kernel waits for its own records and touches none of the KV state.
+__global__ void __launch_bounds__(kTile)
+kv_commit_reserve_kernel(int B, int bs, int max_blocks, int num_blocks, int num_new,
+                         int num_new_next, const int32_t* __restrict__ accept_len,
+                         int64_t* __restrict__ block_table, int64_t* __restrict__ context_lens,
+                         int32_t* __restrict__ free_stack, int32_t* __restrict__ free_top,
+                         int32_t* __restrict__ ref_counts, int32_t* __restrict__ out_ok,
+                         uint32_t* status) {
+  kyro::dev::pdl_trigger();
+  kyro::dev::pdl_wait();
+  commit_body(B, bs, max_blocks, num_blocks, num_new, accept_len, nullptr, block_table,
+              context_lens, free_stack, free_top, ref_counts, status);
+  if (num_new_next > 0)
+    reserve_body<false>(B, bs, max_blocks, num_blocks, num_new_next, block_table, context_lens,
+                        free_stack, free_top, ref_counts, out_ok, nullptr, status);
 }
 
 constexpr int kMaxLayerPtrs = 32;
@@ -537,6 +590,39 @@ int check_kv(const kyro_kv_params* p, const char* fn) {
 }
 
 }  // namespace
+
+namespace kyro {
+namespace kv {
+
+int check_commit_args(const kyro_kv_params* p, int32_t num_new, int32_t num_new_next,
+                      const int32_t* accept_len, const int64_t* block_table,
+                      const int64_t* context_lens, const int32_t* free_stack,
+                      const int32_t* free_top, const int32_t* ref_counts, const char* what) {
+  KY_TRY(check_kv(p, what));
+  KY_REQUIRE(num_new >= 0 && num_new_next >= 0, "%s: num_new = %d, num_new_next = %d", what,
+             num_new, num_new_next);
+  KY_REQUIRE(accept_len && block_table && context_lens && free_stack && free_top && ref_counts,
+             "%s: a required KV pointer is NULL", what);
+  return KYRO_OK;
+}
+
+int launch_commit_reserve(kyro_ctx* ctx, const kyro_kv_params* p, int32_t num_new,
+                          int32_t num_new_next, const int32_t* accept_len, int64_t* block_table,
+                          int64_t* context_lens, int32_t* free_stack, int32_t* free_top,
+                          int32_t* ref_counts, int32_t* out_ok) {
+  if (p->batch == 0) return KYRO_OK;
+  // a CTA no larger than the batch: it launches between the acceptance's
+  // decide and final kernels and must find room on an SM beside them
+  const int threads = std::min(kTile, std::max(32, (p->batch + 31) / 32 * 32));
+  return kyro::launch_pdl(kv_commit_reserve_kernel, dim3(1), dim3(threads), 0, ctx->stream,
+                          "kv_commit_reserve_kernel", p->batch, p->block_size,
+                          p->max_blocks_per_seq, p->num_blocks, (int)num_new, (int)num_new_next,
+                          accept_len, block_table, context_lens, free_stack, free_top,
+                          ref_counts, out_ok, ctx->d_status);
+}
+
+}  // namespace kv
+}  // namespace kyro
 
 extern "C" {
 

@@ -78,6 +78,20 @@ int tree_attention_launch(kyro_ctx* ctx, const kyro_attn_params* p, const void* 
                           const void* k_cache, const void* v_cache, const int64_t* block_table,
                           const int64_t* context_lens, const uint64_t* tree_mask, void* out);
 
+// The KV commit of an acceptance call's accepted slots, then the reserve of
+// the next step's slots, as one launch on the context's stream
+// (kv_commit.cu); check_commit_args validates the KV arguments first.
+namespace kv {
+int check_commit_args(const kyro_kv_params* p, int32_t num_new, int32_t num_new_next,
+                      const int32_t* accept_len, const int64_t* block_table,
+                      const int64_t* context_lens, const int32_t* free_stack,
+                      const int32_t* free_top, const int32_t* ref_counts, const char* what);
+int launch_commit_reserve(kyro_ctx* ctx, const kyro_kv_params* p, int32_t num_new,
+                          int32_t num_new_next, const int32_t* accept_len, int64_t* block_table,
+                          int64_t* context_lens, int32_t* free_stack, int32_t* free_top,
+                          int32_t* ref_counts, int32_t* out_ok);
+}  // namespace kv
+
 // NCCL, loaded at run time (nccl_comm.cu).  Collectives enqueue on the
 // context's stream over its tensor-parallel communicator.
 namespace nccl {

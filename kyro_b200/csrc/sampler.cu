@@ -1183,17 +1183,19 @@ __device__ __forceinline__ void chunk_weight_sums2(const Args& a, const FinalRow
 template <bool VEC>
 __device__ __forceinline__ int cut_index(const Args& a, const FinalRow& fr, bool residual,
                                          const unsigned long long* W, int wstride,
-                                         unsigned long long T) {
+                                         unsigned long long T,
+                                         const unsigned long long* pre = nullptr) {
   const int lane = threadIdx.x & 31;
   const int nc = a.nchunks;
   int sub = -1;
   unsigned long long base = 0;
-  // up to 256 chunk sums load in one round trip, then the scan runs on them
+  // up to 256 chunk sums load in one round trip (or come preloaded: chunk
+  // j*32 + lane in pre[j]), then the scan runs on them
   unsigned long long wr[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     const int c = j * 32 + lane;
-    wr[j] = (c < nc && nc <= 256) ? __ldcg(&W[(int64_t)c * wstride]) : 0ull;
+    wr[j] = (c < nc && nc <= 256) ? (pre ? pre[j] : __ldcg(&W[(int64_t)c * wstride])) : 0ull;
   }
   for (int s0 = 0; s0 < nc && sub < 0; s0 += 32) {
     unsigned long long ws;
@@ -1258,8 +1260,8 @@ __device__ __forceinline__ void final_search(const Args& a, int b, const FinalRo
   unsigned long long* W = a.W + (int64_t)b * nc;
   bool residual = fr.q_row >= 0;
   unsigned long long tot = 0;
+  unsigned long long ww[8];  // the first 256 chunk sums, kept for the search
   for (int g = 0; g < nc; g += 256) {
-    unsigned long long ww[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int c = g + j * 32 + lane;
@@ -1284,7 +1286,11 @@ __device__ __forceinline__ void final_search(const Args& a, int b, const FinalRo
   }
   int token = (int)a.V - 1;
   if (tot != 0) {
-    const int found = cut_index<VEC>(a, fr, residual, W, 1, ky_cdf_threshold(fr.odd, tot));
+    // the sums in ww are the ones just added up, unless the residual had no
+    // mass and W was refilled with the p weights
+    const bool keep = nc <= 256 && (fr.q_row < 0 || residual);
+    const int found = cut_index<VEC>(a, fr, residual, W, 1, ky_cdf_threshold(fr.odd, tot),
+                                     keep ? ww : nullptr);
     if (found >= 0) token = found;
   }
   if (lane == 0) {
@@ -2255,28 +2261,48 @@ bool launch_tree_cluster(int B, const Args& a, cudaStream_t stream, int* rc) {
   return true;
 }
 
+// The KV commit (and next reserve) that kyro_spec_accept_commit runs inside
+// the acceptance, right after the decide kernel.
+struct CommitSpec {
+  const kyro_kv_params* kv;
+  int32_t num_new, num_new_next;
+  int64_t* block_table;
+  int64_t* context_lens;
+  int32_t *free_stack, *free_top, *ref_counts, *out_ok;
+};
+
 template <bool VEC, bool STOCH>
-int launch_t(kyro_ctx* ctx, const Args& a) {
+int launch_t(kyro_ctx* ctx, const Args& a, const CommitSpec* commit) {
   const long long need = ((long long)a.units + kWarps - 1) / kWarps;
   const int resident = resident_ctas<VEC, STOCH>(ctx->num_sms);
   const int grid = (int)(need < resident ? need : resident);
+  // launched plainly: a persistent grid launched early would take SM slots
+  // in a long predecessor's last wave (measured 5 us slower behind attention)
   accept_stats_kernel<VEC, STOCH><<<grid, kThreads, 0, ctx->stream>>>(a);
   KY_TRY(kyro::check_launch("accept_stats_kernel"));
   const int dwarps = min(a.R + (a.sample ? 0 : 1), kDecideWarps);
   KY_TRY(launch_dependent(accept_decide_kernel, (unsigned)a.B, (unsigned)dwarps * 32, ctx->stream,
                           a, "accept_decide_kernel"));
+  // the commit needs only the accept lengths: it waits for the decide kernel
+  // and runs beside the final pass (which waits for its flags, not for it)
+  if (commit)
+    KY_TRY(kyro::kv::launch_commit_reserve(ctx, commit->kv, commit->num_new, commit->num_new_next,
+                                           a.out_accept_len, commit->block_table,
+                                           commit->context_lens, commit->free_stack,
+                                           commit->free_top, commit->ref_counts, commit->out_ok));
   if (!STOCH) return KYRO_OK;  // greedy: the decide step wrote every token
   const unsigned nfinal = (unsigned)a.B * (unsigned)((a.nchunks + kFinalPerCta - 1) / kFinalPerCta);
   return launch_dependent(accept_final_kernel<VEC, false>, nfinal, kThreads, ctx->stream, a,
                           "accept_final_kernel");
 }
 
-int launch(kyro_ctx* ctx, Args& a, const Workspace& ws, bool vec) {
+int launch(kyro_ctx* ctx, Args& a, const Workspace& ws, bool vec,
+           const CommitSpec* commit = nullptr) {
   (void)ws;
-  if (vec && a.stoch) return launch_t<true, true>(ctx, a);
-  if (vec) return launch_t<true, false>(ctx, a);
-  if (a.stoch) return launch_t<false, true>(ctx, a);
-  return launch_t<false, false>(ctx, a);
+  if (vec && a.stoch) return launch_t<true, true>(ctx, a, commit);
+  if (vec) return launch_t<true, false>(ctx, a, commit);
+  if (a.stoch) return launch_t<false, true>(ctx, a, commit);
+  return launch_t<false, false>(ctx, a, commit);
 }
 
 // The tensor-parallel sequence (kernels and collectives on the context's
@@ -2350,11 +2376,14 @@ size_t kyro_spec_accept_workspace_size(const kyro_accept_params* p) {
   return carve(nullptr, p->batch, R, nchunks).bytes;
 }
 
-int kyro_spec_accept(kyro_ctx* ctx, const kyro_accept_params* p, const float* target_logits,
-                     const float* draft_logits, const int32_t* draft_tokens,
-                     int32_t* out_accept_len, int32_t* out_tokens, int32_t* out_num_tokens,
-                     float* out_probs, void* workspace, size_t workspace_bytes) {
-  KY_NVTX("kyro_spec_accept");
+}  // extern "C"
+
+namespace {
+
+int accept_impl(kyro_ctx* ctx, const kyro_accept_params* p, const float* target_logits,
+                const float* draft_logits, const int32_t* draft_tokens, int32_t* out_accept_len,
+                int32_t* out_tokens, int32_t* out_num_tokens, float* out_probs, void* workspace,
+                size_t workspace_bytes, const CommitSpec* commit) {
   KY_TRY(kyro::enter(ctx));
   KY_REQUIRE(p, "kyro_spec_accept: params is NULL");
   KY_REQUIRE(p->batch >= 0, "kyro_spec_accept: batch = %d", p->batch);
@@ -2409,7 +2438,42 @@ int kyro_spec_accept(kyro_ctx* ctx, const kyro_accept_params* p, const float* ta
   a.gen = ctx->d_pipe_counts;
   a.done = ctx->d_pipe_counts + 1;
   a.salt = ctx->pipe_salt;
-  return launch(ctx, a, ws, use_vec(target_logits, a.qlog, V));
+  return launch(ctx, a, ws, use_vec(target_logits, a.qlog, V), commit);
+}
+
+}  // namespace
+
+extern "C" {
+
+int kyro_spec_accept(kyro_ctx* ctx, const kyro_accept_params* p, const float* target_logits,
+                     const float* draft_logits, const int32_t* draft_tokens,
+                     int32_t* out_accept_len, int32_t* out_tokens, int32_t* out_num_tokens,
+                     float* out_probs, void* workspace, size_t workspace_bytes) {
+  KY_NVTX("kyro_spec_accept");
+  return accept_impl(ctx, p, target_logits, draft_logits, draft_tokens, out_accept_len,
+                     out_tokens, out_num_tokens, out_probs, workspace, workspace_bytes, nullptr);
+}
+
+int kyro_spec_accept_commit(kyro_ctx* ctx, const kyro_accept_params* p,
+                            const float* target_logits, const float* draft_logits,
+                            const int32_t* draft_tokens, int32_t* out_accept_len,
+                            int32_t* out_tokens, int32_t* out_num_tokens, float* out_probs,
+                            void* workspace, size_t workspace_bytes, const kyro_kv_params* kv,
+                            int32_t num_new, int32_t num_new_next, int64_t* block_table,
+                            int64_t* context_lens, int32_t* free_stack, int32_t* free_top,
+                            int32_t* ref_counts, int32_t* out_ok) {
+  KY_NVTX("kyro_spec_accept_commit");
+  KY_TRY(kyro::enter(ctx));
+  KY_REQUIRE(p && kv, "kyro_spec_accept_commit: params is NULL");
+  KY_REQUIRE(kv->batch == p->batch, "kyro_spec_accept_commit: kv batch %d != accept batch %d",
+             kv->batch, p->batch);
+  KY_TRY(kyro::kv::check_commit_args(kv, num_new, num_new_next, out_accept_len, block_table,
+                                     context_lens, free_stack, free_top, ref_counts,
+                                     "kyro_spec_accept_commit"));
+  const CommitSpec commit{kv, num_new, num_new_next, block_table, context_lens,
+                          free_stack, free_top, ref_counts, out_ok};
+  return accept_impl(ctx, p, target_logits, draft_logits, draft_tokens, out_accept_len,
+                     out_tokens, out_num_tokens, out_probs, workspace, workspace_bytes, &commit);
 }
 
 size_t kyro_sample_workspace_size(const kyro_sample_params* p) {

@@ -18,7 +18,13 @@ lm_head:
   verify_attention  the k + 1 query rows against the paged cache
   spec_accept    accept lengths and emitted tokens from the target / draft
                  logits (stochastic, greedy, or the reference's greedy rule)
-  kv_commit      keep accept_len + 1 slots, release the rest
+  kv_commit      keep accept_len + 1 slots, release the rest (one call with
+                 the acceptance, kyro_spec_accept_commit: the commit runs
+                 beside the acceptance's final pass)
+
+In a decode loop the next step's reserve joins the commit (reserve_next):
+call the first step with reserve=True, the later ones with reserve=False,
+and every step with reserve_next=k+1.
 
 The caller owns the KV state and the inputs; the step owns its outputs and
 workspaces, allocated once, so a step can be captured in a CUDA graph and
@@ -33,8 +39,8 @@ from typing import Optional
 import torch
 
 from . import _lib
-from .verify import (ACCEPT_STOCHASTIC, Context, attn_params, kv_commit, kv_reserve, kv_write,
-                     rope_kv_write, spec_accept, verify_attention)
+from .verify import (ACCEPT_STOCHASTIC, Context, attn_params, kv_reserve, kv_write,
+                     rope_kv_write, spec_accept_commit, verify_attention)
 
 
 @dataclass
@@ -83,11 +89,15 @@ class VerifyStep:
 
     def __call__(self, kv: KVState, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
                  target_logits: torch.Tensor, draft_logits: Optional[torch.Tensor],
-                 draft_tokens: torch.Tensor, step: int, events: Optional[dict] = None):
+                 draft_tokens: torch.Tensor, step: int, events: Optional[dict] = None,
+                 reserve: bool = True, reserve_next: int = 0):
         """Run the step on the current stream.  q bf16 [B, k+1, Hq, D]; k_new /
         v_new bf16 [B, k+1, Hkv, D]; logits fp32 [B, k+1, V] / [B, k, V];
         draft_tokens int32 [B, k].  Returns (attention out, ok, accept_len,
-        tokens, num_tokens), all owned by the step.  `events`, if given, maps
+        tokens, num_tokens), all owned by the step.  reserve: reserve this
+        step's k + 1 slots first (False when the previous step's commit
+        reserved them); reserve_next: slots the commit reserves for the next
+        step (ok then reports that reserve).  `events`, if given, maps
         "attention" and "accept" to lists that get a (start, end) pair of CUDA
         events around those launches (events between launches break their
         programmatic chaining, so timed steps should pass None)."""
@@ -98,8 +108,9 @@ class VerifyStep:
             e.record()
             return e
 
-        kv_reserve(ctx, nq, kv.block_table, kv.context_lens, kv.free_stack, kv.free_top,
-                   kv.ref_counts, bs, out_ok=self.ok)
+        if reserve:
+            kv_reserve(ctx, nq, kv.block_table, kv.context_lens, kv.free_stack, kv.free_top,
+                       kv.ref_counts, bs, out_ok=self.ok)
         if self.rope_theta is not None:
             rope_kv_write(ctx, q, k_new, v_new, kv.block_table, kv.context_lens, kv.k_cache,
                           kv.v_cache, bs, theta=self.rope_theta, q_out=self.q_rot)
@@ -112,20 +123,21 @@ class VerifyStep:
         verify_attention(ctx, qq, kv.k_cache, kv.v_cache, kv.block_table, kv.context_lens,
                          out=self.attn_out, workspace=self.ws_attn)
         e1 = mark() if events is not None else None
-        spec_accept(ctx, target_logits, draft_logits, draft_tokens, mode=self.mode,
-                    temperature=self.temperature, seed=self.seed, step=step,
-                    seq_offset=self.seq_offset, out=(self.acc, self.toks, self.num, None),
-                    workspace=self.ws_acc)
+        spec_accept_commit(ctx, target_logits, draft_logits, draft_tokens, kv.block_table,
+                           kv.context_lens, kv.free_stack, kv.free_top, kv.ref_counts, bs,
+                           num_new=nq, num_new_next=reserve_next, mode=self.mode,
+                           temperature=self.temperature, seed=self.seed, step=step,
+                           seq_offset=self.seq_offset, out=(self.acc, self.toks, self.num, None),
+                           workspace=self.ws_acc, out_ok=self.ok if reserve_next else None)
         if events is not None:
             e2 = mark()
             events.setdefault("attention", []).append((e0, e1))
             events.setdefault("accept", []).append((e1, e2))
-        kv_commit(ctx, nq, self.acc, kv.block_table, kv.context_lens, kv.free_stack, kv.free_top,
-                  kv.ref_counts, bs)
         return self.attn_out, self.ok, self.acc, self.toks, self.num
 
-    # launches per call: reserve, rope/kv write, attention, the acceptance's
-    # stats, decide and final kernels (greedy modes: no final), commit
-    def launches(self) -> int:
+    def launches(self, reserve: bool = True) -> int:
+        """Kernels one call launches: reserve (if asked), rope/kv write,
+        attention, the acceptance's stats and decide kernels, the commit, and
+        the final kernel (stochastic mode only)."""
         from .verify import ACCEPT_STOCHASTIC as S
-        return 7 if (self.mode == S and self.temperature > 0) else 6
+        return int(reserve) + 5 + int(self.mode == S and self.temperature > 0)

@@ -17,7 +17,7 @@ from ._lib import (ACCEPT_GREEDY, ACCEPT_GREEDY_REF, ACCEPT_STOCHASTIC, AcceptPa
                    KVParams, SampleParams, check)
 
 __all__ = [
-    "Context", "spec_accept", "sample_tokens", "verify_attention", "kv_reserve", "kv_commit",
+    "Context", "spec_accept", "spec_accept_commit", "sample_tokens", "verify_attention", "kv_reserve", "kv_commit",
     "kv_commit_tree", "kv_write", "philox_uniforms", "ACCEPT_STOCHASTIC", "ACCEPT_GREEDY", "ACCEPT_GREEDY_REF",
 ]
 
@@ -151,6 +151,52 @@ def spec_accept(ctx: Context, target_logits: torch.Tensor, draft_logits: Optiona
     check(L.kyro_spec_accept(ctx.handle, C.byref(p), _ptr(target_logits), _ptr(draft_logits),
                              _ptr(draft_tokens), _ptr(acc), _ptr(toks), _ptr(num), _ptr(probs),
                              _ptr(ws), ws.numel()))
+    return acc, toks, num, probs
+
+
+def spec_accept_commit(ctx: Context, target_logits: torch.Tensor,
+                       draft_logits: Optional[torch.Tensor], draft_tokens: torch.Tensor,
+                       block_table, context_lens, free_stack, free_top, ref_counts,
+                       block_size: int, num_new: int, num_new_next: int = 0,
+                       mode: int = ACCEPT_STOCHASTIC, temperature: float = 1.0, seed: int = 0,
+                       step: int = 0, seq_offset: int = 0, out=None,
+                       workspace: Optional[torch.Tensor] = None, out_ok=None):
+    """kyro_spec_accept_commit: the acceptance, then the KV commit of the
+    accepted slots (and the reserve of num_new_next slots for the next step)
+    in one call; the commit runs beside the acceptance's final pass.
+    Returns (accept_len, tokens, num_tokens, probs or None) like spec_accept."""
+    dev = ctx.device
+    _need(target_logits, "target_logits", torch.float32, dev, 3)
+    B, k1, V = target_logits.shape
+    k = k1 - 1
+    _need(draft_tokens, "draft_tokens", torch.int32, dev)
+    if draft_tokens.numel() != B * k:
+        raise ValueError(f"draft_tokens must hold B*k = {B * k} entries")
+    if draft_logits is not None:
+        _need(draft_logits, "draft_logits", torch.float32, dev, 3)
+        if tuple(draft_logits.shape) != (B, k, V):
+            raise ValueError(f"draft_logits must be {(B, k, V)}, got {tuple(draft_logits.shape)}")
+    _check_kv_state(ctx, block_table, context_lens, free_stack, free_top, ref_counts)
+    if block_table.shape[0] != B:
+        raise ValueError("block_table batch differs from the logits' batch")
+    if out is None:
+        out = (torch.empty(B, dtype=torch.int32, device=dev),
+               torch.empty(B, k + 1, dtype=torch.int32, device=dev),
+               torch.empty(B, dtype=torch.int32, device=dev), None)
+    acc, toks, num, probs = out
+    p = AcceptParams(B, k, V, mode, float(temperature), step & 0xFFFFFFFF,
+                     seed & 0xFFFFFFFFFFFFFFFF, seq_offset)
+    kvp = _kv_params(block_table, block_size, ref_counts.numel())
+    L = _lib.load()
+    need = L.kyro_spec_accept_workspace_size(C.byref(p))
+    ws = workspace if workspace is not None else ctx.workspace(need)
+    ctx.bind_stream()
+    check(L.kyro_spec_accept_commit(ctx.handle, C.byref(p), _ptr(target_logits),
+                                    _ptr(draft_logits), _ptr(draft_tokens), _ptr(acc), _ptr(toks),
+                                    _ptr(num), _ptr(probs), _ptr(ws), ws.numel(), C.byref(kvp),
+                                    int(num_new), int(num_new_next), _ptr(block_table),
+                                    _ptr(context_lens), _ptr(free_stack), _ptr(free_top),
+                                    _ptr(ref_counts), _ptr(out_ok)))
     return acc, toks, num, probs
 
 

@@ -293,7 +293,7 @@ def rope_kv_write(q, k_new, v_new, block_table, context_lens, k_cache, v_cache, 
 
 def verify_step(state: dict, q, k_new, v_new, target_logits, draft_logits, draft_tokens,
                 block_size, mode=MODE_STOCHASTIC, temperature=1.0, seed=0, step=0,
-                seq_offset=0, rope_theta=None, nthreads=1):
+                seq_offset=0, rope_theta=None, nthreads=1, reserve=True, reserve_next=0):
     """One batched verify step, composed from the restatements above in the
     order SpeculativeDecoder::step runs it (src/speculative.rs:342-353) with
     the paged cache of the verify path:
@@ -308,12 +308,17 @@ def verify_step(state: dict, q, k_new, v_new, target_logits, draft_logits, draft
     `state` holds numpy arrays block_table, context_lens, free_stack,
     free_top, ref_counts and the uint16 caches k_cache, v_cache; all are
     modified in place.  q / k_new / v_new are uint16 bf16 bit patterns.
+    reserve=False skips the first reserve (an earlier step reserved the
+    slots); reserve_next > 0 reserves that many slots after the commit, and
+    `ok` is then that reserve's result.
     Returns dict(attention fp32 [B, k+1, Hq, D], ok, accept_len, tokens,
     num_tokens, probs)."""
     nq = np.asarray(target_logits).shape[1]
     s = state
-    ok = kv_reserve(nq, s["block_table"], s["context_lens"], s["free_stack"], s["free_top"],
-                    s["ref_counts"], block_size)
+    ok = None
+    if reserve:
+        ok = kv_reserve(nq, s["block_table"], s["context_lens"], s["free_stack"],
+                        s["free_top"], s["ref_counts"], block_size)
     if rope_theta is not None:
         qq = rope_kv_write(q, k_new, v_new, s["block_table"], s["context_lens"], s["k_cache"],
                            s["v_cache"], block_size, theta=rope_theta)
@@ -328,5 +333,8 @@ def verify_step(state: dict, q, k_new, v_new, target_logits, draft_logits, draft
                                         seq_offset=seq_offset, nthreads=nthreads)
     kv_commit(nq, acc, s["block_table"], s["context_lens"], s["free_stack"], s["free_top"],
               s["ref_counts"], block_size)
+    if reserve_next:
+        ok = kv_reserve(reserve_next, s["block_table"], s["context_lens"], s["free_stack"],
+                        s["free_top"], s["ref_counts"], block_size)
     return {"attention": att, "ok": ok, "accept_len": acc, "tokens": toks, "num_tokens": num,
             "probs": probs}

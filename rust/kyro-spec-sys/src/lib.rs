@@ -131,6 +131,14 @@ extern "C" {
         draft_logits: *const f32, draft_tokens: *const i32, out_accept_len: *mut i32,
         out_tokens: *mut i32, out_num_tokens: *mut i32, out_probs: *mut f32,
     ) -> c_int;
+    pub fn kyro_spec_accept_commit(
+        ctx: *mut kyro_ctx, p: *const kyro_accept_params, target_logits: *const f32,
+        draft_logits: *const f32, draft_tokens: *const i32, out_accept_len: *mut i32,
+        out_tokens: *mut i32, out_num_tokens: *mut i32, out_probs: *mut f32,
+        workspace: *mut c_void, workspace_bytes: usize, kv: *const kyro_kv_params, num_new: i32,
+        num_new_next: i32, block_table: *mut i64, context_lens: *mut i64, free_stack: *mut i32,
+        free_top: *mut i32, ref_counts: *mut i32, out_ok: *mut i32,
+    ) -> c_int;
     pub fn kyro_sample_workspace_size(p: *const kyro_sample_params) -> usize;
     pub fn kyro_sample_tokens(
         ctx: *mut kyro_ctx, p: *const kyro_sample_params, logits: *const f32,

@@ -27,8 +27,13 @@ def _np(t):
     return t.detach().cpu().numpy()
 
 
-@pytest.mark.parametrize("rope,mode,T", [(True, 0, 1.0), (False, 0, 0.7), (True, 2, 1.0)])
-def test_composed_step_matches_oracle(ctx, oracle, rope, mode, T):
+@pytest.mark.parametrize("rope,mode,T,loop", [(True, 0, 1.0, False), (False, 0, 0.7, False),
+                                               (True, 2, 1.0, False), (True, 0, 1.0, True),
+                                               (True, 1, 1.0, True)])
+def test_composed_step_matches_oracle(ctx, oracle, rope, mode, T, loop):
+    """loop: the decode-loop form, where a step's commit also reserves the
+    next step's slots (kyro_spec_accept_commit with num_new_next = k + 1)
+    after one initial reserve."""
     from kyro_b200.step import KVState, VerifyStep
     from kyro_b200.workloads import ChainConfig, accept_inputs, bf16_bits, paged_state
     # config-1 layer and vocabulary, a smaller batch with config-1 context draws
@@ -53,12 +58,22 @@ def test_composed_step_matches_oracle(ctx, oracle, rope, mode, T):
     step = VerifyStep(ctx, cfg.batch, cfg.k, cfg.num_heads, kv, cfg.vocab, cfg.block_size,
                       mode=mode, temperature=T, seed=7, seq_offset=100, rope_theta=theta)
     drf_in = drf if mode == 0 else None
+    nxt = cfg.num_query if loop else 0
+    if loop:
+        from kyro_b200.verify import kv_reserve
+        kv_reserve(ctx, cfg.num_query, st.block_table, st.context_lens, st.free_stack,
+                   st.free_top, st.ref_counts, cfg.block_size)
+        oracle.kv_reserve(cfg.num_query, host["block_table"], host["context_lens"],
+                          host["free_stack"], host["free_top"], host["ref_counts"],
+                          cfg.block_size)
     for i in range(2):
-        att, ok, acc, toks, num = step(kv, st.q, k_new, v_new, tgt, drf_in, drafts_d, step=i)
+        att, ok, acc, toks, num = step(kv, st.q, k_new, v_new, tgt, drf_in, drafts_d, step=i,
+                                       reserve=not loop, reserve_next=nxt)
         ref = oracle.verify_step(host, bf16_bits(st.q), bf16_bits(k_new), bf16_bits(v_new),
                                  _np(tgt), None if drf_in is None else _np(drf), drafts,
                                  cfg.block_size, mode=mode, temperature=T, seed=7, step=i,
-                                 seq_offset=100, rope_theta=theta, nthreads=NTHREADS)
+                                 seq_offset=100, rope_theta=theta, nthreads=NTHREADS,
+                                 reserve=not loop, reserve_next=nxt)
         torch.cuda.synchronize()
         assert np.array_equal(_np(ok), ref["ok"]), i
         assert np.array_equal(_np(acc), ref["accept_len"]), (i, _np(acc), ref["accept_len"])
