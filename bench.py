@@ -3,9 +3,9 @@
 One step = one batched verify pass over 64 sequences per GPU, the workload
 BASELINE.json's metric is quoted on (config 1), run by
 kyro_b200.step.VerifyStep:
-  rope_kv_write (RoPE of the new q/k rows at context_len + j, paged store
-  of the new K/V) -> verify attention (Llama-3-8B layer: Hq 32, Hkv 8,
-  D 128, bf16 paged KV, block 16, context ~ U[512, 4096]) -> acceptance
+  verify attention with RoPE of the new q/k rows at context_len + j and
+  the paged store of the new K/V in its prologue (Llama-3-8B layer: Hq 32,
+  Hkv 8, D 128, bf16 paged KV, block 16, context ~ U[512, 4096]) -> acceptance
   sampling (k = 5, V = 128256, fp32, T = 1.0) -> kv_commit of the accepted
   slots and kv_reserve of the next step's k+1 slots (the decode-loop form:
   kyro_spec_accept_commit runs the commit beside the acceptance's final
@@ -423,7 +423,7 @@ def run_ours(args):
 
     # algorithmic bytes per step, from the context lengths every step starts from
     lens0 = kvsnap.initial("context_lens").cpu().numpy()
-    per = chain_bytes_per_step(lens0, cfg, rope=True)
+    per = chain_bytes_per_step(lens0, cfg, separate_rope=not vstep.fused_rope)
     att_ms = float(np.mean([a.elapsed_time(b) for a, b in ev["attention"]]))
     acc_ms = float(np.mean([a.elapsed_time(b) for a, b in ev["accept"]]))
     rows = gather_rows([rank, int(lens0.sum()), per["attention"], per["accept"], att_ms, acc_ms,

@@ -231,6 +231,25 @@ int kyro_verify_attention(kyro_ctx* ctx, const kyro_attn_params* p, const void* 
                           const int64_t* context_lens, const uint64_t* tree_mask, void* out,
                           void* workspace, size_t workspace_bytes);
 
+/* LlamaAttention::forward's rotary embedding, new-token KV append and
+ * attention (src/model/llama.rs:73-90) in one launch: q, k_new and v_new
+ * (bf16 [B, num_query, Hq or Hkv, D]) arrive unrotated; query and key j are
+ * rotated at position context_len + pos_offsets[j] (pos_offsets NULL: + j),
+ * the keys and values are stored at slot context_len + j of the paged cache
+ * (the slots must be reserved), and the attention runs as in
+ * kyro_verify_attention.  The cache ends, and out is, bit for bit what
+ * kyro_rope_kv_write followed by kyro_verify_attention give; the rotated
+ * queries are not written out.  Same workspace as kyro_verify_attention.
+ * Shapes that take the tensor-core tree kernel (kyro_verify_attention on
+ * draft trees of >= 128 query rows per KV head) are rejected with
+ * KYRO_ERR_INVALID_ARG. */
+int kyro_verify_attention_rope(kyro_ctx* ctx, const kyro_attn_params* p, float rope_theta,
+                               const int32_t* pos_offsets, const void* q, const void* k_new,
+                               const void* v_new, void* k_cache, void* v_cache,
+                               const int64_t* block_table, const int64_t* context_lens,
+                               const uint64_t* tree_mask, void* out, void* workspace,
+                               size_t workspace_bytes);
+
 /* ------------------------------------------------ K3: KV commit / rollback */
 
 typedef struct kyro_kv_params {

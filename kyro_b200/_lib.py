@@ -43,6 +43,7 @@ EXPORTS = (
     "kyro_spec_accept_commit",
     "kyro_sample_workspace_size",
     "kyro_sample_tokens", "kyro_verify_attention_workspace_size", "kyro_verify_attention",
+    "kyro_verify_attention_rope",
     "kyro_kv_reserve", "kyro_kv_reserve_cow", "kyro_kv_commit", "kyro_kv_commit_tree", "kyro_kv_write",
     "kyro_rope_kv_write", "kyro_philox_uniforms", "kyro_selftest_exp",
     "kyro_tp_unique_id", "kyro_ctx_tp_init", "kyro_ctx_tp_transport",
@@ -129,6 +130,8 @@ def load():
         "kyro_verify_attention_workspace_size": (sz, [P(AttnParams)]),
         "kyro_verify_attention": (C.c_int, [vp, P(AttnParams), vp, vp, vp, vp, vp, vp, vp, vp,
                                             sz]),
+        "kyro_verify_attention_rope": (C.c_int, [vp, P(AttnParams), C.c_float, vp, vp, vp, vp, vp,
+                                                 vp, vp, vp, vp, vp, vp, sz]),
         "kyro_kv_reserve": (C.c_int, [vp, P(KVParams), i32, vp, vp, vp, vp, vp, vp]),
         "kyro_kv_commit": (C.c_int, [vp, P(KVParams), i32, vp, vp, vp, vp, vp, vp]),
         "kyro_kv_reserve_cow": (C.c_int, [vp, P(KVParams), i32, i32, vp, vp, i32, i32, vp, vp, vp,

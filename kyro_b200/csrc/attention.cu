@@ -28,10 +28,12 @@
 // that finishes last (an epoch-tagged atomic ticket) merges them.
 #include <cuda_bf16.h>
 
+#include <cmath>
 #include <mutex>
 
 #include "kyro_internal.cuh"
 #include "ptx.cuh"
+#include "rope.cuh"
 
 namespace {
 
@@ -73,6 +75,18 @@ struct AttnArgs {
   uint32_t epoch;  // nonzero, new on every call: split tickets of older calls count as zero
 };
 
+// The rotary embedding fused into the prologue (kyro_verify_attention_rope):
+// the unrotated new keys and values, the caches they are stored into, and
+// the rotary frequencies (D <= 128).
+struct RopeIn {
+  const uint4* k_new;          // bf16 [B, nq, Hkv, D]
+  const uint4* v_new;
+  const int32_t* pos_offsets;  // [nq] or NULL (offset j)
+  uint8_t* k_cache;
+  uint8_t* v_cache;
+  float inv_freq[64];
+};
+
 // byte offset of (token row, 16-byte chunk along D) inside a swizzled tile:
 // 64-column halves of 2 KB, rows of 128 B, chunk index XOR (row & 7)
 __device__ __forceinline__ uint32_t kv_off(int row, int cidx) {
@@ -99,15 +113,20 @@ __device__ __forceinline__ void load_block(uint32_t slot, const uint8_t* __restr
   }
 }
 
-template <int NT, int D, int NS>
+// ROPE: the queries arrive unrotated and this step's keys and values are not
+// in the cache yet.  The prologue rotates the CTA's query rows, and a CTA
+// whose blocks hold new slots rotates those keys and stores them with their
+// values before it streams the blocks (the cache is read only by cp.async,
+// after a fence and a barrier).
+template <int NT, int D, int NS, bool ROPE>
 __global__ void __launch_bounds__(kThreads, 3)
 verify_attention_kernel(const __nv_bfloat16* __restrict__ q,
-                        const uint8_t* __restrict__ k_base, const uint8_t* __restrict__ v_base,
+                        const uint8_t* k_base, const uint8_t* v_base,
                         const int64_t* __restrict__ block_table,
                         const int64_t* __restrict__ context_lens,
                         const uint64_t* __restrict__ tree_mask, __nv_bfloat16* __restrict__ out,
                         float* __restrict__ part_o, float* __restrict__ part_ml,
-                        unsigned long long* __restrict__ tickets, AttnArgs a,
+                        unsigned long long* __restrict__ tickets, AttnArgs a, RopeIn r,
                         uint32_t* status) {
   extern __shared__ __align__(128) uint8_t smem[];
   using G = Geo<D, NS>;
@@ -181,16 +200,22 @@ verify_attention_kernel(const __nv_bfloat16* __restrict__ q,
   const uint32_t q_s = ring_s + G::kRingBytes;
 
   // ---- this warp's first blocks go out before the setup below, so their
-  // latency overlaps it
+  // latency overlaps it.  With ROPE, a block from ctx / kBS on receives new
+  // keys below: its load waits until they are stored ("late").
   const int nmy = nb > warp ? (nb - warp + kWarps - 1) / kWarps : 0;
   const uint32_t wring0 = kyro::ptx::smem_addr(smem) + warp * G::kWarpRing;
+  uint32_t late = 0;
 #pragma unroll
   for (int p = 0; p < NS - 1; ++p) {
     if (p < nmy) {
-      int64_t phys = first_ids[p];
-      if (phys < 0 || phys >= a.num_blocks) phys = 0;  // flagged below
-      load_block<D>(wring0 + p * kSlotBytes, k_base, v_base, (phys * a.hkv + kvh) * kTileBytes,
-                    lane);
+      if (ROPE && blk0 + p * kWarps + warp >= ctx / kBS) {
+        late |= 1u << p;
+      } else {
+        int64_t phys = first_ids[p];
+        if (phys < 0 || phys >= a.num_blocks) phys = 0;  // flagged below
+        load_block<D>(wring0 + p * kSlotBytes, k_base, v_base, (phys * a.hkv + kvh) * kTileBytes,
+                      lane);
+      }
     }
     kyro::ptx::cp_async_commit();
   }
@@ -208,11 +233,13 @@ verify_attention_kernel(const __nv_bfloat16* __restrict__ q,
       ids[i] = (int32_t)phys;
     }
   }
+  if (!ROPE) {
 #pragma unroll
-  for (int j = 0; j < kQPerThread; ++j) {
-    const int i = tid + j * kThreads;
-    const int col = i / (kD / 8), ch = i % (kD / 8);
-    *reinterpret_cast<uint4*>(qtile + col * kQStride * 2 + ch * 16) = my_q[j];
+    for (int j = 0; j < kQPerThread; ++j) {
+      const int i = tid + j * kThreads;
+      const int col = i / (kD / 8), ch = i % (kD / 8);
+      *reinterpret_cast<uint4*>(qtile + col * kQStride * 2 + ch * 16) = my_q[j];
+    }
   }
   for (int col = tid; col < kMaxCols; col += kThreads) {
     uint64_t m = 0;
@@ -223,7 +250,112 @@ verify_attention_kernel(const __nv_bfloat16* __restrict__ q,
     }
     col_mask[col] = m;
   }
+  // ROPE: cos and sin of every new position, in the ring slot that no
+  // prefetch fills (slot NS-1 of each warp; position p in warp p / kTabRows)
+  constexpr int kHalf = kD / 2;
+  constexpr int kTabRowBytes = kHalf * 8;
+  constexpr int kTabRows = kSlotBytes / kTabRowBytes;
+  static_assert(kWarps * kTabRows >= 64, "the table holds 64 positions");
+  auto tab = [&](int p) -> const float2* {
+    return reinterpret_cast<const float2*>(ring + (p / kTabRows) * G::kWarpRing +
+                                           (NS - 1) * kSlotBytes + (p % kTabRows) * kTabRowBytes);
+  };
+  if (ROPE) {
+    for (int idx = tid; idx < a.nq * kHalf; idx += kThreads) {
+      const int p = idx / kHalf, i = idx - p * kHalf;
+      // the rotary position: (index + offset) as f32 (layers.rs:45)
+      const float pf = (float)(ctx + (r.pos_offsets ? r.pos_offsets[p] : p));
+      float c, sn;
+      kyro::rope::angle(pf, r.inv_freq[i], c, sn);
+      const_cast<float2*>(tab(p))[i] = make_float2(c, sn);
+    }
+  }
   __syncthreads();
+  if (ROPE) {
+    // the query rows: thread tid holds 16-byte piece ch of row col (i = tid
+    // + j * kThreads); the piece with the other half of the same dims sits
+    // in thread tid ^ kHalfPieces
+    constexpr int kHalfPieces = kD / 16;
+#pragma unroll
+    for (int j = 0; j < kQPerThread; ++j) {
+      const int i = tid + j * kThreads;
+      const int col = i / (kD / 8), ch = i % (kD / 8);
+      const uint4 x = my_q[j];
+      uint4 y;
+      y.x = __shfl_xor_sync(0xffffffffu, x.x, kHalfPieces);
+      y.y = __shfl_xor_sync(0xffffffffu, x.y, kHalfPieces);
+      y.z = __shfl_xor_sync(0xffffffffu, x.z, kHalfPieces);
+      y.w = __shfl_xor_sync(0xffffffffu, x.w, kHalfPieces);
+      uint4 o = make_uint4(0, 0, 0, 0);
+      if (col < ncols) {
+        const bool first = ch < kHalfPieces;
+        const uint4 wa = first ? x : y, wb = first ? y : x;
+        const uint32_t a4[4] = {wa.x, wa.y, wa.z, wa.w}, b4[4] = {wb.x, wb.y, wb.z, wb.w};
+        const float2* cs = tab((col0 + col) / a.group) + (first ? ch : ch - kHalfPieces) * 8;
+        uint32_t o4[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 t0 = cs[2 * e], t1 = cs[2 * e + 1];
+          uint32_t lo, hi;
+          kyro::rope::rotate_pair(a4[e], b4[e], t0.x, t1.x, t0.y, t1.y, lo, hi);
+          o4[e] = first ? lo : hi;
+        }
+        o = make_uint4(o4[0], o4[1], o4[2], o4[3]);
+      }
+      *reinterpret_cast<uint4*>(qtile + col * kQStride * 2 + ch * 16) = o;
+    }
+    // the new slots ctx + j that fall in this split's blocks: rotated keys
+    // (a piece and its partner per item) and values (one piece per item)
+    const int64_t s_lo = (int64_t)blk0 * kBS - ctx, s_hi = (int64_t)(blk0 + nb) * kBS - ctx;
+    const int j_lo = (int)(s_lo > 0 ? s_lo : 0);
+    const int j_hi = (int)(s_hi < a.nq ? s_hi : a.nq);
+    const int nrow = j_hi - j_lo;
+    for (int it = tid; it < nrow * (kHalfPieces + kD / 8); it += kThreads) {
+      const bool is_k = it < nrow * kHalfPieces;
+      const int rel = is_k ? it : it - nrow * kHalfPieces;
+      const int per = is_k ? kHalfPieces : kD / 8;
+      const int j = j_lo + rel / per, c = rel - (rel / per) * per;
+      const int64_t slot = ctx + j;
+      const int64_t phys = block_table[(int64_t)b * a.max_blocks + slot / kBS];
+      if (phys < 0 || phys >= a.num_blocks) continue;  // flagged with the block ids
+      const int64_t row = ((phys * a.hkv + kvh) * kBS + slot % kBS) * (kD / 8);  // uint4 units
+      const int64_t src = (((int64_t)b * a.nq + j) * a.hkv + kvh) * (kD / 8);
+      if (is_k) {
+        const uint4 x1 = r.k_new[src + c], x2 = r.k_new[src + kHalfPieces + c];
+        const uint32_t a4[4] = {x1.x, x1.y, x1.z, x1.w}, b4[4] = {x2.x, x2.y, x2.z, x2.w};
+        const float2* cs = tab(j) + c * 8;
+        uint32_t lo[4], hi[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 t0 = cs[2 * e], t1 = cs[2 * e + 1];
+          kyro::rope::rotate_pair(a4[e], b4[e], t0.x, t1.x, t0.y, t1.y, lo[e], hi[e]);
+        }
+        uint4* dst = reinterpret_cast<uint4*>(r.k_cache) + row;
+        dst[c] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        dst[kHalfPieces + c] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+      } else {
+        reinterpret_cast<uint4*>(r.v_cache)[row + c] = r.v_new[src + c];
+      }
+    }
+    // the stores reach L2 before any cp.async of this CTA reads the blocks;
+    // the table's slot is free again after the barrier
+    __threadfence();
+    __syncthreads();
+    // the late blocks: one copy group for every prefetch position from the
+    // first late one on (empty where the warp has no block), in order, so
+    // that the ring's group count still finds block i complete at iteration i
+    if (late) {
+      const int p0 = __ffs(late) - 1;
+#pragma unroll
+      for (int p = 0; p < NS - 1; ++p) {
+        if (p < p0) continue;
+        if (late & (1u << p))
+          load_block<D>(wring0 + p * kSlotBytes, k_base, v_base,
+                        ((int64_t)ids[p * kWarps + warp] * a.hkv + kvh) * kTileBytes, lane);
+        kyro::ptx::cp_async_commit();
+      }
+    }
+  }
 
   // ---- this warp's blocks: w, w + 4, w + 8, ... of the split (the first
   // NS-1 already in flight)
@@ -616,32 +748,82 @@ size_t ws_bytes(const Plan& pl) {
   return align256(pl.part_o_bytes) + align256(pl.part_ml_bytes) + align256(pl.ticket_bytes);
 }
 
-template <int NT, int D>
+template <int NT, int D, bool ROPE>
 void launch(const Plan& pl, dim3 grid, cudaStream_t st, const void* q, const void* kc,
             const void* vc, const int64_t* bt, const int64_t* cl, const uint64_t* tm, void* out,
-            float* po, float* pml, unsigned long long* tk, uint32_t* status) {
+            float* po, float* pml, unsigned long long* tk, const RopeIn& r, uint32_t* status) {
   constexpr int kStages = stages_for<D>();
   constexpr int smem = Geo<D, kStages>::kSmemBytes;
   static std::once_flag attr_once;  // one host call per kernel, never inside a graph capture
   std::call_once(attr_once, [] {
-    cudaFuncSetAttribute(verify_attention_kernel<NT, D, kStages>,
+    cudaFuncSetAttribute(verify_attention_kernel<NT, D, kStages, ROPE>,
                          cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   });
-  kyro::launch_pdl(verify_attention_kernel<NT, D, kStages>, grid, dim3(kThreads), smem, st,
+  kyro::launch_pdl(verify_attention_kernel<NT, D, kStages, ROPE>, grid, dim3(kThreads), smem, st,
                    "verify_attention_kernel", (const __nv_bfloat16*)q, (const uint8_t*)kc,
-                   (const uint8_t*)vc, bt, cl, tm, (__nv_bfloat16*)out, po, pml, tk, pl.a, status);
+                   (const uint8_t*)vc, bt, cl, tm, (__nv_bfloat16*)out, po, pml, tk, pl.a, r,
+                   status);
 }
 
-template <int D>
+template <int D, bool ROPE>
 void launch_d(const Plan& pl, dim3 grid, cudaStream_t st, const void* q, const void* kc,
               const void* vc, const int64_t* bt, const int64_t* cl, const uint64_t* tm,
-              void* out, float* po, float* pml, unsigned long long* tk, uint32_t* status) {
+              void* out, float* po, float* pml, unsigned long long* tk, const RopeIn& r,
+              uint32_t* status) {
   switch (pl.nt) {
-    case 1: launch<1, D>(pl, grid, st, q, kc, vc, bt, cl, tm, out, po, pml, tk, status); break;
-    case 2: launch<2, D>(pl, grid, st, q, kc, vc, bt, cl, tm, out, po, pml, tk, status); break;
-    case 3: launch<3, D>(pl, grid, st, q, kc, vc, bt, cl, tm, out, po, pml, tk, status); break;
-    default: launch<4, D>(pl, grid, st, q, kc, vc, bt, cl, tm, out, po, pml, tk, status); break;
+    case 1: launch<1, D, ROPE>(pl, grid, st, q, kc, vc, bt, cl, tm, out, po, pml, tk, r, status); break;
+    case 2: launch<2, D, ROPE>(pl, grid, st, q, kc, vc, bt, cl, tm, out, po, pml, tk, r, status); break;
+    case 3: launch<3, D, ROPE>(pl, grid, st, q, kc, vc, bt, cl, tm, out, po, pml, tk, r, status); break;
+    default: launch<4, D, ROPE>(pl, grid, st, q, kc, vc, bt, cl, tm, out, po, pml, tk, r, status); break;
   }
+}
+
+// The split-KV kernel (not the tcgen05 tree kernel) on a planned call; r
+// non-null fuses the rotary embedding.
+int run_split_kernel(kyro_ctx* ctx, const kyro_attn_params* p, Plan& pl, const void* q,
+                     const void* k_cache, const void* v_cache, const int64_t* block_table,
+                     const int64_t* context_lens, const uint64_t* tree_mask, void* out,
+                     void* workspace, size_t workspace_bytes, const RopeIn* r, const char* fn) {
+  const size_t need = ws_bytes(pl);
+  if (need > 0 && (workspace_bytes < need || !workspace))
+    return kyro::set_error(KYRO_ERR_WORKSPACE, "%s: workspace %zu < %zu bytes", fn,
+                           workspace_bytes, need);
+  KY_REQUIRE(need == 0 || (uintptr_t)workspace % 256 == 0,
+             "%s: workspace must be 256-byte aligned", fn);
+  float* po = (float*)workspace;
+  float* pml = (float*)((char*)workspace + align256(pl.part_o_bytes));
+  unsigned long long* tk = (unsigned long long*)((char*)workspace + align256(pl.part_o_bytes) +
+                                                 align256(pl.part_ml_bytes));
+  dim3 grid((unsigned)pl.a.max_splits, (unsigned)(pl.a.hkv * pl.a.ngroups), (unsigned)pl.a.B);
+  cudaStream_t st = ctx->stream;
+  // split tickets carry the call's epoch, so one workspace needs zeroing
+  // only the first time this context sees it (a zeroed ticket holds epoch 0,
+  // which no call uses)
+  if (++ctx->attn_epoch == 0) ctx->attn_epoch = 1;
+  pl.a.epoch = ctx->attn_epoch;
+  if (pl.ticket_bytes && workspace != ctx->attn_ws_zeroed) {
+    cudaError_t err = cudaMemsetAsync(tk, 0, pl.ticket_bytes, st);
+    if (err != cudaSuccess) return kyro::cuda_error(err, "cudaMemsetAsync(attention tickets)");
+    ctx->attn_ws_zeroed = workspace;
+  }
+  RopeIn none{};
+  const RopeIn& rr = r ? *r : none;
+  if (p->head_dim == 128) {
+    if (r)
+      launch_d<128, true>(pl, grid, st, q, k_cache, v_cache, block_table, context_lens, tree_mask,
+                          out, po, pml, tk, rr, ctx->d_status);
+    else
+      launch_d<128, false>(pl, grid, st, q, k_cache, v_cache, block_table, context_lens, tree_mask,
+                           out, po, pml, tk, rr, ctx->d_status);
+  } else {
+    if (r)
+      launch_d<64, true>(pl, grid, st, q, k_cache, v_cache, block_table, context_lens, tree_mask,
+                         out, po, pml, tk, rr, ctx->d_status);
+    else
+      launch_d<64, false>(pl, grid, st, q, k_cache, v_cache, block_table, context_lens, tree_mask,
+                          out, po, pml, tk, rr, ctx->d_status);
+  }
+  return kyro::check_launch("verify_attention_kernel");
 }
 
 }  // namespace
@@ -676,35 +858,47 @@ int kyro_verify_attention(kyro_ctx* ctx, const kyro_attn_params* p, const void* 
   if (kyro::tree_attention_eligible(p))
     return kyro::tree_attention_launch(ctx, p, q, k_cache, v_cache, block_table, context_lens,
                                        tree_mask, out);
-  const size_t need = ws_bytes(pl);
-  if (need > 0 && (workspace_bytes < need || !workspace))
-    return kyro::set_error(KYRO_ERR_WORKSPACE, "kyro_verify_attention: workspace %zu < %zu bytes",
-                           workspace_bytes, need);
-  KY_REQUIRE(need == 0 || (uintptr_t)workspace % 256 == 0,
-             "kyro_verify_attention: workspace must be 256-byte aligned");
-  float* po = (float*)workspace;
-  float* pml = (float*)((char*)workspace + align256(pl.part_o_bytes));
-  unsigned long long* tk = (unsigned long long*)((char*)workspace + align256(pl.part_o_bytes) +
-                                                 align256(pl.part_ml_bytes));
-  dim3 grid((unsigned)pl.a.max_splits, (unsigned)(pl.a.hkv * pl.a.ngroups), (unsigned)pl.a.B);
-  cudaStream_t st = ctx->stream;
-  // split tickets carry the call's epoch, so one workspace needs zeroing
-  // only the first time this context sees it (a zeroed ticket holds epoch 0,
-  // which no call uses)
-  if (++ctx->attn_epoch == 0) ctx->attn_epoch = 1;
-  pl.a.epoch = ctx->attn_epoch;
-  if (pl.ticket_bytes && workspace != ctx->attn_ws_zeroed) {
-    cudaError_t err = cudaMemsetAsync(tk, 0, pl.ticket_bytes, st);
-    if (err != cudaSuccess) return kyro::cuda_error(err, "cudaMemsetAsync(attention tickets)");
-    ctx->attn_ws_zeroed = workspace;
-  }
-  if (p->head_dim == 128)
-    launch_d<128>(pl, grid, st, q, k_cache, v_cache, block_table, context_lens, tree_mask, out, po,
-                  pml, tk, ctx->d_status);
-  else
-    launch_d<64>(pl, grid, st, q, k_cache, v_cache, block_table, context_lens, tree_mask, out, po,
-                 pml, tk, ctx->d_status);
-  return kyro::check_launch("verify_attention_kernel");
+  return run_split_kernel(ctx, p, pl, q, k_cache, v_cache, block_table, context_lens, tree_mask,
+                          out, workspace, workspace_bytes, nullptr, "kyro_verify_attention");
+}
+
+int kyro_verify_attention_rope(kyro_ctx* ctx, const kyro_attn_params* p, float rope_theta,
+                               const int32_t* pos_offsets, const void* q, const void* k_new,
+                               const void* v_new, void* k_cache, void* v_cache,
+                               const int64_t* block_table, const int64_t* context_lens,
+                               const uint64_t* tree_mask, void* out, void* workspace,
+                               size_t workspace_bytes) {
+  KY_NVTX("kyro_verify_attention_rope");
+  KY_TRY(kyro::enter(ctx));
+  Plan pl;
+  KY_TRY(plan(p, 148, &pl));
+  KY_REQUIRE(rope_theta > 0.0f, "kyro_verify_attention_rope: rope_theta = %g",
+             (double)rope_theta);
+  KY_REQUIRE(!kyro::tree_attention_eligible(p),
+             "kyro_verify_attention_rope: this shape runs on the tensor-core tree kernel; "
+             "use kyro_rope_kv_write and kyro_verify_attention");
+  if (p->batch == 0) return KYRO_OK;
+  KY_REQUIRE(q && k_new && v_new && k_cache && v_cache && block_table && context_lens && out,
+             "kyro_verify_attention_rope: a required pointer is NULL");
+  KY_REQUIRE((uintptr_t)k_cache % 16 == 0 && (uintptr_t)v_cache % 16 == 0 &&
+                 (uintptr_t)q % 16 == 0 && (uintptr_t)k_new % 16 == 0 &&
+                 (uintptr_t)v_new % 16 == 0,
+             "kyro_verify_attention_rope: q, k_new, v_new and the caches must be 16-byte "
+             "aligned");
+  KY_REQUIRE(pl.a.B <= 65535, "kyro_verify_attention_rope: batch %d > 65535", pl.a.B);
+  RopeIn r{};
+  r.k_new = (const uint4*)k_new;
+  r.v_new = (const uint4*)v_new;
+  r.pos_offsets = pos_offsets;
+  r.k_cache = (uint8_t*)k_cache;
+  r.v_cache = (uint8_t*)v_cache;
+  // RotaryEmbedding::new (layers.rs:26-33): 1 / theta^(2i/D) in double, then fp32
+  for (int i = 0; i < 64; ++i)
+    r.inv_freq[i] = i < p->head_dim / 2
+                        ? (float)(1.0 / std::pow((double)rope_theta, 2.0 * i / p->head_dim))
+                        : 0.0f;
+  return run_split_kernel(ctx, p, pl, q, k_cache, v_cache, block_table, context_lens, tree_mask,
+                          out, workspace, workspace_bytes, &r, "kyro_verify_attention_rope");
 }
 
 }  // extern "C"

@@ -69,10 +69,11 @@ extern "C" {
 int kyro_version(void) { return KYRO_VERSION; }
 
 const char* kyro_kernel_names(void) {
-  return "accept_stats_kernel;accept_decide_kernel;accept_final_kernel;accept_wave_kernel;accept_tree_kernel;accept_tree_cluster_kernel;"
-         "accept_tp_max_kernel;accept_tp_sum_kernel;accept_tp_decide_kernel;"
-         "accept_tp_search_kernel;accept_tp_write_kernel;verify_attention_kernel;"
-         "kv_reserve_kernel;kv_commit_kernel;kv_commit_reserve_kernel;kv_tree_move_kernel;kv_write_kernel;rope_kv_write_kernel;kv_block_copy_kernel;"
+  return "accept_stats_kernel;accept_decide_kernel;accept_final_kernel;accept_tree_kernel;"
+         "accept_tree_cluster_kernel;accept_tp_max_kernel;accept_tp_sum_kernel;"
+         "accept_tp_decide_kernel;accept_tp_search_kernel;accept_tp_write_kernel;"
+         "verify_attention_kernel;kv_reserve_kernel;kv_commit_kernel;kv_commit_reserve_kernel;"
+         "kv_tree_move_kernel;kv_write_kernel;rope_kv_write_kernel;kv_block_copy_kernel;"
          "philox_uniforms_kernel;exp_selftest_kernel;tree_attention_tc_kernel;peer_exchange_kernel";
 }
 
@@ -131,6 +132,7 @@ int kyro_ctx_create(int device, void* stream, kyro_ctx** out) {
   ctx->tp_world = 1;
   ctx->attn_epoch = 0;
   ctx->attn_ws_zeroed = nullptr;
+  ctx->accept_ws_zeroed = nullptr;
   {
     // a salt per context: tags of different contexts differ
     static std::atomic<uint32_t> contexts{0};

@@ -22,6 +22,7 @@
 #include <cmath>
 
 #include "kyro_internal.cuh"
+#include "rope.cuh"
 
 namespace {
 
@@ -451,15 +452,8 @@ kv_write_kernel(int num_new, int hkv, int d, int bs, int max_blocks, int num_blo
 }
 
 // Rotary position embedding of the new tokens, fused with the paged K/V
-// store (LlamaAttention::forward, src/model/llama.rs:77-82, then append_kv).
-// RotaryEmbedding::apply (src/model/layers.rs:37-61) rotates the two halves
-// of every head: y[i] = x[i]*cos(f_i) - x[i+D/2]*sin(f_i) and y[i+D/2] =
-// x[i+D/2]*cos(f_i) + x[i]*sin(f_i), with f_i = pos * inv_freq[i] in fp32
-// and inv_freq[i] = (float)(1 / theta^(2i/D)) formed in double (:26-33).
-// Each product and the sum round to fp32 separately, as the reference's
-// broadcast_mul / add do; cos and sin are those of the fp32 angle, rounded
-// to fp32 (evaluated in double, so they are the correctly rounded values in
-// all but vanishingly rare cases).
+// store (LlamaAttention::forward, src/model/llama.rs:77-82, then append_kv);
+// the arithmetic is kyro::rope's (rope.cuh).
 constexpr int kRopeMaxHalf = 128;  // head_dim <= 256
 constexpr int kRopeThreads = 256;
 constexpr int kRopePrefetch = 2;   // rotation pieces per thread loaded before the angles
@@ -468,15 +462,6 @@ struct RopeArgs {
   int num_new, hq, hkv, d, bs, max_blocks, num_blocks;
   float inv_freq[kRopeMaxHalf];
 };
-
-__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
-__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
-
-__device__ __forceinline__ uint32_t bf16_pack(float lo, float hi) {
-  uint32_t r;
-  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
-  return r;
-}
 
 // grid (B, num_new): one CTA rotates the query and key heads of one new
 // token, writes the queries to q_out and the rotated keys and the values to
@@ -521,12 +506,8 @@ rope_kv_write_kernel(RopeArgs a, const int32_t* __restrict__ pos_offsets,
   bool slot_ok = ctx >= 0 && pos / a.bs < a.max_blocks;
   int64_t blk = -1;
   if (slot_ok) blk = block_table[(int64_t)b * a.max_blocks + pos / a.bs];
-  for (int i = threadIdx.x; i < half; i += blockDim.x) {
-    double sd, cd;
-    sincos((double)__fmul_rn(pf, a.inv_freq[i]), &sd, &cd);
-    cs[i] = (float)cd;
-    sn[i] = (float)sd;
-  }
+  for (int i = threadIdx.x; i < half; i += blockDim.x)
+    kyro::rope::angle(pf, a.inv_freq[i], cs[i], sn[i]);
   if (slot_ok && (blk < 0 || blk >= a.num_blocks)) {
     if (threadIdx.x == 0) kyro::dev::flag(status, KYRO_DEV_BAD_BLOCK);
     slot_ok = false;
@@ -555,13 +536,7 @@ rope_kv_write_kernel(RopeArgs a, const int32_t* __restrict__ pos_offsets,
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const int i0 = c * 8 + 2 * e;
-      const float a0 = bf16_lo(w1[e]), a1 = bf16_hi(w1[e]);
-      const float b0 = bf16_lo(w2[e]), b1 = bf16_hi(w2[e]);
-      const float c0 = cs[i0], c1 = cs[i0 + 1], s0 = sn[i0], s1 = sn[i0 + 1];
-      y1[e] = bf16_pack(__fadd_rn(__fmul_rn(a0, c0), __fmul_rn(-b0, s0)),
-                        __fadd_rn(__fmul_rn(a1, c1), __fmul_rn(-b1, s1)));
-      y2[e] = bf16_pack(__fadd_rn(__fmul_rn(b0, c0), __fmul_rn(a0, s0)),
-                        __fadd_rn(__fmul_rn(b1, c1), __fmul_rn(a1, s1)));
+      kyro::rope::rotate_pair(w1[e], w2[e], cs[i0], cs[i0 + 1], sn[i0], sn[i0 + 1], y1[e], y2[e]);
     }
     const uint4 o1 = make_uint4(y1[0], y1[1], y1[2], y1[3]);
     const uint4 o2 = make_uint4(y2[0], y2[1], y2[2], y2[3]);

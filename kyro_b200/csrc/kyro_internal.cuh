@@ -35,6 +35,7 @@ struct kyro_ctx {
   // workspace whose tickets this context has zeroed
   uint32_t attn_epoch;
   const void* attn_ws_zeroed;
+  const void* accept_ws_zeroed;  // workspace whose stats unit counter this context zeroed
   // the acceptance pipeline's generation count and finished-sequence
   // count (device words owned by the context; sampler.cu), and the salt
   // of its record tags

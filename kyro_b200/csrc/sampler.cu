@@ -53,6 +53,9 @@ constexpr int kMaxRows = 2 * kMaxDraft + 1;
 constexpr int kDecideWarps = 16;
 constexpr int kFinalPerWarp = 4;   // chunks per warp in the final kernel
 constexpr int kFinalPerCta = kWarps * kFinalPerWarp;
+// Resident final CTAs per SM: 7 x 148 holds config 1's 1024 CTAs in one
+// wave, so no CTA waits for a slot behind CTAs that wait for their flags.
+constexpr int kFinalMinCtas = 7;
 
 static_assert(kChunk == 512, "the kernels assume 16 logits per lane");
 
@@ -168,6 +171,9 @@ struct Args {
   unsigned long long* W;        // [B][nchunks] weight sums of the chosen rows
   uint32_t* cnt_c;              // [B] finished weight sums per sequence
   uint32_t units;               // stats units: B * R * nchunks
+  // Dynamic stats units (non-null): [0] the next unit to take, [1] retired
+  // warps; both back at zero when the stats kernel ends
+  uint32_t* unit_ctr;
   uint32_t* status;
   // tensor parallelism (vocabulary shards): V above is this shard's width
   int64_t V_global;             // the full vocabulary (V without a group)
@@ -190,8 +196,11 @@ struct Args {
 
 __host__ __device__ inline size_t align_up(size_t x) { return (x + 255) & ~size_t(255); }
 
-// Workspace layout.  cnt_c is zeroed by the decide kernel of each call.
+// Workspace layout.  cnt_c is zeroed by the decide kernel of each call; the
+// stats kernel's unit counter (first 8 bytes) is left at zero by every call
+// that uses it, and zeroed once when a context first sees the workspace.
 struct Workspace {
+  uint32_t* unit_ctr;  // 2 words at offset 0 in every layout
   uint32_t* cnt_c;
   size_t counter_bytes;
   ChunkStat* stats;
@@ -206,6 +215,8 @@ Workspace carve(void* base, int64_t B, int64_t R, int64_t nchunks) {
   Workspace w;
   char* p = (char*)base;
   size_t off = 0;
+  w.unit_ctr = (uint32_t*)(p + off);
+  off += 256;
   w.cnt_c = (uint32_t*)(p + off);
   off += align_up(4 * (size_t)B);
   w.counter_bytes = off;
@@ -740,17 +751,74 @@ __device__ __forceinline__ void reduce_slice(const Args& a, Slice& s, uint32_t t
   if (lane == 0) st_stat(a.stats + (int64_t)s.srow * a.nchunks + s.c, st.m, st.E, tag);
 }
 
-// Persistent and grid-stride: warp w takes units w, w + W, w + 2W, ... (W =
-// warps in the grid), so neighbouring warps read neighbouring chunks.  Each
-// warp loads unit i+1 before it reduces unit i.
+// Units a warp takes from the counter at a time (dynamic distribution).
+constexpr uint32_t kGrab = 4;
+
+__device__ __forceinline__ uint32_t take_units(uint32_t* ctr) {
+  uint32_t v = 0;
+  if ((threadIdx.x & 31) == 0) v = atomicAdd(ctr, kGrab);
+  return __shfl_sync(0xffffffffu, v, 0);
+}
+
+// Persistent; each warp loads unit i+1 before it reduces unit i.
+//
+// Static (unit_ctr null): warp w takes units w, w + W, w + 2W, ... (W =
+// warps in the grid), so neighbouring warps read neighbouring chunks.
+//
+// Dynamic (unit_ctr set): warps take batches of kGrab consecutive units
+// from a counter, one batch ahead, so a warp on an SM that streams faster
+// takes more of them.  Measured on config 1, a static split left half of
+// the warps idle for the last quarter of the pass (warp end times 48 to
+// 71 us, median 54).  Every warp retires once it has seen the counter past
+// the last unit; the last one to retire sets the counter back to zero for
+// the next call on this workspace.
 template <bool VEC, bool STOCH>
 __global__ void __launch_bounds__(kThreads, kStatsMinCtas) accept_stats_kernel(Args a) {
   allow_dependents();
   const uint32_t tag = call_tag(a);
+  Slice s0, s1;
+  if (a.unit_ctr) {
+    uint32_t u = take_units(a.unit_ctr);
+    uint32_t nxt = take_units(a.unit_ctr);
+    if (u < a.units) {
+      uint32_t end = min(u + kGrab, a.units);
+      // the unit after u, or a value >= units when the warp is done
+      auto advance = [&](uint32_t cur) -> uint32_t {
+        if (cur + 1 < end) return cur + 1;
+        const uint32_t n = nxt;
+        if (n < a.units) {
+          end = min(n + kGrab, a.units);
+          nxt = take_units(a.unit_ctr);
+        }
+        return n;
+      };
+      load_slice<VEC>(a, u, s0);
+      while (true) {
+        uint32_t un = advance(u);
+        if (un < a.units) load_slice<VEC>(a, un, s1);
+        reduce_slice<STOCH>(a, s0, tag);
+        if (un >= a.units) break;
+        u = un;
+        un = advance(u);
+        if (un < a.units) load_slice<VEC>(a, un, s0);
+        reduce_slice<STOCH>(a, s1, tag);
+        if (un >= a.units) break;
+        u = un;
+      }
+    }
+    // every take of this warp has returned: retire; the last warp resets
+    if ((threadIdx.x & 31) == 0) {
+      __threadfence();
+      if (atomicAdd(a.unit_ctr + 1, 1u) == gridDim.x * (uint32_t)kWarps - 1u) {
+        a.unit_ctr[0] = 0u;
+        a.unit_ctr[1] = 0u;
+      }
+    }
+    return;
+  }
   const uint32_t stride = gridDim.x * kWarps;
   uint32_t u = blockIdx.x * kWarps + (threadIdx.x >> 5);
   if (u >= a.units) return;
-  Slice s0, s1;
   load_slice<VEC>(a, u, s0);
   while (true) {
     uint32_t un = u + stride;
@@ -1078,43 +1146,48 @@ __device__ __forceinline__ float4 load4(const float* __restrict__ row, int64_t e
   return f;
 }
 
-// fix62 weights of 4 logits of a final row: residual max(p - q, 0) or p.
-// Residual: each element's p and q exps form one packed pair; from p
-// alone, neighbouring elements pair up.
+// fix62 weights of 4 logits of a final row: residual max(p - q, 0) or p,
+// in element order.  Neighbouring elements of one row form the packed pairs
+// (x, y) and (z, w), so a float4 splits into pairs without register moves;
+// each half rounds as the scalar operation would.  wp_out, if given, gets
+// the p weights alone (ky_weight_p of the same e_p).
 __device__ __forceinline__ void weights_of4(float inv_t, bool residual, const FinalScale& s,
                                             float4 zp, float4 zq, unsigned long long (&w)[4],
                                             unsigned long long* wp_out = nullptr) {
-  const float p4[4] = {zp.x, zp.y, zp.z, zp.w};
-  const float q4[4] = {zq.x, zq.y, zq.z, zq.w};
+  const f2_t it = f2_pack(inv_t, inv_t);
+  const f2_t mp2 = f2_pack(s.mp, s.mp), gp2 = f2_pack(s.gp62, s.gp62);
+  f2_t p01 = f2_pack(zp.x, zp.y), p23 = f2_pack(zp.z, zp.w);
+  if (inv_t != 1.0f) {
+    p01 = f2_mul(p01, it);
+    p23 = f2_mul(p23, it);
+  }
+  p01 = f2_mul(exp_pair(f2_sub(p01, mp2)), gp2);
+  p23 = f2_mul(exp_pair(f2_sub(p23, mp2)), gp2);
+  float wp[4];
+  f2_unpack(p01, wp[0], wp[1]);
+  f2_unpack(p23, wp[2], wp[3]);
   if (residual) {
-    const f2_t mm = f2_pack(s.mp, s.mq);
-    const f2_t gg = f2_pack(s.gp62, s.gq62);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      f2_t z = f2_pack(p4[j], q4[j]);
-      if (inv_t != 1.0f) z = f2_mul(z, f2_pack(inv_t, inv_t));
-      float wp, wq;
-      f2_unpack(f2_mul(exp_pair(f2_sub(z, mm)), gg), wp, wq);
-      const float d = __fsub_rn(wp, wq);
-      w[j] = d > 0.0f ? __float2ull_rz(d) : 0ull;
-      if (wp_out) wp_out[j] = __float2ull_rz(wp);  // ky_weight_p of the same e_p
+    const f2_t mq2 = f2_pack(s.mq, s.mq), gq2 = f2_pack(s.gq62, s.gq62);
+    f2_t q01 = f2_pack(zq.x, zq.y), q23 = f2_pack(zq.z, zq.w);
+    if (inv_t != 1.0f) {
+      q01 = f2_mul(q01, it);
+      q23 = f2_mul(q23, it);
     }
+    q01 = f2_mul(exp_pair(f2_sub(q01, mq2)), gq2);
+    q23 = f2_mul(exp_pair(f2_sub(q23, mq2)), gq2);
+    float d[4];
+    f2_unpack(f2_sub(p01, q01), d[0], d[1]);
+    f2_unpack(f2_sub(p23, q23), d[2], d[3]);
+    // d > 0 ? d : 0 (a NaN difference weighs 0, as in ky_weight_residual)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) w[j] = __float2ull_rz(fmaxf(d[j], 0.0f));
   } else {
-    const f2_t mm = f2_pack(s.mp, s.mp);
-    const f2_t gg = f2_pack(s.gp62, s.gp62);
 #pragma unroll
-    for (int j = 0; j < 4; j += 2) {
-      f2_t z = f2_pack(p4[j], p4[j + 1]);
-      if (inv_t != 1.0f) z = f2_mul(z, f2_pack(inv_t, inv_t));
-      float w0, w1;
-      f2_unpack(f2_mul(exp_pair(f2_sub(z, mm)), gg), w0, w1);
-      w[j] = __float2ull_rz(w0);
-      w[j + 1] = __float2ull_rz(w1);
-      if (wp_out) {
-        wp_out[j] = w[j];
-        wp_out[j + 1] = w[j + 1];
-      }
-    }
+    for (int j = 0; j < 4; ++j) w[j] = __float2ull_rz(wp[j]);
+  }
+  if (wp_out) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) wp_out[j] = residual ? __float2ull_rz(wp[j]) : w[j];
   }
 }
 
@@ -1313,7 +1386,7 @@ __device__ __forceinline__ void final_search(const Args& a, int b, const FinalRo
 // parallelism (TP), sums this rank's residual and p weights for the
 // exchange that precedes the search.
 template <bool VEC, bool TP>
-__global__ void __launch_bounds__(kThreads) accept_final_kernel(Args a) {
+__global__ void __launch_bounds__(kThreads, kFinalMinCtas) accept_final_kernel(Args a) {
   __shared__ int last_cta;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int per_seq = (a.nchunks + kFinalPerCta - 1) / kFinalPerCta;
@@ -2435,6 +2508,14 @@ int accept_impl(kyro_ctx* ctx, const kyro_accept_params* p, const float* target_
   a.status = ctx->d_status;
   // chained: the decide and final kernels wait for tagged records
   a.poll = 1;
+  // dynamic stats units; the counter is zeroed the first time this context
+  // sees the workspace (every call leaves it at zero)
+  a.unit_ctr = ws.unit_ctr;
+  if (workspace != ctx->accept_ws_zeroed) {
+    const cudaError_t err = cudaMemsetAsync(ws.unit_ctr, 0, 8, ctx->stream);
+    if (err != cudaSuccess) return kyro::cuda_error(err, "cudaMemsetAsync(accept unit counter)");
+    ctx->accept_ws_zeroed = workspace;
+  }
   a.gen = ctx->d_pipe_counts;
   a.done = ctx->d_pipe_counts + 1;
   a.salt = ctx->pipe_salt;

@@ -11,11 +11,12 @@ lm_head:
 
   kv_reserve     k + 1 slots per sequence, popped from the device free list
                  (BlockManager::allocate semantics, block_manager.rs:109-125)
-  rope_kv_write  RoPE of the new queries and keys at context_len + j and the
-                 paged store of the new K/V rows (LlamaAttention::forward,
-                 src/model/llama.rs:73-82); or kv_write for rows that are
-                 already rotated
-  verify_attention  the k + 1 query rows against the paged cache
+  verify_attention_rope  RoPE of the new queries and keys at context_len + j,
+                 the paged store of the new K/V rows (LlamaAttention::forward,
+                 src/model/llama.rs:73-82) and the attention of the k + 1
+                 query rows against the paged cache, in one launch; or
+                 kv_write + verify_attention for rows that are already
+                 rotated
   spec_accept    accept lengths and emitted tokens from the target / draft
                  logits (stochastic, greedy, or the reference's greedy rule)
   kv_commit      keep accept_len + 1 slots, release the rest (one call with
@@ -40,7 +41,20 @@ import torch
 
 from . import _lib
 from .verify import (ACCEPT_STOCHASTIC, Context, attn_params, kv_reserve, kv_write,
-                     rope_kv_write, spec_accept_commit, verify_attention)
+                     rope_kv_write, spec_accept_commit, verify_attention, verify_attention_rope)
+
+
+def tree_kernel_shape(num_heads: int, num_kv_heads: int, head_dim: int, block_size: int,
+                      num_query: int) -> bool:
+    """Whether kyro_verify_attention runs this shape on the tcgen05 tree kernel
+    (128 query rows per KV head: head_dim 128, block 16, Hq/Hkv dividing 128
+    and num_query a multiple of 128 / (Hq/Hkv), at most 64), which the fused
+    RoPE entry point does not cover."""
+    group = num_heads // num_kv_heads
+    if head_dim != 128 or block_size != 16 or group > 128 or 128 % group:
+        return False
+    npt = 128 // group
+    return npt <= num_query <= 64 and num_query % npt == 0
 
 
 @dataclass
@@ -74,7 +88,12 @@ class VerifyStep:
         nq = k + 1
         d = kv.k_cache.shape[3]
         self.attn_out = torch.empty(batch, nq, num_heads, d, dtype=torch.bfloat16, device=dev)
-        self.q_rot = torch.empty_like(self.attn_out)
+        # RoPE runs inside the attention launch unless the shape takes the
+        # tree kernel (then rope_kv_write writes the rotated queries here)
+        self.fused_rope = rope_theta is not None and not tree_kernel_shape(
+            num_heads, kv.k_cache.shape[1], d, block_size, nq)
+        self.q_rot = (torch.empty_like(self.attn_out)
+                      if rope_theta is not None and not self.fused_rope else None)
         self.ok = torch.empty(batch, dtype=torch.int32, device=dev)
         self.acc = torch.empty(batch, dtype=torch.int32, device=dev)
         self.toks = torch.empty(batch, nq, dtype=torch.int32, device=dev)
@@ -111,17 +130,24 @@ class VerifyStep:
         if reserve:
             kv_reserve(ctx, nq, kv.block_table, kv.context_lens, kv.free_stack, kv.free_top,
                        kv.ref_counts, bs, out_ok=self.ok)
-        if self.rope_theta is not None:
-            rope_kv_write(ctx, q, k_new, v_new, kv.block_table, kv.context_lens, kv.k_cache,
-                          kv.v_cache, bs, theta=self.rope_theta, q_out=self.q_rot)
-            qq = self.q_rot
+        e0 = None
+        if self.fused_rope:
+            e0 = mark() if events is not None else None
+            verify_attention_rope(ctx, q, k_new, v_new, kv.k_cache, kv.v_cache, kv.block_table,
+                                  kv.context_lens, theta=self.rope_theta, out=self.attn_out,
+                                  workspace=self.ws_attn)
         else:
-            kv_write(ctx, k_new, v_new, kv.block_table, kv.context_lens, kv.k_cache, kv.v_cache,
-                     bs)
-            qq = q
-        e0 = mark() if events is not None else None
-        verify_attention(ctx, qq, kv.k_cache, kv.v_cache, kv.block_table, kv.context_lens,
-                         out=self.attn_out, workspace=self.ws_attn)
+            if self.rope_theta is not None:
+                rope_kv_write(ctx, q, k_new, v_new, kv.block_table, kv.context_lens, kv.k_cache,
+                              kv.v_cache, bs, theta=self.rope_theta, q_out=self.q_rot)
+                qq = self.q_rot
+            else:
+                kv_write(ctx, k_new, v_new, kv.block_table, kv.context_lens, kv.k_cache,
+                         kv.v_cache, bs)
+                qq = q
+            e0 = mark() if events is not None else None
+            verify_attention(ctx, qq, kv.k_cache, kv.v_cache, kv.block_table, kv.context_lens,
+                             out=self.attn_out, workspace=self.ws_attn)
         e1 = mark() if events is not None else None
         spec_accept_commit(ctx, target_logits, draft_logits, draft_tokens, kv.block_table,
                            kv.context_lens, kv.free_stack, kv.free_top, kv.ref_counts, bs,
@@ -136,8 +162,10 @@ class VerifyStep:
         return self.attn_out, self.ok, self.acc, self.toks, self.num
 
     def launches(self, reserve: bool = True) -> int:
-        """Kernels one call launches: reserve (if asked), rope/kv write,
-        attention, the acceptance's stats and decide kernels, the commit, and
-        the final kernel (stochastic mode only)."""
+        """Kernels one call launches: reserve (if asked), the kv write (unless
+        RoPE is fused into the attention), attention, the acceptance's stats
+        and decide kernels, the commit, and the final kernel (stochastic mode
+        only)."""
         from .verify import ACCEPT_STOCHASTIC as S
-        return int(reserve) + 5 + int(self.mode == S and self.temperature > 0)
+        return (int(reserve) + int(not self.fused_rope) + 4
+                + int(self.mode == S and self.temperature > 0))

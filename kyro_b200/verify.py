@@ -351,6 +351,56 @@ def verify_attention(ctx: Context, q: torch.Tensor, k_cache: torch.Tensor, v_cac
     return out
 
 
+def verify_attention_rope(ctx: Context, q: torch.Tensor, k_new: torch.Tensor,
+                          v_new: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                          block_table: torch.Tensor, context_lens: torch.Tensor,
+                          theta: float = 10000.0, pos_offsets: Optional[torch.Tensor] = None,
+                          tree_mask: Optional[torch.Tensor] = None, scale: Optional[float] = None,
+                          kv_split_blocks: int = 0, out: Optional[torch.Tensor] = None,
+                          workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """kyro_verify_attention_rope: the rotary embedding of q and k_new (bf16
+    [B, nq, Hq or Hkv, D], unrotated), the store of the rotated keys and of
+    v_new into the paged slots context_lens[b] + j, and the verify attention,
+    in one launch.  Same result as rope_kv_write then verify_attention."""
+    dev = ctx.device
+    _need(q, "q", torch.bfloat16, dev, 4)
+    _need(k_new, "k_new", torch.bfloat16, dev, 4)
+    _need(v_new, "v_new", torch.bfloat16, dev, 4)
+    _need(k_cache, "k_cache", torch.bfloat16, dev, 4)
+    _need(v_cache, "v_cache", torch.bfloat16, dev, 4)
+    if k_cache.shape != v_cache.shape:
+        raise ValueError("k_cache and v_cache shapes differ")
+    _need(block_table, "block_table", torch.int64, dev, 2)
+    _need(context_lens, "context_lens", torch.int64, dev, 1)
+    B, n, hq, d = q.shape
+    hkv = k_cache.shape[1]
+    if (tuple(k_new.shape) != (B, n, hkv, d) or tuple(v_new.shape) != (B, n, hkv, d)
+            or k_cache.shape[3] != d):
+        raise ValueError("q / k_new / v_new / cache shapes disagree")
+    if block_table.shape[0] != B or context_lens.shape[0] != B:
+        raise ValueError("block_table / context_lens batch mismatch")
+    if pos_offsets is not None:
+        _need(pos_offsets, "pos_offsets", torch.int32, dev, 1)
+        if pos_offsets.numel() != n:
+            raise ValueError("pos_offsets needs one entry per new token")
+    if tree_mask is not None:
+        if tree_mask.dtype not in (torch.int64, torch.uint64):
+            raise TypeError("tree_mask must be int64 or uint64")
+        _need(tree_mask, "tree_mask", tree_mask.dtype, dev, 2)
+    p = attn_params(q, k_cache, block_table, scale, kv_split_blocks)
+    if out is None:
+        out = torch.empty_like(q)
+    L = _lib.load()
+    need = L.kyro_verify_attention_workspace_size(C.byref(p))
+    ws = workspace if workspace is not None else ctx.workspace(need)
+    ctx.bind_stream()
+    check(L.kyro_verify_attention_rope(
+        ctx.handle, C.byref(p), float(theta), _ptr(pos_offsets), _ptr(q), _ptr(k_new),
+        _ptr(v_new), _ptr(k_cache), _ptr(v_cache), _ptr(block_table), _ptr(context_lens),
+        _ptr(tree_mask), _ptr(out), _ptr(ws), ws.numel()))
+    return out
+
+
 def _kv_params(block_table: torch.Tensor, block_size: int, num_blocks: int) -> KVParams:
     return KVParams(block_table.shape[0], block_size, block_table.shape[1], num_blocks)
 

@@ -136,21 +136,24 @@ def bf16_bits(t: torch.Tensor) -> np.ndarray:
     return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
 
 
-def chain_bytes_per_step(context_lens: np.ndarray, cfg: ChainConfig, rope: bool = False) -> dict:
+def chain_bytes_per_step(context_lens: np.ndarray, cfg: ChainConfig,
+                         separate_rope: bool = False) -> dict:
     """Algorithmic bytes of one verify step, per unit:
       attention: every K and V element of the context plus the k+1 new
                  positions, once per KV head (2 * Hkv * D * 2 bytes per
                  token), plus Q read and O written (bf16);
       accept:    every target (k+1 rows) and draft (k rows) logit once (fp32);
       new_rows:  the store of the k+1 new K/V rows: read and written once
-                 (4 * Hkv * D * 2 bytes per new token), and with RoPE also
-                 the queries read and written once rotated (2 * Hq * D * 2)."""
+                 (4 * Hkv * D * 2 bytes per new token); with a separate RoPE
+                 pass (separate_rope) also the rotated queries written and
+                 read back (2 * Hq * D * 2).  RoPE inside the attention
+                 launch reads the queries once, as part of attention."""
     toks = int(np.sum(context_lens + cfg.num_query))
     kv = toks * 2 * cfg.num_kv_heads * cfg.head_dim * 2
     qo = 2 * cfg.batch * cfg.num_query * cfg.num_heads * cfg.head_dim * 2
     logits = cfg.batch * (2 * cfg.k + 1) * cfg.vocab * 4
     new = cfg.batch * cfg.num_query * 4 * cfg.num_kv_heads * cfg.head_dim * 2
-    if rope:
+    if separate_rope:
         new += cfg.batch * cfg.num_query * 2 * cfg.num_heads * cfg.head_dim * 2
     return {"attention": kv + qo, "accept": logits, "new_rows": new,
             "total": kv + qo + logits + new}

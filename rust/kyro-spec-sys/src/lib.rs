@@ -152,6 +152,12 @@ extern "C" {
         v_cache: *const c_void, block_table: *const i64, context_lens: *const i64,
         tree_mask: *const u64, out: *mut c_void, workspace: *mut c_void, workspace_bytes: usize,
     ) -> c_int;
+    pub fn kyro_verify_attention_rope(
+        ctx: *mut kyro_ctx, p: *const kyro_attn_params, rope_theta: f32, pos_offsets: *const i32,
+        q: *const c_void, k_new: *const c_void, v_new: *const c_void, k_cache: *mut c_void,
+        v_cache: *mut c_void, block_table: *const i64, context_lens: *const i64,
+        tree_mask: *const u64, out: *mut c_void, workspace: *mut c_void, workspace_bytes: usize,
+    ) -> c_int;
 
     // ------------------------------------------------------------ K3: KV commit / rollback
     pub fn kyro_kv_reserve(

@@ -112,3 +112,52 @@ def test_bad_block_id_is_flagged(ctx):
     ctx.device_status(clear=True)
     verify_attention(ctx, st.q, st.k_cache, st.v_cache, st.block_table, st.context_lens)
     assert ctx.device_status() & DEV_BAD_BLOCK
+
+
+@pytest.mark.parametrize("hq,hkv,d,nq,lens,split,tree", [
+    (32, 8, 128, 6, [0, 1, 15, 16, 17, 600, 2100], 0, False),       # config-1 layer shape
+    (32, 8, 128, 6, [11, 12, 13, 58, 59, 60, 61, 250], 4, False),   # new slots across block
+                                                                     # and split edges
+    (64, 8, 128, 8, [40, 700], 0, False),    # two row groups store the same slots
+    (32, 8, 64, 5, [10, 47, 500], 3, False),  # head_dim 64
+    (16, 4, 128, 6, [30, 333], 0, True),      # tree depths as positions, tree mask
+])
+def test_fused_rope_attention_matches_separate_launches(ctx, hq, hkv, d, nq, lens, split, tree):
+    """kyro_verify_attention_rope against kyro_rope_kv_write followed by
+    kyro_verify_attention on a copy of the same state: the output and both
+    caches bit for bit."""
+    from kyro_b200.verify import rope_kv_write, verify_attention, verify_attention_rope
+    cfg, st, mask = _setup(ctx, hq, hkv, d, nq, lens, seed=hq + 7 * nq + split, tree=tree)
+    g = torch.Generator(device=ctx.device).manual_seed(nq + d)
+    shape = (len(lens), nq, hkv, d)
+    k_new = torch.randn(shape, generator=g, device=ctx.device, dtype=torch.bfloat16)
+    v_new = torch.randn(shape, generator=g, device=ctx.device, dtype=torch.bfloat16)
+    pos = None
+    if tree:
+        depth = [bin(int(m)).count("1") - 1 for m in mask[0].cpu().numpy().view(np.uint64)]
+        pos = torch.tensor(depth, dtype=torch.int32, device=ctx.device)
+    theta = 500000.0
+    kc, vc = st.k_cache.clone(), st.v_cache.clone()
+    q_rot = rope_kv_write(ctx, st.q, k_new, v_new, st.block_table, st.context_lens, kc, vc,
+                          cfg.block_size, theta=theta, pos_offsets=pos)
+    ref = verify_attention(ctx, q_rot, kc, vc, st.block_table, st.context_lens, tree_mask=mask,
+                           kv_split_blocks=split)
+    out = verify_attention_rope(ctx, st.q, k_new, v_new, st.k_cache, st.v_cache, st.block_table,
+                                st.context_lens, theta=theta, pos_offsets=pos, tree_mask=mask,
+                                kv_split_blocks=split)
+    torch.cuda.synchronize()
+    assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
+    assert torch.equal(st.k_cache.view(torch.int16), kc.view(torch.int16))
+    assert torch.equal(st.v_cache.view(torch.int16), vc.view(torch.int16))
+    assert ctx.device_status() == 0
+
+
+def test_fused_rope_rejects_tree_kernel_shapes(ctx):
+    """Shapes that take the tcgen05 tree kernel are refused, not run."""
+    from kyro_b200.verify import verify_attention_rope
+    from kyro_b200._lib import KyroError
+    cfg, st, mask = _setup(ctx, 32, 8, 128, 32, [100], seed=3, tree=True)
+    k_new = torch.zeros(1, 32, 8, 128, device=ctx.device, dtype=torch.bfloat16)
+    with pytest.raises(KyroError):
+        verify_attention_rope(ctx, st.q, k_new, k_new, st.k_cache, st.v_cache, st.block_table,
+                              st.context_lens, tree_mask=mask)
