@@ -752,7 +752,7 @@ __device__ __forceinline__ void reduce_slice(const Args& a, Slice& s, uint32_t t
 }
 
 // Units a warp takes from the counter at a time (dynamic distribution).
-constexpr uint32_t kGrab = 4;
+constexpr uint32_t kGrab = 8;
 
 __device__ __forceinline__ uint32_t take_units(uint32_t* ctr) {
   uint32_t v = 0;
@@ -766,12 +766,15 @@ __device__ __forceinline__ uint32_t take_units(uint32_t* ctr) {
 // warps in the grid), so neighbouring warps read neighbouring chunks.
 //
 // Dynamic (unit_ctr set): warps take batches of kGrab consecutive units
-// from a counter, one batch ahead, so a warp on an SM that streams faster
-// takes more of them.  Measured on config 1, a static split left half of
-// the warps idle for the last quarter of the pass (warp end times 48 to
-// 71 us, median 54).  Every warp retires once it has seen the counter past
-// the last unit; the last one to retire sets the counter back to zero for
-// the next call on this workspace.
+// from one counter, one batch ahead, so a warp on an SM that streams faster
+// takes more of them and the whole grid still reads the rows in order.
+// Measured on config 1 (acceptance alone): static 100.5 us; one counter
+// with batches of 2 / 4 / 8 / 12 / 16 / 32 units 132 / 100.4 / 99.2 / 102.0
+// / 101.9 / 149 us (short batches queue on the counter, long ones leave
+// warps idle at the end); 16 ranges with a counter each, 107-116 us (the
+// grid then reads 16 places at once).  Every warp retires once it has seen
+// the counter past the last unit; the last one to retire sets the counter
+// back to zero for the next call on this workspace.
 template <bool VEC, bool STOCH>
 __global__ void __launch_bounds__(kThreads, kStatsMinCtas) accept_stats_kernel(Args a) {
   allow_dependents();
