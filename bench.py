@@ -777,7 +777,6 @@ def tp_measure(world, rank, local, dev, steps, warmup):
     kvsnap = KvStateSnapshot(st)
     nq = k + 1
     ok = torch.empty(B, dtype=torch.int32, device=dev)
-    stream = torch.cuda.current_stream(dev)
     peak, _ = load_peaks()
     rank_bytes = (2 * k + 1) * B * Vs * 4
     for tr in transports:
@@ -807,37 +806,56 @@ def tp_measure(world, rank, local, dev, steps, warmup):
         ev = []
 
         def step(i, timed):
+            s = torch.cuda.current_stream(dev)
             kvsnap.restore()
             kv_reserve(ctx, nq, st.block_table, st.context_lens, st.free_stack, st.free_top,
                        st.ref_counts, cfg.block_size, out_ok=ok)
             if timed:
                 e0 = torch.cuda.Event(enable_timing=True)
-                e0.record(stream)
+                e0.record(s)
             acc, _, _, _ = spec_accept_tp(ctx, tgt, drf, drafts, V, temperature=T, seed=0, step=i)
             if timed:
                 e1 = torch.cuda.Event(enable_timing=True)
-                e1.record(stream)
+                e1.record(s)
                 ev.append((e0, e1))
             kv_commit(ctx, nq, acc, st.block_table, st.context_lens, st.free_stack, st.free_top,
                       st.ref_counts, cfg.block_size)
             return acc
 
-        ctx.bind_stream()
-        for i in range(warmup):
-            step(i, False)
+        # the timed steps replay one captured step (every rank captures the
+        # same sequence of kernels and collectives), so that host launch time
+        # does not set the pace; the per-call events come from plain steps
+        side = torch.cuda.Stream(dev)
+        graph = None
+        with torch.cuda.stream(side):
+            ctx.bind_stream()
+            for i in range(warmup):
+                step(i, False)
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=side):
+                step(warmup, False)
+            for _ in range(3):
+                graph.replay()
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        t0.record(stream)
-        for i in range(warmup, warmup + steps):
-            acc = step(i, False)
-        t1.record(stream)
+        with torch.cuda.stream(side):
+            t0.record(side)
+            for i in range(steps):
+                graph.replay()
+            t1.record(side)
         torch.cuda.synchronize()
         ms = t0.elapsed_time(t1)
-        for i in range(PER_KERNEL_STEPS):
-            step(warmup + steps + i, True)
+        with torch.cuda.stream(side):
+            for i in range(PER_KERNEL_STEPS):
+                step(warmup + steps + i, True)
         torch.cuda.synchronize()
+        del graph  # before the context (and its NCCL communicator) goes
+        ctx.bind_stream()
         acc_ms = float(np.mean([a.elapsed_time(b) for a, b in ev]))
         ms, acc_ms = max_over_ranks([ms, acc_ms], world, dev)
         status = ctx.device_status()
@@ -845,6 +863,7 @@ def tp_measure(world, rank, local, dev, steps, warmup):
         if world > 1:
             dist.barrier()
         res[tr] = {"transport": got, "parity_ok": parity_ok, "ms_per_step": ms / steps,
+                   "timing": "CUDA graph replays of the step (restore, reserve, accept, commit)",
                    "accept_ms": acc_ms, "positions_per_s": B * nq * steps / (ms * 1e-3),
                    "per_rank_GBps": rank_bytes / (acc_ms * 1e-3) / 1e9,
                    "frac_hbm_per_rank": rank_bytes / (acc_ms * 1e-3) / 1e9 / peak,

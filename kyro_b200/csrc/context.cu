@@ -132,7 +132,8 @@ int kyro_ctx_create(int device, void* stream, kyro_ctx** out) {
   ctx->tp_world = 1;
   ctx->attn_epoch = 0;
   ctx->attn_ws_zeroed = nullptr;
-  ctx->accept_ws_zeroed = nullptr;
+  for (int i = 0; i < KYRO_ZEROED_WS; ++i) ctx->stats_ws_zeroed[i] = nullptr;
+  ctx->stats_ws_next = 0;
   {
     // a salt per context: tags of different contexts differ
     static std::atomic<uint32_t> contexts{0};

@@ -21,6 +21,7 @@
 
 #define KYRO_MAX_TP_WORLD 8
 // counts of the acceptance pipeline kept in each context (sampler.cu)
+#define KYRO_ZEROED_WS 8
 #define KYRO_PIPE_COUNTS 128
 
 struct kyro_ctx {
@@ -35,7 +36,10 @@ struct kyro_ctx {
   // workspace whose tickets this context has zeroed
   uint32_t attn_epoch;
   const void* attn_ws_zeroed;
-  const void* accept_ws_zeroed;  // workspace whose stats unit counter this context zeroed
+  // workspaces whose stats unit counter this context has zeroed (the last
+  // KYRO_ZEROED_WS seen)
+  const void* stats_ws_zeroed[KYRO_ZEROED_WS];
+  int stats_ws_next;
   // the acceptance pipeline's generation count and finished-sequence
   // count (device words owned by the context; sampler.cu), and the salt
   // of its record tags

@@ -109,6 +109,9 @@ peer_exchange_kernel(Peers peers, int rank, int world, const uint8_t* __restrict
   uint8_t* own = peers.p[rank];
   unsigned long long* ctr = reinterpret_cast<unsigned long long*>(own + kSeqOffset);
   kyro::dev::pdl_wait();
+  // the consumer of recv may begin launching now: it waits for this grid to
+  // complete before it reads
+  kyro::dev::pdl_trigger();
   // every CTA reads the round number before CTA 0 advances it
   const unsigned long long seq = *reinterpret_cast<volatile unsigned long long*>(ctr) + 1ull;
   cluster_sync_all();
@@ -153,7 +156,6 @@ peer_exchange_kernel(Peers peers, int rank, int world, const uint8_t* __restrict
       reinterpret_cast<int32_t*>(recv)[i] = m;
     }
   }
-  kyro::dev::pdl_trigger();
 }
 
 bool forced_nccl() {

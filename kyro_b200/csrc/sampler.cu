@@ -171,8 +171,8 @@ struct Args {
   unsigned long long* W;        // [B][nchunks] weight sums of the chosen rows
   uint32_t* cnt_c;              // [B] finished weight sums per sequence
   uint32_t units;               // stats units: B * R * nchunks
-  // Dynamic stats units (non-null): [0] the next unit to take, [1] retired
-  // warps; both back at zero when the stats kernel ends
+  // The stats units' counter: [0] the next unit to take, [1] retired warps;
+  // both back at zero when the stats kernel ends
   uint32_t* unit_ctr;
   uint32_t* status;
   // tensor parallelism (vocabulary shards): V above is this shard's width
@@ -760,80 +760,60 @@ __device__ __forceinline__ uint32_t take_units(uint32_t* ctr) {
   return __shfl_sync(0xffffffffu, v, 0);
 }
 
-// Persistent; each warp loads unit i+1 before it reduces unit i.
-//
-// Static (unit_ctr null): warp w takes units w, w + W, w + 2W, ... (W =
-// warps in the grid), so neighbouring warps read neighbouring chunks.
-//
-// Dynamic (unit_ctr set): warps take batches of kGrab consecutive units
-// from one counter, one batch ahead, so a warp on an SM that streams faster
-// takes more of them and the whole grid still reads the rows in order.
-// Measured on config 1 (acceptance alone): static 100.5 us; one counter
-// with batches of 2 / 4 / 8 / 12 / 16 / 32 units 132 / 100.4 / 99.2 / 102.0
-// / 101.9 / 149 us (short batches queue on the counter, long ones leave
-// warps idle at the end); 16 ranges with a counter each, 107-116 us (the
-// grid then reads 16 places at once).  Every warp retires once it has seen
-// the counter past the last unit; the last one to retire sets the counter
-// back to zero for the next call on this workspace.
+// Persistent; each warp loads unit i+1 before it reduces unit i.  Warps
+// take batches of kGrab consecutive units from one counter (a.unit_ctr, at
+// the start of the workspace), one batch ahead, so a warp on an SM that
+// streams faster takes more of them and the whole grid still reads the rows
+// in order.  Measured on config 1 (acceptance alone): a static split (warp
+// w takes units w, w + W, ...) 100.5 us, with warp end times from 48 to
+// 71 us; one counter with batches of 2 / 4 / 8 / 12 / 16 / 32 units 132 /
+// 100.4 / 99.2 / 102.0 / 101.9 / 149 us (short batches queue on the
+// counter, long ones leave warps idle at the end); 16 ranges with a counter
+// each, 107-116 us (the grid then reads 16 places at once).  On config 3
+// over two ranks the static split's warps ended between 149 and 226 us.
+// Every warp retires once it has seen the counter past the last unit; the
+// last one to retire sets the counter back to zero for the next call on
+// this workspace.
 template <bool VEC, bool STOCH>
 __global__ void __launch_bounds__(kThreads, kStatsMinCtas) accept_stats_kernel(Args a) {
   allow_dependents();
   const uint32_t tag = call_tag(a);
   Slice s0, s1;
-  if (a.unit_ctr) {
-    uint32_t u = take_units(a.unit_ctr);
-    uint32_t nxt = take_units(a.unit_ctr);
-    if (u < a.units) {
-      uint32_t end = min(u + kGrab, a.units);
-      // the unit after u, or a value >= units when the warp is done
-      auto advance = [&](uint32_t cur) -> uint32_t {
-        if (cur + 1 < end) return cur + 1;
-        const uint32_t n = nxt;
-        if (n < a.units) {
-          end = min(n + kGrab, a.units);
-          nxt = take_units(a.unit_ctr);
-        }
-        return n;
-      };
-      load_slice<VEC>(a, u, s0);
-      while (true) {
-        uint32_t un = advance(u);
-        if (un < a.units) load_slice<VEC>(a, un, s1);
-        reduce_slice<STOCH>(a, s0, tag);
-        if (un >= a.units) break;
-        u = un;
-        un = advance(u);
-        if (un < a.units) load_slice<VEC>(a, un, s0);
-        reduce_slice<STOCH>(a, s1, tag);
-        if (un >= a.units) break;
-        u = un;
+  uint32_t u = take_units(a.unit_ctr);
+  uint32_t nxt = take_units(a.unit_ctr);
+  if (u < a.units) {
+    uint32_t end = min(u + kGrab, a.units);
+    // the unit after u, or a value >= units when the warp is done
+    auto advance = [&](uint32_t cur) -> uint32_t {
+      if (cur + 1 < end) return cur + 1;
+      const uint32_t n = nxt;
+      if (n < a.units) {
+        end = min(n + kGrab, a.units);
+        nxt = take_units(a.unit_ctr);
       }
+      return n;
+    };
+    load_slice<VEC>(a, u, s0);
+    while (true) {
+      uint32_t un = advance(u);
+      if (un < a.units) load_slice<VEC>(a, un, s1);
+      reduce_slice<STOCH>(a, s0, tag);
+      if (un >= a.units) break;
+      u = un;
+      un = advance(u);
+      if (un < a.units) load_slice<VEC>(a, un, s0);
+      reduce_slice<STOCH>(a, s1, tag);
+      if (un >= a.units) break;
+      u = un;
     }
-    // every take of this warp has returned: retire; the last warp resets
-    if ((threadIdx.x & 31) == 0) {
-      __threadfence();
-      if (atomicAdd(a.unit_ctr + 1, 1u) == gridDim.x * (uint32_t)kWarps - 1u) {
-        a.unit_ctr[0] = 0u;
-        a.unit_ctr[1] = 0u;
-      }
-    }
-    return;
   }
-  const uint32_t stride = gridDim.x * kWarps;
-  uint32_t u = blockIdx.x * kWarps + (threadIdx.x >> 5);
-  if (u >= a.units) return;
-  load_slice<VEC>(a, u, s0);
-  while (true) {
-    uint32_t un = u + stride;
-    if (un < a.units) load_slice<VEC>(a, un, s1);
-    reduce_slice<STOCH>(a, s0, tag);
-    if (un >= a.units) break;
-    u = un;
-    un = u + stride;
-    if (un < a.units) load_slice<VEC>(a, un, s0);
-    reduce_slice<STOCH>(a, s1, tag);
-    if (un >= a.units) break;
-    u = un;
+  // every take of this warp has returned: retire; the last warp resets
+  if ((threadIdx.x & 31) == 0) {
+    __threadfence();
+    if (atomicAdd(a.unit_ctr + 1, 1u) == gridDim.x * (uint32_t)kWarps - 1u) {
+      a.unit_ctr[0] = 0u;
+      a.unit_ctr[1] = 0u;
+    }
   }
 }
 
@@ -2337,6 +2317,20 @@ bool launch_tree_cluster(int B, const Args& a, cudaStream_t stream, int* rc) {
   return true;
 }
 
+// Every stats launch distributes its units dynamically, through the counter
+// at the start of the workspace.  Each call leaves it at zero; a context
+// zeroes it the first time it sees a workspace (it remembers the last few).
+int use_unit_counter(kyro_ctx* ctx, Args& a, const Workspace& ws, const void* base) {
+  a.unit_ctr = ws.unit_ctr;
+  for (int i = 0; i < KYRO_ZEROED_WS; ++i)
+    if (ctx->stats_ws_zeroed[i] == base) return KYRO_OK;
+  const cudaError_t err = cudaMemsetAsync(ws.unit_ctr, 0, 8, ctx->stream);
+  if (err != cudaSuccess) return kyro::cuda_error(err, "cudaMemsetAsync(stats unit counter)");
+  ctx->stats_ws_zeroed[ctx->stats_ws_next] = base;
+  ctx->stats_ws_next = (ctx->stats_ws_next + 1) % KYRO_ZEROED_WS;
+  return KYRO_OK;
+}
+
 // The KV commit (and next reserve) that kyro_spec_accept_commit runs inside
 // the acceptance, right after the decide kernel.
 struct CommitSpec {
@@ -2511,14 +2505,7 @@ int accept_impl(kyro_ctx* ctx, const kyro_accept_params* p, const float* target_
   a.status = ctx->d_status;
   // chained: the decide and final kernels wait for tagged records
   a.poll = 1;
-  // dynamic stats units; the counter is zeroed the first time this context
-  // sees the workspace (every call leaves it at zero)
-  a.unit_ctr = ws.unit_ctr;
-  if (workspace != ctx->accept_ws_zeroed) {
-    const cudaError_t err = cudaMemsetAsync(ws.unit_ctr, 0, 8, ctx->stream);
-    if (err != cudaSuccess) return kyro::cuda_error(err, "cudaMemsetAsync(accept unit counter)");
-    ctx->accept_ws_zeroed = workspace;
-  }
+  KY_TRY(use_unit_counter(ctx, a, ws, workspace));
   a.gen = ctx->d_pipe_counts;
   a.done = ctx->d_pipe_counts + 1;
   a.salt = ctx->pipe_salt;
@@ -2611,6 +2598,7 @@ int kyro_sample_tokens(kyro_ctx* ctx, const kyro_sample_params* p, const float* 
   a.out_tokens = out_tokens;
   a.out_probs = out_probs;
   a.status = ctx->d_status;
+  KY_TRY(use_unit_counter(ctx, a, ws, workspace));
   return launch(ctx, a, ws, use_vec(logits, nullptr, V));
 }
 
@@ -2705,6 +2693,7 @@ int kyro_spec_accept_tp(kyro_ctx* ctx, const kyro_accept_params* p, const float*
   a.send4 = ws.send4;
   a.recv4 = ws.recv4;
   a.W2 = ws.W2;
+  KY_TRY(use_unit_counter(ctx, a, ws.base, workspace));
   const bool vec = use_vec(target_shard, a.qlog, Vl);
   int st;
   if (vec && stoch) st = launch_tp<true, true>(ctx, a);
@@ -2775,6 +2764,7 @@ int kyro_spec_accept_tree(kyro_ctx* ctx, const kyro_tree_params* p, const float*
   a.out_tokens = out_tokens;
   a.out_num_tokens = out_num_tokens;
   a.status = ctx->d_status;
+  KY_TRY(use_unit_counter(ctx, a, ws, workspace));
   const bool vec = use_vec(target_logits, a.qlog, V);
   const long long units = (long long)a.units;
   if (vec && stoch) {
