@@ -70,7 +70,7 @@ int kyro_version(void) { return KYRO_VERSION; }
 
 const char* kyro_kernel_names(void) {
   return "accept_stats_kernel;accept_decide_kernel;accept_final_kernel;accept_tree_kernel;"
-         "accept_tree_cluster_kernel;accept_tp_max_kernel;accept_tp_sum_kernel;"
+         "accept_tree_cluster_kernel;accept_tp_max_kernel;accept_tp_part_kernel;"
          "accept_tp_decide_kernel;accept_tp_search_kernel;accept_tp_write_kernel;"
          "verify_attention_kernel;kv_reserve_kernel;kv_commit_kernel;kv_commit_reserve_kernel;"
          "kv_tree_move_kernel;kv_write_kernel;rope_kv_write_kernel;kv_block_copy_kernel;"

@@ -242,16 +242,21 @@ KY_HD uint64_t ky_cdf_threshold(uint32_t odd, uint64_t W) {
  *   e_i = ky_exp(s_i - m_c) at each of the chunk's KY_CHUNK positions; a
  *         position past the shard end has s_i = -inf (so e_i = ky_exp(-87))
  *   E_c = ky_chunk_sum(e_c)                   (fp32, the fixed tree below)
- *   M   = max_c m_c
- *   mass_c = E_c * ky_exp(m_c - M)            (double)
+ *   M_r = max of m_c over the chunks of shard r
+ *   M   = max_r M_r
+ *   mass_c = E_c * ky_exp(m_c - M_r)          (double; c in shard r)
  *   S_r = butterfly sum of the chunk masses of shard r:
  *           t[l] = sum of mass_c over c = l, l+32, l+64, ... (in that order,
  *                  starting from 0.0), l = 0..31;
  *           for off = 16, 8, 4, 2, 1: t[l] = t[l] + t[l ^ off];  S_r = t[0]
  *         (the xor-shuffle reduction of a 32-lane warp, every lane ends
  *          with the same value)
- *   S   = sum of S_r over shards in rank order, starting from 0.0
+ *   S   = sum of S_r * ky_shard_scale(M_r, M) over shards in rank order,
+ *         starting from 0.0 (double)
  *   g_c = (float)(ky_exp(m_c - M) / S)        (double division)
+ * Each shard's part is taken under its own maximum, so a rank sends its
+ * (M_r, S_r) in one exchange round; with one shard, M_0 = M and the scale
+ * is exactly 1, so S = S_0.
  *   p_i = e_i * g_c                           (fp32)
  * The same row statistics drive the accept test, the residual and the
  * bonus sample. */
@@ -295,6 +300,13 @@ KY_HD float ky_inv_temperature(float t) { return (float)KY_DDIV(1.0, (double)t);
 
 KY_HD double ky_chunk_mass(float E, float m_c, float M) {
   return KY_DMUL((double)E, (double)ky_exp(KY_FSUB(m_c, M)));
+}
+
+/* The factor that brings shard r's normaliser part S_r (taken under its own
+ * maximum M_r) to the row maximum M: exactly 1 when M_r == M (one shard, the
+ * shard holding the maximum, or an all -inf row). */
+KY_HD double ky_shard_scale(float M_r, float M) {
+  return M_r == M ? 1.0 : (double)ky_exp(KY_FSUB(M_r, M));
 }
 
 KY_HD float ky_chunk_scale(float m_c, float M, double S) {

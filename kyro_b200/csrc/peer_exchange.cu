@@ -1,10 +1,10 @@
-// peer_exchange.cu -- the tensor-parallel sampler's four exchange rounds over
+// peer_exchange.cu -- the tensor-parallel sampler's exchange rounds over
 // NVLink peer memory instead of NCCL collectives.
 //
 // DistributedContext (src/distributed.rs:61-98) shards the vocabulary; the
-// sharded acceptance then needs four small exchanges per step (row maxima,
-// normaliser parts, weight totals, the sampled token), each a few KB to a
-// few hundred KB.  At that size an NCCL collective costs its launch and
+// sharded acceptance then needs three small exchanges per step (row maxima
+// with the normaliser parts under them, weight totals, the sampled token),
+// each a few KB to a few hundred KB.  At that size an NCCL collective costs its launch and
 // protocol latency (~20 us a round measured on two B200s).  Here every rank
 // maps every peer's exchange region once (CUDA IPC, at kyro_ctx_tp_init) and
 // one kernel per round stores this rank's payload straight into each peer's

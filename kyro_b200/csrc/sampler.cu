@@ -121,16 +121,18 @@ __device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv& f) {
 }
 
 // Tensor-parallel exchange records (one per row or per sequence and rank).
-struct TpRow1 {  // round 1: this rank's row max, or its argmax as a global id
+struct TpRow1 {  // round 1 (greedy): this rank's row max and argmax as a global id
   float M;
   int32_t arg;
 };
-struct TpRow2 {  // round 2: this rank's part of the normaliser under the
-  double S;      // global max; e and the chunk max at the draft token when
-  float ex;      // this rank holds the token, else 0
+struct TpRow2 {  // round 1 (stochastic): this rank's row max M, its part of
+  double S;      // the normaliser under M, and e and the chunk max at the
+  float ex;      // draft token when this rank holds the token (else 0)
   float mcx;
+  float M;
+  int32_t _pad;
 };
-struct TpSeq3 {  // round 3: this rank's weight totals of the chosen row
+struct TpSeq3 {  // round 2: this rank's weight totals of the chosen row
   unsigned long long w_res, w_p;
 };
 
@@ -1441,15 +1443,18 @@ __global__ void __launch_bounds__(kThreads, kFinalMinCtas) accept_final_kernel(A
 //
 // Vocabulary shards (DistributedContext::shard_dim, src/distributed.rs:90-98):
 // each rank runs the stats kernel on its own columns, then
-//   accept_tp_max_kernel    row maxima (argmax, greedy)         -> all-gather 1
-//   accept_tp_sum_kernel    normaliser parts under the global
-//                           max, owner values at the drafts     -> all-gather 2
+//   accept_tp_part_kernel   row maxima, the normaliser parts under
+//                           them, owner values at the drafts     -> all-gather 1
+//   (greedy: accept_tp_max_kernel, row maxima and argmaxes        -> all-gather 1)
 //   accept_tp_decide_kernel the decision, the same on every rank
-//   accept_final_kernel<TP> this rank's weight totals            -> all-gather 3
-//   accept_tp_search_kernel the owner rank finds the token      -> int32 max 4
+//   accept_final_kernel<TP> this rank's weight totals            -> all-gather 2
+//   accept_tp_search_kernel the owner rank finds the token      -> int32 max 3
 //   accept_tp_write_kernel  every rank writes it
 // Ranks contribute to sums through all-gathers and add the parts in rank
-// order, so every rank computes the contract's rank-ordered sums.
+// order, so every rank computes the contract's rank-ordered sums.  Each
+// rank's normaliser part is taken under its own row maximum and scaled to
+// the row maximum by the receivers (kyro_math.h), which lets the maxima and
+// the parts travel in one round.
 
 // Row max of stats row srow over this rank's chunks (one warp).
 __device__ __forceinline__ float row_max(const Args& a, int64_t srow) {
@@ -1490,14 +1495,24 @@ __device__ __forceinline__ double row_sum_part(const Args& a, int64_t srow, floa
   return warp_butterfly(t);
 }
 
-__device__ __forceinline__ float global_row_max(const Args& a, int64_t srow) {
+// The row's statistics from every rank's round-1 part: M the largest shard
+// maximum, S the parts brought to M and added in rank order (kyro_math.h).
+__device__ __forceinline__ RowStat gathered_row_stat(const Args& a, int64_t srow) {
   const int64_t rows = (int64_t)a.B * a.R;
-  float M = -INFINITY;
-  for (int q = 0; q < a.tp_world; ++q) M = fmaxf(M, a.recv1[q * rows + srow].M);
-  return M;
+  RowStat v;
+  v.arg = 0;
+  v.M = -INFINITY;
+  for (int q = 0; q < a.tp_world; ++q) v.M = fmaxf(v.M, a.recv2[q * rows + srow].M);
+  v.S = 0.0;
+  for (int q = 0; q < a.tp_world; ++q) {
+    const TpRow2 r = a.recv2[q * rows + srow];
+    v.S = KY_DADD(v.S, KY_DMUL(r.S, ky_shard_scale(r.M, v.M)));
+  }
+  return v;
 }
 
 // One CTA per sequence, one warp per row.
+// Greedy: this rank's row maxima and argmaxes (one warp per row).
 __global__ void __launch_bounds__(kDecideWarps * 32) accept_tp_max_kernel(Args a) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   const int b = blockIdx.x;
@@ -1505,32 +1520,29 @@ __global__ void __launch_bounds__(kDecideWarps * 32) accept_tp_max_kernel(Args a
   allow_dependents();
   for (int r = warp; r < a.R; r += nwarps) {
     const int64_t srow = (int64_t)b * a.R + r;
+    const RowStat rs = row_stat(a, srow);
     TpRow1 v;
-    if (a.stoch) {
-      v.M = row_max(a, srow);
-      v.arg = 0;
-    } else {
-      const RowStat rs = row_stat(a, srow);
-      v.M = rs.M;
-      v.arg = (int32_t)(rs.arg + a.vocab_offset);
-    }
+    v.M = rs.M;
+    v.arg = (int32_t)(rs.arg + a.vocab_offset);
     if (lane == 0) a.send1[srow] = v;
   }
 }
 
-// One CTA per sequence, one warp per row (stochastic mode only).
-__global__ void __launch_bounds__(kDecideWarps * 32) accept_tp_sum_kernel(Args a) {
+// Stochastic: this rank's row maxima, the normaliser parts under them, and
+// the owner's values at the draft tokens, for round 1 (one warp per row).
+__global__ void __launch_bounds__(kDecideWarps * 32) accept_tp_part_kernel(Args a) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   const int b = blockIdx.x;
-  grid_dependency_wait();  // round 1 has landed
+  grid_dependency_wait();  // the chunk statistics are complete
   allow_dependents();
   for (int r = warp; r < a.R; r += nwarps) {
     const int64_t srow = (int64_t)b * a.R + r;
-    const float M = global_row_max(a, srow);
     TpRow2 v;
-    v.S = row_sum_part(a, srow, M);
+    v.M = row_max(a, srow);
+    v.S = row_sum_part(a, srow, v.M);
     v.ex = 0.0f;
     v.mcx = 0.0f;
+    v._pad = 0;
     const int xg = draft_token_of_row(a, b, r);
     const int64_t xl = (int64_t)xg - a.vocab_offset;
     if (xg >= 0 && xg < a.V_global && xl >= 0 && xl < a.V) {
@@ -1541,7 +1553,6 @@ __global__ void __launch_bounds__(kDecideWarps * 32) accept_tp_sum_kernel(Args a
   }
 }
 
-// The inputs of accept test j from the rank that holds the draft token.
 __device__ __forceinline__ TestInputs tp_test(const Args& a, int b, int j) {
   TestInputs t;
   t.x = -1;
@@ -1577,8 +1588,7 @@ __global__ void __launch_bounds__(kDecideWarps * 32) accept_tp_decide_kernel(Arg
     v.S = 0.0;
     v.arg = 0;
     if (a.stoch) {
-      v.M = global_row_max(a, srow);
-      for (int q = 0; q < a.tp_world; ++q) v.S = KY_DADD(v.S, a.recv2[q * rows + srow].S);
+      v = gathered_row_stat(a, srow);
     } else {
       // shards are contiguous: the first strict maximum in rank order is the
       // lowest global index among equal maxima
@@ -1606,7 +1616,7 @@ template <bool VEC>
 __global__ void __launch_bounds__(kThreads) accept_tp_search_kernel(Args a) {
   const int lane = threadIdx.x & 31;
   const int b = blockIdx.x * kWarps + (threadIdx.x >> 5);
-  grid_dependency_wait();  // round 3 has landed
+  grid_dependency_wait();  // round 2 has landed
   allow_dependents();
   if (b >= a.B) return;
   const FinalRow fr = a.final_rows[b];
@@ -1644,7 +1654,7 @@ __global__ void __launch_bounds__(kThreads) accept_tp_search_kernel(Args a) {
 
 __global__ void accept_tp_write_kernel(Args a) {
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
-  grid_dependency_wait();  // round 4 has landed
+  grid_dependency_wait();  // round 3 has landed
   allow_dependents();
   if (b >= a.B) return;
   const FinalRow fr = a.final_rows[b];
@@ -2386,15 +2396,16 @@ int launch_tp(kyro_ctx* ctx, const Args& a) {
   accept_stats_kernel<VEC, STOCH><<<grid, kThreads, 0, ctx->stream>>>(a);
   KY_TRY(kyro::check_launch("accept_stats_kernel"));
   const unsigned dthreads = 32u * (unsigned)(a.R < kDecideWarps ? a.R : kDecideWarps);
-  KY_TRY(launch_dependent(accept_tp_max_kernel, (unsigned)a.B, dthreads, ctx->stream, a,
-                          "accept_tp_max_kernel"));
-  KY_TRY(kyro::xchg::all_gather(ctx, a.send1, a.recv1, sizeof(TpRow1) * rows,
-                                "kyro_spec_accept_tp: row maxima"));
   if (STOCH) {
-    KY_TRY(launch_dependent(accept_tp_sum_kernel, (unsigned)a.B, dthreads, ctx->stream, a,
-                            "accept_tp_sum_kernel"));
+    KY_TRY(launch_dependent(accept_tp_part_kernel, (unsigned)a.B, dthreads, ctx->stream, a,
+                            "accept_tp_part_kernel"));
     KY_TRY(kyro::xchg::all_gather(ctx, a.send2, a.recv2, sizeof(TpRow2) * rows,
-                                  "kyro_spec_accept_tp: normaliser parts"));
+                                  "kyro_spec_accept_tp: row maxima and normaliser parts"));
+  } else {
+    KY_TRY(launch_dependent(accept_tp_max_kernel, (unsigned)a.B, dthreads, ctx->stream, a,
+                            "accept_tp_max_kernel"));
+    KY_TRY(kyro::xchg::all_gather(ctx, a.send1, a.recv1, sizeof(TpRow1) * rows,
+                                  "kyro_spec_accept_tp: row maxima"));
   }
   KY_TRY(launch_dependent(accept_tp_decide_kernel, (unsigned)a.B, dthreads, ctx->stream, a,
                           "accept_tp_decide_kernel"));

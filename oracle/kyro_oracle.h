@@ -78,8 +78,10 @@ void ko_spec_accept_tree(int32_t batch, int32_t num_nodes, int32_t vocab, int32_
                          int32_t nthreads);
 
 /* One rank's pieces of a vocabulary-sharded row (its contiguous columns,
- * len entries): the shard's row max; its butterfly part of the normaliser
- * under the global max M; e and the chunk max at one of its entries; its
+ * len entries): the shard's row max M_r; its butterfly part of the
+ * normaliser under a given max M (the protocol passes M_r, and every rank
+ * brings the parts to the row max with ky_shard_scale); e and the chunk max
+ * at one of its entries; its
  * residual (q_shard != NULL) and p weight totals under the global row
  * statistics; and the entry where its weights first reach T. */
 float ko_tp_row_max(const float* shard, int32_t len, float temperature);

@@ -86,9 +86,18 @@ static void rowstat_init(ko_rowstat* st, const float* row, int32_t vocab, int32_
       E[gc] = ky_chunk_sum(e);
     }
   }
+  /* shard maxima M_r, the row max M, and each shard's part under its own
+   * maximum, brought to M in rank order (kyro_math.h) */
+  float* Mr = (float*)malloc(sizeof(float) * (size_t)num_shards);
   float M = -INFINITY;
-  for (int32_t c = 0; c < nc; ++c)
-    if (st->m[c] > M) M = st->m[c];
+  for (int32_t r = 0; r < num_shards; ++r) {
+    Mr[r] = -INFINITY;
+    for (int32_t c = 0; c < st->chunks_per_shard; ++c) {
+      int32_t gc = r * st->chunks_per_shard + c;
+      if (st->m[gc] > Mr[r]) Mr[r] = st->m[gc];
+    }
+    if (Mr[r] > M) M = Mr[r];
+  }
   double S = 0.0;
   for (int32_t r = 0; r < num_shards; ++r) {
     double t[32];
@@ -96,11 +105,12 @@ static void rowstat_init(ko_rowstat* st, const float* row, int32_t vocab, int32_
       t[l] = 0.0;
       for (int32_t c = l; c < st->chunks_per_shard; c += 32) {
         int32_t gc = r * st->chunks_per_shard + c;
-        t[l] = KY_DADD(t[l], ky_chunk_mass(E[gc], st->m[gc], M));
+        t[l] = KY_DADD(t[l], ky_chunk_mass(E[gc], st->m[gc], Mr[r]));
       }
     }
-    S = KY_DADD(S, ky_butterfly32(t));
+    S = KY_DADD(S, KY_DMUL(ky_butterfly32(t), ky_shard_scale(Mr[r], M)));
   }
+  free(Mr);
   for (int32_t c = 0; c < nc; ++c) {
     st->g[c] = ky_chunk_scale(st->m[c], M, S);
     st->g62[c] = ky_scale62(st->g[c]);

@@ -3,10 +3,10 @@ ranks on the CPU.
 
 Each rank holds only its columns of the target and draft rows (the shard
 rule of src/distributed.rs:90-98) and computes its pieces with the oracle's
-per-shard functions.  The pieces travel in the same four rounds the GPU
-path uses (all-gathers of row maxima, of normaliser parts with the owner's
-values at the draft tokens, of weight totals; a max-reduction of the token
-id) and are combined in rank order.  Both ranks must reach the decisions of
+per-shard functions.  The pieces travel in the same three rounds the GPU
+path uses (an all-gather of row maxima with the normaliser parts under
+them and the owner's values at the draft tokens; an all-gather of weight
+totals; a max-reduction of the token id) and are combined in rank order.  Both ranks must reach the decisions of
 the single-process oracle over the same shards.
 """
 import os
@@ -68,24 +68,30 @@ def _protocol(O, rank, world, tgt, drf, drafts, T, seed):
             return int(drafts[b, r - k - 1])
         return -1
 
-    # round 1: row maxima
+    # round 1: each rank's row max, its normaliser part under that max, and
+    # the owner's e and chunk max at the draft token
     m_loc = np.array([[O.tp_row_max(row(b, r), T) for r in range(R)] for b in range(B)],
                      dtype=np.float32)
-    M = np.max(np.stack(_gather(m_loc)), axis=0)
-    # round 2: normaliser parts under the global max; the owner's e and chunk max
     S_loc = np.zeros((B, R), dtype=np.float64)
     ex = np.zeros((B, R), dtype=np.float32)
     mcx = np.zeros((B, R), dtype=np.float32)
     for b in range(B):
         for r in range(R):
-            S_loc[b, r] = O.tp_row_sum_part(row(b, r), T, float(M[b, r]))
+            S_loc[b, r] = O.tp_row_sum_part(row(b, r), T, float(m_loc[b, r]))
             x = token_of_row(b, r)
             if lo <= x < lo + Vs:
                 ex[b, r], mcx[b, r] = O.tp_entry(row(b, r), T, x - lo)
-    S_all, ex_all, mcx_all = _gather(S_loc), _gather(ex), _gather(mcx)
+    m_all, S_all, ex_all, mcx_all = _gather(m_loc), _gather(S_loc), _gather(ex), _gather(mcx)
+    M = np.max(np.stack(m_all), axis=0)
+
+    def shard_scale(mr, mm):  # ky_shard_scale
+        return 1.0 if mr == mm else float(np.float64(O.exp(np.float32(mr) - np.float32(mm))))
+
     S = np.zeros((B, R), dtype=np.float64)
     for q in range(world):  # rank order
-        S = S + S_all[q]
+        for b in range(B):
+            for r in range(R):
+                S[b, r] = S[b, r] + S_all[q][b, r] * shard_scale(m_all[q][b, r], M[b, r])
 
     def scale(m_c, Mr, Sr):
         return np.float32(np.float64(O.exp(np.float32(m_c) - np.float32(Mr))) / Sr)
@@ -114,7 +120,7 @@ def _protocol(O, rank, world, tgt, drf, drafts, T, seed):
         Sq = float(S[b, k + 1 + aa]) if aa < k else 1.0
         totals[b] = O.tp_weight_totals(ts[b, aa], q_shard, T, float(M[b, aa]), float(S[b, aa]),
                                        Mq, Sq)
-    # round 3: weight totals; the owner rank of the cut point finds the token
+    # round 2: weight totals; the owner rank of the cut point finds the token
     tot_all = _gather(totals)
     cand = np.full(B, -1, dtype=np.int64)
     for b in range(B):
@@ -139,7 +145,7 @@ def _protocol(O, rank, world, tgt, drf, drafts, T, seed):
             local = O.tp_cut(ts[b, aa], q_shard, T, float(M[b, aa]), float(S[b, aa]), Mq, Sq,
                              residual, thr - before)
             cand[b] = lo + local
-    # round 4: the token id, from its owner
+    # round 3: the token id, from its owner
     t = torch.from_numpy(cand)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     for b in range(B):
