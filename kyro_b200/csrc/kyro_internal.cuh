@@ -126,6 +126,12 @@ size_t setup_bytes(int world);
 int init(kyro_ctx* ctx, uint8_t* dh);
 void release(kyro_ctx* ctx);
 int all_gather(kyro_ctx* ctx, const void* send, void* recv, size_t bytes, const char* what);
+// Whether the next round (a payload of `bytes` per rank) can be stored by its
+// producer kernel straight into the peers' regions (xchg.cuh): fills
+// `peers` and takes this rank's fault-injection skip for the round (1: it
+// stores and flags only its own slot), as the exchange kernel would.
+struct Peers;
+bool push_round(kyro_ctx* ctx, size_t bytes, Peers* peers, int* skip);
 int all_reduce_max_i32(kyro_ctx* ctx, const int32_t* send, int32_t* recv, size_t count,
                        const char* what);
 }  // namespace xchg

@@ -4,19 +4,17 @@
 // DistributedContext (src/distributed.rs:61-98) shards the vocabulary; the
 // sharded acceptance then needs three small exchanges per step (row maxima
 // with the normaliser parts under them, weight totals, the sampled token),
-// each a few KB to a few hundred KB.  At that size an NCCL collective costs its launch and
-// protocol latency (~20 us a round measured on two B200s).  Here every rank
+// each a few KB to a few hundred KB.  At that size an NCCL collective costs
+// its launch and protocol latency (~20 us a round measured on two B200s).  Here every rank
 // maps every peer's exchange region once (CUDA IPC, at kyro_ctx_tp_init) and
 // one kernel per round stores this rank's payload straight into each peer's
 // region over NVLink, raises a per-sender flag there, and waits for the
 // peers' flags on its own.
 //
-// Region of one rank:
-//   [0, 64 * 2 * 8)    flag[p][s]: the last round of parity s whose payload
-//                      peer p has completed in this region (64 bytes apart)
-//   [2048, 2056)       this rank's round counter
-//   [4096, 4096+2H)    two halves (round parity) of world slots, slot p
-//                      holding peer p's payload of the current round
+// The region's layout is in xchg.cuh.  Round 1 of the sampler is stored by
+// its producer kernel straight into the peers' slots (sampler.cu); the
+// other rounds run through the exchange kernel below.
+//
 // Rounds are numbered on the device (the counter), so a captured CUDA graph
 // replays with fresh numbers.  A slot of parity s is written again only in
 // round s + 2, which a sender starts after it has seen the receiver's flag
@@ -37,41 +35,20 @@
 #include <cstring>
 
 #include "kyro_internal.cuh"
+#include "xchg.cuh"
 
 namespace {
 
-constexpr size_t kCtlBytes = 4096;
-constexpr size_t kFlagStride = 64;
-constexpr size_t kSeqOffset = 2048;
-static_assert(2 * KYRO_MAX_TP_WORLD * kFlagStride <= kSeqOffset, "flags overlap the counter");
+using kyro::xchg::flag_of;
+using kyro::xchg::globaltimer;
+using kyro::xchg::kCtlBytes;
+using kyro::xchg::kHalfBytes;
+using kyro::xchg::kSeqOffset;
+using kyro::xchg::ld_acquire_sys;
+using kyro::xchg::Peers;
+using kyro::xchg::st_release_sys;
 
-// flag[p][s] of a region
-__device__ __forceinline__ unsigned long long* flag_of(uint8_t* region, int p, unsigned long long seq) {
-  return reinterpret_cast<unsigned long long*>(region + ((size_t)p * 2 + (size_t)(seq & 1ull)) *
-                                                             kFlagStride);
-}
-constexpr size_t kHalfBytes = size_t(4) << 20;  // one parity half: world slots of one round
 constexpr int kXchgThreads = 512;
-
-struct Peers {
-  uint8_t* p[KYRO_MAX_TP_WORLD];  // every rank's region, mapped here (own: local)
-};
-
-__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
-  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-
-__device__ __forceinline__ unsigned long long globaltimer() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  return t;
-}
 
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
@@ -317,6 +294,18 @@ static int launch(kyro_ctx* ctx, const void* send, void* recv, size_t bytes, int
 bool fits(kyro_ctx* ctx, size_t bytes) {
   return ctx->xchg_ready && bytes % 4 == 0 &&
          ((bytes + 15) & ~size_t(15)) * (size_t)ctx->tp_world <= kHalfBytes;
+}
+
+bool push_round(kyro_ctx* ctx, size_t bytes, Peers* peers, int* skip) {
+  if (!fits(ctx, bytes)) return false;
+  *skip = 0;
+  if (ctx->xchg_skip_rounds > 0) {  // fault injection: this rank skips the round
+    --ctx->xchg_skip_rounds;
+    *skip = 1;
+  }
+  for (int r = 0; r < KYRO_MAX_TP_WORLD; ++r)
+    peers->p[r] = r < ctx->tp_world ? ctx->xchg_peer[r] : nullptr;
+  return true;
 }
 
 int all_gather(kyro_ctx* ctx, const void* send, void* recv, size_t bytes, const char* what) {

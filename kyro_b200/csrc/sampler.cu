@@ -38,6 +38,7 @@
 
 #include "kyro_internal.cuh"
 #include "kyro_math.h"
+#include "xchg.cuh"
 
 namespace {
 
@@ -186,6 +187,12 @@ struct Args {
   TpSeq3 *send3, *recv3;        // [B], [world][B]
   int32_t *send4, *recv4;       // [B]
   unsigned long long* W2;       // [B][nchunks][2]: residual and p weight sums
+  // round 1 stored by accept_tp_part_kernel straight into the peers'
+  // exchange regions (xpush != 0; recv2 unused): xskip is the round's
+  // fault injection, xwait_ns the readers' wait bound
+  int xpush, xskip;
+  unsigned long long xwait_ns;
+  kyro::xchg::Peers xpeers;
   // tree verification: rows per sequence are k+1 = N target rows, then
   // q_rows draft rows (k for the chain)
   int q_rows;
@@ -1497,19 +1504,7 @@ __device__ __forceinline__ double row_sum_part(const Args& a, int64_t srow, floa
 
 // The row's statistics from every rank's round-1 part: M the largest shard
 // maximum, S the parts brought to M and added in rank order (kyro_math.h).
-__device__ __forceinline__ RowStat gathered_row_stat(const Args& a, int64_t srow) {
-  const int64_t rows = (int64_t)a.B * a.R;
-  RowStat v;
-  v.arg = 0;
-  v.M = -INFINITY;
-  for (int q = 0; q < a.tp_world; ++q) v.M = fmaxf(v.M, a.recv2[q * rows + srow].M);
-  v.S = 0.0;
-  for (int q = 0; q < a.tp_world; ++q) {
-    const TpRow2 r = a.recv2[q * rows + srow];
-    v.S = KY_DADD(v.S, KY_DMUL(r.S, ky_shard_scale(r.M, v.M)));
-  }
-  return v;
-}
+
 
 // One CTA per sequence, one warp per row.
 // Greedy: this rank's row maxima and argmaxes (one warp per row).
@@ -1530,11 +1525,26 @@ __global__ void __launch_bounds__(kDecideWarps * 32) accept_tp_max_kernel(Args a
 
 // Stochastic: this rank's row maxima, the normaliser parts under them, and
 // the owner's values at the draft tokens, for round 1 (one warp per row).
+//
+// With a.xpush the records go straight into every peer's slot of this rank
+// for the round (P2P stores over NVLink, spread over all of the grid's
+// CTAs); the CTA that finishes last advances the round counter and raises
+// this rank's flag in every peer's region.
 __global__ void __launch_bounds__(kDecideWarps * 32) accept_tp_part_kernel(Args a) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   const int b = blockIdx.x;
+  __shared__ unsigned long long sh_seq;
   grid_dependency_wait();  // the chunk statistics are complete
   allow_dependents();
+  uint8_t* own = a.xpush ? a.xpeers.p[a.tp_rank] : nullptr;
+  if (a.xpush) {
+    // every CTA reads the round number before the last one advances it
+    if (threadIdx.x == 0)
+      sh_seq = *reinterpret_cast<volatile unsigned long long*>(kyro::xchg::round_counter(own)) + 1ull;
+    __syncthreads();
+  }
+  const unsigned long long seq = a.xpush ? sh_seq : 0ull;
+  const size_t stride = kyro::xchg::slot_stride(sizeof(TpRow2) * (size_t)a.B * a.R);
   for (int r = warp; r < a.R; r += nwarps) {
     const int64_t srow = (int64_t)b * a.R + r;
     TpRow2 v;
@@ -1549,21 +1559,102 @@ __global__ void __launch_bounds__(kDecideWarps * 32) accept_tp_part_kernel(Args 
       v.ex = ld_ex(a, srow);
       v.mcx = a.stats[srow * a.nchunks + xl / kChunk].m;
     }
-    if (lane == 0) a.send2[srow] = v;
+    if (lane == 0) {
+      if (!a.xpush) {
+        a.send2[srow] = v;
+      } else {
+        for (int q = 0; q < a.tp_world; ++q)
+          if (a.xskip == 0 || q == a.tp_rank)
+            reinterpret_cast<TpRow2*>(kyro::xchg::slot_of(a.xpeers.p[q], seq, a.tp_rank, stride))
+                [srow] = v;
+      }
+    }
+  }
+  if (!a.xpush) return;
+  __threadfence_system();  // this CTA's records are visible in the peers' memory
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t* done = reinterpret_cast<uint32_t*>(own + kyro::xchg::kDoneOffset);
+    if (atomicAdd(done, 1u) == gridDim.x - 1u) {
+      *done = 0u;
+      __threadfence();
+      *reinterpret_cast<volatile unsigned long long*>(kyro::xchg::round_counter(own)) = seq;
+      for (int q = 0; q < a.tp_world; ++q)
+        if (a.xskip == 0 || q == a.tp_rank)
+          kyro::xchg::st_release_sys(kyro::xchg::flag_of(a.xpeers.p[q], a.tp_rank, seq), seq);
+    }
   }
 }
 
-__device__ __forceinline__ TestInputs tp_test(const Args& a, int b, int j) {
+// Round 1's records as this rank received them: rank q's record of stats row
+// srow, from the exchange's receive buffer or (a.xpush) from rank q's slot in
+// this rank's region, read from L2.  `base` is the round's slot 0 in the
+// region (pushed rounds only).
+__device__ __forceinline__ TpRow2 round1_row(const Args& a, const uint8_t* base, int q,
+                                             int64_t srow) {
+  const int64_t rows = (int64_t)a.B * a.R;
+  if (!a.xpush) return a.recv2[q * rows + srow];
+  const size_t stride = kyro::xchg::slot_stride(sizeof(TpRow2) * (size_t)rows);
+  const unsigned long long* w =
+      reinterpret_cast<const unsigned long long*>(base + (size_t)q * stride) + srow * 3;
+  const unsigned long long w0 = __ldcg(w), w1 = __ldcg(w + 1), w2 = __ldcg(w + 2);
+  TpRow2 v;
+  v.S = __longlong_as_double((long long)w0);
+  v.ex = __uint_as_float((uint32_t)w1);
+  v.mcx = __uint_as_float((uint32_t)(w1 >> 32));
+  v.M = __uint_as_float((uint32_t)w2);
+  v._pad = (int32_t)(w2 >> 32);
+  return v;
+}
+
+// A CTA that reads round 1: with a.xpush, thread 0 waits (bounded) for every
+// rank's flag of the round and the CTA gets the round's slot 0 in this
+// rank's region; else null (the receive buffer holds the round).
+__device__ __forceinline__ const uint8_t* round1_base(const Args& a) {
+  __shared__ const uint8_t* sh_base;
+  if (!a.xpush) return nullptr;
+  if (threadIdx.x == 0) {
+    uint8_t* own = a.xpeers.p[a.tp_rank];
+    const unsigned long long seq =
+        *reinterpret_cast<volatile unsigned long long*>(kyro::xchg::round_counter(own));
+    for (int q = 0; q < a.tp_world; ++q)
+      if (!kyro::xchg::wait_flag(own, q, seq, a.xwait_ns)) {
+        kyro::dev::flag(a.status, KYRO_DEV_WAIT_TIMEOUT);
+        break;
+      }
+    sh_base = kyro::xchg::slot_of(own, seq, 0,
+                                  kyro::xchg::slot_stride(sizeof(TpRow2) * (size_t)a.B * a.R));
+  }
+  __syncthreads();
+  return sh_base;
+}
+
+// The row's statistics from every rank's round-1 part: M the largest shard
+// maximum, S the parts brought to M and added in rank order (kyro_math.h).
+__device__ __forceinline__ RowStat gathered_row_stat(const Args& a, const uint8_t* base,
+                                                     int64_t srow) {
+  RowStat v;
+  v.arg = 0;
+  v.M = -INFINITY;
+  for (int q = 0; q < a.tp_world; ++q) v.M = fmaxf(v.M, round1_row(a, base, q, srow).M);
+  v.S = 0.0;
+  for (int q = 0; q < a.tp_world; ++q) {
+    const TpRow2 r = round1_row(a, base, q, srow);
+    v.S = KY_DADD(v.S, KY_DMUL(r.S, ky_shard_scale(r.M, v.M)));
+  }
+  return v;
+}
+
+__device__ __forceinline__ TestInputs tp_test(const Args& a, const uint8_t* base, int b, int j) {
   TestInputs t;
   t.x = -1;
   t.ep = t.eq = t.mp = t.mq = 0.0f;
   if (j >= a.k) return t;
   t.x = a.draft_tokens[(int64_t)b * a.k + j];
   if (a.stoch && t.x >= 0 && t.x < a.V_global) {
-    const int64_t rows = (int64_t)a.B * a.R;
     const int owner = (int)(t.x / a.V);
-    const TpRow2 pr = a.recv2[owner * rows + (int64_t)b * a.R + j];
-    const TpRow2 qr = a.recv2[owner * rows + (int64_t)b * a.R + a.k + 1 + j];
+    const TpRow2 pr = round1_row(a, base, owner, (int64_t)b * a.R + j);
+    const TpRow2 qr = round1_row(a, base, owner, (int64_t)b * a.R + a.k + 1 + j);
     t.ep = pr.ex;
     t.mp = pr.mcx;
     t.eq = qr.ex;
@@ -1579,8 +1670,9 @@ __global__ void __launch_bounds__(kDecideWarps * 32) accept_tp_decide_kernel(Arg
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int b = blockIdx.x;
   const int64_t rows = (int64_t)a.B * a.R;
-  grid_dependency_wait();  // the last exchange round has landed
+  grid_dependency_wait();  // round 1 has landed, or (pushed) its producer is done
   allow_dependents();
+  const uint8_t* base = a.stoch ? round1_base(a) : nullptr;
   if (threadIdx.x == 0) a.cnt_c[b] = 0;
   for (int r = threadIdx.x; r < a.R; r += blockDim.x) {
     const int64_t srow = (int64_t)b * a.R + r;
@@ -1588,7 +1680,7 @@ __global__ void __launch_bounds__(kDecideWarps * 32) accept_tp_decide_kernel(Arg
     v.S = 0.0;
     v.arg = 0;
     if (a.stoch) {
-      v = gathered_row_stat(a, srow);
+      v = gathered_row_stat(a, base, srow);
     } else {
       // shards are contiguous: the first strict maximum in rank order is the
       // lowest global index among equal maxima
@@ -1606,7 +1698,7 @@ __global__ void __launch_bounds__(kDecideWarps * 32) accept_tp_decide_kernel(Arg
   }
   __syncthreads();
   if (warp != 0) return;
-  const TestInputs t0 = tp_test(a, b, lane), t1 = tp_test(a, b, lane + 32);
+  const TestInputs t0 = tp_test(a, base, b, lane), t1 = tp_test(a, base, b, lane + 32);
   decide_sequence(a, b, rs, t0, t1);
 }
 
@@ -2388,8 +2480,16 @@ int launch(kyro_ctx* ctx, Args& a, const Workspace& ws, bool vec,
 // The tensor-parallel sequence (kernels and collectives on the context's
 // stream; every rank issues the same collectives in the same order).
 template <bool VEC, bool STOCH>
-int launch_tp(kyro_ctx* ctx, const Args& a) {
+int launch_tp(kyro_ctx* ctx, const Args& a_in) {
+  Args a = a_in;
   const int64_t rows = (int64_t)a.B * a.R;
+  // round 1 (stochastic) goes straight into the peers' regions when the
+  // context's exchange is on peer memory
+  a.xpush = 0;
+  if (STOCH && kyro::xchg::push_round(ctx, sizeof(TpRow2) * (size_t)rows, &a.xpeers, &a.xskip)) {
+    a.xpush = 1;
+    a.xwait_ns = (unsigned long long)ctx->wait_ns;
+  }
   const long long need = ((long long)a.units + kWarps - 1) / kWarps;
   const int resident = resident_ctas<VEC, STOCH>(ctx->num_sms);
   const int grid = (int)(need < resident ? need : resident);
@@ -2399,8 +2499,9 @@ int launch_tp(kyro_ctx* ctx, const Args& a) {
   if (STOCH) {
     KY_TRY(launch_dependent(accept_tp_part_kernel, (unsigned)a.B, dthreads, ctx->stream, a,
                             "accept_tp_part_kernel"));
-    KY_TRY(kyro::xchg::all_gather(ctx, a.send2, a.recv2, sizeof(TpRow2) * rows,
-                                  "kyro_spec_accept_tp: row maxima and normaliser parts"));
+    if (!a.xpush)
+      KY_TRY(kyro::xchg::all_gather(ctx, a.send2, a.recv2, sizeof(TpRow2) * rows,
+                                    "kyro_spec_accept_tp: row maxima and normaliser parts"));
   } else {
     KY_TRY(launch_dependent(accept_tp_max_kernel, (unsigned)a.B, dthreads, ctx->stream, a,
                             "accept_tp_max_kernel"));
