@@ -429,7 +429,10 @@ def run_ours(args):
     rows = gather_rows([rank, int(lens0.sum()), per["attention"], per["accept"], att_ms, acc_ms,
                         ms_rank / args.steps], world, dev)
     ms = max(r[6] for r in rows) * args.steps
-    att_bytes, acc_bytes = float(per["attention"]), float(per["accept"])
+    # with RoPE fused, the attention launch also reads the new K/V rows and
+    # stores them in their paged slots
+    att_bytes = float(per["attention"] + (per["new_rows"] if vstep.fused_rope else 0))
+    acc_bytes = float(per["accept"])
     peak, peak_kind = load_peaks()
     traffic = load_traffic()
     if att_ms >= acc_ms:
