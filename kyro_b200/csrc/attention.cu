@@ -179,6 +179,29 @@ verify_attention_kernel(const __nv_bfloat16* __restrict__ q,
           *reinterpret_cast<const uint4*>(q + (((int64_t)b * a.nq + jq) * a.hq + h) * D + ch * 8);
     }
   }
+  // ROPE: this KV head's new K/V rows load in the same round trip (which of
+  // them fall in this split depends on the context length).  Item it of
+  // kRowItems per row: a K piece and its partner half, or one V piece;
+  // thread tid holds items tid and tid + kThreads, the rest load later.
+  constexpr int kHalfPieces = kD / 16;
+  constexpr int kRowItems = kHalfPieces + kD / 8;
+  constexpr int kNewPre = 2;
+  uint4 pre1[kNewPre], pre2[kNewPre];
+#pragma unroll
+  for (int u = 0; u < kNewPre; ++u) {
+    pre1[u] = pre2[u] = make_uint4(0, 0, 0, 0);
+    const int it = tid + u * kThreads;
+    if (ROPE && it < a.nq * kRowItems) {
+      const int j = it / kRowItems, c0 = it - j * kRowItems;
+      const int64_t src = (((int64_t)b * a.nq + j) * a.hkv + kvh) * (kD / 8);
+      if (c0 < kHalfPieces) {
+        pre1[u] = r.k_new[src + c0];
+        pre2[u] = r.k_new[src + kHalfPieces + c0];
+      } else {
+        pre1[u] = r.v_new[src + c0 - kHalfPieces];
+      }
+    }
+  }
   const int64_t ctx = context_lens[b];
   const int64_t total = ctx + a.nq;
   if (ctx < 0 || (total + kBS - 1) / kBS > a.max_blocks) {
@@ -221,6 +244,7 @@ verify_attention_kernel(const __nv_bfloat16* __restrict__ q,
   }
 
   // ---- block ids of this split, Q rows, column masks into shared memory
+  int bad_id = 0;
 #pragma unroll
   for (int j = 0; j < kIdsPerThread; ++j) {
     const int i = tid + j * kThreads;
@@ -229,6 +253,7 @@ verify_attention_kernel(const __nv_bfloat16* __restrict__ q,
       if (phys < 0 || phys >= a.num_blocks) {
         kyro::dev::flag(status, KYRO_DEV_BAD_BLOCK);
         phys = 0;
+        bad_id = 1;
       }
       ids[i] = (int32_t)phys;
     }
@@ -270,12 +295,11 @@ verify_attention_kernel(const __nv_bfloat16* __restrict__ q,
       const_cast<float2*>(tab(p))[i] = make_float2(c, sn);
     }
   }
-  __syncthreads();
+  const int any_bad_id = __syncthreads_or(bad_id);  // the ids, the mask and the table are in place
   if (ROPE) {
     // the query rows: thread tid holds 16-byte piece ch of row col (i = tid
     // + j * kThreads); the piece with the other half of the same dims sits
     // in thread tid ^ kHalfPieces
-    constexpr int kHalfPieces = kD / 16;
 #pragma unroll
     for (int j = 0; j < kQPerThread; ++j) {
       const int i = tid + j * kThreads;
@@ -305,41 +329,61 @@ verify_attention_kernel(const __nv_bfloat16* __restrict__ q,
       *reinterpret_cast<uint4*>(qtile + col * kQStride * 2 + ch * 16) = o;
     }
     // the new slots ctx + j that fall in this split's blocks: rotated keys
-    // (a piece and its partner per item) and values (one piece per item)
+    // (a piece and its partner half per item) and values (one piece per
+    // item), the items numbered as their speculative loads above
     const int64_t s_lo = (int64_t)blk0 * kBS - ctx, s_hi = (int64_t)(blk0 + nb) * kBS - ctx;
     const int j_lo = (int)(s_lo > 0 ? s_lo : 0);
     const int j_hi = (int)(s_hi < a.nq ? s_hi : a.nq);
-    const int nrow = j_hi - j_lo;
-    for (int it = tid; it < nrow * (kHalfPieces + kD / 8); it += kThreads) {
-      const bool is_k = it < nrow * kHalfPieces;
-      const int rel = is_k ? it : it - nrow * kHalfPieces;
-      const int per = is_k ? kHalfPieces : kD / 8;
-      const int j = j_lo + rel / per, c = rel - (rel / per) * per;
-      const int64_t slot = ctx + j;
-      const int64_t phys = block_table[(int64_t)b * a.max_blocks + slot / kBS];
-      if (phys < 0 || phys >= a.num_blocks) continue;  // flagged with the block ids
-      const int64_t row = ((phys * a.hkv + kvh) * kBS + slot % kBS) * (kD / 8);  // uint4 units
-      const int64_t src = (((int64_t)b * a.nq + j) * a.hkv + kvh) * (kD / 8);
-      if (is_k) {
-        const uint4 x1 = r.k_new[src + c], x2 = r.k_new[src + kHalfPieces + c];
-        const uint32_t a4[4] = {x1.x, x1.y, x1.z, x1.w}, b4[4] = {x2.x, x2.y, x2.z, x2.w};
-        const float2* cs = tab(j) + c * 8;
-        uint32_t lo[4], hi[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 t0 = cs[2 * e], t1 = cs[2 * e + 1];
-          kyro::rope::rotate_pair(a4[e], b4[e], t0.x, t1.x, t0.y, t1.y, lo[e], hi[e]);
+    bool stored = false;
+    if (j_lo < j_hi) {
+      for (int it = tid, u = 0; it < a.nq * kRowItems; it += kThreads, ++u) {
+        const int j = it / kRowItems, c0 = it - j * kRowItems;
+        if (j < j_lo || j >= j_hi) continue;
+        const int64_t slot = ctx + j;
+        int64_t phys = ids[slot / kBS - blk0];
+        if (any_bad_id) {  // ids of bad entries read 0 in shared memory: check the table
+          phys = block_table[(int64_t)b * a.max_blocks + slot / kBS];
+          if (phys < 0 || phys >= a.num_blocks) continue;  // flagged with the block ids
         }
-        uint4* dst = reinterpret_cast<uint4*>(r.k_cache) + row;
-        dst[c] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-        dst[kHalfPieces + c] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-      } else {
-        reinterpret_cast<uint4*>(r.v_cache)[row + c] = r.v_new[src + c];
+        const int64_t row = ((phys * a.hkv + kvh) * kBS + slot % kBS) * (kD / 8);  // uint4 units
+        const int64_t src = (((int64_t)b * a.nq + j) * a.hkv + kvh) * (kD / 8);
+        const bool is_k = c0 < kHalfPieces;
+        uint4 x1, x2;
+        if (u == 0) {
+          x1 = pre1[0];
+          x2 = pre2[0];
+        } else if (u == 1) {
+          x1 = pre1[kNewPre - 1];
+          x2 = pre2[kNewPre - 1];
+        } else if (is_k) {
+          x1 = r.k_new[src + c0];
+          x2 = r.k_new[src + kHalfPieces + c0];
+        } else {
+          x1 = r.v_new[src + c0 - kHalfPieces];
+        }
+        if (is_k) {
+          const int c = c0;
+          const uint32_t a4[4] = {x1.x, x1.y, x1.z, x1.w}, b4[4] = {x2.x, x2.y, x2.z, x2.w};
+          const float2* cs = tab(j) + c * 8;
+          uint32_t lo[4], hi[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 t0 = cs[2 * e], t1 = cs[2 * e + 1];
+            kyro::rope::rotate_pair(a4[e], b4[e], t0.x, t1.x, t0.y, t1.y, lo[e], hi[e]);
+          }
+          uint4* dst = reinterpret_cast<uint4*>(r.k_cache) + row;
+          dst[c] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+          dst[kHalfPieces + c] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        } else {
+          reinterpret_cast<uint4*>(r.v_cache)[row + c0 - kHalfPieces] = x1;
+        }
+        stored = true;
       }
     }
-    // the stores reach L2 before any cp.async of this CTA reads the blocks;
-    // the table's slot is free again after the barrier
-    __threadfence();
+    // the stores reach L2 before any cp.async of this CTA reads the blocks
+    // (only a thread that stored has anything to fence); the table's slot is
+    // free again after the barrier
+    if (stored) __threadfence();
     __syncthreads();
     // the late blocks: one copy group for every prefetch position from the
     // first late one on (empty where the warp has no block), in order, so
