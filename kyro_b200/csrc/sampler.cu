@@ -2350,6 +2350,13 @@ bool use_vec(const void* a, const void* b, int64_t V) {
   return (V % 4 == 0) && ((uintptr_t)a % 16 == 0) && (b == nullptr || (uintptr_t)b % 16 == 0);
 }
 
+// CTAs a stats launch needs: one warp per batch of kGrab units (more warps
+// would only find the counter exhausted); capped by the resident count.
+long long stats_ctas_needed(uint32_t units) {
+  const long long per_cta = (long long)kGrab * kWarps;
+  return ((long long)units + per_cta - 1) / per_cta;
+}
+
 template <bool VEC, bool STOCH>
 int resident_ctas(int num_sms) {
   // one occupancy query per kernel (not repeated inside a graph capture)
@@ -2445,7 +2452,7 @@ struct CommitSpec {
 
 template <bool VEC, bool STOCH>
 int launch_t(kyro_ctx* ctx, const Args& a, const CommitSpec* commit) {
-  const long long need = ((long long)a.units + kWarps - 1) / kWarps;
+  const long long need = stats_ctas_needed(a.units);
   const int resident = resident_ctas<VEC, STOCH>(ctx->num_sms);
   const int grid = (int)(need < resident ? need : resident);
   // launched plainly: a persistent grid launched early would take SM slots
@@ -2490,7 +2497,7 @@ int launch_tp(kyro_ctx* ctx, const Args& a_in) {
     a.xpush = 1;
     a.xwait_ns = (unsigned long long)ctx->wait_ns;
   }
-  const long long need = ((long long)a.units + kWarps - 1) / kWarps;
+  const long long need = stats_ctas_needed(a.units);
   const int resident = resident_ctas<VEC, STOCH>(ctx->num_sms);
   const int grid = (int)(need < resident ? need : resident);
   accept_stats_kernel<VEC, STOCH><<<grid, kThreads, 0, ctx->stream>>>(a);
@@ -2878,10 +2885,9 @@ int kyro_spec_accept_tree(kyro_ctx* ctx, const kyro_tree_params* p, const float*
   a.status = ctx->d_status;
   KY_TRY(use_unit_counter(ctx, a, ws, workspace));
   const bool vec = use_vec(target_logits, a.qlog, V);
-  const long long units = (long long)a.units;
   if (vec && stoch) {
     const int resident = resident_ctas<true, true>(ctx->num_sms);
-    const long long need_ctas = (units + kWarps - 1) / kWarps;
+    const long long need_ctas = stats_ctas_needed(a.units);
     accept_stats_kernel<true, true><<<(int)(need_ctas < resident ? need_ctas : resident),
                                       kThreads, 0, ctx->stream>>>(a);
     KY_TRY(kyro::check_launch("accept_stats_kernel"));
@@ -2892,7 +2898,7 @@ int kyro_spec_accept_tree(kyro_ctx* ctx, const kyro_tree_params* p, const float*
   }
   if (vec) {
     const int resident = resident_ctas<true, false>(ctx->num_sms);
-    const long long need_ctas = (units + kWarps - 1) / kWarps;
+    const long long need_ctas = stats_ctas_needed(a.units);
     accept_stats_kernel<true, false><<<(int)(need_ctas < resident ? need_ctas : resident),
                                        kThreads, 0, ctx->stream>>>(a);
     KY_TRY(kyro::check_launch("accept_stats_kernel"));
@@ -2901,7 +2907,7 @@ int kyro_spec_accept_tree(kyro_ctx* ctx, const kyro_tree_params* p, const float*
   }
   if (stoch) {
     const int resident = resident_ctas<false, true>(ctx->num_sms);
-    const long long need_ctas = (units + kWarps - 1) / kWarps;
+    const long long need_ctas = stats_ctas_needed(a.units);
     accept_stats_kernel<false, true><<<(int)(need_ctas < resident ? need_ctas : resident),
                                        kThreads, 0, ctx->stream>>>(a);
     KY_TRY(kyro::check_launch("accept_stats_kernel"));
@@ -2911,7 +2917,7 @@ int kyro_spec_accept_tree(kyro_ctx* ctx, const kyro_tree_params* p, const float*
                             ctx->stream, a, "accept_tree_kernel");
   }
   const int resident = resident_ctas<false, false>(ctx->num_sms);
-  const long long need_ctas = (units + kWarps - 1) / kWarps;
+  const long long need_ctas = stats_ctas_needed(a.units);
   accept_stats_kernel<false, false><<<(int)(need_ctas < resident ? need_ctas : resident),
                                       kThreads, 0, ctx->stream>>>(a);
   KY_TRY(kyro::check_launch("accept_stats_kernel"));
