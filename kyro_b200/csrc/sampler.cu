@@ -630,19 +630,48 @@ struct Slice {
   int x;              // draft token scored in this row, -1 if none
 };
 
-// Issue the loads of unit u (entries past V read as -inf).
-template <bool VEC>
-__device__ __forceinline__ void load_slice(const Args& a, uint32_t u, Slice& s) {
-  const int lane = threadIdx.x & 31;
+// Where a batch's first unit lies: its stats row, chunk, draft token and
+// logits row.  The batch's other units follow it chunk by chunk (a batch of
+// kGrab units crosses into the next row at most once).
+struct RowCursor {
+  uint32_t u0, srow;
+  int c0, x;
+  const float* row;
+};
+
+__device__ __forceinline__ void cursor_at(const Args& a, uint32_t u, RowCursor& rc) {
   const uint32_t srow = fdiv(u, a.div_chunks);
-  const int c = (int)(u - srow * (uint32_t)a.nchunks);
   const int b = (int)fdiv(srow, a.div_rows);
   const int r = (int)(srow - (uint32_t)b * (uint32_t)a.R);
+  const int xg = draft_token_of_row(a, b, r);  // global id, -1 for none
+  rc.u0 = u;
+  rc.srow = srow;
+  rc.c0 = (int)(u - srow * (uint32_t)a.nchunks);
+  rc.x = xg < 0 ? -1 : (int)(xg - a.vocab_offset);
+  rc.row = stats_row_ptr(a, b, r);
+}
+
+// Issue the loads of unit u, a unit of the batch rc starts (entries past V
+// read as -inf).
+template <bool VEC>
+__device__ __forceinline__ void load_slice(const Args& a, const RowCursor& rc, uint32_t u,
+                                           Slice& s) {
+  const int lane = threadIdx.x & 31;
+  int c = rc.c0 + (int)(u - rc.u0);
+  uint32_t srow = rc.srow;
+  int x = rc.x;
+  const float* row = rc.row;
+  if (c >= a.nchunks) {  // past the end of the batch's first row
+    RowCursor t;
+    cursor_at(a, u, t);
+    srow = t.srow;
+    c = t.c0;
+    x = t.x;
+    row = t.row;
+  }
   s.srow = srow;
   s.c = c;
-  const int xg = draft_token_of_row(a, b, r);  // global id, -1 for none
-  s.x = xg < 0 ? -1 : (int)(xg - a.vocab_offset);
-  const float* row = stats_row_ptr(a, b, r);
+  s.x = x;
   const int64_t base = (int64_t)c * kChunk;
   if (VEC && base + kChunk <= a.V) {
     const float4* src = reinterpret_cast<const float4*>(row + base) + lane;
@@ -792,6 +821,8 @@ __global__ void __launch_bounds__(kThreads, kStatsMinCtas) accept_stats_kernel(A
   uint32_t nxt = take_units(a.unit_ctr);
   if (u < a.units) {
     uint32_t end = min(u + kGrab, a.units);
+    RowCursor rc;  // the current batch's position, decoded once per batch
+    cursor_at(a, u, rc);
     // the unit after u, or a value >= units when the warp is done
     auto advance = [&](uint32_t cur) -> uint32_t {
       if (cur + 1 < end) return cur + 1;
@@ -799,18 +830,19 @@ __global__ void __launch_bounds__(kThreads, kStatsMinCtas) accept_stats_kernel(A
       if (n < a.units) {
         end = min(n + kGrab, a.units);
         nxt = take_units(a.unit_ctr);
+        cursor_at(a, n, rc);
       }
       return n;
     };
-    load_slice<VEC>(a, u, s0);
+    load_slice<VEC>(a, rc, u, s0);
     while (true) {
       uint32_t un = advance(u);
-      if (un < a.units) load_slice<VEC>(a, un, s1);
+      if (un < a.units) load_slice<VEC>(a, rc, un, s1);
       reduce_slice<STOCH>(a, s0, tag);
       if (un >= a.units) break;
       u = un;
       un = advance(u);
-      if (un < a.units) load_slice<VEC>(a, un, s0);
+      if (un < a.units) load_slice<VEC>(a, rc, un, s0);
       reduce_slice<STOCH>(a, s1, tag);
       if (un >= a.units) break;
       u = un;
