@@ -146,6 +146,7 @@ struct Args {
   int R;                        // stats rows per sequence
   int64_t V;
   int nchunks;
+  int nfull;                    // chunks wholly inside V (the rest pad with -inf)
   FastDiv div_chunks, div_rows;  // by nchunks, by R
   float inv_t;
   int stoch;                    // softmax statistics (else argmax only)
@@ -625,9 +626,10 @@ __device__ __forceinline__ void chain_seq_done(const Args& a) {
 // One chunk in flight: its 16 logits per lane and where it belongs.
 struct Slice {
   float v[kPerLane];  // float4 i (0..3) holds chunk entries (i*32 + lane)*4 + 0..3
+  ChunkStat* dst;     // the chunk's record
   uint32_t srow;      // stats row: b * R + r
   int c;              // chunk index in the row
-  int x;              // draft token scored in this row, -1 if none
+  int x;              // draft token scored in this row (in [0, V)), -1 if none
 };
 
 // Where a batch's first unit lies: its stats row, chunk, draft token and
@@ -637,6 +639,7 @@ struct RowCursor {
   uint32_t u0, srow;
   int c0, x;
   const float* row;
+  ChunkStat* st;  // the row's chunk records
 };
 
 __device__ __forceinline__ void cursor_at(const Args& a, uint32_t u, RowCursor& rc) {
@@ -647,8 +650,10 @@ __device__ __forceinline__ void cursor_at(const Args& a, uint32_t u, RowCursor& 
   rc.u0 = u;
   rc.srow = srow;
   rc.c0 = (int)(u - srow * (uint32_t)a.nchunks);
-  rc.x = xg < 0 ? -1 : (int)(xg - a.vocab_offset);
+  const int64_t xl = xg < 0 ? -1 : (int64_t)xg - a.vocab_offset;
+  rc.x = (xl >= 0 && xl < a.V) ? (int)xl : -1;
   rc.row = stats_row_ptr(a, b, r);
+  rc.st = a.stats + (int64_t)srow * a.nchunks;
 }
 
 // Issue the loads of unit u, a unit of the batch rc starts (entries past V
@@ -661,6 +666,7 @@ __device__ __forceinline__ void load_slice(const Args& a, const RowCursor& rc, u
   uint32_t srow = rc.srow;
   int x = rc.x;
   const float* row = rc.row;
+  ChunkStat* st = rc.st;
   if (c >= a.nchunks) {  // past the end of the batch's first row
     RowCursor t;
     cursor_at(a, u, t);
@@ -668,12 +674,14 @@ __device__ __forceinline__ void load_slice(const Args& a, const RowCursor& rc, u
     c = t.c0;
     x = t.x;
     row = t.row;
+    st = t.st;
   }
+  s.dst = st + c;
   s.srow = srow;
   s.c = c;
   s.x = x;
   const int64_t base = (int64_t)c * kChunk;
-  if (VEC && base + kChunk <= a.V) {
+  if (VEC && c < a.nfull) {
     const float4* src = reinterpret_cast<const float4*>(row + base) + lane;
 #pragma unroll
     for (int i = 0; i < kVec; ++i) {
@@ -706,7 +714,6 @@ __device__ __forceinline__ void load_slice(const Args& a, const RowCursor& rc, u
 template <bool STOCH>
 __device__ __forceinline__ void reduce_slice(const Args& a, Slice& s, uint32_t tag) {
   const int lane = threadIdx.x & 31;
-  const int64_t base = (int64_t)s.c * kChunk;
   ChunkStat st;
   if (STOCH) {
     // columns (0,1) and (2,3) of each float4 as packed pairs
@@ -762,10 +769,11 @@ __device__ __forceinline__ void reduce_slice(const Args& a, Slice& s, uint32_t t
     f2_unpack(acc23, a2, a3);
     st.m = m;
     st.E = warp_butterfly_f(__fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3)));
-    // e at the draft token, by the lane that holds it (s.v holds z * inv_t)
-    const int64_t xo = (int64_t)s.x - base;
-    if (s.x >= 0 && s.x < a.V && xo >= 0 && xo < kChunk && lane == (int)((xo >> 2) & 31)) {
-      const int q = (int)(((xo >> 7) << 2) | (xo & 3));
+    // e at the draft token, by the lane that holds it (s.v holds z * inv_t);
+    // xo is negative for a row without one (s.x == -1)
+    const int xo = s.x - s.c * kChunk;
+    if ((unsigned)xo < (unsigned)kChunk && lane == ((xo >> 2) & 31)) {
+      const int q = ((xo >> 7) << 2) | (xo & 3);
       float z = s.v[0];
 #pragma unroll
       for (int i = 1; i < kPerLane; ++i)
@@ -774,19 +782,20 @@ __device__ __forceinline__ void reduce_slice(const Args& a, Slice& s, uint32_t t
                      ((unsigned long long)tag << 32);
     }
   } else {
+    const int base = s.c * kChunk;  // token ids are int32
     float m = -INFINITY;
     int arg = 0x7fffffff;
 #pragma unroll
     for (int i = 0; i < kPerLane; ++i)
       if (s.v[i] > m) {
         m = s.v[i];
-        arg = (int)(base + ((i >> 2) * 32 + lane) * 4 + (i & 3));
+        arg = base + ((i >> 2) * 32 + lane) * 4 + (i & 3);
       }
     kyro::dev::warp_argmax(m, arg);
     st.m = m;
     st.E = __int_as_float(arg);
   }
-  if (lane == 0) st_stat(a.stats + (int64_t)s.srow * a.nchunks + s.c, st.m, st.E, tag);
+  if (lane == 0) st_stat(s.dst, st.m, st.E, tag);
 }
 
 // Units a warp takes from the counter at a time (dynamic distribution).
@@ -2568,6 +2577,7 @@ void fill_common(Args& a, const Workspace& ws, int64_t V, int B, int R) {
   a.B = B;
   a.R = R;
   a.nchunks = (int)((V + kChunk - 1) / kChunk);
+  a.nfull = (int)(V / kChunk);
   a.div_chunks = make_fastdiv((uint32_t)a.nchunks);
   a.div_rows = make_fastdiv((uint32_t)R);
   a.units = (uint32_t)((int64_t)B * R * a.nchunks);
