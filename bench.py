@@ -550,13 +550,33 @@ def run_e2e(args, ctx, cfg, st, kv, vstep, tgt, drf, drafts, k_new, v_new, world
 
 # ------------------------------------------------------------------ extras
 def run_extras(args, ctx, world, rank, local, dev):
-    """Configs 0, 2 and 3 on the same ranks, each with its own short timed
+    """Configs 0, 2, 3 and 4 on the same ranks, each with its own short timed
     region (max over ranks).  Every rank takes the same collective steps."""
     out = {}
     out["config0"] = extra_config0(ctx, world, dev)
     out["config2"] = tree_measure(ctx, world, rank, dev, steps=args.extra_steps, warmup=3)
     out["tp_accept"] = tp_measure(world, rank, local, dev, steps=args.extra_steps, warmup=3)
+    out["config4"] = extra_config4(args, world, rank, local, dev)
     return out
+
+
+def extra_config4(args, world, rank, local, dev):
+    """Config 4 (the end-to-end speculative step, bench.py --config 4) in
+    short: a few graph-replayed steps, the step time and its parts."""
+    import types
+    a = types.SimpleNamespace(warmup=3, steps=max(3, args.extra_steps // 4), no_graph=False,
+                              requests=None, target_layers=None)
+    m = e2e_model_measure(a, world, rank, local, dev)
+    cfg, k, ms = m["cfg"], m["k"], m["ms"]
+    return {"workload": "config4: end-to-end speculative step, 16-layer Llama target + 2-layer "
+                        "draft, k 4, T 0.7, 512 requests split over the ranks (strong scaling)",
+            "steps": a.steps, "ms_per_step": ms / a.steps,
+            "positions_per_s": cfg.requests * (k + 1) * a.steps / (ms * 1e-3),
+            "emitted_tokens_per_s": m["emitted"] / (ms * 1e-3),
+            "parts_ms_per_step": m["part"],
+            "target_attention": {"GBps": m["att_gbs"], "frac_hbm": m["att_gbs"] / m["peak"]},
+            "accept": {"GBps": m["acc_gbs"], "frac_hbm": m["acc_gbs"] / m["peak"]},
+            "timing": "CUDA graph replays of the step, max over ranks"}
 
 
 def extra_config0(ctx, world, dev, steps=200):
@@ -1040,13 +1060,16 @@ class _EventTimer:
         return sum(a.elapsed_time(b) for a, b in self.pairs.get(name, [])) / per
 
 
-def run_e2e_model(args):
+def e2e_model_measure(args, world, rank, local, dev):
     """Config 4: the end-to-end batched speculative step over a random-init
     16-layer Llama target and a 2-layer draft (kyro_b200/e2e_model.py).
     512 requests in total, split over the N ranks (strong scaling, no
     collective); every step drafts k = 4 tokens per request, verifies k + 1
     positions through the target, accepts, and commits, with the contexts
-    growing from step to step.  Timed as CUDA graph replays of one step."""
+    growing from step to step.  Timed as CUDA graph replays of one step
+    (args: warmup, steps, no_graph, requests, target_layers).  Returns the
+    measurements (max over ranks, byte counts over all ranks) on every rank;
+    every rank takes the same collective steps."""
     import torch
     import torch.distributed as dist
 
@@ -1054,7 +1077,6 @@ def run_e2e_model(args):
     from kyro_b200.verify import Context
     from kyro_b200.workloads import ChainConfig, paged_state
 
-    world, rank, local, dev = init_ranks(args, timeout_s=300)
     cfg, shape = CONFIG4, CONFIG4_SHAPE
     if args.requests or args.target_layers:
         # a smaller case of the same step, for profiler captures (not a bench line)
@@ -1149,6 +1171,25 @@ def run_e2e_model(args):
     small = load_traffic().get("verify_attention_kernel_config4_small")
     traffic4 = (small["dram_bytes"] / small["algorithmic_bytes"] * att_bytes / world / shape.layers
                 if small else None)
+    ctx_t.close()
+    ctx_d.close()
+    return {"cfg": cfg, "shape": shape, "B": B, "k": k, "ms": ms, "emitted": emitted,
+            "part": part, "att_bytes": att_bytes, "att_ms": att_ms, "att_gbs": att_gbs,
+            "acc_bytes": acc_bytes, "acc_ms": acc_ms, "acc_gbs": acc_gbs, "peak": peak,
+            "peak_kind": peak_kind, "traffic4": traffic4, "clocks": clk}
+
+
+def run_e2e_model(args):
+    """Config 4 as its own bench line (bench.py --config 4)."""
+    import torch.distributed as dist
+
+    world, rank, local, dev = init_ranks(args, timeout_s=300)
+    m = e2e_model_measure(args, world, rank, local, dev)
+    cfg, shape, B, k, ms, emitted, part = (m[n] for n in ("cfg", "shape", "B", "k", "ms", "emitted",
+                                                          "part"))
+    att_bytes, att_ms, att_gbs = m["att_bytes"], m["att_ms"], m["att_gbs"]
+    acc_bytes, acc_ms, acc_gbs = m["acc_bytes"], m["acc_ms"], m["acc_gbs"]
+    peak, peak_kind, traffic4, clk = m["peak"], m["peak_kind"], m["traffic4"], m["clocks"]
     if rank == 0:
         line = {
             "metric": "spec-decode verified positions/s, end-to-end step (config 4)",
@@ -1184,8 +1225,6 @@ def run_e2e_model(args):
             "clocks": clk,
         }
         print(json.dumps(line), flush=True)
-    ctx_t.close()
-    ctx_d.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
