@@ -24,8 +24,10 @@
 // four warps' states merge in shared memory in one pass (each warp
 // publishes its (O, m, l), per-column factors are formed once, then every
 // thread combines four dims at a time); when a sequence needs more than one
-// split, each split writes its partial state to the workspace and the split
-// that finishes last (an epoch-tagged atomic ticket) merges them.
+// split, every split takes an epoch-tagged ticket, and the one whose ticket
+// completes the count merges them all from its own state on chip and the
+// partial states the other splits store in the workspace (each raises a
+// ready flag once its partial is out).
 #include <cuda_bf16.h>
 
 #include <cmath>
@@ -43,6 +45,9 @@ constexpr int kThreads = kWarps * 32;
 constexpr int kMaxCols = 32;          // query rows per work item
 constexpr int kMaxSplitBlocks = 256;  // KV blocks per work item
 constexpr int kMaxSplits = 64;        // work items per (sequence, KV head, row group)
+// 64-bit words of a work item's ticket region: the ticket, then a 32-bit
+// ready flag per split
+__host__ __device__ constexpr int ticket_words(int max_splits) { return 1 + (max_splits + 1) / 2; }
 constexpr float kLazyRescale = 8.0f;  // log2 headroom before a column's running max moves
 
 // Shared-memory geometry for head_dim D (64 or 128) and NS ring stages.
@@ -118,6 +123,191 @@ __device__ __forceinline__ void load_block(uint32_t slot, const uint8_t* __restr
 // whose blocks hold new slots rotates those keys and stores them with their
 // values before it streams the blocks (the cache is read only by cp.async,
 // after a fence and a barrier).
+// The end of a work item after its warp merge, out of line so that its
+// registers do not weigh on the streaming loop's: a single split writes its
+// rows; with more than one split, the split whose ticket completes the count
+// merges them all.  The ticket comes first, so the merging split keeps its
+// own state on chip; every other split stores its partial and raises its
+// ready flag.  A ticket is (epoch << 32 | splits done); a ticket of another
+// epoch (a workspace that held other data) counts as zero.
+template <int D, int NS>
+__device__ __noinline__ void split_merge(const AttnArgs a, const float* mo, const float* mf,
+                                         const float* mM, const float* mL, int* sh_last, int b,
+                                         int kvh, int grp, int split, int nsplit, int ncols,
+                                         int col0, __nv_bfloat16* __restrict__ out,
+                                         float* __restrict__ part_o, float* __restrict__ part_ml,
+                                         unsigned long long* __restrict__ tickets,
+                                         uint32_t* status) {
+  constexpr int kD = D;
+  constexpr int kMoStride = Geo<D, NS>::kMoStride;
+  const int tid = threadIdx.x;
+  const bool single = nsplit == 1;
+  const int64_t item = ((int64_t)b * a.hkv + kvh) * a.ngroups + grp;
+  float* po = part_o + item * a.max_splits * (kMaxCols * kD);
+  float* pml = part_ml + item * a.max_splits * (kMaxCols * 2);
+  // the item's ticket and its splits' ready flags (ticket_words per item)
+  unsigned long long* tkt = tickets + item * ticket_words(a.max_splits);
+  uint32_t* ready = reinterpret_cast<uint32_t*>(tkt + 1);
+
+  bool last = single;
+  if (!single) {
+    if (tid == 0) {
+      // guess that this split completes the count: one CAS when it does
+      unsigned long long cur = ((unsigned long long)a.epoch << 32) | (uint32_t)(nsplit - 1);
+      uint32_t done;
+      for (;;) {
+        done = (uint32_t)(cur >> 32) == a.epoch ? (uint32_t)cur + 1u : 1u;
+        const unsigned long long nw = ((unsigned long long)a.epoch << 32) | done;
+        const unsigned long long prev = atomicCAS(tkt, cur, nw);
+        if (prev == cur) break;
+        cur = prev;
+      }
+      *sh_last = done == (uint32_t)nsplit;
+    }
+    __syncthreads();
+    last = *sh_last != 0;
+  }
+
+  // this split's merged O at (col, d4..d4+3), formed from the warps' states
+  // in shared memory wherever it is needed (the same operations each time);
+  // a thread's entries are tid, tid + kThreads, ... (four dims each)
+  constexpr int kEnt = kMaxCols * (kD / 4) / kThreads;
+  auto own_o = [&](int col, int d4) -> float4 {
+    float4 O = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const float f = mf[w * kMaxCols + col];
+      const float4 v = *reinterpret_cast<const float4*>(&mo[(w * kMaxCols + col) * kMoStride + d4]);
+      O.x += f * v.x;
+      O.y += f * v.y;
+      O.z += f * v.z;
+      O.w += f * v.w;
+    }
+    return O;
+  };
+  auto store_out = [&](int col, int d4, float4 O, float inv) {
+    const int r = col0 + col, j = r / a.group, gi = r % a.group;
+    const int h = kvh * a.group + gi;
+    *reinterpret_cast<uint2*>(&out[(((int64_t)b * a.nq + j) * a.hq + h) * kD + d4]) =
+        make_uint2(kyro::ptx::pack_bf16x2(O.x * inv, O.y * inv),
+                   kyro::ptx::pack_bf16x2(O.z * inv, O.w * inv));
+  };
+  if (single) {
+#pragma unroll
+    for (int e = 0; e < kEnt; ++e) {
+      const int i4 = tid + e * kThreads;
+      const int col = i4 / (kD / 4), d4 = (i4 % (kD / 4)) * 4;
+      if (col >= ncols) continue;
+      const float L = mL[col];
+      store_out(col, d4, own_o(col, d4), L > 0.0f ? 1.0f / L : 0.0f);
+    }
+    return;
+  }
+  if (!last) {
+#pragma unroll
+    for (int e = 0; e < kEnt; ++e) {
+      const int i4 = tid + e * kThreads;
+      const int col = i4 / (kD / 4), d4 = (i4 % (kD / 4)) * 4;
+      if (col >= ncols) continue;
+      *reinterpret_cast<float4*>(&po[(split * kMaxCols + col) * kD + d4]) = own_o(col, d4);
+      if (d4 == 0) {
+        pml[(split * kMaxCols + col) * 2 + 0] = mM[col];
+        pml[(split * kMaxCols + col) * 2 + 1] = mL[col];
+      }
+    }
+    __syncthreads();
+    if (tid == 0) {
+      __threadfence();  // every thread's partial (observed through the barrier) first
+      asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(ready + split), "r"(a.epoch)
+                   : "memory");
+    }
+    return;
+  }
+  // the merging split: the others' ready flags (each split took its ticket
+  // before this one and stores without waiting, so the wait is short;
+  // bounded all the same)
+  if (tid < nsplit && tid != split) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ready + tid) : "memory");
+    if (v != a.epoch) {
+      unsigned long long t0, t;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+      while (true) {
+        __nanosleep(64);
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ready + tid) : "memory");
+        if (v == a.epoch) break;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        if (t - t0 > 1000000000ull) {
+          kyro::dev::flag(status, KYRO_DEV_WAIT_TIMEOUT);
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  // every thread merges its own entries: the splits' maxima of its columns,
+  // then factors, sums and O in split order (this split's own state in place
+  // of its partial)
+  float Mu[kEnt];
+#pragma unroll
+  for (int e = 0; e < kEnt; ++e) {
+    const int col = min((tid + e * kThreads) / (kD / 4), kMaxCols - 1);
+    Mu[e] = mM[col];
+  }
+#pragma unroll 1
+  for (int sp = 0; sp < nsplit; ++sp) {
+    if (sp == split) continue;
+#pragma unroll
+    for (int e = 0; e < kEnt; ++e) {
+      const int col = min((tid + e * kThreads) / (kD / 4), kMaxCols - 1);
+      Mu[e] = fmaxf(Mu[e], __ldcg(&pml[(sp * kMaxCols + col) * 2]));
+    }
+  }
+  float Ls[kEnt];
+  float4 O[kEnt];
+#pragma unroll
+  for (int e = 0; e < kEnt; ++e) {
+    if (Mu[e] == -INFINITY) Mu[e] = 0.0f;
+    Ls[e] = 0.0f;
+    O[e] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  }
+#pragma unroll 1
+  for (int sp = 0; sp < nsplit; ++sp) {
+#pragma unroll
+    for (int e = 0; e < kEnt; ++e) {
+      const int i4 = tid + e * kThreads;
+      const int col = min(i4 / (kD / 4), kMaxCols - 1), d4 = (i4 % (kD / 4)) * 4;
+      float m, l;
+      float4 v;
+      if (sp == split) {
+        m = mM[col];
+        l = mL[col];
+        v = own_o(col, d4);
+      } else {
+        m = __ldcg(&pml[(sp * kMaxCols + col) * 2]);
+        l = __ldcg(&pml[(sp * kMaxCols + col) * 2 + 1]);
+        v = __ldcg(reinterpret_cast<const float4*>(&po[(sp * kMaxCols + col) * kD + d4]));
+      }
+      const float f = kyro::ptx::fast_exp2(m - Mu[e]);
+      Ls[e] += f * l;
+      O[e].x += f * v.x;
+      O[e].y += f * v.y;
+      O[e].z += f * v.z;
+      O[e].w += f * v.w;
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < kEnt; ++e) {
+    const int i4 = tid + e * kThreads;
+    const int col = i4 / (kD / 4), d4 = (i4 % (kD / 4)) * 4;
+    if (col >= ncols) continue;
+    store_out(col, d4, O[e], Ls[e] > 0.0f ? 1.0f / Ls[e] : 0.0f);
+  }
+  // back to zero for the next call (a replayed graph reuses its epoch)
+  if (tid < nsplit && tid != split) ready[tid] = 0u;
+  if (tid == 0) *tkt = 0ull;
+}
+
 template <int NT, int D, int NS, bool ROPE>
 __global__ void __launch_bounds__(kThreads, 3)
 verify_attention_kernel(const __nv_bfloat16* __restrict__ q,
@@ -606,105 +796,8 @@ verify_attention_kernel(const __nv_bfloat16* __restrict__ q,
   }
   __syncthreads();
 
-  const bool single = nsplit == 1;
-  const int64_t item = ((int64_t)b * a.hkv + kvh) * a.ngroups + grp;
-  float* po = part_o + item * a.max_splits * (kMaxCols * kD);
-  float* pml = part_ml + item * a.max_splits * (kMaxCols * 2);
-  for (int i4 = tid; i4 < ncols * (kD / 4); i4 += kThreads) {
-    const int col = i4 / (kD / 4), d4 = (i4 % (kD / 4)) * 4;
-    float4 O = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) {
-      const float f = mf[w * kMaxCols + col];
-      const float4 v = *reinterpret_cast<const float4*>(&mo[(w * kMaxCols + col) * kMoStride + d4]);
-      O.x += f * v.x;
-      O.y += f * v.y;
-      O.z += f * v.z;
-      O.w += f * v.w;
-    }
-    const float L = mL[col];
-    if (single) {
-      const float inv = L > 0.0f ? 1.0f / L : 0.0f;
-      const int r = col0 + col, j = r / a.group, gi = r % a.group;
-      const int h = kvh * a.group + gi;
-      *reinterpret_cast<uint2*>(&out[(((int64_t)b * a.nq + j) * a.hq + h) * kD + d4]) =
-          make_uint2(kyro::ptx::pack_bf16x2(O.x * inv, O.y * inv),
-                     kyro::ptx::pack_bf16x2(O.z * inv, O.w * inv));
-    } else {
-      *reinterpret_cast<float4*>(&po[(split * kMaxCols + col) * kD + d4]) = O;
-      if (d4 == 0) {
-        pml[(split * kMaxCols + col) * 2 + 0] = mM[col];
-        pml[(split * kMaxCols + col) * 2 + 1] = L;
-      }
-    }
-  }
-  if (single) return;
-
-  // ---- the last split of this (sequence, KV head, row group) merges all splits
-  __syncthreads();
-  if (tid == 0) {
-    // a ticket is (epoch << 32 | splits done); the merging split zeroes it,
-    // and a ticket of another epoch (a workspace that held other data)
-    // counts as zero
-    __threadfence();
-    unsigned long long cur = *(volatile unsigned long long*)&tickets[item];
-    uint32_t done;
-    for (;;) {
-      done = (uint32_t)(cur >> 32) == a.epoch ? (uint32_t)cur + 1u : 1u;
-      const unsigned long long nw = ((unsigned long long)a.epoch << 32) | done;
-      const unsigned long long prev = atomicCAS(&tickets[item], cur, nw);
-      if (prev == cur) break;
-      cur = prev;
-    }
-    *sh_last = done == (uint32_t)nsplit;
-  }
-  __syncthreads();
-  if (!*sh_last) return;
-  __threadfence();
-  // every split's (m, l) per column, copied in one parallel pass
-  float* sml = reinterpret_cast<float*>(ring);                    // [split][col][2]
-  float* fscale = sml + kMaxSplits * kMaxCols * 2;                // [split][col]
-  float* finv = fscale + kMaxSplits * kMaxCols;                   // [col]
-  for (int i = tid; i < nsplit * kMaxCols * 2; i += kThreads) sml[i] = __ldcg(&pml[i]);
-  __syncthreads();
-  for (int col = tid; col < ncols; col += kThreads) {
-    float M = -INFINITY;
-    for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, sml[(sp * kMaxCols + col) * 2]);
-    const float Mu = M == -INFINITY ? 0.0f : M;
-    float L = 0.0f;
-    for (int sp = 0; sp < nsplit; ++sp) {
-      const float f = kyro::ptx::fast_exp2(sml[(sp * kMaxCols + col) * 2] - Mu);
-      fscale[sp * kMaxCols + col] = f;
-      L += f * sml[(sp * kMaxCols + col) * 2 + 1];
-    }
-    finv[col] = L > 0.0f ? 1.0f / L : 0.0f;
-  }
-  __syncthreads();
-  // four dims per thread per step; the splits' loads are independent, so
-  // several are in flight at once
-#pragma unroll 2
-  for (int i4 = tid; i4 < ncols * (kD / 4); i4 += kThreads) {
-    const int col = i4 / (kD / 4), d4 = (i4 % (kD / 4)) * 4;
-    float4 O = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-#pragma unroll 4
-    for (int sp = 0; sp < nsplit; ++sp) {
-      const float f = fscale[sp * kMaxCols + col];
-      const float4 v =
-          __ldcg(reinterpret_cast<const float4*>(&po[(sp * kMaxCols + col) * kD + d4]));
-      O.x += f * v.x;
-      O.y += f * v.y;
-      O.z += f * v.z;
-      O.w += f * v.w;
-    }
-    const float inv = finv[col];
-    const int r = col0 + col, j = r / a.group, gi = r % a.group;
-    const int h = kvh * a.group + gi;
-    *reinterpret_cast<uint2*>(&out[(((int64_t)b * a.nq + j) * a.hq + h) * kD + d4]) =
-        make_uint2(kyro::ptx::pack_bf16x2(O.x * inv, O.y * inv),
-                   kyro::ptx::pack_bf16x2(O.z * inv, O.w * inv));
-  }
-  // back to zero for the next call (a replayed graph reuses its epoch)
-  if (tid == 0) tickets[item] = 0ull;
+  split_merge<D, NS>(a, mo, mf, mM, mL, sh_last, b, kvh, grp, split, nsplit, ncols, col0, out,
+                     part_o, part_ml, tickets, status);
 }
 
 // ------------------------------------------------------------------ host
@@ -781,7 +874,7 @@ int plan(const kyro_attn_params* p, int num_sms, Plan* out) {
   const int64_t items = groups * (a.max_splits > 1 ? a.max_splits : 0);
   pl.part_o_bytes = (size_t)items * kMaxCols * p->head_dim * 4;
   pl.part_ml_bytes = (size_t)items * kMaxCols * 2 * 4;
-  pl.ticket_bytes = a.max_splits > 1 ? (size_t)groups * 8 : 0;
+  pl.ticket_bytes = a.max_splits > 1 ? (size_t)groups * 8 * ticket_words(a.max_splits) : 0;
   *out = pl;
   return KYRO_OK;
 }
