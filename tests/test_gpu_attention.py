@@ -71,6 +71,36 @@ def test_split_kv_merge(ctx, oracle, d, split):
     assert np.abs(out.float().cpu().numpy() - ref).max() < ATOL
 
 
+def test_split_merge_graph_replays(ctx, oracle):
+    """Replays of a captured call reuse its epoch: the merging split sets the
+    ticket and the other splits' ready flags back to zero, so every replay
+    merges afresh (64 splits of 4 blocks on the longest sequence)."""
+    from kyro_b200.verify import verify_attention
+    cfg, st, _ = _setup(ctx, 32, 8, 128, 6, [3000, 47, 1500, 4096], seed=11)
+    ref = _oracle(oracle, st, cfg, None)
+    out = torch.empty_like(st.q)
+    side = torch.cuda.Stream(ctx.device)
+    try:
+        with torch.cuda.stream(side):
+            ctx.bind_stream()
+            verify_attention(ctx, st.q, st.k_cache, st.v_cache, st.block_table, st.context_lens,
+                             out=out, kv_split_blocks=4)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=side):
+                verify_attention(ctx, st.q, st.k_cache, st.v_cache, st.block_table,
+                                 st.context_lens, out=out, kv_split_blocks=4)
+        for _ in range(3):
+            with torch.cuda.stream(side):
+                out.zero_()
+                graph.replay()
+            torch.cuda.synchronize()
+            assert np.abs(out.float().cpu().numpy() - ref).max() < ATOL
+        del graph
+    finally:
+        ctx.bind_stream()
+    assert ctx.device_status() == 0
+
+
 def test_tree_mask_attention(ctx, oracle):
     from kyro_b200.verify import verify_attention
     cfg, st, mask = _setup(ctx, 64, 8, 128, 64, [300, 1000], seed=9, tree=True)
