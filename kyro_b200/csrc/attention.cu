@@ -850,11 +850,15 @@ int plan(const kyro_attn_params* p, int num_sms, Plan* out) {
   a.d = p->head_dim;
   int64_t split = p->kv_split_blocks;
   if (split == 0) {
-    // aim for about two waves of work items at three CTAs per SM, assuming
-    // half the table width is used on average
+    // aim for about 1.6 waves of work items at three CTAs per SM, assuming
+    // half the table width is used on average.  Measured with the RoPE
+    // prologue on 64 sequences of U[512, 4096] context (Hq 32 / Hkv 8, 320
+    // table columns): splits of 112 / 120 / 124 / 128 blocks 115.7 / 116.4 /
+    // 116.5 / 117.0 us, the two-wave choice (92 blocks) 120.0 us, and 64 /
+    // 80 / 96 / 144 / 160 blocks 119.8 / 125.6 / 120.6 / 121.2 / 121.3 us
     const int64_t items = (int64_t)a.B * a.hkv * a.ngroups;
     const int64_t avg_blocks = (a.max_blocks + 1) / 2;
-    const int64_t target = (int64_t)num_sms * 3 * 2;
+    const int64_t target = (int64_t)num_sms * 3 * 8 / 5;
     split = (items * avg_blocks + target - 1) / (target > 0 ? target : 1);
     split = (split + kWarps - 1) / kWarps * kWarps;
     if (split < 16) split = 16;
