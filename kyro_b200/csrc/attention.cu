@@ -66,9 +66,7 @@ struct Geo {
   static constexpr int kMoStride = D + 4;
   static constexpr int kMergeBytes =
       (kWarps * kMaxCols * kMoStride + 3 * kWarps * kMaxCols + 2 * kMaxCols) * 4;
-  static constexpr int kFinalBytes = (3 * kMaxSplits * kMaxCols + kMaxCols) * 4;
   static_assert(kMergeBytes <= kRingBytes + kQBytes, "the warp merge reuses the ring and Q tile");
-  static_assert(kFinalBytes <= kRingBytes, "the split merge reuses the ring");
   static constexpr int kSmemBytes =
       kRingBytes + kQBytes + kMaxCols * 8 + kMaxSplitBlocks * 4 + 16;
 };
@@ -118,11 +116,6 @@ __device__ __forceinline__ void load_block(uint32_t slot, const uint8_t* __restr
   }
 }
 
-// ROPE: the queries arrive unrotated and this step's keys and values are not
-// in the cache yet.  The prologue rotates the CTA's query rows, and a CTA
-// whose blocks hold new slots rotates those keys and stores them with their
-// values before it streams the blocks (the cache is read only by cp.async,
-// after a fence and a barrier).
 // The end of a work item after its warp merge, out of line so that its
 // registers do not weigh on the streaming loop's: a single split writes its
 // rows; with more than one split, the split whose ticket completes the count
@@ -308,6 +301,11 @@ __device__ __noinline__ void split_merge(const AttnArgs a, const float* mo, cons
   if (tid == 0) *tkt = 0ull;
 }
 
+// ROPE: the queries arrive unrotated and this step's keys and values are not
+// in the cache yet.  The prologue rotates the CTA's query rows, and a CTA
+// whose blocks hold new slots rotates those keys and stores them with their
+// values before it streams the blocks (the cache is read only by cp.async,
+// after a fence and a barrier).
 template <int NT, int D, int NS, bool ROPE>
 __global__ void __launch_bounds__(kThreads, 3)
 verify_attention_kernel(const __nv_bfloat16* __restrict__ q,
